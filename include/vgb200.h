@@ -1,0 +1,153 @@
+/*
+ * libvgb200 — B200 (sm_100a) renderer of Voronoi-Gaussian radiance fields, C ABI.
+ *
+ * Drop-in boundary for the CUDA extensions of daovietanh190499/voronoi-gauss. Each entry point below
+ * replaces one pybind11 function of the reference (file:line of the reference given beside it): same
+ * argument meaning, layouts and output semantics, with torch tensors replaced by raw device pointers
+ * and element counts, outputs allocated by the caller, and an integer status instead of a Python
+ * exception.
+ *
+ * Conventions
+ *   - All pointers are device pointers unless stated otherwise; all arrays are C-contiguous, float32 or
+ *     int32 exactly as in the reference (foam.cu:34-37 CHECK_INPUT, foam.cu:481-494).
+ *   - `stream` is a cudaStream_t (0 = legacy default stream); work is enqueued asynchronously on the
+ *     device that is current on the calling thread, nothing synchronises the host.
+ *   - `workspace` is caller-allocated device scratch of at least the size returned by the matching
+ *     *_workspace_bytes function (256-byte aligned). The library allocates no device memory.
+ *   - Return value: VG_OK (0) or an error code; vg_last_error() gives a message (thread-local).
+ *     Loop caps (4096 walk steps, 8192 cells per ray, foam.cu:29-30) truncate as in the reference;
+ *     vg_status() reports, after the stream has been synchronised, whether a launch hit one.
+ *
+ * Scene graph. The reference passes (points, offsets, adj) to every call and keeps them fixed
+ * (ext.Graph, ext.py:46-58). Here they are packed once by vg_graph_pack into a caller buffer (Morton-
+ * ordered self-first neighbourhoods of 16-byte records); every render call takes that pack instead.
+ */
+#ifndef VGB200_H
+#define VGB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    VG_OK = 0,
+    VG_ERR_INVALID_ARG = 1,  /* shape / dtype / size / null pointer: the reference's TORCH_CHECK */
+    VG_ERR_WORKSPACE = 2,    /* workspace or pack buffer smaller than required */
+    VG_ERR_CUDA = 3          /* a CUDA launch or runtime call failed */
+};
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+int vg_version(void);
+
+/* Message of the last error on this thread ("" if none). */
+const char* vg_last_error(void);
+
+/* Bits of the status word accumulated by the render launches since the last vg_status_reset():
+ * 1 = a greedy walk hit its 4096-step cap, 2 = a ray hit the 8192-cell cap. Synchronises the device. */
+int vg_status(int* bits);
+int vg_status_reset(void);
+
+/* ---------------------------------------------------------------------------------- scene graph */
+
+/* Bytes of the packed graph of n_sites sites with n_adj adjacency entries. */
+size_t vg_graph_pack_bytes(int64_t n_sites, int64_t n_adj);
+
+/* Packs (points (N, 3) float32, offsets (N + 1) int32, adj (M) int32) — the CSR Delaunay adjacency
+ * of ext.Graph (ext.py:46-52) — into `pack`. Replaces the per-call (points, offsets, adj) triple of
+ * every function below. */
+int vg_graph_pack(const float* points, const int32_t* offsets, const int32_t* adj, int64_t n_sites,
+                  int64_t n_adj, void* pack, size_t pack_bytes, void* stream);
+
+/* ------------------------------------------------------------------------- interaction points */
+
+/* Workspace of vg_foam_forward / vg_march_forward (backward = 0) or of the backward functions
+ * (backward = 1) for n_sites sites at SH degree sh_deg. */
+size_t vg_foam_workspace_bytes(int64_t n_sites, int sh_deg, int backward);
+
+/* foam_forward (foam.cu:505-526): rendering at the ray / Voronoi-face interaction points.
+ * raw (N), dA (N, 6), cA (N, 6), sh (N, 16, 3); o, d (B, 3); start (B) site near each origin;
+ * near, far (B). Outputs rgb (B, 3) foreground colour, T (B) final transmittance, depth (B),
+ * stats (B, 3) int32 = (samples, coloured segments, walk steps); with record_cap K > 0 also
+ * rec (B, K, 8) = the first K samples of every ray (t, site bits, sigma, C rgb, m_min, 1 / sum of
+ * colour weights) for vg_foam_backward; rec may be NULL when K == 0. */
+int vg_foam_forward(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA,
+                    const float* cA, const float* sh, int sh_deg, const float* o, const float* d,
+                    const int32_t* start, const float* near, const float* far, int64_t n_rays, float t_thresh,
+                    float w_thresh, int record_cap, float* rgb, float* T, float* depth, int32_t* stats,
+                    float* rec, void* workspace, size_t workspace_bytes, void* stream);
+
+/* foam_backward (foam.cu:528-558): gradients g_raw (N), g_dA (N, 6), g_cA (N, 6), g_sh (N, 16, 3)
+ * (overwritten) of sum(g_rgb * rgb) + sum(g_T * T). Replays the records of rays with
+ * stats[r, 0] <= record_cap and re-traces the others (record_cap = 0: re-trace every ray). */
+int vg_foam_backward(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA,
+                     const float* cA, const float* sh, int sh_deg, const float* o, const float* d,
+                     const int32_t* start, const float* near, const float* far, int64_t n_rays,
+                     float t_thresh, float w_thresh, const float* rgb, const float* T, const float* g_rgb,
+                     const float* g_T, const float* rec, int record_cap, const int32_t* stats, float* g_raw,
+                     float* g_dA, float* g_cA, float* g_sh, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/* The two halves of vg_foam_backward, for data-parallel training: the gradients of this device's
+ * rays are summed into grad_pack (N, 64) float32 (zero-filled first when zero_first != 0; layout
+ * g_raw, g_dA[6], 0, g_cA[6], 0, 0, g_sh[48] in packed site order), which can be all-reduced across
+ * devices before vg_grad_unpack writes the reference's four gradient arrays. No reference
+ * counterpart: the reference is single-GPU. */
+int vg_foam_backward_packed(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA,
+                            const float* cA, const float* sh, int sh_deg, const float* o, const float* d,
+                            const int32_t* start, const float* near, const float* far, int64_t n_rays,
+                            float t_thresh, float w_thresh, const float* rgb, const float* T,
+                            const float* g_rgb, const float* g_T, const float* rec, int record_cap,
+                            const int32_t* stats, float* grad_pack, int zero_first, void* workspace,
+                            size_t workspace_bytes, void* stream);
+int vg_grad_unpack(const void* pack, int64_t n_sites, int64_t n_adj, const float* grad_pack, int sh_deg,
+                   float* g_raw, float* g_dA, float* g_cA, float* g_sh, void* stream);
+
+/* ------------------------------------------------------------------------------- fixed steps */
+
+/* march_forward (march.cu:383-403): midpoints of steps dt in [near, mid], n_bg disparity steps in
+ * [mid, far]; outputs as vg_foam_forward without records. */
+int vg_march_forward(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA,
+                     const float* cA, const float* sh, int sh_deg, const float* o, const float* d,
+                     const int32_t* start, const float* near, const float* mid, const float* far, int64_t n_rays,
+                     float dt, int n_bg, float t_thresh, float w_thresh, float* rgb, float* T, float* depth,
+                     int32_t* stats, void* workspace, size_t workspace_bytes, void* stream);
+
+/* march_backward (march.cu:405-429): re-marches every ray; gradients overwritten. */
+int vg_march_backward(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA,
+                      const float* cA, const float* sh, int sh_deg, const float* o, const float* d,
+                      const int32_t* start, const float* near, const float* mid, const float* far, int64_t n_rays,
+                      float dt, int n_bg, float t_thresh, float w_thresh, const float* rgb, const float* T,
+                      const float* g_rgb, const float* g_T, float* g_raw, float* g_dA, float* g_cA, float* g_sh,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------------- conics */
+
+/* conic_forward (vgf.cu:535-546): A (N, 6) = R(q) diag(1 / (exp(2 clamp(ls)) + floor^2)) R^T. */
+int vg_conic_forward(const float* log_scale, const float* quat, int64_t n, double floor, float* A, void* stream);
+
+/* conic_backward (vgf.cu:548-561): g_ls (N, 3), g_quat (N, 4) from gA (N, 6). */
+int vg_conic_backward(const float* log_scale, const float* quat, int64_t n, double floor, const float* gA,
+                      float* g_ls, float* g_quat, void* stream);
+
+/* ---------------------------------------------------------------------------------- inference */
+
+/* foam_infer (foam_infer.cu:376-435) on the packed inference layout of render.pack_foam: points (N, 4),
+ * offsets (N + 1) into self-first neighbourhoods, nbr (E), edge (E, 4) = (p, half2(r2, lam)),
+ * attr (N, 20), sh (N, 16, 3) float32 (sh_half = 0) or float16 (sh_half = 1, may be NULL for baked
+ * colours), orig (N) or NULL, cap (B) or NULL. color_mode 0 lazy / 1 baked / 2 fused; stage 0..2.
+ * Outputs rgb (B, 3), T (B), depth (B), stats (B, 5). */
+int vg_foam_infer(const float* points, const int32_t* offsets, const int32_t* nbr, const float* edge,
+                  const float* attr, const void* sh, int sh_half, int sh_deg, int64_t n_sites, int64_t n_edges,
+                  const float* o, const float* d, const int32_t* start, const float* near, const float* far,
+                  int64_t n_rays, float t_thresh, float w_thresh, float color_cut, int color_mode, int stage,
+                  const int32_t* cap, const int32_t* orig, float* rgb, float* T, float* depth, int32_t* stats,
+                  void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,251 @@
+"""Generates the golden fixtures in this directory from the reference's own CPU code.
+
+Run where the reference checkout is available (VG_REFERENCE, default /root/reference); the GPU box
+and the tests only read the committed .npz files. Every fixture stores its inputs and the outputs of
+the reference's float64 restatements:
+
+* foam_small.npz   - test_foam.py's scene (300 sites, rng(2)), 64 rays, thresholds disabled:
+                     test_foam.trace cell sequences (test_foam.py:18-37), float64 compositing and
+                     autograd gradients of raw / dA / cA / sh (test_foam.py:76-104); the reference
+                     pack_foam layouts (render.py:179-225) for four option sets, with ext.conic
+                     replaced by its torch twin ext.conic_reference (ext.py:139-149) because the
+                     CUDA conic cannot run here; render.morton_order (render.py:168-176).
+* march_small.npz  - test_march.py's scene (rng(1)), dt 0.05, n_bg 8, conic floor 0.01: samples()
+                     + exact nearest sites + float64 compositing and gradients (test_march.py:14-88).
+* conic.npz        - ext.conic_reference in float64 and its autograd gradients.
+* sh_basis.npz     - render.sh_basis for degrees 0..3 (render.py:143-165).
+* foam_config1.npz - 64 rays of an orbit camera over the config-1 scene (10k uniform sites), float64
+                     trace + compositing + sparse gradients.
+"""
+
+import os
+import sys
+from types import SimpleNamespace
+
+import numpy as np
+import torch
+
+REF = os.environ.get('VG_REFERENCE', '/root/reference')
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REF)
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+
+import ext as ref_ext  # noqa: E402
+import render as ref_render  # noqa: E402
+import sites as ref_sites  # noqa: E402
+import test_foam  # noqa: E402
+import test_grad  # noqa: E402
+import test_march  # noqa: E402
+from scipy.spatial import cKDTree  # noqa: E402
+
+torch.set_default_dtype(torch.float32)
+
+
+def ragged(seqs, dtype):
+    off = np.zeros(len(seqs) + 1, dtype=np.int64)
+    off[1:] = np.cumsum([len(s) for s in seqs])
+    return np.concatenate(seqs).astype(dtype), off
+
+
+def foam_reference(pts, offsets, adj, raw, dA, cA, sh, o, d, near, far, g_rgb, g_T, cells0=None, sh_deg=3):
+    """float64 trace + compositing + gradients, as test_foam.py:76-104; only the first (sh_deg + 1)^2 SH
+    bands are used, as the kernels do (foam.cu:143-153)."""
+    n = len(pts)
+    tree = cKDTree(pts)
+    P = torch.tensor(pts, dtype=torch.float64)
+    ref = [torch.tensor(np.asarray(t), dtype=torch.float64).requires_grad_() for t in (raw, dA, cA, sh)]
+    rraw, rdA, rcA, rsh = ref
+    o64, d64 = np.asarray(o, np.float64), np.asarray(d, np.float64)
+    fg_ref, T_ref, ts, cells = [], [], [], []
+    for r in range(len(o64)):
+        x0 = o64[r] + float(near[r]) * d64[r]
+        start_cell = tree.query(x0)[1] if cells0 is None else cells0[r]
+        t, cl = test_foam.trace(pts, offsets, adj, o64[r], d64[r], float(near[r]), float(far[r]), start_cell)
+        ts.append(t)
+        cells.append(cl)
+        X = torch.tensor(o64[r][None] + t[:, None] * d64[r][None])
+        mask = test_grad.neighborhood_mask(offsets, adj, torch.tensor(cl), n)
+        sigma = (torch.exp(rraw)[None] * torch.exp(-0.5 * test_march.mahalanobis6(P, rdA, X)) * mask).sum(1)
+        a = torch.softmax((-0.5 * test_march.mahalanobis6(P, rcA, X)).masked_fill(~mask, -float('inf')), 1)
+        D = torch.tensor(d64[r])
+        basis = test_grad.sh_basis(D) * (torch.arange(16) < (sh_deg + 1) ** 2)
+        ck = (torch.einsum('j,njc->nc', basis, rsh) + 0.5).clamp_min(0)
+        C = a @ ck
+        delta = torch.tensor(t[1:] - t[:-1])
+        alpha = 1 - torch.exp(-0.5 * (sigma[1:] + sigma[:-1]) * delta)
+        trans = torch.cumprod(torch.cat([torch.ones(1, dtype=torch.float64), 1 - alpha]), 0)
+        w = alpha * trans[:-1]
+        fg_ref.append((w[:, None] * 0.5 * (C[1:] + C[:-1])).sum(0))
+        T_ref.append(trans[-1])
+    fg_ref, T_ref = torch.stack(fg_ref), torch.stack(T_ref)
+    ((fg_ref * torch.tensor(g_rgb, dtype=torch.float64)).sum() +
+     (T_ref * torch.tensor(g_T, dtype=torch.float64)).sum()).backward()
+    t_flat, t_off = ragged(ts, np.float64)
+    c_flat, _ = ragged(cells, np.int32)
+    return dict(ref_fg=fg_ref.detach().numpy(), ref_T=T_ref.detach().numpy(), ref_t=t_flat, ref_t_off=t_off,
+                ref_cells=c_flat, ref_g_raw=rraw.grad.numpy(), ref_g_dA=rdA.grad.numpy(),
+                ref_g_cA=rcA.grad.numpy(), ref_g_sh=rsh.grad.numpy())
+
+
+def small_scene(seed):
+    """Scene and parameters of test_foam.py:41-60 / test_march.py:35-49 (CPU generator)."""
+    torch.manual_seed(0)
+    rng = np.random.default_rng(seed)
+    pts, _, offsets, adj = ref_sites.delaunay_graph(rng.uniform(-0.9, 0.9, (300, 3)))
+    n = len(pts)
+    raw = torch.randn(n) * 0.5 + 1.0
+    ls = torch.randn(n, 3) * 0.3 - 1.8
+    q = torch.randn(n, 4)
+    cls = torch.randn(n, 3) * 0.3 - 1.8
+    cq = torch.randn(n, 4)
+    sh = torch.randn(n, 16, 3) * 0.3
+    return rng, pts, offsets, adj, raw, ls, q, cls, cq, sh
+
+
+def make_foam_small():
+    rng, pts, offsets, adj, raw, ls, q, cls, cq, sh = small_scene(2)
+    B = 64
+    o = torch.tensor(rng.uniform(-0.5, 0.5, (B, 3)), dtype=torch.float32)
+    d = torch.nn.functional.normalize(torch.randn(B, 3), dim=-1)
+    start = torch.tensor(cKDTree(pts).query(o.numpy())[1], dtype=torch.int32)
+    near, _, far = ref_render.ray_bounds(o, d, 0.02, 2.0)
+    g_rgb, g_T = torch.randn(B, 3), torch.randn(B)
+    dA, cA = ref_ext.conic_reference(ls, q), ref_ext.conic_reference(cls, cq)
+    out = dict(points=pts.astype(np.float32), offsets=offsets, adj=adj, raw=raw.numpy(), ls=ls.numpy(),
+               quat=q.numpy(), cls=cls.numpy(), cquat=cq.numpy(), dA=dA.numpy(), cA=cA.numpy(), sh=sh.numpy(),
+               o=o.numpy(), d=d.numpy(), start=start.numpy(), near=near.numpy(), far=far.numpy(),
+               g_rgb=g_rgb.numpy(), g_T=g_T.numpy(), sh_deg=3, far_radius=2.0)
+    out.update(foam_reference(pts.astype(np.float32).astype(np.float64), offsets, adj, raw.numpy(), dA.numpy(),
+                              cA.numpy(), sh.numpy(), o.numpy(), d.numpy(), near.numpy(), far.numpy(),
+                              g_rgb.numpy(), g_T.numpy()))
+    # reference inference packs (ext.conic -> its torch twin, since CUDA is not available here)
+    graph = SimpleNamespace(points=torch.tensor(pts, dtype=torch.float32), offsets=torch.tensor(offsets),
+                            adj=torch.tensor(adj))
+    model = SimpleNamespace(graph=graph, raw=raw, d_log_scale=ls, d_quat=q, c_log_scale=cls, c_quat=cq,
+                            sh=lambda: sh, sh_deg=3)
+    saved = ref_ext.conic
+    ref_ext.conic = ref_ext.conic_reference
+    try:
+        for tag, kw in (('plain', {}), ('morton', dict(reorder=True)),
+                        ('eps', dict(eps_density=1e-3, sh_half=True)),
+                        ('eps_morton', dict(eps_density=1e-3, sh_half=True, reorder=True, scale_floor=0.01))):
+            pk = ref_render.pack_foam(model, **kw)
+            for key in ('points', 'offsets', 'nbr', 'edge', 'attr', 'orig'):
+                out[f'pack_{tag}_{key}'] = pk[key].numpy()
+            out[f'pack_{tag}_sh'] = pk['sh'].numpy()
+        out['morton_perm'] = ref_render.morton_order(graph.points).numpy()
+    finally:
+        ref_ext.conic = saved
+    np.savez_compressed(os.path.join(HERE, 'foam_small.npz'), **out)
+
+
+def make_march_small():
+    rng, pts, offsets, adj, raw, ls, q, cls, cq, sh = small_scene(1)
+    n = len(pts)
+    dA, cA = ref_ext.conic_reference(ls, q, 0.01), ref_ext.conic_reference(cls, cq, 0.01)
+    B, dt, n_bg = 64, 0.05, 8
+    o = torch.tensor(rng.uniform(-0.5, 0.5, (B, 3)), dtype=torch.float32)
+    d = torch.nn.functional.normalize(torch.randn(B, 3), dim=-1)
+    start = torch.tensor(cKDTree(pts).query(o.numpy())[1], dtype=torch.int32)
+    near, mid, far = ref_render.ray_bounds(o, d, 0.02, 2.0)
+    g_rgb, g_T = torch.randn(B, 3), torch.randn(B)
+    P = torch.tensor(pts.astype(np.float32), dtype=torch.float64)
+    ref = [t.double().requires_grad_() for t in (raw, dA, cA, sh)]
+    rraw, rdA, rcA, rsh = ref
+    tree = cKDTree(pts.astype(np.float32).astype(np.float64))
+    fg_ref, T_ref, sites_all = [], [], []
+    for r in range(B):
+        t, delta = test_march.samples(near[r].item(), mid[r].item(), far[r].item(), dt, n_bg)
+        O, D = o[r].double(), d[r].double()
+        X = O[None] + torch.tensor(t)[:, None] * D[None]
+        site = torch.tensor(tree.query(X.numpy())[1])
+        sites_all.append(site.numpy().astype(np.int32))
+        mask = test_grad.neighborhood_mask(offsets, adj, site, n)
+        sigma = (torch.exp(rraw)[None] * torch.exp(-0.5 * test_march.mahalanobis6(P, rdA, X)) * mask).sum(1)
+        alpha = 1 - torch.exp(-sigma * torch.tensor(delta))
+        trans = torch.cumprod(torch.cat([torch.ones(1, dtype=torch.float64), 1 - alpha]), 0)
+        w = alpha * trans[:-1]
+        a = torch.softmax((-0.5 * test_march.mahalanobis6(P, rcA, X)).masked_fill(~mask, -float('inf')), 1)
+        ck = (torch.einsum('j,njc->nc', test_grad.sh_basis(D), rsh) + 0.5).clamp_min(0)
+        fg_ref.append((w[:, None] * (a @ ck)).sum(0))
+        T_ref.append(trans[-1])
+    fg_ref, T_ref = torch.stack(fg_ref), torch.stack(T_ref)
+    ((fg_ref * g_rgb.double()).sum() + (T_ref * g_T.double()).sum()).backward()
+    s_flat, s_off = ragged(sites_all, np.int32)
+    np.savez_compressed(
+        os.path.join(HERE, 'march_small.npz'), points=pts.astype(np.float32), offsets=offsets, adj=adj,
+        raw=raw.numpy(), dA=dA.numpy(), cA=cA.numpy(), sh=sh.numpy(), o=o.numpy(), d=d.numpy(),
+        start=start.numpy(), near=near.numpy(), mid=mid.numpy(), far=far.numpy(), g_rgb=g_rgb.numpy(),
+        g_T=g_T.numpy(), dt=dt, n_bg=n_bg, sh_deg=3, ref_fg=fg_ref.detach().numpy(), ref_T=T_ref.detach().numpy(),
+        ref_sites=s_flat, ref_sites_off=s_off, ref_g_raw=rraw.grad.numpy(), ref_g_dA=rdA.grad.numpy(),
+        ref_g_cA=rcA.grad.numpy(), ref_g_sh=rsh.grad.numpy())
+
+
+def make_conic():
+    g = torch.Generator().manual_seed(5)
+    n = 512
+    ls = torch.randn(n, 3, generator=g) * 0.8 - 1.5
+    ls[:4] = torch.tensor([[25.0, -25.0, 0.0]])  # clamp branch
+    q = torch.randn(n, 4, generator=g)
+    gA = torch.randn(n, 6, generator=g)
+    out = dict(ls=ls.numpy(), quat=q.numpy(), gA=gA.numpy())
+    for floor in (0.0, 0.01):
+        L, Q = ls.double().requires_grad_(), q.double().requires_grad_()
+        A = ref_ext.conic_reference(L, Q, floor)
+        (A * gA.double()).sum().backward()
+        out[f'A_{floor}'] = A.detach().numpy()
+        out[f'g_ls_{floor}'] = L.grad.numpy()
+        out[f'g_quat_{floor}'] = Q.grad.numpy()
+    np.savez_compressed(os.path.join(HERE, 'conic.npz'), **out)
+
+
+def make_sh_basis():
+    g = torch.Generator().manual_seed(7)
+    dirs = torch.nn.functional.normalize(torch.randn(256, 3, generator=g, dtype=torch.float64), dim=-1)
+    out = {'dirs': dirs.numpy()}
+    for deg in range(4):
+        out[f'b{deg}'] = ref_render.sh_basis(dirs, deg).numpy()
+    np.savez_compressed(os.path.join(HERE, 'sh_basis.npz'), **out)
+
+
+def make_foam_config1():
+    from voronoi_gauss_b200 import scenes
+    pts0 = np.random.default_rng(0).uniform(-1, 1, (10000, 3))
+    pts, _, offsets, adj = ref_sites.delaunay_graph(pts0)
+    prm = scenes.make_params(1, pts)
+    dA = ref_ext.conic_reference(prm['d_log_scale'], prm['d_quat'])
+    cA = ref_ext.conic_reference(prm['c_log_scale'], prm['c_quat'])
+    centre, c2w = scenes.orbit_camera(0, 4)
+    o, d = scenes.camera_rays(centre, c2w, 64, 64, 50.0, order=scenes.tile_order(64, 64))
+    sel = np.arange(0, 64 * 64, 64)  # 64 rays spread over the image
+    o, d = o[sel].contiguous(), d[sel].contiguous()
+    near, _, far = ref_render.ray_bounds(o, d, 0.02, 4.0)
+    start = np.full(len(o), ref_sites.nearest_sites(pts, centre[None])[0], dtype=np.int32)
+    g = torch.Generator().manual_seed(11)
+    g_rgb, g_T = torch.randn(len(o), 3, generator=g), torch.randn(len(o), generator=g)
+    p32 = pts.astype(np.float32)
+    # starting cell: nearest site of x(near) (what the walk from the camera site reaches)
+    x0 = o.double().numpy() + near.double().numpy()[:, None] * d.double().numpy()
+    cells0 = cKDTree(p32.astype(np.float64)).query(x0)[1]
+    ref = foam_reference(p32.astype(np.float64), offsets, adj, prm['raw'].numpy(), dA.numpy(), cA.numpy(),
+                         prm['sh'].numpy(), o.numpy(), d.numpy(), near.numpy(), far.numpy(), g_rgb.numpy(),
+                         g_T.numpy(), cells0=cells0, sh_deg=1)
+    ref['ref_g_sh'] = ref['ref_g_sh'][:, :4]
+    sparse = {}
+    for key in ('ref_g_raw', 'ref_g_dA', 'ref_g_cA', 'ref_g_sh'):
+        gk = ref.pop(key)
+        rows = np.nonzero(np.abs(gk.reshape(len(gk), -1)).sum(1))[0].astype(np.int32)
+        sparse[key + '_rows'] = rows
+        sparse[key + '_vals'] = gk[rows].astype(np.float32)
+    np.savez_compressed(os.path.join(HERE, 'foam_config1.npz'), sel=sel, start=start, o=o.numpy(), d=d.numpy(),
+                        near=near.numpy(), far=far.numpy(), g_rgb=g_rgb.numpy(), g_T=g_T.numpy(),
+                        n_sites=len(pts), n_adj=len(adj), **ref, **sparse)
+
+
+if __name__ == '__main__':
+    make_sh_basis()
+    make_conic()
+    make_foam_small()
+    make_march_small()
+    make_foam_config1()
+    print('fixtures written to', HERE)

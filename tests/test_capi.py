@@ -1,0 +1,71 @@
+"""The C ABI (include/vgb200.h) without a GPU: the in-tree library loads, exports every declared entry
+point, and rejects bad arguments on the host with the reference's error categories."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, 'include', 'vgb200.h')
+
+
+def declared():
+    src = open(HEADER).read()
+    src = re.sub(r'/\*.*?\*/', '', src, flags=re.S)
+    return sorted(set(re.findall(r'\b(vg_\w+)\s*\(', src)))
+
+
+@pytest.fixture(scope='module')
+def lib():
+    from voronoi_gauss_b200 import _lib
+    if not os.path.exists(_lib.LIB_PATH):
+        from voronoi_gauss_b200 import build
+        build.build()
+    return _lib.lib()
+
+
+def test_library_exports_every_declared_symbol(lib):
+    names = declared()
+    assert len(names) >= 14
+    for n in names:
+        assert hasattr(lib, n), n
+
+
+def test_python_signatures_cover_the_header():
+    from voronoi_gauss_b200 import _lib
+    assert sorted(_lib.SIGNATURES) == declared()
+
+
+def test_version(lib):
+    assert lib.vg_version() == 100
+
+
+def test_host_side_argument_errors(lib):
+    """Null scene / bad degree / workspace too small are rejected before any device work."""
+    null = None
+    rc = lib.vg_foam_forward(null, 10, 10, null, null, null, null, 3, null, null, null, null, null, 0, 1e-4, 1e-4, 0,
+                             null, null, null, null, null, null, 0, null)
+    assert rc == 1 and b'graph pack is null' in lib.vg_last_error()
+    buf = ctypes.create_string_buffer(64)
+    p = ctypes.addressof(buf)
+    rc = lib.vg_foam_forward(p, 10, 10, p, p, p, p, 4, p, p, p, p, p, 1, 1e-4, 1e-4, 0, p, p, p, p, null, p, 0, null)
+    assert rc == 1 and b'sh_deg' in lib.vg_last_error()
+    rc = lib.vg_foam_forward(p, 10, 10, p, p, p, p, 3, p, p, p, p, p, 1, 1e-4, 1e-4, -1, p, p, p, p, null, p, 0, null)
+    assert rc == 1 and b'record_cap' in lib.vg_last_error()
+    rc = lib.vg_foam_infer(p, p, p, p, p, p, 0, 3, 10, 20, p, p, p, p, p, 1, 1e-4, 1e-4, 1.0, 5, 2, null, null, p, p, p,
+                           p, null)
+    assert rc == 1 and b'color_mode' in lib.vg_last_error()
+    rc = lib.vg_conic_forward(null, null, -1, 0.0, null, null)
+    assert rc == 1
+
+
+def test_python_layer_rejects_cpu_tensors():
+    """ext raises the reference's CHECK_INPUT messages (foam.cu:34-37) before touching the library."""
+    import torch
+    from voronoi_gauss_b200 import ext
+    x = torch.zeros(4, 3)
+    with pytest.raises(RuntimeError, match='must be a CUDA tensor'):
+        ext.extension().conic_forward(x, torch.zeros(4, 4), 0.0)

@@ -1,0 +1,74 @@
+"""ctypes binding of libvgb200.so (include/vgb200.h).
+
+The library is built in-tree by ``python -m voronoi_gauss_b200.build`` (or ``__graft_entry__.build()``).
+There is no fallback: every render call goes through this library, and a missing or unloadable
+library raises at the first call.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, '_lib', 'libvgb200.so')
+
+_lib = None
+
+P = ctypes.c_void_p
+I64 = ctypes.c_int64
+I32 = ctypes.c_int
+F32 = ctypes.c_float
+F64 = ctypes.c_double
+SZ = ctypes.c_size_t
+
+# entry point -> (restype, argtypes); mirrors include/vgb200.h
+SIGNATURES = {
+    'vg_version': (I32, []),
+    'vg_last_error': (ctypes.c_char_p, []),
+    'vg_status': (I32, [P]),
+    'vg_status_reset': (I32, []),
+    'vg_graph_pack_bytes': (SZ, [I64, I64]),
+    'vg_graph_pack': (I32, [P, P, P, I64, I64, P, SZ, P]),
+    'vg_foam_workspace_bytes': (SZ, [I64, I32, I32]),
+    'vg_foam_forward': (I32, [P, I64, I64, P, P, P, P, I32, P, P, P, P, P, I64, F32, F32, I32, P, P, P, P, P, P, SZ,
+                              P]),
+    'vg_foam_backward': (I32, [P, I64, I64, P, P, P, P, I32, P, P, P, P, P, I64, F32, F32, P, P, P, P, P, I32, P, P, P,
+                               P, P, P, SZ, P]),
+    'vg_foam_backward_packed': (I32, [P, I64, I64, P, P, P, P, I32, P, P, P, P, P, I64, F32, F32, P, P, P, P, P, I32,
+                                      P, P, I32, P, SZ, P]),
+    'vg_grad_unpack': (I32, [P, I64, I64, P, I32, P, P, P, P, P]),
+    'vg_march_forward': (I32, [P, I64, I64, P, P, P, P, I32, P, P, P, P, P, P, I64, F32, I32, F32, F32, P, P, P, P, P,
+                               SZ, P]),
+    'vg_march_backward': (I32, [P, I64, I64, P, P, P, P, I32, P, P, P, P, P, P, I64, F32, I32, F32, F32, P, P, P, P,
+                                P, P, P, P, P, SZ, P]),
+    'vg_conic_forward': (I32, [P, P, I64, F64, P, P]),
+    'vg_conic_backward': (I32, [P, P, I64, F64, P, P, P, P]),
+    'vg_foam_infer': (I32, [P, P, P, P, P, P, I32, I32, I64, I64, P, P, P, P, P, I64, F32, F32, F32, I32, I32, P, P, P,
+                            P, P, P, P]),
+}
+
+
+def lib():
+    """The loaded library (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f'{LIB_PATH} is missing: build it with `python -m voronoi_gauss_b200.build`')
+        handle = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype, fn.argtypes = res, args
+        _lib = handle
+    return _lib
+
+
+def check(rc, what):
+    if rc != 0:
+        msg = lib().vg_last_error().decode(errors='replace')
+        raise RuntimeError(f'{what}: {msg}')
+
+
+def call(name, *args):
+    """Calls entry point `name` and raises RuntimeError with the library's message on failure."""
+    check(getattr(lib(), name)(*args), name)

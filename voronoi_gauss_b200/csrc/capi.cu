@@ -1,0 +1,369 @@
+// extern "C" entry points of libvgb200 (declared in include/vgb200.h): argument checks with the
+// reference's error semantics, workspace carving and dispatch to the kernels.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/vgb200.h"
+#include "vg_common.cuh"
+
+namespace {
+
+thread_local std::string g_error;
+
+// status word of the render launches, one per device (module memory; addressed per device below)
+__device__ int g_status_word;
+constexpr int kMaxDevices = 64;
+int* g_status_ptr[kMaxDevices] = {};
+std::mutex g_status_mu;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(VG_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+int* status_ptr() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+    std::lock_guard<std::mutex> lock(g_status_mu);
+    if (g_status_ptr[dev] == nullptr) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_status_word) != cudaSuccess) return nullptr;
+        g_status_ptr[dev] = static_cast<int*>(p);
+    }
+    return g_status_ptr[dev];
+}
+
+inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+#define REQUIRE(cond, ...)                                   \
+    do {                                                     \
+        if (!(cond)) return fail(VG_ERR_INVALID_ARG, __VA_ARGS__); \
+    } while (0)
+
+int check_scene(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA, const float* cA,
+                const float* sh, int sh_deg) {
+    REQUIRE(pack != nullptr, "graph pack is null");
+    REQUIRE(n_sites > 0 && n_sites < INT32_MAX, "n_sites must be in [1, 2^31)");
+    REQUIRE(n_adj >= 0 && n_sites + n_adj < INT32_MAX, "adjacency too large for int32 offsets");
+    REQUIRE(raw && dA && cA && sh, "raw, dA, cA and sh must be non-null");
+    REQUIRE(sh_deg >= 0 && sh_deg <= 3, "sh_deg must be in 0..3");
+    return VG_OK;
+}
+
+int check_rays(int64_t n_rays, const float* o, const float* d, const int32_t* start, const float* near,
+               const float* far) {
+    REQUIRE(n_rays >= 0, "n_rays must be >= 0");
+    REQUIRE(n_rays == 0 || (o && d && start && near && far), "ray arrays must be non-null");
+    return VG_OK;
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+// Vector loads / stores of the kernels: conics and their gradients as float2, SH rows as float4,
+// records as float4.
+int check_alignment(const float* dA, const float* cA, const float* sh, const float* rec) {
+    REQUIRE(aligned(dA, 8) && aligned(cA, 8), "conics must be 8-byte aligned");
+    REQUIRE(aligned(sh, 16), "sh must be 16-byte aligned");
+    REQUIRE(rec == nullptr || aligned(rec, 16), "rec must be 16-byte aligned");
+    return VG_OK;
+}
+
+size_t field_ws(int64_t n, int deg) { return align256(vg::field_bytes(n, deg)); }
+size_t grad_ws(int64_t n) { return align256(static_cast<size_t>(n) * vg::kGradStride * sizeof(float)); }
+
+}  // namespace
+
+extern "C" {
+
+int vg_version(void) { return 100; }
+
+const char* vg_last_error(void) { return g_error.c_str(); }
+
+int vg_status(int* bits) {
+    REQUIRE(bits != nullptr, "bits is null");
+    int* p = status_ptr();
+    if (p == nullptr) return fail(VG_ERR_CUDA, "status word unavailable");
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e, "vg_status");
+    e = cudaMemcpy(bits, p, sizeof(int), cudaMemcpyDeviceToHost);
+    return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_status");
+}
+
+int vg_status_reset(void) {
+    int* p = status_ptr();
+    if (p == nullptr) return fail(VG_ERR_CUDA, "status word unavailable");
+    const cudaError_t e = cudaMemset(p, 0, sizeof(int));
+    return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_status_reset");
+}
+
+size_t vg_graph_pack_bytes(int64_t n_sites, int64_t n_adj) {
+    if (n_sites <= 0 || n_adj < 0) return 0;
+    return vg::graph_pack_bytes(n_sites, n_adj);
+}
+
+int vg_graph_pack(const float* points, const int32_t* offsets, const int32_t* adj, int64_t n_sites, int64_t n_adj,
+                  void* pack, size_t pack_bytes, void* stream) {
+    REQUIRE(points && offsets && pack, "points, offsets and pack must be non-null");
+    REQUIRE(n_adj == 0 || adj != nullptr, "adj is null");
+    REQUIRE(n_sites > 0 && n_sites < INT32_MAX, "n_sites must be in [1, 2^31)");
+    REQUIRE(n_adj >= 0 && n_sites + n_adj < INT32_MAX, "adjacency too large for int32 offsets");
+    REQUIRE((reinterpret_cast<uintptr_t>(pack) & 255) == 0, "pack must be 256-byte aligned");
+    const size_t need = vg::graph_pack_bytes(n_sites, n_adj);
+    if (pack_bytes < need) return fail(VG_ERR_WORKSPACE, "graph pack needs %zu bytes, got %zu", need, pack_bytes);
+    const cudaError_t e = vg::graph_pack(points, offsets, adj, n_sites, n_adj, pack, pack_bytes,
+                                         static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_graph_pack");
+}
+
+size_t vg_foam_workspace_bytes(int64_t n_sites, int sh_deg, int backward) {
+    if (n_sites <= 0 || sh_deg < 0 || sh_deg > 3) return 0;
+    return field_ws(n_sites, sh_deg) + (backward ? grad_ws(n_sites) : 0);
+}
+
+int vg_foam_forward(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA,
+                    const float* cA, const float* sh, int sh_deg, const float* o, const float* d,
+                    const int32_t* start, const float* near, const float* far, int64_t n_rays, float t_thresh,
+                    float w_thresh, int record_cap, float* rgb, float* T, float* depth, int32_t* stats, float* rec,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+    int rc = check_scene(pack, n_sites, n_adj, raw, dA, cA, sh, sh_deg);
+    if (rc) return rc;
+    if ((rc = check_rays(n_rays, o, d, start, near, far))) return rc;
+    REQUIRE(record_cap >= 0, "record_cap must be >= 0");
+    REQUIRE(n_rays == 0 || (rgb && T && depth && stats), "outputs must be non-null");
+    REQUIRE(record_cap == 0 || n_rays == 0 || rec != nullptr, "rec is null with record_cap > 0");
+    if ((rc = check_alignment(dA, cA, sh, record_cap > 0 ? rec : nullptr))) return rc;
+    REQUIRE(aligned(workspace, 256), "workspace must be 256-byte aligned");
+    const size_t need = field_ws(n_sites, sh_deg);
+    if (workspace_bytes < need || workspace == nullptr)
+        return fail(VG_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);
+    if (n_rays == 0) return VG_OK;
+    int* status = status_ptr();
+    if (status == nullptr) return fail(VG_ERR_CUDA, "status word unavailable");
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const vg::GraphView g = vg::graph_view(pack, n_sites, n_adj);
+    cudaError_t e = vg::field_pack(g, raw, dA, cA, sh, sh_deg, workspace, st);
+    if (e != cudaSuccess) return cuda_fail(e, "field pack");
+    const vg::FieldView F = vg::field_view(workspace, n_sites, sh_deg);
+    const vg::RayView R{o, d, start, near, nullptr, far, n_rays};
+    const vg::FoamCfg c{t_thresh, w_thresh, record_cap};
+    const vg::Outputs out{rgb, T, depth, stats, record_cap > 0 ? rec : nullptr};
+    e = vg::foam_forward(g, F, R, c, out, status, st);
+    return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_foam_forward");
+}
+
+static int foam_backward_impl(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA,
+                              const float* cA, const float* sh, int sh_deg, const float* o, const float* d,
+                              const int32_t* start, const float* near, const float* far, int64_t n_rays,
+                              float t_thresh, float w_thresh, const float* rgb, const float* T, const float* g_rgb,
+                              const float* g_T, const float* rec, int record_cap, const int32_t* stats, float* grad,
+                              bool zero_first, void* workspace, size_t workspace_bytes, size_t need,
+                              cudaStream_t st) {
+    int rc = check_scene(pack, n_sites, n_adj, raw, dA, cA, sh, sh_deg);
+    if (rc) return rc;
+    if ((rc = check_rays(n_rays, o, d, start, near, far))) return rc;
+    REQUIRE(record_cap >= 0, "record_cap must be >= 0");
+    REQUIRE(n_rays == 0 || (rgb && T && g_rgb && g_T && stats), "rgb, T, g_rgb, g_T and stats must be non-null");
+    if ((rc = check_alignment(dA, cA, sh, record_cap > 0 ? rec : nullptr))) return rc;
+    REQUIRE(aligned(workspace, 256), "workspace must be 256-byte aligned");
+    if (workspace_bytes < need || workspace == nullptr)
+        return fail(VG_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);
+    int* status = status_ptr();
+    if (status == nullptr) return fail(VG_ERR_CUDA, "status word unavailable");
+    cudaError_t e = cudaSuccess;
+    if (zero_first) {
+        e = cudaMemsetAsync(grad, 0, static_cast<size_t>(n_sites) * vg::kGradStride * sizeof(float), st);
+        if (e != cudaSuccess) return cuda_fail(e, "zero gradients");
+    }
+    if (n_rays == 0) return VG_OK;
+    const vg::GraphView g = vg::graph_view(pack, n_sites, n_adj);
+    e = vg::field_pack(g, raw, dA, cA, sh, sh_deg, workspace, st);
+    if (e != cudaSuccess) return cuda_fail(e, "field pack");
+    const vg::FieldView F = vg::field_view(workspace, n_sites, sh_deg);
+    const vg::RayView R{o, d, start, near, nullptr, far, n_rays};
+    const vg::FoamCfg c{t_thresh, w_thresh, record_cap};
+    const vg::GradIn gi{rgb, T, g_rgb, g_T, record_cap > 0 ? rec : nullptr, stats, record_cap};
+    e = vg::foam_backward(g, F, R, c, gi, grad, status, st);
+    return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_foam_backward");
+}
+
+int vg_foam_backward(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA,
+                     const float* cA, const float* sh, int sh_deg, const float* o, const float* d,
+                     const int32_t* start, const float* near, const float* far, int64_t n_rays, float t_thresh,
+                     float w_thresh, const float* rgb, const float* T, const float* g_rgb, const float* g_T,
+                     const float* rec, int record_cap, const int32_t* stats, float* g_raw, float* g_dA, float* g_cA,
+                     float* g_sh, void* workspace, size_t workspace_bytes, void* stream) {
+    REQUIRE(g_raw && g_dA && g_cA && g_sh, "gradient outputs must be non-null");
+    REQUIRE(aligned(g_dA, 8) && aligned(g_cA, 8) && aligned(g_sh, 16), "gradient outputs misaligned");
+    if (sh_deg < 0 || sh_deg > 3) return fail(VG_ERR_INVALID_ARG, "sh_deg must be in 0..3");
+    const size_t need = vg_foam_workspace_bytes(n_sites, sh_deg, 1);
+    float* grad = reinterpret_cast<float*>(static_cast<char*>(workspace) + field_ws(n_sites, sh_deg));
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int rc = foam_backward_impl(pack, n_sites, n_adj, raw, dA, cA, sh, sh_deg, o, d, start, near, far, n_rays,
+                                t_thresh, w_thresh, rgb, T, g_rgb, g_T, rec, record_cap, stats, grad, true, workspace,
+                                workspace_bytes, need, st);
+    if (rc) return rc;
+    const cudaError_t e =
+        vg::grad_unpack(vg::graph_view(pack, n_sites, n_adj), grad, sh_deg, g_raw, g_dA, g_cA, g_sh, st);
+    return e == cudaSuccess ? VG_OK : cuda_fail(e, "gradient unpack");
+}
+
+int vg_foam_backward_packed(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA,
+                            const float* cA, const float* sh, int sh_deg, const float* o, const float* d,
+                            const int32_t* start, const float* near, const float* far, int64_t n_rays, float t_thresh,
+                            float w_thresh, const float* rgb, const float* T, const float* g_rgb, const float* g_T,
+                            const float* rec, int record_cap, const int32_t* stats, float* grad_pack, int zero_first,
+                            void* workspace, size_t workspace_bytes, void* stream) {
+    REQUIRE(grad_pack != nullptr, "grad_pack is null");
+    REQUIRE((reinterpret_cast<uintptr_t>(grad_pack) & 15) == 0, "grad_pack must be 16-byte aligned");
+    if (sh_deg < 0 || sh_deg > 3) return fail(VG_ERR_INVALID_ARG, "sh_deg must be in 0..3");
+    return foam_backward_impl(pack, n_sites, n_adj, raw, dA, cA, sh, sh_deg, o, d, start, near, far, n_rays, t_thresh,
+                              w_thresh, rgb, T, g_rgb, g_T, rec, record_cap, stats, grad_pack, zero_first != 0,
+                              workspace, workspace_bytes, vg_foam_workspace_bytes(n_sites, sh_deg, 0),
+                              static_cast<cudaStream_t>(stream));
+}
+
+int vg_grad_unpack(const void* pack, int64_t n_sites, int64_t n_adj, const float* grad_pack, int sh_deg,
+                   float* g_raw, float* g_dA, float* g_cA, float* g_sh, void* stream) {
+    REQUIRE(pack && grad_pack && g_raw && g_dA && g_cA && g_sh, "arguments must be non-null");
+    REQUIRE(aligned(grad_pack, 16) && aligned(g_dA, 8) && aligned(g_cA, 8) && aligned(g_sh, 16),
+            "gradient arrays misaligned");
+    REQUIRE(n_sites > 0 && n_sites < INT32_MAX, "n_sites must be in [1, 2^31)");
+    REQUIRE(sh_deg >= 0 && sh_deg <= 3, "sh_deg must be in 0..3");
+    const cudaError_t e = vg::grad_unpack(vg::graph_view(pack, n_sites, n_adj), grad_pack, sh_deg, g_raw, g_dA, g_cA,
+                                          g_sh, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_grad_unpack");
+}
+
+int vg_march_forward(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA,
+                     const float* cA, const float* sh, int sh_deg, const float* o, const float* d,
+                     const int32_t* start, const float* near, const float* mid, const float* far, int64_t n_rays,
+                     float dt, int n_bg, float t_thresh, float w_thresh, float* rgb, float* T, float* depth,
+                     int32_t* stats, void* workspace, size_t workspace_bytes, void* stream) {
+    int rc = check_scene(pack, n_sites, n_adj, raw, dA, cA, sh, sh_deg);
+    if (rc) return rc;
+    if ((rc = check_rays(n_rays, o, d, start, near, far))) return rc;
+    REQUIRE(n_rays == 0 || mid != nullptr, "mid is null");
+    REQUIRE(n_rays == 0 || (rgb && T && depth && stats), "outputs must be non-null");
+    REQUIRE(n_bg >= 0, "n_bg must be >= 0");
+    if ((rc = check_alignment(dA, cA, sh, nullptr))) return rc;
+    REQUIRE(aligned(workspace, 256), "workspace must be 256-byte aligned");
+    const size_t need = field_ws(n_sites, sh_deg);
+    if (workspace_bytes < need || workspace == nullptr)
+        return fail(VG_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);
+    if (n_rays == 0) return VG_OK;
+    int* status = status_ptr();
+    if (status == nullptr) return fail(VG_ERR_CUDA, "status word unavailable");
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const vg::GraphView g = vg::graph_view(pack, n_sites, n_adj);
+    cudaError_t e = vg::field_pack(g, raw, dA, cA, sh, sh_deg, workspace, st);
+    if (e != cudaSuccess) return cuda_fail(e, "field pack");
+    const vg::FieldView F = vg::field_view(workspace, n_sites, sh_deg);
+    const vg::RayView R{o, d, start, near, mid, far, n_rays};
+    const vg::MarchCfg c{dt, n_bg, t_thresh, w_thresh};
+    const vg::Outputs out{rgb, T, depth, stats, nullptr};
+    e = vg::march_forward(g, F, R, c, out, status, st);
+    return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_march_forward");
+}
+
+int vg_march_backward(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA,
+                      const float* cA, const float* sh, int sh_deg, const float* o, const float* d,
+                      const int32_t* start, const float* near, const float* mid, const float* far, int64_t n_rays,
+                      float dt, int n_bg, float t_thresh, float w_thresh, const float* rgb, const float* T,
+                      const float* g_rgb, const float* g_T, float* g_raw, float* g_dA, float* g_cA, float* g_sh,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+    int rc = check_scene(pack, n_sites, n_adj, raw, dA, cA, sh, sh_deg);
+    if (rc) return rc;
+    if ((rc = check_rays(n_rays, o, d, start, near, far))) return rc;
+    REQUIRE(n_rays == 0 || mid != nullptr, "mid is null");
+    REQUIRE(n_rays == 0 || (rgb && T && g_rgb && g_T), "rgb, T, g_rgb and g_T must be non-null");
+    REQUIRE(g_raw && g_dA && g_cA && g_sh, "gradient outputs must be non-null");
+    REQUIRE(n_bg >= 0, "n_bg must be >= 0");
+    if ((rc = check_alignment(dA, cA, sh, nullptr))) return rc;
+    REQUIRE(aligned(workspace, 256), "workspace must be 256-byte aligned");
+    REQUIRE(aligned(g_dA, 8) && aligned(g_cA, 8) && aligned(g_sh, 16), "gradient outputs misaligned");
+    const size_t need = vg_foam_workspace_bytes(n_sites, sh_deg, 1);
+    if (workspace_bytes < need || workspace == nullptr)
+        return fail(VG_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);
+    int* status = status_ptr();
+    if (status == nullptr) return fail(VG_ERR_CUDA, "status word unavailable");
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const vg::GraphView g = vg::graph_view(pack, n_sites, n_adj);
+    float* grad = reinterpret_cast<float*>(static_cast<char*>(workspace) + field_ws(n_sites, sh_deg));
+    cudaError_t e = cudaMemsetAsync(grad, 0, static_cast<size_t>(n_sites) * vg::kGradStride * sizeof(float), st);
+    if (e != cudaSuccess) return cuda_fail(e, "zero gradients");
+    if (n_rays > 0) {
+        e = vg::field_pack(g, raw, dA, cA, sh, sh_deg, workspace, st);
+        if (e != cudaSuccess) return cuda_fail(e, "field pack");
+        const vg::FieldView F = vg::field_view(workspace, n_sites, sh_deg);
+        const vg::RayView R{o, d, start, near, mid, far, n_rays};
+        const vg::MarchCfg c{dt, n_bg, t_thresh, w_thresh};
+        const vg::GradIn gi{rgb, T, g_rgb, g_T, nullptr, nullptr, 0};
+        e = vg::march_backward(g, F, R, c, gi, grad, status, st);
+        if (e != cudaSuccess) return cuda_fail(e, "vg_march_backward");
+    }
+    e = vg::grad_unpack(g, grad, sh_deg, g_raw, g_dA, g_cA, g_sh, st);
+    return e == cudaSuccess ? VG_OK : cuda_fail(e, "gradient unpack");
+}
+
+int vg_conic_forward(const float* log_scale, const float* quat, int64_t n, double floor, float* A, void* stream) {
+    REQUIRE(n >= 0, "n must be >= 0");
+    REQUIRE(n == 0 || (log_scale && quat && A), "arguments must be non-null");
+    REQUIRE(aligned(quat, 16) && aligned(A, 8), "quat must be 16-byte and A 8-byte aligned");
+    const cudaError_t e = vg::conic_forward(log_scale, quat, n, static_cast<float>(floor * floor), A,
+                                            static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_conic_forward");
+}
+
+int vg_conic_backward(const float* log_scale, const float* quat, int64_t n, double floor, const float* gA,
+                      float* g_ls, float* g_quat, void* stream) {
+    REQUIRE(n >= 0, "n must be >= 0");
+    REQUIRE(n == 0 || (log_scale && quat && gA && g_ls && g_quat), "arguments must be non-null");
+    REQUIRE(aligned(quat, 16) && aligned(gA, 8) && aligned(g_quat, 16), "conic arrays misaligned");
+    const cudaError_t e = vg::conic_backward(log_scale, quat, n, static_cast<float>(floor * floor), gA, g_ls, g_quat,
+                                             static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_conic_backward");
+}
+
+int vg_foam_infer(const float* points, const int32_t* offsets, const int32_t* nbr, const float* edge,
+                  const float* attr, const void* sh, int sh_half, int sh_deg, int64_t n_sites, int64_t n_edges,
+                  const float* o, const float* d, const int32_t* start, const float* near, const float* far,
+                  int64_t n_rays, float t_thresh, float w_thresh, float color_cut, int color_mode, int stage,
+                  const int32_t* cap, const int32_t* orig, float* rgb, float* T, float* depth, int32_t* stats,
+                  void* stream) {
+    REQUIRE(points && offsets && nbr && edge && attr, "pack arrays must be non-null");
+    REQUIRE(n_sites > 0 && n_sites < INT32_MAX && n_edges >= n_sites && n_edges < INT32_MAX, "bad pack sizes");
+    REQUIRE(color_mode >= 0 && color_mode <= 2, "color_mode must be 0 (lazy), 1 (baked) or 2 (fused)");
+    REQUIRE(stage >= 0 && stage <= 2, "stage must be 0, 1 or 2");
+    REQUIRE(sh_deg >= 0 && sh_deg <= 3, "sh_deg must be in 0..3");
+    REQUIRE(color_mode == 1 || stage < 2 || sh != nullptr, "sh must be (N, 16, 3)");
+    REQUIRE(aligned(points, 16) && aligned(edge, 16) && aligned(attr, 16) && aligned(sh, 16),
+            "points, edge, attr and sh must be 16-byte aligned");
+    int rc = check_rays(n_rays, o, d, start, near, far);
+    if (rc) return rc;
+    REQUIRE(n_rays == 0 || (rgb && T && depth && stats), "outputs must be non-null");
+    if (n_rays == 0) return VG_OK;
+    int* status = status_ptr();
+    if (status == nullptr) return fail(VG_ERR_CUDA, "status word unavailable");
+    const vg::InferNet N{reinterpret_cast<const float4*>(points), offsets, nbr, reinterpret_cast<const float4*>(edge),
+                         reinterpret_cast<const float4*>(attr), sh, orig, sh_half};
+    const vg::InferCfg c{t_thresh, w_thresh, color_cut, sh_deg, color_mode, stage, cap};
+    const vg::RayView R{o, d, start, near, nullptr, far, n_rays};
+    const vg::Outputs out{rgb, T, depth, stats, nullptr};
+    const cudaError_t e = vg::foam_infer(N, c, R, out, status, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_foam_infer");
+}
+
+}  // extern "C"

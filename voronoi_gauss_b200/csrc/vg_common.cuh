@@ -1,0 +1,298 @@
+// Shared device code of the B200 Voronoi-Gaussian renderer (sm_100a).
+//
+// Data layout in HBM (built by pack.cu, read by foam.cu / march.cu):
+//
+//   graph pack (once per scene graph; sites renumbered along a 30-bit Morton curve)
+//     perm  (N)      internal id -> original id (ties are broken on original ids, as the reference)
+//     inv   (N)      original id -> internal id
+//     off   (N + 1)  self-first CSR offsets, internal order
+//     edge  (N + M)  float4 (p_j.x, p_j.y, p_j.z, bits(internal j)); the first edge of a cell is the
+//                    cell's own site, so one pass over 16-byte records gives the site, its Delaunay
+//                    neighbours and their positions (exit faces, walks and neighbourhood sums)
+//   field pack (per call, internal order)
+//     rec   (N, 4) float4: (dA xx, xy, xz, yy), (dA yz, zz, min(raw, 30), 0),
+//                          (cA xx, xy, xz, yy), (cA yz, zz, 0, 0)          64 B per site
+//     sh    (N, S4) float4: the 3 (sh_deg + 1)^2 used SH coefficients, channel-interleaved as in the
+//                           reference (coefficient j, channel c at 3 j + c), zero-padded to float4
+//   gradient pack (backward, internal order; summed with vector atomics and, across GPUs, NCCL)
+//     grad  (N, 64) float: g_raw, g_dA[6], 0 | g_cA[6], 0, 0 | g_sh[48]   256 B per site
+//
+// Arithmetic that decides which cells a ray visits (walk distances, exit-face parameters, sample
+// positions) uses explicit round-to-nearest intrinsics in the order nvcc contracts the reference's
+// source (a0 b0 + a1 b1 + a2 b2 -> fma(a2, b2, fma(a0, b0, a1 b1)), o + t d -> fma(t, d, o)), so the
+// cell sequences do not depend on this compiler's contraction choices.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <climits>
+#include <cstdint>
+
+namespace vg {
+
+constexpr float kInf = 3.402823466e38f;  // largest finite float: "no exit face yet" (foam.cu:27)
+constexpr int kWalkCap = 4096;           // greedy walk steps per query (foam.cu:29)
+constexpr int kMaxCells = 8192;          // cells per ray (foam.cu:30)
+constexpr float kMinWeight = 1e-7f;      // normalised colour weights below get no gradient (foam.cu:31)
+constexpr int kRecord = 8;               // floats per recorded sample (foam.cu:274)
+constexpr int kGradStride = 64;          // floats per site in the gradient pack
+constexpr int kFieldVec = 4;             // float4 per site in the field pack
+
+// error bits written to the status word of a launch
+constexpr int kErrWalkCap = 1;   // a greedy walk hit kWalkCap
+constexpr int kErrCellCap = 2;   // a ray hit kMaxCells
+
+inline __host__ __device__ int sh_coeffs(int deg) { return (deg + 1) * (deg + 1); }
+inline __host__ __device__ int sh_vec4(int deg) { return (3 * sh_coeffs(deg) + 3) / 4; }
+
+struct GraphView {
+    const int* perm;
+    const int* inv;
+    const int* off;
+    const float4* edge;
+    int n;
+};
+
+struct FieldView {
+    const float4* rec;  // (N, 4)
+    const float4* sh;   // (N, S4)
+    int sh_deg;
+    int s4;
+};
+
+// ------------------------------------------------------------------------------------- arithmetic
+
+__device__ __forceinline__ float dot3c(float a0, float a1, float a2, float b0, float b1, float b2) {
+    return __fmaf_rn(a2, b2, __fmaf_rn(a0, b0, __fmul_rn(a1, b1)));
+}
+
+__device__ __forceinline__ float along(float o, float t, float d) { return __fmaf_rn(t, d, o); }
+
+// v^T A v of a conic stored (xx, xy, xz, yy) | (yz, zz, ., .) (foam.cu:101-105).
+__device__ __forceinline__ float maha(const float4& a, const float4& b, float v0, float v1, float v2) {
+    return a.x * v0 * v0 + a.w * v1 * v1 + b.y * v2 * v2 + 2.f * (a.y * v0 * v1 + a.z * v0 * v2 + b.x * v1 * v2);
+}
+
+// Real SH basis with the constants and signs of the reference (foam.cu:118-141).
+__device__ __forceinline__ void sh_basis(float x, float y, float z, int deg, float (&b)[16]) {
+    b[0] = 0.28209479177387814f;
+#pragma unroll
+    for (int i = 1; i < 16; ++i) b[i] = 0.f;
+    if (deg < 1) return;
+    b[1] = -0.4886025119029199f * y;
+    b[2] = 0.4886025119029199f * z;
+    b[3] = -0.4886025119029199f * x;
+    if (deg < 2) return;
+    const float xx = x * x, yy = y * y, zz = z * z;
+    b[4] = 1.0925484305920792f * x * y;
+    b[5] = -1.0925484305920792f * y * z;
+    b[6] = 0.31539156525252005f * (2.f * zz - xx - yy);
+    b[7] = -1.0925484305920792f * x * z;
+    b[8] = 0.5462742152960396f * (xx - yy);
+    if (deg < 3) return;
+    b[9] = -0.5900435899266435f * y * (3.f * xx - yy);
+    b[10] = 2.890611442640554f * x * y * z;
+    b[11] = -0.4570457994644658f * y * (4.f * zz - xx - yy);
+    b[12] = 0.3731763325901154f * z * (2.f * zz - 3.f * xx - 3.f * yy);
+    b[13] = -0.4570457994644658f * x * (4.f * zz - xx - yy);
+    b[14] = 1.445305721320277f * z * (xx - yy);
+    b[15] = -0.5900435899266435f * x * (xx - 3.f * yy);
+}
+
+// SH_k(d) + 1/2 per channel (unclamped) from the packed coefficients of site k.
+__device__ __forceinline__ void sh_color(const FieldView& F, int k, const float (&b)[16], float (&c)[3]) {
+    c[0] = c[1] = c[2] = 0.5f;
+    const float4* s = F.sh + static_cast<int64_t>(F.s4) * k;
+#pragma unroll
+    for (int q = 0; q < 12; ++q) {
+        if (q >= F.s4) break;
+        const float4 v = __ldg(s + q);
+        const float f[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int i = 4 * q + u;
+            if (i < 48) c[i % 3] += b[i / 3] * f[u];
+        }
+    }
+}
+
+__device__ __forceinline__ int site_of(const float4& e) { return __float_as_int(e.w); }
+
+// (t, k) precedes (bt, bk) with ties broken by the smaller original index.
+__device__ __forceinline__ bool better(float t, int k, float bt, int bk, const int* __restrict__ perm) {
+    if (t < bt) return true;
+    if (t == bt) return bk < 0 || __ldg(perm + k) < __ldg(perm + bk);
+    return false;
+}
+
+// Greedy walk on the packed graph to the nearest site of x, ties to the smaller original index
+// (foam.cu:163-181): each step moves to the neighbour minimising (|x - p|^2, original id).
+__device__ __forceinline__ int walk_to(const GraphView& g, int cur, float x0, float x1, float x2, int& steps,
+                                       int& err) {
+    for (int it = 0; it < kWalkCap; ++it) {
+        const int e0 = __ldg(g.off + cur), e1 = __ldg(g.off + cur + 1);
+        float bd = kInf;
+        int bk = -1;
+        for (int e = e0; e < e1; ++e) {
+            const float4 E = __ldg(g.edge + e);
+            const float v0 = __fsub_rn(x0, E.x), v1 = __fsub_rn(x1, E.y), v2 = __fsub_rn(x2, E.z);
+            const float dk = dot3c(v0, v1, v2, v0, v1, v2);
+            const int k = site_of(E);
+            if (better(dk, k, bd, bk, g.perm)) bd = dk, bk = k;
+        }
+        if (bk == cur || bk < 0) return cur;
+        cur = bk;
+        ++steps;
+    }
+    err |= kErrWalkCap;
+    return cur;
+}
+
+// Exit-face candidate of cell c (site pc) through the face shared with neighbour E (foam.cu:191-205).
+__device__ __forceinline__ void exit_candidate(const float4& E, float pc0, float pc1, float pc2, const float (&o)[3],
+                                               const float (&d)[3], float& bt, int& bk, const int* __restrict__ perm) {
+    const float n0 = __fsub_rn(E.x, pc0), n1 = __fsub_rn(E.y, pc1), n2 = __fsub_rn(E.z, pc2);
+    const float dn = dot3c(n0, n1, n2, d[0], d[1], d[2]);
+    if (dn > 0.f) {
+        const float m0 = __fmaf_rn(0.5f, __fadd_rn(E.x, pc0), -o[0]);
+        const float m1 = __fmaf_rn(0.5f, __fadd_rn(E.y, pc1), -o[1]);
+        const float m2 = __fmaf_rn(0.5f, __fadd_rn(E.z, pc2), -o[2]);
+        const float t = __fdiv_rn(dot3c(m0, m1, m2, n0, n1, n2), dn);
+        const int k = site_of(E);
+        if (better(t, k, bt, bk, perm)) bt = t, bk = k;
+    }
+}
+
+// Online normalised blend sum_k a_k c_k / sum_k a_k, a_k = exp(-(m_k - m_min) / 2), keeping the
+// running minimum m (the same quantity as the reference's two passes, foam.cu:224-249).
+struct Blend {
+    float m, a, r, g, b;
+};
+
+__device__ __forceinline__ void blend_init(Blend& B) { B.m = kInf, B.a = B.r = B.g = B.b = 0.f; }
+
+__device__ __forceinline__ void blend_add(Blend& B, float m, float r, float g, float b) {
+    if (m < B.m) {
+        const float s = __expf(-0.5f * (B.m - m));
+        B.a *= s, B.r *= s, B.g *= s, B.b *= s, B.m = m;
+    }
+    const float w = __expf(-0.5f * (m - B.m));
+    B.a += w, B.r += w * r, B.g += w * g, B.b += w * b;
+}
+
+// Per-thread direct-mapped cache of the clamped site colours max(SH_k(d) + 1/2, 0) in shared memory:
+// a site belongs to the neighbourhoods of several consecutive cells of a ray and its colour depends
+// only on the ray direction. Slot s of thread t lives at base[s * stride + t].
+template <int SLOTS>
+struct ColorCache {
+    float4* base;
+    int stride;
+    __device__ __forceinline__ void init() {
+#pragma unroll
+        for (int s = 0; s < SLOTS; ++s) base[s * stride] = make_float4(0.f, 0.f, 0.f, __int_as_float(-1));
+    }
+    __device__ __forceinline__ void get(const FieldView& F, int k, const float (&b)[16], float (&c)[3]) {
+        float4& e = base[(k & (SLOTS - 1)) * stride];
+        const float4 v = e;
+        if (__float_as_int(v.w) == k) {
+            c[0] = v.x, c[1] = v.y, c[2] = v.z;
+            return;
+        }
+        sh_color(F, k, b, c);
+        c[0] = fmaxf(c[0], 0.f), c[1] = fmaxf(c[1], 0.f), c[2] = fmaxf(c[2], 0.f);
+        e = make_float4(c[0], c[1], c[2], __int_as_float(k));
+    }
+};
+
+// ------------------------------------------------------------------------------ host-side launchers
+
+struct RayView {
+    const float* o;
+    const float* d;
+    const int* start;  // original site ids
+    const float* near;
+    const float* mid;  // march only
+    const float* far;
+    int64_t n;
+};
+
+struct FoamCfg {
+    float t_thresh, w_thresh;
+    int record_cap;
+};
+
+struct MarchCfg {
+    float dt;
+    int n_bg;
+    float t_thresh, w_thresh;
+};
+
+struct Outputs {
+    float* rgb;
+    float* T;
+    float* depth;
+    int* stats;
+    float* rec;
+};
+
+struct GradIn {
+    const float* rgb;
+    const float* T;
+    const float* g_rgb;
+    const float* g_T;
+    const float* rec;
+    const int* stats;
+    int record_cap;
+};
+
+// pack.cu
+size_t graph_pack_bytes(int64_t n, int64_t m);
+cudaError_t graph_pack(const float* points, const int* offsets, const int* adj, int64_t n, int64_t m, void* pack,
+                       size_t bytes, cudaStream_t st);
+GraphView graph_view(const void* pack, int64_t n, int64_t m);
+size_t field_bytes(int64_t n, int sh_deg);
+cudaError_t field_pack(const GraphView& g, const float* raw, const float* dA, const float* cA, const float* sh,
+                       int sh_deg, void* field, cudaStream_t st);
+FieldView field_view(const void* field, int64_t n, int sh_deg);
+cudaError_t grad_unpack(const GraphView& g, const float* grad, int sh_deg, float* g_raw, float* g_dA, float* g_cA,
+                        float* g_sh, cudaStream_t st);
+
+// foam.cu
+cudaError_t foam_forward(const GraphView& g, const FieldView& F, const RayView& R, const FoamCfg& c,
+                         const Outputs& out, int* status, cudaStream_t st);
+cudaError_t foam_backward(const GraphView& g, const FieldView& F, const RayView& R, const FoamCfg& c,
+                          const GradIn& gi, float* grad, int* status, cudaStream_t st);
+
+// march.cu
+cudaError_t march_forward(const GraphView& g, const FieldView& F, const RayView& R, const MarchCfg& c,
+                          const Outputs& out, int* status, cudaStream_t st);
+cudaError_t march_backward(const GraphView& g, const FieldView& F, const RayView& R, const MarchCfg& c,
+                           const GradIn& gi, float* grad, int* status, cudaStream_t st);
+
+// conic.cu
+// floor2 = floor^2 rounded to float once (the reference passes static_cast<float>(floor * floor))
+cudaError_t conic_forward(const float* log_scale, const float* quat, int64_t n, float floor2, float* A,
+                          cudaStream_t st);
+cudaError_t conic_backward(const float* log_scale, const float* quat, int64_t n, float floor2, const float* gA,
+                           float* g_ls, float* g_quat, cudaStream_t st);
+
+// infer.cu
+struct InferNet {
+    const float4* points;
+    const int* offsets;
+    const int* nbr;
+    const float4* edge;
+    const float4* attr;
+    const void* sh;
+    const int* orig;
+    int sh_half;
+};
+struct InferCfg {
+    float t_thresh, w_thresh, color_cut;
+    int sh_deg, color_mode, stage;
+    const int* cap;
+};
+cudaError_t foam_infer(const InferNet& N, const InferCfg& c, const RayView& R, const Outputs& out, int* status,
+                       cudaStream_t st);
+
+}  // namespace vg

@@ -1,0 +1,61 @@
+"""Data-parallel rendering and training across the GPUs of one node (one process per GPU).
+
+Rays are independent, so rendering shards with no data-path communication: an image is cut into 16x16
+pixel tiles dealt round-robin to the ranks (``tile_pixels``), or every rank renders its own view. The
+scene (sites, adjacency, parameters) is replicated on every GPU. The one exchange step is in training:
+the per-site gradients of all ranks are summed before the (replicated) optimizer step, as one coalesced
+NCCL all-reduce over NVLink (``allreduce_grads``). The reference is single-GPU; this layer has no
+counterpart there.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+TILE = 16
+
+
+def tile_pixels(H, W, world, rank, tile=TILE):
+    """Pixel indices (row-major into H x W) of the tiles owned by `rank`: tile t (row-major over the tile
+    grid) belongs to rank t mod world; inside a rank, tiles keep their order and pixels are listed tile
+    by tile in 4 x 8 sub-tiles so that 32 consecutive rays cover a compact patch."""
+    ty, tx = (H + tile - 1) // tile, (W + tile - 1) // tile
+    tiles = np.arange(ty * tx)
+    mine = tiles[tiles % world == rank]
+    out = []
+    sy, sx = np.meshgrid(np.arange(tile), np.arange(tile), indexing='ij')
+    key = ((sy // 4) * (tile // 8) + sx // 8) * 32 + (sy % 4) * 8 + sx % 8
+    sub = np.argsort(key.ravel(), kind='stable')
+    sy, sx = sy.ravel()[sub], sx.ravel()[sub]
+    for t in mine:
+        y0, x0 = (t // tx) * tile, (t % tx) * tile
+        y, x = y0 + sy, x0 + sx
+        keep = (y < H) & (x < W)
+        out.append(y[keep] * W + x[keep])
+    return np.concatenate(out) if out else np.zeros(0, np.int64)
+
+
+def allreduce_grads(params, group=None):
+    """Sums the .grad of `params` over the ranks in one coalesced all-reduce (parameters without a
+    gradient contribute zeros). Every rank must call it with the same parameter list."""
+    grads = []
+    for p in params:
+        if p.grad is None:
+            p.grad = torch.zeros_like(p)
+        grads.append(p.grad)
+    if dist.get_world_size(group) == 1:
+        return
+    flat = torch._utils._flatten_dense_tensors(grads)
+    dist.all_reduce(flat, group=group)
+    for src, dst in zip(torch._utils._unflatten_dense_tensors(flat, grads), grads):
+        dst.copy_(src)
+
+
+def allreduce_max(values, device, group=None):
+    """Element-wise maximum over the ranks of a list of floats (timings: the slowest rank counts)."""
+    t = torch.tensor(values, dtype=torch.float64, device=device)
+    if dist.is_initialized() and dist.get_world_size(group) > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    return [float(x) for x in t]

@@ -1,0 +1,472 @@
+"""Drop-in replacement of the reference's extension module (voronoi-gauss ext.py) on libvgb200.
+
+Same public surface and contracts as ext.py:30-216:
+
+* ``Graph(points, offsets, adj)``: fixed sites and their CSR Delaunay adjacency on the GPU
+  (ext.py:46-52). The packed, Morton-ordered neighbourhoods used by the kernels are built on first use
+  and cached on the Graph.
+* ``foam(graph, raw, dA, cA, sh, sh_deg, o, d, start, near, far, t_thresh, w_thresh, record_cap)``
+  -> (rgb, T, depth, stats), autograd through raw / dA / cA / sh (ext.py:185-216);
+  ``march(...)`` (ext.py:152-182); ``conic(log_scale, quat, floor)`` (ext.py:120-136) and its torch twin
+  ``conic_reference`` (ext.py:139-149).
+* ``foam_extension()``, ``march_extension()``, ``extension()``, ``foam_infer_extension()`` return objects
+  with the reference's extension-level functions and signatures (foam.cu:560-565, march.cu:431-434,
+  vgf.cu:563-571 conic part, foam_infer.cu:437-440): tensors in, freshly allocated tensors out,
+  ``RuntimeError`` on a bad argument (the reference's TORCH_CHECK).
+
+Every call runs on the input's device and on torch's current stream of that device, asynchronously.
+"""
+
+from __future__ import annotations
+
+import weakref
+
+import torch
+
+from . import _lib
+
+__all__ = ['Graph', 'foam', 'march', 'conic', 'conic_reference', 'extension', 'march_extension', 'foam_extension',
+           'foam_infer_extension', 'GraphPack', 'graph_pack']
+
+
+# (start, end) CUDA events recorded on the launching stream around the foam backward launch while set
+# (used by bench.py to time the kernel inside a training step)
+BACKWARD_EVENTS = None
+
+
+def _ptr(t):
+    return None if t is None or t.numel() == 0 else t.data_ptr()
+
+
+def _stream(dev):
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _check(x, name, dtype):
+    """The reference's CHECK_INPUT (foam.cu:34-37)."""
+    if not x.is_cuda:
+        raise RuntimeError(f'{name} must be a CUDA tensor')
+    if not x.is_contiguous():
+        raise RuntimeError(f'{name} must be contiguous')
+    if x.dtype != dtype:
+        raise RuntimeError(f'{name} has the wrong dtype')
+
+
+# ----------------------------------------------------------------------------------- graph packs
+
+class GraphPack:
+    """Packed scene graph (vg_graph_pack) of (points, offsets, adj) on their device."""
+
+    def __init__(self, points, offsets, adj):
+        _check(points, 'points', torch.float32)
+        _check(offsets, 'offsets', torch.int32)
+        _check(adj, 'adj', torch.int32)
+        if points.dim() != 2 or points.size(1) != 3:
+            raise RuntimeError('points must be (N, 3)')
+        if offsets.numel() != points.size(0) + 1:
+            raise RuntimeError('offsets must be (N + 1)')
+        self.n, self.m = points.size(0), adj.numel()
+        self.device = points.device
+        nbytes = _lib.lib().vg_graph_pack_bytes(self.n, self.m)
+        self.buf = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+        with torch.cuda.device(self.device):
+            _lib.call('vg_graph_pack', points.data_ptr(), offsets.data_ptr(), _ptr(adj), self.n, self.m,
+                      self.buf.data_ptr(), nbytes, _stream(self.device))
+        self._src = tuple(weakref.ref(t) for t in (points, offsets, adj))
+        self._ver = tuple(t._version for t in (points, offsets, adj))
+
+    def matches(self, points, offsets, adj):
+        for ref, ver, t in zip(self._src, self._ver, (points, offsets, adj)):
+            if ref() is not t or t._version != ver:
+                return False
+        return True
+
+    @property
+    def ptr(self):
+        return self.buf.data_ptr()
+
+
+_PACKS: list = []
+
+
+def graph_pack(points, offsets, adj):
+    """Cached GraphPack of these exact tensors (rebuilt when one of them is modified in place)."""
+    for p in _PACKS:
+        if p.matches(points, offsets, adj):
+            return p
+    p = GraphPack(points, offsets, adj)
+    _PACKS.insert(0, p)
+    del _PACKS[4:]
+    return p
+
+
+class Graph:
+    """Fixed sites and their Delaunay adjacency (CSR, int32) on the GPU (ext.py:46-58)."""
+
+    def __init__(self, points, offsets, adj):
+        self.points = points.float().contiguous()
+        self.offsets = offsets.int().contiguous()
+        self.adj = adj.int().contiguous()
+        self._pack = None
+
+    @property
+    def pack(self):
+        if self._pack is None or not self._pack.matches(self.points, self.offsets, self.adj):
+            self._pack = graph_pack(self.points, self.offsets, self.adj)
+        return self._pack
+
+    def walk(self, o, d, z, start):
+        raise NotImplementedError('Graph.walk (the NeRF-sampler walk of vgf.cu) is not part of this build')
+
+
+# ------------------------------------------------------------------------- extension-level functions
+
+def _scene_checks(points, offsets, adj, raw, dA, cA, sh):
+    for x, name, dt in ((points, 'points', torch.float32), (offsets, 'offsets', torch.int32),
+                        (adj, 'adj', torch.int32), (raw, 'raw', torch.float32), (dA, 'dA', torch.float32),
+                        (cA, 'cA', torch.float32), (sh, 'sh', torch.float32)):
+        _check(x, name, dt)
+    n = points.size(0)
+    if sh.dim() != 3 or sh.size(1) != 16 or sh.size(2) != 3:
+        raise RuntimeError('sh must be (N, 16, 3)')
+    if dA.dim() != 2 or cA.dim() != 2 or dA.size(1) != 6 or cA.size(1) != 6:
+        raise RuntimeError('conics must be (N, 6)')
+    if raw.numel() != n or dA.size(0) != n or cA.size(0) != n or sh.size(0) != n:
+        raise RuntimeError('per-site tensors must have N rows')
+
+
+def _ray_checks(**rays):
+    for name, x in rays.items():
+        _check(x, name, torch.int32 if name == 'start' else torch.float32)
+    B = rays['o'].size(0)
+    if rays['o'].shape != (B, 3) or rays['d'].shape != (B, 3):
+        raise RuntimeError('o and d must be (B, 3)')
+    for name, x in rays.items():
+        if name not in ('o', 'd') and x.numel() != B:
+            raise RuntimeError(f'{name} must be (B)')
+    return B
+
+
+def _workspace(n, sh_deg, backward, dev):
+    nbytes = _lib.lib().vg_foam_workspace_bytes(n, int(sh_deg), int(backward))
+    return torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev), nbytes
+
+
+def _sh_deg(sh_deg):
+    if not 0 <= int(sh_deg) <= 3:
+        raise RuntimeError('sh_deg must be in 0..3')
+    return int(sh_deg)
+
+
+class FoamExtension:
+    """foam_forward / foam_backward with the reference's signatures (foam.cu:505-558)."""
+
+    @staticmethod
+    def foam_forward(points, offsets, adj, raw, dA, cA, sh, sh_deg, o, d, start, near, far, t_thresh, w_thresh,
+                     record_cap):
+        _scene_checks(points, offsets, adj, raw, dA, cA, sh)
+        B = _ray_checks(o=o, d=d, start=start, near=near, far=far)
+        sh_deg, K = _sh_deg(sh_deg), int(record_cap)
+        if K < 0:
+            raise RuntimeError('record_cap must be >= 0')
+        dev = o.device
+        rgb = torch.empty(B, 3, device=dev)
+        T = torch.empty(B, device=dev)
+        depth = torch.empty(B, device=dev)
+        stats = torch.empty(B, 3, dtype=torch.int32, device=dev)
+        rec = torch.empty(B if K > 0 else 0, K, 8, device=dev)
+        if B == 0:
+            return [rgb, T, depth, stats, rec]
+        pk = graph_pack(points, offsets, adj)
+        ws, nbytes = _workspace(pk.n, sh_deg, False, dev)
+        with torch.cuda.device(dev):
+            _lib.call('vg_foam_forward', pk.ptr, pk.n, pk.m, raw.data_ptr(), dA.data_ptr(), cA.data_ptr(),
+                      sh.data_ptr(), sh_deg, o.data_ptr(), d.data_ptr(), start.data_ptr(), near.data_ptr(),
+                      far.data_ptr(), B, float(t_thresh), float(w_thresh), K, rgb.data_ptr(), T.data_ptr(),
+                      depth.data_ptr(), stats.data_ptr(), _ptr(rec), ws.data_ptr(), nbytes, _stream(dev))
+        return [rgb, T, depth, stats, rec]
+
+    @staticmethod
+    def foam_backward(points, offsets, adj, raw, dA, cA, sh, sh_deg, o, d, start, near, far, t_thresh, w_thresh,
+                      rgb, T, g_rgb, g_T, rec, stats):
+        _scene_checks(points, offsets, adj, raw, dA, cA, sh)
+        B = _ray_checks(o=o, d=d, start=start, near=near, far=far)
+        for x, name, dt in ((rgb, 'rgb', torch.float32), (T, 'T', torch.float32), (g_rgb, 'g_rgb', torch.float32),
+                            (g_T, 'g_T', torch.float32), (rec, 'rec', torch.float32),
+                            (stats, 'stats', torch.int32)):
+            _check(x, name, dt)
+        replay = rec.numel() > 0
+        if replay and (rec.dim() != 3 or rec.size(0) != B or rec.size(2) != 8):
+            raise RuntimeError('rec must be (B, K, 8)')
+        sh_deg = _sh_deg(sh_deg)
+        dev = o.device
+        g_raw, g_dA, g_cA, g_sh = (torch.empty_like(x) for x in (raw, dA, cA, sh))
+        pk = graph_pack(points, offsets, adj)
+        ws, nbytes = _workspace(pk.n, sh_deg, True, dev)
+        ev = BACKWARD_EVENTS
+        with torch.cuda.device(dev):
+            if ev is not None:
+                ev[0].record()
+            _lib.call('vg_foam_backward', pk.ptr, pk.n, pk.m, raw.data_ptr(), dA.data_ptr(), cA.data_ptr(),
+                      sh.data_ptr(), sh_deg, _ptr(o), _ptr(d), _ptr(start), _ptr(near), _ptr(far), B,
+                      float(t_thresh), float(w_thresh), _ptr(rgb), _ptr(T), _ptr(g_rgb), _ptr(g_T),
+                      _ptr(rec) if replay else None, rec.size(1) if replay else 0, _ptr(stats), g_raw.data_ptr(),
+                      g_dA.data_ptr(), g_cA.data_ptr(), g_sh.data_ptr(), ws.data_ptr(), nbytes, _stream(dev))
+            if ev is not None:
+                ev[1].record()
+        return [g_raw, g_dA, g_cA, g_sh]
+
+
+class MarchExtension:
+    """march_forward / march_backward with the reference's signatures (march.cu:383-429)."""
+
+    @staticmethod
+    def march_forward(points, offsets, adj, raw, dA, cA, sh, sh_deg, o, d, start, near, mid, far, dt, n_bg, t_thresh,
+                      w_thresh):
+        _scene_checks(points, offsets, adj, raw, dA, cA, sh)
+        B = _ray_checks(o=o, d=d, start=start, near=near, mid=mid, far=far)
+        sh_deg = _sh_deg(sh_deg)
+        dev = o.device
+        rgb = torch.empty(B, 3, device=dev)
+        T = torch.empty(B, device=dev)
+        depth = torch.empty(B, device=dev)
+        stats = torch.empty(B, 3, dtype=torch.int32, device=dev)
+        if B == 0:
+            return [rgb, T, depth, stats]
+        pk = graph_pack(points, offsets, adj)
+        ws, nbytes = _workspace(pk.n, sh_deg, False, dev)
+        with torch.cuda.device(dev):
+            _lib.call('vg_march_forward', pk.ptr, pk.n, pk.m, raw.data_ptr(), dA.data_ptr(), cA.data_ptr(),
+                      sh.data_ptr(), sh_deg, o.data_ptr(), d.data_ptr(), start.data_ptr(), near.data_ptr(),
+                      mid.data_ptr(), far.data_ptr(), B, float(dt), int(n_bg), float(t_thresh), float(w_thresh),
+                      rgb.data_ptr(), T.data_ptr(), depth.data_ptr(), stats.data_ptr(), ws.data_ptr(), nbytes,
+                      _stream(dev))
+        return [rgb, T, depth, stats]
+
+    @staticmethod
+    def march_backward(points, offsets, adj, raw, dA, cA, sh, sh_deg, o, d, start, near, mid, far, dt, n_bg, t_thresh,
+                       w_thresh, rgb, T, g_rgb, g_T):
+        _scene_checks(points, offsets, adj, raw, dA, cA, sh)
+        B = _ray_checks(o=o, d=d, start=start, near=near, mid=mid, far=far)
+        for x, name in ((rgb, 'rgb'), (T, 'T'), (g_rgb, 'g_rgb'), (g_T, 'g_T')):
+            _check(x, name, torch.float32)
+        sh_deg = _sh_deg(sh_deg)
+        dev = o.device
+        g_raw, g_dA, g_cA, g_sh = (torch.empty_like(x) for x in (raw, dA, cA, sh))
+        pk = graph_pack(points, offsets, adj)
+        ws, nbytes = _workspace(pk.n, sh_deg, True, dev)
+        with torch.cuda.device(dev):
+            _lib.call('vg_march_backward', pk.ptr, pk.n, pk.m, raw.data_ptr(), dA.data_ptr(), cA.data_ptr(),
+                      sh.data_ptr(), sh_deg, _ptr(o), _ptr(d), _ptr(start), _ptr(near), _ptr(mid), _ptr(far), B,
+                      float(dt), int(n_bg), float(t_thresh), float(w_thresh), _ptr(rgb), _ptr(T), _ptr(g_rgb),
+                      _ptr(g_T), g_raw.data_ptr(), g_dA.data_ptr(), g_cA.data_ptr(), g_sh.data_ptr(), ws.data_ptr(),
+                      nbytes, _stream(dev))
+        return [g_raw, g_dA, g_cA, g_sh]
+
+
+class FieldExtension:
+    """conic_forward / conic_backward (vgf.cu:535-561). The NeRF-sampler functions of the same module
+    (walk, density_*, color_*: vgf.cu:438-533) are not part of this build."""
+
+    @staticmethod
+    def conic_forward(log_scale, quat, floor):
+        _check(log_scale, 'log_scale', torch.float32)
+        _check(quat, 'quat', torch.float32)
+        n = quat.size(0)
+        A = torch.empty(n, 6, device=quat.device)
+        if n:
+            with torch.cuda.device(quat.device):
+                _lib.call('vg_conic_forward', log_scale.data_ptr(), quat.data_ptr(), n, float(floor), A.data_ptr(),
+                          _stream(quat.device))
+        return A
+
+    @staticmethod
+    def conic_backward(log_scale, quat, floor, gA):
+        _check(log_scale, 'log_scale', torch.float32)
+        _check(quat, 'quat', torch.float32)
+        _check(gA, 'gA', torch.float32)
+        n = quat.size(0)
+        g_ls, g_quat = torch.empty_like(log_scale), torch.empty_like(quat)
+        if n:
+            with torch.cuda.device(quat.device):
+                _lib.call('vg_conic_backward', log_scale.data_ptr(), quat.data_ptr(), n, float(floor), gA.data_ptr(),
+                          g_ls.data_ptr(), g_quat.data_ptr(), _stream(quat.device))
+        return [g_ls, g_quat]
+
+    def __getattr__(self, name):
+        if name in ('walk', 'density_forward', 'density_backward', 'color_forward', 'color_backward'):
+            raise NotImplementedError(f'{name} (NeRF-sampler field kernel of vgf.cu) is not part of this build')
+        raise AttributeError(name)
+
+
+class FoamInferExtension:
+    """foam_infer with the reference's signature (foam_infer.cu:376-435)."""
+
+    @staticmethod
+    def foam_infer(points, offsets, nbr, edge, attr, sh, sh_deg, o, d, start, near, far, t_thresh, w_thresh,
+                   color_cut, color_mode, stage, cap, orig):
+        for x, name, dt in ((points, 'points', torch.float32), (offsets, 'offsets', torch.int32),
+                            (nbr, 'nbr', torch.int32), (edge, 'edge', torch.float32), (attr, 'attr', torch.float32),
+                            (cap, 'cap', torch.int32), (orig, 'orig', torch.int32)):
+            _check(x, name, dt)
+        B = _ray_checks(o=o, d=d, start=start, near=near, far=far)
+        if not (sh.is_cuda and sh.is_contiguous()):
+            raise RuntimeError('sh must be a contiguous CUDA tensor')
+        half = sh.dtype == torch.float16
+        if not (half or sh.dtype == torch.float32):
+            raise RuntimeError('sh must be float32 or float16')
+        n = points.size(0)
+        if points.dim() != 2 or points.size(1) != 4:
+            raise RuntimeError('points must be (N, 4)')
+        if offsets.numel() != n + 1:
+            raise RuntimeError('offsets must be (N + 1)')
+        if edge.dim() != 2 or edge.size(1) != 4 or edge.size(0) != nbr.numel():
+            raise RuntimeError('edge must be (E, 4)')
+        if attr.dim() != 2 or attr.size(1) != 20 or attr.size(0) != n:
+            raise RuntimeError('attr must be (N, 20)')
+        color_mode, stage = int(color_mode), int(stage)
+        if not 0 <= color_mode <= 2:
+            raise RuntimeError('color_mode must be 0 (lazy), 1 (baked) or 2 (fused)')
+        baked = color_mode == 1
+        if not baked and not (sh.dim() == 3 and sh.size(0) == n and sh.size(1) == 16 and sh.size(2) == 3):
+            raise RuntimeError('sh must be (N, 16, 3)')
+        if not 0 <= stage <= 2:
+            raise RuntimeError('stage must be 0, 1 or 2')
+        dev = o.device
+        rgb = torch.empty(B, 3, device=dev)
+        T = torch.empty(B, device=dev)
+        depth = torch.empty(B, device=dev)
+        stats = torch.empty(B, 5, dtype=torch.int32, device=dev)
+        if B == 0:
+            return [rgb, T, depth, stats]
+        with torch.cuda.device(dev):
+            _lib.call('vg_foam_infer', points.data_ptr(), offsets.data_ptr(), nbr.data_ptr(), edge.data_ptr(),
+                      attr.data_ptr(), None if baked else _ptr(sh), int(half), _sh_deg(sh_deg), n, nbr.numel(),
+                      o.data_ptr(), d.data_ptr(), start.data_ptr(), near.data_ptr(), far.data_ptr(), B,
+                      float(t_thresh), float(w_thresh), float(color_cut), color_mode, stage,
+                      _ptr(cap) if cap.numel() == B else None, _ptr(orig) if orig.numel() == n else None,
+                      rgb.data_ptr(), T.data_ptr(), depth.data_ptr(), stats.data_ptr(), _stream(dev))
+        return [rgb, T, depth, stats]
+
+
+_FOAM, _MARCH, _FIELD, _INFER = FoamExtension(), MarchExtension(), FieldExtension(), FoamInferExtension()
+
+
+def extension():
+    return _FIELD
+
+
+def march_extension():
+    return _MARCH
+
+
+def foam_extension():
+    return _FOAM
+
+
+def foam_infer_extension():
+    return _INFER
+
+
+# ---------------------------------------------------------------------------------------- autograd
+
+class _Conic(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, log_scale, quat, floor):
+        ctx.save_for_backward(log_scale, quat)
+        ctx.floor = floor
+        return extension().conic_forward(log_scale, quat, floor)
+
+    @staticmethod
+    def backward(ctx, gA):
+        log_scale, quat = ctx.saved_tensors
+        g_ls, g_quat = extension().conic_backward(log_scale, quat, ctx.floor, gA.contiguous())
+        return g_ls, g_quat, None
+
+
+def conic(log_scale, quat, floor=0.0):
+    """(N, 6) inverse covariances (xx, xy, xz, yy, yz, zz) of R diag(s^2 + floor^2) R^T (ext.py:134-136)."""
+    return _Conic.apply(log_scale.contiguous(), quat.contiguous(), float(floor))
+
+
+def conic_reference(log_scale, quat, floor=0.0):
+    """Plain torch version of conic (ext.py:139-149), for tests."""
+    q = quat / quat.norm(dim=-1, keepdim=True).clamp_min(1e-12)
+    w, x, y, z = q.unbind(-1)
+    R = torch.stack([
+        1 - 2 * (y * y + z * z), 2 * (x * y - w * z), 2 * (x * z + w * y),
+        2 * (x * y + w * z), 1 - 2 * (x * x + z * z), 2 * (y * z - w * x),
+        2 * (x * z - w * y), 2 * (y * z + w * x), 1 - 2 * (x * x + y * y)], -1).view(-1, 3, 3)
+    inv_var = 1.0 / (torch.exp(2 * log_scale.clamp(-20, 20)) + floor * floor)
+    A = torch.einsum('nak,nk,nbk->nab', R, inv_var, R)
+    return torch.stack([A[:, 0, 0], A[:, 0, 1], A[:, 0, 2], A[:, 1, 1], A[:, 1, 2], A[:, 2, 2]], -1).contiguous()
+
+
+class _March(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, raw, dA, cA, sh, graph, rays, cfg):
+        rgb, T, depth, stats = march_extension().march_forward(graph.points, graph.offsets, graph.adj, raw, dA, cA, sh,
+                                                               cfg[0], *rays, *cfg[1:])
+        ctx.save_for_backward(raw, dA, cA, sh, rgb, T, *rays)
+        ctx.graph, ctx.cfg = graph, cfg
+        ctx.mark_non_differentiable(depth, stats)
+        return rgb, T, depth, stats
+
+    @staticmethod
+    def backward(ctx, g_rgb, g_T, _g_depth, _g_stats):
+        raw, dA, cA, sh, rgb, T, *rays = ctx.saved_tensors
+        g, cfg = ctx.graph, ctx.cfg
+        g_rgb = torch.zeros_like(rgb) if g_rgb is None else g_rgb.contiguous()
+        g_T = torch.zeros_like(T) if g_T is None else g_T.contiguous()
+        g_raw, g_dA, g_cA, g_sh = march_extension().march_backward(g.points, g.offsets, g.adj, raw, dA, cA, sh, cfg[0],
+                                                                   *rays, *cfg[1:], rgb, T, g_rgb, g_T)
+        return g_raw, g_dA, g_cA, g_sh, None, None, None
+
+
+def march(graph, raw, dA, cA, sh, sh_deg, o, d, start, near, mid, far, dt, n_bg, t_thresh=1e-4, w_thresh=1e-4):
+    """Uniform-step fused rendering -> foreground rgb (B, 3), final transmittance (B,), depth (B,), per-ray
+    stats (B, 3) int: samples marched, samples with colour, walk steps (ext.py:172-182)."""
+    rays = tuple(t.float().contiguous() for t in (o, d)) + (start.int().contiguous(),) + \
+        tuple(t.float().contiguous() for t in (near, mid, far))
+    cfg = (int(sh_deg), float(dt), int(n_bg), float(t_thresh), float(w_thresh))
+    params = [p.contiguous() for p in (raw, dA, cA, sh)]
+    if not torch.is_grad_enabled() or not any(p.requires_grad for p in params):
+        return march_extension().march_forward(graph.points, graph.offsets, graph.adj, *[p.detach() for p in params],
+                                               cfg[0], *rays, *cfg[1:])
+    return _March.apply(*params, graph, rays, cfg)
+
+
+class _Foam(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, raw, dA, cA, sh, graph, rays, cfg, record_cap):
+        rgb, T, depth, stats, rec = foam_extension().foam_forward(graph.points, graph.offsets, graph.adj, raw, dA, cA,
+                                                                  sh, cfg[0], *rays, *cfg[1:], record_cap)
+        ctx.save_for_backward(raw, dA, cA, sh, rgb, T, rec, stats, *rays)
+        ctx.graph, ctx.cfg = graph, cfg
+        ctx.mark_non_differentiable(depth, stats)
+        return rgb, T, depth, stats
+
+    @staticmethod
+    def backward(ctx, g_rgb, g_T, _g_depth, _g_stats):
+        raw, dA, cA, sh, rgb, T, rec, stats, *rays = ctx.saved_tensors
+        g, cfg = ctx.graph, ctx.cfg
+        g_rgb = torch.zeros_like(rgb) if g_rgb is None else g_rgb.contiguous()
+        g_T = torch.zeros_like(T) if g_T is None else g_T.contiguous()
+        g_raw, g_dA, g_cA, g_sh = foam_extension().foam_backward(g.points, g.offsets, g.adj, raw, dA, cA, sh, cfg[0],
+                                                                 *rays, *cfg[1:], rgb, T, g_rgb, g_T, rec, stats)
+        return g_raw, g_dA, g_cA, g_sh, None, None, None, None
+
+
+def foam(graph, raw, dA, cA, sh, sh_deg, o, d, start, near, far, t_thresh=1e-4, w_thresh=1e-4, record_cap=256):
+    """Rendering at the interaction points of the rays with the Voronoi faces -> foreground rgb (B, 3), final
+    transmittance (B,), depth (B,), per-ray stats (B, 3) int: samples, segments with colour, walk steps to
+    x(near). With gradients, up to record_cap samples per ray are kept for the backward pass (0: re-trace every
+    ray) (ext.py:205-216)."""
+    rays = tuple(t.float().contiguous() for t in (o, d)) + (start.int().contiguous(),) + \
+        tuple(t.float().contiguous() for t in (near, far))
+    cfg = (int(sh_deg), float(t_thresh), float(w_thresh))
+    params = [p.contiguous() for p in (raw, dA, cA, sh)]
+    if not torch.is_grad_enabled() or not any(p.requires_grad for p in params):
+        return foam_extension().foam_forward(graph.points, graph.offsets, graph.adj, *[p.detach() for p in params],
+                                             cfg[0], *rays, *cfg[1:], 0)[:4]
+    return _Foam.apply(*params, graph, rays, cfg, int(record_cap))
