@@ -63,9 +63,10 @@ int vg_graph_pack(const float* points, const int32_t* offsets, const int32_t* ad
 
 /* ------------------------------------------------------------------------- interaction points */
 
-/* Workspace of vg_foam_forward / vg_march_forward (backward = 0) or of the backward functions
- * (backward = 1) for n_sites sites at SH degree sh_deg. */
-size_t vg_foam_workspace_bytes(int64_t n_sites, int sh_deg, int backward);
+/* Workspace of vg_foam_forward / vg_march_forward (backward = 0), of vg_foam_backward /
+ * vg_march_backward (backward = 1) or of vg_foam_backward_packed (backward = 2), for n_sites sites at
+ * SH degree sh_deg, n_rays rays and records of capacity record_cap (0 for march). */
+size_t vg_foam_workspace_bytes(int64_t n_sites, int sh_deg, int64_t n_rays, int record_cap, int backward);
 
 /* foam_forward (foam.cu:505-526): rendering at the ray / Voronoi-face interaction points.
  * raw (N), dA (N, 6), cA (N, 6), sh (N, 16, 3); o, d (B, 3); start (B) site near each origin;

@@ -98,7 +98,12 @@ def test_records_are_reference_format(foam_small):
         assert (np.diff(rec[r, :s, 0]) >= 0).all()
         for a, b in zip(cells[:-1], cells[1:]):
             assert a == b or b in adj[off[a]:off[a + 1]]
-        assert (rec[r, :s, 7] > 0).all()
+        # 1 / sum of colour weights: 0 for samples whose colour was never needed (foam.cu:285), as in the
+        # reference; every endpoint of a coloured segment has one
+        coloured = rec[r, :s, 7] > 0
+        assert (rec[r, :s, 7] >= 0).all()
+        if stats[r, 1] > 0:
+            assert coloured.sum() >= stats[r, 1] + 1 or coloured.sum() == s
 
 
 def test_bad_arguments_raise_reference_errors(foam_small):

@@ -1,0 +1,164 @@
+"""The product against the reference's own CUDA kernels, built unchanged from its sources for sm_100a
+into oracle/_ref (oracle/ref_build.py), on identical inputs: per-ray visited-cell sequences and sample
+parameters bit for bit, stats equal, images within 1e-4 and gradients within 1e-3 relative. Skipped when
+oracle/_ref was not built (the reference checkout is needed to build it)."""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import bits, cuda, rel, small_inputs
+
+pytestmark = pytest.mark.gpu
+
+IMG_TOL = 1e-4
+GRAD_TOL = 1e-3
+
+
+def ref(name):
+    from oracle import ref_build
+    if not ref_build.available(name):
+        pytest.skip(f'oracle/_ref/{name} not built')
+    return ref_build.load_reference(name)
+
+
+def _ext():
+    from voronoi_gauss_b200 import ext
+    return ext
+
+
+def compare_records(stats, rec, r_stats, r_rec, K):
+    """Rays whose samples all fit in the records: identical cell sequence and t bit for bit."""
+    stats, rec, r_stats, r_rec = (x.cpu().numpy() for x in (stats, rec, r_stats, r_rec))
+    assert (stats[:, 0] == r_stats[:, 0]).all(), 'samples per ray differ'
+    assert (stats[:, 2] == r_stats[:, 2]).all(), 'walk steps differ'
+    fits = stats[:, 0] <= K
+    s = np.minimum(stats[:, 0], K)
+    valid = np.arange(K)[None, :] < s[:, None]
+    valid &= fits[:, None]
+    assert (bits(rec[..., 1])[valid] == bits(r_rec[..., 1])[valid]).all(), 'visited cells differ'
+    assert (bits(rec[..., 0])[valid] == bits(r_rec[..., 0])[valid]).all(), 'sample t differs'
+    np.testing.assert_allclose(rec[..., 2][valid], r_rec[..., 2][valid], rtol=1e-4, atol=1e-5)
+    return stats, r_stats
+
+
+def test_foam_small_against_reference_kernels(foam_small):
+    rf = ref('vgf_foam')
+    ext = _ext()
+    z = foam_small
+    x = small_inputs(z)
+    g = ext.Graph(cuda(z['points']), cuda(z['offsets']), cuda(z['adj']))
+    for t_thresh, w_thresh in ((0.0, -1.0), (1e-4, 1e-4)):
+        args = (g.points, g.offsets, g.adj, x['raw'], x['dA'], x['cA'], x['sh'], 3, x['o'], x['d'], x['start'],
+                x['near'], x['far'], t_thresh, w_thresh)
+        mine = ext.foam_extension().foam_forward(*args, 256)
+        theirs = rf.foam_forward(*args, 256)
+        stats, r_stats = compare_records(mine[3], mine[4], theirs[3], theirs[4], 256)
+        assert (stats == r_stats).all()
+        for a, b in zip(mine[:3], theirs[:3]):
+            assert float((a - b).abs().max()) <= IMG_TOL
+        g_rgb, g_T = cuda(z['g_rgb']), cuda(z['g_T'])
+        for K in (256, 0):
+            gm = ext.foam_extension().foam_backward(*args, mine[0], mine[1], g_rgb, g_T,
+                                                    mine[4] if K else mine[4][:0], mine[3])
+            gr = rf.foam_backward(*args, theirs[0], theirs[1], g_rgb, g_T, theirs[4] if K else theirs[4][:0],
+                                  theirs[3])
+            for name, a, b in zip(('raw', 'dA', 'cA', 'sh'), gm, gr):
+                assert rel(a.cpu().numpy(), b.cpu().numpy()) <= GRAD_TOL, name
+
+
+def test_foam_full_size_scene_against_reference_kernels():
+    """BASELINE config 3 scene (3M sites, surface-biased), a 480 x 270 view of the bench camera: every ray's
+    visited-cell sequence and sample parameters bit for bit, stats, images and gradients."""
+    rf = ref('vgf_foam')
+    ext = _ext()
+    from voronoi_gauss_b200 import render, scenes, sites
+    gr = scenes.build_graph(3)
+    prm = scenes.make_params(3, gr['points'].astype(np.float64))
+    centre, c2w = scenes.orbit_camera(0, 8)
+    W, H = 480, 270
+    o, d = scenes.camera_rays(centre, c2w, W, H, 50.0, order=scenes.tile_order(H, W))
+    o, d = o.cuda(), d.cuda()
+    start = torch.full((len(o),), int(sites.nearest_sites(gr['points'], centre[None])[0]), dtype=torch.int32,
+                       device='cuda')
+    near, _, far = render.ray_bounds(o, d, 0.02, 4.0)
+    g = ext.Graph(cuda(gr['points']), cuda(gr['offsets']), cuda(gr['adj']))
+    dA = ext.conic(cuda(prm['d_log_scale']), cuda(prm['d_quat']))
+    cA = ext.conic(cuda(prm['c_log_scale']), cuda(prm['c_quat']))
+    raw, sh = cuda(prm['raw']), cuda(prm['sh'])
+    K = 512
+    args = (g.points, g.offsets, g.adj, raw, dA, cA, sh, 3, o, d, start, near, far, 1e-4, 1e-4)
+    mine = ext.foam_extension().foam_forward(*args, K)
+    theirs = rf.foam_forward(*args, K)
+    stats, r_stats = compare_records(mine[3], mine[4], theirs[3], theirs[4], K)
+    assert (stats[:, 0] <= K).mean() > 0.99
+    same = (stats == r_stats).all(1)
+    assert same.mean() >= 0.999
+    for a, b in zip(mine[:3], theirs[:3]):
+        assert float((a - b).abs().max()) <= IMG_TOL
+    gen = torch.Generator().manual_seed(1)
+    g_rgb, g_T = torch.randn(len(o), 3, generator=gen).cuda(), torch.randn(len(o), generator=gen).cuda()
+    gm = ext.foam_extension().foam_backward(*args, mine[0], mine[1], g_rgb, g_T, mine[4], mine[3])
+    grr = rf.foam_backward(*args, theirs[0], theirs[1], g_rgb, g_T, theirs[4], theirs[3])
+    for name, a, b in zip(('raw', 'dA', 'cA', 'sh'), gm, grr):
+        assert rel(a.cpu().numpy(), b.cpu().numpy()) <= GRAD_TOL, name
+
+
+def test_march_against_reference_kernels(march_small):
+    rm = ref('vgf_march')
+    ext = _ext()
+    z = march_small
+    x = small_inputs(z, ('raw', 'dA', 'cA', 'sh', 'o', 'd', 'start', 'near', 'mid', 'far'))
+    g = ext.Graph(cuda(z['points']), cuda(z['offsets']), cuda(z['adj']))
+    for dt, n_bg, tt, wt in ((float(z['dt']), int(z['n_bg']), 0.0, -1.0), (0.02, 4, 1e-4, 1e-4)):
+        args = (g.points, g.offsets, g.adj, x['raw'], x['dA'], x['cA'], x['sh'], 3, x['o'], x['d'], x['start'],
+                x['near'], x['mid'], x['far'], dt, n_bg, tt, wt)
+        mine = ext.march_extension().march_forward(*args)
+        theirs = rm.march_forward(*args)
+        assert torch.equal(mine[3], theirs[3])
+        for a, b in zip(mine[:3], theirs[:3]):
+            assert float((a - b).abs().max()) <= IMG_TOL
+        g_rgb, g_T = cuda(z['g_rgb']), cuda(z['g_T'])
+        gm = ext.march_extension().march_backward(*args, mine[0], mine[1], g_rgb, g_T)
+        gr = rm.march_backward(*args, theirs[0], theirs[1], g_rgb, g_T)
+        for name, a, b in zip(('raw', 'dA', 'cA', 'sh'), gm, gr):
+            assert rel(a.cpu().numpy(), b.cpu().numpy()) <= GRAD_TOL, name
+
+
+@pytest.mark.parametrize('tag', ['plain', 'morton', 'eps_morton'])
+def test_foam_infer_against_reference_kernel(foam_small, tag):
+    ri = ref('vgf_foam_infer')
+    ext = _ext()
+    z = foam_small
+    sh = z[f'pack_{tag}_sh']
+    p = [cuda(z[f'pack_{tag}_{k}']) for k in ('points', 'offsets', 'nbr', 'edge', 'attr')]
+    shp = cuda(sh, torch.float16 if sh.dtype == np.float16 else torch.float32)
+    orig = cuda(z[f'pack_{tag}_orig'], torch.int32)
+    start = z['start'] if tag == 'plain' else np.argsort(z[f'pack_{tag}_orig'])[z['start']]
+    x = small_inputs(z, ('o', 'd', 'near', 'far'))
+    cap = torch.empty(0, dtype=torch.int32, device='cuda')
+    cut = 2 * np.log(1e3) if tag.startswith('eps') else float('inf')
+    for mode in (0, 1, 2):
+        for stage in (0, 1, 2):
+            args = (*p, shp, 3, x['o'], x['d'], cuda(start.astype(np.int32)), x['near'], x['far'], 0.0, -1.0, cut,
+                    mode, stage, cap, orig)
+            mine = ext.foam_infer_extension().foam_infer(*args)
+            theirs = ri.foam_infer(*args)
+            assert torch.equal(mine[3], theirs[3]), (mode, stage)
+            for a, b in zip(mine[:3], theirs[:3]):
+                assert float((a - b).abs().max()) <= IMG_TOL
+
+
+def test_conic_against_reference_kernel():
+    rv = ref('vgf_ext')
+    ext = _ext()
+    from conftest import golden
+    z = golden('conic.npz')
+    ls, q, gA = cuda(z['ls']), cuda(z['quat']), cuda(z['gA'])
+    for floor in (0.0, 0.01):
+        a = ext.extension().conic_forward(ls, q, floor)
+        b = rv.conic_forward(ls, q, floor)
+        assert rel(a.cpu().numpy(), b.cpu().numpy()) <= 1e-6
+        ga, gb = ext.extension().conic_backward(ls, q, floor, gA), rv.conic_backward(ls, q, floor, gA)
+        for u, v in zip(ga, gb):
+            assert rel(u.cpu().numpy(), v.cpu().numpy()) <= 1e-5

@@ -30,7 +30,7 @@ SIGNATURES = {
     'vg_status_reset': (I32, []),
     'vg_graph_pack_bytes': (SZ, [I64, I64]),
     'vg_graph_pack': (I32, [P, P, P, I64, I64, P, SZ, P]),
-    'vg_foam_workspace_bytes': (SZ, [I64, I32, I32]),
+    'vg_foam_workspace_bytes': (SZ, [I64, I32, I64, I32, I32]),
     'vg_foam_forward': (I32, [P, I64, I64, P, P, P, P, I32, P, P, P, P, P, I64, F32, F32, I32, P, P, P, P, P, P, SZ,
                               P]),
     'vg_foam_backward': (I32, [P, I64, I64, P, P, P, P, I32, P, P, P, P, P, I64, F32, F32, P, P, P, P, P, I32, P, P, P,

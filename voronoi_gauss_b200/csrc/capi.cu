@@ -6,7 +6,7 @@
 #include <mutex>
 #include <string>
 
-#include "../../include/vgb200.h"
+#include "vgb200.h"  // include/ (on the -I path)
 #include "vg_common.cuh"
 
 namespace {
@@ -128,9 +128,11 @@ int vg_graph_pack(const float* points, const int32_t* offsets, const int32_t* ad
     return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_graph_pack");
 }
 
-size_t vg_foam_workspace_bytes(int64_t n_sites, int sh_deg, int backward) {
-    if (n_sites <= 0 || sh_deg < 0 || sh_deg > 3) return 0;
-    return field_ws(n_sites, sh_deg) + (backward ? grad_ws(n_sites) : 0);
+size_t vg_foam_workspace_bytes(int64_t n_sites, int sh_deg, int64_t n_rays, int record_cap, int backward) {
+    if (n_sites <= 0 || sh_deg < 0 || sh_deg > 3 || n_rays < 0 || record_cap < 0) return 0;
+    if (backward == 0) return field_ws(n_sites, sh_deg);
+    const size_t cm = align256(vg::foam_backward_workspace(n_sites, n_rays, record_cap));
+    return field_ws(n_sites, sh_deg) + (backward == 1 ? grad_ws(n_sites) : 0) + cm;
 }
 
 int vg_foam_forward(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA,
@@ -169,7 +171,7 @@ static int foam_backward_impl(const void* pack, int64_t n_sites, int64_t n_adj, 
                               const int32_t* start, const float* near, const float* far, int64_t n_rays,
                               float t_thresh, float w_thresh, const float* rgb, const float* T, const float* g_rgb,
                               const float* g_T, const float* rec, int record_cap, const int32_t* stats, float* grad,
-                              bool zero_first, void* workspace, size_t workspace_bytes, size_t need,
+                              bool zero_first, void* workspace, size_t workspace_bytes, size_t need, size_t cm_off,
                               cudaStream_t st) {
     int rc = check_scene(pack, n_sites, n_adj, raw, dA, cA, sh, sh_deg);
     if (rc) return rc;
@@ -195,7 +197,8 @@ static int foam_backward_impl(const void* pack, int64_t n_sites, int64_t n_adj, 
     const vg::RayView R{o, d, start, near, nullptr, far, n_rays};
     const vg::FoamCfg c{t_thresh, w_thresh, record_cap};
     const vg::GradIn gi{rgb, T, g_rgb, g_T, record_cap > 0 ? rec : nullptr, stats, record_cap};
-    e = vg::foam_backward(g, F, R, c, gi, grad, status, st);
+    void* cm = static_cast<char*>(workspace) + cm_off;
+    e = vg::foam_backward(g, F, R, c, gi, grad, status, cm, workspace_bytes - cm_off, st);
     return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_foam_backward");
 }
 
@@ -208,12 +211,12 @@ int vg_foam_backward(const void* pack, int64_t n_sites, int64_t n_adj, const flo
     REQUIRE(g_raw && g_dA && g_cA && g_sh, "gradient outputs must be non-null");
     REQUIRE(aligned(g_dA, 8) && aligned(g_cA, 8) && aligned(g_sh, 16), "gradient outputs misaligned");
     if (sh_deg < 0 || sh_deg > 3) return fail(VG_ERR_INVALID_ARG, "sh_deg must be in 0..3");
-    const size_t need = vg_foam_workspace_bytes(n_sites, sh_deg, 1);
+    const size_t need = vg_foam_workspace_bytes(n_sites, sh_deg, n_rays, record_cap, 1);
     float* grad = reinterpret_cast<float*>(static_cast<char*>(workspace) + field_ws(n_sites, sh_deg));
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     int rc = foam_backward_impl(pack, n_sites, n_adj, raw, dA, cA, sh, sh_deg, o, d, start, near, far, n_rays,
                                 t_thresh, w_thresh, rgb, T, g_rgb, g_T, rec, record_cap, stats, grad, true, workspace,
-                                workspace_bytes, need, st);
+                                workspace_bytes, need, field_ws(n_sites, sh_deg) + grad_ws(n_sites), st);
     if (rc) return rc;
     const cudaError_t e =
         vg::grad_unpack(vg::graph_view(pack, n_sites, n_adj), grad, sh_deg, g_raw, g_dA, g_cA, g_sh, st);
@@ -231,8 +234,8 @@ int vg_foam_backward_packed(const void* pack, int64_t n_sites, int64_t n_adj, co
     if (sh_deg < 0 || sh_deg > 3) return fail(VG_ERR_INVALID_ARG, "sh_deg must be in 0..3");
     return foam_backward_impl(pack, n_sites, n_adj, raw, dA, cA, sh, sh_deg, o, d, start, near, far, n_rays, t_thresh,
                               w_thresh, rgb, T, g_rgb, g_T, rec, record_cap, stats, grad_pack, zero_first != 0,
-                              workspace, workspace_bytes, vg_foam_workspace_bytes(n_sites, sh_deg, 0),
-                              static_cast<cudaStream_t>(stream));
+                              workspace, workspace_bytes, vg_foam_workspace_bytes(n_sites, sh_deg, n_rays, record_cap, 2),
+                              field_ws(n_sites, sh_deg), static_cast<cudaStream_t>(stream));
 }
 
 int vg_grad_unpack(const void* pack, int64_t n_sites, int64_t n_adj, const float* grad_pack, int sh_deg,
@@ -294,7 +297,7 @@ int vg_march_backward(const void* pack, int64_t n_sites, int64_t n_adj, const fl
     if ((rc = check_alignment(dA, cA, sh, nullptr))) return rc;
     REQUIRE(aligned(workspace, 256), "workspace must be 256-byte aligned");
     REQUIRE(aligned(g_dA, 8) && aligned(g_cA, 8) && aligned(g_sh, 16), "gradient outputs misaligned");
-    const size_t need = vg_foam_workspace_bytes(n_sites, sh_deg, 1);
+    const size_t need = vg_foam_workspace_bytes(n_sites, sh_deg, n_rays, 0, 1);
     if (workspace_bytes < need || workspace == nullptr)
         return fail(VG_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);
     int* status = status_ptr();

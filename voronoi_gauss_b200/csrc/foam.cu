@@ -10,20 +10,59 @@
 // weights) in the reference's (B, K, 8) record format; the backward pass replays the records front to
 // back with the reference's suffix formula (foam.cu:16, 428-467) and re-traces rays with more than K
 // samples. Gradients go to the (N, 64) gradient pack with 16-byte vector atomics.
+#include <algorithm>
+#include <cub/device/device_scan.cuh>
+
 #include "render_core.cuh"
+
+// Build-time tuning knobs (defaults chosen by measurement on B200, config-3 scenes at 1080p):
+//   VG_FWD_SLOTS / VG_BWD_SLOTS  per-ray colour cache slots in shared memory (0: no cache; a site's
+//                  colour is reused by few consecutive samples of a ray, the cache lost 20-30 %)
+//   VG_LAZY_COLOR  1: colours only for samples next to a segment with weight > w_thresh, in a second
+//                  pass over the cell (~40 % of the samples never need one)
+//   VG_BWD_AGG     1: warp-aggregated gradient atomics through shared memory (2x slower: the staging
+//                  traffic costs more than the atomics it saves)
+//   VG_FWD_MINB / VG_BWD_MINB  minimum resident blocks of 128 threads per SM (register budget)
+#ifndef VG_FWD_SLOTS
+#define VG_FWD_SLOTS 0
+#endif
+#ifndef VG_BWD_SLOTS
+#define VG_BWD_SLOTS 0
+#endif
+#ifndef VG_LAZY_COLOR
+#define VG_LAZY_COLOR 1
+#endif
+#ifndef VG_BWD_AGG
+#define VG_BWD_AGG 0
+#endif
+#ifndef VG_FWD_MINB
+#define VG_FWD_MINB 8
+#endif
+#ifndef VG_BWD_MINB
+#define VG_BWD_MINB 1
+#endif
+// VG_BWD_CELL_MAJOR  1: samples of fully recorded rays scattered cell-major (see cm_scatter_kernel)
+#ifndef VG_BWD_CELL_MAJOR
+#define VG_BWD_CELL_MAJOR 1
+#endif
 
 namespace vg {
 namespace {
 
 constexpr int kBlock = 128;
-constexpr int kSlots = 8;
+constexpr int kFwdSlots = VG_FWD_SLOTS;
+constexpr int kBwdSlots = VG_BWD_SLOTS;
+constexpr int kFwdSlotMem = kFwdSlots > 0 ? kFwdSlots * kBlock : 1;
+constexpr int kBwdSlotMem = kBwdSlots > 0 ? kBwdSlots * kBlock : 1;
+constexpr bool kLazy = VG_LAZY_COLOR != 0;
+constexpr bool kAgg = VG_BWD_AGG != 0;
 
 __device__ __forceinline__ void store_sample(float* __restrict__ rec, int64_t r, int K, int s, const Sample& P,
-                                             const int* __restrict__ perm) {
+                                             bool has_c, const int* __restrict__ perm) {
     if (s >= K) return;
     float4* q = reinterpret_cast<float4*>(rec + (r * K + s) * kRecord);
     q[0] = make_float4(P.t, __int_as_float(__ldg(perm + P.cell)), P.sigma, P.C0);
-    q[1] = make_float4(P.C1, P.C2, P.mmin, P.inv_a);
+    q[1] = make_float4(P.C1, P.C2, P.mmin, has_c ? P.inv_a : 0.f);
 }
 
 __device__ __forceinline__ void load_sample(const float* __restrict__ rec, int64_t r, int K, int s,
@@ -47,12 +86,12 @@ __device__ __forceinline__ void load_ray(const RayView& R, int64_t r, float (&o)
 }
 
 template <bool RECORD>
-__global__ void __launch_bounds__(kBlock)
+__global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
     foam_forward_kernel(GraphView g, FieldView F, RayView R, FoamCfg c, Outputs out, int* status) {
-    __shared__ float4 cache_mem[kSlots * kBlock];
+    __shared__ float4 cache_mem[kFwdSlotMem];
     const int64_t r = static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
     if (r >= R.n) return;
-    ColorCache<kSlots> cache{cache_mem + threadIdx.x, kBlock};
+    ColorCache<kFwdSlots> cache{cache_mem + threadIdx.x, kBlock};
     cache.init();
     float o[3], d[3], near, far;
     load_ray(R, r, o, d, near, far);
@@ -65,7 +104,8 @@ __global__ void __launch_bounds__(kBlock)
     Sample P;
     float t_exit;
     int next;
-    eval_sample(g, F, cur, near, o, d, b, cache, true, P, t_exit, next);
+    eval_sample<kFwdSlots, !kLazy>(g, F, cur, near, o, d, b, cache, true, P, t_exit, next);
+    bool has_p = !kLazy;
     float T = 1.f, acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, dep = 0.f;
     int it = 0;
     for (; it < kMaxCells; ++it) {
@@ -73,13 +113,18 @@ __global__ void __launch_bounds__(kBlock)
         Sample Q;
         float t_exit_q;
         int next_q;
-        eval_sample(g, F, last ? P.cell : next, last ? far : fmaxf(t_exit, P.t), o, d, b, cache, !last, Q, t_exit_q,
-                    next_q);
+        eval_sample<kFwdSlots, !kLazy>(g, F, last ? P.cell : next, last ? far : fmaxf(t_exit, P.t), o, d, b, cache, !last,
+                                    Q, t_exit_q, next_q);
+        bool has_q = !kLazy;
         ++n_samples;
         const float delta = Q.t - P.t;
         const float alpha = 1.f - __expf(-0.5f * (P.sigma + Q.sigma) * delta);
         const float w = T * alpha;
         if (w > c.w_thresh) {
+            if (kLazy) {
+                if (!has_p) eval_color(g, F, b, cache, P), has_p = true;
+                eval_color(g, F, b, cache, Q), has_q = true;
+            }
             acc0 += w * 0.5f * (P.C0 + Q.C0);
             acc1 += w * 0.5f * (P.C1 + Q.C1);
             acc2 += w * 0.5f * (P.C2 + Q.C2);
@@ -87,13 +132,14 @@ __global__ void __launch_bounds__(kBlock)
             ++n_color;
         }
         T *= 1.f - alpha;
-        if (RECORD) store_sample(out.rec, r, K, n_samples - 2, P, g.perm);
+        if (RECORD) store_sample(out.rec, r, K, n_samples - 2, P, has_p, g.perm);
         P = Q;
+        has_p = has_q;
         t_exit = t_exit_q, next = next_q;
         if (last || T < c.t_thresh) break;
     }
     if (it == kMaxCells) err |= kErrCellCap;
-    if (RECORD) store_sample(out.rec, r, K, n_samples - 1, P, g.perm);
+    if (RECORD) store_sample(out.rec, r, K, n_samples - 1, P, has_p, g.perm);
     out.rgb[3 * r] = acc0, out.rgb[3 * r + 1] = acc1, out.rgb[3 * r + 2] = acc2;
     out.T[r] = T;
     out.depth[r] = dep;
@@ -101,13 +147,50 @@ __global__ void __launch_bounds__(kBlock)
     if (err) atomicOr(status, err);
 }
 
-__global__ void __launch_bounds__(kBlock)
+// Per-sample record of the cell-major backward: the sample's gradient scalars, written by the replay
+// (one slot per recorded sample, indexed ray * K + sample) and consumed by cm_scatter_kernel.
+//   (gs, gC r, gC g, gC b) | (gC . C, m_min, 1 / sum of colour weights or 0, bits(cell) or -1)
+__device__ __forceinline__ void emit_item(float4* __restrict__ items, int64_t slot, const Sample& P, float gs,
+                                          float gC0, float gC1, float gC2, bool has_c, int* __restrict__ count) {
+    const bool do_c = has_c && (gC0 != 0.f || gC1 != 0.f || gC2 != 0.f);
+    float4* it = items + 2 * slot;
+    if (gs == 0.f && !do_c) {
+        it[1] = make_float4(0.f, 0.f, 0.f, __int_as_float(-1));
+        return;
+    }
+    const float gCC = gC0 * P.C0 + gC1 * P.C1 + gC2 * P.C2;
+    it[0] = make_float4(gs, do_c ? gC0 : 0.f, do_c ? gC1 : 0.f, do_c ? gC2 : 0.f);
+    it[1] = make_float4(gCC, P.mmin, do_c ? P.inv_a : 0.f, __int_as_float(P.cell));
+    atomicAdd(count + P.cell, 1);
+}
+
+// What the replay does with each sample's gradients: scatter them to the sites of its neighbourhood
+// (every ray, or only the rays that were not recorded in full), or write them as items of the
+// cell-major backward (only fully recorded rays).
+enum BwdMode { kScatterAll = 0, kScatterRetraced = 1, kItems = 2 };
+
+struct ItemOut {
+    float4* items;  // (rays of the chunk) x K x 2 float4
+    int* count;     // (N + 1) samples per cell
+    int64_t r0;     // first ray of the chunk
+    int64_t n;      // rays in the chunk
+};
+
+template <int MODE>
+__global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
     foam_backward_kernel(GraphView g, FieldView F, RayView R, FoamCfg c, GradIn gi, float* __restrict__ grad,
-                         int* status) {
-    __shared__ float4 cache_mem[kSlots * kBlock];
-    const int64_t r = static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
-    if (r >= R.n) return;
-    ColorCache<kSlots> cache{cache_mem + threadIdx.x, kBlock};
+                         ItemOut io, int* status) {
+    __shared__ float4 cache_mem[kBwdSlotMem];
+    __shared__ float4 stage_mem[kAgg ? 16 * kBlock : 1];
+    const int64_t r = (MODE == kItems ? io.r0 : 0) + static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
+    if (r >= (MODE == kItems ? io.r0 + io.n : R.n)) return;
+    {
+        const int K_ = gi.record_cap;
+        const bool replayable = gi.rec != nullptr && K_ > 0 && __ldg(gi.stats + 3 * r) <= K_;
+        if (MODE == kItems && !replayable) return;
+        if (MODE == kScatterRetraced && replayable) return;
+    }
+    ColorCache<kBwdSlots> cache{cache_mem + threadIdx.x, kBlock};
     cache.init();
     float o[3], d[3], near, far;
     load_ray(R, r, o, d, near, far);
@@ -130,10 +213,13 @@ __global__ void __launch_bounds__(kBlock)
         int walk_steps = 0;
         const int cur = walk_to(g, __ldg(g.inv + __ldg(R.start + r)), along(o[0], near, d[0]),
                                 along(o[1], near, d[1]), along(o[2], near, d[2]), walk_steps, err);
-        eval_sample(g, F, cur, near, o, d, b, cache, true, P, t_exit, next);
+        eval_sample<kBwdSlots, true>(g, F, cur, near, o, d, b, cache, true, P, t_exit, next);
     }
+    float4* stage = stage_mem + (kAgg ? 16 * (threadIdx.x & ~31) : 0);
+    const int lane = threadIdx.x & 31;
     float T = 1.f, acc0 = 0.f, acc1 = 0.f, acc2 = 0.f;
     float gs_pending = 0.f, gP0 = 0.f, gP1 = 0.f, gP2 = 0.f;  // gradients of P from the segment before it
+    int n_done = 0;  // index of P
     for (int it = 0; it < kMaxCells; ++it) {
         Sample Q;
         bool last, has_q = true;
@@ -145,8 +231,8 @@ __global__ void __launch_bounds__(kBlock)
             last = it + 2 >= n_stored;
         } else {
             last = next < 0 || t_exit >= far;
-            eval_sample(g, F, last ? P.cell : next, last ? far : fmaxf(t_exit, P.t), o, d, b, cache, !last, Q,
-                        t_exit_q, next_q);
+            eval_sample<kBwdSlots, true>(g, F, last ? P.cell : next, last ? far : fmaxf(t_exit, P.t), o, d, b, cache,
+                                      !last, Q, t_exit_q, next_q);
         }
         const float delta = Q.t - P.t;
         const float alpha = 1.f - __expf(-0.5f * (P.sigma + Q.sigma) * delta);
@@ -155,6 +241,9 @@ __global__ void __launch_bounds__(kBlock)
         const bool active = w > c.w_thresh;
         float c0 = 0.f, c1 = 0.f, c2 = 0.f;
         if (active) {
+            // colours of records written without them (foam.cu:443-445)
+            if (!has_p) eval_color(g, F, b, cache, P), has_p = true;
+            if (!has_q) eval_color(g, F, b, cache, Q), has_q = true;
             c0 = 0.5f * (P.C0 + Q.C0), c1 = 0.5f * (P.C1 + Q.C1), c2 = 0.5f * (P.C2 + Q.C2);
             acc0 += w * c0, acc1 += w * c1, acc2 += w * c2;
         }
@@ -163,17 +252,190 @@ __global__ void __launch_bounds__(kBlock)
         g_sbar = delta * (g_sbar - gT_final);
         const float h0 = active ? 0.5f * w * gR0 : 0.f, h1 = active ? 0.5f * w * gR1 : 0.f,
                     h2 = active ? 0.5f * w * gR2 : 0.f;
-        scatter_sample(g, F, P, gs_pending + 0.5f * g_sbar, gP0 + h0, gP1 + h1, gP2 + h2, has_p, b, cache, grad);
+        if (MODE == kItems)
+            emit_item(io.items, (r - io.r0) * K + it, P, gs_pending + 0.5f * g_sbar, gP0 + h0, gP1 + h1, gP2 + h2,
+                      has_p, io.count);
+        else if (kAgg)
+            scatter_sample_agg(g, F, P, gs_pending + 0.5f * g_sbar, gP0 + h0, gP1 + h1, gP2 + h2, has_p, b, cache, grad,
+                               stage, lane);
+        else
+            scatter_sample(g, F, P, gs_pending + 0.5f * g_sbar, gP0 + h0, gP1 + h1, gP2 + h2, has_p, b, cache, grad);
         gs_pending = 0.5f * g_sbar;
         gP0 = h0, gP1 = h1, gP2 = h2;
         T = T_next;
         P = Q;
         has_p = has_q;
         t_exit = t_exit_q, next = next_q;
+        n_done = it + 1;
         if (last || T < c.t_thresh) break;
     }
-    scatter_sample(g, F, P, gs_pending, gP0, gP1, gP2, has_p, b, cache, grad);
+    if (MODE == kItems)
+        emit_item(io.items, (r - io.r0) * K + n_done, P, gs_pending, gP0, gP1, gP2, has_p, io.count);
+    else if (kAgg)
+        scatter_sample_agg(g, F, P, gs_pending, gP0, gP1, gP2, has_p, b, cache, grad, stage, lane);
+    else
+        scatter_sample(g, F, P, gs_pending, gP0, gP1, gP2, has_p, b, cache, grad);
     if (err) atomicOr(status, err);
+}
+
+// ----------------------------------------------------------------------------- cell-major scatter
+//
+// The gradient of a sample goes to the ~20 sites of its cell's neighbourhood. Thread-per-ray scatter
+// issues one set of atomics per (sample, site); but the rays of a view cross each visited cell many
+// times (~70 samples per cell at 1080p), so the samples are bucketed by cell (counting sort over the
+// cells) and a warp processes up to 32 samples of one cell with ONE LANE PER NEIGHBOUR SITE: the lane
+// keeps its site's field record and SH coefficients in registers, loops over the samples (staged in
+// shared memory, read as broadcasts), accumulates the site's gradient in registers and issues one set
+// of 16-byte atomics per (chunk, site).
+
+// Counting sort of the items of a ray chunk by cell: order[offsets[cell] + k] = item slot.
+__global__ void __launch_bounds__(kBlock)
+    cm_bucket_kernel(const float4* __restrict__ items, const int* __restrict__ stats, int64_t r0, int64_t n, int K,
+                     const int* __restrict__ offsets, int* __restrict__ fill, int* __restrict__ order) {
+    const int64_t rl = static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
+    if (rl >= n) return;
+    const int S = __ldg(stats + 3 * (r0 + rl));
+    if (S > K) return;
+    for (int s = 0; s < S; ++s) {
+        const int64_t slot = rl * K + s;
+        const int cell = __float_as_int(__ldg(items + 2 * slot + 1).w);
+        if (cell < 0) continue;
+        order[__ldg(offsets + cell) + atomicAdd(fill + cell, 1)] = static_cast<int>(slot);
+    }
+}
+
+// Chunks of at most 32 samples of one cell: (cell, first position in order, count).
+__global__ void __launch_bounds__(kBlock)
+    cm_chunks_kernel(const int* __restrict__ offsets, int n_cells, int4* __restrict__ chunks, int* n_chunks) {
+    const int i = blockIdx.x * kBlock + threadIdx.x;
+    const int lane = threadIdx.x & 31;
+    int cnt = 0, a = 0;
+    if (i < n_cells) a = __ldg(offsets + i), cnt = __ldg(offsets + i + 1) - a;
+    const int nch = (cnt + 31) >> 5;
+    int incl = nch;  // warp inclusive scan of the chunk counts, one atomic per warp
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+    }
+    int base = 0;
+    if (lane == 31 && incl > 0) base = atomicAdd(n_chunks, incl);
+    base = __shfl_sync(0xffffffffu, base, 31);
+    const int first = base + incl - nch;
+    for (int c = 0; c < nch; ++c) chunks[first + c] = make_int4(i, a + 32 * c, min(32, cnt - 32 * c), 0);
+}
+
+// Shared-memory image of one staged sample: x, gs | gC, gC.C | m_min, 1/sum a, -, - | SH basis (16).
+constexpr int kItemVec = 7;
+
+template <int S4>
+__global__ void __launch_bounds__(kBlock, 3)
+    cm_scatter_kernel(GraphView g, FieldView F, RayView R, const float* __restrict__ rec, int K,
+                      const float4* __restrict__ items, const int* __restrict__ order, const int4* __restrict__ chunks,
+                      const int* __restrict__ n_chunks_ptr, int64_t r0, float* __restrict__ grad) {
+    __shared__ float4 smem[(kBlock / 32) * 32 * kItemVec];
+    const int lane = threadIdx.x & 31;
+    float4* st = smem + (threadIdx.x >> 5) * 32 * kItemVec;
+    const int n_chunks = *n_chunks_ptr;
+    const int warps = gridDim.x * (kBlock / 32);
+    for (int ch = blockIdx.x * (kBlock / 32) + (threadIdx.x >> 5); ch < n_chunks; ch += warps) {
+        const int4 C = __ldg(chunks + ch);
+        const int cell = C.x, cnt = C.z;
+        if (lane < cnt) {  // stage this lane's sample
+            const int slot = __ldg(order + C.y + lane);
+            const int64_t r = r0 + slot / K;
+            const int sidx = slot % K;
+            const float t = __ldg(rec + (r * K + sidx) * kRecord);
+            float o[3], d[3];
+#pragma unroll
+            for (int a = 0; a < 3; ++a) o[a] = __ldg(R.o + 3 * r + a), d[a] = __ldg(R.d + 3 * r + a);
+            const float4 i0 = __ldg(items + 2 * static_cast<int64_t>(slot));
+            const float4 i1 = __ldg(items + 2 * static_cast<int64_t>(slot) + 1);
+            float b[16];
+            sh_basis(d[0], d[1], d[2], F.sh_deg, b);
+            float4* q = st + kItemVec * lane;
+            q[0] = make_float4(along(o[0], t, d[0]), along(o[1], t, d[1]), along(o[2], t, d[2]), i0.x);
+            q[1] = make_float4(i0.y, i0.z, i0.w, i1.x);
+            q[2] = make_float4(i1.y, i1.z, 0.f, 0.f);
+            q[3] = make_float4(b[0], b[1], b[2], b[3]);
+            q[4] = make_float4(b[4], b[5], b[6], b[7]);
+            q[5] = make_float4(b[8], b[9], b[10], b[11]);
+            q[6] = make_float4(b[12], b[13], b[14], b[15]);
+        }
+        __syncwarp();
+        const int e0 = __ldg(g.off + cell), e1 = __ldg(g.off + cell + 1);
+        for (int e = e0 + lane; e < e1; e += 32) {  // one neighbour site per lane
+            const float4 E = __ldg(g.edge + e);
+            const int j = site_of(E);
+            const float4* fr = F.rec + kFieldVec * static_cast<int64_t>(j);
+            const float4 r0_ = __ldg(fr), r1_ = __ldg(fr + 1), r2_ = __ldg(fr + 2), r3_ = __ldg(fr + 3);
+            float4 coef[S4];
+#pragma unroll
+            for (int q = 0; q < S4; ++q) coef[q] = __ldg(F.sh + static_cast<int64_t>(S4) * j + q);
+            float ad[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // g_raw, g_dA[6], -
+            float ac[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};              // g_cA[6]
+            float ash[4 * S4];                                          // g_sh
+#pragma unroll
+            for (int u = 0; u < 4 * S4; ++u) ash[u] = 0.f;
+            for (int i = 0; i < cnt; ++i) {
+                const float4* q = st + kItemVec * i;
+                const float4 q0 = q[0];
+                const float v0 = q0.x - E.x, v1 = q0.y - E.y, v2 = q0.z - E.z;
+                const float gs = q0.w;
+                if (gs != 0.f) {
+                    const float gc = gs * __expf(r1_.z - 0.5f * maha(r0_, r1_, v0, v1, v2));
+                    if (fabsf(gc) > 1e-12f) {
+                        const float gm = -0.5f * gc;
+                        ad[0] += gc, ad[1] += gm * v0 * v0, ad[2] += 2.f * gm * v0 * v1, ad[3] += 2.f * gm * v0 * v2;
+                        ad[4] += gm * v1 * v1, ad[5] += 2.f * gm * v1 * v2, ad[6] += gm * v2 * v2;
+                    }
+                }
+                const float4 q1 = q[1], q2 = q[2];
+                if (q2.y > 0.f) {  // the sample has a colour gradient
+                    const float a = __expf(-0.5f * (maha(r2_, r3_, v0, v1, v2) - q2.x)) * q2.y;
+                    if (a >= kMinWeight) {
+                        float b[16];
+                        const float4 b0 = q[3], b1 = q[4], b2 = q[5], b3 = q[6];
+                        b[0] = b0.x, b[1] = b0.y, b[2] = b0.z, b[3] = b0.w, b[4] = b1.x, b[5] = b1.y, b[6] = b1.z;
+                        b[7] = b1.w, b[8] = b2.x, b[9] = b2.y, b[10] = b2.z, b[11] = b2.w, b[12] = b3.x;
+                        b[13] = b3.y, b[14] = b3.z, b[15] = b3.w;
+                        float c[3] = {0.5f, 0.5f, 0.5f};
+#pragma unroll
+                        for (int qq = 0; qq < S4; ++qq) {
+                            const float f[4] = {coef[qq].x, coef[qq].y, coef[qq].z, coef[qq].w};
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) {
+                                const int k = 4 * qq + u;
+                                if (k < 48) c[k % 3] += b[k / 3] * f[u];
+                            }
+                        }
+                        const float dc[3] = {c[0] > 0.f ? a * q1.x : 0.f, c[1] > 0.f ? a * q1.y : 0.f,
+                                             c[2] > 0.f ? a * q1.z : 0.f};
+#pragma unroll
+                        for (int k = 0; k < 4 * S4; ++k)
+                            if (k < 48) ash[k] += b[k / 3] * dc[k % 3];
+                        const float ga = q1.x * fmaxf(c[0], 0.f) + q1.y * fmaxf(c[1], 0.f) + q1.z * fmaxf(c[2], 0.f);
+                        const float gm = -0.5f * a * (ga - q1.w);
+                        ac[0] += gm * v0 * v0, ac[1] += 2.f * gm * v0 * v1, ac[2] += 2.f * gm * v0 * v2;
+                        ac[3] += gm * v1 * v1, ac[4] += 2.f * gm * v1 * v2, ac[5] += gm * v2 * v2;
+                    }
+                }
+            }
+            float* G = grad + kGradStride * static_cast<int64_t>(j);
+            const float4 d0 = make_float4(ad[0], ad[1], ad[2], ad[3]), d1 = make_float4(ad[4], ad[5], ad[6], 0.f);
+            const float4 c0 = make_float4(ac[0], ac[1], ac[2], ac[3]), c1 = make_float4(ac[4], ac[5], 0.f, 0.f);
+            if (nonzero(d0)) red4(G, d0);
+            if (nonzero(d1)) red4(G + 4, d1);
+            if (nonzero(c0)) red4(G + 8, c0);
+            if (nonzero(c1)) red4(G + 12, c1);
+#pragma unroll
+            for (int qq = 0; qq < S4; ++qq) {
+                const float4 v = make_float4(ash[4 * qq], ash[4 * qq + 1], ash[4 * qq + 2], ash[4 * qq + 3]);
+                if (nonzero(v)) red4(G + 16 + 4 * qq, v);
+            }
+        }
+        __syncwarp();
+    }
 }
 
 inline int blocks(int64_t n) { return static_cast<int>((n + kBlock - 1) / kBlock); }
@@ -190,11 +452,111 @@ cudaError_t foam_forward(const GraphView& g, const FieldView& F, const RayView& 
     return cudaGetLastError();
 }
 
+namespace {
+
+constexpr int64_t kCmItems = int64_t(1) << 26;  // samples bucketed at once (2 GB of items)
+
+inline size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct CmLayout {
+    size_t items, order, count, fill, offsets, chunks, counter, temp, temp_bytes, total;
+    int64_t rays_per_pass;
+};
+
+CmLayout cm_layout(int64_t n_sites, int64_t n_rays, int K) {
+    CmLayout L{};
+    if (K <= 0 || n_rays <= 0) return L;
+    L.rays_per_pass = std::max<int64_t>(1, std::min<int64_t>(n_rays, kCmItems / K));
+    const int64_t slots = L.rays_per_pass * K;
+    size_t at = 0;
+    auto take = [&](size_t b) {
+        const size_t h = at;
+        at += al256(b);
+        return h;
+    };
+    L.items = take(32 * slots);
+    L.order = take(4 * slots);
+    L.count = take(4 * (n_sites + 1));
+    L.fill = take(4 * n_sites);
+    L.offsets = take(4 * (n_sites + 1));
+    L.chunks = take(16 * (slots / 32 + n_sites + 1));
+    L.counter = take(16);
+    size_t scan = 0;
+    cub::DeviceScan::ExclusiveSum(nullptr, scan, static_cast<const int*>(nullptr), static_cast<int*>(nullptr),
+                                  static_cast<int>(n_sites + 1));
+    L.temp_bytes = scan;
+    L.temp = take(scan);
+    L.total = at;
+    return L;
+}
+
+int sm_count() {
+    static int n = 0;
+    if (n == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+}  // namespace
+
+size_t foam_backward_workspace(int64_t n_sites, int64_t n_rays, int record_cap) {
+    return cm_layout(n_sites, n_rays, record_cap).total;
+}
+
 cudaError_t foam_backward(const GraphView& g, const FieldView& F, const RayView& R, const FoamCfg& c,
-                          const GradIn& gi, float* grad, int* status, cudaStream_t st) {
+                          const GradIn& gi, float* grad, int* status, void* cm_ws, size_t cm_bytes, cudaStream_t st) {
     if (R.n == 0) return cudaSuccess;
-    foam_backward_kernel<<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, gi, grad, status);
-    return cudaGetLastError();
+    const int K = gi.record_cap;
+    const CmLayout L = cm_layout(g.n, R.n, K);
+    const ItemOut none{nullptr, nullptr, 0, 0};
+    if (!VG_BWD_CELL_MAJOR || gi.rec == nullptr || K <= 0 || cm_ws == nullptr || cm_bytes < L.total ||
+        L.total == 0) {
+        foam_backward_kernel<kScatterAll><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, gi, grad, none, status);
+        return cudaGetLastError();
+    }
+    // rays with more samples than records: re-traced and scattered per ray
+    foam_backward_kernel<kScatterRetraced><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, gi, grad, none, status);
+    char* b = static_cast<char*>(cm_ws);
+    float4* items = reinterpret_cast<float4*>(b + L.items);
+    int* order = reinterpret_cast<int*>(b + L.order);
+    int* count = reinterpret_cast<int*>(b + L.count);
+    int* fill = reinterpret_cast<int*>(b + L.fill);
+    int* offsets = reinterpret_cast<int*>(b + L.offsets);
+    int4* chunks = reinterpret_cast<int4*>(b + L.chunks);
+    int* counter = reinterpret_cast<int*>(b + L.counter);
+    const int n = g.n;
+    const int grid = sm_count() * 3;
+    for (int64_t r0 = 0; r0 < R.n; r0 += L.rays_per_pass) {
+        const int64_t nr = std::min<int64_t>(L.rays_per_pass, R.n - r0);
+        cudaError_t e = cudaMemsetAsync(count, 0, 4 * static_cast<size_t>(n + 1), st);
+        if (e == cudaSuccess) e = cudaMemsetAsync(fill, 0, 4 * static_cast<size_t>(n), st);
+        if (e == cudaSuccess) e = cudaMemsetAsync(counter, 0, 16, st);
+        if (e != cudaSuccess) return e;
+        const ItemOut io{items, count, r0, nr};
+        foam_backward_kernel<kItems><<<blocks(nr), kBlock, 0, st>>>(g, F, R, c, gi, grad, io, status);
+        size_t tb = L.temp_bytes;
+        e = cub::DeviceScan::ExclusiveSum(b + L.temp, tb, count, offsets, n + 1, st);
+        if (e != cudaSuccess) return e;
+        cm_bucket_kernel<<<blocks(nr), kBlock, 0, st>>>(items, gi.stats, r0, nr, K, offsets, fill, order);
+        cm_chunks_kernel<<<blocks(n), kBlock, 0, st>>>(offsets, n, chunks, counter);
+        switch (F.s4) {
+            case 1: cm_scatter_kernel<1><<<grid, kBlock, 0, st>>>(g, F, R, gi.rec, K, items, order, chunks, counter, r0,
+                                                                  grad); break;
+            case 3: cm_scatter_kernel<3><<<grid, kBlock, 0, st>>>(g, F, R, gi.rec, K, items, order, chunks, counter, r0,
+                                                                  grad); break;
+            case 7: cm_scatter_kernel<7><<<grid, kBlock, 0, st>>>(g, F, R, gi.rec, K, items, order, chunks, counter, r0,
+                                                                  grad); break;
+            default: cm_scatter_kernel<12><<<grid, kBlock, 0, st>>>(g, F, R, gi.rec, K, items, order, chunks, counter,
+                                                                    r0, grad); break;
+        }
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 }  // namespace vg

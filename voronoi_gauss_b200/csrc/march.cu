@@ -7,11 +7,21 @@
 // ray with identical arithmetic and scatters gradients with 16-byte vector atomics (march.cu:264-345).
 #include "render_core.cuh"
 
+// Colour cache slots and warp-aggregated atomics: see foam.cu.
+#ifndef VG_MARCH_SLOTS
+#define VG_MARCH_SLOTS 0
+#endif
+#ifndef VG_BWD_AGG
+#define VG_BWD_AGG 0
+#endif
+
 namespace vg {
 namespace {
 
 constexpr int kBlock = 128;
-constexpr int kSlots = 8;
+constexpr int kSlots = VG_MARCH_SLOTS;
+constexpr int kSlotMem = kSlots > 0 ? kSlots * kBlock : 1;
+constexpr bool kAgg = VG_BWD_AGG != 0;
 
 struct MRay {
     float o[3], d[3];
@@ -43,7 +53,7 @@ __device__ __forceinline__ void sample_at(const MRay& M, const MarchCfg& c, int 
 
 __global__ void __launch_bounds__(kBlock)
     march_forward_kernel(GraphView g, FieldView F, RayView R, MarchCfg c, Outputs out, int* status) {
-    __shared__ float4 cache_mem[kSlots * kBlock];
+    __shared__ float4 cache_mem[kSlotMem];
     const int64_t r = static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
     if (r >= R.n) return;
     ColorCache<kSlots> cache{cache_mem + threadIdx.x, kBlock};
@@ -84,7 +94,10 @@ __global__ void __launch_bounds__(kBlock)
 __global__ void __launch_bounds__(kBlock)
     march_backward_kernel(GraphView g, FieldView F, RayView R, MarchCfg c, GradIn gi, float* __restrict__ grad,
                           int* status) {
-    __shared__ float4 cache_mem[kSlots * kBlock];
+    __shared__ float4 cache_mem[kSlotMem];
+    __shared__ float4 stage_mem[kAgg ? 16 * kBlock : 1];
+    float4* stage = stage_mem + (kAgg ? 16 * (threadIdx.x & ~31) : 0);
+    const int lane = threadIdx.x & 31;
     const int64_t r = static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
     if (r >= R.n) return;
     ColorCache<kSlots> cache{cache_mem + threadIdx.x, kBlock};
@@ -118,8 +131,12 @@ __global__ void __launch_bounds__(kBlock)
         float gsig = gR0 * (T_next * S.C0 - (fg0 - acc0)) + gR1 * (T_next * S.C1 - (fg1 - acc1)) +
                      gR2 * (T_next * S.C2 - (fg2 - acc2));
         gsig = delta * (gsig - gT_final);
-        scatter_sample(g, F, S, gsig, active ? w * gR0 : 0.f, active ? w * gR1 : 0.f, active ? w * gR2 : 0.f, active,
-                       b, cache, grad);
+        if (kAgg)
+            scatter_sample_agg(g, F, S, gsig, active ? w * gR0 : 0.f, active ? w * gR1 : 0.f, active ? w * gR2 : 0.f,
+                               active, b, cache, grad, stage, lane);
+        else
+            scatter_sample(g, F, S, gsig, active ? w * gR0 : 0.f, active ? w * gR1 : 0.f, active ? w * gR2 : 0.f,
+                           active, b, cache, grad);
         T = T_next;
         if (T < c.t_thresh) break;
     }

@@ -180,9 +180,15 @@ __device__ __forceinline__ void blend_add(Blend& B, float m, float r, float g, f
     B.a += w, B.r += w * r, B.g += w * g, B.b += w * b;
 }
 
-// Per-thread direct-mapped cache of the clamped site colours max(SH_k(d) + 1/2, 0) in shared memory:
-// a site belongs to the neighbourhoods of several consecutive cells of a ray and its colour depends
-// only on the ray direction. Slot s of thread t lives at base[s * stride + t].
+// Clamped site colour max(SH_k(d) + 1/2, 0) of site k for the ray direction of basis b.
+__device__ __forceinline__ void site_color(const FieldView& F, int k, const float (&b)[16], float (&c)[3]) {
+    sh_color(F, k, b, c);
+    c[0] = fmaxf(c[0], 0.f), c[1] = fmaxf(c[1], 0.f), c[2] = fmaxf(c[2], 0.f);
+}
+
+// Per-thread direct-mapped cache of the clamped site colours in shared memory: a site belongs to the
+// neighbourhoods of several consecutive cells of a ray and its colour depends only on the ray
+// direction. Slot s of thread t lives at base[s * stride + t]. SLOTS = 0: no cache.
 template <int SLOTS>
 struct ColorCache {
     float4* base;
@@ -198,9 +204,18 @@ struct ColorCache {
             c[0] = v.x, c[1] = v.y, c[2] = v.z;
             return;
         }
-        sh_color(F, k, b, c);
-        c[0] = fmaxf(c[0], 0.f), c[1] = fmaxf(c[1], 0.f), c[2] = fmaxf(c[2], 0.f);
+        site_color(F, k, b, c);
         e = make_float4(c[0], c[1], c[2], __int_as_float(k));
+    }
+};
+
+template <>
+struct ColorCache<0> {
+    float4* base;
+    int stride;
+    __device__ __forceinline__ void init() {}
+    __device__ __forceinline__ void get(const FieldView& F, int k, const float (&b)[16], float (&c)[3]) {
+        site_color(F, k, b, c);
     }
 };
 
@@ -260,8 +275,10 @@ cudaError_t grad_unpack(const GraphView& g, const float* grad, int sh_deg, float
 // foam.cu
 cudaError_t foam_forward(const GraphView& g, const FieldView& F, const RayView& R, const FoamCfg& c,
                          const Outputs& out, int* status, cudaStream_t st);
+// Scratch of the cell-major backward (rays fully recorded in records of capacity record_cap).
+size_t foam_backward_workspace(int64_t n_sites, int64_t n_rays, int record_cap);
 cudaError_t foam_backward(const GraphView& g, const FieldView& F, const RayView& R, const FoamCfg& c,
-                          const GradIn& gi, float* grad, int* status, cudaStream_t st);
+                          const GradIn& gi, float* grad, int* status, void* cm_ws, size_t cm_bytes, cudaStream_t st);
 
 // march.cu
 cudaError_t march_forward(const GraphView& g, const FieldView& F, const RayView& R, const MarchCfg& c,

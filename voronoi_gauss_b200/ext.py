@@ -147,8 +147,8 @@ def _ray_checks(**rays):
     return B
 
 
-def _workspace(n, sh_deg, backward, dev):
-    nbytes = _lib.lib().vg_foam_workspace_bytes(n, int(sh_deg), int(backward))
+def _workspace(n, sh_deg, backward, dev, n_rays=0, record_cap=0):
+    nbytes = _lib.lib().vg_foam_workspace_bytes(n, int(sh_deg), int(n_rays), int(record_cap), int(backward))
     return torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev), nbytes
 
 
@@ -202,7 +202,7 @@ class FoamExtension:
         dev = o.device
         g_raw, g_dA, g_cA, g_sh = (torch.empty_like(x) for x in (raw, dA, cA, sh))
         pk = graph_pack(points, offsets, adj)
-        ws, nbytes = _workspace(pk.n, sh_deg, True, dev)
+        ws, nbytes = _workspace(pk.n, sh_deg, 1, dev, B, rec.size(1) if replay else 0)
         ev = BACKWARD_EVENTS
         with torch.cuda.device(dev):
             if ev is not None:
