@@ -106,6 +106,21 @@ int vg_foam_backward_packed(const void* pack, int64_t n_sites, int64_t n_adj, co
 int vg_grad_unpack(const void* pack, int64_t n_sites, int64_t n_adj, const float* grad_pack, int sh_deg,
                    float* g_raw, float* g_dA, float* g_cA, float* g_sh, void* stream);
 
+/* vg_foam_forward for callers that cannot allocate device memory while rendering (a plugin inside a
+ * host that owns a fixed memory pool, a real-time viewer that reserves all buffers at start-up, a
+ * process whose device memory belongs to another framework's allocator). No counterpart in the
+ * reference. Same arguments and outputs as vg_foam_forward without the workspace: the per-site
+ * scratch lives in a static device array (32 MiB, allocated when the library loads on a device and
+ * held by every device that loads it until exit), so n_sites is limited to 131072 (VG_ERR_WORKSPACE
+ * beyond). The first call on a device looks up that array's address (make it before any stream
+ * capture). Calls share the array: calls that overlap on the GPU race and must be ordered by the
+ * caller (e.g. one stream). Allocates and frees nothing. */
+int vg_foam_forward_noalloc(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA,
+                            const float* cA, const float* sh, int sh_deg, const float* o, const float* d,
+                            const int32_t* start, const float* near, const float* far, int64_t n_rays,
+                            float t_thresh, float w_thresh, int record_cap, float* rgb, float* T, float* depth,
+                            int32_t* stats, float* rec, void* stream);
+
 /* ------------------------------------------------------------------------------- fixed steps */
 
 /* march_forward (march.cu:383-403): midpoints of steps dt in [near, mid], n_bg disparity steps in

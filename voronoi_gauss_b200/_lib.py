@@ -33,6 +33,8 @@ SIGNATURES = {
     'vg_foam_workspace_bytes': (SZ, [I64, I32, I64, I32, I32]),
     'vg_foam_forward': (I32, [P, I64, I64, P, P, P, P, I32, P, P, P, P, P, I64, F32, F32, I32, P, P, P, P, P, P, SZ,
                               P]),
+    'vg_foam_forward_noalloc': (I32, [P, I64, I64, P, P, P, P, I32, P, P, P, P, P, I64, F32, F32, I32, P, P, P, P,
+                                      P, P]),
     'vg_foam_backward': (I32, [P, I64, I64, P, P, P, P, I32, P, P, P, P, P, I64, F32, F32, P, P, P, P, P, I32, P, P, P,
                                P, P, P, SZ, P]),
     'vg_foam_backward_packed': (I32, [P, I64, I64, P, P, P, P, I32, P, P, P, P, P, I64, F32, F32, P, P, P, P, P, I32,

@@ -86,6 +86,10 @@ size_t grad_ws(int64_t n) { return align256(static_cast<size_t>(n) * vg::kGradSt
 
 }  // namespace
 
+namespace vg {
+int set_error(int code, const char* msg) { return fail(code, "%s", msg); }
+}  // namespace vg
+
 extern "C" {
 
 int vg_version(void) { return 100; }

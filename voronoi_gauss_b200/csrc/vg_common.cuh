@@ -260,6 +260,9 @@ struct GradIn {
     int record_cap;
 };
 
+// capi.cu: records the message returned by vg_last_error on this thread and returns code
+int set_error(int code, const char* msg);
+
 // pack.cu
 size_t graph_pack_bytes(int64_t n, int64_t m);
 cudaError_t graph_pack(const float* points, const int* offsets, const int* adj, int64_t n, int64_t m, void* pack,
