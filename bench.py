@@ -150,6 +150,14 @@ def algorithmic_bytes(stats, rec, offsets, nb):
     return float(fwd), float(bwd), n_bar
 
 
+def launches_per_step(n_rays, record_cap):
+    """libvgb200 kernels launched by one training step: 2 conics, field pack + forward, field pack +
+    per-ray backward (re-traced rays) + 4 cell-major kernels per pass of at most 2^26 recorded samples,
+    gradient unpack, 2 conic backwards (the CUB scan inside each pass is not counted)."""
+    passes = math.ceil(n_rays / max(1, (1 << 26) // record_cap))
+    return 2 + 2 + 2 + 4 * passes + 1 + 2
+
+
 # --------------------------------------------------------------------------------------- b200 arm
 
 def run_b200(args):
@@ -315,7 +323,7 @@ def run_b200(args):
                              'layout); L1/L2 reuse across the rays of a tile lets achieved exceed DRAM traffic'},
         'e2e': {'value': round(rays_total / (e2e_ms * 1e-3) / 1e6, 3), 'unit': 'Mrays/s', 'ms_per_step':
                 round(e2e_ms, 3), 'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': 4},
-        'gpu_launches': 9 * args.steps,
+        'gpu_launches': launches_per_step(B, RECORD_CAP) * args.steps,
         'clocks': clocks,
     }
     traffic = os.path.join(ROOT, 'profiles', 'traffic.json')
