@@ -134,7 +134,7 @@ int vg_graph_pack(const float* points, const int32_t* offsets, const int32_t* ad
 
 size_t vg_foam_workspace_bytes(int64_t n_sites, int sh_deg, int64_t n_rays, int record_cap, int backward) {
     if (n_sites <= 0 || sh_deg < 0 || sh_deg > 3 || n_rays < 0 || record_cap < 0) return 0;
-    if (backward == 0) return field_ws(n_sites, sh_deg);
+    if (backward == 0) return field_ws(n_sites, sh_deg) + align256(vg::foam_forward_workspace(n_sites, n_rays, record_cap));
     const size_t cm = align256(vg::foam_backward_workspace(n_sites, n_rays, record_cap));
     return field_ws(n_sites, sh_deg) + (backward == 1 ? grad_ws(n_sites) : 0) + cm;
 }
@@ -166,7 +166,9 @@ int vg_foam_forward(const void* pack, int64_t n_sites, int64_t n_adj, const floa
     const vg::RayView R{o, d, start, near, nullptr, far, n_rays};
     const vg::FoamCfg c{t_thresh, w_thresh, record_cap};
     const vg::Outputs out{rgb, T, depth, stats, record_cap > 0 ? rec : nullptr};
-    e = vg::foam_forward(g, F, R, c, out, status, st);
+    // scratch beyond the field records enables the cell-major colour pass (inline colours otherwise)
+    const size_t fw = field_ws(n_sites, sh_deg);
+    e = vg::foam_forward(g, F, R, c, out, status, static_cast<char*>(workspace) + fw, workspace_bytes - fw, st);
     return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_foam_forward");
 }
 

@@ -41,6 +41,10 @@
 #ifndef VG_BWD_MINB
 #define VG_BWD_MINB 1
 #endif
+// VG_FWD_CELL_MAJOR  1: colours of fully recorded rays evaluated cell-major (see cmf_color_kernel)
+#ifndef VG_FWD_CELL_MAJOR
+#define VG_FWD_CELL_MAJOR 1
+#endif
 // VG_BWD_CELL_MAJOR  1: samples of fully recorded rays scattered cell-major (see cm_scatter_kernel)
 #ifndef VG_BWD_CELL_MAJOR
 #define VG_BWD_CELL_MAJOR 1
@@ -57,12 +61,14 @@ constexpr int kBwdSlotMem = kBwdSlots > 0 ? kBwdSlots * kBlock : 1;
 constexpr bool kLazy = VG_LAZY_COLOR != 0;
 constexpr bool kAgg = VG_BWD_AGG != 0;
 
+// deferred: the colour fields are filled later; the last field marks the samples that need one (-1)
 __device__ __forceinline__ void store_sample(float* __restrict__ rec, int64_t r, int K, int s, const Sample& P,
-                                             bool has_c, const int* __restrict__ perm) {
+                                             bool has_c, bool deferred, const int* __restrict__ perm) {
     if (s >= K) return;
     float4* q = reinterpret_cast<float4*>(rec + (r * K + s) * kRecord);
-    q[0] = make_float4(P.t, __int_as_float(__ldg(perm + P.cell)), P.sigma, P.C0);
-    q[1] = make_float4(P.C1, P.C2, P.mmin, has_c ? P.inv_a : 0.f);
+    q[0] = make_float4(P.t, __int_as_float(__ldg(perm + P.cell)), P.sigma, deferred ? 0.f : P.C0);
+    q[1] = deferred ? make_float4(0.f, 0.f, 0.f, has_c ? -1.f : 0.f)
+                    : make_float4(P.C1, P.C2, P.mmin, has_c ? P.inv_a : 0.f);
 }
 
 __device__ __forceinline__ void load_sample(const float* __restrict__ rec, int64_t r, int K, int s,
@@ -85,27 +91,34 @@ __device__ __forceinline__ void load_ray(const RayView& R, int64_t r, float (&o)
     near = __ldg(R.near + r), far = __ldg(R.far + r);
 }
 
-template <bool RECORD>
+// What the forward does with colours: evaluate them inline for the segments that need them (every ray,
+// or only the rays with more samples than records), or defer them to the cell-major colour pass and
+// only mark, in the record's last field, the samples that need one (-1; 0 otherwise).
+enum FwdMode { kImmediate = 0, kImmediateOverflow = 1, kDeferred = 2 };
+
+template <bool RECORD, int MODE>
 __global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
     foam_forward_kernel(GraphView g, FieldView F, RayView R, FoamCfg c, Outputs out, int* status) {
     __shared__ float4 cache_mem[kFwdSlotMem];
     const int64_t r = static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
     if (r >= R.n) return;
+    const int K = c.record_cap;
+    if (MODE == kImmediateOverflow && __ldg(out.stats + 3 * r) <= K) return;
+    constexpr bool kDefer = MODE == kDeferred;
     ColorCache<kFwdSlots> cache{cache_mem + threadIdx.x, kBlock};
     cache.init();
     float o[3], d[3], near, far;
     load_ray(R, r, o, d, near, far);
     float b[16];
-    sh_basis(d[0], d[1], d[2], F.sh_deg, b);
+    if (!kDefer) sh_basis(d[0], d[1], d[2], F.sh_deg, b);
     int err = 0, walk_steps = 0, n_samples = 1, n_color = 0;
-    const int K = c.record_cap;
     int cur = walk_to(g, __ldg(g.inv + __ldg(R.start + r)), along(o[0], near, d[0]), along(o[1], near, d[1]),
                       along(o[2], near, d[2]), walk_steps, err);
     Sample P;
     float t_exit;
     int next;
-    eval_sample<kFwdSlots, !kLazy>(g, F, cur, near, o, d, b, cache, true, P, t_exit, next);
-    bool has_p = !kLazy;
+    eval_sample<kFwdSlots, !kLazy && !kDefer>(g, F, cur, near, o, d, b, cache, true, P, t_exit, next);
+    bool has_p = !kLazy && !kDefer;
     float T = 1.f, acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, dep = 0.f;
     int it = 0;
     for (; it < kMaxCells; ++it) {
@@ -113,38 +126,173 @@ __global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
         Sample Q;
         float t_exit_q;
         int next_q;
-        eval_sample<kFwdSlots, !kLazy>(g, F, last ? P.cell : next, last ? far : fmaxf(t_exit, P.t), o, d, b, cache, !last,
-                                    Q, t_exit_q, next_q);
-        bool has_q = !kLazy;
+        eval_sample<kFwdSlots, !kLazy && !kDefer>(g, F, last ? P.cell : next, last ? far : fmaxf(t_exit, P.t), o, d, b,
+                                                  cache, !last, Q, t_exit_q, next_q);
+        bool has_q = !kLazy && !kDefer;
         ++n_samples;
         const float delta = Q.t - P.t;
         const float alpha = 1.f - __expf(-0.5f * (P.sigma + Q.sigma) * delta);
         const float w = T * alpha;
         if (w > c.w_thresh) {
-            if (kLazy) {
-                if (!has_p) eval_color(g, F, b, cache, P), has_p = true;
-                eval_color(g, F, b, cache, Q), has_q = true;
+            if (kDefer) {
+                has_p = has_q = true;  // marked: coloured by the cell-major pass
+            } else {
+                if (kLazy) {
+                    if (!has_p) eval_color(g, F, b, cache, P), has_p = true;
+                    eval_color(g, F, b, cache, Q), has_q = true;
+                }
+                acc0 += w * 0.5f * (P.C0 + Q.C0);
+                acc1 += w * 0.5f * (P.C1 + Q.C1);
+                acc2 += w * 0.5f * (P.C2 + Q.C2);
             }
-            acc0 += w * 0.5f * (P.C0 + Q.C0);
-            acc1 += w * 0.5f * (P.C1 + Q.C1);
-            acc2 += w * 0.5f * (P.C2 + Q.C2);
             dep += w * 0.5f * (P.t + Q.t);
             ++n_color;
         }
         T *= 1.f - alpha;
-        if (RECORD) store_sample(out.rec, r, K, n_samples - 2, P, has_p, g.perm);
+        if (RECORD) store_sample(out.rec, r, K, n_samples - 2, P, has_p, kDefer, g.perm);
         P = Q;
         has_p = has_q;
         t_exit = t_exit_q, next = next_q;
         if (last || T < c.t_thresh) break;
     }
     if (it == kMaxCells) err |= kErrCellCap;
-    if (RECORD) store_sample(out.rec, r, K, n_samples - 1, P, has_p, g.perm);
-    out.rgb[3 * r] = acc0, out.rgb[3 * r + 1] = acc1, out.rgb[3 * r + 2] = acc2;
+    if (RECORD) store_sample(out.rec, r, K, n_samples - 1, P, has_p, kDefer, g.perm);
+    if (!kDefer) out.rgb[3 * r] = acc0, out.rgb[3 * r + 1] = acc1, out.rgb[3 * r + 2] = acc2;
     out.T[r] = T;
     out.depth[r] = dep;
     out.stats[3 * r] = n_samples, out.stats[3 * r + 1] = n_color, out.stats[3 * r + 2] = walk_steps;
     if (err) atomicOr(status, err);
+}
+
+// ------------------------------------------------------------------- cell-major colours (forward)
+//
+// Deferred colours: the traversal marks the samples that border a segment with weight > w_thresh;
+// those samples are bucketed by cell (the counting sort of the backward) and a warp evaluates up to
+// 32 samples of one cell at a time, one lane per sample: every lane walks the same neighbour list, so
+// the edge, site-record and SH loads are warp-uniform broadcasts. The blend visits the neighbours in
+// the cell's order with the same arithmetic as eval_color, so the colours are bit-identical to the
+// inline path; cmf_composite_kernel then sums the segments of every ray from its records.
+
+// Samples of a ray chunk that need a colour, counted per cell.
+__global__ void __launch_bounds__(kBlock)
+    cmf_count_kernel(const float* __restrict__ rec, const int* __restrict__ stats, const int* __restrict__ inv,
+                     int64_t r0, int64_t n, int K, int* __restrict__ count) {
+    const int64_t rl = static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
+    if (rl >= n) return;
+    const int64_t r = r0 + rl;
+    const int S = __ldg(stats + 3 * r);
+    if (S > K) return;
+    for (int s = 0; s < S; ++s) {
+        const float4 q1 = __ldg(reinterpret_cast<const float4*>(rec + (r * K + s) * kRecord) + 1);
+        if (q1.w < 0.f) {
+            const int site = __float_as_int(__ldg(rec + (r * K + s) * kRecord + 1));
+            atomicAdd(count + __ldg(inv + site), 1);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kBlock)
+    cmf_bucket_kernel(const float* __restrict__ rec, const int* __restrict__ stats, const int* __restrict__ inv,
+                      int64_t r0, int64_t n, int K, const int* __restrict__ offsets, int* __restrict__ fill,
+                      int* __restrict__ order) {
+    const int64_t rl = static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
+    if (rl >= n) return;
+    const int64_t r = r0 + rl;
+    const int S = __ldg(stats + 3 * r);
+    if (S > K) return;
+    for (int s = 0; s < S; ++s) {
+        const float4 q1 = __ldg(reinterpret_cast<const float4*>(rec + (r * K + s) * kRecord) + 1);
+        if (q1.w < 0.f) {
+            const int cell = __ldg(inv + __float_as_int(__ldg(rec + (r * K + s) * kRecord + 1)));
+            order[__ldg(offsets + cell) + atomicAdd(fill + cell, 1)] = static_cast<int>(rl * K + s);
+        }
+    }
+}
+
+template <int S4>
+__global__ void __launch_bounds__(kBlock)
+    cmf_color_kernel(GraphView g, FieldView F, RayView R, float* __restrict__ rec, int K,
+                     const int* __restrict__ order, const int4* __restrict__ chunks, const int* __restrict__ n_chunks_ptr,
+                     int64_t r0) {
+    const int lane = threadIdx.x & 31;
+    const int n_chunks = *n_chunks_ptr;
+    const int warps = gridDim.x * (kBlock / 32);
+    for (int ch = blockIdx.x * (kBlock / 32) + (threadIdx.x >> 5); ch < n_chunks; ch += warps) {
+        const int4 C = __ldg(chunks + ch);
+        const bool on = lane < C.z;
+        int64_t r = r0, s = 0;
+        float x0 = 0.f, x1 = 0.f, x2 = 0.f, b[16];
+        if (on) {
+            const int slot = __ldg(order + C.y + lane);
+            r = r0 + slot / K, s = slot % K;
+            const float t = rec[(r * K + s) * kRecord];
+            float o[3], d[3];
+#pragma unroll
+            for (int a = 0; a < 3; ++a) o[a] = __ldg(R.o + 3 * r + a), d[a] = __ldg(R.d + 3 * r + a);
+            x0 = along(o[0], t, d[0]), x1 = along(o[1], t, d[1]), x2 = along(o[2], t, d[2]);
+            sh_basis(d[0], d[1], d[2], F.sh_deg, b);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 16; ++k) b[k] = 0.f;
+        }
+        const int e0 = __ldg(g.off + C.x), e1 = __ldg(g.off + C.x + 1);
+        Blend B;
+        blend_init(B);
+        for (int e = e0; e < e1; ++e) {  // warp-uniform: one cell per chunk
+            const float4 E = __ldg(g.edge + e);
+            const int j = site_of(E);
+            const float4* fr = F.rec + kFieldVec * static_cast<int64_t>(j);
+            const float4 r2 = __ldg(fr + 2), r3 = __ldg(fr + 3);
+            const float v0 = x0 - E.x, v1 = x1 - E.y, v2 = x2 - E.z;
+            float c[3] = {0.5f, 0.5f, 0.5f};
+            const float4* sp = F.sh + static_cast<int64_t>(S4) * j;
+#pragma unroll
+            for (int q = 0; q < S4; ++q) {
+                const float4 v = __ldg(sp + q);
+                const float f[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int i = 4 * q + u;
+                    if (i < 48) c[i % 3] += b[i / 3] * f[u];
+                }
+            }
+            blend_add(B, maha(r2, r3, v0, v1, v2), fmaxf(c[0], 0.f), fmaxf(c[1], 0.f), fmaxf(c[2], 0.f));
+        }
+        if (on) {
+            const float inv_a = 1.f / B.a;
+            float* q = rec + (r * K + s) * kRecord;
+            q[3] = B.r * inv_a;
+            reinterpret_cast<float4*>(q)[1] = make_float4(B.g * inv_a, B.b * inv_a, B.m, inv_a);
+        }
+    }
+}
+
+// Sums the coloured segments of every fully recorded ray from its records (same arithmetic as the
+// traversal, so the weights and the set of coloured segments are the same).
+__global__ void __launch_bounds__(kBlock)
+    cmf_composite_kernel(const float* __restrict__ rec, const int* __restrict__ stats, int64_t n, int K,
+                         float w_thresh, float* __restrict__ rgb) {
+    const int64_t r = static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
+    if (r >= n) return;
+    const int S = __ldg(stats + 3 * r);
+    if (S > K) return;
+    const float4* q = reinterpret_cast<const float4*>(rec + r * K * kRecord);
+    float4 a0 = __ldg(q), a1 = __ldg(q + 1);
+    float T = 1.f, acc0 = 0.f, acc1 = 0.f, acc2 = 0.f;
+    for (int s = 1; s < S; ++s) {
+        const float4 b0 = __ldg(q + 2 * s), b1 = __ldg(q + 2 * s + 1);
+        const float delta = b0.x - a0.x;
+        const float alpha = 1.f - __expf(-0.5f * (a0.z + b0.z) * delta);
+        const float w = T * alpha;
+        if (w > w_thresh) {
+            acc0 += w * 0.5f * (a0.w + b0.w);
+            acc1 += w * 0.5f * (a1.x + b1.x);
+            acc2 += w * 0.5f * (a1.y + b1.y);
+        }
+        T *= 1.f - alpha;
+        a0 = b0, a1 = b1;
+    }
+    rgb[3 * r] = acc0, rgb[3 * r + 1] = acc1, rgb[3 * r + 2] = acc2;
 }
 
 // Per-sample record of the cell-major backward: the sample's gradient scalars, written by the replay
@@ -442,16 +590,6 @@ inline int blocks(int64_t n) { return static_cast<int>((n + kBlock - 1) / kBlock
 
 }  // namespace
 
-cudaError_t foam_forward(const GraphView& g, const FieldView& F, const RayView& R, const FoamCfg& c,
-                         const Outputs& out, int* status, cudaStream_t st) {
-    if (R.n == 0) return cudaSuccess;
-    if (c.record_cap > 0 && out.rec != nullptr)
-        foam_forward_kernel<true><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, out, status);
-    else
-        foam_forward_kernel<false><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, out, status);
-    return cudaGetLastError();
-}
-
 namespace {
 
 constexpr int64_t kCmItems = int64_t(1) << 26;  // samples bucketed at once (2 GB of items)
@@ -463,7 +601,10 @@ struct CmLayout {
     int64_t rays_per_pass;
 };
 
-CmLayout cm_layout(int64_t n_sites, int64_t n_rays, int K) {
+// Scratch of the cell-major passes over rays [r0, r0 + rays_per_pass): per-sample items (backward
+// only), the cell-sorted order, per-cell counts / fill cursors / offsets, the chunk list, a counter and
+// the CUB scan storage.
+CmLayout cm_layout(int64_t n_sites, int64_t n_rays, int K, bool with_items) {
     CmLayout L{};
     if (K <= 0 || n_rays <= 0) return L;
     L.rays_per_pass = std::max<int64_t>(1, std::min<int64_t>(n_rays, kCmItems / K));
@@ -474,7 +615,7 @@ CmLayout cm_layout(int64_t n_sites, int64_t n_rays, int K) {
         at += al256(b);
         return h;
     };
-    L.items = take(32 * slots);
+    L.items = take(with_items ? 32 * slots : 0);
     L.order = take(4 * slots);
     L.count = take(4 * (n_sites + 1));
     L.fill = take(4 * n_sites);
@@ -504,14 +645,69 @@ int sm_count() {
 }  // namespace
 
 size_t foam_backward_workspace(int64_t n_sites, int64_t n_rays, int record_cap) {
-    return cm_layout(n_sites, n_rays, record_cap).total;
+    return cm_layout(n_sites, n_rays, record_cap, true).total;
+}
+
+size_t foam_forward_workspace(int64_t n_sites, int64_t n_rays, int record_cap) {
+    return VG_FWD_CELL_MAJOR ? cm_layout(n_sites, n_rays, record_cap, false).total : 0;
+}
+
+cudaError_t foam_forward(const GraphView& g, const FieldView& F, const RayView& R, const FoamCfg& c,
+                         const Outputs& out, int* status, void* cm_ws, size_t cm_bytes, cudaStream_t st) {
+    if (R.n == 0) return cudaSuccess;
+    const int K = c.record_cap;
+    const bool record = K > 0 && out.rec != nullptr;
+    const CmLayout L = cm_layout(g.n, R.n, K, false);
+    if (!record) {
+        foam_forward_kernel<false, kImmediate><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, out, status);
+        return cudaGetLastError();
+    }
+    if (!VG_FWD_CELL_MAJOR || cm_ws == nullptr || L.total == 0 || cm_bytes < L.total) {
+        foam_forward_kernel<true, kImmediate><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, out, status);
+        return cudaGetLastError();
+    }
+    // traversal with deferred colours, then inline colours for the rays with more samples than records
+    foam_forward_kernel<true, kDeferred><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, out, status);
+    foam_forward_kernel<true, kImmediateOverflow><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, out, status);
+    char* b = static_cast<char*>(cm_ws);
+    int* order = reinterpret_cast<int*>(b + L.order);
+    int* count = reinterpret_cast<int*>(b + L.count);
+    int* fill = reinterpret_cast<int*>(b + L.fill);
+    int* offsets = reinterpret_cast<int*>(b + L.offsets);
+    int4* chunks = reinterpret_cast<int4*>(b + L.chunks);
+    int* counter = reinterpret_cast<int*>(b + L.counter);
+    const int n = g.n;
+    const int grid = sm_count() * 8;
+    for (int64_t r0 = 0; r0 < R.n; r0 += L.rays_per_pass) {
+        const int64_t nr = std::min<int64_t>(L.rays_per_pass, R.n - r0);
+        cudaError_t e = cudaMemsetAsync(count, 0, 4 * static_cast<size_t>(n + 1), st);
+        if (e == cudaSuccess) e = cudaMemsetAsync(fill, 0, 4 * static_cast<size_t>(n), st);
+        if (e == cudaSuccess) e = cudaMemsetAsync(counter, 0, 16, st);
+        if (e != cudaSuccess) return e;
+        cmf_count_kernel<<<blocks(nr), kBlock, 0, st>>>(out.rec, out.stats, g.inv, r0, nr, K, count);
+        size_t tb = L.temp_bytes;
+        e = cub::DeviceScan::ExclusiveSum(b + L.temp, tb, count, offsets, n + 1, st);
+        if (e != cudaSuccess) return e;
+        cmf_bucket_kernel<<<blocks(nr), kBlock, 0, st>>>(out.rec, out.stats, g.inv, r0, nr, K, offsets, fill, order);
+        cm_chunks_kernel<<<blocks(n), kBlock, 0, st>>>(offsets, n, chunks, counter);
+        switch (F.s4) {
+            case 1: cmf_color_kernel<1><<<grid, kBlock, 0, st>>>(g, F, R, out.rec, K, order, chunks, counter, r0); break;
+            case 3: cmf_color_kernel<3><<<grid, kBlock, 0, st>>>(g, F, R, out.rec, K, order, chunks, counter, r0); break;
+            case 7: cmf_color_kernel<7><<<grid, kBlock, 0, st>>>(g, F, R, out.rec, K, order, chunks, counter, r0); break;
+            default: cmf_color_kernel<12><<<grid, kBlock, 0, st>>>(g, F, R, out.rec, K, order, chunks, counter, r0);
+        }
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    cmf_composite_kernel<<<blocks(R.n), kBlock, 0, st>>>(out.rec, out.stats, R.n, K, c.w_thresh, out.rgb);
+    return cudaGetLastError();
 }
 
 cudaError_t foam_backward(const GraphView& g, const FieldView& F, const RayView& R, const FoamCfg& c,
                           const GradIn& gi, float* grad, int* status, void* cm_ws, size_t cm_bytes, cudaStream_t st) {
     if (R.n == 0) return cudaSuccess;
     const int K = gi.record_cap;
-    const CmLayout L = cm_layout(g.n, R.n, K);
+    const CmLayout L = cm_layout(g.n, R.n, K, true);
     const ItemOut none{nullptr, nullptr, 0, 0};
     if (!VG_BWD_CELL_MAJOR || gi.rec == nullptr || K <= 0 || cm_ws == nullptr || cm_bytes < L.total ||
         L.total == 0) {

@@ -275,9 +275,11 @@ FieldView field_view(const void* field, int64_t n, int sh_deg);
 cudaError_t grad_unpack(const GraphView& g, const float* grad, int sh_deg, float* g_raw, float* g_dA, float* g_cA,
                         float* g_sh, cudaStream_t st);
 
-// foam.cu
+// foam.cu. The forward takes optional scratch (cm_ws, foam_forward_workspace bytes) for the cell-major
+// colour pass of the rays whose samples all fit in the records; without it colours are evaluated inline.
+size_t foam_forward_workspace(int64_t n_sites, int64_t n_rays, int record_cap);
 cudaError_t foam_forward(const GraphView& g, const FieldView& F, const RayView& R, const FoamCfg& c,
-                         const Outputs& out, int* status, cudaStream_t st);
+                         const Outputs& out, int* status, void* cm_ws, size_t cm_bytes, cudaStream_t st);
 // Scratch of the cell-major backward (rays fully recorded in records of capacity record_cap).
 size_t foam_backward_workspace(int64_t n_sites, int64_t n_rays, int record_cap);
 cudaError_t foam_backward(const GraphView& g, const FieldView& F, const RayView& R, const FoamCfg& c,

@@ -178,7 +178,7 @@ class FoamExtension:
         if B == 0:
             return [rgb, T, depth, stats, rec]
         pk = graph_pack(points, offsets, adj)
-        ws, nbytes = _workspace(pk.n, sh_deg, False, dev)
+        ws, nbytes = _workspace(pk.n, sh_deg, 0, dev, B, K)
         with torch.cuda.device(dev):
             _lib.call('vg_foam_forward', pk.ptr, pk.n, pk.m, raw.data_ptr(), dA.data_ptr(), cA.data_ptr(),
                       sh.data_ptr(), sh_deg, o.data_ptr(), d.data_ptr(), start.data_ptr(), near.data_ptr(),
