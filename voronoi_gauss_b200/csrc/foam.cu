@@ -41,6 +41,11 @@
 #ifndef VG_BWD_MINB
 #define VG_BWD_MINB 1
 #endif
+// VG_CM_CHUNK  samples of one cell per warp in the cell-major passes (32 or 64; 64 = two per lane in
+//              the colour pass), which sets how often a cell's neighbourhood is reloaded
+#ifndef VG_CM_CHUNK
+#define VG_CM_CHUNK 64
+#endif
 // VG_FWD_CELL_MAJOR  1: colours of fully recorded rays evaluated cell-major (see cmf_color_kernel)
 #ifndef VG_FWD_CELL_MAJOR
 #define VG_FWD_CELL_MAJOR 1
@@ -60,6 +65,8 @@ constexpr int kFwdSlotMem = kFwdSlots > 0 ? kFwdSlots * kBlock : 1;
 constexpr int kBwdSlotMem = kBwdSlots > 0 ? kBwdSlots * kBlock : 1;
 constexpr bool kLazy = VG_LAZY_COLOR != 0;
 constexpr bool kAgg = VG_BWD_AGG != 0;
+constexpr int kChunk = VG_CM_CHUNK;
+static_assert(kChunk == 32 || kChunk == 64, "VG_CM_CHUNK must be 32 or 64");
 
 // deferred: the colour fields are filled later; the last field marks the samples that need one (-1)
 __device__ __forceinline__ void store_sample(float* __restrict__ rec, int64_t r, int K, int s, const Sample& P,
@@ -214,55 +221,68 @@ __global__ void __launch_bounds__(kBlock)
     cmf_color_kernel(GraphView g, FieldView F, RayView R, float* __restrict__ rec, int K,
                      const int* __restrict__ order, const int4* __restrict__ chunks, const int* __restrict__ n_chunks_ptr,
                      int64_t r0) {
+    constexpr int kPer = kChunk / 32;  // samples per lane
     const int lane = threadIdx.x & 31;
     const int n_chunks = *n_chunks_ptr;
     const int warps = gridDim.x * (kBlock / 32);
     for (int ch = blockIdx.x * (kBlock / 32) + (threadIdx.x >> 5); ch < n_chunks; ch += warps) {
         const int4 C = __ldg(chunks + ch);
-        const bool on = lane < C.z;
-        int64_t r = r0, s = 0;
-        float x0 = 0.f, x1 = 0.f, x2 = 0.f, b[16];
-        if (on) {
-            const int slot = __ldg(order + C.y + lane);
-            r = r0 + slot / K, s = slot % K;
-            const float t = rec[(r * K + s) * kRecord];
-            float o[3], d[3];
+        int64_t slot[kPer];
+        float x[kPer][3], b[kPer][16];
+        Blend B[kPer];
 #pragma unroll
-            for (int a = 0; a < 3; ++a) o[a] = __ldg(R.o + 3 * r + a), d[a] = __ldg(R.d + 3 * r + a);
-            x0 = along(o[0], t, d[0]), x1 = along(o[1], t, d[1]), x2 = along(o[2], t, d[2]);
-            sh_basis(d[0], d[1], d[2], F.sh_deg, b);
-        } else {
+        for (int p = 0; p < kPer; ++p) {
+            const int li = lane + 32 * p;
+            slot[p] = -1;
+            x[p][0] = x[p][1] = x[p][2] = 0.f;
 #pragma unroll
-            for (int k = 0; k < 16; ++k) b[k] = 0.f;
+            for (int k = 0; k < 16; ++k) b[p][k] = 0.f;
+            blend_init(B[p]);
+            if (li < C.z) {
+                const int sl = __ldg(order + C.y + li);
+                const int64_t r = r0 + sl / K, s = sl % K;
+                slot[p] = r * K + s;
+                const float t = rec[slot[p] * kRecord];
+                float o[3], d[3];
+#pragma unroll
+                for (int a = 0; a < 3; ++a) o[a] = __ldg(R.o + 3 * r + a), d[a] = __ldg(R.d + 3 * r + a);
+                x[p][0] = along(o[0], t, d[0]), x[p][1] = along(o[1], t, d[1]), x[p][2] = along(o[2], t, d[2]);
+                sh_basis(d[0], d[1], d[2], F.sh_deg, b[p]);
+            }
         }
         const int e0 = __ldg(g.off + C.x), e1 = __ldg(g.off + C.x + 1);
-        Blend B;
-        blend_init(B);
         for (int e = e0; e < e1; ++e) {  // warp-uniform: one cell per chunk
             const float4 E = __ldg(g.edge + e);
             const int j = site_of(E);
             const float4* fr = F.rec + kFieldVec * static_cast<int64_t>(j);
             const float4 r2 = __ldg(fr + 2), r3 = __ldg(fr + 3);
-            const float v0 = x0 - E.x, v1 = x1 - E.y, v2 = x2 - E.z;
-            float c[3] = {0.5f, 0.5f, 0.5f};
+            float4 coef[S4];
             const float4* sp = F.sh + static_cast<int64_t>(S4) * j;
 #pragma unroll
-            for (int q = 0; q < S4; ++q) {
-                const float4 v = __ldg(sp + q);
-                const float f[4] = {v.x, v.y, v.z, v.w};
+            for (int q = 0; q < S4; ++q) coef[q] = __ldg(sp + q);
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int i = 4 * q + u;
-                    if (i < 48) c[i % 3] += b[i / 3] * f[u];
+            for (int p = 0; p < kPer; ++p) {
+                const float v0 = x[p][0] - E.x, v1 = x[p][1] - E.y, v2 = x[p][2] - E.z;
+                float c[3] = {0.5f, 0.5f, 0.5f};
+#pragma unroll
+                for (int q = 0; q < S4; ++q) {
+                    const float f[4] = {coef[q].x, coef[q].y, coef[q].z, coef[q].w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int i = 4 * q + u;
+                        if (i < 48) c[i % 3] += b[p][i / 3] * f[u];
+                    }
                 }
+                blend_add(B[p], maha(r2, r3, v0, v1, v2), fmaxf(c[0], 0.f), fmaxf(c[1], 0.f), fmaxf(c[2], 0.f));
             }
-            blend_add(B, maha(r2, r3, v0, v1, v2), fmaxf(c[0], 0.f), fmaxf(c[1], 0.f), fmaxf(c[2], 0.f));
         }
-        if (on) {
-            const float inv_a = 1.f / B.a;
-            float* q = rec + (r * K + s) * kRecord;
-            q[3] = B.r * inv_a;
-            reinterpret_cast<float4*>(q)[1] = make_float4(B.g * inv_a, B.b * inv_a, B.m, inv_a);
+#pragma unroll
+        for (int p = 0; p < kPer; ++p) {
+            if (slot[p] < 0) continue;
+            const float inv_a = 1.f / B[p].a;
+            float* q = rec + slot[p] * kRecord;
+            q[3] = B[p].r * inv_a;
+            reinterpret_cast<float4*>(q)[1] = make_float4(B[p].g * inv_a, B[p].b * inv_a, B[p].m, inv_a);
         }
     }
 }
@@ -452,14 +472,14 @@ __global__ void __launch_bounds__(kBlock)
     }
 }
 
-// Chunks of at most 32 samples of one cell: (cell, first position in order, count).
+// Chunks of at most kChunk samples of one cell: (cell, first position in order, count).
 __global__ void __launch_bounds__(kBlock)
     cm_chunks_kernel(const int* __restrict__ offsets, int n_cells, int4* __restrict__ chunks, int* n_chunks) {
     const int i = blockIdx.x * kBlock + threadIdx.x;
     const int lane = threadIdx.x & 31;
     int cnt = 0, a = 0;
     if (i < n_cells) a = __ldg(offsets + i), cnt = __ldg(offsets + i + 1) - a;
-    const int nch = (cnt + 31) >> 5;
+    const int nch = (cnt + kChunk - 1) / kChunk;
     int incl = nch;  // warp inclusive scan of the chunk counts, one atomic per warp
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -470,7 +490,7 @@ __global__ void __launch_bounds__(kBlock)
     if (lane == 31 && incl > 0) base = atomicAdd(n_chunks, incl);
     base = __shfl_sync(0xffffffffu, base, 31);
     const int first = base + incl - nch;
-    for (int c = 0; c < nch; ++c) chunks[first + c] = make_int4(i, a + 32 * c, min(32, cnt - 32 * c), 0);
+    for (int c = 0; c < nch; ++c) chunks[first + c] = make_int4(i, a + kChunk * c, min(kChunk, cnt - kChunk * c), 0);
 }
 
 // Shared-memory image of one staged sample: x, gs | gC, gC.C | m_min, 1/sum a, -, - | SH basis (16).
@@ -481,16 +501,16 @@ __global__ void __launch_bounds__(kBlock, 3)
     cm_scatter_kernel(GraphView g, FieldView F, RayView R, const float* __restrict__ rec, int K,
                       const float4* __restrict__ items, const int* __restrict__ order, const int4* __restrict__ chunks,
                       const int* __restrict__ n_chunks_ptr, int64_t r0, float* __restrict__ grad) {
-    __shared__ float4 smem[(kBlock / 32) * 32 * kItemVec];
+    __shared__ float4 smem[(kBlock / 32) * kChunk * kItemVec];
     const int lane = threadIdx.x & 31;
-    float4* st = smem + (threadIdx.x >> 5) * 32 * kItemVec;
+    float4* st = smem + (threadIdx.x >> 5) * kChunk * kItemVec;
     const int n_chunks = *n_chunks_ptr;
     const int warps = gridDim.x * (kBlock / 32);
     for (int ch = blockIdx.x * (kBlock / 32) + (threadIdx.x >> 5); ch < n_chunks; ch += warps) {
         const int4 C = __ldg(chunks + ch);
         const int cell = C.x, cnt = C.z;
-        if (lane < cnt) {  // stage this lane's sample
-            const int slot = __ldg(order + C.y + lane);
+        for (int li = lane; li < cnt; li += 32) {  // stage the chunk's samples
+            const int slot = __ldg(order + C.y + li);
             const int64_t r = r0 + slot / K;
             const int sidx = slot % K;
             const float t = __ldg(rec + (r * K + sidx) * kRecord);
@@ -501,7 +521,7 @@ __global__ void __launch_bounds__(kBlock, 3)
             const float4 i1 = __ldg(items + 2 * static_cast<int64_t>(slot) + 1);
             float b[16];
             sh_basis(d[0], d[1], d[2], F.sh_deg, b);
-            float4* q = st + kItemVec * lane;
+            float4* q = st + kItemVec * li;
             q[0] = make_float4(along(o[0], t, d[0]), along(o[1], t, d[1]), along(o[2], t, d[2]), i0.x);
             q[1] = make_float4(i0.y, i0.z, i0.w, i1.x);
             q[2] = make_float4(i1.y, i1.z, 0.f, 0.f);
@@ -648,28 +668,27 @@ size_t foam_backward_workspace(int64_t n_sites, int64_t n_rays, int record_cap) 
     return cm_layout(n_sites, n_rays, record_cap, true).total;
 }
 
+// Records kept per ray when the caller keeps none (record_cap 0): the no-record forward still defers
+// colours, with scratch records for passes of kCmItems / kScratchK rays.
+constexpr int kScratchK = 256;
+
 size_t foam_forward_workspace(int64_t n_sites, int64_t n_rays, int record_cap) {
-    return VG_FWD_CELL_MAJOR ? cm_layout(n_sites, n_rays, record_cap, false).total : 0;
+    if (!VG_FWD_CELL_MAJOR || n_rays <= 0) return 0;
+    if (record_cap > 0) return cm_layout(n_sites, n_rays, record_cap, false).total;
+    const CmLayout L = cm_layout(n_sites, n_rays, kScratchK, false);
+    return L.total + al256(static_cast<size_t>(L.rays_per_pass) * kScratchK * kRecord * sizeof(float));
 }
 
-cudaError_t foam_forward(const GraphView& g, const FieldView& F, const RayView& R, const FoamCfg& c,
-                         const Outputs& out, int* status, void* cm_ws, size_t cm_bytes, cudaStream_t st) {
-    if (R.n == 0) return cudaSuccess;
+namespace {
+
+// Traversal with deferred colours over the rays of R (records out.rec of capacity c.record_cap, all
+// rays of R recorded), inline colours for the rays with more samples than records, then the
+// cell-major colour passes and the composite.
+cudaError_t forward_deferred(const GraphView& g, const FieldView& F, const RayView& R, const FoamCfg& c,
+                             const Outputs& out, int* status, const CmLayout& L, char* b, cudaStream_t st) {
     const int K = c.record_cap;
-    const bool record = K > 0 && out.rec != nullptr;
-    const CmLayout L = cm_layout(g.n, R.n, K, false);
-    if (!record) {
-        foam_forward_kernel<false, kImmediate><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, out, status);
-        return cudaGetLastError();
-    }
-    if (!VG_FWD_CELL_MAJOR || cm_ws == nullptr || L.total == 0 || cm_bytes < L.total) {
-        foam_forward_kernel<true, kImmediate><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, out, status);
-        return cudaGetLastError();
-    }
-    // traversal with deferred colours, then inline colours for the rays with more samples than records
     foam_forward_kernel<true, kDeferred><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, out, status);
     foam_forward_kernel<true, kImmediateOverflow><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, out, status);
-    char* b = static_cast<char*>(cm_ws);
     int* order = reinterpret_cast<int*>(b + L.order);
     int* count = reinterpret_cast<int*>(b + L.count);
     int* fill = reinterpret_cast<int*>(b + L.fill);
@@ -701,6 +720,41 @@ cudaError_t foam_forward(const GraphView& g, const FieldView& F, const RayView& 
     }
     cmf_composite_kernel<<<blocks(R.n), kBlock, 0, st>>>(out.rec, out.stats, R.n, K, c.w_thresh, out.rgb);
     return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t foam_forward(const GraphView& g, const FieldView& F, const RayView& R, const FoamCfg& c,
+                         const Outputs& out, int* status, void* cm_ws, size_t cm_bytes, cudaStream_t st) {
+    if (R.n == 0) return cudaSuccess;
+    const int K = c.record_cap;
+    const bool record = K > 0 && out.rec != nullptr;
+    const bool room = VG_FWD_CELL_MAJOR && cm_ws != nullptr && cm_bytes >= foam_forward_workspace(g.n, R.n, K);
+    char* b = static_cast<char*>(cm_ws);
+    if (record) {
+        if (!room) {
+            foam_forward_kernel<true, kImmediate><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, out, status);
+            return cudaGetLastError();
+        }
+        return forward_deferred(g, F, R, c, out, status, cm_layout(g.n, R.n, K, false), b, st);
+    }
+    if (!room) {
+        foam_forward_kernel<false, kImmediate><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, out, status);
+        return cudaGetLastError();
+    }
+    // no records wanted: scratch records for one pass of rays at a time
+    const CmLayout L = cm_layout(g.n, R.n, kScratchK, false);
+    float* scratch_rec = reinterpret_cast<float*>(b + L.total);
+    FoamCfg cs = c;
+    cs.record_cap = kScratchK;
+    for (int64_t r0 = 0; r0 < R.n; r0 += L.rays_per_pass) {
+        const int64_t nr = std::min<int64_t>(L.rays_per_pass, R.n - r0);
+        const RayView Rs{R.o + 3 * r0, R.d + 3 * r0, R.start + r0, R.near + r0, nullptr, R.far + r0, nr};
+        const Outputs os{out.rgb + 3 * r0, out.T + r0, out.depth + r0, out.stats + 3 * r0, scratch_rec};
+        const cudaError_t e = forward_deferred(g, F, Rs, cs, os, status, L, b, st);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 cudaError_t foam_backward(const GraphView& g, const FieldView& F, const RayView& R, const FoamCfg& c,
