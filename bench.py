@@ -163,6 +163,7 @@ def launches_per_step(n_rays, record_cap):
 def run_b200(args):
     import torch.distributed as dist
 
+    from voronoi_gauss_b200 import dist as vdist
     from voronoi_gauss_b200 import ext, render, scenes, sites
     from voronoi_gauss_b200.model import VoronoiGaussField
 
@@ -219,11 +220,7 @@ def run_b200(args):
         loss.backward()
         ext.BACKWARD_EVENTS = None
         if world > 1:
-            grads = [p.grad for p in params]
-            flat = torch._utils._flatten_dense_tensors(grads)
-            dist.all_reduce(flat)
-            for gsrc, gdst in zip(torch._utils._unflatten_dense_tensors(flat, grads), grads):
-                gdst.copy_(gsrc)
+            vdist.allreduce_grads(params)
         opt.step()
         if ev:
             timing['ev'] = ev

@@ -38,8 +38,10 @@ def tile_pixels(H, W, world, rank, tile=TILE):
 
 
 def allreduce_grads(params, group=None):
-    """Sums the .grad of `params` over the ranks in one coalesced all-reduce (parameters without a
-    gradient contribute zeros). Every rank must call it with the same parameter list."""
+    """Sums the .grad of `params` over the ranks, in place: one asynchronous all-reduce per gradient
+    tensor (the per-site gradients are a few large contiguous tensors, so no flattening copies), then
+    waits for all of them. Parameters without a gradient contribute zeros. Every rank must call it with
+    the same parameter list."""
     grads = []
     for p in params:
         if p.grad is None:
@@ -47,10 +49,9 @@ def allreduce_grads(params, group=None):
         grads.append(p.grad)
     if dist.get_world_size(group) == 1:
         return
-    flat = torch._utils._flatten_dense_tensors(grads)
-    dist.all_reduce(flat, group=group)
-    for src, dst in zip(torch._utils._unflatten_dense_tensors(flat, grads), grads):
-        dst.copy_(src)
+    works = [dist.all_reduce(g, group=group, async_op=True) for g in grads]
+    for w in works:
+        w.wait()
 
 
 def allreduce_max(values, device, group=None):
