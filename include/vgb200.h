@@ -46,7 +46,8 @@ int vg_version(void);
 const char* vg_last_error(void);
 
 /* Bits of the status word accumulated by the render launches since the last vg_status_reset():
- * 1 = a greedy walk hit its 4096-step cap, 2 = a ray hit the 8192-cell cap. Synchronises the device. */
+ * 1 = a greedy walk hit its 4096-step cap, 2 = a ray hit the 8192-cell cap, 4 = a start or sample site
+ * outside [0, N) was skipped. Synchronises the device. */
 int vg_status(int* bits);
 int vg_status_reset(void);
 
@@ -147,6 +148,50 @@ int vg_conic_forward(const float* log_scale, const float* quat, int64_t n, doubl
 /* conic_backward (vgf.cu:548-561): g_ls (N, 3), g_quat (N, 4) from gA (N, 6). */
 int vg_conic_backward(const float* log_scale, const float* quat, int64_t n, double floor, const float* gA,
                       float* g_ls, float* g_quat, void* stream);
+
+/* ------------------------------------------------------------------ NeRF-sampler field kernels */
+
+/* walk (vgf.cu:438-456): nearest site of every sample o + z d of the (B, S) sorted sample depths z,
+ * each found by a greedy walk from the previous sample's site (the first from start[r]); a step moves
+ * to the first neighbour, in adjacency order, strictly closer than the current best. Outputs
+ * site (B, S) int32 original site ids and steps (B) int32 walk steps per ray. A start outside [0, N)
+ * gives site -1 for that ray and sets status bit 4. */
+int vg_walk(const void* pack, int64_t n_sites, int64_t n_adj, const float* o, const float* d, const float* z,
+            const int32_t* start, int64_t n_rays, int64_t n_samples, int32_t* site, int32_t* steps,
+            void* stream);
+
+/* Workspace of the field functions for n_sites sites: kind 0 vg_density_forward, 1
+ * vg_density_backward, 2 vg_color_forward, 3 vg_color_backward (sh_deg used by 2 and 3). */
+size_t vg_field_workspace_bytes(int64_t n_sites, int sh_deg, int kind);
+
+/* density_forward (vgf.cu:458-475): sigma (M) = sum over the neighbourhood {i} U adj(i) of the
+ * sample's site i of exp(min(raw_k, 30) - v^T A_k v / 2), A_k the conic of (log_scale, quat) widened
+ * by scale_mult (A / scale_mult^2). raw (N), log_scale (N, 3), quat (N, 4), x (M, 3), site (M).
+ * A site outside [0, N) gives sigma 0 and sets status bit 4. */
+int vg_density_forward(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* log_scale,
+                       const float* quat, const float* x, const int32_t* site, int64_t n_samples,
+                       double scale_mult, float* sigma, void* workspace, size_t workspace_bytes, void* stream);
+
+/* density_backward (vgf.cu:477-492): g_raw (N), g_ls (N, 3), g_quat (N, 4) (overwritten) of
+ * sum(grad_sigma * sigma) at scale_mult 1. */
+int vg_density_backward(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* log_scale,
+                        const float* quat, const float* x, const int32_t* site, int64_t n_samples,
+                        const float* grad_sigma, float* g_raw, float* g_ls, float* g_quat, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
+/* color_forward (vgf.cu:494-513): rgb (M, 3) = sum_k a_k max(SH_k(d) + 1/2, 0) / sum_k a_k over the
+ * neighbourhood of the sample's site, a_k = exp(-(m_k - min m) / 2), m_k = v^T A_k v with the colour
+ * conics of (log_scale, quat); dirs (M, 3) need not be unit; sh (N, 16, 3), sh_deg 0..3. */
+int vg_color_forward(const void* pack, int64_t n_sites, int64_t n_adj, const float* log_scale, const float* quat,
+                     const float* sh, int sh_deg, const float* x, const float* dirs, const int32_t* site,
+                     int64_t n_samples, float* rgb, void* workspace, size_t workspace_bytes, void* stream);
+
+/* color_backward (vgf.cu:515-533): g_ls (N, 3), g_quat (N, 4), g_sh (N, 16, 3) (overwritten) of
+ * sum(grad_rgb * rgb), rgb the forward's output. */
+int vg_color_backward(const void* pack, int64_t n_sites, int64_t n_adj, const float* log_scale, const float* quat,
+                      const float* sh, int sh_deg, const float* x, const float* dirs, const int32_t* site,
+                      int64_t n_samples, const float* rgb, const float* grad_rgb, float* g_ls, float* g_quat,
+                      float* g_sh, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------------- inference */
 

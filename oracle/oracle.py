@@ -3,7 +3,7 @@
 Used by tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg to check and time the
 product; the product itself never imports this module. Inputs/outputs are numpy arrays (or CPU
 torch tensors) in the reference layouts; signatures follow the reference extension functions
-(foam.cu:505-533, march.cu:383-410, vgf.cu:535-561, foam_infer.cu:376-380).
+(foam.cu:505-533, march.cu:383-410, vgf.cu:438-561, foam_infer.cu:376-380).
 """
 
 from __future__ import annotations
@@ -42,8 +42,15 @@ def lib():
         _lib.vgo_conic_backward.argtypes = [P, P, i64, f32, P, P, P]
         _lib.vgo_foam_infer.argtypes = [P, P, P, P, P, P, i32, i32, i64, P, P, P, P, P, i64, f32, f32, f32,
                                         i32, i32, P, P, P, P, P, P, i32]
+        f64 = ctypes.c_double
+        _lib.vgo_walk.argtypes = [P, P, P, i64, P, P, P, P, i64, i32, P, P]
+        _lib.vgo_density_forward.argtypes = [P, P, P, i64, P, P, P, P, P, i64, f64, P]
+        _lib.vgo_density_backward.argtypes = [P, P, P, i64, P, P, P, P, P, i64, P, P, P, P]
+        _lib.vgo_color_forward.argtypes = [P, P, P, i64, P, P, P, i32, P, P, P, i64, P]
+        _lib.vgo_color_backward.argtypes = [P, P, P, i64, P, P, P, i32, P, P, P, i64, P, P, P, P, P]
         for f in ('vgo_foam_forward', 'vgo_foam_backward', 'vgo_march_forward', 'vgo_march_backward',
-                  'vgo_foam_infer'):
+                  'vgo_foam_infer', 'vgo_walk', 'vgo_density_forward', 'vgo_density_backward', 'vgo_color_forward',
+                  'vgo_color_backward'):
             getattr(_lib, f).restype = ctypes.c_int
     return _lib
 
@@ -177,3 +184,66 @@ def foam_infer(points, offsets, nbr, edge, attr, sh, sh_deg, o, d, start, near, 
     if rc:
         raise RuntimeError(f'oracle foam_infer failed ({rc})')
     return rgb, T, depth, stats
+
+
+# ------------------------------------------------------------------- NeRF-sampler field kernels
+
+def _graph(points, offsets, adj):
+    return _np(points, np.float32), _np(offsets, np.int32), _np(adj, np.int32)
+
+
+def walk(points, offsets, adj, o, d, z, start):
+    """-> site (B, S) int32, steps (B) int32 (vgf.cu:438-456)."""
+    g = _graph(points, offsets, adj)
+    o, d, z, start = _np(o, np.float32), _np(d, np.float32), _np(z, np.float32), _np(start, np.int32)
+    B, S = z.shape
+    site, steps = np.zeros((B, S), np.int32), np.zeros(B, np.int32)
+    lib().vgo_walk(*map(_p, g), len(g[0]), _p(o), _p(d), _p(z), _p(start), B, S, _p(site), _p(steps))
+    return site, steps
+
+
+def density_forward(points, offsets, adj, raw, log_scale, quat, x, site, scale_mult=1.0):
+    """-> sigma (M) (vgf.cu:458-475)."""
+    g = _graph(points, offsets, adj)
+    f = [_np(a, np.float32) for a in (raw, log_scale, quat, x)]
+    site = _np(site, np.int32)
+    sigma = np.zeros(len(site), np.float32)
+    lib().vgo_density_forward(*map(_p, g), len(g[0]), *map(_p, f), _p(site), len(site), float(scale_mult),
+                              _p(sigma))
+    return sigma
+
+
+def density_backward(points, offsets, adj, raw, log_scale, quat, x, site, grad_sigma):
+    """-> g_raw (N), g_ls (N, 3), g_quat (N, 4) (vgf.cu:477-492)."""
+    g = _graph(points, offsets, adj)
+    f = [_np(a, np.float32) for a in (raw, log_scale, quat, x)]
+    site, gs = _np(site, np.int32), _np(grad_sigma, np.float32)
+    n = len(g[0])
+    g_raw, g_ls, g_quat = np.zeros(n, np.float32), np.zeros((n, 3), np.float32), np.zeros((n, 4), np.float32)
+    lib().vgo_density_backward(*map(_p, g), n, *map(_p, f), _p(site), len(site), _p(gs), _p(g_raw), _p(g_ls),
+                               _p(g_quat))
+    return g_raw, g_ls, g_quat
+
+
+def color_forward(points, offsets, adj, log_scale, quat, sh, sh_deg, x, dirs, site):
+    """-> rgb (M, 3) (vgf.cu:494-513)."""
+    g = _graph(points, offsets, adj)
+    ls, q, sh = _np(log_scale, np.float32), _np(quat, np.float32), _np(sh, np.float32)
+    x, dirs, site = _np(x, np.float32), _np(dirs, np.float32), _np(site, np.int32)
+    rgb = np.zeros((len(site), 3), np.float32)
+    lib().vgo_color_forward(*map(_p, g), len(g[0]), _p(ls), _p(q), _p(sh), int(sh_deg), _p(x), _p(dirs), _p(site),
+                            len(site), _p(rgb))
+    return rgb
+
+
+def color_backward(points, offsets, adj, log_scale, quat, sh, sh_deg, x, dirs, site, rgb, grad_rgb):
+    """-> g_ls (N, 3), g_quat (N, 4), g_sh (N, 16, 3) (vgf.cu:515-533)."""
+    g = _graph(points, offsets, adj)
+    ls, q, sh = _np(log_scale, np.float32), _np(quat, np.float32), _np(sh, np.float32)
+    x, dirs, site = _np(x, np.float32), _np(dirs, np.float32), _np(site, np.int32)
+    rgb, grad_rgb = _np(rgb, np.float32), _np(grad_rgb, np.float32)
+    n = len(g[0])
+    g_ls, g_quat, g_sh = np.zeros((n, 3), np.float32), np.zeros((n, 4), np.float32), np.zeros((n, 16, 3), np.float32)
+    lib().vgo_color_backward(*map(_p, g), n, _p(ls), _p(q), _p(sh), int(sh_deg), _p(x), _p(dirs), _p(site), len(site),
+                             _p(rgb), _p(grad_rgb), _p(g_ls), _p(g_quat), _p(g_sh))
+    return g_ls, g_quat, g_sh

@@ -740,6 +740,230 @@ void vgo_conic_backward(const float* ls, const float* quat, int64_t n, float flo
     }
 }
 
+/* ------------------------------------------------------------------ NeRF-sampler field kernels */
+
+/* vgf.cu:51-78: greedy walk of every sorted sample of a ray from the previous sample's site; a step
+ * moves to the first neighbour (adjacency order) strictly closer than the best so far. */
+int vgo_walk(const float* points, const int32_t* offsets, const int32_t* adj, int64_t n_sites, const float* o,
+             const float* d, const float* z, const int32_t* start, int64_t n_rays, int n_samples, int32_t* site,
+             int32_t* steps) {
+    (void)n_sites;
+    for (int64_t r = 0; r < n_rays; ++r) {
+        const float* orr = o + 3 * r;
+        const float* dr = d + 3 * r;
+        int cur = start[r], total = 0;
+        for (int s = 0; s < n_samples; ++s) {
+            const float t = z[r * n_samples + s];
+            const float x[3] = {fmaf(t, dr[0], orr[0]), fmaf(t, dr[1], orr[1]), fmaf(t, dr[2], orr[2])};
+            const float* pc = points + 3 * (int64_t)cur;
+            const float u0 = x[0] - pc[0], u1 = x[1] - pc[1], u2 = x[2] - pc[2];
+            float best_d = dot3c(u0, u1, u2, u0, u1, u2);
+            for (int it = 0; it < WALK_CAP; ++it) {
+                int best = cur;
+                for (int e = offsets[cur]; e < offsets[cur + 1]; ++e) {
+                    const int q = adj[e];
+                    const float* pq = points + 3 * (int64_t)q;
+                    const float v0 = x[0] - pq[0], v1 = x[1] - pq[1], v2 = x[2] - pq[2];
+                    const float dq = dot3c(v0, v1, v2, v0, v1, v2);
+                    if (dq < best_d) best_d = dq, best = q;
+                }
+                if (best == cur) break;
+                cur = best;
+                ++total;
+            }
+            site[r * n_samples + s] = cur;
+        }
+        steps[r] = total;
+    }
+    return 0;
+}
+
+typedef struct {
+    float v[3], y[3], is2[3], qn[4], qnorm, R[9], m;
+} GaussLocal;
+
+/* vgf.cu:99-124: the Gaussian of site i at x, rotation rebuilt from the quaternion. */
+static void gauss_local(const float* points, const float* ls, const float* quat, int i, const float x[3],
+                        float inv_mult2, GaussLocal* L) {
+    const int64_t i3 = 3 * (int64_t)i;
+    for (int a = 0; a < 3; ++a) L->v[a] = x[a] - points[i3 + a];
+    const float* q = quat + 4 * (int64_t)i;
+    L->qnorm = fmaxf(sqrtf(q[0] * q[0] + q[1] * q[1] + q[2] * q[2] + q[3] * q[3]), 1e-12f);
+    for (int k = 0; k < 4; ++k) L->qn[k] = q[k] / L->qnorm;
+    quat_to_rot(L->qn[0], L->qn[1], L->qn[2], L->qn[3], L->R);
+    L->m = 0.f;
+    for (int k = 0; k < 3; ++k) {
+        L->y[k] = L->R[k] * L->v[0] + L->R[3 + k] * L->v[1] + L->R[6 + k] * L->v[2];
+        const float s = expf(fminf(fmaxf(ls[i3 + k], -20.f), 20.f));
+        L->is2[k] = inv_mult2 / (s * s);
+        L->m += L->y[k] * L->y[k] * L->is2[k];
+    }
+}
+
+/* vgf.cu:126-153: dL/dls and dL/dq of one Gaussian from gm = dL/dm (accumulated). */
+static void scatter_gauss_grad(const GaussLocal* L, float gm, int i, float* g_ls, float* g_quat) {
+    const int64_t i3 = 3 * (int64_t)i;
+    float yk[3];
+    for (int k = 0; k < 3; ++k) {
+        yk[k] = 2.f * gm * L->y[k] * L->is2[k];
+        g_ls[i3 + k] += -2.f * gm * L->y[k] * L->y[k] * L->is2[k];
+    }
+    float GR[9];
+    for (int a = 0; a < 3; ++a)
+        for (int b = 0; b < 3; ++b) GR[3 * a + b] = L->v[a] * yk[b];
+    const float w = L->qn[0], x = L->qn[1], y = L->qn[2], z = L->qn[3];
+    float dq[4];
+    dq[0] = 2.f * (-z * GR[1] + y * GR[2] + z * GR[3] - x * GR[5] - y * GR[6] + x * GR[7]);
+    dq[1] = 2.f * (y * GR[1] + z * GR[2] + y * GR[3] - 2.f * x * GR[4] - w * GR[5] + z * GR[6] + w * GR[7] -
+                   2.f * x * GR[8]);
+    dq[2] = 2.f * (-2.f * y * GR[0] + x * GR[1] + w * GR[2] + x * GR[3] + z * GR[5] - w * GR[6] + z * GR[7] -
+                   2.f * y * GR[8]);
+    dq[3] = 2.f * (-2.f * z * GR[0] - w * GR[1] + x * GR[2] + w * GR[3] - 2.f * z * GR[4] + y * GR[5] + x * GR[6] +
+                   y * GR[7]);
+    const float proj = dq[0] * w + dq[1] * x + dq[2] * y + dq[3] * z;
+    for (int k = 0; k < 4; ++k) g_quat[4 * (int64_t)i + k] += (dq[k] - proj * L->qn[k]) / L->qnorm;
+}
+
+/* neighbourhood {i} U adj(i) in the reference's order (vgf.cu:155-161) */
+static inline int nbhd(const int32_t* offsets, const int32_t* adj, int i, int j) {
+    return j == 0 ? i : adj[offsets[i] + j - 1];
+}
+
+/* vgf.cu:163-177 */
+int vgo_density_forward(const float* points, const int32_t* offsets, const int32_t* adj, int64_t n_sites,
+                        const float* raw, const float* ls, const float* quat, const float* x, const int32_t* site,
+                        int64_t m, double scale_mult, float* sigma) {
+    (void)n_sites;
+    const float inv_mult2 = (float)(1.0 / (scale_mult * scale_mult));
+    for (int64_t t = 0; t < m; ++t) {
+        const int i = site[t];
+        const int n = offsets[i + 1] - offsets[i] + 1;
+        float s = 0.f;
+        for (int j = 0; j < n; ++j) {
+            const int k = nbhd(offsets, adj, i, j);
+            GaussLocal L;
+            gauss_local(points, ls, quat, k, x + 3 * t, inv_mult2, &L);
+            s += expf(fminf(raw[k], 30.f) - 0.5f * L.m);
+        }
+        sigma[t] = s;
+    }
+    return 0;
+}
+
+/* vgf.cu:179-198 (gradients accumulated into zero-filled outputs) */
+int vgo_density_backward(const float* points, const int32_t* offsets, const int32_t* adj, int64_t n_sites,
+                         const float* raw, const float* ls, const float* quat, const float* x, const int32_t* site,
+                         int64_t m, const float* grad_sigma, float* g_raw, float* g_ls, float* g_quat) {
+    (void)n_sites;
+    for (int64_t t = 0; t < m; ++t) {
+        const float gs = grad_sigma[t];
+        if (gs == 0.f) continue;
+        const int i = site[t];
+        const int n = offsets[i + 1] - offsets[i] + 1;
+        for (int j = 0; j < n; ++j) {
+            const int k = nbhd(offsets, adj, i, j);
+            GaussLocal L;
+            gauss_local(points, ls, quat, k, x + 3 * t, 1.f, &L);
+            const float c = expf(fminf(raw[k], 30.f) - 0.5f * L.m);
+            if (c * fabsf(gs) > 1e-12f) {
+                g_raw[k] += gs * c;
+                scatter_gauss_grad(&L, -0.5f * gs * c, k, g_ls, g_quat);
+            }
+        }
+    }
+    return 0;
+}
+
+static void unit_dir(const float* dirs, int64_t t, float d[3]) {
+    d[0] = dirs[3 * t], d[1] = dirs[3 * t + 1], d[2] = dirs[3 * t + 2];
+    const float inv = 1.f / sqrtf(fmaxf(d[0] * d[0] + d[1] * d[1] + d[2] * d[2], 1e-20f));
+    d[0] *= inv, d[1] *= inv, d[2] *= inv;
+}
+
+/* vgf.cu:248-282 */
+int vgo_color_forward(const float* points, const int32_t* offsets, const int32_t* adj, int64_t n_sites,
+                      const float* ls, const float* quat, const float* sh, int sh_deg, const float* x,
+                      const float* dirs, const int32_t* site, int64_t m, float* rgb) {
+    (void)n_sites;
+    const int nb = (sh_deg + 1) * (sh_deg + 1);
+    for (int64_t t = 0; t < m; ++t) {
+        float d[3], b[16];
+        unit_dir(dirs, t, d);
+        sh_basis(d[0], d[1], d[2], sh_deg, b);
+        const int i = site[t];
+        const int n = offsets[i + 1] - offsets[i] + 1;
+        float mmin = KINF, A = 0.f, cr = 0.f, cg = 0.f, cb = 0.f;
+        for (int j = 0; j < n; ++j) {
+            const int k = nbhd(offsets, adj, i, j);
+            GaussLocal L;
+            gauss_local(points, ls, quat, k, x + 3 * t, 1.f, &L);
+            if (L.m < mmin) {
+                const float f = mmin == KINF ? 0.f : expf(-0.5f * (mmin - L.m));
+                A *= f, cr *= f, cg *= f, cb *= f;
+                mmin = L.m;
+            }
+            const float a = expf(-0.5f * (L.m - mmin));
+            float c[3];
+            sh_eval(sh, k, b, nb, c);
+            A += a;
+            cr += a * fmaxf(c[0], 0.f);
+            cg += a * fmaxf(c[1], 0.f);
+            cb += a * fmaxf(c[2], 0.f);
+        }
+        rgb[3 * t] = cr / A, rgb[3 * t + 1] = cg / A, rgb[3 * t + 2] = cb / A;
+    }
+    return 0;
+}
+
+/* vgf.cu:284-335 (gradients accumulated into zero-filled outputs) */
+int vgo_color_backward(const float* points, const int32_t* offsets, const int32_t* adj, int64_t n_sites,
+                       const float* ls, const float* quat, const float* sh, int sh_deg, const float* x,
+                       const float* dirs, const int32_t* site, int64_t m, const float* rgb, const float* grad_rgb,
+                       float* g_ls, float* g_quat, float* g_sh) {
+    (void)n_sites;
+    const int nb = (sh_deg + 1) * (sh_deg + 1);
+    for (int64_t t = 0; t < m; ++t) {
+        const float gr = grad_rgb[3 * t], gg = grad_rgb[3 * t + 1], gb = grad_rgb[3 * t + 2];
+        if (gr == 0.f && gg == 0.f && gb == 0.f) continue;
+        const int i = site[t];
+        const int n = offsets[i + 1] - offsets[i] + 1;
+        float mmin = KINF;
+        for (int j = 0; j < n; ++j) {
+            GaussLocal L;
+            gauss_local(points, ls, quat, nbhd(offsets, adj, i, j), x + 3 * t, 1.f, &L);
+            mmin = fminf(mmin, L.m);
+        }
+        float A = 0.f;
+        for (int j = 0; j < n; ++j) {
+            GaussLocal L;
+            gauss_local(points, ls, quat, nbhd(offsets, adj, i, j), x + 3 * t, 1.f, &L);
+            A += expf(-0.5f * (L.m - mmin));
+        }
+        const float inv_a = 1.f / A;
+        const float gCC = gr * rgb[3 * t] + gg * rgb[3 * t + 1] + gb * rgb[3 * t + 2];
+        float d[3], b[16];
+        unit_dir(dirs, t, d);
+        sh_basis(d[0], d[1], d[2], sh_deg, b);
+        for (int j = 0; j < n; ++j) {
+            const int k = nbhd(offsets, adj, i, j);
+            GaussLocal L;
+            gauss_local(points, ls, quat, k, x + 3 * t, 1.f, &L);
+            const float a = expf(-0.5f * (L.m - mmin)) * inv_a;
+            if (a < MIN_WEIGHT) continue;
+            float c[3];
+            sh_eval(sh, k, b, nb, c);
+            const float dc[3] = {c[0] > 0.f ? a * gr : 0.f, c[1] > 0.f ? a * gg : 0.f, c[2] > 0.f ? a * gb : 0.f};
+            float* gs = g_sh + 48 * (int64_t)k;
+            for (int q = 0; q < nb; ++q)
+                for (int ch = 0; ch < 3; ++ch) gs[3 * q + ch] += b[q] * dc[ch];
+            const float ga = gr * fmaxf(c[0], 0.f) + gg * fmaxf(c[1], 0.f) + gb * fmaxf(c[2], 0.f);
+            const float gm = -0.5f * a * (ga - gCC);
+            if (gm != 0.f) scatter_gauss_grad(&L, gm, k, g_ls, g_quat);
+        }
+    }
+    return 0;
+}
+
 /* -------------------------------------------------------------------------------- foam_infer */
 
 /* IEEE 754 binary16 -> binary32 (exact). */

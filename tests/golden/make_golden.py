@@ -16,6 +16,9 @@ the reference's float64 restatements:
 * sh_basis.npz     - render.sh_basis for degrees 0..3 (render.py:143-165).
 * foam_config1.npz - 64 rays of an orbit camera over the config-1 scene (10k uniform sites), float64
                      trace + compositing + sparse gradients.
+* field_small.npz  - test_grad.py's setup (400 uniform sites, rng(0)): exact nearest sites (cKDTree) of
+                     sorted ray samples for the walk, and the float64 density / colour fields with
+                     their autograd gradients (test_grad.py:45-125).
 """
 
 import os
@@ -242,10 +245,61 @@ def make_foam_config1():
                         n_sites=len(pts), n_adj=len(adj), **ref, **sparse)
 
 
+def make_field_small():
+    rng = np.random.default_rng(0)
+    pts, _, offsets, adj = ref_sites.delaunay_graph(rng.uniform(-1, 1, (400, 3)))
+    n = len(pts)
+    p32 = pts.astype(np.float32)
+    tree = cKDTree(p32.astype(np.float64))
+    g = torch.Generator().manual_seed(3)
+    # walk: rays from random origins, sorted samples (test_grad.py:62-72)
+    B, S = 500, 40
+    o = torch.tensor(rng.uniform(-1.2, 1.2, (B, 3)), dtype=torch.float32)
+    d = torch.nn.functional.normalize(torch.randn(B, 3, generator=g), dim=-1)
+    z = torch.sort(torch.rand(B, S, generator=g) * 2.5, 1)[0]
+    start = tree.query(o.double().numpy())[1].astype(np.int32)
+    x_walk = (o[:, None].double() + d[:, None].double() * z[..., None].double()).reshape(-1, 3).numpy()
+    nn_dist, nn_site = tree.query(x_walk, k=2)
+    # fields (test_grad.py:74-125)
+    m = 3000
+    x = torch.tensor(rng.uniform(-1, 1, (m, 3)), dtype=torch.float32)
+    site = torch.tensor(tree.query(x.double().numpy())[1], dtype=torch.int32)
+    raw = torch.randn(n, generator=g) * 0.5
+    ls = torch.randn(n, 3, generator=g) * 0.3 - 1.2
+    q = torch.randn(n, 4, generator=g)
+    cls = torch.randn(n, 3, generator=g) * 0.3 - 1.2
+    cq = torch.randn(n, 4, generator=g)
+    sh = torch.randn(n, 16, 3, generator=g) * 0.3
+    dirs = torch.randn(m, 3, generator=g)
+    g_sigma = torch.randn(m, generator=g)
+    g_rgb = torch.randn(m, 3, generator=g)
+    P = torch.tensor(p32, dtype=torch.float64)
+    ref = [p.double().requires_grad_() for p in (raw, ls, q, cls, cq, sh)]
+    rraw, rls, rq, rcls, rcq, rsh = ref
+    X = x.double()
+    mask = test_grad.neighborhood_mask(offsets, adj, site, n)
+    md = test_grad.mahalanobis(P, rls, rq, X)
+    sigma_ref = (torch.exp(rraw)[None] * torch.exp(-0.5 * md) * mask).sum(1)
+    mc = test_grad.mahalanobis(P, rcls, rcq, X).masked_fill(~mask, float('inf'))
+    a = torch.softmax(-0.5 * mc, 1)
+    D = torch.nn.functional.normalize(dirs.double(), dim=-1)
+    ck = (torch.einsum('mj,njc->mnc', test_grad.sh_basis(D), rsh) + 0.5).clamp_min(0)
+    rgb_ref = (a[..., None] * ck).sum(1)
+    ((sigma_ref * g_sigma.double()).sum() + (rgb_ref * g_rgb.double()).sum()).backward()
+    np.savez_compressed(
+        os.path.join(HERE, 'field_small.npz'), points=p32, offsets=offsets, adj=adj, o=o.numpy(), d=d.numpy(),
+        z=z.numpy(), start=start, nn_site=nn_site.astype(np.int32), nn_dist=nn_dist, x=x.numpy(),
+        site=site.numpy(), raw=raw.numpy(), ls=ls.numpy(), quat=q.numpy(), cls=cls.numpy(), cquat=cq.numpy(),
+        sh=sh.numpy(), dirs=dirs.numpy(), g_sigma=g_sigma.numpy(), g_rgb=g_rgb.numpy(), sh_deg=3,
+        ref_sigma=sigma_ref.detach().numpy(), ref_rgb=rgb_ref.detach().numpy(),
+        **{f'ref_g_{k}': r.grad.numpy() for k, r in zip(('raw', 'ls', 'quat', 'cls', 'cquat', 'sh'), ref)})
+
+
 if __name__ == '__main__':
     make_sh_basis()
     make_conic()
     make_foam_small()
     make_march_small()
     make_foam_config1()
+    make_field_small()
     print('fixtures written to', HERE)

@@ -84,6 +84,23 @@ int check_alignment(const float* dA, const float* cA, const float* sh, const flo
 size_t field_ws(int64_t n, int deg) { return align256(vg::field_bytes(n, deg)); }
 size_t grad_ws(int64_t n) { return align256(static_cast<size_t>(n) * vg::kGradStride * sizeof(float)); }
 
+int check_field(const void* pack, int64_t n_sites, int64_t n_adj, const float* ls, const float* quat, const float* x,
+                const int32_t* site, int64_t m, void* workspace, size_t workspace_bytes, int sh_deg, int kind) {
+    REQUIRE(pack != nullptr, "graph pack is null");
+    REQUIRE(n_sites > 0 && n_sites < INT32_MAX, "n_sites must be in [1, 2^31)");
+    REQUIRE(n_adj >= 0 && n_sites + n_adj < INT32_MAX, "adjacency too large for int32 offsets");
+    REQUIRE(ls && quat, "log_scale and quat must be non-null");
+    REQUIRE(aligned(quat, 16), "quat must be 16-byte aligned");
+    REQUIRE(m >= 0, "n_samples must be >= 0");
+    REQUIRE(m == 0 || (x && site), "x and site must be non-null");
+    REQUIRE(sh_deg >= 0 && sh_deg <= 3, "sh_deg must be in 0..3");
+    REQUIRE(aligned(workspace, 256), "workspace must be 256-byte aligned");
+    const size_t need = vg::field_workspace(n_sites, sh_deg, kind);
+    if (workspace == nullptr || workspace_bytes < need)
+        return fail(VG_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);
+    return VG_OK;
+}
+
 }  // namespace
 
 namespace vg {
@@ -344,6 +361,103 @@ int vg_conic_backward(const float* log_scale, const float* quat, int64_t n, doub
     const cudaError_t e = vg::conic_backward(log_scale, quat, n, static_cast<float>(floor * floor), gA, g_ls, g_quat,
                                              static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_conic_backward");
+}
+
+int vg_walk(const void* pack, int64_t n_sites, int64_t n_adj, const float* o, const float* d, const float* z,
+            const int32_t* start, int64_t n_rays, int64_t n_samples, int32_t* site, int32_t* steps, void* stream) {
+    REQUIRE(pack != nullptr, "graph pack is null");
+    REQUIRE(n_sites > 0 && n_sites < INT32_MAX, "n_sites must be in [1, 2^31)");
+    REQUIRE(n_adj >= 0 && n_sites + n_adj < INT32_MAX, "adjacency too large for int32 offsets");
+    REQUIRE(n_rays >= 0 && n_samples >= 0 && n_samples < INT32_MAX, "bad sample counts");
+    REQUIRE(n_rays == 0 || (o && d && start && steps), "ray arrays must be non-null");
+    REQUIRE(n_rays * n_samples == 0 || (z && site), "z and site must be non-null");
+    if (n_rays == 0) return VG_OK;
+    int* status = status_ptr();
+    if (status == nullptr) return fail(VG_ERR_CUDA, "status word unavailable");
+    const vg::GraphView g = vg::graph_view(pack, n_sites, n_adj);
+    const cudaError_t e = vg::sampler_walk(g, o, d, z, start, n_rays, static_cast<int>(n_samples), site, steps, status,
+                                           static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_walk");
+}
+
+size_t vg_field_workspace_bytes(int64_t n_sites, int sh_deg, int kind) {
+    if (n_sites <= 0 || kind < 0 || kind > 3 || sh_deg < 0 || sh_deg > 3) return 0;
+    return vg::field_workspace(n_sites, sh_deg, kind);
+}
+
+int vg_density_forward(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* log_scale,
+                       const float* quat, const float* x, const int32_t* site, int64_t n_samples, double scale_mult,
+                       float* sigma, void* workspace, size_t workspace_bytes, void* stream) {
+    int rc = check_field(pack, n_sites, n_adj, log_scale, quat, x, site, n_samples, workspace, workspace_bytes, 0, 0);
+    if (rc) return rc;
+    REQUIRE(raw != nullptr, "raw must be non-null");
+    REQUIRE(n_samples == 0 || sigma != nullptr, "sigma must be non-null");
+    REQUIRE(scale_mult != 0.0, "scale_mult must be nonzero");
+    if (n_samples == 0) return VG_OK;
+    int* status = status_ptr();
+    if (status == nullptr) return fail(VG_ERR_CUDA, "status word unavailable");
+    const vg::GraphView g = vg::graph_view(pack, n_sites, n_adj);
+    const cudaError_t e = vg::density_field(g, raw, log_scale, quat, x, site, n_samples,
+                                            static_cast<float>(1.0 / (scale_mult * scale_mult)), nullptr, sigma,
+                                            nullptr, nullptr, nullptr, workspace, status,
+                                            static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_density_forward");
+}
+
+int vg_density_backward(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* log_scale,
+                        const float* quat, const float* x, const int32_t* site, int64_t n_samples,
+                        const float* grad_sigma, float* g_raw, float* g_ls, float* g_quat, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+    int rc = check_field(pack, n_sites, n_adj, log_scale, quat, x, site, n_samples, workspace, workspace_bytes, 0, 1);
+    if (rc) return rc;
+    REQUIRE(raw != nullptr, "raw must be non-null");
+    REQUIRE(n_samples == 0 || grad_sigma != nullptr, "grad_sigma must be non-null");
+    REQUIRE(g_raw && g_ls && g_quat, "gradient outputs must be non-null");
+    REQUIRE(aligned(g_quat, 16), "g_quat must be 16-byte aligned");
+    int* status = status_ptr();
+    if (status == nullptr) return fail(VG_ERR_CUDA, "status word unavailable");
+    const vg::GraphView g = vg::graph_view(pack, n_sites, n_adj);
+    const cudaError_t e = vg::density_field(g, raw, log_scale, quat, x, site, n_samples, 1.f, grad_sigma, nullptr,
+                                            g_raw, g_ls, g_quat, workspace, status, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_density_backward");
+}
+
+int vg_color_forward(const void* pack, int64_t n_sites, int64_t n_adj, const float* log_scale, const float* quat,
+                     const float* sh, int sh_deg, const float* x, const float* dirs, const int32_t* site,
+                     int64_t n_samples, float* rgb, void* workspace, size_t workspace_bytes, void* stream) {
+    int rc = check_field(pack, n_sites, n_adj, log_scale, quat, x, site, n_samples, workspace, workspace_bytes,
+                         sh_deg, 2);
+    if (rc) return rc;
+    REQUIRE(sh != nullptr, "sh must be non-null");
+    REQUIRE(n_samples == 0 || (dirs && rgb), "dirs and rgb must be non-null");
+    if (n_samples == 0) return VG_OK;
+    int* status = status_ptr();
+    if (status == nullptr) return fail(VG_ERR_CUDA, "status word unavailable");
+    const vg::GraphView g = vg::graph_view(pack, n_sites, n_adj);
+    const cudaError_t e = vg::color_field(g, log_scale, quat, sh, sh_deg, x, dirs, site, n_samples, nullptr, nullptr,
+                                          rgb, nullptr, nullptr, nullptr, workspace, status,
+                                          static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_color_forward");
+}
+
+int vg_color_backward(const void* pack, int64_t n_sites, int64_t n_adj, const float* log_scale, const float* quat,
+                      const float* sh, int sh_deg, const float* x, const float* dirs, const int32_t* site,
+                      int64_t n_samples, const float* rgb, const float* grad_rgb, float* g_ls, float* g_quat,
+                      float* g_sh, void* workspace, size_t workspace_bytes, void* stream) {
+    int rc = check_field(pack, n_sites, n_adj, log_scale, quat, x, site, n_samples, workspace, workspace_bytes,
+                         sh_deg, 3);
+    if (rc) return rc;
+    REQUIRE(sh != nullptr, "sh must be non-null");
+    REQUIRE(n_samples == 0 || (dirs && rgb && grad_rgb), "dirs, rgb and grad_rgb must be non-null");
+    REQUIRE(g_ls && g_quat && g_sh, "gradient outputs must be non-null");
+    REQUIRE(aligned(g_quat, 16) && aligned(g_sh, 16), "g_quat and g_sh must be 16-byte aligned");
+    int* status = status_ptr();
+    if (status == nullptr) return fail(VG_ERR_CUDA, "status word unavailable");
+    const vg::GraphView g = vg::graph_view(pack, n_sites, n_adj);
+    const cudaError_t e = vg::color_field(g, log_scale, quat, sh, sh_deg, x, dirs, site, n_samples, rgb, grad_rgb,
+                                          nullptr, g_ls, g_quat, g_sh, workspace, status,
+                                          static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_color_backward");
 }
 
 int vg_foam_infer(const float* points, const int32_t* offsets, const int32_t* nbr, const float* edge,

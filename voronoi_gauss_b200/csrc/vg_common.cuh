@@ -41,6 +41,7 @@ constexpr int kFieldVec = 4;             // float4 per site in the field pack
 // error bits written to the status word of a launch
 constexpr int kErrWalkCap = 1;   // a greedy walk hit kWalkCap
 constexpr int kErrCellCap = 2;   // a ray hit kMaxCells
+constexpr int kErrBadSite = 4;   // a start or sample site outside [0, N): that ray or sample is skipped
 
 inline __host__ __device__ int sh_coeffs(int deg) { return (deg + 1) * (deg + 1); }
 inline __host__ __device__ int sh_vec4(int deg) { return (3 * sh_coeffs(deg) + 3) / 4; }
@@ -297,6 +298,20 @@ cudaError_t conic_forward(const float* log_scale, const float* quat, int64_t n, 
                           cudaStream_t st);
 cudaError_t conic_backward(const float* log_scale, const float* quat, int64_t n, float floor2, const float* gA,
                            float* g_ls, float* g_quat, cudaStream_t st);
+
+// field.cu: the NeRF-sampler field kernels. kind: 0 density forward, 1 density backward, 2 colour
+// forward, 3 colour backward. inv_mult2 = 1 / scale_mult^2 (forward only; the backward uses 1). A
+// backward call is selected by a non-null g_sigma / g_rgb.
+size_t field_workspace(int64_t n_sites, int sh_deg, int kind);
+cudaError_t sampler_walk(const GraphView& g, const float* o, const float* d, const float* z, const int* start,
+                         int64_t n_rays, int n_samples, int* site, int* steps, int* status, cudaStream_t st);
+cudaError_t density_field(const GraphView& g, const float* raw, const float* ls, const float* quat, const float* x,
+                          const int* site, int64_t m, float inv_mult2, const float* g_sigma, float* sigma,
+                          float* g_raw, float* g_ls, float* g_quat, void* ws, int* status, cudaStream_t st);
+cudaError_t color_field(const GraphView& g, const float* ls, const float* quat, const float* sh, int sh_deg,
+                        const float* x, const float* dirs, const int* site, int64_t m, const float* rgb_in,
+                        const float* g_rgb, float* rgb, float* g_ls, float* g_quat, float* g_sh, void* ws, int* status,
+                        cudaStream_t st);
 
 // infer.cu
 struct InferNet {

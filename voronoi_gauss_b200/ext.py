@@ -8,10 +8,11 @@ Same public surface and contracts as ext.py:30-216:
 * ``foam(graph, raw, dA, cA, sh, sh_deg, o, d, start, near, far, t_thresh, w_thresh, record_cap)``
   -> (rgb, T, depth, stats), autograd through raw / dA / cA / sh (ext.py:185-216);
   ``march(...)`` (ext.py:152-182); ``conic(log_scale, quat, floor)`` (ext.py:120-136) and its torch twin
-  ``conic_reference`` (ext.py:139-149).
+  ``conic_reference`` (ext.py:139-149); the NeRF-sampler fields ``density(...)`` / ``color(...)``
+  (ext.py:61-117) and ``Graph.walk`` (ext.py:54-58).
 * ``foam_extension()``, ``march_extension()``, ``extension()``, ``foam_infer_extension()`` return objects
   with the reference's extension-level functions and signatures (foam.cu:560-565, march.cu:431-434,
-  vgf.cu:563-571 conic part, foam_infer.cu:437-440): tensors in, freshly allocated tensors out,
+  vgf.cu:563-571, foam_infer.cu:437-440): tensors in, freshly allocated tensors out,
   ``RuntimeError`` on a bad argument (the reference's TORCH_CHECK).
 
 Every call runs on the input's device and on torch's current stream of that device, asynchronously.
@@ -25,8 +26,8 @@ import torch
 
 from . import _lib
 
-__all__ = ['Graph', 'foam', 'march', 'conic', 'conic_reference', 'extension', 'march_extension', 'foam_extension',
-           'foam_infer_extension', 'GraphPack', 'graph_pack']
+__all__ = ['Graph', 'foam', 'march', 'conic', 'conic_reference', 'density', 'color', 'extension', 'march_extension',
+           'foam_extension', 'foam_infer_extension', 'GraphPack', 'graph_pack']
 
 
 # (start, end) CUDA events recorded on the launching stream around the foam backward launch while set
@@ -116,7 +117,11 @@ class Graph:
         return self._pack
 
     def walk(self, o, d, z, start):
-        raise NotImplementedError('Graph.walk (the NeRF-sampler walk of vgf.cu) is not part of this build')
+        """Nearest site of every sample o + z d; z (B, S) sorted along each ray, start (B,) a site near o
+        (ext.py:54-58). Returns (site (B, S) int32, steps (B) int32)."""
+        site, steps = extension().walk(self.points, self.offsets, self.adj, o.float().contiguous(),
+                                       d.float().contiguous(), z.float().contiguous(), start.int().contiguous())
+        return site, steps
 
 
 # ------------------------------------------------------------------------- extension-level functions
@@ -265,8 +270,116 @@ class MarchExtension:
 
 
 class FieldExtension:
-    """conic_forward / conic_backward (vgf.cu:535-561). The NeRF-sampler functions of the same module
-    (walk, density_*, color_*: vgf.cu:438-533) are not part of this build."""
+    """The functions of the reference's vgf.cu module (vgf.cu:438-571): the NeRF-sampler walk, density
+    and colour fields with their gradients, and the conics."""
+
+    @staticmethod
+    def walk(points, offsets, adj, o, d, z, start):
+        for x, name, dt in ((points, 'points', torch.float32), (offsets, 'offsets', torch.int32),
+                            (adj, 'adj', torch.int32), (o, 'o', torch.float32), (d, 'd', torch.float32),
+                            (z, 'z', torch.float32), (start, 'start', torch.int32)):
+            _check(x, name, dt)
+        if z.dim() != 2:
+            raise RuntimeError('z must be (B, S)')
+        B, S = z.size(0), z.size(1)
+        if o.shape != (B, 3) or d.shape != (B, 3) or start.numel() != B:
+            raise RuntimeError('o, d must be (B, 3) and start (B)')
+        site = torch.empty(B, S, dtype=torch.int32, device=z.device)
+        steps = torch.empty(B, dtype=torch.int32, device=z.device)
+        if B == 0:
+            return [site, steps]
+        pk = graph_pack(points, offsets, adj)
+        with torch.cuda.device(z.device):
+            _lib.call('vg_walk', pk.ptr, pk.n, pk.m, o.data_ptr(), d.data_ptr(), _ptr(z), start.data_ptr(), B, S,
+                      _ptr(site), steps.data_ptr(), _stream(z.device))
+        return [site, steps]
+
+    @staticmethod
+    def _field_checks(points, offsets, adj, log_scale, quat, x, site, **extra):
+        for t, name, dt in ((points, 'points', torch.float32), (offsets, 'offsets', torch.int32),
+                            (adj, 'adj', torch.int32), (log_scale, 'log_scale', torch.float32),
+                            (quat, 'quat', torch.float32), (x, 'x', torch.float32), (site, 'site', torch.int32)):
+            _check(t, name, dt)
+        for name, t in extra.items():
+            _check(t, name, torch.float32)
+        n, m = points.size(0), x.size(0)
+        if log_scale.shape != (n, 3) or quat.shape != (n, 4):
+            raise RuntimeError('log_scale must be (N, 3) and quat (N, 4)')
+        if x.dim() != 2 or x.size(1) != 3 or site.numel() != m:
+            raise RuntimeError('x must be (M, 3) and site (M)')
+        return m
+
+    @staticmethod
+    def _ws(n, sh_deg, kind, dev):
+        nbytes = _lib.lib().vg_field_workspace_bytes(n, int(sh_deg), kind)
+        return torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev), nbytes
+
+    @classmethod
+    def density_forward(cls, points, offsets, adj, raw, log_scale, quat, x, site, scale_mult):
+        m = cls._field_checks(points, offsets, adj, log_scale, quat, x, site, raw=raw)
+        if raw.numel() != points.size(0):
+            raise RuntimeError('raw must be (N)')
+        sigma = torch.empty(m, device=x.device)
+        if m == 0:
+            return sigma
+        pk = graph_pack(points, offsets, adj)
+        ws, nbytes = cls._ws(pk.n, 0, 0, x.device)
+        with torch.cuda.device(x.device):
+            _lib.call('vg_density_forward', pk.ptr, pk.n, pk.m, raw.data_ptr(), log_scale.data_ptr(),
+                      quat.data_ptr(), x.data_ptr(), site.data_ptr(), m, float(scale_mult), sigma.data_ptr(),
+                      ws.data_ptr(), nbytes, _stream(x.device))
+        return sigma
+
+    @classmethod
+    def density_backward(cls, points, offsets, adj, raw, log_scale, quat, x, site, grad_sigma):
+        m = cls._field_checks(points, offsets, adj, log_scale, quat, x, site, raw=raw, grad_sigma=grad_sigma)
+        if raw.numel() != points.size(0) or grad_sigma.numel() != m:
+            raise RuntimeError('raw must be (N) and grad_sigma (M)')
+        g_raw, g_ls, g_quat = torch.empty_like(raw), torch.empty_like(log_scale), torch.empty_like(quat)
+        pk = graph_pack(points, offsets, adj)
+        ws, nbytes = cls._ws(pk.n, 0, 1, x.device)
+        with torch.cuda.device(x.device):
+            _lib.call('vg_density_backward', pk.ptr, pk.n, pk.m, raw.data_ptr(), log_scale.data_ptr(),
+                      quat.data_ptr(), _ptr(x), _ptr(site), m, _ptr(grad_sigma), g_raw.data_ptr(), g_ls.data_ptr(),
+                      g_quat.data_ptr(), ws.data_ptr(), nbytes, _stream(x.device))
+        return [g_raw, g_ls, g_quat]
+
+    @classmethod
+    def color_forward(cls, points, offsets, adj, log_scale, quat, sh, sh_deg, x, dirs, site):
+        m = cls._field_checks(points, offsets, adj, log_scale, quat, x, site, sh=sh, dirs=dirs)
+        if sh.dim() != 3 or sh.size(1) != 16 or sh.size(2) != 3:
+            raise RuntimeError('sh must be (N, 16, 3)')
+        if dirs.shape != (m, 3):
+            raise RuntimeError('dirs must be (M, 3)')
+        sh_deg = _sh_deg(sh_deg)
+        rgb = torch.empty(m, 3, device=x.device)
+        if m == 0:
+            return rgb
+        pk = graph_pack(points, offsets, adj)
+        ws, nbytes = cls._ws(pk.n, sh_deg, 2, x.device)
+        with torch.cuda.device(x.device):
+            _lib.call('vg_color_forward', pk.ptr, pk.n, pk.m, log_scale.data_ptr(), quat.data_ptr(), sh.data_ptr(),
+                      sh_deg, x.data_ptr(), dirs.data_ptr(), site.data_ptr(), m, rgb.data_ptr(), ws.data_ptr(),
+                      nbytes, _stream(x.device))
+        return rgb
+
+    @classmethod
+    def color_backward(cls, points, offsets, adj, log_scale, quat, sh, sh_deg, x, dirs, site, rgb, grad_rgb):
+        m = cls._field_checks(points, offsets, adj, log_scale, quat, x, site, sh=sh, dirs=dirs, rgb=rgb,
+                              grad_rgb=grad_rgb)
+        if sh.dim() != 3 or sh.size(1) != 16 or sh.size(2) != 3:
+            raise RuntimeError('sh must be (N, 16, 3)')
+        if dirs.shape != (m, 3) or rgb.shape != (m, 3) or grad_rgb.shape != (m, 3):
+            raise RuntimeError('dirs, rgb and grad_rgb must be (M, 3)')
+        sh_deg = _sh_deg(sh_deg)
+        g_ls, g_quat, g_sh = torch.empty_like(log_scale), torch.empty_like(quat), torch.empty_like(sh)
+        pk = graph_pack(points, offsets, adj)
+        ws, nbytes = cls._ws(pk.n, sh_deg, 3, x.device)
+        with torch.cuda.device(x.device):
+            _lib.call('vg_color_backward', pk.ptr, pk.n, pk.m, log_scale.data_ptr(), quat.data_ptr(), sh.data_ptr(),
+                      sh_deg, _ptr(x), _ptr(dirs), _ptr(site), m, _ptr(rgb), _ptr(grad_rgb), g_ls.data_ptr(),
+                      g_quat.data_ptr(), g_sh.data_ptr(), ws.data_ptr(), nbytes, _stream(x.device))
+        return [g_ls, g_quat, g_sh]
 
     @staticmethod
     def conic_forward(log_scale, quat, floor):
@@ -292,11 +405,6 @@ class FieldExtension:
                 _lib.call('vg_conic_backward', log_scale.data_ptr(), quat.data_ptr(), n, float(floor), gA.data_ptr(),
                           g_ls.data_ptr(), g_quat.data_ptr(), _stream(quat.device))
         return [g_ls, g_quat]
-
-    def __getattr__(self, name):
-        if name in ('walk', 'density_forward', 'density_backward', 'color_forward', 'color_backward'):
-            raise NotImplementedError(f'{name} (NeRF-sampler field kernel of vgf.cu) is not part of this build')
-        raise AttributeError(name)
 
 
 class FoamInferExtension:
@@ -400,6 +508,66 @@ def conic_reference(log_scale, quat, floor=0.0):
     inv_var = 1.0 / (torch.exp(2 * log_scale.clamp(-20, 20)) + floor * floor)
     A = torch.einsum('nak,nk,nbk->nab', R, inv_var, R)
     return torch.stack([A[:, 0, 0], A[:, 0, 1], A[:, 0, 2], A[:, 1, 1], A[:, 1, 2], A[:, 2, 2]], -1).contiguous()
+
+
+class _Density(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, raw, log_scale, quat, x, site, graph):
+        sigma = extension().density_forward(graph.points, graph.offsets, graph.adj, raw, log_scale, quat, x, site, 1.0)
+        ctx.save_for_backward(raw, log_scale, quat, x, site)
+        ctx.graph = graph
+        return sigma
+
+    @staticmethod
+    def backward(ctx, grad_sigma):
+        raw, log_scale, quat, x, site = ctx.saved_tensors
+        g = ctx.graph
+        g_raw, g_ls, g_quat = extension().density_backward(g.points, g.offsets, g.adj, raw, log_scale, quat, x, site,
+                                                           grad_sigma.contiguous())
+        return g_raw, g_ls, g_quat, None, None, None
+
+
+def density(graph, raw, log_scale, quat, x, site, scale_mult=1.0):
+    """sigma(x) = sum over the Voronoi neighbourhood of site of exp(raw_k) G_k(x) (ext.py:78-87).
+    scale_mult widens the Gaussians (proposal passes, no gradient)."""
+    x = x.detach().float().contiguous()
+    site = site.int().contiguous()
+    params = [p.contiguous() for p in (raw, log_scale, quat)]
+    if scale_mult != 1.0 or not torch.is_grad_enabled() or not any(p.requires_grad for p in params):
+        return extension().density_forward(graph.points, graph.offsets, graph.adj, *[p.detach() for p in params], x,
+                                           site, float(scale_mult))
+    return _Density.apply(*params, x, site, graph)
+
+
+class _Color(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, log_scale, quat, sh, x, dirs, site, graph, sh_deg):
+        rgb = extension().color_forward(graph.points, graph.offsets, graph.adj, log_scale, quat, sh, sh_deg, x, dirs,
+                                        site)
+        ctx.save_for_backward(log_scale, quat, sh, x, dirs, site, rgb)
+        ctx.graph, ctx.sh_deg = graph, sh_deg
+        return rgb
+
+    @staticmethod
+    def backward(ctx, grad_rgb):
+        log_scale, quat, sh, x, dirs, site, rgb = ctx.saved_tensors
+        g = ctx.graph
+        g_ls, g_quat, g_sh = extension().color_backward(g.points, g.offsets, g.adj, log_scale, quat, sh, ctx.sh_deg,
+                                                        x, dirs, site, rgb, grad_rgb.contiguous())
+        return g_ls, g_quat, g_sh, None, None, None, None, None
+
+
+def color(graph, log_scale, quat, sh, x, dirs, site, sh_deg=3):
+    """C(x, d) = sum_k H_k(x) c_k(d) / sum_k H_k(x) over the Voronoi neighbourhood of site; sh (N, 16, 3)
+    (ext.py:109-117)."""
+    x = x.detach().float().contiguous()
+    dirs = dirs.detach().float().contiguous()
+    site = site.int().contiguous()
+    params = [p.contiguous() for p in (log_scale, quat, sh)]
+    if not torch.is_grad_enabled() or not any(p.requires_grad for p in params):
+        return extension().color_forward(graph.points, graph.offsets, graph.adj, *[p.detach() for p in params],
+                                         int(sh_deg), x, dirs, site)
+    return _Color.apply(*params, x, dirs, site, graph, int(sh_deg))
 
 
 class _March(torch.autograd.Function):

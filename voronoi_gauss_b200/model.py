@@ -67,6 +67,10 @@ class VoronoiGaussField(nn.Module):
     def sh(self):
         return torch.cat([self.sh_dc, self.sh_rest], 1)
 
+    def walk(self, o, d, z, start):
+        """Nearest sites of the sorted samples o + z d (model.py:48-49)."""
+        return self.graph.walk(o, d, z, start)
+
     def param_groups(self, lr):
         return [
             {'params': [self.raw], 'lr': lr['raw'], 'name': 'raw'},

@@ -7,10 +7,12 @@
 * ``render_rays_uniform`` (render.py:109-124): the same with ``ext.march`` and a conic floor of dt / 2.
 * ``sh_basis``, ``morton_order``, ``pack_foam``, ``bake_colors``, ``render_rays_foam_infer``
   (render.py:143-257): the inference layout and its renderer.
+* ``s_to_t``, ``sample_pdf``, ``composite``, ``proposal_weights``, ``resample``, ``render_rays``
+  (render.py:28-106): the NeRF-style proposal sampler over the field kernels (``Graph.walk``,
+  ``ext.density``, ``ext.color``): 64 stratified samples in a normalised ray coordinate s (linear in t
+  inside the unit ball, linear in disparity beyond), two gradient-free proposal passes with widened
+  density Gaussians, then the merged samples walked to their sites and rendered with gradients.
 * ``render_image`` (render.py:260-266).
-
-The NeRF-style proposal sampler (``render_rays``, render.py:77-106) uses the vgf.cu field kernels, which
-are not part of this build.
 """
 
 from __future__ import annotations
@@ -32,6 +34,95 @@ def ray_bounds(o, d, near, far_radius):
     t_mid = sphere_exit(o, d, 1.0).clamp_min(near + 1e-3)
     t_far = torch.maximum(sphere_exit(o, d, far_radius), t_mid + 1e-3)
     return torch.full_like(t_mid, near), t_mid, t_far
+
+
+def s_to_t(s, t_near, t_mid, t_far):
+    """Ray depth of the normalised coordinate s in [0, 1] (render.py:28-33): s < 1/2 maps linearly onto
+    [near, mid], s >= 1/2 linearly in disparity onto [mid, far]."""
+    t_near, t_mid, t_far = t_near[:, None], t_mid[:, None], t_far[:, None]
+    inside = t_near + (t_mid - t_near) * (2 * s).clamp(max=1)
+    u = (2 * s - 1).clamp(min=0)
+    beyond = 1.0 / (1.0 / t_mid + u * (1.0 / t_far - 1.0 / t_mid))
+    return torch.where(s < 0.5, inside, beyond)
+
+
+def sample_pdf(bins, weights, n, det=True):
+    """n samples per row from the piecewise-constant density of `weights` over `bins` (render.py:36-50):
+    inverse-CDF sampling at stratified midpoints (det) or uniform draws."""
+    w = weights + 1e-5
+    cdf = torch.cumsum(w / w.sum(-1, keepdim=True), -1)
+    cdf = torch.cat([torch.zeros_like(cdf[:, :1]), cdf], -1)
+    if det:
+        u = torch.linspace(0.5 / n, 1 - 0.5 / n, n, device=bins.device).expand(len(bins), n).contiguous()
+    else:
+        u = torch.rand(len(bins), n, device=bins.device)
+    hi = torch.searchsorted(cdf, u, right=True)
+    lo = (hi - 1).clamp_min(0)
+    hi = hi.clamp_max(cdf.shape[-1] - 1)
+    c0, c1 = cdf.gather(1, lo), cdf.gather(1, hi)
+    b0, b1 = bins.gather(1, lo), bins.gather(1, hi)
+    span = c1 - c0
+    span = torch.where(span < 1e-5, torch.ones_like(span), span)
+    return b0 + (u - c0) / span * (b1 - b0)
+
+
+def composite(sigma, t, t_far):
+    """Front-to-back weights of point samples (render.py:53-57): the last interval runs to t_far;
+    returns (weights (B, S), final transmittance (B))."""
+    delta = torch.cat([t[:, 1:] - t[:, :-1], (t_far[:, None] - t[:, -1:]).clamp_min(0)], 1)
+    alpha = 1.0 - torch.exp(-sigma * delta)
+    trans = torch.cumprod(torch.cat([torch.ones_like(alpha[:, :1]), 1.0 - alpha + 1e-10], 1), 1)
+    return alpha * trans[:, :-1], trans[:, -1]
+
+
+def proposal_weights(model, o, d, s, bounds, start, scale_mult):
+    """Compositing weights of samples s under the density widened by scale_mult, without gradients
+    (render.py:60-68)."""
+    t = s_to_t(s, *bounds)
+    site, _ = model.walk(o, d, t, start)
+    x = (o[:, None] + d[:, None] * t[..., None]).reshape(-1, 3)
+    with torch.no_grad():
+        sigma = ext.density(model.graph, model.raw, model.d_log_scale, model.d_quat, x, site.reshape(-1),
+                            scale_mult).view_as(t)
+    w, _ = composite(sigma, t, bounds[2])
+    return w
+
+
+def resample(s, w, n, det):
+    """n new samples drawn from the weights w of the sorted samples s (render.py:71-74)."""
+    mid = 0.5 * (s[:, 1:] + s[:, :-1])
+    bins = torch.cat([torch.zeros_like(s[:, :1]), mid, torch.ones_like(s[:, :1])], 1)
+    return sample_pdf(bins, w, n, det)
+
+
+def render_rays(model, o, d, start, n_coarse=64, n_fine=(64, 64), proposal_mult=(4.0, 2.0), near=0.02,
+                far_radius=4.0, perturb=True, min_weight=1e-4):
+    """NeRF-style rendering (render.py:77-106): o, d (B, 3) rays, start (B,) the site containing each
+    origin -> dict with rgb (B, 3), acc, depth and sampler statistics. Colours are evaluated only for the
+    samples with weight > min_weight."""
+    B = len(o)
+    bounds = ray_bounds(o, d, near, far_radius)
+    s = torch.linspace(0, 1, n_coarse + 1, device=o.device)[:-1].expand(B, n_coarse)
+    s = s + (torch.rand_like(s) if perturb else 0.5) / n_coarse
+    with torch.no_grad():
+        for n, mult in zip(n_fine, proposal_mult):
+            w = proposal_weights(model, o, d, s, bounds, start, mult)
+            s, _ = torch.sort(torch.cat([s, resample(s, w, n, det=not perturb)], 1), 1)
+        t = s_to_t(s, *bounds)
+        site, steps = model.walk(o, d, t, start)
+    S = t.shape[1]
+    x = (o[:, None] + d[:, None] * t[..., None]).reshape(-1, 3)
+    site = site.reshape(-1)
+    sigma = ext.density(model.graph, model.raw, model.d_log_scale, model.d_quat, x, site).view(B, S)
+    w, t_final = composite(sigma, t, bounds[2])
+    active = (w.detach() > min_weight).reshape(-1).nonzero().squeeze(1)
+    dirs = d[:, None].expand(B, S, 3).reshape(-1, 3)
+    c = ext.color(model.graph, model.c_log_scale, model.c_quat, model.sh(), x[active], dirs[active], site[active],
+                  model.sh_deg)
+    rgb_s = torch.zeros(B * S, 3, device=o.device, dtype=c.dtype).index_put((active,), c).view(B, S, 3)
+    rgb = (w[..., None] * rgb_s).sum(1) + t_final[:, None] * torch.sigmoid(model.bg_logit)
+    return {'rgb': rgb, 'acc': 1.0 - t_final, 'depth': (w * t).sum(1), 'walk_steps': steps.float().mean() / S,
+            'active': len(active) / (B * S)}
 
 
 def render_rays_uniform(model, o, d, start, dt=1 / 512, n_bg=64, near=0.02, far_radius=4.0, t_thresh=1e-4,
@@ -186,7 +277,7 @@ def render_rays_foam_infer(model, pack, o, d, start, near=0.02, far_radius=4.0, 
 
 
 @torch.no_grad()
-def render_image(model, scene, i, start, chunk=8192, renderer=render_rays_foam, **kw):
+def render_image(model, scene, i, start, chunk=8192, renderer=render_rays, **kw):
     """Renders image i of a scene with .image_rays(i) -> (o, d, gt) and .H, .W (render.py:260-266)."""
     o, d, gt = scene.image_rays(i)
     start = torch.full((len(o),), int(start), dtype=torch.int32, device=o.device)
