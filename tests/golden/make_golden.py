@@ -16,6 +16,8 @@ the reference's float64 restatements:
 * sh_basis.npz     - render.sh_basis for degrees 0..3 (render.py:143-165).
 * foam_config1.npz - 64 rays of an orbit camera over the config-1 scene (10k uniform sites), float64
                      trace + compositing + sparse gradients.
+* ckpt_small.pth   - a checkpoint written in train.py's format (train.py:168-170) from the reference's
+                     own VoronoiGaussField (model.py:19-59), 300 sites, randomised parameters.
 * field_small.npz  - test_grad.py's setup (400 uniform sites, rng(0)): exact nearest sites (cKDTree) of
                      sorted ray samples for the walk, and the float64 density / colour fields with
                      their autograd gradients (test_grad.py:45-125).
@@ -295,6 +297,23 @@ def make_field_small():
         **{f'ref_g_{k}': r.grad.numpy() for k, r in zip(('raw', 'ls', 'quat', 'cls', 'cquat', 'sh'), ref)})
 
 
+def make_ckpt_small():
+    import model as ref_model
+    rng, pts, offsets, adj, *_ = small_scene(4)
+    n = len(pts)
+    P = torch.tensor(pts, dtype=torch.float32)
+    m = ref_model.VoronoiGaussField(P, torch.tensor(offsets), torch.tensor(adj), torch.rand(n, 3),
+                                    torch.full((n,), 0.05))
+    g = torch.Generator().manual_seed(9)
+    with torch.no_grad():
+        for p in m.parameters():
+            p.add_(torch.randn(p.shape, generator=g) * 0.1)
+    m.sh_deg = 2
+    torch.save({'state': m.state_dict(), 'points': m.graph.points, 'offsets': m.graph.offsets, 'adj': m.graph.adj,
+                'sh_deg': m.sh_deg, 'normalization': {'scale': 1.0}, 'args': {'iters': 0}},
+               os.path.join(HERE, 'ckpt_small.pth'))
+
+
 if __name__ == '__main__':
     make_sh_basis()
     make_conic()
@@ -302,4 +321,5 @@ if __name__ == '__main__':
     make_march_small()
     make_foam_config1()
     make_field_small()
+    make_ckpt_small()
     print('fixtures written to', HERE)
