@@ -195,6 +195,29 @@ int vg_color_backward(const void* pack, int64_t n_sites, int64_t n_adj, const fl
 
 /* ---------------------------------------------------------------------------------- inference */
 
+/* Workspace of vg_infer_pack. */
+size_t vg_infer_pack_workspace_bytes(int64_t n_sites);
+
+/* render.pack_foam (render.py:179-225) on the device: the inference layout of vg_foam_infer from the
+ * scene (points (N, 3), offsets (N + 1), adj (M)) and the model parameters (raw (N), d/c log-scales
+ * (N, 3), d/c quaternions (N, 4), sh (N, 16, 3) fp32). Outputs points4 (N, 4), offsets_out (N + 1),
+ * nbr (N + M), edge (N + M, 4), attr (N, 20) (baked colours zero), sh_out (N, 16, 3) in fp16 when
+ * sh_half else fp32, sh32 (N, 16, 3) fp32 in the output order (may be NULL) and, with reorder, orig (N)
+ * = the Morton permutation of the graph pack `pack` (which must then be non-null). Bit-identical to
+ * pack_foam on the GPU. */
+int vg_infer_pack(const void* pack, int64_t n_sites, int64_t n_adj, const float* points, const int32_t* offsets,
+                  const int32_t* adj, const float* raw, const float* d_log_scale, const float* d_quat,
+                  const float* c_log_scale, const float* c_quat, const float* sh, double scale_floor,
+                  double eps_density, int sh_half, int reorder, float* points4, int32_t* offsets_out, int32_t* nbr,
+                  float* edge, float* attr, void* sh_out, float* sh32, int32_t* orig, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
+/* render.bake_colors (render.py:228-235): attr[:, 16:19] = max(SH_k(d_k) + 1/2, 0) for the unit
+ * direction d_k from the camera centre (cx, cy, cz) to site k; points4 and sh32 as written by
+ * vg_infer_pack. */
+int vg_bake_colors(const float* points4, const float* sh32, int sh_deg, int64_t n_sites, float cx, float cy, float cz,
+                   float* attr, void* stream);
+
 /* foam_infer (foam_infer.cu:376-435) on the packed inference layout of render.pack_foam: points (N, 4),
  * offsets (N + 1) into self-first neighbourhoods, nbr (E), edge (E, 4) = (p, half2(r2, lam)),
  * attr (N, 20), sh (N, 16, 3) float32 (sh_half = 0) or float16 (sh_half = 1, may be NULL for baked

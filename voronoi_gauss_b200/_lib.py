@@ -52,6 +52,10 @@ SIGNATURES = {
     'vg_density_backward': (I32, [P, I64, I64, P, P, P, P, P, I64, P, P, P, P, P, SZ, P]),
     'vg_color_forward': (I32, [P, I64, I64, P, P, P, I32, P, P, P, I64, P, P, SZ, P]),
     'vg_color_backward': (I32, [P, I64, I64, P, P, P, I32, P, P, P, I64, P, P, P, P, P, P, SZ, P]),
+    'vg_infer_pack_workspace_bytes': (SZ, [I64]),
+    'vg_infer_pack': (I32, [P, I64, I64, P, P, P, P, P, P, P, P, P, F64, F64, I32, I32, P, P, P, P, P, P, P, P, P, SZ,
+                            P]),
+    'vg_bake_colors': (I32, [P, P, I32, I64, F32, F32, F32, P, P]),
     'vg_foam_infer': (I32, [P, P, P, P, P, P, I32, I32, I64, I64, P, P, P, P, P, I64, F32, F32, F32, I32, I32, P, P, P,
                             P, P, P, P]),
 }

@@ -1,5 +1,6 @@
 // extern "C" entry points of libvgb200 (declared in include/vgb200.h): argument checks with the
 // reference's error semantics, workspace carving and dispatch to the kernels.
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -458,6 +459,51 @@ int vg_color_backward(const void* pack, int64_t n_sites, int64_t n_adj, const fl
                                           nullptr, g_ls, g_quat, g_sh, workspace, status,
                                           static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_color_backward");
+}
+
+size_t vg_infer_pack_workspace_bytes(int64_t n_sites) {
+    return n_sites > 0 ? vg::infer_pack_workspace(n_sites) : 0;
+}
+
+int vg_infer_pack(const void* pack, int64_t n_sites, int64_t n_adj, const float* points, const int32_t* offsets,
+                  const int32_t* adj, const float* raw, const float* d_log_scale, const float* d_quat,
+                  const float* c_log_scale, const float* c_quat, const float* sh, double scale_floor,
+                  double eps_density, int sh_half, int reorder, float* points4, int32_t* offsets_out, int32_t* nbr,
+                  float* edge, float* attr, void* sh_out, float* sh32, int32_t* orig, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+    REQUIRE(n_sites > 0 && n_sites < INT32_MAX, "n_sites must be in [1, 2^31)");
+    REQUIRE(n_adj >= 0 && n_sites + n_adj < INT32_MAX, "adjacency too large for int32 offsets");
+    REQUIRE(points && offsets && (adj || n_adj == 0), "points, offsets and adj must be non-null");
+    REQUIRE(raw && d_log_scale && d_quat && c_log_scale && c_quat && sh, "parameters must be non-null");
+    REQUIRE(aligned(d_quat, 16) && aligned(c_quat, 16), "quaternions must be 16-byte aligned");
+    REQUIRE(points4 && offsets_out && nbr && edge && attr && sh_out, "outputs must be non-null");
+    REQUIRE(aligned(points4, 16) && aligned(edge, 16), "points4 and edge must be 16-byte aligned");
+    REQUIRE(!reorder || (pack && orig), "reorder needs the graph pack and orig");
+    REQUIRE(eps_density >= 0.0, "eps_density must be >= 0");
+    REQUIRE(aligned(workspace, 256), "workspace must be 256-byte aligned");
+    const size_t need = vg::infer_pack_workspace(n_sites);
+    if (workspace == nullptr || workspace_bytes < need)
+        return fail(VG_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);
+    vg::GraphView g{};
+    if (reorder) g = vg::graph_view(pack, n_sites, n_adj);
+    const float log_eps = eps_density > 0.0 ? static_cast<float>(std::log(eps_density)) : 0.f;
+    const cudaError_t e =
+        vg::infer_pack(reorder ? &g : nullptr, n_sites, points, offsets, adj, raw, d_log_scale, d_quat, c_log_scale,
+                       c_quat, sh, static_cast<float>(scale_floor * scale_floor), log_eps, eps_density > 0.0, sh_half,
+                       points4, offsets_out, nbr, edge, attr, sh_out, sh32, orig, workspace,
+                       static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_infer_pack");
+}
+
+int vg_bake_colors(const float* points4, const float* sh32, int sh_deg, int64_t n_sites, float cx, float cy, float cz,
+                   float* attr, void* stream) {
+    REQUIRE(n_sites >= 0 && n_sites < INT32_MAX, "n_sites must be in [0, 2^31)");
+    REQUIRE(n_sites == 0 || (points4 && sh32 && attr), "arrays must be non-null");
+    REQUIRE(aligned(points4, 16), "points4 must be 16-byte aligned");
+    REQUIRE(sh_deg >= 0 && sh_deg <= 3, "sh_deg must be in 0..3");
+    const cudaError_t e = vg::bake_colors(points4, sh32, sh_deg, n_sites, cx, cy, cz, attr,
+                                          static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_bake_colors");
 }
 
 int vg_foam_infer(const float* points, const int32_t* offsets, const int32_t* nbr, const float* edge,

@@ -313,6 +313,17 @@ cudaError_t color_field(const GraphView& g, const float* ls, const float* quat, 
                         const float* g_rgb, float* rgb, float* g_ls, float* g_quat, float* g_sh, void* ws, int* status,
                         cudaStream_t st);
 
+// infer_pack.cu: the inference layout of render.pack_foam / bake_colors. g (the graph pack) renumbers
+// the sites in Morton order when non-null; floor2 = fp32(scale_floor^2), log_eps = fp32(log eps_density).
+size_t infer_pack_workspace(int64_t n_sites);
+cudaError_t infer_pack(const GraphView* g, int64_t n, const float* points, const int* offsets, const int* adj,
+                       const float* raw, const float* d_ls, const float* d_quat, const float* c_ls,
+                       const float* c_quat, const float* sh, float floor2, float log_eps, int with_eps, int sh_half,
+                       float* points4, int* offsets_out, int* nbr, float* edge, float* attr, void* sh_out,
+                       float* sh32, int* orig, void* ws, cudaStream_t st);
+cudaError_t bake_colors(const float* points4, const float* sh32, int sh_deg, int64_t n, float cx, float cy, float cz,
+                        float* attr, cudaStream_t st);
+
 // infer.cu
 struct InferNet {
     const float4* points;

@@ -197,62 +197,59 @@ def morton_order(points, bits=10):
 
 @torch.no_grad()
 def pack_foam(model, scale_floor=0.0, eps_density=0.0, sh_half=False, reorder=False):
-    """Records of the inference renderer (render.py:179-225): self-first neighbourhoods (offsets (N + 1),
-    nbr (E)) with one float4 per edge = (p_j, half2(r2_j, lam_j)); r2 the squared distance beyond which
-    rho_j G_j < eps_density (inf when eps_density = 0), lam the smallest eigenvalue of the colour conic, both
-    rounded to the safe side; attr (N, 20) = (density conic, min(raw, 30), 0, colour conic, 0, 0, baked rgb, 0);
-    sh (N, 16, 3) fp32 or fp16. reorder renumbers the sites along a Z-order curve (perm: new -> old, inv:
-    old -> new; orig = perm breaks ties as before the renumbering)."""
+    """Records of the inference renderer (render.py:179-225), built on the device by vg_infer_pack:
+    self-first neighbourhoods (offsets (N + 1), nbr (E)) with one float4 per edge = (p_j, half2(r2_j,
+    lam_j)); r2 the squared distance beyond which rho_j G_j < eps_density (inf when eps_density = 0), lam
+    the smallest eigenvalue of the colour conic, both rounded to the safe side; attr (N, 20) = (density
+    conic, min(raw, 30), 0, colour conic, 0, 0, baked rgb, 0); sh (N, 16, 3) fp32 or fp16. reorder renumbers
+    the sites along a Z-order curve (perm: new -> old, inv: old -> new; orig = perm breaks ties as before
+    the renumbering)."""
+    from . import _lib
     g = model.graph
-    n = len(g.points)
+    n, m = len(g.points), len(g.adj)
     dev = g.points.device
-    raw = model.raw.clamp(max=30.0)
-    if eps_density > 0:
-        s_max2 = (torch.exp(2 * model.d_log_scale.clamp(-20, 20)) + scale_floor ** 2).amax(-1)
-        r2 = 2 * s_max2 * (raw - math.log(eps_density)).clamp_min(0) * (1 + 2 ** -9)
-    else:
-        r2 = torch.full_like(raw, float('inf'))
-    lam = 1.0 / (torch.exp(2 * model.c_log_scale.clamp(-20, 20)) + scale_floor ** 2).amax(-1)
-    lam = (lam * (1 - 2 ** -9)).clamp(max=65000.0)
-    cut = torch.stack([r2, lam], -1).half().view(torch.float32)[:, 0]
-    off = g.offsets.long()
-    deg = off[1:] - off[:-1]
-    offsets = off + torch.arange(n + 1, device=dev)          # self-first: one extra edge per cell
-    row = torch.repeat_interleave(torch.arange(n, device=dev), deg)
-    nbr = torch.empty(len(g.adj) + n, dtype=torch.long, device=dev)
-    nbr[offsets[:-1]] = torch.arange(n, device=dev)
-    nbr[torch.arange(len(g.adj), device=dev) + row + 1] = g.adj.long()
-    edge = torch.cat([g.points[nbr], cut[nbr, None]], 1).contiguous()
-    points = torch.cat([g.points, torch.zeros_like(raw)[:, None]], 1).contiguous()
-    dA = ext.conic(model.d_log_scale, model.d_quat, scale_floor)
-    cA = ext.conic(model.c_log_scale, model.c_quat, scale_floor)
-    z = torch.zeros_like(raw)[:, None]
-    attr = torch.cat([dA, raw[:, None], z, cA, z, z, z, z, z, z], 1).contiguous()
-    sh = model.sh().contiguous()
+    if dev.type != 'cuda':
+        raise RuntimeError('pack_foam needs the scene on a CUDA device')
+    f = [t.detach().float().contiguous() for t in (model.raw, model.d_log_scale, model.d_quat, model.c_log_scale,
+                                                    model.c_quat, model.sh())]
+    points = torch.empty(n, 4, device=dev)
+    offsets = torch.empty(n + 1, dtype=torch.int32, device=dev)
+    nbr = torch.empty(n + m, dtype=torch.int32, device=dev)
+    edge = torch.empty(n + m, 4, device=dev)
+    attr = torch.empty(n, 20, device=dev)
+    sh = torch.empty(n, 16, 3, dtype=torch.float16 if sh_half else torch.float32, device=dev)
+    sh32 = torch.empty(n, 16, 3, device=dev)
+    orig = torch.empty(n if reorder else 0, dtype=torch.int32, device=dev)
+    nbytes = _lib.lib().vg_infer_pack_workspace_bytes(n)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    pk = g.pack if reorder else None
+    with torch.cuda.device(dev):
+        _lib.call('vg_infer_pack', pk.ptr if pk is not None else None, n, m, g.points.data_ptr(),
+                  g.offsets.data_ptr(), g.adj.data_ptr() if m else None, *(t.data_ptr() for t in f),
+                  float(scale_floor), float(eps_density), int(sh_half), int(reorder), points.data_ptr(),
+                  offsets.data_ptr(), nbr.data_ptr(), edge.data_ptr(), attr.data_ptr(), sh.data_ptr(),
+                  sh32.data_ptr(), orig.data_ptr() if reorder else None, ws.data_ptr(), nbytes,
+                  torch.cuda.current_stream(dev).cuda_stream)
     perm = inv = None
     if reorder:
-        perm = morton_order(g.points)
+        perm = orig.long()
         inv = torch.empty_like(perm)
         inv[perm] = torch.arange(n, device=dev)
-        size = (deg + 1)[perm]
-        new_off = torch.cat([torch.zeros_like(size[:1]), torch.cumsum(size, 0)])
-        cell = torch.repeat_interleave(torch.arange(n, device=dev), size)
-        old = offsets[perm][cell] + torch.arange(len(nbr), device=dev) - new_off[cell]
-        offsets, nbr, edge = new_off, inv[nbr[old]], edge[old].contiguous()
-        points, attr, sh = points[perm].contiguous(), attr[perm].contiguous(), sh[perm].contiguous()
-    return {'points': points, 'offsets': offsets.int().contiguous(), 'nbr': nbr.int().contiguous(), 'edge': edge,
-            'attr': attr, 'sh': sh.half() if sh_half else sh, 'sh32': sh, 'perm': perm, 'inv': inv,
-            'orig': (perm if reorder else torch.empty(0, device=dev)).int().contiguous(), 'baked_center': None}
+    return {'points': points, 'offsets': offsets, 'nbr': nbr, 'edge': edge, 'attr': attr, 'sh': sh, 'sh32': sh32,
+            'perm': perm, 'inv': inv, 'orig': orig, 'baked_center': None}
 
 
 @torch.no_grad()
 def bake_colors(model, pack, center):
     """Site colours max(SH_k(d_k) + 1/2, 0) for the direction d_k from the camera centre to site k
-    (render.py:228-235)."""
-    points = model.graph.points if pack['perm'] is None else model.graph.points[pack['perm']]
-    dirs = torch.nn.functional.normalize(points - center.view(1, 3), dim=-1)
-    rgb = torch.einsum('nj,njc->nc', sh_basis(dirs, model.sh_deg), pack['sh32']).add_(0.5).clamp_min_(0.0)
-    pack['attr'][:, 16:19] = rgb
+    (render.py:228-235), written into pack['attr'][:, 16:19] on the device (vg_bake_colors)."""
+    from . import _lib
+    c = [float(v) for v in center.reshape(-1).tolist()]
+    n = len(pack['points'])
+    dev = pack['points'].device
+    with torch.cuda.device(dev):
+        _lib.call('vg_bake_colors', pack['points'].data_ptr(), pack['sh32'].data_ptr(), int(model.sh_deg), n, *c,
+                  pack['attr'].data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
     pack['baked_center'] = center
 
 
