@@ -218,6 +218,22 @@ int vg_infer_pack(const void* pack, int64_t n_sites, int64_t n_adj, const float*
 int vg_bake_colors(const float* points4, const float* sh32, int sh_deg, int64_t n_sites, float cx, float cy, float cz,
                    float* attr, void* stream);
 
+/* ------------------------------------------------------------------------------ scene preparation */
+
+/* Pinhole rays of a width x height image (colmap.py:129-134): d = c2w K^-1 (px + 0.5, py + 0.5, 1)
+ * normalised, o = centre. K_inv, c2w: HOST 3 x 3 row-major arrays (K_inv of a pinhole camera: row 1
+ * column 0 zero, last row (0, 0, 1)); centre: HOST 3 floats. Outputs o, d (W H, 3) on the device, in
+ * tile_h x tile_w pixel tiles (tiles row-major, pixels row-major inside a tile; the ray order of
+ * bench_infer.py:37-41), or row-major pixels when tile_h == 0. */
+int vg_camera_rays(const float* K_inv, const float* c2w, const float* centre, int width, int height, int tile_h,
+                   int tile_w, float* o, float* d, void* stream);
+
+/* sites.nearest_sites (sites.py:38-39): the site nearest to each of the n_queries points queries
+ * (n_queries, 3), as original ids in site (n_queries) int32, by greedy walks on the packed graph (distance
+ * ties to the smaller id). Used for the `start` site of every ray (render.py:263). */
+int vg_nearest_sites(const void* pack, int64_t n_sites, int64_t n_adj, const float* queries, int64_t n_queries,
+                     int32_t* site, void* stream);
+
 /* foam_infer (foam_infer.cu:376-435) on the packed inference layout of render.pack_foam: points (N, 4),
  * offsets (N + 1) into self-first neighbourhoods, nbr (E), edge (E, 4) = (p, half2(r2, lam)),
  * attr (N, 20), sh (N, 16, 3) float32 (sh_half = 0) or float16 (sh_half = 1, may be NULL for baked

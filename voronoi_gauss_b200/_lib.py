@@ -56,6 +56,8 @@ SIGNATURES = {
     'vg_infer_pack': (I32, [P, I64, I64, P, P, P, P, P, P, P, P, P, F64, F64, I32, I32, P, P, P, P, P, P, P, P, P, SZ,
                             P]),
     'vg_bake_colors': (I32, [P, P, I32, I64, F32, F32, F32, P, P]),
+    'vg_camera_rays': (I32, [P, P, P, I32, I32, I32, I32, P, P, P]),
+    'vg_nearest_sites': (I32, [P, I64, I64, P, I64, P, P]),
     'vg_foam_infer': (I32, [P, P, P, P, P, P, I32, I32, I64, I64, P, P, P, P, P, I64, F32, F32, F32, I32, I32, P, P, P,
                             P, P, P, P]),
 }

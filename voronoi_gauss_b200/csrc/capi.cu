@@ -506,6 +506,34 @@ int vg_bake_colors(const float* points4, const float* sh32, int sh_deg, int64_t 
     return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_bake_colors");
 }
 
+int vg_camera_rays(const float* K_inv, const float* c2w, const float* centre, int width, int height, int tile_h,
+                   int tile_w, float* o, float* d, void* stream) {
+    REQUIRE(K_inv && c2w && centre, "K_inv, c2w and centre must be non-null host arrays");
+    REQUIRE(width >= 0 && height >= 0, "image size must be >= 0");
+    REQUIRE(tile_h >= 0 && (tile_h == 0 || tile_w > 0), "tile sizes must be positive (tile_h 0: row-major)");
+    REQUIRE(K_inv[3] == 0.f && K_inv[6] == 0.f && K_inv[7] == 0.f && K_inv[8] == 1.f,
+            "K_inv must be the inverse of a pinhole intrinsic matrix (row 1 column 0 zero, last row 0 0 1)");
+    REQUIRE(static_cast<int64_t>(width) * height == 0 || (o && d), "o and d must be non-null");
+    const cudaError_t e = vg::camera_rays(K_inv, c2w, centre, width, height, tile_h, tile_w, o, d,
+                                          static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_camera_rays");
+}
+
+int vg_nearest_sites(const void* pack, int64_t n_sites, int64_t n_adj, const float* queries, int64_t n_queries,
+                     int32_t* site, void* stream) {
+    REQUIRE(pack != nullptr, "graph pack is null");
+    REQUIRE(n_sites > 0 && n_sites < INT32_MAX, "n_sites must be in [1, 2^31)");
+    REQUIRE(n_adj >= 0 && n_sites + n_adj < INT32_MAX, "adjacency too large for int32 offsets");
+    REQUIRE(n_queries >= 0, "n_queries must be >= 0");
+    REQUIRE(n_queries == 0 || (queries && site), "queries and site must be non-null");
+    if (n_queries == 0) return VG_OK;
+    int* status = status_ptr();
+    if (status == nullptr) return fail(VG_ERR_CUDA, "status word unavailable");
+    const cudaError_t e = vg::nearest_sites(vg::graph_view(pack, n_sites, n_adj), queries, n_queries, site, status,
+                                            static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_nearest_sites");
+}
+
 int vg_foam_infer(const float* points, const int32_t* offsets, const int32_t* nbr, const float* edge,
                   const float* attr, const void* sh, int sh_half, int sh_deg, int64_t n_sites, int64_t n_edges,
                   const float* o, const float* d, const int32_t* start, const float* near, const float* far,

@@ -324,6 +324,13 @@ cudaError_t infer_pack(const GraphView* g, int64_t n, const float* points, const
 cudaError_t bake_colors(const float* points4, const float* sh32, int sh_deg, int64_t n, float cx, float cy, float cz,
                         float* attr, cudaStream_t st);
 
+// rays.cu: camera rays in pixel-tile order (th = 0: row-major) and nearest sites by greedy walks.
+// K_inv, c2w: host 3 x 3 row-major; centre: host 3.
+cudaError_t camera_rays(const float* K_inv, const float* c2w, const float* centre, int W, int H, int th, int tw,
+                        float* o, float* d, cudaStream_t st);
+cudaError_t nearest_sites(const GraphView& g, const float* queries, int64_t n_queries, int* out, int* status,
+                          cudaStream_t st);
+
 // infer.cu
 struct InferNet {
     const float4* points;

@@ -27,7 +27,7 @@ import torch
 from . import _lib
 
 __all__ = ['Graph', 'foam', 'march', 'conic', 'conic_reference', 'density', 'color', 'extension', 'march_extension',
-           'foam_extension', 'foam_infer_extension', 'GraphPack', 'graph_pack']
+           'foam_extension', 'foam_infer_extension', 'GraphPack', 'graph_pack', 'nearest_sites']
 
 
 # (start, end) CUDA events recorded on the launching stream around the foam backward launch while set
@@ -122,6 +122,22 @@ class Graph:
         site, steps = extension().walk(self.points, self.offsets, self.adj, o.float().contiguous(),
                                        d.float().contiguous(), z.float().contiguous(), start.int().contiguous())
         return site, steps
+
+
+def nearest_sites(graph, queries):
+    """Original id of the site nearest to each query point (Q, 3) on the device (greedy walks on the
+    packed graph; the reference does this on the host with a k-d tree, sites.py:38-39). -> (Q,) int32."""
+    q = queries.detach().float().contiguous()
+    _check(q, 'queries', torch.float32)
+    if q.dim() != 2 or q.size(1) != 3:
+        raise RuntimeError('queries must be (Q, 3)')
+    out = torch.empty(q.size(0), dtype=torch.int32, device=q.device)
+    if q.size(0):
+        pk = graph.pack
+        with torch.cuda.device(q.device):
+            _lib.call('vg_nearest_sites', pk.ptr, pk.n, pk.m, q.data_ptr(), q.size(0), out.data_ptr(),
+                      _stream(q.device))
+    return out
 
 
 # ------------------------------------------------------------------------- extension-level functions

@@ -199,6 +199,27 @@ def tile_order(H, W, th=4, tw=8):
     return np.argsort(key.ravel(), kind='stable')
 
 
+def camera_rays_device(centre, c2w, W, H, fov_deg=50.0, device='cuda', tile=(4, 8)):
+    """camera_rays generated on the device by vg_camera_rays, directly in tile[0] x tile[1] pixel-tile
+    order (the order of tile_order(H, W, *tile); tile None: row-major). -> o, d (W H, 3) float32."""
+    from . import _lib
+    f = 0.5 * W / math.tan(math.radians(fov_deg) / 2.0)
+    K = np.array([[f, 0.0, W / 2.0], [0.0, f, H / 2.0], [0.0, 0.0, 1.0]])
+    k_inv = np.ascontiguousarray(np.linalg.inv(K), np.float32)
+    k_inv[1, 0] = k_inv[2, 0] = k_inv[2, 1] = 0.0
+    k_inv[2, 2] = 1.0
+    rot = np.ascontiguousarray(np.asarray(c2w, np.float64), np.float32)
+    ctr = np.ascontiguousarray(np.asarray(centre, np.float64), np.float32)
+    dev = torch.device(device)
+    o = torch.empty(W * H, 3, device=dev)
+    d = torch.empty(W * H, 3, device=dev)
+    th, tw = tile if tile is not None else (0, 0)
+    with torch.cuda.device(dev):
+        _lib.call('vg_camera_rays', k_inv.ctypes.data, rot.ctypes.data, ctr.ctypes.data, int(W), int(H), int(th),
+                  int(tw), o.data_ptr(), d.data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
+    return o, d
+
+
 def camera_rays(centre, c2w, W, H, fov_deg=50.0, device='cpu', order=None):
     """Pinhole rays of every pixel (colmap.py:129-134): d = c2w K^-1 (px + 0.5, py + 0.5, 1),
     normalised. -> o (P, 3), d (P, 3) float32, in `order` (a pixel permutation) if given."""
