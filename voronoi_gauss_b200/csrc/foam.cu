@@ -54,6 +54,12 @@
 #ifndef VG_BWD_CELL_MAJOR
 #define VG_BWD_CELL_MAJOR 1
 #endif
+// VG_BWD_BALANCE     1: cm_scatter_kernel spreads a chunk's (neighbour, sample) pairs over all 32 lanes
+//                    for cells with fewer than 32 neighbours (replicas / two phases, see balanced_scatter);
+//                    0: one lane per neighbour
+#ifndef VG_BWD_BALANCE
+#define VG_BWD_BALANCE 1
+#endif
 
 namespace vg {
 namespace {
@@ -496,6 +502,156 @@ __global__ void __launch_bounds__(kBlock)
 // Shared-memory image of one staged sample: x, gs | gC, gC.C | m_min, 1/sum a, -, - | SH basis (16).
 constexpr int kItemVec = 7;
 
+// Gradient sums of one neighbour site over a range of a chunk's samples.
+template <int S4>
+struct PairAcc {
+    float ad[8];        // g_raw, g_dA[6], -
+    float ac[6];        // g_cA[6]
+    float ash[4 * S4];  // g_sh
+    __device__ __forceinline__ void zero() {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) ad[u] = 0.f;
+#pragma unroll
+        for (int u = 0; u < 6; ++u) ac[u] = 0.f;
+#pragma unroll
+        for (int u = 0; u < 4 * S4; ++u) ash[u] = 0.f;
+    }
+    // adds the sums held by lane `src` (every lane of the warp takes part; lanes with take == false
+    // discard what they receive)
+    __device__ __forceinline__ void pull(int src, bool take) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const float v = __shfl_sync(0xffffffffu, ad[u], src);
+            if (take) ad[u] += v;
+        }
+#pragma unroll
+        for (int u = 0; u < 6; ++u) {
+            const float v = __shfl_sync(0xffffffffu, ac[u], src);
+            if (take) ac[u] += v;
+        }
+#pragma unroll
+        for (int u = 0; u < 4 * S4; ++u) {
+            const float v = __shfl_sync(0xffffffffu, ash[u], src);
+            if (take) ash[u] += v;
+        }
+    }
+    __device__ __forceinline__ void flush(float* __restrict__ grad, int j) const {
+        float* G = grad + kGradStride * static_cast<int64_t>(j);
+        const float4 d0 = make_float4(ad[0], ad[1], ad[2], ad[3]), d1 = make_float4(ad[4], ad[5], ad[6], 0.f);
+        const float4 c0 = make_float4(ac[0], ac[1], ac[2], ac[3]), c1 = make_float4(ac[4], ac[5], 0.f, 0.f);
+        if (nonzero(d0)) red4(G, d0);
+        if (nonzero(d1)) red4(G + 4, d1);
+        if (nonzero(c0)) red4(G + 8, c0);
+        if (nonzero(c1)) red4(G + 12, c1);
+#pragma unroll
+        for (int qq = 0; qq < S4; ++qq) {
+            const float4 v = make_float4(ash[4 * qq], ash[4 * qq + 1], ash[4 * qq + 2], ash[4 * qq + 3]);
+            if (nonzero(v)) red4(G + 16 + 4 * qq, v);
+        }
+    }
+};
+
+// Adds to A the gradients of the neighbour site of edge e from the staged samples [s0, s1) of a chunk
+// (the per-sample formulas of foam.cu:303-343 with the sample's items); returns the site.
+template <int S4>
+__device__ __forceinline__ int scatter_range(const GraphView& g, const FieldView& F, int e, const float4* st, int s0,
+                                             int s1, PairAcc<S4>& A) {
+    const float4 E = __ldg(g.edge + e);
+    const int j = site_of(E);
+    if (s0 >= s1) return j;
+    const float4* fr = F.rec + kFieldVec * static_cast<int64_t>(j);
+    const float4 r0_ = __ldg(fr), r1_ = __ldg(fr + 1), r2_ = __ldg(fr + 2), r3_ = __ldg(fr + 3);
+    float4 coef[S4];
+#pragma unroll
+    for (int q = 0; q < S4; ++q) coef[q] = __ldg(F.sh + static_cast<int64_t>(S4) * j + q);
+    for (int i = s0; i < s1; ++i) {
+        const float4* q = st + kItemVec * i;
+        const float4 q0 = q[0];
+        const float v0 = q0.x - E.x, v1 = q0.y - E.y, v2 = q0.z - E.z;
+        const float gs = q0.w;
+        if (gs != 0.f) {
+            const float gc = gs * __expf(r1_.z - 0.5f * maha(r0_, r1_, v0, v1, v2));
+            if (fabsf(gc) > 1e-12f) {
+                const float gm = -0.5f * gc;
+                A.ad[0] += gc, A.ad[1] += gm * v0 * v0, A.ad[2] += 2.f * gm * v0 * v1, A.ad[3] += 2.f * gm * v0 * v2;
+                A.ad[4] += gm * v1 * v1, A.ad[5] += 2.f * gm * v1 * v2, A.ad[6] += gm * v2 * v2;
+            }
+        }
+        const float4 q1 = q[1], q2 = q[2];
+        if (q2.y > 0.f) {  // the sample has a colour gradient
+            const float a = __expf(-0.5f * (maha(r2_, r3_, v0, v1, v2) - q2.x)) * q2.y;
+            if (a >= kMinWeight) {
+                float b[16];
+                const float4 b0 = q[3], b1 = q[4], b2 = q[5], b3 = q[6];
+                b[0] = b0.x, b[1] = b0.y, b[2] = b0.z, b[3] = b0.w, b[4] = b1.x, b[5] = b1.y, b[6] = b1.z;
+                b[7] = b1.w, b[8] = b2.x, b[9] = b2.y, b[10] = b2.z, b[11] = b2.w, b[12] = b3.x;
+                b[13] = b3.y, b[14] = b3.z, b[15] = b3.w;
+                float c[3] = {0.5f, 0.5f, 0.5f};
+#pragma unroll
+                for (int qq = 0; qq < S4; ++qq) {
+                    const float f[4] = {coef[qq].x, coef[qq].y, coef[qq].z, coef[qq].w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int k = 4 * qq + u;
+                        if (k < 48) c[k % 3] += b[k / 3] * f[u];
+                    }
+                }
+                const float dc[3] = {c[0] > 0.f ? a * q1.x : 0.f, c[1] > 0.f ? a * q1.y : 0.f,
+                                     c[2] > 0.f ? a * q1.z : 0.f};
+#pragma unroll
+                for (int k = 0; k < 4 * S4; ++k)
+                    if (k < 48) A.ash[k] += b[k / 3] * dc[k % 3];
+                const float ga = q1.x * fmaxf(c[0], 0.f) + q1.y * fmaxf(c[1], 0.f) + q1.z * fmaxf(c[2], 0.f);
+                const float gm = -0.5f * a * (ga - q1.w);
+                A.ac[0] += gm * v0 * v0, A.ac[1] += 2.f * gm * v0 * v1, A.ac[2] += 2.f * gm * v0 * v2;
+                A.ac[3] += gm * v1 * v1, A.ac[4] += 2.f * gm * v1 * v2, A.ac[5] += gm * v2 * v2;
+            }
+        }
+    }
+    return j;
+}
+
+// The (neighbour, sample) pairs of a chunk of a cell with n < 32 neighbour sites (self included) spread
+// over the 32 lanes so that every lane does about n cnt / 32 of them, in at most two phases whose
+// boundaries all lanes cross together:
+//   n <= 16  R = 32 / n replicas of every neighbour, replica r taking the r-th of R slices of the samples;
+//   n > 16   phase 1: lane l < n takes neighbour l, and the m = 32 - n spare lanes each take the second
+//            half of the samples of neighbours 0..m-1, whose owners take the first half; the owners of
+//            neighbours m..n-1 take ceil(cnt / 2) samples. Phase 2: the remaining floor(cnt / 2) samples
+//            of those q = n - m neighbours, split among U = 32 / q lanes each.
+// Lanes holding sums of the same neighbour combine them with warp shuffles, then one lane per neighbour
+// adds them to the gradient pack. Same sums as one lane per neighbour, in another order.
+template <int S4>
+__device__ __forceinline__ void balanced_scatter(const GraphView& g, const FieldView& F, const float4* st, int e0,
+                                                 int n, int cnt, int lane, float* __restrict__ grad) {
+    PairAcc<S4> A;
+    A.zero();
+    if (n <= 16) {
+        const int R = 32 / n;
+        const int j = lane % n, r = lane / n;
+        int site = 0;
+        if (r < R) site = scatter_range<S4>(g, F, e0 + j, st, (r * cnt) / R, ((r + 1) * cnt) / R, A);
+        for (int u = 1; u < R; ++u) A.pull(min(lane + u * n, 31), lane < n);
+        if (lane < n) A.flush(grad, site);
+        return;
+    }
+    const int m = 32 - n, h = cnt / 2, T1 = cnt - h;
+    int site;
+    if (lane < n)
+        site = scatter_range<S4>(g, F, e0 + lane, st, 0, lane < m ? h : T1, A);
+    else
+        site = scatter_range<S4>(g, F, e0 + lane - n, st, h, cnt, A);
+    A.pull(min(lane + n, 31), lane < m);
+    if (lane < n) A.flush(grad, site);
+    if (h == 0) return;
+    const int q = n - m, U = 32 / q;
+    const int j = m + lane % q, u = lane / q;
+    A.zero();
+    if (u < U) site = scatter_range<S4>(g, F, e0 + j, st, T1 + (u * h) / U, T1 + ((u + 1) * h) / U, A);
+    for (int w = 1; w < U; ++w) A.pull(min(lane + w * q, 31), lane < q);
+    if (lane < q) A.flush(grad, site);
+}
+
 template <int S4>
 __global__ void __launch_bounds__(kBlock, 3)
     cm_scatter_kernel(GraphView g, FieldView F, RayView R, const float* __restrict__ rec, int K,
@@ -532,74 +688,14 @@ __global__ void __launch_bounds__(kBlock, 3)
         }
         __syncwarp();
         const int e0 = __ldg(g.off + cell), e1 = __ldg(g.off + cell + 1);
-        for (int e = e0 + lane; e < e1; e += 32) {  // one neighbour site per lane
-            const float4 E = __ldg(g.edge + e);
-            const int j = site_of(E);
-            const float4* fr = F.rec + kFieldVec * static_cast<int64_t>(j);
-            const float4 r0_ = __ldg(fr), r1_ = __ldg(fr + 1), r2_ = __ldg(fr + 2), r3_ = __ldg(fr + 3);
-            float4 coef[S4];
-#pragma unroll
-            for (int q = 0; q < S4; ++q) coef[q] = __ldg(F.sh + static_cast<int64_t>(S4) * j + q);
-            float ad[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // g_raw, g_dA[6], -
-            float ac[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};              // g_cA[6]
-            float ash[4 * S4];                                          // g_sh
-#pragma unroll
-            for (int u = 0; u < 4 * S4; ++u) ash[u] = 0.f;
-            for (int i = 0; i < cnt; ++i) {
-                const float4* q = st + kItemVec * i;
-                const float4 q0 = q[0];
-                const float v0 = q0.x - E.x, v1 = q0.y - E.y, v2 = q0.z - E.z;
-                const float gs = q0.w;
-                if (gs != 0.f) {
-                    const float gc = gs * __expf(r1_.z - 0.5f * maha(r0_, r1_, v0, v1, v2));
-                    if (fabsf(gc) > 1e-12f) {
-                        const float gm = -0.5f * gc;
-                        ad[0] += gc, ad[1] += gm * v0 * v0, ad[2] += 2.f * gm * v0 * v1, ad[3] += 2.f * gm * v0 * v2;
-                        ad[4] += gm * v1 * v1, ad[5] += 2.f * gm * v1 * v2, ad[6] += gm * v2 * v2;
-                    }
-                }
-                const float4 q1 = q[1], q2 = q[2];
-                if (q2.y > 0.f) {  // the sample has a colour gradient
-                    const float a = __expf(-0.5f * (maha(r2_, r3_, v0, v1, v2) - q2.x)) * q2.y;
-                    if (a >= kMinWeight) {
-                        float b[16];
-                        const float4 b0 = q[3], b1 = q[4], b2 = q[5], b3 = q[6];
-                        b[0] = b0.x, b[1] = b0.y, b[2] = b0.z, b[3] = b0.w, b[4] = b1.x, b[5] = b1.y, b[6] = b1.z;
-                        b[7] = b1.w, b[8] = b2.x, b[9] = b2.y, b[10] = b2.z, b[11] = b2.w, b[12] = b3.x;
-                        b[13] = b3.y, b[14] = b3.z, b[15] = b3.w;
-                        float c[3] = {0.5f, 0.5f, 0.5f};
-#pragma unroll
-                        for (int qq = 0; qq < S4; ++qq) {
-                            const float f[4] = {coef[qq].x, coef[qq].y, coef[qq].z, coef[qq].w};
-#pragma unroll
-                            for (int u = 0; u < 4; ++u) {
-                                const int k = 4 * qq + u;
-                                if (k < 48) c[k % 3] += b[k / 3] * f[u];
-                            }
-                        }
-                        const float dc[3] = {c[0] > 0.f ? a * q1.x : 0.f, c[1] > 0.f ? a * q1.y : 0.f,
-                                             c[2] > 0.f ? a * q1.z : 0.f};
-#pragma unroll
-                        for (int k = 0; k < 4 * S4; ++k)
-                            if (k < 48) ash[k] += b[k / 3] * dc[k % 3];
-                        const float ga = q1.x * fmaxf(c[0], 0.f) + q1.y * fmaxf(c[1], 0.f) + q1.z * fmaxf(c[2], 0.f);
-                        const float gm = -0.5f * a * (ga - q1.w);
-                        ac[0] += gm * v0 * v0, ac[1] += 2.f * gm * v0 * v1, ac[2] += 2.f * gm * v0 * v2;
-                        ac[3] += gm * v1 * v1, ac[4] += 2.f * gm * v1 * v2, ac[5] += gm * v2 * v2;
-                    }
-                }
-            }
-            float* G = grad + kGradStride * static_cast<int64_t>(j);
-            const float4 d0 = make_float4(ad[0], ad[1], ad[2], ad[3]), d1 = make_float4(ad[4], ad[5], ad[6], 0.f);
-            const float4 c0 = make_float4(ac[0], ac[1], ac[2], ac[3]), c1 = make_float4(ac[4], ac[5], 0.f, 0.f);
-            if (nonzero(d0)) red4(G, d0);
-            if (nonzero(d1)) red4(G + 4, d1);
-            if (nonzero(c0)) red4(G + 8, c0);
-            if (nonzero(c1)) red4(G + 12, c1);
-#pragma unroll
-            for (int qq = 0; qq < S4; ++qq) {
-                const float4 v = make_float4(ash[4 * qq], ash[4 * qq + 1], ash[4 * qq + 2], ash[4 * qq + 3]);
-                if (nonzero(v)) red4(G + 16 + 4 * qq, v);
+        if (VG_BWD_BALANCE && e1 - e0 < 32) {
+            balanced_scatter<S4>(g, F, st, e0, e1 - e0, cnt, lane, grad);
+        } else {
+            for (int e = e0 + lane; e < e1; e += 32) {  // one neighbour site per lane
+                PairAcc<S4> A;
+                A.zero();
+                const int j = scatter_range<S4>(g, F, e, st, 0, cnt, A);
+                A.flush(grad, j);
             }
         }
         __syncwarp();
