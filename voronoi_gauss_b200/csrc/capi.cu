@@ -399,7 +399,7 @@ int vg_density_forward(const void* pack, int64_t n_sites, int64_t n_adj, const f
     if (status == nullptr) return fail(VG_ERR_CUDA, "status word unavailable");
     const vg::GraphView g = vg::graph_view(pack, n_sites, n_adj);
     const cudaError_t e = vg::density_field(g, raw, log_scale, quat, x, site, n_samples,
-                                            static_cast<float>(1.0 / (scale_mult * scale_mult)), nullptr, sigma,
+                                            static_cast<float>(1.0 / (scale_mult * scale_mult)), false, nullptr, sigma,
                                             nullptr, nullptr, nullptr, workspace, status,
                                             static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_density_forward");
@@ -418,7 +418,7 @@ int vg_density_backward(const void* pack, int64_t n_sites, int64_t n_adj, const 
     int* status = status_ptr();
     if (status == nullptr) return fail(VG_ERR_CUDA, "status word unavailable");
     const vg::GraphView g = vg::graph_view(pack, n_sites, n_adj);
-    const cudaError_t e = vg::density_field(g, raw, log_scale, quat, x, site, n_samples, 1.f, grad_sigma, nullptr,
+    const cudaError_t e = vg::density_field(g, raw, log_scale, quat, x, site, n_samples, 1.f, true, grad_sigma, nullptr,
                                             g_raw, g_ls, g_quat, workspace, status, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_density_backward");
 }
@@ -435,7 +435,7 @@ int vg_color_forward(const void* pack, int64_t n_sites, int64_t n_adj, const flo
     int* status = status_ptr();
     if (status == nullptr) return fail(VG_ERR_CUDA, "status word unavailable");
     const vg::GraphView g = vg::graph_view(pack, n_sites, n_adj);
-    const cudaError_t e = vg::color_field(g, log_scale, quat, sh, sh_deg, x, dirs, site, n_samples, nullptr, nullptr,
+    const cudaError_t e = vg::color_field(g, log_scale, quat, sh, sh_deg, x, dirs, site, n_samples, false, nullptr, nullptr,
                                           rgb, nullptr, nullptr, nullptr, workspace, status,
                                           static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_color_forward");
@@ -455,7 +455,7 @@ int vg_color_backward(const void* pack, int64_t n_sites, int64_t n_adj, const fl
     int* status = status_ptr();
     if (status == nullptr) return fail(VG_ERR_CUDA, "status word unavailable");
     const vg::GraphView g = vg::graph_view(pack, n_sites, n_adj);
-    const cudaError_t e = vg::color_field(g, log_scale, quat, sh, sh_deg, x, dirs, site, n_samples, rgb, grad_rgb,
+    const cudaError_t e = vg::color_field(g, log_scale, quat, sh, sh_deg, x, dirs, site, n_samples, true, rgb, grad_rgb,
                                           nullptr, g_ls, g_quat, g_sh, workspace, status,
                                           static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_color_backward");

@@ -344,9 +344,8 @@ cudaError_t sampler_walk(const GraphView& g, const float* o, const float* d, con
 }
 
 cudaError_t density_field(const GraphView& g, const float* raw, const float* ls, const float* quat, const float* x,
-                          const int* site, int64_t m, float inv_mult2, const float* g_sigma, float* sigma,
+                          const int* site, int64_t m, float inv_mult2, bool backward, const float* g_sigma, float* sigma,
                           float* g_raw, float* g_ls, float* g_quat, void* ws, int* status, cudaStream_t st) {
-    const bool backward = g_sigma != nullptr;
     const FieldLayout L = field_layout(g.n, 0, backward ? 1 : 0);
     char* b = static_cast<char*>(ws);
     float4* gauss = reinterpret_cast<float4*>(b + L.gauss);
@@ -368,10 +367,9 @@ cudaError_t density_field(const GraphView& g, const float* raw, const float* ls,
 }
 
 cudaError_t color_field(const GraphView& g, const float* ls, const float* quat, const float* sh, int sh_deg,
-                        const float* x, const float* dirs, const int* site, int64_t m, const float* rgb_in,
+                        const float* x, const float* dirs, const int* site, int64_t m, bool backward, const float* rgb_in,
                         const float* g_rgb, float* rgb, float* g_ls, float* g_quat, float* g_sh, void* ws, int* status,
                         cudaStream_t st) {
-    const bool backward = g_rgb != nullptr;
     const FieldLayout L = field_layout(g.n, sh_deg, backward ? 3 : 2);
     char* b = static_cast<char*>(ws);
     float4* gauss = reinterpret_cast<float4*>(b + L.gauss);

@@ -300,16 +300,15 @@ cudaError_t conic_backward(const float* log_scale, const float* quat, int64_t n,
                            float* g_ls, float* g_quat, cudaStream_t st);
 
 // field.cu: the NeRF-sampler field kernels. kind: 0 density forward, 1 density backward, 2 colour
-// forward, 3 colour backward. inv_mult2 = 1 / scale_mult^2 (forward only; the backward uses 1). A
-// backward call is selected by a non-null g_sigma / g_rgb.
+// forward, 3 colour backward. inv_mult2 = 1 / scale_mult^2 (forward only; the backward uses 1).
 size_t field_workspace(int64_t n_sites, int sh_deg, int kind);
 cudaError_t sampler_walk(const GraphView& g, const float* o, const float* d, const float* z, const int* start,
                          int64_t n_rays, int n_samples, int* site, int* steps, int* status, cudaStream_t st);
 cudaError_t density_field(const GraphView& g, const float* raw, const float* ls, const float* quat, const float* x,
-                          const int* site, int64_t m, float inv_mult2, const float* g_sigma, float* sigma,
+                          const int* site, int64_t m, float inv_mult2, bool backward, const float* g_sigma, float* sigma,
                           float* g_raw, float* g_ls, float* g_quat, void* ws, int* status, cudaStream_t st);
 cudaError_t color_field(const GraphView& g, const float* ls, const float* quat, const float* sh, int sh_deg,
-                        const float* x, const float* dirs, const int* site, int64_t m, const float* rgb_in,
+                        const float* x, const float* dirs, const int* site, int64_t m, bool backward, const float* rgb_in,
                         const float* g_rgb, float* rgb, float* g_ls, float* g_quat, float* g_sh, void* ws, int* status,
                         cudaStream_t st);
 
