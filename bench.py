@@ -297,7 +297,7 @@ def run_b200(args):
     rays_total = B * world
     value = rays_total / (ms * 1e-3) / 1e6
     peak, peak_kind = measured_peak()
-    dom = 'foam_backward_kernel' if bwd_ms >= fwd_ms else 'foam_forward_kernel'
+    dom = 'foam_backward' if bwd_ms >= fwd_ms else 'foam_forward'
     dom_ms, dom_bytes = (bwd_ms, bwd_bytes) if bwd_ms >= fwd_ms else (fwd_ms, fwd_bytes)
     achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
     line = {
@@ -312,7 +312,8 @@ def run_b200(args):
                    'l2': 'inputs larger than L2 (scene records + adjacency ~1 GB read every step)'},
         'fps': round(1000.0 / ms, 3), 'fwd_ms': round(fwd_ms, 3), 'bwd_ms': round(bwd_ms, 3),
         'fwd_mrays_s': round(B / (fwd_ms * 1e-3) / 1e6, 3), 'samples_per_ray': round(samples_per_ray, 2),
-        'roofline': {'bound': 'hbm', 'kernel': dom, 'achieved': round(achieved, 1), 'peak': peak, 'unit': 'GB/s',
+        'roofline': {'bound': 'hbm', 'kernel': f'{dom} (one vg_{dom} call: all its kernels)',
+                     'achieved': round(achieved, 1), 'peak': peak, 'unit': 'GB/s',
                      'frac': round(achieved / peak, 4), 'traffic': None, 'peak_kind': peak_kind,
                      'algorithmic_bytes_per_launch': {'forward': fwd_bytes, 'backward': bwd_bytes},
                      'n_bar': round(n_bar, 3),
@@ -324,11 +325,15 @@ def run_b200(args):
         'clocks': clocks,
     }
     traffic = os.path.join(ROOT, 'profiles', 'traffic.json')
-    if os.path.exists(traffic):
+    if os.path.exists(traffic) and W * H == 1920 * 1080 and args.config == 3 and args.sites is None:
         with open(traffic) as f:
             tr = json.load(f)
         if dom in tr:
-            line['roofline']['traffic'] = tr[dom]['bytes_per_launch_full']
+            t_bytes = float(tr[dom]['dram_bytes_per_call'])
+            line['roofline']['traffic'] = t_bytes
+            line['roofline']['dram_gbs'] = round(t_bytes / (dom_ms * 1e-3) / 1e9, 1)
+            line['roofline']['dram_frac'] = round(t_bytes / (dom_ms * 1e-3) / 1e9 / peak, 4)
+            line['roofline']['traffic_source'] = tr['source']
     if rank == 0 and world == 1 and not args.no_baselines:
         line['cpu_baseline'] = cpu_baseline(gr, model, o_h, d_h, start_site, args)
         line['ref_cuda'] = ref_cuda_baseline(model, o, d, start, target, args)

@@ -228,6 +228,9 @@ __global__ void __launch_bounds__(kBlock)
                      const int* __restrict__ order, const int4* __restrict__ chunks, const int* __restrict__ n_chunks_ptr,
                      int64_t r0) {
     constexpr int kPer = kChunk / 32;  // samples per lane
+    constexpr int kNv = 3 + S4;        // float4 per staged neighbour: edge, colour conic (2), SH rows
+    __shared__ float4 nbr_smem[(kBlock / 32) * 32 * kNv];
+    float4* nbr = nbr_smem + (threadIdx.x >> 5) * 32 * kNv;
     const int lane = threadIdx.x & 31;
     const int n_chunks = *n_chunks_ptr;
     const int warps = gridDim.x * (kBlock / 32);
@@ -257,29 +260,43 @@ __global__ void __launch_bounds__(kBlock)
             }
         }
         const int e0 = __ldg(g.off + C.x), e1 = __ldg(g.off + C.x + 1);
-        for (int e = e0; e < e1; ++e) {  // warp-uniform: one cell per chunk
-            const float4 E = __ldg(g.edge + e);
-            const int j = site_of(E);
-            const float4* fr = F.rec + kFieldVec * static_cast<int64_t>(j);
-            const float4 r2 = __ldg(fr + 2), r3 = __ldg(fr + 3);
-            float4 coef[S4];
-            const float4* sp = F.sh + static_cast<int64_t>(S4) * j;
+        // the cell's neighbour data, up to 32 neighbours at a time, staged in shared memory by one lane
+        // each (all loads in flight together), then read back as warp-wide broadcasts
+        for (int eb = e0; eb < e1; eb += 32) {
+            const int nb = min(32, e1 - eb);
+            __syncwarp();
+            if (lane < nb) {
+                const float4 E = __ldg(g.edge + eb + lane);
+                const int j = site_of(E);
+                const float4* fr = F.rec + kFieldVec * static_cast<int64_t>(j);
+                const float4* sp = F.sh + static_cast<int64_t>(S4) * j;
+                float4* dst = nbr + lane * kNv;
+                dst[0] = E, dst[1] = __ldg(fr + 2), dst[2] = __ldg(fr + 3);
 #pragma unroll
-            for (int q = 0; q < S4; ++q) coef[q] = __ldg(sp + q);
+                for (int q = 0; q < S4; ++q) dst[3 + q] = __ldg(sp + q);
+            }
+            __syncwarp();
+            for (int k = 0; k < nb; ++k) {  // warp-uniform: one cell per chunk
+                const float4* src = nbr + k * kNv;
+                const float4 E = src[0], r2 = src[1], r3 = src[2];
+                float4 coef[S4];
 #pragma unroll
-            for (int p = 0; p < kPer; ++p) {
-                const float v0 = x[p][0] - E.x, v1 = x[p][1] - E.y, v2 = x[p][2] - E.z;
-                float c[3] = {0.5f, 0.5f, 0.5f};
+                for (int q = 0; q < S4; ++q) coef[q] = src[3 + q];
 #pragma unroll
-                for (int q = 0; q < S4; ++q) {
-                    const float f[4] = {coef[q].x, coef[q].y, coef[q].z, coef[q].w};
+                for (int p = 0; p < kPer; ++p) {
+                    const float v0 = x[p][0] - E.x, v1 = x[p][1] - E.y, v2 = x[p][2] - E.z;
+                    float c[3] = {0.5f, 0.5f, 0.5f};
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int i = 4 * q + u;
-                        if (i < 48) c[i % 3] += b[p][i / 3] * f[u];
+                    for (int q = 0; q < S4; ++q) {
+                        const float f[4] = {coef[q].x, coef[q].y, coef[q].z, coef[q].w};
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int i = 4 * q + u;
+                            if (i < 48) c[i % 3] += b[p][i / 3] * f[u];
+                        }
                     }
+                    blend_add(B[p], maha(r2, r3, v0, v1, v2), fmaxf(c[0], 0.f), fmaxf(c[1], 0.f), fmaxf(c[2], 0.f));
                 }
-                blend_add(B[p], maha(r2, r3, v0, v1, v2), fmaxf(c[0], 0.f), fmaxf(c[1], 0.f), fmaxf(c[2], 0.f));
             }
         }
 #pragma unroll
