@@ -60,6 +60,12 @@
 #ifndef VG_BWD_BALANCE
 #define VG_BWD_BALANCE 1
 #endif
+// VG_BWD_DIRECT      1: the replay writes 64-byte items (position, gradients, direction) straight into
+//                    their cell's bucket (counted beforehand), so the scatter reads them in order;
+//                    0: 32-byte items in ray order, bucketed through an index array
+#ifndef VG_BWD_DIRECT
+#define VG_BWD_DIRECT 1
+#endif
 
 namespace vg {
 namespace {
@@ -186,10 +192,10 @@ __global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
 // the cell's order with the same arithmetic as eval_color, so the colours are bit-identical to the
 // inline path; cmf_composite_kernel then sums the segments of every ray from its records.
 
-// Samples of a ray chunk that need a colour, counted per cell.
+// Samples of a ray chunk counted per cell: those that need a colour (colour_only), or all of them.
 __global__ void __launch_bounds__(kBlock)
     cmf_count_kernel(const float* __restrict__ rec, const int* __restrict__ stats, const int* __restrict__ inv,
-                     int64_t r0, int64_t n, int K, int* __restrict__ count) {
+                     int64_t r0, int64_t n, int K, int* __restrict__ count, bool colour_only) {
     const int64_t rl = static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
     if (rl >= n) return;
     const int64_t r = r0 + rl;
@@ -197,7 +203,7 @@ __global__ void __launch_bounds__(kBlock)
     if (S > K) return;
     for (int s = 0; s < S; ++s) {
         const float4 q1 = __ldg(reinterpret_cast<const float4*>(rec + (r * K + s) * kRecord) + 1);
-        if (q1.w < 0.f) {
+        if (!colour_only || q1.w < 0.f) {
             const int site = __float_as_int(__ldg(rec + (r * K + s) * kRecord + 1));
             atomicAdd(count + __ldg(inv + site), 1);
         }
@@ -341,6 +347,22 @@ __global__ void __launch_bounds__(kBlock)
 // Per-sample record of the cell-major backward: the sample's gradient scalars, written by the replay
 // (one slot per recorded sample, indexed ray * K + sample) and consumed by cm_scatter_kernel.
 //   (gs, gC r, gC g, gC b) | (gC . C, m_min, 1 / sum of colour weights or 0, bits(cell) or -1)
+// Direct form (VG_BWD_DIRECT): 64 bytes at the sample's place in its cell's bucket,
+//   (x, gs) | (gC, gC . C) | (m_min, 1 / sum of colour weights or 0, 0, 0) | (d, 0)
+// where every recorded sample gets an item (zero gradients for the samples that have none).
+__device__ __forceinline__ void emit_item_direct(float4* __restrict__ items, const int* __restrict__ offsets,
+                                                 int* __restrict__ fill, const Sample& P, float gs, float gC0,
+                                                 float gC1, float gC2, bool has_c, const float (&d)[3]) {
+    const bool do_c = has_c && (gC0 != 0.f || gC1 != 0.f || gC2 != 0.f);
+    const int64_t pos = __ldg(offsets + P.cell) + atomicAdd(fill + P.cell, 1);
+    float4* it = items + 4 * pos;
+    const float gCC = do_c ? gC0 * P.C0 + gC1 * P.C1 + gC2 * P.C2 : 0.f;
+    it[0] = make_float4(P.x0, P.x1, P.x2, gs);
+    it[1] = make_float4(do_c ? gC0 : 0.f, do_c ? gC1 : 0.f, do_c ? gC2 : 0.f, gCC);
+    it[2] = make_float4(P.mmin, do_c ? P.inv_a : 0.f, 0.f, 0.f);
+    it[3] = make_float4(d[0], d[1], d[2], 0.f);
+}
+
 __device__ __forceinline__ void emit_item(float4* __restrict__ items, int64_t slot, const Sample& P, float gs,
                                           float gC0, float gC1, float gC2, bool has_c, int* __restrict__ count) {
     const bool do_c = has_c && (gC0 != 0.f || gC1 != 0.f || gC2 != 0.f);
@@ -361,10 +383,12 @@ __device__ __forceinline__ void emit_item(float4* __restrict__ items, int64_t sl
 enum BwdMode { kScatterAll = 0, kScatterRetraced = 1, kItems = 2 };
 
 struct ItemOut {
-    float4* items;  // (rays of the chunk) x K x 2 float4
-    int* count;     // (N + 1) samples per cell
-    int64_t r0;     // first ray of the chunk
-    int64_t n;      // rays in the chunk
+    float4* items;         // (rays of the chunk) x K x 2 float4, or the bucketed direct items
+    int* count;            // (N + 1) samples per cell
+    int64_t r0;            // first ray of the chunk
+    int64_t n;             // rays in the chunk
+    const int* offsets;    // direct items: first bucket position of every cell
+    int* fill;             // direct items: bucket fill cursors
 };
 
 template <int MODE>
@@ -443,7 +467,10 @@ __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
         g_sbar = delta * (g_sbar - gT_final);
         const float h0 = active ? 0.5f * w * gR0 : 0.f, h1 = active ? 0.5f * w * gR1 : 0.f,
                     h2 = active ? 0.5f * w * gR2 : 0.f;
-        if (MODE == kItems)
+        if (MODE == kItems && VG_BWD_DIRECT)
+            emit_item_direct(io.items, io.offsets, io.fill, P, gs_pending + 0.5f * g_sbar, gP0 + h0, gP1 + h1,
+                             gP2 + h2, has_p, d);
+        else if (MODE == kItems)
             emit_item(io.items, (r - io.r0) * K + it, P, gs_pending + 0.5f * g_sbar, gP0 + h0, gP1 + h1, gP2 + h2,
                       has_p, io.count);
         else if (kAgg)
@@ -460,8 +487,19 @@ __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
         n_done = it + 1;
         if (last || T < c.t_thresh) break;
     }
-    if (MODE == kItems)
+    if (MODE == kItems && VG_BWD_DIRECT) {
+        emit_item_direct(io.items, io.offsets, io.fill, P, gs_pending, gP0, gP1, gP2, has_p, d);
+        // every recorded sample was counted into its bucket: fill the places of any the replay did not
+        // reach with zero-gradient items (the replay follows the forward, so normally there are none)
+        for (int s = n_done + 1; s < n_stored; ++s) {
+            Sample Z;
+            bool has_z;
+            load_sample(gi.rec, r, K, s, o, d, g.inv, Z, has_z);
+            emit_item_direct(io.items, io.offsets, io.fill, Z, 0.f, 0.f, 0.f, 0.f, false, d);
+        }
+    } else if (MODE == kItems) {
         emit_item(io.items, (r - io.r0) * K + n_done, P, gs_pending, gP0, gP1, gP2, has_p, io.count);
+    }
     else if (kAgg)
         scatter_sample_agg(g, F, P, gs_pending, gP0, gP1, gP2, has_p, b, cache, grad, stage, lane);
     else
@@ -682,7 +720,19 @@ __global__ void __launch_bounds__(kBlock, 3)
     for (int ch = blockIdx.x * (kBlock / 32) + (threadIdx.x >> 5); ch < n_chunks; ch += warps) {
         const int4 C = __ldg(chunks + ch);
         const int cell = C.x, cnt = C.z;
-        for (int li = lane; li < cnt; li += 32) {  // stage the chunk's samples
+        for (int li = lane; li < cnt && VG_BWD_DIRECT; li += 32) {  // stage the chunk's bucketed items
+            const float4* it = items + 4 * (static_cast<int64_t>(C.y) + li);
+            const float4 i3 = __ldg(it + 3);
+            float b[16];
+            sh_basis(i3.x, i3.y, i3.z, F.sh_deg, b);
+            float4* q = st + kItemVec * li;
+            q[0] = __ldg(it), q[1] = __ldg(it + 1), q[2] = __ldg(it + 2);
+            q[3] = make_float4(b[0], b[1], b[2], b[3]);
+            q[4] = make_float4(b[4], b[5], b[6], b[7]);
+            q[5] = make_float4(b[8], b[9], b[10], b[11]);
+            q[6] = make_float4(b[12], b[13], b[14], b[15]);
+        }
+        for (int li = lane; li < cnt && !VG_BWD_DIRECT; li += 32) {  // stage the chunk's samples
             const int slot = __ldg(order + C.y + li);
             const int64_t r = r0 + slot / K;
             const int sidx = slot % K;
@@ -748,7 +798,7 @@ CmLayout cm_layout(int64_t n_sites, int64_t n_rays, int K, bool with_items) {
         at += al256(b);
         return h;
     };
-    L.items = take(with_items ? 32 * slots : 0);
+    L.items = take(with_items ? (VG_BWD_DIRECT ? 64 : 32) * slots : 0);
     L.order = take(4 * slots);
     L.count = take(4 * (n_sites + 1));
     L.fill = take(4 * n_sites);
@@ -816,7 +866,7 @@ cudaError_t forward_deferred(const GraphView& g, const FieldView& F, const RayVi
         if (e == cudaSuccess) e = cudaMemsetAsync(fill, 0, 4 * static_cast<size_t>(n), st);
         if (e == cudaSuccess) e = cudaMemsetAsync(counter, 0, 16, st);
         if (e != cudaSuccess) return e;
-        cmf_count_kernel<<<blocks(nr), kBlock, 0, st>>>(out.rec, out.stats, g.inv, r0, nr, K, count);
+        cmf_count_kernel<<<blocks(nr), kBlock, 0, st>>>(out.rec, out.stats, g.inv, r0, nr, K, count, true);
         size_t tb = L.temp_bytes;
         e = cub::DeviceScan::ExclusiveSum(b + L.temp, tb, count, offsets, n + 1, st);
         if (e != cudaSuccess) return e;
@@ -875,7 +925,7 @@ cudaError_t foam_backward(const GraphView& g, const FieldView& F, const RayView&
     if (R.n == 0) return cudaSuccess;
     const int K = gi.record_cap;
     const CmLayout L = cm_layout(g.n, R.n, K, true);
-    const ItemOut none{nullptr, nullptr, 0, 0};
+    const ItemOut none{nullptr, nullptr, 0, 0, nullptr, nullptr};
     if (!VG_BWD_CELL_MAJOR || gi.rec == nullptr || K <= 0 || cm_ws == nullptr || cm_bytes < L.total ||
         L.total == 0) {
         foam_backward_kernel<kScatterAll><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, gi, grad, none, status);
@@ -899,12 +949,19 @@ cudaError_t foam_backward(const GraphView& g, const FieldView& F, const RayView&
         if (e == cudaSuccess) e = cudaMemsetAsync(fill, 0, 4 * static_cast<size_t>(n), st);
         if (e == cudaSuccess) e = cudaMemsetAsync(counter, 0, 16, st);
         if (e != cudaSuccess) return e;
-        const ItemOut io{items, count, r0, nr};
-        foam_backward_kernel<kItems><<<blocks(nr), kBlock, 0, st>>>(g, F, R, c, gi, grad, io, status);
+        const ItemOut io{items, count, r0, nr, offsets, fill};
         size_t tb = L.temp_bytes;
-        e = cub::DeviceScan::ExclusiveSum(b + L.temp, tb, count, offsets, n + 1, st);
-        if (e != cudaSuccess) return e;
-        cm_bucket_kernel<<<blocks(nr), kBlock, 0, st>>>(items, gi.stats, r0, nr, K, offsets, fill, order);
+        if (VG_BWD_DIRECT) {
+            cmf_count_kernel<<<blocks(nr), kBlock, 0, st>>>(gi.rec, gi.stats, g.inv, r0, nr, K, count, false);
+            e = cub::DeviceScan::ExclusiveSum(b + L.temp, tb, count, offsets, n + 1, st);
+            if (e != cudaSuccess) return e;
+            foam_backward_kernel<kItems><<<blocks(nr), kBlock, 0, st>>>(g, F, R, c, gi, grad, io, status);
+        } else {
+            foam_backward_kernel<kItems><<<blocks(nr), kBlock, 0, st>>>(g, F, R, c, gi, grad, io, status);
+            e = cub::DeviceScan::ExclusiveSum(b + L.temp, tb, count, offsets, n + 1, st);
+            if (e != cudaSuccess) return e;
+            cm_bucket_kernel<<<blocks(nr), kBlock, 0, st>>>(items, gi.stats, r0, nr, K, offsets, fill, order);
+        }
         cm_chunks_kernel<<<blocks(n), kBlock, 0, st>>>(offsets, n, chunks, counter);
         switch (F.s4) {
             case 1: cm_scatter_kernel<1><<<grid, kBlock, 0, st>>>(g, F, R, gi.rec, K, items, order, chunks, counter, r0,
