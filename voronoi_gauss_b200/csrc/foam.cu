@@ -66,6 +66,11 @@
 #ifndef VG_BWD_DIRECT
 #define VG_BWD_DIRECT 1
 #endif
+// VG_BWD_ASYNC       1 (with VG_BWD_DIRECT): cm_scatter_kernel copies the next chunk's items into shared
+//                    memory asynchronously (cp.async) while it scatters the current one
+#ifndef VG_BWD_ASYNC
+#define VG_BWD_ASYNC 1
+#endif
 
 namespace vg {
 namespace {
@@ -557,6 +562,14 @@ __global__ void __launch_bounds__(kBlock)
 // Shared-memory image of one staged sample: x, gs | gC, gC.C | m_min, 1/sum a, -, - | SH basis (16).
 constexpr int kItemVec = 7;
 
+// 16-byte asynchronous copy global -> shared (sm_80+ cp.async, L2 only), its group commit and wait.
+__device__ __forceinline__ void cp_async16(float4* smem, const float4* gmem) {
+    const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+
 // Gradient sums of one neighbour site over a range of a chunk's samples.
 template <int S4>
 struct PairAcc {
@@ -712,11 +725,61 @@ __global__ void __launch_bounds__(kBlock, 3)
     cm_scatter_kernel(GraphView g, FieldView F, RayView R, const float* __restrict__ rec, int K,
                       const float4* __restrict__ items, const int* __restrict__ order, const int4* __restrict__ chunks,
                       const int* __restrict__ n_chunks_ptr, int64_t r0, float* __restrict__ grad) {
+    constexpr bool kAsync = VG_BWD_DIRECT && VG_BWD_ASYNC;
     __shared__ float4 smem[(kBlock / 32) * kChunk * kItemVec];
+    __shared__ float4 raw_smem[kAsync ? (kBlock / 32) * kChunk * 4 : 1];
     const int lane = threadIdx.x & 31;
     float4* st = smem + (threadIdx.x >> 5) * kChunk * kItemVec;
     const int n_chunks = *n_chunks_ptr;
     const int warps = gridDim.x * (kBlock / 32);
+    if (kAsync) {
+        // items of chunk i+1 are copied while chunk i is scattered: wait for the copy, expand the items
+        // (SH basis of the direction) into the staging area, start the next copy, then scatter
+        float4* raw = raw_smem + (threadIdx.x >> 5) * kChunk * 4;
+        int ch = blockIdx.x * (kBlock / 32) + (threadIdx.x >> 5);
+        int4 C = make_int4(0, 0, 0, 0);
+        if (ch < n_chunks) {
+            C = __ldg(chunks + ch);
+            for (int k = lane; k < 4 * C.z; k += 32) cp_async16(raw + k, items + 4 * static_cast<int64_t>(C.y) + k);
+            cp_async_commit();
+        }
+        for (; ch < n_chunks; ch += warps) {
+            cp_async_wait_all();
+            __syncwarp();
+            for (int li = lane; li < C.z; li += 32) {
+                const float4 i3 = raw[4 * li + 3];
+                float b[16];
+                sh_basis(i3.x, i3.y, i3.z, F.sh_deg, b);
+                float4* q = st + kItemVec * li;
+                q[0] = raw[4 * li], q[1] = raw[4 * li + 1], q[2] = raw[4 * li + 2];
+                q[3] = make_float4(b[0], b[1], b[2], b[3]);
+                q[4] = make_float4(b[4], b[5], b[6], b[7]);
+                q[5] = make_float4(b[8], b[9], b[10], b[11]);
+                q[6] = make_float4(b[12], b[13], b[14], b[15]);
+            }
+            __syncwarp();
+            const int4 Cur = C;
+            if (ch + warps < n_chunks) {
+                C = __ldg(chunks + ch + warps);
+                for (int k = lane; k < 4 * C.z; k += 32)
+                    cp_async16(raw + k, items + 4 * static_cast<int64_t>(C.y) + k);
+                cp_async_commit();
+            }
+            const int e0 = __ldg(g.off + Cur.x), e1 = __ldg(g.off + Cur.x + 1);
+            if (VG_BWD_BALANCE && e1 - e0 < 32) {
+                balanced_scatter<S4>(g, F, st, e0, e1 - e0, Cur.z, lane, grad);
+            } else {
+                for (int e = e0 + lane; e < e1; e += 32) {
+                    PairAcc<S4> A;
+                    A.zero();
+                    const int j = scatter_range<S4>(g, F, e, st, 0, Cur.z, A);
+                    A.flush(grad, j);
+                }
+            }
+            __syncwarp();
+        }
+        return;
+    }
     for (int ch = blockIdx.x * (kBlock / 32) + (threadIdx.x >> 5); ch < n_chunks; ch += warps) {
         const int4 C = __ldg(chunks + ch);
         const int cell = C.x, cnt = C.z;
