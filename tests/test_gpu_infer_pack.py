@@ -45,7 +45,8 @@ def test_device_pack_matches_torch_checker_and_reference(foam_small, model, tag,
         assert np.array_equal(pk[key].cpu().numpy(), z[f'pack_{tag}_{key}']), key
     e, ze = pk['edge'].cpu().numpy(), z[f'pack_{tag}_edge']
     assert np.array_equal(e[:, :3], ze[:, :3])
-    h, zh = e[:, 3].view(np.uint16).astype(np.int32), ze[:, 3].view(np.uint16).astype(np.int32)
+    h = np.ascontiguousarray(e[:, 3]).view(np.uint16).astype(np.int32)
+    zh = np.ascontiguousarray(ze[:, 3]).view(np.uint16).astype(np.int32)
     assert np.abs(h - zh).max() <= 1  # fp16 cuts: libm vs CUDA expf may differ by one unit before rounding
 
 

@@ -58,7 +58,7 @@
 //                    for cells with fewer than 32 neighbours (replicas / two phases, see balanced_scatter);
 //                    0: one lane per neighbour
 #ifndef VG_BWD_BALANCE
-#define VG_BWD_BALANCE 1
+#define VG_BWD_BALANCE 0
 #endif
 // VG_BWD_DIRECT      1: the replay writes 64-byte items (position, gradients, direction) straight into
 //                    their cell's bucket (counted beforehand), so the scatter reads them in order;
@@ -70,6 +70,11 @@
 //                    memory asynchronously (cp.async) while it scatters the current one
 #ifndef VG_BWD_ASYNC
 #define VG_BWD_ASYNC 1
+#endif
+// VG_FWD_COUNT       1: the deferred traversal counts the samples that need a colour per (pass, cell) as
+//                    it stores them (no counting pass over the records); 0: cmf_count_kernel per pass
+#ifndef VG_FWD_COUNT
+#define VG_FWD_COUNT 1
 #endif
 
 namespace vg {
@@ -128,6 +133,14 @@ __global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
     if (r >= R.n) return;
     const int K = c.record_cap;
     if (MODE == kImmediateOverflow && __ldg(out.stats + 3 * r) <= K) return;
+    if (MODE == kImmediateOverflow && c.cm_count != nullptr) {
+        // the deferred traversal counted this ray's marked records; it leaves the colour pass
+        int* cnt = c.cm_count + (r / c.cm_rays) * c.cm_stride;
+        for (int s = 0; s < K; ++s) {
+            const float* q = out.rec + (r * K + s) * kRecord;
+            if (q[7] < 0.f) atomicAdd(cnt + __ldg(g.inv + __float_as_int(q[1])), -1);
+        }
+    }
     constexpr bool kDefer = MODE == kDeferred;
     ColorCache<kFwdSlots> cache{cache_mem + threadIdx.x, kBlock};
     cache.init();
@@ -174,6 +187,8 @@ __global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
         }
         T *= 1.f - alpha;
         if (RECORD) store_sample(out.rec, r, K, n_samples - 2, P, has_p, kDefer, g.perm);
+        if (kDefer && has_p && n_samples - 2 < K && c.cm_count != nullptr)
+            atomicAdd(c.cm_count + (r / c.cm_rays) * c.cm_stride + P.cell, 1);
         P = Q;
         has_p = has_q;
         t_exit = t_exit_q, next = next_q;
@@ -181,6 +196,8 @@ __global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
     }
     if (it == kMaxCells) err |= kErrCellCap;
     if (RECORD) store_sample(out.rec, r, K, n_samples - 1, P, has_p, kDefer, g.perm);
+    if (kDefer && has_p && n_samples - 1 < K && c.cm_count != nullptr)
+        atomicAdd(c.cm_count + (r / c.cm_rays) * c.cm_stride + P.cell, 1);
     if (!kDefer) out.rgb[3 * r] = acc0, out.rgb[3 * r + 1] = acc1, out.rgb[3 * r + 2] = acc2;
     out.T[r] = T;
     out.depth[r] = dep;
@@ -863,7 +880,8 @@ CmLayout cm_layout(int64_t n_sites, int64_t n_rays, int K, bool with_items) {
     };
     L.items = take(with_items ? (VG_BWD_DIRECT ? 64 : 32) * slots : 0);
     L.order = take(4 * slots);
-    L.count = take(4 * (n_sites + 1));
+    const int64_t passes = (n_rays + L.rays_per_pass - 1) / L.rays_per_pass;
+    L.count = take(4 * (n_sites + 1) * (with_items || !VG_FWD_COUNT ? 1 : passes));
     L.fill = take(4 * n_sites);
     L.offsets = take(4 * (n_sites + 1));
     L.chunks = take(16 * (slots / 32 + n_sites + 1));
@@ -913,10 +931,17 @@ namespace {
 cudaError_t forward_deferred(const GraphView& g, const FieldView& F, const RayView& R, const FoamCfg& c,
                              const Outputs& out, int* status, const CmLayout& L, char* b, cudaStream_t st) {
     const int K = c.record_cap;
-    foam_forward_kernel<true, kDeferred><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, out, status);
-    foam_forward_kernel<true, kImmediateOverflow><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, out, status);
+    int* count_all = reinterpret_cast<int*>(b + L.count);
+    FoamCfg cc = c;
+    if (VG_FWD_COUNT) {
+        const int64_t passes = (R.n + L.rays_per_pass - 1) / L.rays_per_pass;
+        const cudaError_t e = cudaMemsetAsync(count_all, 0, 4 * static_cast<size_t>(g.n + 1) * passes, st);
+        if (e != cudaSuccess) return e;
+        cc.cm_count = count_all, cc.cm_rays = L.rays_per_pass, cc.cm_stride = g.n + 1;
+    }
+    foam_forward_kernel<true, kDeferred><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, cc, out, status);
+    foam_forward_kernel<true, kImmediateOverflow><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, cc, out, status);
     int* order = reinterpret_cast<int*>(b + L.order);
-    int* count = reinterpret_cast<int*>(b + L.count);
     int* fill = reinterpret_cast<int*>(b + L.fill);
     int* offsets = reinterpret_cast<int*>(b + L.offsets);
     int4* chunks = reinterpret_cast<int4*>(b + L.chunks);
@@ -925,11 +950,14 @@ cudaError_t forward_deferred(const GraphView& g, const FieldView& F, const RayVi
     const int grid = sm_count() * 8;
     for (int64_t r0 = 0; r0 < R.n; r0 += L.rays_per_pass) {
         const int64_t nr = std::min<int64_t>(L.rays_per_pass, R.n - r0);
-        cudaError_t e = cudaMemsetAsync(count, 0, 4 * static_cast<size_t>(n + 1), st);
+        int* count = VG_FWD_COUNT ? count_all + (r0 / L.rays_per_pass) * static_cast<int64_t>(n + 1) : count_all;
+        cudaError_t e = cudaSuccess;
+        if (!VG_FWD_COUNT) e = cudaMemsetAsync(count, 0, 4 * static_cast<size_t>(n + 1), st);
         if (e == cudaSuccess) e = cudaMemsetAsync(fill, 0, 4 * static_cast<size_t>(n), st);
         if (e == cudaSuccess) e = cudaMemsetAsync(counter, 0, 16, st);
         if (e != cudaSuccess) return e;
-        cmf_count_kernel<<<blocks(nr), kBlock, 0, st>>>(out.rec, out.stats, g.inv, r0, nr, K, count, true);
+        if (!VG_FWD_COUNT)
+            cmf_count_kernel<<<blocks(nr), kBlock, 0, st>>>(out.rec, out.stats, g.inv, r0, nr, K, count, true);
         size_t tb = L.temp_bytes;
         e = cub::DeviceScan::ExclusiveSum(b + L.temp, tb, count, offsets, n + 1, st);
         if (e != cudaSuccess) return e;

@@ -235,6 +235,11 @@ struct RayView {
 struct FoamCfg {
     float t_thresh, w_thresh;
     int record_cap;
+    // set by foam_forward for the deferred traversal: per-pass counts of the samples that need a
+    // colour, cm_count[(ray / cm_rays) * cm_stride + cell] (null: not counted)
+    int* cm_count = nullptr;
+    int64_t cm_rays = 1;
+    int cm_stride = 0;
 };
 
 struct MarchCfg {
