@@ -65,8 +65,9 @@ int vg_graph_pack(const float* points, const int32_t* offsets, const int32_t* ad
 /* ------------------------------------------------------------------------- interaction points */
 
 /* Workspace of vg_foam_forward / vg_march_forward (backward = 0), of vg_foam_backward /
- * vg_march_backward (backward = 1) or of vg_foam_backward_packed (backward = 2), for n_sites sites at
- * SH degree sh_deg, n_rays rays and records of capacity record_cap (0 for march). */
+ * vg_march_backward (backward = 1), of vg_foam_backward_packed (backward = 2), or of vg_march_backward
+ * with its cell-major gradient scatter (backward = 3: more memory, faster), for n_sites sites at SH
+ * degree sh_deg, n_rays rays and records of capacity record_cap (0 for march). */
 size_t vg_foam_workspace_bytes(int64_t n_sites, int sh_deg, int64_t n_rays, int record_cap, int backward);
 
 /* foam_forward (foam.cu:505-526): rendering at the ray / Voronoi-face interaction points.
@@ -132,7 +133,9 @@ int vg_march_forward(const void* pack, int64_t n_sites, int64_t n_adj, const flo
                      float dt, int n_bg, float t_thresh, float w_thresh, float* rgb, float* T, float* depth,
                      int32_t* stats, void* workspace, size_t workspace_bytes, void* stream);
 
-/* march_backward (march.cu:405-429): re-marches every ray; gradients overwritten. */
+/* march_backward (march.cu:405-429): re-marches every ray; gradients overwritten. Given the larger
+ * workspace of vg_foam_workspace_bytes(..., backward = 3), the samples' gradients are bucketed by cell
+ * and scattered cell-major; with the backward = 1 size, per sample. */
 int vg_march_backward(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA,
                       const float* cA, const float* sh, int sh_deg, const float* o, const float* d,
                       const int32_t* start, const float* near, const float* mid, const float* far, int64_t n_rays,

@@ -153,6 +153,7 @@ int vg_graph_pack(const float* points, const int32_t* offsets, const int32_t* ad
 size_t vg_foam_workspace_bytes(int64_t n_sites, int sh_deg, int64_t n_rays, int record_cap, int backward) {
     if (n_sites <= 0 || sh_deg < 0 || sh_deg > 3 || n_rays < 0 || record_cap < 0) return 0;
     if (backward == 0) return field_ws(n_sites, sh_deg) + align256(vg::foam_forward_workspace(n_sites, n_rays, record_cap));
+    if (backward == 3) return field_ws(n_sites, sh_deg) + grad_ws(n_sites) + align256(vg::march_backward_workspace(n_sites, n_rays));
     const size_t cm = align256(vg::foam_backward_workspace(n_sites, n_rays, record_cap));
     return field_ws(n_sites, sh_deg) + (backward == 1 ? grad_ws(n_sites) : 0) + cm;
 }
@@ -329,6 +330,8 @@ int vg_march_backward(const void* pack, int64_t n_sites, int64_t n_adj, const fl
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     const vg::GraphView g = vg::graph_view(pack, n_sites, n_adj);
     float* grad = reinterpret_cast<float*>(static_cast<char*>(workspace) + field_ws(n_sites, sh_deg));
+    char* cm_ws = static_cast<char*>(workspace) + need;  // cell-major scratch when the caller gave more
+    const size_t cm_bytes = workspace_bytes - need;
     cudaError_t e = cudaMemsetAsync(grad, 0, static_cast<size_t>(n_sites) * vg::kGradStride * sizeof(float), st);
     if (e != cudaSuccess) return cuda_fail(e, "zero gradients");
     if (n_rays > 0) {
@@ -338,7 +341,7 @@ int vg_march_backward(const void* pack, int64_t n_sites, int64_t n_adj, const fl
         const vg::RayView R{o, d, start, near, mid, far, n_rays};
         const vg::MarchCfg c{dt, n_bg, t_thresh, w_thresh};
         const vg::GradIn gi{rgb, T, g_rgb, g_T, nullptr, nullptr, 0};
-        e = vg::march_backward(g, F, R, c, gi, grad, status, st);
+        e = vg::march_backward(g, F, R, c, gi, grad, status, cm_bytes > 0 ? cm_ws : nullptr, cm_bytes, st);
         if (e != cudaSuccess) return cuda_fail(e, "vg_march_backward");
     }
     e = vg::grad_unpack(g, grad, sh_deg, g_raw, g_dA, g_cA, g_sh, st);

@@ -76,6 +76,12 @@
 #ifndef VG_FWD_COUNT
 #define VG_FWD_COUNT 1
 #endif
+// VG_FWD_REFILL      1: the deferred traversal runs as a persistent grid whose lanes take the next ray
+//                    from a global counter as soon as theirs ends (no lane idles while the longest ray
+//                    of its warp finishes); 0: one ray per thread
+#ifndef VG_FWD_REFILL
+#define VG_FWD_REFILL 1
+#endif
 
 namespace vg {
 namespace {
@@ -203,6 +209,86 @@ __global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
     out.depth[r] = dep;
     out.stats[3 * r] = n_samples, out.stats[3 * r + 1] = n_color, out.stats[3 * r + 2] = walk_steps;
     if (err) atomicOr(status, err);
+}
+
+// The deferred traversal (foam_forward_kernel<true, kDeferred>) with lane refill: every lane runs the
+// same per-ray steps, one cell per loop trip, and a lane whose ray has ended takes the next unclaimed ray
+// (one atomic per warp and refill). Outputs are those of the one-ray-per-thread kernel, bit for bit.
+__global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
+    foam_deferred_refill_kernel(GraphView g, FieldView F, RayView R, FoamCfg c, Outputs out, int* status,
+                                unsigned long long* next_ray) {
+    const int lane = threadIdx.x & 31;
+    const int K = c.record_cap;
+    ColorCache<0> cache{nullptr, 0};
+    const float b[16] = {};  // no colours in the traversal
+    int64_t r = 0;
+    float o[3] = {0.f, 0.f, 0.f}, d[3] = {0.f, 0.f, 0.f}, near = 0.f, far = 0.f;
+    Sample P{};
+    float t_exit = kInf, T = 1.f, dep = 0.f;
+    int next = -1, err = 0, walk_steps = 0, n_samples = 1, n_color = 0, it = 0;
+    bool has_p = false, active = false, exhausted = false;
+    int* cnt = nullptr;
+    for (;;) {
+        const unsigned need = __ballot_sync(0xffffffffu, !active && !exhausted);
+        if (need) {
+            const int leader = __ffs(need) - 1;
+            unsigned long long base = 0;
+            if (lane == leader) base = atomicAdd(next_ray, static_cast<unsigned long long>(__popc(need)));
+            base = __shfl_sync(0xffffffffu, base, leader);
+            if (!active && !exhausted) {
+                const int64_t mine = static_cast<int64_t>(base) + __popc(need & ((1u << lane) - 1u));
+                if (mine < R.n) {
+                    r = mine;
+                    active = true;
+                    load_ray(R, r, o, d, near, far);
+                    err = 0, walk_steps = 0, n_samples = 1, n_color = 0, it = 0;
+                    const int cur = walk_to(g, __ldg(g.inv + __ldg(R.start + r)), along(o[0], near, d[0]),
+                                            along(o[1], near, d[1]), along(o[2], near, d[2]), walk_steps, err);
+                    eval_sample<0, false>(g, F, cur, near, o, d, b, cache, true, P, t_exit, next);
+                    has_p = false, T = 1.f, dep = 0.f;
+                    cnt = c.cm_count != nullptr ? c.cm_count + (r / c.cm_rays) * c.cm_stride : nullptr;
+                } else {
+                    exhausted = true;
+                }
+            }
+        }
+        if (__ballot_sync(0xffffffffu, active) == 0) break;
+        if (!active) continue;
+        const bool last = next < 0 || t_exit >= far;
+        Sample Q;
+        float t_exit_q;
+        int next_q;
+        eval_sample<0, false>(g, F, last ? P.cell : next, last ? far : fmaxf(t_exit, P.t), o, d, b, cache, !last, Q,
+                              t_exit_q, next_q);
+        bool has_q = false;
+        ++n_samples;
+        const float delta = Q.t - P.t;
+        const float alpha = 1.f - __expf(-0.5f * (P.sigma + Q.sigma) * delta);
+        const float w = T * alpha;
+        if (w > c.w_thresh) {
+            has_p = has_q = true;
+            dep += w * 0.5f * (P.t + Q.t);
+            ++n_color;
+        }
+        T *= 1.f - alpha;
+        store_sample(out.rec, r, K, n_samples - 2, P, has_p, true, g.perm);
+        if (has_p && n_samples - 2 < K && cnt != nullptr) atomicAdd(cnt + P.cell, 1);
+        P = Q;
+        has_p = has_q;
+        t_exit = t_exit_q, next = next_q;
+        ++it;
+        const bool capped = it == kMaxCells;
+        if (last || T < c.t_thresh || capped) {
+            if (capped && !(last || T < c.t_thresh)) err |= kErrCellCap;
+            store_sample(out.rec, r, K, n_samples - 1, P, has_p, true, g.perm);
+            if (has_p && n_samples - 1 < K && cnt != nullptr) atomicAdd(cnt + P.cell, 1);
+            out.T[r] = T;
+            out.depth[r] = dep;
+            out.stats[3 * r] = n_samples, out.stats[3 * r + 1] = n_color, out.stats[3 * r + 2] = walk_steps;
+            if (err) atomicOr(status, err);
+            active = false;
+        }
+    }
 }
 
 // ------------------------------------------------------------------- cell-major colours (forward)
@@ -737,12 +823,17 @@ __device__ __forceinline__ void balanced_scatter(const GraphView& g, const Field
     if (lane < q) A.flush(grad, site);
 }
 
-template <int S4>
+// Where cm_scatter_kernel finds a chunk's samples: 64-byte items stored contiguously per cell (kBucketed),
+// 64-byte items reached through the cell-sorted index array (kIndexed), or 32-byte items through the
+// index array plus the sample's t in the records and its ray (kRecords).
+enum StageMode { kBucketed = 0, kIndexed = 1, kRecords = 2 };
+
+template <int S4, int STAGE>
 __global__ void __launch_bounds__(kBlock, 3)
     cm_scatter_kernel(GraphView g, FieldView F, RayView R, const float* __restrict__ rec, int K,
                       const float4* __restrict__ items, const int* __restrict__ order, const int4* __restrict__ chunks,
                       const int* __restrict__ n_chunks_ptr, int64_t r0, float* __restrict__ grad) {
-    constexpr bool kAsync = VG_BWD_DIRECT && VG_BWD_ASYNC;
+    constexpr bool kAsync = STAGE == kBucketed && VG_BWD_ASYNC;
     __shared__ float4 smem[(kBlock / 32) * kChunk * kItemVec];
     __shared__ float4 raw_smem[kAsync ? (kBlock / 32) * kChunk * 4 : 1];
     const int lane = threadIdx.x & 31;
@@ -800,8 +891,9 @@ __global__ void __launch_bounds__(kBlock, 3)
     for (int ch = blockIdx.x * (kBlock / 32) + (threadIdx.x >> 5); ch < n_chunks; ch += warps) {
         const int4 C = __ldg(chunks + ch);
         const int cell = C.x, cnt = C.z;
-        for (int li = lane; li < cnt && VG_BWD_DIRECT; li += 32) {  // stage the chunk's bucketed items
-            const float4* it = items + 4 * (static_cast<int64_t>(C.y) + li);
+        for (int li = lane; li < cnt && STAGE != kRecords; li += 32) {  // stage the chunk's 64-byte items
+            const int64_t at = STAGE == kIndexed ? __ldg(order + C.y + li) : static_cast<int64_t>(C.y) + li;
+            const float4* it = items + 4 * at;
             const float4 i3 = __ldg(it + 3);
             float b[16];
             sh_basis(i3.x, i3.y, i3.z, F.sh_deg, b);
@@ -812,7 +904,7 @@ __global__ void __launch_bounds__(kBlock, 3)
             q[5] = make_float4(b[8], b[9], b[10], b[11]);
             q[6] = make_float4(b[12], b[13], b[14], b[15]);
         }
-        for (int li = lane; li < cnt && !VG_BWD_DIRECT; li += 32) {  // stage the chunk's samples
+        for (int li = lane; li < cnt && STAGE == kRecords; li += 32) {  // stage the chunk's samples
             const int slot = __ldg(order + C.y + li);
             const int64_t r = r0 + slot / K;
             const int sidx = slot % K;
@@ -849,25 +941,105 @@ __global__ void __launch_bounds__(kBlock, 3)
     }
 }
 
+// ------------------------------------------------------------ cell-major backward of the march path
+//
+// The march backward (march.cu) re-marches every ray; instead of scattering each sample's gradients
+// per lane, march_items_kernel writes the first kMarchCap samples of a ray as 64-byte items (the direct
+// item layout, with the sample's cell in the third vector) at slot (ray, sample) and counts them per
+// cell; march_bucket_kernel sorts the slots by cell and cm_scatter_kernel<kIndexed> scatters them.
+// Samples beyond kMarchCap are scattered per lane, as before.
+
+__global__ void __launch_bounds__(kBlock)
+    march_items_kernel(GraphView g, FieldView F, RayView R, MarchCfg c, GradIn gi, float* __restrict__ grad,
+                       float4* __restrict__ items, int* __restrict__ n_items, int* __restrict__ count, int64_t r0,
+                       int64_t nr, int cap, int* status) {
+    const int64_t rl = static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
+    if (rl >= nr) return;
+    const int64_t r = r0 + rl;
+    ColorCache<0> cache{nullptr, 0};
+    MRay M;
+    load_mray(R, c, r, M);
+    float b[16];
+    sh_basis(M.d[0], M.d[1], M.d[2], F.sh_deg, b);
+    const float gR0 = __ldg(gi.g_rgb + 3 * r), gR1 = __ldg(gi.g_rgb + 3 * r + 1), gR2 = __ldg(gi.g_rgb + 3 * r + 2);
+    const float fg0 = __ldg(gi.rgb + 3 * r), fg1 = __ldg(gi.rgb + 3 * r + 1), fg2 = __ldg(gi.rgb + 3 * r + 2);
+    const float gT_final = __ldg(gi.g_T + r) * __ldg(gi.T + r);
+    int err = 0, cur = __ldg(g.inv + __ldg(R.start + r)), walk_steps = 0, k = 0;
+    float T = 1.f, acc0 = 0.f, acc1 = 0.f, acc2 = 0.f;
+    for (; k < M.n_total; ++k) {
+        float t, delta;
+        march_sample_at(M, c, k, t, delta);
+        Sample S;
+        S.t = t;
+        S.x0 = along(M.o[0], t, M.d[0]), S.x1 = along(M.o[1], t, M.d[1]), S.x2 = along(M.o[2], t, M.d[2]);
+        cur = walk_to(g, cur, S.x0, S.x1, S.x2, walk_steps, err);
+        S.cell = cur;
+        const float alpha = 1.f - __expf(-eval_density(g, F, cur, S.x0, S.x1, S.x2) * delta);
+        const float w = T * alpha;
+        const float T_next = T * (1.f - alpha);
+        const bool active = w > c.w_thresh;
+        S.C0 = S.C1 = S.C2 = 0.f, S.mmin = 0.f, S.inv_a = 0.f;
+        if (active) {
+            eval_color(g, F, b, cache, S);
+            acc0 += w * S.C0, acc1 += w * S.C1, acc2 += w * S.C2;
+        }
+        float gsig = gR0 * (T_next * S.C0 - (fg0 - acc0)) + gR1 * (T_next * S.C1 - (fg1 - acc1)) +
+                     gR2 * (T_next * S.C2 - (fg2 - acc2));
+        gsig = delta * (gsig - gT_final);
+        const float gC0 = active ? w * gR0 : 0.f, gC1 = active ? w * gR1 : 0.f, gC2 = active ? w * gR2 : 0.f;
+        if (k < cap) {
+            const bool do_c = active && (gC0 != 0.f || gC1 != 0.f || gC2 != 0.f);
+            float4* it = items + 4 * (rl * cap + k);
+            it[0] = make_float4(S.x0, S.x1, S.x2, gsig);
+            it[1] = make_float4(do_c ? gC0 : 0.f, do_c ? gC1 : 0.f, do_c ? gC2 : 0.f,
+                                do_c ? gC0 * S.C0 + gC1 * S.C1 + gC2 * S.C2 : 0.f);
+            it[2] = make_float4(S.mmin, do_c ? S.inv_a : 0.f, __int_as_float(cur), 0.f);
+            it[3] = make_float4(M.d[0], M.d[1], M.d[2], 0.f);
+            atomicAdd(count + cur, 1);
+        } else {
+            scatter_sample(g, F, S, gsig, gC0, gC1, gC2, active, b, cache, grad);
+        }
+        T = T_next;
+        if (T < c.t_thresh) {
+            ++k;
+            break;
+        }
+    }
+    n_items[rl] = min(k, cap);
+    if (err) atomicOr(status, err);
+}
+
+// Counting sort of the march items by cell (one thread per item slot).
+__global__ void __launch_bounds__(kBlock)
+    march_bucket_kernel(const float4* __restrict__ items, const int* __restrict__ n_items, int64_t nr, int cap,
+                        const int* __restrict__ offsets, int* __restrict__ fill, int* __restrict__ order) {
+    const int64_t slot = static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
+    if (slot >= nr * cap) return;
+    if (static_cast<int>(slot % cap) >= __ldg(n_items + slot / cap)) return;
+    const int cell = __float_as_int(__ldg(items + 4 * slot + 2).z);
+    order[__ldg(offsets + cell) + atomicAdd(fill + cell, 1)] = static_cast<int>(slot);
+}
+
 inline int blocks(int64_t n) { return static_cast<int>((n + kBlock - 1) / kBlock); }
 
 }  // namespace
 
 namespace {
 
-constexpr int64_t kCmItems = int64_t(1) << 26;  // samples bucketed at once (2 GB of items)
+constexpr int64_t kCmItems = int64_t(1) << 26;  // samples bucketed at once (2-4 GB of items)
+constexpr int kMarchCap = 256;                    // march samples per ray taken cell-major
 
 inline size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct CmLayout {
-    size_t items, order, count, fill, offsets, chunks, counter, temp, temp_bytes, total;
+    size_t items, n_items, order, count, fill, offsets, chunks, counter, ray_counter, temp, temp_bytes, total;
     int64_t rays_per_pass;
 };
 
 // Scratch of the cell-major passes over rays [r0, r0 + rays_per_pass): per-sample items (backward
 // only), the cell-sorted order, per-cell counts / fill cursors / offsets, the chunk list, a counter and
 // the CUB scan storage.
-CmLayout cm_layout(int64_t n_sites, int64_t n_rays, int K, bool with_items) {
+CmLayout cm_layout(int64_t n_sites, int64_t n_rays, int K, bool with_items, int item_bytes = VG_BWD_DIRECT ? 64 : 32) {
     CmLayout L{};
     if (K <= 0 || n_rays <= 0) return L;
     L.rays_per_pass = std::max<int64_t>(1, std::min<int64_t>(n_rays, kCmItems / K));
@@ -878,7 +1050,8 @@ CmLayout cm_layout(int64_t n_sites, int64_t n_rays, int K, bool with_items) {
         at += al256(b);
         return h;
     };
-    L.items = take(with_items ? (VG_BWD_DIRECT ? 64 : 32) * slots : 0);
+    L.items = take(with_items ? static_cast<size_t>(item_bytes) * slots : 0);
+    L.n_items = take(with_items ? 4 * L.rays_per_pass : 0);
     L.order = take(4 * slots);
     const int64_t passes = (n_rays + L.rays_per_pass - 1) / L.rays_per_pass;
     L.count = take(4 * (n_sites + 1) * (with_items || !VG_FWD_COUNT ? 1 : passes));
@@ -886,6 +1059,7 @@ CmLayout cm_layout(int64_t n_sites, int64_t n_rays, int K, bool with_items) {
     L.offsets = take(4 * (n_sites + 1));
     L.chunks = take(16 * (slots / 32 + n_sites + 1));
     L.counter = take(16);
+    L.ray_counter = take(16);
     size_t scan = 0;
     cub::DeviceScan::ExclusiveSum(nullptr, scan, static_cast<const int*>(nullptr), static_cast<int*>(nullptr),
                                   static_cast<int>(n_sites + 1));
@@ -910,6 +1084,54 @@ int sm_count() {
 
 size_t foam_backward_workspace(int64_t n_sites, int64_t n_rays, int record_cap) {
     return cm_layout(n_sites, n_rays, record_cap, true).total;
+}
+
+size_t march_backward_workspace(int64_t n_sites, int64_t n_rays) {
+    return cm_layout(n_sites, n_rays, kMarchCap, true, 64).total;
+}
+
+cudaError_t march_backward_cm(const GraphView& g, const FieldView& F, const RayView& R, const MarchCfg& c,
+                              const GradIn& gi, float* grad, int* status, void* cm_ws, cudaStream_t st) {
+    const CmLayout L = cm_layout(g.n, R.n, kMarchCap, true, 64);
+    char* b = static_cast<char*>(cm_ws);
+    float4* items = reinterpret_cast<float4*>(b + L.items);
+    int* n_items = reinterpret_cast<int*>(b + L.n_items);
+    int* order = reinterpret_cast<int*>(b + L.order);
+    int* count = reinterpret_cast<int*>(b + L.count);
+    int* fill = reinterpret_cast<int*>(b + L.fill);
+    int* offsets = reinterpret_cast<int*>(b + L.offsets);
+    int4* chunks = reinterpret_cast<int4*>(b + L.chunks);
+    int* counter = reinterpret_cast<int*>(b + L.counter);
+    const int n = g.n;
+    const int grid = sm_count() * 3;
+    for (int64_t r0 = 0; r0 < R.n; r0 += L.rays_per_pass) {
+        const int64_t nr = std::min<int64_t>(L.rays_per_pass, R.n - r0);
+        cudaError_t e = cudaMemsetAsync(count, 0, 4 * static_cast<size_t>(n + 1), st);
+        if (e == cudaSuccess) e = cudaMemsetAsync(fill, 0, 4 * static_cast<size_t>(n), st);
+        if (e == cudaSuccess) e = cudaMemsetAsync(counter, 0, 16, st);
+        if (e != cudaSuccess) return e;
+        march_items_kernel<<<blocks(nr), kBlock, 0, st>>>(g, F, R, c, gi, grad, items, n_items, count, r0, nr,
+                                                          kMarchCap, status);
+        size_t tb = L.temp_bytes;
+        e = cub::DeviceScan::ExclusiveSum(b + L.temp, tb, count, offsets, n + 1, st);
+        if (e != cudaSuccess) return e;
+        march_bucket_kernel<<<blocks(nr * kMarchCap), kBlock, 0, st>>>(items, n_items, nr, kMarchCap, offsets, fill,
+                                                                        order);
+        cm_chunks_kernel<<<blocks(n), kBlock, 0, st>>>(offsets, n, chunks, counter);
+        switch (F.s4) {
+            case 1: cm_scatter_kernel<1, kIndexed><<<grid, kBlock, 0, st>>>(g, F, R, nullptr, 0, items, order, chunks,
+                                                                            counter, r0, grad); break;
+            case 3: cm_scatter_kernel<3, kIndexed><<<grid, kBlock, 0, st>>>(g, F, R, nullptr, 0, items, order, chunks,
+                                                                            counter, r0, grad); break;
+            case 7: cm_scatter_kernel<7, kIndexed><<<grid, kBlock, 0, st>>>(g, F, R, nullptr, 0, items, order, chunks,
+                                                                            counter, r0, grad); break;
+            default: cm_scatter_kernel<12, kIndexed><<<grid, kBlock, 0, st>>>(g, F, R, nullptr, 0, items, order,
+                                                                              chunks, counter, r0, grad); break;
+        }
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 // Records kept per ray when the caller keeps none (record_cap 0): the no-record forward still defers
@@ -939,7 +1161,15 @@ cudaError_t forward_deferred(const GraphView& g, const FieldView& F, const RayVi
         if (e != cudaSuccess) return e;
         cc.cm_count = count_all, cc.cm_rays = L.rays_per_pass, cc.cm_stride = g.n + 1;
     }
-    foam_forward_kernel<true, kDeferred><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, cc, out, status);
+    if (VG_FWD_REFILL) {
+        auto* next_ray = reinterpret_cast<unsigned long long*>(b + L.ray_counter);
+        const cudaError_t e = cudaMemsetAsync(next_ray, 0, sizeof(unsigned long long), st);
+        if (e != cudaSuccess) return e;
+        const int grid = static_cast<int>(std::min<int64_t>(blocks(R.n), static_cast<int64_t>(sm_count()) * VG_FWD_MINB));
+        foam_deferred_refill_kernel<<<grid, kBlock, 0, st>>>(g, F, R, cc, out, status, next_ray);
+    } else {
+        foam_forward_kernel<true, kDeferred><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, cc, out, status);
+    }
     foam_forward_kernel<true, kImmediateOverflow><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, cc, out, status);
     int* order = reinterpret_cast<int*>(b + L.order);
     int* fill = reinterpret_cast<int*>(b + L.fill);
@@ -1034,6 +1264,7 @@ cudaError_t foam_backward(const GraphView& g, const FieldView& F, const RayView&
     int* counter = reinterpret_cast<int*>(b + L.counter);
     const int n = g.n;
     const int grid = sm_count() * 3;
+    constexpr int kStage = VG_BWD_DIRECT ? kBucketed : kRecords;
     for (int64_t r0 = 0; r0 < R.n; r0 += L.rays_per_pass) {
         const int64_t nr = std::min<int64_t>(L.rays_per_pass, R.n - r0);
         cudaError_t e = cudaMemsetAsync(count, 0, 4 * static_cast<size_t>(n + 1), st);
@@ -1055,13 +1286,13 @@ cudaError_t foam_backward(const GraphView& g, const FieldView& F, const RayView&
         }
         cm_chunks_kernel<<<blocks(n), kBlock, 0, st>>>(offsets, n, chunks, counter);
         switch (F.s4) {
-            case 1: cm_scatter_kernel<1><<<grid, kBlock, 0, st>>>(g, F, R, gi.rec, K, items, order, chunks, counter, r0,
+            case 1: cm_scatter_kernel<1, kStage><<<grid, kBlock, 0, st>>>(g, F, R, gi.rec, K, items, order, chunks, counter, r0,
                                                                   grad); break;
-            case 3: cm_scatter_kernel<3><<<grid, kBlock, 0, st>>>(g, F, R, gi.rec, K, items, order, chunks, counter, r0,
+            case 3: cm_scatter_kernel<3, kStage><<<grid, kBlock, 0, st>>>(g, F, R, gi.rec, K, items, order, chunks, counter, r0,
                                                                   grad); break;
-            case 7: cm_scatter_kernel<7><<<grid, kBlock, 0, st>>>(g, F, R, gi.rec, K, items, order, chunks, counter, r0,
+            case 7: cm_scatter_kernel<7, kStage><<<grid, kBlock, 0, st>>>(g, F, R, gi.rec, K, items, order, chunks, counter, r0,
                                                                   grad); break;
-            default: cm_scatter_kernel<12><<<grid, kBlock, 0, st>>>(g, F, R, gi.rec, K, items, order, chunks, counter,
+            default: cm_scatter_kernel<12, kStage><<<grid, kBlock, 0, st>>>(g, F, R, gi.rec, K, items, order, chunks, counter,
                                                                     r0, grad); break;
         }
         e = cudaGetLastError();

@@ -4,7 +4,8 @@
 // [mid, far] (march.cu:143-153). At every sample the thread walks greedily from the previous site to
 // the nearest one, sums the density Gaussians of its neighbourhood and, when the sample's weight
 // exceeds w_thresh, blends the colour Gaussians (march.cu:221-262). The backward pass re-marches the
-// ray with identical arithmetic and scatters gradients with 16-byte vector atomics (march.cu:264-345).
+// ray with identical arithmetic (march.cu:264-345); its samples' gradients go to the cell-major scatter
+// of foam.cu (items bucketed by cell) when the workspace allows, else per lane with 16-byte atomics.
 #include "render_core.cuh"
 
 // Colour cache slots and warp-aggregated atomics: see foam.cu.
@@ -14,6 +15,11 @@
 #ifndef VG_BWD_AGG
 #define VG_BWD_AGG 0
 #endif
+// VG_MARCH_CELL_MAJOR  1: the backward writes its samples as items scattered cell-major (foam.cu) when
+//                      the caller's workspace holds them; 0: per-lane scatter only
+#ifndef VG_MARCH_CELL_MAJOR
+#define VG_MARCH_CELL_MAJOR 1
+#endif
 
 namespace vg {
 namespace {
@@ -22,34 +28,6 @@ constexpr int kBlock = 128;
 constexpr int kSlots = VG_MARCH_SLOTS;
 constexpr int kSlotMem = kSlots > 0 ? kSlots * kBlock : 1;
 constexpr bool kAgg = VG_BWD_AGG != 0;
-
-struct MRay {
-    float o[3], d[3];
-    float near, mid, far;
-    int n_in, n_total;
-};
-
-__device__ __forceinline__ void load_mray(const RayView& R, const MarchCfg& c, int64_t r, MRay& M) {
-#pragma unroll
-    for (int a = 0; a < 3; ++a) M.o[a] = __ldg(R.o + 3 * r + a), M.d[a] = __ldg(R.d + 3 * r + a);
-    M.near = __ldg(R.near + r), M.mid = __ldg(R.mid + r), M.far = __ldg(R.far + r);
-    M.n_in = M.mid > M.near ? static_cast<int>(ceilf(__fdiv_rn(__fsub_rn(M.mid, M.near), c.dt))) : 0;
-    M.n_total = M.n_in + c.n_bg;
-}
-
-__device__ __forceinline__ void sample_at(const MRay& M, const MarchCfg& c, int k, float& t, float& delta) {
-    if (k < M.n_in) {
-        const float t0 = __fmaf_rn(static_cast<float>(k), c.dt, M.near), t1 = fminf(__fadd_rn(t0, c.dt), M.mid);
-        t = __fmul_rn(0.5f, __fadd_rn(t0, t1)), delta = __fsub_rn(t1, t0);
-    } else {
-        const float i0 = __fdiv_rn(1.f, M.mid), i1 = __fdiv_rn(1.f, M.far), di = __fsub_rn(i1, i0);
-        const float nb = static_cast<float>(c.n_bg);
-        const float u0 = __fdiv_rn(static_cast<float>(k - M.n_in), nb);
-        const float u1 = __fdiv_rn(static_cast<float>(k - M.n_in + 1), nb);
-        t = __fdiv_rn(1.f, __fmaf_rn(__fmul_rn(0.5f, __fadd_rn(u0, u1)), di, i0));
-        delta = __fsub_rn(__fdiv_rn(1.f, __fmaf_rn(u1, di, i0)), __fdiv_rn(1.f, __fmaf_rn(u0, di, i0)));
-    }
-}
 
 __global__ void __launch_bounds__(kBlock)
     march_forward_kernel(GraphView g, FieldView F, RayView R, MarchCfg c, Outputs out, int* status) {
@@ -66,7 +44,7 @@ __global__ void __launch_bounds__(kBlock)
     float T = 1.f, acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, dep = 0.f;
     for (int k = 0; k < M.n_total; ++k) {
         float t, delta;
-        sample_at(M, c, k, t, delta);
+        march_sample_at(M, c, k, t, delta);
         Sample S;
         S.t = t;
         S.x0 = along(M.o[0], t, M.d[0]), S.x1 = along(M.o[1], t, M.d[1]), S.x2 = along(M.o[2], t, M.d[2]);
@@ -113,7 +91,7 @@ __global__ void __launch_bounds__(kBlock)
     float T = 1.f, acc0 = 0.f, acc1 = 0.f, acc2 = 0.f;
     for (int k = 0; k < M.n_total; ++k) {
         float t, delta;
-        sample_at(M, c, k, t, delta);
+        march_sample_at(M, c, k, t, delta);
         Sample S;
         S.t = t;
         S.x0 = along(M.o[0], t, M.d[0]), S.x1 = along(M.o[1], t, M.d[1]), S.x2 = along(M.o[2], t, M.d[2]);
@@ -155,8 +133,10 @@ cudaError_t march_forward(const GraphView& g, const FieldView& F, const RayView&
 }
 
 cudaError_t march_backward(const GraphView& g, const FieldView& F, const RayView& R, const MarchCfg& c,
-                           const GradIn& gi, float* grad, int* status, cudaStream_t st) {
+                           const GradIn& gi, float* grad, int* status, void* cm_ws, size_t cm_bytes, cudaStream_t st) {
     if (R.n == 0) return cudaSuccess;
+    if (VG_MARCH_CELL_MAJOR && cm_ws != nullptr && cm_bytes >= march_backward_workspace(g.n, R.n))
+        return march_backward_cm(g, F, R, c, gi, grad, status, cm_ws, st);
     march_backward_kernel<<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, gi, grad, status);
     return cudaGetLastError();
 }

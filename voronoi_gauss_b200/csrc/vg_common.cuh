@@ -294,8 +294,13 @@ cudaError_t foam_backward(const GraphView& g, const FieldView& F, const RayView&
 // march.cu
 cudaError_t march_forward(const GraphView& g, const FieldView& F, const RayView& R, const MarchCfg& c,
                           const Outputs& out, int* status, cudaStream_t st);
+// The backward takes optional scratch (march_backward_workspace bytes) for the cell-major scatter.
 cudaError_t march_backward(const GraphView& g, const FieldView& F, const RayView& R, const MarchCfg& c,
-                           const GradIn& gi, float* grad, int* status, cudaStream_t st);
+                           const GradIn& gi, float* grad, int* status, void* cm_ws, size_t cm_bytes, cudaStream_t st);
+// foam.cu: the cell-major part of the march backward
+size_t march_backward_workspace(int64_t n_sites, int64_t n_rays);
+cudaError_t march_backward_cm(const GraphView& g, const FieldView& F, const RayView& R, const MarchCfg& c,
+                              const GradIn& gi, float* grad, int* status, void* cm_ws, cudaStream_t st);
 
 // conic.cu
 // floor2 = floor^2 rounded to float once (the reference passes static_cast<float>(floor * floor))

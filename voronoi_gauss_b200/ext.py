@@ -275,7 +275,7 @@ class MarchExtension:
         dev = o.device
         g_raw, g_dA, g_cA, g_sh = (torch.empty_like(x) for x in (raw, dA, cA, sh))
         pk = graph_pack(points, offsets, adj)
-        ws, nbytes = _workspace(pk.n, sh_deg, True, dev)
+        ws, nbytes = _workspace(pk.n, sh_deg, 3, dev, B)
         with torch.cuda.device(dev):
             _lib.call('vg_march_backward', pk.ptr, pk.n, pk.m, raw.data_ptr(), dA.data_ptr(), cA.data_ptr(),
                       sh.data_ptr(), sh_deg, _ptr(o), _ptr(d), _ptr(start), _ptr(near), _ptr(mid), _ptr(far), B,
