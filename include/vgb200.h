@@ -163,9 +163,11 @@ int vg_walk(const void* pack, int64_t n_sites, int64_t n_adj, const float* o, co
             const int32_t* start, int64_t n_rays, int64_t n_samples, int32_t* site, int32_t* steps,
             void* stream);
 
-/* Workspace of the field functions for n_sites sites: kind 0 vg_density_forward, 1
- * vg_density_backward, 2 vg_color_forward, 3 vg_color_backward (sh_deg used by 2 and 3). */
-size_t vg_field_workspace_bytes(int64_t n_sites, int sh_deg, int kind);
+/* Workspace of the field functions for n_sites sites and n_samples samples: kind 0
+ * vg_density_forward, 1 vg_density_backward, 2 vg_color_forward, 3 vg_color_backward (sh_deg used by 2
+ * and 3). A backward given this much buckets its samples by cell and scatters the gradients
+ * cell-major; given only the size for n_samples = 0, it scatters them per sample. */
+size_t vg_field_workspace_bytes(int64_t n_sites, int sh_deg, int kind, int64_t n_samples);
 
 /* density_forward (vgf.cu:458-475): sigma (M) = sum over the neighbourhood {i} U adj(i) of the
  * sample's site i of exp(min(raw_k, 30) - v^T A_k v / 2), A_k the conic of (log_scale, quat) widened

@@ -283,3 +283,37 @@ def test_render_rays_matches_reference_kernels(scene10k, monkeypatch):
     assert float((mine[0] - ref[0]).abs().max()) < 1e-4
     for a, b in zip(mine[1], ref[1]):
         assert rel(a.cpu().numpy(), b.cpu().numpy()) < GRAD_TOL
+
+
+def test_backward_paths_agree(fz):
+    """The per-sample scatter (workspace sized for no samples) and the cell-major scatter (workspace
+    sized for the samples, the default of ext) give the same gradients."""
+    from voronoi_gauss_b200 import _lib
+    z = fz
+    g = _graph(z)
+    pk = g.pack
+    fe = _ext().extension()
+    x, dirs, site = _f(z, 'x'), _f(z, 'dirs'), cuda(z['site'], torch.int32)
+    m = x.size(0)
+    raw, ls, q, cls, cq, sh = (_f(z, k) for k in ('raw', 'ls', 'quat', 'cls', 'cquat', 'sh'))
+    gs, grgb = _f(z, 'g_sigma'), _f(z, 'g_rgb')
+    stream = torch.cuda.current_stream().cuda_stream
+    small = _lib.lib().vg_field_workspace_bytes(pk.n, 0, 1, 0)
+    assert small < _lib.lib().vg_field_workspace_bytes(pk.n, 0, 1, m)
+    ws = torch.empty(small, dtype=torch.uint8, device='cuda')
+    per = [torch.empty_like(raw), torch.empty_like(ls), torch.empty_like(q)]
+    _lib.call('vg_density_backward', pk.ptr, pk.n, pk.m, raw.data_ptr(), ls.data_ptr(), q.data_ptr(), x.data_ptr(),
+              site.data_ptr(), m, gs.data_ptr(), *(t.data_ptr() for t in per), ws.data_ptr(), small, stream)
+    cm = fe.density_backward(g.points, g.offsets, g.adj, raw, ls, q, x, site, gs)
+    for a, b in zip(per, cm):
+        assert rel(a.cpu().numpy(), b.cpu().numpy()) < GRAD_TOL
+    rgb = fe.color_forward(g.points, g.offsets, g.adj, cls, cq, sh, 3, x, dirs, site)
+    small = _lib.lib().vg_field_workspace_bytes(pk.n, 3, 3, 0)
+    ws = torch.empty(small, dtype=torch.uint8, device='cuda')
+    per = [torch.empty_like(cls), torch.empty_like(cq), torch.empty_like(sh)]
+    _lib.call('vg_color_backward', pk.ptr, pk.n, pk.m, cls.data_ptr(), cq.data_ptr(), sh.data_ptr(), 3, x.data_ptr(),
+              dirs.data_ptr(), site.data_ptr(), m, rgb.data_ptr(), grgb.data_ptr(), *(t.data_ptr() for t in per),
+              ws.data_ptr(), small, stream)
+    cm = fe.color_backward(g.points, g.offsets, g.adj, cls, cq, sh, 3, x, dirs, site, rgb, grgb)
+    for a, b in zip(per, cm):
+        assert rel(a.cpu().numpy(), b.cpu().numpy()) < GRAD_TOL

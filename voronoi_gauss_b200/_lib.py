@@ -47,7 +47,7 @@ SIGNATURES = {
     'vg_conic_forward': (I32, [P, P, I64, F64, P, P]),
     'vg_conic_backward': (I32, [P, P, I64, F64, P, P, P, P]),
     'vg_walk': (I32, [P, I64, I64, P, P, P, P, I64, I64, P, P, P]),
-    'vg_field_workspace_bytes': (SZ, [I64, I32, I32]),
+    'vg_field_workspace_bytes': (SZ, [I64, I32, I32, I64]),
     'vg_density_forward': (I32, [P, I64, I64, P, P, P, P, P, I64, F64, P, P, SZ, P]),
     'vg_density_backward': (I32, [P, I64, I64, P, P, P, P, P, I64, P, P, P, P, P, SZ, P]),
     'vg_color_forward': (I32, [P, I64, I64, P, P, P, I32, P, P, P, I64, P, P, SZ, P]),

@@ -1,5 +1,6 @@
 // extern "C" entry points of libvgb200 (declared in include/vgb200.h): argument checks with the
 // reference's error semantics, workspace carving and dispatch to the kernels.
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -384,9 +385,10 @@ int vg_walk(const void* pack, int64_t n_sites, int64_t n_adj, const float* o, co
     return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_walk");
 }
 
-size_t vg_field_workspace_bytes(int64_t n_sites, int sh_deg, int kind) {
-    if (n_sites <= 0 || kind < 0 || kind > 3 || sh_deg < 0 || sh_deg > 3) return 0;
-    return vg::field_workspace(n_sites, sh_deg, kind);
+size_t vg_field_workspace_bytes(int64_t n_sites, int sh_deg, int kind, int64_t n_samples) {
+    if (n_sites <= 0 || kind < 0 || kind > 3 || sh_deg < 0 || sh_deg > 3 || n_samples < 0) return 0;
+    return std::max(vg::field_workspace(n_sites, sh_deg, kind),
+                    n_samples > 0 ? vg::field_cm_workspace(n_sites, sh_deg, kind, n_samples) : size_t(0));
 }
 
 int vg_density_forward(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* log_scale,
@@ -403,7 +405,7 @@ int vg_density_forward(const void* pack, int64_t n_sites, int64_t n_adj, const f
     const vg::GraphView g = vg::graph_view(pack, n_sites, n_adj);
     const cudaError_t e = vg::density_field(g, raw, log_scale, quat, x, site, n_samples,
                                             static_cast<float>(1.0 / (scale_mult * scale_mult)), false, nullptr, sigma,
-                                            nullptr, nullptr, nullptr, workspace, status,
+                                            nullptr, nullptr, nullptr, workspace, workspace_bytes, status,
                                             static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_density_forward");
 }
@@ -422,7 +424,8 @@ int vg_density_backward(const void* pack, int64_t n_sites, int64_t n_adj, const 
     if (status == nullptr) return fail(VG_ERR_CUDA, "status word unavailable");
     const vg::GraphView g = vg::graph_view(pack, n_sites, n_adj);
     const cudaError_t e = vg::density_field(g, raw, log_scale, quat, x, site, n_samples, 1.f, true, grad_sigma, nullptr,
-                                            g_raw, g_ls, g_quat, workspace, status, static_cast<cudaStream_t>(stream));
+                                            g_raw, g_ls, g_quat, workspace, workspace_bytes, status,
+                                            static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_density_backward");
 }
 
@@ -439,7 +442,7 @@ int vg_color_forward(const void* pack, int64_t n_sites, int64_t n_adj, const flo
     if (status == nullptr) return fail(VG_ERR_CUDA, "status word unavailable");
     const vg::GraphView g = vg::graph_view(pack, n_sites, n_adj);
     const cudaError_t e = vg::color_field(g, log_scale, quat, sh, sh_deg, x, dirs, site, n_samples, false, nullptr, nullptr,
-                                          rgb, nullptr, nullptr, nullptr, workspace, status,
+                                          rgb, nullptr, nullptr, nullptr, workspace, workspace_bytes, status,
                                           static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_color_forward");
 }
@@ -459,7 +462,7 @@ int vg_color_backward(const void* pack, int64_t n_sites, int64_t n_adj, const fl
     if (status == nullptr) return fail(VG_ERR_CUDA, "status word unavailable");
     const vg::GraphView g = vg::graph_view(pack, n_sites, n_adj);
     const cudaError_t e = vg::color_field(g, log_scale, quat, sh, sh_deg, x, dirs, site, n_samples, true, rgb, grad_rgb,
-                                          nullptr, g_ls, g_quat, g_sh, workspace, status,
+                                          nullptr, g_ls, g_quat, g_sh, workspace, workspace_bytes, status,
                                           static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_color_backward");
 }

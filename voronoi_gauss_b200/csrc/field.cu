@@ -17,6 +17,16 @@
 // that applies the conic chain rule (gauss.cuh) and scatters to the caller's (original-order) tensors:
 // g_ls, g_quat, and g_raw (density) or g_sh (colour). Mathematically the same gradients as the
 // reference's per-sample scatter_gauss_grad (vgf.cu:126-153); the summation order differs.
+//
+// With a workspace sized for the sample count (vg_field_workspace_bytes), the backward passes instead
+// bucket the samples by cell and reuse the cell-major scatter of the foam backward (foam.cu): a sample's
+// density and colour gradients take the same per-neighbour form there (dL/dsigma times the density
+// Gaussian; the normalised colour weight a_k with its m_min / 1 / sum a), so one 64-byte item per sample
+// in its cell's bucket feeds cm_scatter_bucketed, and one thread per site applies the conic chain rule.
+#include <cub/device/device_scan.cuh>
+
+#include <algorithm>
+
 #include "gauss.cuh"
 #include "vg_common.cuh"
 
@@ -310,6 +320,141 @@ __global__ void __launch_bounds__(kPrepBlock)
     }
 }
 
+// ------------------------------------------------------------------------ cell-major backward passes
+
+// Site records in the foam field-pack layout (vg_common.cuh) with one of the two conics: the density
+// conic and min(raw, 30) (colour = false) or the colour conic and the SH rows (colour = true).
+__global__ void __launch_bounds__(kPrepBlock)
+    field_rec_kernel(const int* __restrict__ perm, int n, const float* __restrict__ raw, const float* __restrict__ ls,
+                     const float* __restrict__ quat, bool colour, const float* __restrict__ sh, int nc, int s4,
+                     float4* __restrict__ rec, float4* __restrict__ shp) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int64_t o = __ldg(perm + i);
+    ConicLocal L;
+    conic_local(ls, quat, o, 0.f, L);
+    float A[6];
+    conic_of(L, A);
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 a0 = make_float4(A[0], A[1], A[2], A[3]);
+    float4* r = rec + 4 * static_cast<int64_t>(i);
+    if (!colour) {
+        r[0] = a0, r[1] = make_float4(A[4], A[5], fminf(__ldg(raw + o), 30.f), 0.f), r[2] = z, r[3] = z;
+    } else {
+        r[0] = z, r[1] = z, r[2] = a0, r[3] = make_float4(A[4], A[5], 0.f, 0.f);
+    }
+    float4* q = shp + static_cast<int64_t>(s4) * i;
+    const float* sr = sh != nullptr ? sh + 48 * o : nullptr;
+    for (int v = 0; v < s4; ++v) {
+        float f[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) f[u] = sr != nullptr && 4 * v + u < nc ? __ldg(sr + 4 * v + u) : 0.f;
+        q[v] = make_float4(f[0], f[1], f[2], f[3]);
+    }
+}
+
+// Samples [t0, t0 + mp) counted per cell (samples whose site is not a site of the graph are skipped by
+// this kernel and by field_items_kernel alike).
+__global__ void __launch_bounds__(kBlock)
+    sample_count_kernel(const GraphView g, const int* __restrict__ site, int64_t t0, int64_t mp,
+                        int* __restrict__ count) {
+    const int64_t t = t0 + static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
+    if (t >= t0 + mp) return;
+    const int i = __ldg(site + t);
+    if (i < 0 || i >= g.n) return;
+    atomicAdd(count + __ldg(g.inv + i), 1);
+}
+
+// One 64-byte item per sample at its place in its cell's bucket: (x, dL/dsigma) | (dL/dC, dL/dC . C) |
+// (m_min, 1 / sum of colour weights, 0, 0) | (unit direction, 0). For the colour, m_min and the weight sum
+// come from the sample's neighbourhood (vgf.cu:297-312); samples without a gradient get a zero item.
+__global__ void __launch_bounds__(kBlock)
+    field_items_kernel(GraphView g, FieldView F, const float* __restrict__ x, const float* __restrict__ dirs,
+                       const int* __restrict__ site, int64_t t0, int64_t mp, const float* __restrict__ g_sigma,
+                       const float* __restrict__ rgb, const float* __restrict__ g_rgb, const int* __restrict__ offsets,
+                       int* __restrict__ fill, float4* __restrict__ items, int* status) {
+    const int64_t t = t0 + static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
+    if (t >= t0 + mp) return;
+    const int c = sample_cell(g, site, t, status);
+    if (c < 0) return;
+    float x0, x1, x2;
+    load_x(x, t, x0, x1, x2);
+    const int64_t pos = __ldg(offsets + c) + atomicAdd(fill + c, 1);
+    float4* it = items + 4 * pos;
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (g_sigma != nullptr) {
+        it[0] = make_float4(x0, x1, x2, __ldg(g_sigma + t)), it[1] = z, it[2] = z, it[3] = z;
+        return;
+    }
+    const float gr = __ldg(g_rgb + 3 * t), gg = __ldg(g_rgb + 3 * t + 1), gb = __ldg(g_rgb + 3 * t + 2);
+    if (gr == 0.f && gg == 0.f && gb == 0.f) {
+        it[0] = make_float4(x0, x1, x2, 0.f), it[1] = z, it[2] = z, it[3] = z;
+        return;
+    }
+    const int e0 = __ldg(g.off + c), e1 = __ldg(g.off + c + 1);
+    float mmin = kInf;
+    for (int e = e0; e < e1; ++e) {
+        const float4 E = __ldg(g.edge + e);
+        const float4* fr = F.rec + kFieldVec * static_cast<int64_t>(site_of(E));
+        const float v0 = __fsub_rn(x0, E.x), v1 = __fsub_rn(x1, E.y), v2 = __fsub_rn(x2, E.z);
+        mmin = fminf(mmin, maha(__ldg(fr + 2), __ldg(fr + 3), v0, v1, v2));
+    }
+    float A = 0.f;
+    for (int e = e0; e < e1; ++e) {
+        const float4 E = __ldg(g.edge + e);
+        const float4* fr = F.rec + kFieldVec * static_cast<int64_t>(site_of(E));
+        const float v0 = __fsub_rn(x0, E.x), v1 = __fsub_rn(x1, E.y), v2 = __fsub_rn(x2, E.z);
+        A += __expf(-0.5f * (maha(__ldg(fr + 2), __ldg(fr + 3), v0, v1, v2) - mmin));
+    }
+    float dx, dy, dz;
+    unit_dir(dirs, t, dx, dy, dz);
+    const float gCC = gr * __ldg(rgb + 3 * t) + gg * __ldg(rgb + 3 * t + 1) + gb * __ldg(rgb + 3 * t + 2);
+    it[0] = make_float4(x0, x1, x2, 0.f);
+    it[1] = make_float4(gr, gg, gb, gCC);
+    it[2] = make_float4(mmin, 1.f / A, 0.f, 0.f);
+    it[3] = make_float4(dx, dy, dz, 0.f);
+}
+
+// One thread per site: the gradient pack (N, 64) of the cell-major scatter -> the caller's outputs via
+// the conic chain rule of the density (colour = false: g_raw, g_dA) or colour (g_cA, g_sh) Gaussian.
+__global__ void __launch_bounds__(kPrepBlock)
+    field_pack_grad_kernel(const int* __restrict__ perm, int n, const float* __restrict__ ls,
+                           const float* __restrict__ quat, const float4* __restrict__ grad, bool colour, int nc,
+                           float* __restrict__ g_raw, float* __restrict__ g_ls, float* __restrict__ g_quat,
+                           float* __restrict__ g_sh) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int64_t o = __ldg(perm + i);
+    const float4* G = grad + (kGradStride / 4) * static_cast<int64_t>(i);
+    float gA[6];
+    if (!colour) {
+        const float4 d0 = G[0], d1 = G[1];
+        gA[0] = d0.y, gA[1] = d0.z, gA[2] = d0.w, gA[3] = d1.x, gA[4] = d1.y, gA[5] = d1.z;
+        g_raw[o] = d0.x;
+    } else {
+        const float4 c0 = G[2], c1 = G[3];
+        gA[0] = c0.x, gA[1] = c0.y, gA[2] = c0.z, gA[3] = c0.w, gA[4] = c1.x, gA[5] = c1.y;
+        float4* sd = reinterpret_cast<float4*>(g_sh + 48 * o);
+#pragma unroll
+        for (int v = 0; v < 12; ++v) {
+            float4 q = G[4 + v];
+            if (4 * v + 0 >= nc) q.x = 0.f;
+            if (4 * v + 1 >= nc) q.y = 0.f;
+            if (4 * v + 2 >= nc) q.z = 0.f;
+            if (4 * v + 3 >= nc) q.w = 0.f;
+            sd[v] = q;
+        }
+    }
+    ConicLocal L;
+    conic_local(ls, quat, o, 0.f, L);
+    float gl[3];
+    float4 gq;
+    conic_grad(L, gA, gl, gq);
+#pragma unroll
+    for (int k = 0; k < 3; ++k) g_ls[3 * o + k] = gl[k];
+    reinterpret_cast<float4*>(g_quat)[o] = gq;
+}
+
 inline int blocks(int64_t n, int bs) { return static_cast<int>((n + bs - 1) / bs); }
 
 inline size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -332,9 +477,93 @@ FieldLayout field_layout(int64_t n, int sh_deg, int kind) {
     return L;
 }
 
+constexpr int64_t kFieldPass = int64_t(1) << 25;  // samples bucketed at once (2 GB of items)
+
+struct FieldCmLayout {
+    size_t rec, sh, grad, items, count, fill, offsets, chunks, counter, temp, temp_bytes, total;
+    int s4;
+    int64_t pass;
+};
+
+// Scratch of the cell-major backward of n sites and m samples (passes of at most kFieldPass samples).
+FieldCmLayout field_cm_layout(int64_t n, int sh_deg, bool colour, int64_t m) {
+    FieldCmLayout L{};
+    L.s4 = colour ? sh_vec4(sh_deg) : 1;
+    L.pass = std::max<int64_t>(1, std::min<int64_t>(m, kFieldPass));
+    size_t at = 0;
+    auto take = [&](size_t b) {
+        const size_t h = at;
+        at += al256(b);
+        return h;
+    };
+    L.rec = take(16 * kFieldVec * static_cast<size_t>(n));
+    L.sh = take(16 * static_cast<size_t>(L.s4) * n);
+    L.grad = take(4 * kGradStride * static_cast<size_t>(n));
+    L.items = take(64 * static_cast<size_t>(L.pass));
+    L.count = take(4 * static_cast<size_t>(n + 1));
+    L.fill = take(4 * static_cast<size_t>(n));
+    L.offsets = take(4 * static_cast<size_t>(n + 1));
+    L.chunks = take(16 * static_cast<size_t>(L.pass / 32 + n + 1));
+    L.counter = take(16);
+    size_t scan = 0;
+    cub::DeviceScan::ExclusiveSum(nullptr, scan, static_cast<const int*>(nullptr), static_cast<int*>(nullptr),
+                                  static_cast<int>(n + 1));
+    L.temp_bytes = scan;
+    L.temp = take(scan);
+    L.total = at;
+    return L;
+}
+
+// The cell-major backward of the density (g_sigma non-null) or colour field into the caller's outputs.
+cudaError_t field_backward_cm(const GraphView& g, const float* raw, const float* ls, const float* quat,
+                              const float* sh, int sh_deg, const float* x, const float* dirs, const int* site,
+                              int64_t m, const float* g_sigma, const float* rgb, const float* g_rgb, float* g_raw,
+                              float* g_ls, float* g_quat, float* g_sh, void* ws, int* status, cudaStream_t st) {
+    const bool colour = g_sigma == nullptr;
+    const FieldCmLayout L = field_cm_layout(g.n, sh_deg, colour, m);
+    char* b = static_cast<char*>(ws);
+    float4* rec = reinterpret_cast<float4*>(b + L.rec);
+    float4* shp = reinterpret_cast<float4*>(b + L.sh);
+    float* grad = reinterpret_cast<float*>(b + L.grad);
+    float4* items = reinterpret_cast<float4*>(b + L.items);
+    int* count = reinterpret_cast<int*>(b + L.count);
+    int* fill = reinterpret_cast<int*>(b + L.fill);
+    int* offsets = reinterpret_cast<int*>(b + L.offsets);
+    int4* chunks = reinterpret_cast<int4*>(b + L.chunks);
+    int* counter = reinterpret_cast<int*>(b + L.counter);
+    const int nc = 3 * sh_coeffs(sh_deg);
+    field_rec_kernel<<<blocks(g.n, kPrepBlock), kPrepBlock, 0, st>>>(g.perm, g.n, raw, ls, quat, colour,
+                                                                     colour ? sh : nullptr, nc, L.s4, rec, shp);
+    cudaError_t e = cudaMemsetAsync(grad, 0, 4 * kGradStride * static_cast<size_t>(g.n), st);
+    if (e != cudaSuccess) return e;
+    const FieldView F{rec, shp, colour ? sh_deg : 0, L.s4};
+    for (int64_t t0 = 0; t0 < m; t0 += L.pass) {
+        const int64_t mp = std::min<int64_t>(L.pass, m - t0);
+        e = cudaMemsetAsync(count, 0, 4 * static_cast<size_t>(g.n + 1), st);
+        if (e == cudaSuccess) e = cudaMemsetAsync(fill, 0, 4 * static_cast<size_t>(g.n), st);
+        if (e != cudaSuccess) return e;
+        sample_count_kernel<<<blocks(mp, kBlock), kBlock, 0, st>>>(g, site, t0, mp, count);
+        size_t tb = L.temp_bytes;
+        e = cub::DeviceScan::ExclusiveSum(b + L.temp, tb, count, offsets, g.n + 1, st);
+        if (e != cudaSuccess) return e;
+        field_items_kernel<<<blocks(mp, kBlock), kBlock, 0, st>>>(g, F, x, dirs, site, t0, mp, g_sigma, rgb, g_rgb,
+                                                                  offsets, fill, items, status);
+        e = cm_scatter_bucketed(g, F, items, offsets, chunks, counter, grad, st);
+        if (e != cudaSuccess) return e;
+    }
+    field_pack_grad_kernel<<<blocks(g.n, kPrepBlock), kPrepBlock, 0, st>>>(
+        g.perm, g.n, ls, quat, reinterpret_cast<const float4*>(grad), colour, nc, g_raw, g_ls, g_quat, g_sh);
+    return cudaGetLastError();
+}
+
 }  // namespace
 
 size_t field_workspace(int64_t n_sites, int sh_deg, int kind) { return field_layout(n_sites, sh_deg, kind).total; }
+
+size_t field_cm_workspace(int64_t n_sites, int sh_deg, int kind, int64_t n_samples) {
+    if (kind != 1 && kind != 3) return 0;
+    return field_cm_layout(n_sites, sh_deg, kind == 3, n_samples).total;
+}
 
 cudaError_t sampler_walk(const GraphView& g, const float* o, const float* d, const float* z, const int* start,
                          int64_t n_rays, int n_samples, int* site, int* steps, int* status, cudaStream_t st) {
@@ -345,7 +574,11 @@ cudaError_t sampler_walk(const GraphView& g, const float* o, const float* d, con
 
 cudaError_t density_field(const GraphView& g, const float* raw, const float* ls, const float* quat, const float* x,
                           const int* site, int64_t m, float inv_mult2, bool backward, const float* g_sigma, float* sigma,
-                          float* g_raw, float* g_ls, float* g_quat, void* ws, int* status, cudaStream_t st) {
+                          float* g_raw, float* g_ls, float* g_quat, void* ws, size_t ws_bytes, int* status,
+                          cudaStream_t st) {
+    if (backward && m > 0 && ws_bytes >= field_cm_workspace(g.n, 0, 1, m))
+        return field_backward_cm(g, raw, ls, quat, nullptr, 0, x, nullptr, site, m, g_sigma, nullptr, nullptr, g_raw,
+                                 g_ls, g_quat, nullptr, ws, status, st);
     const FieldLayout L = field_layout(g.n, 0, backward ? 1 : 0);
     char* b = static_cast<char*>(ws);
     float4* gauss = reinterpret_cast<float4*>(b + L.gauss);
@@ -368,8 +601,11 @@ cudaError_t density_field(const GraphView& g, const float* raw, const float* ls,
 
 cudaError_t color_field(const GraphView& g, const float* ls, const float* quat, const float* sh, int sh_deg,
                         const float* x, const float* dirs, const int* site, int64_t m, bool backward, const float* rgb_in,
-                        const float* g_rgb, float* rgb, float* g_ls, float* g_quat, float* g_sh, void* ws, int* status,
-                        cudaStream_t st) {
+                        const float* g_rgb, float* rgb, float* g_ls, float* g_quat, float* g_sh, void* ws,
+                        size_t ws_bytes, int* status, cudaStream_t st) {
+    if (backward && m > 0 && ws_bytes >= field_cm_workspace(g.n, sh_deg, 3, m))
+        return field_backward_cm(g, nullptr, ls, quat, sh, sh_deg, x, dirs, site, m, nullptr, rgb_in, g_rgb, nullptr,
+                                 g_ls, g_quat, g_sh, ws, status, st);
     const FieldLayout L = field_layout(g.n, sh_deg, backward ? 3 : 2);
     char* b = static_cast<char*>(ws);
     float4* gauss = reinterpret_cast<float4*>(b + L.gauss);

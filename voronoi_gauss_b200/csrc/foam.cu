@@ -76,12 +76,6 @@
 #ifndef VG_FWD_COUNT
 #define VG_FWD_COUNT 1
 #endif
-// VG_FWD_REFILL      1: the deferred traversal runs as a persistent grid whose lanes take the next ray
-//                    from a global counter as soon as theirs ends (no lane idles while the longest ray
-//                    of its warp finishes); 0: one ray per thread
-#ifndef VG_FWD_REFILL
-#define VG_FWD_REFILL 1
-#endif
 
 namespace vg {
 namespace {
@@ -209,86 +203,6 @@ __global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
     out.depth[r] = dep;
     out.stats[3 * r] = n_samples, out.stats[3 * r + 1] = n_color, out.stats[3 * r + 2] = walk_steps;
     if (err) atomicOr(status, err);
-}
-
-// The deferred traversal (foam_forward_kernel<true, kDeferred>) with lane refill: every lane runs the
-// same per-ray steps, one cell per loop trip, and a lane whose ray has ended takes the next unclaimed ray
-// (one atomic per warp and refill). Outputs are those of the one-ray-per-thread kernel, bit for bit.
-__global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
-    foam_deferred_refill_kernel(GraphView g, FieldView F, RayView R, FoamCfg c, Outputs out, int* status,
-                                unsigned long long* next_ray) {
-    const int lane = threadIdx.x & 31;
-    const int K = c.record_cap;
-    ColorCache<0> cache{nullptr, 0};
-    const float b[16] = {};  // no colours in the traversal
-    int64_t r = 0;
-    float o[3] = {0.f, 0.f, 0.f}, d[3] = {0.f, 0.f, 0.f}, near = 0.f, far = 0.f;
-    Sample P{};
-    float t_exit = kInf, T = 1.f, dep = 0.f;
-    int next = -1, err = 0, walk_steps = 0, n_samples = 1, n_color = 0, it = 0;
-    bool has_p = false, active = false, exhausted = false;
-    int* cnt = nullptr;
-    for (;;) {
-        const unsigned need = __ballot_sync(0xffffffffu, !active && !exhausted);
-        if (need) {
-            const int leader = __ffs(need) - 1;
-            unsigned long long base = 0;
-            if (lane == leader) base = atomicAdd(next_ray, static_cast<unsigned long long>(__popc(need)));
-            base = __shfl_sync(0xffffffffu, base, leader);
-            if (!active && !exhausted) {
-                const int64_t mine = static_cast<int64_t>(base) + __popc(need & ((1u << lane) - 1u));
-                if (mine < R.n) {
-                    r = mine;
-                    active = true;
-                    load_ray(R, r, o, d, near, far);
-                    err = 0, walk_steps = 0, n_samples = 1, n_color = 0, it = 0;
-                    const int cur = walk_to(g, __ldg(g.inv + __ldg(R.start + r)), along(o[0], near, d[0]),
-                                            along(o[1], near, d[1]), along(o[2], near, d[2]), walk_steps, err);
-                    eval_sample<0, false>(g, F, cur, near, o, d, b, cache, true, P, t_exit, next);
-                    has_p = false, T = 1.f, dep = 0.f;
-                    cnt = c.cm_count != nullptr ? c.cm_count + (r / c.cm_rays) * c.cm_stride : nullptr;
-                } else {
-                    exhausted = true;
-                }
-            }
-        }
-        if (__ballot_sync(0xffffffffu, active) == 0) break;
-        if (!active) continue;
-        const bool last = next < 0 || t_exit >= far;
-        Sample Q;
-        float t_exit_q;
-        int next_q;
-        eval_sample<0, false>(g, F, last ? P.cell : next, last ? far : fmaxf(t_exit, P.t), o, d, b, cache, !last, Q,
-                              t_exit_q, next_q);
-        bool has_q = false;
-        ++n_samples;
-        const float delta = Q.t - P.t;
-        const float alpha = 1.f - __expf(-0.5f * (P.sigma + Q.sigma) * delta);
-        const float w = T * alpha;
-        if (w > c.w_thresh) {
-            has_p = has_q = true;
-            dep += w * 0.5f * (P.t + Q.t);
-            ++n_color;
-        }
-        T *= 1.f - alpha;
-        store_sample(out.rec, r, K, n_samples - 2, P, has_p, true, g.perm);
-        if (has_p && n_samples - 2 < K && cnt != nullptr) atomicAdd(cnt + P.cell, 1);
-        P = Q;
-        has_p = has_q;
-        t_exit = t_exit_q, next = next_q;
-        ++it;
-        const bool capped = it == kMaxCells;
-        if (last || T < c.t_thresh || capped) {
-            if (capped && !(last || T < c.t_thresh)) err |= kErrCellCap;
-            store_sample(out.rec, r, K, n_samples - 1, P, has_p, true, g.perm);
-            if (has_p && n_samples - 1 < K && cnt != nullptr) atomicAdd(cnt + P.cell, 1);
-            out.T[r] = T;
-            out.depth[r] = dep;
-            out.stats[3 * r] = n_samples, out.stats[3 * r + 1] = n_color, out.stats[3 * r + 2] = walk_steps;
-            if (err) atomicOr(status, err);
-            active = false;
-        }
-    }
 }
 
 // ------------------------------------------------------------------- cell-major colours (forward)
@@ -1032,7 +946,7 @@ constexpr int kMarchCap = 256;                    // march samples per ray taken
 inline size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct CmLayout {
-    size_t items, n_items, order, count, fill, offsets, chunks, counter, ray_counter, temp, temp_bytes, total;
+    size_t items, n_items, order, count, fill, offsets, chunks, counter, temp, temp_bytes, total;
     int64_t rays_per_pass;
 };
 
@@ -1059,7 +973,6 @@ CmLayout cm_layout(int64_t n_sites, int64_t n_rays, int K, bool with_items, int 
     L.offsets = take(4 * (n_sites + 1));
     L.chunks = take(16 * (slots / 32 + n_sites + 1));
     L.counter = take(16);
-    L.ray_counter = take(16);
     size_t scan = 0;
     cub::DeviceScan::ExclusiveSum(nullptr, scan, static_cast<const int*>(nullptr), static_cast<int*>(nullptr),
                                   static_cast<int>(n_sites + 1));
@@ -1084,6 +997,27 @@ int sm_count() {
 
 size_t foam_backward_workspace(int64_t n_sites, int64_t n_rays, int record_cap) {
     return cm_layout(n_sites, n_rays, record_cap, true).total;
+}
+
+cudaError_t cm_scatter_bucketed(const GraphView& g, const FieldView& F, const float4* items, const int* offsets,
+                                int4* chunks, int* counter, float* grad, cudaStream_t st) {
+    const int n = g.n;
+    cudaError_t e = cudaMemsetAsync(counter, 0, 16, st);
+    if (e != cudaSuccess) return e;
+    cm_chunks_kernel<<<blocks(n), kBlock, 0, st>>>(offsets, n, chunks, counter);
+    const int grid = sm_count() * 3;
+    const RayView none{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 0};
+    switch (F.s4) {
+        case 1: cm_scatter_kernel<1, kBucketed><<<grid, kBlock, 0, st>>>(g, F, none, nullptr, 0, items, nullptr, chunks,
+                                                                         counter, 0, grad); break;
+        case 3: cm_scatter_kernel<3, kBucketed><<<grid, kBlock, 0, st>>>(g, F, none, nullptr, 0, items, nullptr, chunks,
+                                                                         counter, 0, grad); break;
+        case 7: cm_scatter_kernel<7, kBucketed><<<grid, kBlock, 0, st>>>(g, F, none, nullptr, 0, items, nullptr, chunks,
+                                                                         counter, 0, grad); break;
+        default: cm_scatter_kernel<12, kBucketed><<<grid, kBlock, 0, st>>>(g, F, none, nullptr, 0, items, nullptr,
+                                                                           chunks, counter, 0, grad); break;
+    }
+    return cudaGetLastError();
 }
 
 size_t march_backward_workspace(int64_t n_sites, int64_t n_rays) {
@@ -1161,15 +1095,7 @@ cudaError_t forward_deferred(const GraphView& g, const FieldView& F, const RayVi
         if (e != cudaSuccess) return e;
         cc.cm_count = count_all, cc.cm_rays = L.rays_per_pass, cc.cm_stride = g.n + 1;
     }
-    if (VG_FWD_REFILL) {
-        auto* next_ray = reinterpret_cast<unsigned long long*>(b + L.ray_counter);
-        const cudaError_t e = cudaMemsetAsync(next_ray, 0, sizeof(unsigned long long), st);
-        if (e != cudaSuccess) return e;
-        const int grid = static_cast<int>(std::min<int64_t>(blocks(R.n), static_cast<int64_t>(sm_count()) * VG_FWD_MINB));
-        foam_deferred_refill_kernel<<<grid, kBlock, 0, st>>>(g, F, R, cc, out, status, next_ray);
-    } else {
-        foam_forward_kernel<true, kDeferred><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, cc, out, status);
-    }
+    foam_forward_kernel<true, kDeferred><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, cc, out, status);
     foam_forward_kernel<true, kImmediateOverflow><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, cc, out, status);
     int* order = reinterpret_cast<int*>(b + L.order);
     int* fill = reinterpret_cast<int*>(b + L.fill);

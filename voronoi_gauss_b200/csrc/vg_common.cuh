@@ -297,6 +297,12 @@ cudaError_t march_forward(const GraphView& g, const FieldView& F, const RayView&
 // The backward takes optional scratch (march_backward_workspace bytes) for the cell-major scatter.
 cudaError_t march_backward(const GraphView& g, const FieldView& F, const RayView& R, const MarchCfg& c,
                            const GradIn& gi, float* grad, int* status, void* cm_ws, size_t cm_bytes, cudaStream_t st);
+// foam.cu: the cell-major gradient scatter of 64-byte items stored contiguously per cell (offsets (N + 1)
+// of the cells' item runs; item layout: (x, dL/dsigma) | (dL/dC, dL/dC . C) | (m_min, 1 / sum of colour
+// weights or 0, -, -) | (unit direction, -)) into the gradient pack grad (N, 64); chunks holds
+// (items / 32 + N + 1) int4, counter 16 bytes.
+cudaError_t cm_scatter_bucketed(const GraphView& g, const FieldView& F, const float4* items, const int* offsets,
+                                int4* chunks, int* counter, float* grad, cudaStream_t st);
 // foam.cu: the cell-major part of the march backward
 size_t march_backward_workspace(int64_t n_sites, int64_t n_rays);
 cudaError_t march_backward_cm(const GraphView& g, const FieldView& F, const RayView& R, const MarchCfg& c,
@@ -312,15 +318,19 @@ cudaError_t conic_backward(const float* log_scale, const float* quat, int64_t n,
 // field.cu: the NeRF-sampler field kernels. kind: 0 density forward, 1 density backward, 2 colour
 // forward, 3 colour backward. inv_mult2 = 1 / scale_mult^2 (forward only; the backward uses 1).
 size_t field_workspace(int64_t n_sites, int sh_deg, int kind);
+// scratch of the cell-major backward (kind 1 or 3) of n_samples samples; a backward given at least this
+// much takes that path
+size_t field_cm_workspace(int64_t n_sites, int sh_deg, int kind, int64_t n_samples);
 cudaError_t sampler_walk(const GraphView& g, const float* o, const float* d, const float* z, const int* start,
                          int64_t n_rays, int n_samples, int* site, int* steps, int* status, cudaStream_t st);
 cudaError_t density_field(const GraphView& g, const float* raw, const float* ls, const float* quat, const float* x,
                           const int* site, int64_t m, float inv_mult2, bool backward, const float* g_sigma, float* sigma,
-                          float* g_raw, float* g_ls, float* g_quat, void* ws, int* status, cudaStream_t st);
+                          float* g_raw, float* g_ls, float* g_quat, void* ws, size_t ws_bytes, int* status,
+                          cudaStream_t st);
 cudaError_t color_field(const GraphView& g, const float* ls, const float* quat, const float* sh, int sh_deg,
                         const float* x, const float* dirs, const int* site, int64_t m, bool backward, const float* rgb_in,
-                        const float* g_rgb, float* rgb, float* g_ls, float* g_quat, float* g_sh, void* ws, int* status,
-                        cudaStream_t st);
+                        const float* g_rgb, float* rgb, float* g_ls, float* g_quat, float* g_sh, void* ws,
+                        size_t ws_bytes, int* status, cudaStream_t st);
 
 // infer_pack.cu: the inference layout of render.pack_foam / bake_colors. g (the graph pack) renumbers
 // the sites in Morton order when non-null; floor2 = fp32(scale_floor^2), log_eps = fp32(log eps_density).

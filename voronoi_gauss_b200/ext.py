@@ -326,8 +326,8 @@ class FieldExtension:
         return m
 
     @staticmethod
-    def _ws(n, sh_deg, kind, dev):
-        nbytes = _lib.lib().vg_field_workspace_bytes(n, int(sh_deg), kind)
+    def _ws(n, sh_deg, kind, dev, m=0):
+        nbytes = _lib.lib().vg_field_workspace_bytes(n, int(sh_deg), kind, int(m))
         return torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev), nbytes
 
     @classmethod
@@ -353,7 +353,7 @@ class FieldExtension:
             raise RuntimeError('raw must be (N) and grad_sigma (M)')
         g_raw, g_ls, g_quat = torch.empty_like(raw), torch.empty_like(log_scale), torch.empty_like(quat)
         pk = graph_pack(points, offsets, adj)
-        ws, nbytes = cls._ws(pk.n, 0, 1, x.device)
+        ws, nbytes = cls._ws(pk.n, 0, 1, x.device, m)
         with torch.cuda.device(x.device):
             _lib.call('vg_density_backward', pk.ptr, pk.n, pk.m, raw.data_ptr(), log_scale.data_ptr(),
                       quat.data_ptr(), _ptr(x), _ptr(site), m, _ptr(grad_sigma), g_raw.data_ptr(), g_ls.data_ptr(),
@@ -390,7 +390,7 @@ class FieldExtension:
         sh_deg = _sh_deg(sh_deg)
         g_ls, g_quat, g_sh = torch.empty_like(log_scale), torch.empty_like(quat), torch.empty_like(sh)
         pk = graph_pack(points, offsets, adj)
-        ws, nbytes = cls._ws(pk.n, sh_deg, 3, x.device)
+        ws, nbytes = cls._ws(pk.n, sh_deg, 3, x.device, m)
         with torch.cuda.device(x.device):
             _lib.call('vg_color_backward', pk.ptr, pk.n, pk.m, log_scale.data_ptr(), quat.data_ptr(), sh.data_ptr(),
                       sh_deg, _ptr(x), _ptr(dirs), _ptr(site), m, _ptr(rgb), _ptr(grad_rgb), g_ls.data_ptr(),
