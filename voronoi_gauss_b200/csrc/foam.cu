@@ -214,37 +214,38 @@ __global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
 // the cell's order with the same arithmetic as eval_color, so the colours are bit-identical to the
 // inline path; cmf_composite_kernel then sums the segments of every ray from its records.
 
-// Samples of a ray chunk counted per cell: those that need a colour (colour_only), or all of them.
+// Samples of a ray chunk counted per cell: those that need a colour (colour_only), or all of them. One
+// warp per ray, lanes over its samples: the records of a ray are read as contiguous 32-byte sectors.
 __global__ void __launch_bounds__(kBlock)
     cmf_count_kernel(const float* __restrict__ rec, const int* __restrict__ stats, const int* __restrict__ inv,
                      int64_t r0, int64_t n, int K, int* __restrict__ count, bool colour_only) {
-    const int64_t rl = static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
+    const int64_t rl = (static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
     if (rl >= n) return;
     const int64_t r = r0 + rl;
     const int S = __ldg(stats + 3 * r);
     if (S > K) return;
-    for (int s = 0; s < S; ++s) {
-        const float4 q1 = __ldg(reinterpret_cast<const float4*>(rec + (r * K + s) * kRecord) + 1);
-        if (!colour_only || q1.w < 0.f) {
-            const int site = __float_as_int(__ldg(rec + (r * K + s) * kRecord + 1));
-            atomicAdd(count + __ldg(inv + site), 1);
-        }
+    for (int s = lane; s < S; s += 32) {
+        const float* q = rec + (r * K + s) * kRecord;
+        if (!colour_only || __ldg(q + 7) < 0.f) atomicAdd(count + __ldg(inv + __float_as_int(__ldg(q + 1))), 1);
     }
 }
 
+// The slots of the samples that need a colour, counting-sorted by cell (one warp per ray).
 __global__ void __launch_bounds__(kBlock)
     cmf_bucket_kernel(const float* __restrict__ rec, const int* __restrict__ stats, const int* __restrict__ inv,
                       int64_t r0, int64_t n, int K, const int* __restrict__ offsets, int* __restrict__ fill,
                       int* __restrict__ order) {
-    const int64_t rl = static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
+    const int64_t rl = (static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
     if (rl >= n) return;
     const int64_t r = r0 + rl;
     const int S = __ldg(stats + 3 * r);
     if (S > K) return;
-    for (int s = 0; s < S; ++s) {
-        const float4 q1 = __ldg(reinterpret_cast<const float4*>(rec + (r * K + s) * kRecord) + 1);
-        if (q1.w < 0.f) {
-            const int cell = __ldg(inv + __float_as_int(__ldg(rec + (r * K + s) * kRecord + 1)));
+    for (int s = lane; s < S; s += 32) {
+        const float* q = rec + (r * K + s) * kRecord;
+        if (__ldg(q + 7) < 0.f) {
+            const int cell = __ldg(inv + __float_as_int(__ldg(q + 1)));
             order[__ldg(offsets + cell) + atomicAdd(fill + cell, 1)] = static_cast<int>(rl * K + s);
         }
     }
@@ -1113,11 +1114,12 @@ cudaError_t forward_deferred(const GraphView& g, const FieldView& F, const RayVi
         if (e == cudaSuccess) e = cudaMemsetAsync(counter, 0, 16, st);
         if (e != cudaSuccess) return e;
         if (!VG_FWD_COUNT)
-            cmf_count_kernel<<<blocks(nr), kBlock, 0, st>>>(out.rec, out.stats, g.inv, r0, nr, K, count, true);
+            cmf_count_kernel<<<blocks(32 * nr), kBlock, 0, st>>>(out.rec, out.stats, g.inv, r0, nr, K, count, true);
         size_t tb = L.temp_bytes;
         e = cub::DeviceScan::ExclusiveSum(b + L.temp, tb, count, offsets, n + 1, st);
         if (e != cudaSuccess) return e;
-        cmf_bucket_kernel<<<blocks(nr), kBlock, 0, st>>>(out.rec, out.stats, g.inv, r0, nr, K, offsets, fill, order);
+        cmf_bucket_kernel<<<blocks(32 * nr), kBlock, 0, st>>>(out.rec, out.stats, g.inv, r0, nr, K, offsets, fill,
+                                                               order);
         cm_chunks_kernel<<<blocks(n), kBlock, 0, st>>>(offsets, n, chunks, counter);
         switch (F.s4) {
             case 1: cmf_color_kernel<1><<<grid, kBlock, 0, st>>>(g, F, R, out.rec, K, order, chunks, counter, r0); break;
@@ -1200,7 +1202,7 @@ cudaError_t foam_backward(const GraphView& g, const FieldView& F, const RayView&
         const ItemOut io{items, count, r0, nr, offsets, fill};
         size_t tb = L.temp_bytes;
         if (VG_BWD_DIRECT) {
-            cmf_count_kernel<<<blocks(nr), kBlock, 0, st>>>(gi.rec, gi.stats, g.inv, r0, nr, K, count, false);
+            cmf_count_kernel<<<blocks(32 * nr), kBlock, 0, st>>>(gi.rec, gi.stats, g.inv, r0, nr, K, count, false);
             e = cub::DeviceScan::ExclusiveSum(b + L.temp, tb, count, offsets, n + 1, st);
             if (e != cudaSuccess) return e;
             foam_backward_kernel<kItems><<<blocks(nr), kBlock, 0, st>>>(g, F, R, c, gi, grad, io, status);

@@ -6,7 +6,15 @@
 
 #include "vg_common.cuh"
 
+// VG_SAMPLE_UNROLL  unroll factor of the neighbour loop of eval_sample (loads of later neighbours can
+//                   then be issued before the arithmetic of earlier ones)
+#ifndef VG_SAMPLE_UNROLL
+#define VG_SAMPLE_UNROLL 1
+#endif
+
 namespace vg {
+
+constexpr int kSampleUnroll = VG_SAMPLE_UNROLL;
 
 // One sample of a ray: position, the cell whose neighbourhood evaluates it, density and colour.
 struct Sample {
@@ -33,6 +41,7 @@ __device__ __forceinline__ void eval_sample(const GraphView& g, const FieldView&
     Blend B;
     blend_init(B);
     t_exit = kInf, next = -1;
+#pragma unroll kSampleUnroll
     for (int e = e0; e < e1; ++e) {
         const float4 E = e == e0 ? Pc : __ldg(g.edge + e);
         const int j = site_of(E);
