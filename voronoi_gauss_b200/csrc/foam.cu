@@ -56,7 +56,8 @@
 #endif
 // VG_BWD_BALANCE     1: cm_scatter_kernel spreads a chunk's (neighbour, sample) pairs over all 32 lanes
 //                    for cells with fewer than 32 neighbours (replicas / two phases, see balanced_scatter);
-//                    0: one lane per neighbour
+//                    2: only for cells with at most 16 neighbours (replicas, one phase); 0: one lane per
+//                    neighbour
 #ifndef VG_BWD_BALANCE
 #define VG_BWD_BALANCE 0
 #endif
@@ -789,7 +790,7 @@ __global__ void __launch_bounds__(kBlock, 3)
                 cp_async_commit();
             }
             const int e0 = __ldg(g.off + Cur.x), e1 = __ldg(g.off + Cur.x + 1);
-            if (VG_BWD_BALANCE && e1 - e0 < 32) {
+            if (VG_BWD_BALANCE && e1 - e0 < (VG_BWD_BALANCE == 2 ? 17 : 32)) {
                 balanced_scatter<S4>(g, F, st, e0, e1 - e0, Cur.z, lane, grad);
             } else {
                 for (int e = e0 + lane; e < e1; e += 32) {
@@ -842,7 +843,7 @@ __global__ void __launch_bounds__(kBlock, 3)
         }
         __syncwarp();
         const int e0 = __ldg(g.off + cell), e1 = __ldg(g.off + cell + 1);
-        if (VG_BWD_BALANCE && e1 - e0 < 32) {
+        if (VG_BWD_BALANCE && e1 - e0 < (VG_BWD_BALANCE == 2 ? 17 : 32)) {
             balanced_scatter<S4>(g, F, st, e0, e1 - e0, cnt, lane, grad);
         } else {
             for (int e = e0 + lane; e < e1; e += 32) {  // one neighbour site per lane
