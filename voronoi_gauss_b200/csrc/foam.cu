@@ -36,7 +36,7 @@
 #define VG_BWD_AGG 0
 #endif
 #ifndef VG_FWD_MINB
-#define VG_FWD_MINB 8
+#define VG_FWD_MINB 6
 #endif
 #ifndef VG_BWD_MINB
 #define VG_BWD_MINB 1

@@ -9,7 +9,7 @@
 // VG_SAMPLE_UNROLL  unroll factor of the neighbour loop of eval_sample (loads of later neighbours can
 //                   then be issued before the arithmetic of earlier ones)
 #ifndef VG_SAMPLE_UNROLL
-#define VG_SAMPLE_UNROLL 1
+#define VG_SAMPLE_UNROLL 4
 #endif
 
 namespace vg {
