@@ -151,11 +151,14 @@ def algorithmic_bytes(stats, rec, offsets, nb):
 
 
 def launches_per_step(n_rays, record_cap):
-    """libvgb200 kernels launched by one training step: 2 conics, field pack + forward, field pack +
-    per-ray backward (re-traced rays) + 4 cell-major kernels per pass of at most 2^26 recorded samples,
-    gradient unpack, 2 conic backwards (the CUB scan inside each pass is not counted)."""
+    """libvgb200 kernels launched by one training step (the CUB scans compiled into the library count
+    as two kernels each): 2 conics; forward: field pack, deferred traversal, overflow rays, per pass of
+    at most 2^26 record slots (scan, bucket, chunks, colour), composite; backward: field pack, re-traced
+    rays, per pass (count, scan, bucketed items, chunks, scatter), gradient unpack; 2 conic backwards."""
     passes = math.ceil(n_rays / max(1, (1 << 26) // record_cap))
-    return 2 + 2 + 2 + 4 * passes + 1 + 2
+    forward = 3 + passes * (2 + 3) + 1
+    backward = 2 + passes * (1 + 2 + 3) + 1
+    return 2 + forward + backward + 2
 
 
 # --------------------------------------------------------------------------------------- b200 arm

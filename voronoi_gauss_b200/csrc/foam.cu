@@ -54,13 +54,13 @@
 #ifndef VG_BWD_CELL_MAJOR
 #define VG_BWD_CELL_MAJOR 1
 #endif
-// VG_BWD_BALANCE     1: cm_scatter_kernel spreads a chunk's (neighbour, sample) pairs over all 32 lanes
-//                    for cells with fewer than 32 neighbours (replicas / two phases, see balanced_scatter);
-//                    2: only for cells with at most 16 neighbours (replicas, one phase); 0: one lane per
-//                    neighbour
+// VG_BWD_BALANCE     largest neighbourhood size (self included) for which cm_scatter_kernel spreads a
+//                    chunk's (neighbour, sample) pairs over all 32 lanes (balanced_scatter: replicas up to
+//                    16, two phases above); larger cells get one lane per neighbour; 0: never
 #ifndef VG_BWD_BALANCE
-#define VG_BWD_BALANCE 0
+#define VG_BWD_BALANCE 16
 #endif
+static_assert(VG_BWD_BALANCE >= 0 && VG_BWD_BALANCE <= 31, "VG_BWD_BALANCE must be in 0..31");
 // VG_BWD_DIRECT      1: the replay writes 64-byte items (position, gradients, direction) straight into
 //                    their cell's bucket (counted beforehand), so the scatter reads them in order;
 //                    0: 32-byte items in ray order, bucketed through an index array
@@ -790,7 +790,7 @@ __global__ void __launch_bounds__(kBlock, 3)
                 cp_async_commit();
             }
             const int e0 = __ldg(g.off + Cur.x), e1 = __ldg(g.off + Cur.x + 1);
-            if (VG_BWD_BALANCE && e1 - e0 < (VG_BWD_BALANCE == 2 ? 17 : 32)) {
+            if (e1 - e0 <= VG_BWD_BALANCE) {
                 balanced_scatter<S4>(g, F, st, e0, e1 - e0, Cur.z, lane, grad);
             } else {
                 for (int e = e0 + lane; e < e1; e += 32) {
@@ -843,7 +843,7 @@ __global__ void __launch_bounds__(kBlock, 3)
         }
         __syncwarp();
         const int e0 = __ldg(g.off + cell), e1 = __ldg(g.off + cell + 1);
-        if (VG_BWD_BALANCE && e1 - e0 < (VG_BWD_BALANCE == 2 ? 17 : 32)) {
+        if (e1 - e0 <= VG_BWD_BALANCE) {
             balanced_scatter<S4>(g, F, st, e0, e1 - e0, cnt, lane, grad);
         } else {
             for (int e = e0 + lane; e < e1; e += 32) {  // one neighbour site per lane
