@@ -60,6 +60,11 @@
 #ifndef VG_BWD_BALANCE
 #define VG_BWD_BALANCE 16
 #endif
+// VG_BWD_SH_SPLIT    1: the scatter evaluates a neighbour's SH colour as two partial sums per channel
+//                    (shorter dependent chains; the colour only gates and weights gradients there)
+#ifndef VG_BWD_SH_SPLIT
+#define VG_BWD_SH_SPLIT 1
+#endif
 static_assert(VG_BWD_BALANCE >= 0 && VG_BWD_BALANCE <= 31, "VG_BWD_BALANCE must be in 0..31");
 // VG_BWD_DIRECT      1: the replay writes 64-byte items (position, gradients, direction) straight into
 //                    their cell's bucket (counted beforehand), so the scatter reads them in order;
@@ -673,16 +678,24 @@ __device__ __forceinline__ int scatter_range(const GraphView& g, const FieldView
                 b[0] = b0.x, b[1] = b0.y, b[2] = b0.z, b[3] = b0.w, b[4] = b1.x, b[5] = b1.y, b[6] = b1.z;
                 b[7] = b1.w, b[8] = b2.x, b[9] = b2.y, b[10] = b2.z, b[11] = b2.w, b[12] = b3.x;
                 b[13] = b3.y, b[14] = b3.z, b[15] = b3.w;
-                float c[3] = {0.5f, 0.5f, 0.5f};
+                // SH colour of the neighbour in two interleaved partial sums per channel (even / odd
+                // basis functions): half the length of each dependent FMA chain
+                float c[3] = {0.5f, 0.5f, 0.5f}, h[3] = {0.f, 0.f, 0.f};
 #pragma unroll
                 for (int qq = 0; qq < S4; ++qq) {
                     const float f[4] = {coef[qq].x, coef[qq].y, coef[qq].z, coef[qq].w};
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
                         const int k = 4 * qq + u;
-                        if (k < 48) c[k % 3] += b[k / 3] * f[u];
+                        if (k < 48) {
+                            if (VG_BWD_SH_SPLIT && ((k / 3) & 1))
+                                h[k % 3] += b[k / 3] * f[u];
+                            else
+                                c[k % 3] += b[k / 3] * f[u];
+                        }
                     }
                 }
+                c[0] += h[0], c[1] += h[1], c[2] += h[2];
                 const float dc[3] = {c[0] > 0.f ? a * q1.x : 0.f, c[1] > 0.f ? a * q1.y : 0.f,
                                      c[2] > 0.f ? a * q1.z : 0.f};
 #pragma unroll
