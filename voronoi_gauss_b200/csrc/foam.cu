@@ -97,11 +97,12 @@ constexpr int kChunk = VG_CM_CHUNK;
 static_assert(kChunk == 32 || kChunk == 64, "VG_CM_CHUNK must be 32 or 64");
 
 // deferred: the colour fields are filled later; the last field marks the samples that need one (-1)
+// orig: the original id of P's site (loaded when P was evaluated, so the store does not wait for it)
 __device__ __forceinline__ void store_sample(float* __restrict__ rec, int64_t r, int K, int s, const Sample& P,
-                                             bool has_c, bool deferred, const int* __restrict__ perm) {
+                                             bool has_c, bool deferred, int orig) {
     if (s >= K) return;
     float4* q = reinterpret_cast<float4*>(rec + (r * K + s) * kRecord);
-    q[0] = make_float4(P.t, __int_as_float(__ldg(perm + P.cell)), P.sigma, deferred ? 0.f : P.C0);
+    q[0] = make_float4(P.t, __int_as_float(orig), P.sigma, deferred ? 0.f : P.C0);
     q[1] = deferred ? make_float4(0.f, 0.f, 0.f, has_c ? -1.f : 0.f)
                     : make_float4(P.C1, P.C2, P.mmin, has_c ? P.inv_a : 0.f);
 }
@@ -161,6 +162,7 @@ __global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
     float t_exit;
     int next;
     eval_sample<kFwdSlots, !kLazy && !kDefer>(g, F, cur, near, o, d, b, cache, true, P, t_exit, next);
+    int p_orig = RECORD ? __ldg(g.perm + P.cell) : 0;
     bool has_p = !kLazy && !kDefer;
     float T = 1.f, acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, dep = 0.f;
     int it = 0;
@@ -172,6 +174,7 @@ __global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
         eval_sample<kFwdSlots, !kLazy && !kDefer>(g, F, last ? P.cell : next, last ? far : fmaxf(t_exit, P.t), o, d, b,
                                                   cache, !last, Q, t_exit_q, next_q);
         bool has_q = !kLazy && !kDefer;
+        const int q_orig = RECORD ? __ldg(g.perm + Q.cell) : 0;
         ++n_samples;
         const float delta = Q.t - P.t;
         const float alpha = 1.f - __expf(-0.5f * (P.sigma + Q.sigma) * delta);
@@ -192,16 +195,17 @@ __global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
             ++n_color;
         }
         T *= 1.f - alpha;
-        if (RECORD) store_sample(out.rec, r, K, n_samples - 2, P, has_p, kDefer, g.perm);
+        if (RECORD) store_sample(out.rec, r, K, n_samples - 2, P, has_p, kDefer, p_orig);
         if (kDefer && has_p && n_samples - 2 < K && c.cm_count != nullptr)
             atomicAdd(c.cm_count + (r / c.cm_rays) * c.cm_stride + P.cell, 1);
         P = Q;
+        p_orig = q_orig;
         has_p = has_q;
         t_exit = t_exit_q, next = next_q;
         if (last || T < c.t_thresh) break;
     }
     if (it == kMaxCells) err |= kErrCellCap;
-    if (RECORD) store_sample(out.rec, r, K, n_samples - 1, P, has_p, kDefer, g.perm);
+    if (RECORD) store_sample(out.rec, r, K, n_samples - 1, P, has_p, kDefer, p_orig);
     if (kDefer && has_p && n_samples - 1 < K && c.cm_count != nullptr)
         atomicAdd(c.cm_count + (r / c.cm_rays) * c.cm_stride + P.cell, 1);
     if (!kDefer) out.rgb[3 * r] = acc0, out.rgb[3 * r + 1] = acc1, out.rgb[3 * r + 2] = acc2;
@@ -378,19 +382,33 @@ __global__ void __launch_bounds__(kBlock)
 //   (gs, gC r, gC g, gC b) | (gC . C, m_min, 1 / sum of colour weights or 0, bits(cell) or -1)
 // Direct form (VG_BWD_DIRECT): 64 bytes at the sample's place in its cell's bucket,
 //   (x, gs) | (gC, gC . C) | (m_min, 1 / sum of colour weights or 0, 0, 0) | (d, 0)
-// where every recorded sample gets an item (zero gradients for the samples that have none).
-__device__ __forceinline__ void emit_item_direct(float4* __restrict__ items, const int* __restrict__ offsets,
-                                                 int* __restrict__ fill, const Sample& P, float gs, float gC0,
-                                                 float gC1, float gC2, bool has_c, const float (&d)[3]) {
-    const bool do_c = has_c && (gC0 != 0.f || gC1 != 0.f || gC2 != 0.f);
-    const int64_t pos = __ldg(offsets + P.cell) + atomicAdd(fill + P.cell, 1);
-    float4* it = items + 4 * pos;
-    const float gCC = do_c ? gC0 * P.C0 + gC1 * P.C1 + gC2 * P.C2 : 0.f;
-    it[0] = make_float4(P.x0, P.x1, P.x2, gs);
-    it[1] = make_float4(do_c ? gC0 : 0.f, do_c ? gC1 : 0.f, do_c ? gC2 : 0.f, gCC);
-    it[2] = make_float4(P.mmin, do_c ? P.inv_a : 0.f, 0.f, 0.f);
-    it[3] = make_float4(d[0], d[1], d[2], 0.f);
-}
+// where every recorded sample gets an item (zero gradients for the samples that have none). The store of
+// an item waits one sample (DirectItems::put writes the previous one) so that the atomic that reserves
+// its place completes while the replay computes the next sample.
+struct DirectItems {
+    float4* items;
+    const int* offsets;
+    int* fill;
+    float4 a, b, c, d;
+    int64_t pos = -1;
+    __device__ __forceinline__ void flush() {
+        if (pos < 0) return;
+        float4* it = items + 4 * pos;
+        it[0] = a, it[1] = b, it[2] = c, it[3] = d;
+    }
+    __device__ __forceinline__ void put(const Sample& P, float gs, float gC0, float gC1, float gC2, bool has_c,
+                                        const float (&dir)[3]) {
+        const bool do_c = has_c && (gC0 != 0.f || gC1 != 0.f || gC2 != 0.f);
+        const int64_t next_pos = __ldg(offsets + P.cell) + atomicAdd(fill + P.cell, 1);
+        flush();
+        const float gCC = do_c ? gC0 * P.C0 + gC1 * P.C1 + gC2 * P.C2 : 0.f;
+        a = make_float4(P.x0, P.x1, P.x2, gs);
+        b = make_float4(do_c ? gC0 : 0.f, do_c ? gC1 : 0.f, do_c ? gC2 : 0.f, gCC);
+        c = make_float4(P.mmin, do_c ? P.inv_a : 0.f, 0.f, 0.f);
+        d = make_float4(dir[0], dir[1], dir[2], 0.f);
+        pos = next_pos;
+    }
+};
 
 __device__ __forceinline__ void emit_item(float4* __restrict__ items, int64_t slot, const Sample& P, float gs,
                                           float gC0, float gC1, float gC2, bool has_c, int* __restrict__ count) {
@@ -463,6 +481,7 @@ __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
     const int lane = threadIdx.x & 31;
     float T = 1.f, acc0 = 0.f, acc1 = 0.f, acc2 = 0.f;
     float gs_pending = 0.f, gP0 = 0.f, gP1 = 0.f, gP2 = 0.f;  // gradients of P from the segment before it
+    DirectItems out_items{io.items, io.offsets, io.fill};
     int n_done = 0;  // index of P
     for (int it = 0; it < kMaxCells; ++it) {
         Sample Q;
@@ -497,8 +516,7 @@ __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
         const float h0 = active ? 0.5f * w * gR0 : 0.f, h1 = active ? 0.5f * w * gR1 : 0.f,
                     h2 = active ? 0.5f * w * gR2 : 0.f;
         if (MODE == kItems && VG_BWD_DIRECT)
-            emit_item_direct(io.items, io.offsets, io.fill, P, gs_pending + 0.5f * g_sbar, gP0 + h0, gP1 + h1,
-                             gP2 + h2, has_p, d);
+            out_items.put(P, gs_pending + 0.5f * g_sbar, gP0 + h0, gP1 + h1, gP2 + h2, has_p, d);
         else if (MODE == kItems)
             emit_item(io.items, (r - io.r0) * K + it, P, gs_pending + 0.5f * g_sbar, gP0 + h0, gP1 + h1, gP2 + h2,
                       has_p, io.count);
@@ -517,15 +535,16 @@ __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
         if (last || T < c.t_thresh) break;
     }
     if (MODE == kItems && VG_BWD_DIRECT) {
-        emit_item_direct(io.items, io.offsets, io.fill, P, gs_pending, gP0, gP1, gP2, has_p, d);
+        out_items.put(P, gs_pending, gP0, gP1, gP2, has_p, d);
         // every recorded sample was counted into its bucket: fill the places of any the replay did not
         // reach with zero-gradient items (the replay follows the forward, so normally there are none)
         for (int s = n_done + 1; s < n_stored; ++s) {
             Sample Z;
             bool has_z;
             load_sample(gi.rec, r, K, s, o, d, g.inv, Z, has_z);
-            emit_item_direct(io.items, io.offsets, io.fill, Z, 0.f, 0.f, 0.f, 0.f, false, d);
+            out_items.put(Z, 0.f, 0.f, 0.f, 0.f, false, d);
         }
+        out_items.flush();
     } else if (MODE == kItems) {
         emit_item(io.items, (r - io.r0) * K + n_done, P, gs_pending, gP0, gP1, gP2, has_p, io.count);
     }
