@@ -183,8 +183,22 @@ def run_b200(args):
     torch.cuda.set_device(local)
     dev = torch.device('cuda', local)
     prm = scenes.make_params(args.config, gr['points'].astype(np.float64))
-    centre, o_h, d_h = camera(args.config, rank, W, H, dev)
-    start_site = int(sites.nearest_sites(gr['points'], centre[None])[0])
+    if world == 1:
+        centre, o_h, d_h = camera(args.config, 0, W, H, dev)
+        start_site = int(sites.nearest_sites(gr['points'], centre[None])[0])
+        start_h = torch.full((len(o_h),), start_site, dtype=torch.int32)
+    else:
+        # N views, 16x16 tiles of each dealt round-robin over the ranks (rank r takes the tiles t of view v
+        # with t = r - v mod N): every rank renders one view's worth of rays from the same mix of views
+        o_l, d_l, s_l = [], [], []
+        for v in range(world):
+            centre, c2w = scenes.orbit_camera(v, 8)
+            o_v, d_v = scenes.camera_rays(centre, c2w, W, H, cfgd['fov'])
+            pix = torch.from_numpy(vdist.tile_pixels(H, W, world, (rank - v) % world))
+            o_l.append(o_v[pix]), d_l.append(d_v[pix])
+            s_l.append(torch.full((len(pix),), int(sites.nearest_sites(gr['points'], centre[None])[0]),
+                                  dtype=torch.int32))
+        o_h, d_h, start_h = torch.cat(o_l).contiguous(), torch.cat(d_l).contiguous(), torch.cat(s_l)
     B = len(o_h)
     gen = torch.Generator().manual_seed(0)
     target_h = torch.rand(B, 3, generator=gen)
@@ -199,7 +213,7 @@ def run_b200(args):
     nb = (model.sh_deg + 1) ** 2
 
     o, d = o_h.to(dev), d_h.to(dev)
-    start = torch.full((B,), start_site, dtype=torch.int32, device=dev)
+    start = start_h.to(dev)
     target = target_h.to(dev)
     timing = {'fwd': [], 'bwd': []}
     last = {}
@@ -276,7 +290,7 @@ def run_b200(args):
 
     # ---- end to end: pinned host inputs in, loss out, every step
     o_p, d_p, t_p = o_h.pin_memory(), d_h.pin_memory(), target_h.pin_memory()
-    s_p = torch.full((B,), start_site, dtype=torch.int32).pin_memory()
+    s_p = start_h.pin_memory()
     loss_h = torch.empty((), dtype=torch.float32).pin_memory()
     h2d = o_p.numel() * 4 + d_p.numel() * 4 + t_p.numel() * 4 + s_p.numel() * 4
     torch.cuda.synchronize()
@@ -308,10 +322,11 @@ def run_b200(args):
         'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(ms, 3),
         'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
         'config': {'workload': f'config{args.config}: {len(gr["points"])} sites ({cfgd["kind"]}), SH deg '
-                               f'{model.sh_deg}, {W}x{H} view per GPU, training step (fwd+bwd+Adam), record_cap '
+                               f'{model.sh_deg}, {W}x{H} rays per GPU, training step (fwd+bwd+Adam), record_cap '
                                f'{RECORD_CAP}, t/w_thresh {T_THRESH:g}',
-                   'rays_per_gpu': B, 'sites': len(gr['points']), 'parallelism': f'dp{world} (view per GPU, '
-                   'NCCL all-reduce of site gradients)' if world > 1 else 'single GPU',
+                   'rays_per_gpu': B, 'sites': len(gr['points']),
+                   'parallelism': f'dp{world} (16x16 tiles of {world} views dealt over the GPUs, NCCL all-reduce of '
+                                  'site gradients)' if world > 1 else 'single GPU',
                    'l2': 'inputs larger than L2 (scene records + adjacency ~1 GB read every step)'},
         'fps': round(1000.0 / ms, 3), 'fwd_ms': round(fwd_ms, 3), 'bwd_ms': round(bwd_ms, 3),
         'fwd_mrays_s': round(B / (fwd_ms * 1e-3) / 1e6, 3), 'samples_per_ray': round(samples_per_ray, 2),
