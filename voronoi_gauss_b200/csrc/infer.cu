@@ -17,6 +17,11 @@ namespace {
 
 constexpr int kBlock = 128;
 constexpr int kCache = 8;
+// unroll factor of the per-cell edge loop (loads of later edges issued before earlier arithmetic)
+#ifndef VG_INFER_UNROLL
+#define VG_INFER_UNROLL 1
+#endif
+constexpr int kInferUnroll = VG_INFER_UNROLL;
 constexpr int kLazy = 0, kBaked = 1, kFused = 2;
 
 struct Net {
@@ -122,6 +127,7 @@ __device__ __forceinline__ void eval_cell(const Net& N, const InferCfg& M, int c
     const int e0 = __ldg(N.offsets + c), e1 = __ldg(N.offsets + c + 1);
     out.sigma = 0.f, out.mmin = kInf, out.t_exit = kInf, out.next = INT_MAX;
     blend_init(out.B);
+#pragma unroll kInferUnroll
     for (int e = e0; e < e1; ++e) {
         const float4 ed = __ldg(N.edge + e);
         const int k = __ldg(N.nbr + e);
