@@ -6,8 +6,8 @@
 
 #include "vg_common.cuh"
 
-// VG_SAMPLE_UNROLL  unroll factor of the neighbour loop of eval_sample (loads of later neighbours can
-//                   then be issued before the arithmetic of earlier ones)
+// VG_SAMPLE_UNROLL  unroll factor of the neighbour loops of eval_sample / eval_density
+//                   (loads of later neighbours can then be issued before the arithmetic of earlier ones)
 #ifndef VG_SAMPLE_UNROLL
 #define VG_SAMPLE_UNROLL 4
 #endif
@@ -72,6 +72,7 @@ __device__ __forceinline__ float eval_density(const GraphView& g, const FieldVie
                                               float x2) {
     const int e0 = __ldg(g.off + cell), e1 = __ldg(g.off + cell + 1);
     float sigma = 0.f;
+#pragma unroll kSampleUnroll
     for (int e = e0; e < e1; ++e) {
         const float4 E = __ldg(g.edge + e);
         const int j = site_of(E);
