@@ -69,3 +69,31 @@ def test_python_layer_rejects_cpu_tensors():
     x = torch.zeros(4, 3)
     with pytest.raises(RuntimeError, match='must be a CUDA tensor'):
         ext.extension().conic_forward(x, torch.zeros(4, 4), 0.0)
+
+
+def test_host_side_argument_errors_of_the_field_packing_and_scene_entry_points(lib):
+    """The field, packing and scene-preparation entry points validate on the host too."""
+    null = None
+    buf = ctypes.create_string_buffer(256)
+    p = ctypes.addressof(buf)
+    rc = lib.vg_walk(null, 10, 10, p, p, p, p, 1, 4, p, p, null)
+    assert rc == 1 and b'graph pack is null' in lib.vg_last_error()
+    assert lib.vg_field_workspace_bytes(10, 3, 7, 0) == 0
+    assert lib.vg_field_workspace_bytes(10, 3, 3, 1000) > lib.vg_field_workspace_bytes(10, 3, 3, 0) > 0
+    rc = lib.vg_density_forward(p, 10, 10, p, p, p, p, p, 5, 1.0, p, null, 0, null)
+    assert rc == 2 and b'workspace' in lib.vg_last_error()
+    rc = lib.vg_color_forward(p, 10, 10, p, p, p, 4, p, p, p, 5, p, p, 1 << 20, null)
+    assert rc == 1 and b'sh_deg' in lib.vg_last_error()
+    k = (ctypes.c_float * 9)(1, 0, 0, 0.5, 1, 0, 0, 0, 1)  # not the inverse of a pinhole intrinsic matrix
+    r = (ctypes.c_float * 9)(1, 0, 0, 0, 1, 0, 0, 0, 1)
+    c = (ctypes.c_float * 3)(0, 0, 0)
+    rc = lib.vg_camera_rays(k, r, c, 4, 4, 4, 8, p, p, null)
+    assert rc == 1 and b'K_inv' in lib.vg_last_error()
+    rc = lib.vg_nearest_sites(null, 10, 10, p, 3, p, null)
+    assert rc == 1 and b'graph pack is null' in lib.vg_last_error()
+    ws = lib.vg_infer_pack_workspace_bytes(10)
+    rc = lib.vg_infer_pack(null, 10, 10, p, p, p, p, p, p, p, p, p, 0.0, 0.0, 0, 1, p, p, p, p, p, p, p, p, p, ws,
+                           null)
+    assert rc == 1 and b'reorder' in lib.vg_last_error()
+    rc = lib.vg_bake_colors(p, p, 5, 10, 0.0, 0.0, 0.0, p, null)
+    assert rc == 1 and b'sh_deg' in lib.vg_last_error()
