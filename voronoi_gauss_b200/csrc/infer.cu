@@ -19,7 +19,7 @@ constexpr int kBlock = 128;
 constexpr int kCache = 8;
 // unroll factor of the per-cell edge loop (loads of later edges issued before earlier arithmetic)
 #ifndef VG_INFER_UNROLL
-#define VG_INFER_UNROLL 1
+#define VG_INFER_UNROLL 2
 #endif
 constexpr int kInferUnroll = VG_INFER_UNROLL;
 constexpr int kLazy = 0, kBaked = 1, kFused = 2;
