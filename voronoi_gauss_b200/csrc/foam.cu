@@ -161,10 +161,7 @@ __global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
     Sample P;
     float t_exit;
     int next;
-    constexpr bool kRun = VG_EDGE_RUN != 0;
-    int2 run_p = make_int2(__ldg(g.off + cur), __ldg(g.off + cur + 1)), run_next = make_int2(0, 0);
-    eval_sample<kFwdSlots, !kLazy && !kDefer, kRun>(g, F, cur, near, o, d, b, cache, true, P, t_exit, next, run_p,
-                                                    &run_next);
+    eval_sample<kFwdSlots, !kLazy && !kDefer>(g, F, cur, near, o, d, b, cache, true, P, t_exit, next);
     int p_orig = RECORD ? __ldg(g.perm + P.cell) : 0;
     bool has_p = !kLazy && !kDefer;
     float T = 1.f, acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, dep = 0.f;
@@ -174,10 +171,8 @@ __global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
         Sample Q;
         float t_exit_q;
         int next_q;
-        const int2 run_q = last ? run_p : run_next;
-        eval_sample<kFwdSlots, !kLazy && !kDefer, kRun>(g, F, last ? P.cell : next, last ? far : fmaxf(t_exit, P.t), o,
-                                                        d, b, cache, !last, Q, t_exit_q, next_q, run_q, &run_next);
-        run_p = run_q;
+        eval_sample<kFwdSlots, !kLazy && !kDefer>(g, F, last ? P.cell : next, last ? far : fmaxf(t_exit, P.t), o, d, b,
+                                                  cache, !last, Q, t_exit_q, next_q);
         bool has_q = !kLazy && !kDefer;
         const int q_orig = RECORD ? __ldg(g.perm + Q.cell) : 0;
         ++n_samples;

@@ -1,8 +1,7 @@
 // Layout transforms around the traversal kernels (see vg_common.cuh for the formats).
 //
 //   graph_pack  points (N, 3), CSR offsets (N + 1), adj (M) in original order
-//               -> Morton-ordered self-first neighbourhoods of float4 (p_j, internal j), and for every
-//               edge the edge run of its site (the traversal then starts a cell without reading off)
+//               -> Morton-ordered self-first neighbourhoods of float4 (p_j, internal j)
 //               Morton codes: 10 bits per axis of the points' bounding box, the quantisation of
 //               render.py:168-176 (morton_order), sorted stably so equal codes keep index order.
 //   field_pack  raw (N), dA (N, 6), cA (N, 6), sh (N, 16, 3) -> 64-byte site records + packed SH
@@ -20,7 +19,7 @@ constexpr int kBlock = 256;
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct PackLayout {
-    size_t perm, inv, off, edge, run, bbox, keys_in, keys_out, vals_in, sizes, temp, temp_bytes, total;
+    size_t perm, inv, off, edge, bbox, keys_in, keys_out, vals_in, sizes, temp, temp_bytes, total;
 };
 
 // Byte offsets of the sections of a graph pack; the CUB scratch comes last, so the views (with_temp =
@@ -37,7 +36,6 @@ PackLayout layout(int64_t n, int64_t m, bool with_temp) {
     L.inv = take(4 * n);
     L.off = take(4 * (n + 1));
     L.edge = take(16 * (n + m));
-    L.run = take(8 * (n + m));
     L.bbox = take(32);
     L.keys_in = take(4 * n);
     L.keys_out = take(4 * n);
@@ -128,21 +126,18 @@ __global__ void __launch_bounds__(kBlock)
 __global__ void __launch_bounds__(kBlock)
     edge_kernel(const float* __restrict__ p, const int* __restrict__ offsets, const int* __restrict__ adj,
                 const int* __restrict__ perm, const int* __restrict__ inv, const int* __restrict__ off, int n,
-                float4* __restrict__ edge, int2* __restrict__ run) {
+                float4* __restrict__ edge) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const int o = perm[i];
     const int64_t base = off[i];
     const int64_t o3 = 3 * static_cast<int64_t>(o);
     edge[base] = make_float4(p[o3], p[o3 + 1], p[o3 + 2], __int_as_float(i));
-    run[base] = make_int2(off[i], off[i + 1]);
     const int a0 = offsets[o], a1 = offsets[o + 1];
     for (int e = a0; e < a1; ++e) {
         const int j = adj[e];
         const int64_t j3 = 3 * static_cast<int64_t>(j);
-        const int jj = inv[j];
-        edge[base + 1 + (e - a0)] = make_float4(p[j3], p[j3 + 1], p[j3 + 2], __int_as_float(jj));
-        run[base + 1 + (e - a0)] = make_int2(off[jj], off[jj + 1]);
+        edge[base + 1 + (e - a0)] = make_float4(p[j3], p[j3 + 1], p[j3 + 2], __int_as_float(inv[j]));
     }
 }
 
@@ -207,8 +202,7 @@ GraphView graph_view(const void* pack, int64_t n, int64_t m) {
     const PackLayout L = layout(n, m, false);
     const char* b = static_cast<const char*>(pack);
     return {reinterpret_cast<const int*>(b + L.perm), reinterpret_cast<const int*>(b + L.inv),
-            reinterpret_cast<const int*>(b + L.off), reinterpret_cast<const float4*>(b + L.edge), static_cast<int>(n),
-            reinterpret_cast<const int2*>(b + L.run)};
+            reinterpret_cast<const int*>(b + L.off), reinterpret_cast<const float4*>(b + L.edge), static_cast<int>(n)};
 }
 
 cudaError_t graph_pack(const float* points, const int* offsets, const int* adj, int64_t n, int64_t m, void* pack,
@@ -220,7 +214,6 @@ cudaError_t graph_pack(const float* points, const int* offsets, const int* adj, 
     int* inv = reinterpret_cast<int*>(b + L.inv);
     int* off = reinterpret_cast<int*>(b + L.off);
     float4* edge = reinterpret_cast<float4*>(b + L.edge);
-    int2* run = reinterpret_cast<int2*>(b + L.run);
     int* bb = reinterpret_cast<int*>(b + L.bbox);
     unsigned* kin = reinterpret_cast<unsigned*>(b + L.keys_in);
     unsigned* kout = reinterpret_cast<unsigned*>(b + L.keys_out);
@@ -238,7 +231,7 @@ cudaError_t graph_pack(const float* points, const int* offsets, const int* adj, 
     tb = L.temp_bytes;
     err = cub::DeviceScan::ExclusiveSum(temp, tb, sizes, off, N + 1, st);
     if (err != cudaSuccess) return err;
-    edge_kernel<<<blocks(n), kBlock, 0, st>>>(points, offsets, adj, perm, inv, off, N, edge, run);
+    edge_kernel<<<blocks(n), kBlock, 0, st>>>(points, offsets, adj, perm, inv, off, N, edge);
     return cudaGetLastError();
 }
 

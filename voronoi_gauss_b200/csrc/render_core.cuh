@@ -11,11 +11,6 @@
 #ifndef VG_SAMPLE_UNROLL
 #define VG_SAMPLE_UNROLL 4
 #endif
-// VG_EDGE_RUN  1: the forward traversal enters each next cell through the edge run read with its exit
-//              face (GraphView::run) instead of reading the CSR offsets after the choice
-#ifndef VG_EDGE_RUN
-#define VG_EDGE_RUN 1
-#endif
 
 namespace vg {
 
@@ -32,18 +27,15 @@ struct Sample {
 // Density sum_k exp(min(raw_k, 30) - v^T dA_k v / 2) over {cell} U adj(cell) (foam.cu:211-221), with
 // COLOR the colour blend of the neighbourhood (foam.cu:224-249, one online pass) and, when want_exit,
 // the exit face of the cell along the ray (foam.cu:185-209; next = -1 when unbounded ahead).
-// RUN: the cell's edge run is given (run_here, from the previous cell's exit face) and the run of the
-// next cell is returned in *run_next, read with the exit-face candidates (GraphView::run).
-template <int SLOTS, bool COLOR, bool RUN = false>
+template <int SLOTS, bool COLOR>
 __device__ __forceinline__ void eval_sample(const GraphView& g, const FieldView& F, int cell, float t,
                                             const float (&o)[3], const float (&d)[3], const float (&b)[16],
                                             ColorCache<SLOTS>& cache, bool want_exit, Sample& S, float& t_exit,
-                                            int& next, int2 run_here = make_int2(0, 0), int2* run_next = nullptr) {
+                                            int& next) {
     S.t = t;
     S.x0 = along(o[0], t, d[0]), S.x1 = along(o[1], t, d[1]), S.x2 = along(o[2], t, d[2]);
     S.cell = cell;
-    const int e0 = RUN ? run_here.x : __ldg(g.off + cell), e1 = RUN ? run_here.y : __ldg(g.off + cell + 1);
-    int2 best_run = make_int2(0, 0);
+    const int e0 = __ldg(g.off + cell), e1 = __ldg(g.off + cell + 1);
     const float4 Pc = __ldg(g.edge + e0);
     float sigma = 0.f;
     Blend B;
@@ -53,12 +45,7 @@ __device__ __forceinline__ void eval_sample(const GraphView& g, const FieldView&
     for (int e = e0; e < e1; ++e) {
         const float4 E = e == e0 ? Pc : __ldg(g.edge + e);
         const int j = site_of(E);
-        if (want_exit && e > e0) {
-            const int2 rn = RUN ? __ldg(g.run + e) : make_int2(0, 0);
-            const int before = next;
-            exit_candidate(E, Pc.x, Pc.y, Pc.z, o, d, t_exit, next, g.perm);
-            if (RUN && next != before) best_run = rn;
-        }
+        if (want_exit && e > e0) exit_candidate(E, Pc.x, Pc.y, Pc.z, o, d, t_exit, next, g.perm);
         const float v0 = S.x0 - E.x, v1 = S.x1 - E.y, v2 = S.x2 - E.z;
         const float4* r = F.rec + kFieldVec * static_cast<int64_t>(j);
         const float4 r0 = __ldg(r), r1 = __ldg(r + 1);
@@ -71,7 +58,6 @@ __device__ __forceinline__ void eval_sample(const GraphView& g, const FieldView&
         }
     }
     S.sigma = sigma;
-    if (RUN) *run_next = best_run;
     if (COLOR) {
         S.mmin = B.m;
         S.inv_a = 1.f / B.a;

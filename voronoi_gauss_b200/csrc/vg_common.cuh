@@ -9,8 +9,6 @@
 //     edge  (N + M)  float4 (p_j.x, p_j.y, p_j.z, bits(internal j)); the first edge of a cell is the
 //                    cell's own site, so one pass over 16-byte records gives the site, its Delaunay
 //                    neighbours and their positions (exit faces, walks and neighbourhood sums)
-//     run   (N + M)  int2 (off[j], off[j + 1]) of the site j of each edge: the traversal reads it with
-//                    the exit-face candidates and enters the next cell without a dependent read of off
 //   field pack (per call, internal order)
 //     rec   (N, 4) float4: (dA xx, xy, xz, yy), (dA yz, zz, min(raw, 30), 0),
 //                          (cA xx, xy, xz, yy), (cA yz, zz, 0, 0)          64 B per site
@@ -54,7 +52,6 @@ struct GraphView {
     const int* off;
     const float4* edge;
     int n;
-    const int2* run;  // (N + M): the edge run [off[j], off[j + 1]) of the site j of every edge
 };
 
 struct FieldView {
