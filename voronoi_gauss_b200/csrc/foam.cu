@@ -41,10 +41,6 @@
 #ifndef VG_BWD_MINB
 #define VG_BWD_MINB 1
 #endif
-// VG_ITEMS_MINB  the same for the record replay that writes the cell-major items
-#ifndef VG_ITEMS_MINB
-#define VG_ITEMS_MINB 1
-#endif
 // VG_CM_CHUNK  samples of one cell per warp in the cell-major passes (32 or 64; 64 = two per lane in
 //              the colour pass), which sets how often a cell's neighbourhood is reloaded
 #ifndef VG_CM_CHUNK
@@ -116,24 +112,6 @@ __device__ __forceinline__ void load_sample(const float* __restrict__ rec, int64
                                             Sample& P, bool& has_c) {
     const float4* q = reinterpret_cast<const float4*>(rec + (r * K + s) * kRecord);
     const float4 a = __ldg(q), b = __ldg(q + 1);
-    P.t = a.x;
-    P.x0 = along(o[0], P.t, d[0]), P.x1 = along(o[1], P.t, d[1]), P.x2 = along(o[2], P.t, d[2]);
-    P.cell = __ldg(inv + __float_as_int(a.y));
-    P.sigma = a.z;
-    P.C0 = a.w, P.C1 = b.x, P.C2 = b.y, P.mmin = b.z, P.inv_a = b.w;
-    has_c = P.inv_a > 0.f;
-}
-
-// load_sample in two halves: the record's two vectors (issued ahead of use) and their decoding.
-__device__ __forceinline__ void fetch_record(const float* __restrict__ rec, int64_t r, int K, int s, float4& a,
-                                             float4& b) {
-    const float4* q = reinterpret_cast<const float4*>(rec + (r * K + s) * kRecord);
-    a = __ldg(q), b = __ldg(q + 1);
-}
-
-__device__ __forceinline__ void decode_record(const float4& a, const float4& b, const float (&o)[3],
-                                              const float (&d)[3], const int* __restrict__ inv, Sample& P,
-                                              bool& has_c) {
     P.t = a.x;
     P.x0 = along(o[0], P.t, d[0]), P.x1 = along(o[1], P.t, d[1]), P.x2 = along(o[2], P.t, d[2]);
     P.cell = __ldg(inv + __float_as_int(a.y));
@@ -461,7 +439,7 @@ struct ItemOut {
 };
 
 template <int MODE>
-__global__ void __launch_bounds__(kBlock, MODE == kItems ? VG_ITEMS_MINB : VG_BWD_MINB)
+__global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
     foam_backward_kernel(GraphView g, FieldView F, RayView R, FoamCfg c, GradIn gi, float* __restrict__ grad,
                          ItemOut io, int* status) {
     __shared__ float4 cache_mem[kBwdSlotMem];
@@ -504,9 +482,6 @@ __global__ void __launch_bounds__(kBlock, MODE == kItems ? VG_ITEMS_MINB : VG_BW
     float T = 1.f, acc0 = 0.f, acc1 = 0.f, acc2 = 0.f;
     float gs_pending = 0.f, gP0 = 0.f, gP1 = 0.f, gP2 = 0.f;  // gradients of P from the segment before it
     DirectItems out_items{io.items, io.offsets, io.fill};
-    // replay: the record of the sample after Q is fetched one iteration ahead
-    float4 ra = make_float4(0.f, 0.f, 0.f, 0.f), rb = ra;
-    if (n_stored > 1) fetch_record(gi.rec, r, K, 1, ra, rb);
     int n_done = 0;  // index of P
     for (int it = 0; it < kMaxCells; ++it) {
         Sample Q;
@@ -515,9 +490,7 @@ __global__ void __launch_bounds__(kBlock, MODE == kItems ? VG_ITEMS_MINB : VG_BW
         int next_q = -1;
         if (n_stored > 0) {
             if (it + 1 >= n_stored) break;
-            const float4 qa = ra, qb = rb;
-            if (it + 2 < n_stored) fetch_record(gi.rec, r, K, it + 2, ra, rb);
-            decode_record(qa, qb, o, d, g.inv, Q, has_q);
+            load_sample(gi.rec, r, K, it + 1, o, d, g.inv, Q, has_q);
             last = it + 2 >= n_stored;
         } else {
             last = next < 0 || t_exit >= far;
