@@ -41,6 +41,13 @@
 #ifndef VG_BWD_MINB
 #define VG_BWD_MINB 1
 #endif
+// VG_COLOR_MINB / VG_SCATTER_MINB  the same for cmf_color_kernel and cm_scatter_kernel
+#ifndef VG_COLOR_MINB
+#define VG_COLOR_MINB 1
+#endif
+#ifndef VG_SCATTER_MINB
+#define VG_SCATTER_MINB 3
+#endif
 // VG_CM_CHUNK  samples of one cell per warp in the cell-major passes (32 or 64; 64 = two per lane in
 //              the colour pass), which sets how often a cell's neighbourhood is reloaded
 #ifndef VG_CM_CHUNK
@@ -262,7 +269,7 @@ __global__ void __launch_bounds__(kBlock)
 }
 
 template <int S4>
-__global__ void __launch_bounds__(kBlock)
+__global__ void __launch_bounds__(kBlock, VG_COLOR_MINB)
     cmf_color_kernel(GraphView g, FieldView F, RayView R, float* __restrict__ rec, int K,
                      const int* __restrict__ order, const int4* __restrict__ chunks, const int* __restrict__ n_chunks_ptr,
                      int64_t r0) {
@@ -777,7 +784,7 @@ __device__ __forceinline__ void balanced_scatter(const GraphView& g, const Field
 enum StageMode { kBucketed = 0, kIndexed = 1, kRecords = 2 };
 
 template <int S4, int STAGE>
-__global__ void __launch_bounds__(kBlock, 3)
+__global__ void __launch_bounds__(kBlock, VG_SCATTER_MINB)
     cm_scatter_kernel(GraphView g, FieldView F, RayView R, const float* __restrict__ rec, int K,
                       const float4* __restrict__ items, const int* __restrict__ order, const int4* __restrict__ chunks,
                       const int* __restrict__ n_chunks_ptr, int64_t r0, float* __restrict__ grad) {
