@@ -18,6 +18,9 @@ the reference's float64 restatements:
                      trace + compositing + sparse gradients.
 * ckpt_small.pth   - a checkpoint written in train.py's format (train.py:168-170) from the reference's
                      own VoronoiGaussField (model.py:19-59), 300 sites, randomised parameters.
+* render_host.npz  - the proposal sampler's host arithmetic on 256 seeded rays: render.ray_bounds,
+                     s_to_t, composite, sample_pdf (stratified and the bin edges of resample) and
+                     resample (render.py:16-74), float32 as the reference computes them.
 * field_small.npz  - test_grad.py's setup (400 uniform sites, rng(0)): exact nearest sites (cKDTree) of
                      sorted ray samples for the walk, and the float64 density / colour fields with
                      their autograd gradients (test_grad.py:45-125).
@@ -314,12 +317,31 @@ def make_ckpt_small():
                os.path.join(HERE, 'ckpt_small.pth'))
 
 
+def make_render_host():
+    g = torch.Generator().manual_seed(11)
+    B, S = 256, 64
+    o = torch.randn(B, 3, generator=g) * 1.5
+    d = torch.nn.functional.normalize(torch.randn(B, 3, generator=g), dim=-1)
+    near, mid, far = ref_render.ray_bounds(o, d, 0.02, 4.0)
+    s = torch.linspace(0, 1, S + 1)[:-1].expand(B, S) + torch.rand(B, S, generator=g) / S
+    t = ref_render.s_to_t(s, near, mid, far)
+    sigma = torch.rand(B, S, generator=g) * 20 * (torch.rand(B, S, generator=g) < 0.3)
+    w, T = ref_render.composite(sigma, t, far)
+    bins = torch.sort(torch.rand(B, S + 1, generator=g), 1)[0]
+    pdf_det = ref_render.sample_pdf(bins, w[:, :S], 48, det=True)
+    s_new = ref_render.resample(s, w, 64, det=True)
+    out = {k: v.numpy() for k, v in dict(o=o, d=d, near=near, mid=mid, far=far, s=s, t=t, sigma=sigma, w=w, T=T,
+                                          bins=bins, pdf_det=pdf_det, s_new=s_new).items()}
+    np.savez_compressed(os.path.join(HERE, 'render_host.npz'), **out)
+
+
+MAKERS = {'sh_basis': make_sh_basis, 'conic': make_conic, 'foam_small': make_foam_small,
+          'march_small': make_march_small, 'foam_config1': make_foam_config1, 'field_small': make_field_small,
+          'ckpt_small': make_ckpt_small, 'render_host': make_render_host}
+
 if __name__ == '__main__':
-    make_sh_basis()
-    make_conic()
-    make_foam_small()
-    make_march_small()
-    make_foam_config1()
-    make_field_small()
-    make_ckpt_small()
+    # python make_golden.py [name ...]: only the named fixtures (default all)
+    for name in sys.argv[1:] or list(MAKERS):
+        MAKERS[name]()
     print('fixtures written to', HERE)
+
