@@ -198,13 +198,13 @@ def run_b200(args):
         start_site = int(sites.nearest_sites(gr['points'], centre[None])[0])
         start_h = torch.full((len(o_h),), start_site, dtype=torch.int32)
     else:
-        # N views, 16x16 tiles of each dealt round-robin over the ranks (rank r takes the tiles t of view v
-        # with t = r - v mod N): every rank renders one view's worth of rays from the same mix of views
+        # N views, 16x16 tiles of each dealt round-robin over the ranks (dist.view_tile_pixels): every rank
+        # renders one view's worth of rays from the same mix of views
         o_l, d_l, s_l = [], [], []
-        for v in range(world):
+        for v, pix in enumerate(vdist.view_tile_pixels(H, W, world, rank)):
             centre, c2w = scenes.orbit_camera(v, 8)
             o_v, d_v = scenes.camera_rays(centre, c2w, W, H, cfgd['fov'])
-            pix = torch.from_numpy(vdist.tile_pixels(H, W, world, (rank - v) % world))
+            pix = torch.from_numpy(pix)
             o_l.append(o_v[pix]), d_l.append(d_v[pix])
             s_l.append(torch.full((len(pix),), int(sites.nearest_sites(gr['points'], centre[None])[0]),
                                   dtype=torch.int32))

@@ -102,3 +102,16 @@ def test_tile_pixels_partition_image():
         assert len(allp) == H * W and len(np.unique(allp)) == H * W
         sizes = [len(p) for p in parts]
         assert max(sizes) - min(sizes) <= 2 * 16 * 16  # at most two tiles apart (ragged edge tiles)
+
+
+def test_view_tile_pixels_cover_every_view_once():
+    from voronoi_gauss_b200 import dist as vdist
+    H, W = 70, 90
+    for world in (1, 2, 4, 8):
+        per_rank = [vdist.view_tile_pixels(H, W, world, r) for r in range(world)]
+        for v in range(world):
+            allp = np.concatenate([per_rank[r][v] for r in range(world)])
+            assert len(allp) == H * W and len(np.unique(allp)) == H * W
+        sizes = [sum(len(p) for p in views) for views in per_rank]
+        # every rank renders about one view's worth of rays
+        assert max(sizes) - min(sizes) <= 2 * world * 16 * 16 and abs(sum(sizes) - world * H * W) == 0

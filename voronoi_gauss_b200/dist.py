@@ -37,6 +37,14 @@ def tile_pixels(H, W, world, rank, tile=TILE):
     return np.concatenate(out) if out else np.zeros(0, np.int64)
 
 
+def view_tile_pixels(H, W, world, rank, tile=TILE):
+    """Weak-scaling deal of `world` views over `world` ranks: the 16x16 tiles of view v go to the ranks
+    as by ``tile_pixels`` shifted by v (rank r takes the tiles t of view v with t = r - v mod world), so
+    every rank renders one view's worth of rays from the same mix of views. Returns one pixel-index
+    array per view."""
+    return [tile_pixels(H, W, world, (rank - v) % world, tile) for v in range(world)]
+
+
 def allreduce_grads(params, group=None):
     """Sums the .grad of `params` over the ranks, in place: one asynchronous all-reduce per gradient
     tensor (the per-site gradients are a few large contiguous tensors, so no flattening copies), then
