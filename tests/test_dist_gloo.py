@@ -115,3 +115,48 @@ def test_view_tile_pixels_cover_every_view_once():
         sizes = [sum(len(p) for p in views) for views in per_rank]
         # every rank renders about one view's worth of rays
         assert max(sizes) - min(sizes) <= 2 * world * 16 * 16 and abs(sum(sizes) - world * H * W) == 0
+
+
+def _scene_worker(rank, world, port, q):
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    from voronoi_gauss_b200 import dist as vdist
+    _init(rank, world, port)
+    # rank 0 holds the scene; the others start from different (wrong) copies
+    pts = torch.arange(12.0).view(4, 3) + 100 * rank
+    adj = torch.arange(7, dtype=torch.int32) * (rank + 1)
+    vdist.broadcast_scene([pts, adj])
+    # every rank shades its own tiles with the pixel index; the gathered frame must be arange
+    H, W = 37, 53
+    pix = torch.from_numpy(vdist.tile_pixels(H, W, world, rank))
+    local = torch.stack([pix.float(), -pix.float()], 1)
+    img = vdist.gather_image(local, H, W)
+    q.put((rank, pts.tolist(), adj.tolist(), img.tolist()))
+    dist.destroy_process_group()
+
+
+def test_broadcast_scene_and_gather_image():
+    world, port = 2, _port()
+    ctx = mp.get_context('spawn')
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_scene_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(60)
+        assert p.exitcode == 0
+    ref = torch.arange(37 * 53, dtype=torch.float32).view(37, 53)
+    for rank, pts, adj, img in res:
+        assert pts == (torch.arange(12.0).view(4, 3)).tolist()
+        assert adj == torch.arange(7).tolist()
+        img = torch.tensor(img)
+        assert torch.equal(img[..., 0], ref) and torch.equal(img[..., 1], -ref)
+
+
+def test_gather_image_single_process():
+    from voronoi_gauss_b200 import dist as vdist
+    H, W = 20, 33
+    pix = torch.from_numpy(vdist.tile_pixels(H, W, 1, 0))
+    img = vdist.gather_image(pix.float()[:, None], H, W)
+    assert torch.equal(img[..., 0], torch.arange(H * W, dtype=torch.float32).view(H, W))

@@ -2,10 +2,11 @@
 
 Rays are independent, so rendering shards with no data-path communication: an image is cut into 16x16
 pixel tiles dealt round-robin to the ranks (``tile_pixels``), or every rank renders its own view. The
-scene (sites, adjacency, parameters) is replicated on every GPU. The one exchange step is in training:
-the per-site gradients of all ranks are summed before the (replicated) optimizer step, as one coalesced
-NCCL all-reduce over NVLink (``allreduce_grads``). The reference is single-GPU; this layer has no
-counterpart there.
+scene (sites, adjacency, parameters) is replicated on every GPU (``broadcast_scene`` at load time), and
+``gather_image`` assembles a tile-sharded frame for output. The one exchange step is in training:
+the per-site gradients of all ranks are summed before the (replicated) optimizer step, by asynchronous
+NCCL all-reduces over NVLink, one per gradient tensor (``allreduce_grads``). The reference is
+single-GPU; this layer has no counterpart there.
 """
 
 from __future__ import annotations
@@ -60,6 +61,38 @@ def allreduce_grads(params, group=None):
     works = [dist.all_reduce(g, group=group, async_op=True) for g in grads]
     for w in works:
         w.wait()
+
+
+def broadcast_scene(tensors, src=0, group=None):
+    """Makes every rank's copy of the scene (sites, adjacency, parameters) equal to rank `src`'s: one
+    in-place broadcast per tensor, issued asynchronously and then waited for. Every rank passes tensors of
+    the same shapes and dtypes in the same order."""
+    if not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return
+    works = [dist.broadcast(t, src, group=group, async_op=True) for t in tensors]
+    for w in works:
+        w.wait()
+
+
+def gather_image(local, H, W, group=None, tile=TILE):
+    """The full H x W image from every rank's pixels of ``tile_pixels`` (`local` (P_r, C), in that pixel
+    order): the ranks' pixel runs, padded to the longest, are all-gathered and scattered back into image
+    order. Returns (H, W, C) on every rank (outside the timed step: this is the output path)."""
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    C = local.shape[1]
+    out = torch.empty(H * W, C, dtype=local.dtype, device=local.device)
+    if world == 1:
+        out[torch.from_numpy(tile_pixels(H, W, 1, 0, tile)).to(local.device)] = local
+        return out.view(H, W, C)
+    sizes = [len(tile_pixels(H, W, world, r, tile)) for r in range(world)]
+    pad = torch.zeros(max(sizes), C, dtype=local.dtype, device=local.device)
+    pad[:len(local)] = local
+    parts = [torch.empty_like(pad) for _ in range(world)]
+    dist.all_gather(parts, pad, group=group)
+    for r in range(world):
+        idx = torch.from_numpy(tile_pixels(H, W, world, r, tile)).to(local.device)
+        out[idx] = parts[r][:sizes[r]]
+    return out.view(H, W, C)
 
 
 def allreduce_max(values, device, group=None):
