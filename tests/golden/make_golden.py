@@ -21,6 +21,10 @@ the reference's float64 restatements:
 * render_host.npz  - the proposal sampler's host arithmetic on 256 seeded rays: render.ray_bounds,
                      s_to_t, composite, sample_pdf (stratified and the bin edges of resample) and
                      resample (render.py:16-74), float32 as the reference computes them.
+* camera_rays.npz  - colmap.ColmapScene.rays (colmap.py:129-134) of every pixel of a 37x23 image, the
+                     intrinsics and camera-to-world matrix built as ColmapScene.__init__ does
+                     (colmap.py:104-114) from a SIMPLE_PINHOLE camera (fov 50 deg) and a seeded pose,
+                     and bench_infer.tile_order (bench_infer.py:37-41) of the image.
 * field_small.npz  - test_grad.py's setup (400 uniform sites, rng(0)): exact nearest sites (cKDTree) of
                      sorted ray samples for the walk, and the float64 density / colour fields with
                      their autograd gradients (test_grad.py:45-125).
@@ -335,9 +339,37 @@ def make_render_host():
     np.savez_compressed(os.path.join(HERE, 'render_host.npz'), **out)
 
 
+def make_camera_rays():
+    import math
+    import colmap as ref_colmap
+    torch.Tensor.cuda = lambda self, *a, **k: self  # tile_order ends with .cuda(); keep it on the CPU
+    import bench_infer as ref_bench_infer
+    W, H, fov = 37, 23, 50.0
+    f = 0.5 * W / math.tan(math.radians(fov) / 2.0)
+    fx, fy, cx, cy = ref_colmap.intrinsics(0, [f, W / 2.0, H / 2.0])
+    K = np.array([[fx, 0, cx], [0, fy, cy], [0, 0, 1]])
+    rng = np.random.default_rng(12)
+    R, _ = np.linalg.qr(rng.normal(size=(3, 3)))
+    R *= np.sign(np.linalg.det(R))
+    c2w = np.eye(4)
+    c2w[:3, :3] = R
+    c2w[:3, 3] = rng.normal(size=3) * 2.0
+    cam = SimpleNamespace(K=torch.tensor(K[None], dtype=torch.float32),
+                          c2w=torch.tensor(c2w[None], dtype=torch.float32))
+    cam.K_inv = torch.linalg.inv(cam.K)
+    cam.centers = cam.c2w[:, :3, 3]
+    py, px = torch.meshgrid(torch.arange(H).float(), torch.arange(W).float(), indexing='ij')
+    img = torch.zeros(H * W, dtype=torch.long)
+    o, d = ref_colmap.ColmapScene.rays(cam, img, px.reshape(-1), py.reshape(-1))
+    order = ref_bench_infer.tile_order(H, W)
+    np.savez_compressed(os.path.join(HERE, 'camera_rays.npz'), W=W, H=H, fov=fov, centre=c2w[:3, 3], rot=R,
+                        o=o.expand(H * W, 3).numpy(), d=d.numpy(), order=order.numpy())
+
+
 MAKERS = {'sh_basis': make_sh_basis, 'conic': make_conic, 'foam_small': make_foam_small,
           'march_small': make_march_small, 'foam_config1': make_foam_config1, 'field_small': make_field_small,
-          'ckpt_small': make_ckpt_small, 'render_host': make_render_host}
+          'ckpt_small': make_ckpt_small, 'render_host': make_render_host,
+          'camera_rays': make_camera_rays}
 
 if __name__ == '__main__':
     # python make_golden.py [name ...]: only the named fixtures (default all)
