@@ -105,9 +105,8 @@ class Graph:
     """Fixed sites and their Delaunay adjacency (CSR, int32) on the GPU (ext.py:46-58)."""
 
     def __init__(self, points, offsets, adj):
-        self.points = points.float().contiguous()
-        self.offsets = offsets.int().contiguous()
-        self.adj = adj.int().contiguous()
+        self.points, self.offsets, self.adj = points.float().contiguous(), offsets.int().contiguous(), \
+            adj.int().contiguous()
         self._pack = None
 
     @property
@@ -119,8 +118,8 @@ class Graph:
     def walk(self, o, d, z, start):
         """Nearest site of every sample o + z d; z (B, S) sorted along each ray, start (B,) a site near o
         (ext.py:54-58). Returns (site (B, S) int32, steps (B) int32)."""
-        site, steps = extension().walk(self.points, self.offsets, self.adj, o.float().contiguous(),
-                                       d.float().contiguous(), z.float().contiguous(), start.int().contiguous())
+        o, d, start = _rays(o, d, start)
+        site, steps = extension().walk(self.points, self.offsets, self.adj, o, d, z.float().contiguous(), start)
         return site, steps
 
 
@@ -493,152 +492,222 @@ def foam_infer_extension():
 
 
 # ---------------------------------------------------------------------------------------- autograd
+#
+# One autograd node type (_OpNode) serves every differentiable op. An op object carries the
+# non-differentiable context of one call (graph, rays, settings) and knows four things: how to run the
+# extension's forward on the differentiable tensors, which tensors its backward needs, which outputs
+# carry no gradient, and how to turn output gradients into input gradients. The contracts are those of
+# the reference's autograd functions (ext.py:61-216): the same saved tensors, the same non-differentiable
+# outputs (depth, stats), gradients for the same inputs, and the same no-gradient shortcuts (the foam
+# forward keeps no records then).
 
-class _Conic(torch.autograd.Function):
+
+def _wants_grad(tensors):
+    return torch.is_grad_enabled() and any(t.requires_grad for t in tensors)
+
+
+def _dense(*tensors):
+    return [t.contiguous() for t in tensors]
+
+
+def _grad_or_zeros(g, like):
+    return torch.zeros_like(like) if g is None else g.contiguous()
+
+
+class _OpNode(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, log_scale, quat, floor):
-        ctx.save_for_backward(log_scale, quat)
-        ctx.floor = floor
-        return extension().conic_forward(log_scale, quat, floor)
+    def forward(ctx, op, *inputs):
+        outputs = op.run(*inputs)
+        ctx.op, ctx.n_inputs = op, len(inputs)
+        ctx.save_for_backward(*inputs, *op.needs(outputs))
+        frozen = op.frozen(outputs)
+        if frozen:
+            ctx.mark_non_differentiable(*frozen)
+        return op.visible(outputs)
 
     @staticmethod
-    def backward(ctx, gA):
-        log_scale, quat = ctx.saved_tensors
-        g_ls, g_quat = extension().conic_backward(log_scale, quat, ctx.floor, gA.contiguous())
-        return g_ls, g_quat, None
+    def backward(ctx, *grads):
+        saved = ctx.saved_tensors
+        n = ctx.n_inputs
+        return (None, *ctx.op.grads(saved[:n], saved[n:], grads))
+
+
+class _Op:
+    """Defaults: the backward needs only the inputs, every output is differentiable and visible."""
+
+    def needs(self, outputs):
+        return ()
+
+    def frozen(self, outputs):
+        return ()
+
+    def visible(self, outputs):
+        return outputs
+
+
+class _ConicOp(_Op):
+    def __init__(self, floor):
+        self.floor = floor
+
+    def run(self, log_scale, quat):
+        return extension().conic_forward(log_scale, quat, self.floor)
+
+    def grads(self, inputs, kept, grads):
+        log_scale, quat = inputs
+        g_ls, g_quat = extension().conic_backward(log_scale, quat, self.floor, grads[0].contiguous())
+        return g_ls, g_quat
+
+
+class _DensityOp(_Op):
+    def __init__(self, graph, x, site):
+        self.graph, self.x, self.site = graph, x, site
+
+    def run(self, raw, log_scale, quat):
+        g = self.graph
+        return extension().density_forward(g.points, g.offsets, g.adj, raw, log_scale, quat, self.x, self.site, 1.0)
+
+    def needs(self, sigma):
+        return self.x, self.site
+
+    def grads(self, inputs, kept, grads):
+        g = self.graph
+        x, site = kept
+        return extension().density_backward(g.points, g.offsets, g.adj, *inputs, x, site, grads[0].contiguous())
+
+
+class _ColorOp(_Op):
+    def __init__(self, graph, x, dirs, site, sh_deg):
+        self.graph, self.x, self.dirs, self.site, self.sh_deg = graph, x, dirs, site, sh_deg
+
+    def run(self, log_scale, quat, sh):
+        g = self.graph
+        return extension().color_forward(g.points, g.offsets, g.adj, log_scale, quat, sh, self.sh_deg, self.x,
+                                         self.dirs, self.site)
+
+    def needs(self, rgb):
+        return self.x, self.dirs, self.site, rgb
+
+    def grads(self, inputs, kept, grads):
+        g = self.graph
+        x, dirs, site, rgb = kept
+        log_scale, quat, sh = inputs
+        return extension().color_backward(g.points, g.offsets, g.adj, log_scale, quat, sh, self.sh_deg, x, dirs, site,
+                                          rgb, grads[0].contiguous())
+
+
+class _RenderOp(_Op):
+    """Shared by foam and march: the scene tensors (raw, dA, cA, sh) are the differentiable inputs, the
+    rays travel with the op; outputs (rgb, T, depth, stats[, rec]), of which depth and stats carry no
+    gradient and rec (foam only) stays hidden."""
+
+    def __init__(self, graph, rays, sh_deg, settings):
+        self.graph, self.rays, self.sh_deg, self.settings = graph, rays, sh_deg, settings
+
+    def frozen(self, outputs):
+        return outputs[2], outputs[3]
+
+    def visible(self, outputs):
+        return tuple(outputs[:4])
+
+    def scene(self):
+        g = self.graph
+        return g.points, g.offsets, g.adj
+
+
+class _FoamOp(_RenderOp):
+    def __init__(self, graph, rays, sh_deg, t_thresh, w_thresh, record_cap):
+        super().__init__(graph, rays, sh_deg, (t_thresh, w_thresh))
+        self.record_cap = record_cap
+
+    def run(self, raw, dA, cA, sh, record_cap=None):
+        cap = self.record_cap if record_cap is None else record_cap
+        return foam_extension().foam_forward(*self.scene(), raw, dA, cA, sh, self.sh_deg, *self.rays, *self.settings,
+                                             cap)
+
+    def needs(self, outputs):
+        rgb, T, _, stats, rec = outputs
+        return (rgb, T, rec, stats, *self.rays)
+
+    def grads(self, inputs, kept, grads):
+        rgb, T, rec, stats, *rays = kept
+        return foam_extension().foam_backward(*self.scene(), *inputs, self.sh_deg, *rays, *self.settings, rgb, T,
+                                              _grad_or_zeros(grads[0], rgb), _grad_or_zeros(grads[1], T), rec,
+                                              stats)
+
+
+class _MarchOp(_RenderOp):
+    def run(self, raw, dA, cA, sh):
+        return march_extension().march_forward(*self.scene(), raw, dA, cA, sh, self.sh_deg, *self.rays,
+                                               *self.settings)
+
+    def needs(self, outputs):
+        rgb, T = outputs[0], outputs[1]
+        return (rgb, T, *self.rays)
+
+    def grads(self, inputs, kept, grads):
+        rgb, T, *rays = kept
+        return march_extension().march_backward(*self.scene(), *inputs, self.sh_deg, *rays, *self.settings, rgb, T,
+                                                _grad_or_zeros(grads[0], rgb), _grad_or_zeros(grads[1], T))
+
+
+def _rays(o, d, start, *bounds):
+    """Ray tensors in the extension's dtypes: float32 o, d and bounds, int32 start sites."""
+    return (o.float().contiguous(), d.float().contiguous(), start.int().contiguous(),
+            *(b.float().contiguous() for b in bounds))
 
 
 def conic(log_scale, quat, floor=0.0):
     """(N, 6) inverse covariances (xx, xy, xz, yy, yz, zz) of R diag(s^2 + floor^2) R^T (ext.py:134-136)."""
-    return _Conic.apply(log_scale.contiguous(), quat.contiguous(), float(floor))
+    return _OpNode.apply(_ConicOp(float(floor)), *_dense(log_scale, quat))
 
 
 def conic_reference(log_scale, quat, floor=0.0):
-    """Plain torch version of conic (ext.py:139-149), for tests."""
-    q = quat / quat.norm(dim=-1, keepdim=True).clamp_min(1e-12)
-    w, x, y, z = q.unbind(-1)
-    R = torch.stack([
-        1 - 2 * (y * y + z * z), 2 * (x * y - w * z), 2 * (x * z + w * y),
-        2 * (x * y + w * z), 1 - 2 * (x * x + z * z), 2 * (y * z - w * x),
-        2 * (x * z - w * y), 2 * (y * z + w * x), 1 - 2 * (x * x + y * y)], -1).view(-1, 3, 3)
+    """Plain torch version of conic, for tests (ext.py:139-149): the rotation of the normalised
+    quaternion (w, x, y, z) from its pairwise products, then R diag(1 / (s^2 + floor^2)) R^T."""
+    u = quat / quat.norm(dim=-1, keepdim=True).clamp_min(1e-12)
+    w, x, y, z = u.unbind(-1)
+    xx, yy, zz = x * x, y * y, z * z
+    xy, xz, yz = x * y, x * z, y * z
+    wx, wy, wz = w * x, w * y, w * z
+    R = torch.stack((1 - 2 * (yy + zz), 2 * (xy - wz), 2 * (xz + wy),
+                     2 * (xy + wz), 1 - 2 * (xx + zz), 2 * (yz - wx),
+                     2 * (xz - wy), 2 * (yz + wx), 1 - 2 * (xx + yy)), -1).view(-1, 3, 3)
     inv_var = 1.0 / (torch.exp(2 * log_scale.clamp(-20, 20)) + floor * floor)
-    A = torch.einsum('nak,nk,nbk->nab', R, inv_var, R)
-    return torch.stack([A[:, 0, 0], A[:, 0, 1], A[:, 0, 2], A[:, 1, 1], A[:, 1, 2], A[:, 2, 2]], -1).contiguous()
-
-
-class _Density(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, raw, log_scale, quat, x, site, graph):
-        sigma = extension().density_forward(graph.points, graph.offsets, graph.adj, raw, log_scale, quat, x, site, 1.0)
-        ctx.save_for_backward(raw, log_scale, quat, x, site)
-        ctx.graph = graph
-        return sigma
-
-    @staticmethod
-    def backward(ctx, grad_sigma):
-        raw, log_scale, quat, x, site = ctx.saved_tensors
-        g = ctx.graph
-        g_raw, g_ls, g_quat = extension().density_backward(g.points, g.offsets, g.adj, raw, log_scale, quat, x, site,
-                                                           grad_sigma.contiguous())
-        return g_raw, g_ls, g_quat, None, None, None
+    A = (R * inv_var[:, None, :]) @ R.transpose(1, 2)
+    return A[:, (0, 0, 0, 1, 1, 2), (0, 1, 2, 1, 2, 2)].contiguous()
 
 
 def density(graph, raw, log_scale, quat, x, site, scale_mult=1.0):
     """sigma(x) = sum over the Voronoi neighbourhood of site of exp(raw_k) G_k(x) (ext.py:78-87).
-    scale_mult widens the Gaussians (proposal passes, no gradient)."""
-    x = x.detach().float().contiguous()
-    site = site.int().contiguous()
-    params = [p.contiguous() for p in (raw, log_scale, quat)]
-    if scale_mult != 1.0 or not torch.is_grad_enabled() or not any(p.requires_grad for p in params):
-        return extension().density_forward(graph.points, graph.offsets, graph.adj, *[p.detach() for p in params], x,
-                                           site, float(scale_mult))
-    return _Density.apply(*params, x, site, graph)
-
-
-class _Color(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, log_scale, quat, sh, x, dirs, site, graph, sh_deg):
-        rgb = extension().color_forward(graph.points, graph.offsets, graph.adj, log_scale, quat, sh, sh_deg, x, dirs,
-                                        site)
-        ctx.save_for_backward(log_scale, quat, sh, x, dirs, site, rgb)
-        ctx.graph, ctx.sh_deg = graph, sh_deg
-        return rgb
-
-    @staticmethod
-    def backward(ctx, grad_rgb):
-        log_scale, quat, sh, x, dirs, site, rgb = ctx.saved_tensors
-        g = ctx.graph
-        g_ls, g_quat, g_sh = extension().color_backward(g.points, g.offsets, g.adj, log_scale, quat, sh, ctx.sh_deg,
-                                                        x, dirs, site, rgb, grad_rgb.contiguous())
-        return g_ls, g_quat, g_sh, None, None, None, None, None
+    scale_mult widens the Gaussians (proposal passes): then, as without autograd, no graph is recorded."""
+    x, site = x.detach().float().contiguous(), site.int().contiguous()
+    params = _dense(raw, log_scale, quat)
+    if scale_mult == 1.0 and _wants_grad(params):
+        return _OpNode.apply(_DensityOp(graph, x, site), *params)
+    return extension().density_forward(graph.points, graph.offsets, graph.adj, *(p.detach() for p in params), x, site,
+                                       float(scale_mult))
 
 
 def color(graph, log_scale, quat, sh, x, dirs, site, sh_deg=3):
     """C(x, d) = sum_k H_k(x) c_k(d) / sum_k H_k(x) over the Voronoi neighbourhood of site; sh (N, 16, 3)
     (ext.py:109-117)."""
-    x = x.detach().float().contiguous()
-    dirs = dirs.detach().float().contiguous()
-    site = site.int().contiguous()
-    params = [p.contiguous() for p in (log_scale, quat, sh)]
-    if not torch.is_grad_enabled() or not any(p.requires_grad for p in params):
-        return extension().color_forward(graph.points, graph.offsets, graph.adj, *[p.detach() for p in params],
-                                         int(sh_deg), x, dirs, site)
-    return _Color.apply(*params, x, dirs, site, graph, int(sh_deg))
-
-
-class _March(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, raw, dA, cA, sh, graph, rays, cfg):
-        rgb, T, depth, stats = march_extension().march_forward(graph.points, graph.offsets, graph.adj, raw, dA, cA, sh,
-                                                               cfg[0], *rays, *cfg[1:])
-        ctx.save_for_backward(raw, dA, cA, sh, rgb, T, *rays)
-        ctx.graph, ctx.cfg = graph, cfg
-        ctx.mark_non_differentiable(depth, stats)
-        return rgb, T, depth, stats
-
-    @staticmethod
-    def backward(ctx, g_rgb, g_T, _g_depth, _g_stats):
-        raw, dA, cA, sh, rgb, T, *rays = ctx.saved_tensors
-        g, cfg = ctx.graph, ctx.cfg
-        g_rgb = torch.zeros_like(rgb) if g_rgb is None else g_rgb.contiguous()
-        g_T = torch.zeros_like(T) if g_T is None else g_T.contiguous()
-        g_raw, g_dA, g_cA, g_sh = march_extension().march_backward(g.points, g.offsets, g.adj, raw, dA, cA, sh, cfg[0],
-                                                                   *rays, *cfg[1:], rgb, T, g_rgb, g_T)
-        return g_raw, g_dA, g_cA, g_sh, None, None, None
+    op = _ColorOp(graph, x.detach().float().contiguous(), dirs.detach().float().contiguous(), site.int().contiguous(),
+                  int(sh_deg))
+    params = _dense(log_scale, quat, sh)
+    if _wants_grad(params):
+        return _OpNode.apply(op, *params)
+    return op.run(*(p.detach() for p in params))
 
 
 def march(graph, raw, dA, cA, sh, sh_deg, o, d, start, near, mid, far, dt, n_bg, t_thresh=1e-4, w_thresh=1e-4):
     """Uniform-step fused rendering -> foreground rgb (B, 3), final transmittance (B,), depth (B,), per-ray
     stats (B, 3) int: samples marched, samples with colour, walk steps (ext.py:172-182)."""
-    rays = tuple(t.float().contiguous() for t in (o, d)) + (start.int().contiguous(),) + \
-        tuple(t.float().contiguous() for t in (near, mid, far))
-    cfg = (int(sh_deg), float(dt), int(n_bg), float(t_thresh), float(w_thresh))
-    params = [p.contiguous() for p in (raw, dA, cA, sh)]
-    if not torch.is_grad_enabled() or not any(p.requires_grad for p in params):
-        return march_extension().march_forward(graph.points, graph.offsets, graph.adj, *[p.detach() for p in params],
-                                               cfg[0], *rays, *cfg[1:])
-    return _March.apply(*params, graph, rays, cfg)
-
-
-class _Foam(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, raw, dA, cA, sh, graph, rays, cfg, record_cap):
-        rgb, T, depth, stats, rec = foam_extension().foam_forward(graph.points, graph.offsets, graph.adj, raw, dA, cA,
-                                                                  sh, cfg[0], *rays, *cfg[1:], record_cap)
-        ctx.save_for_backward(raw, dA, cA, sh, rgb, T, rec, stats, *rays)
-        ctx.graph, ctx.cfg = graph, cfg
-        ctx.mark_non_differentiable(depth, stats)
-        return rgb, T, depth, stats
-
-    @staticmethod
-    def backward(ctx, g_rgb, g_T, _g_depth, _g_stats):
-        raw, dA, cA, sh, rgb, T, rec, stats, *rays = ctx.saved_tensors
-        g, cfg = ctx.graph, ctx.cfg
-        g_rgb = torch.zeros_like(rgb) if g_rgb is None else g_rgb.contiguous()
-        g_T = torch.zeros_like(T) if g_T is None else g_T.contiguous()
-        g_raw, g_dA, g_cA, g_sh = foam_extension().foam_backward(g.points, g.offsets, g.adj, raw, dA, cA, sh, cfg[0],
-                                                                 *rays, *cfg[1:], rgb, T, g_rgb, g_T, rec, stats)
-        return g_raw, g_dA, g_cA, g_sh, None, None, None, None
+    op = _MarchOp(graph, _rays(o, d, start, near, mid, far), int(sh_deg),
+                  (float(dt), int(n_bg), float(t_thresh), float(w_thresh)))
+    params = _dense(raw, dA, cA, sh)
+    if _wants_grad(params):
+        return _OpNode.apply(op, *params)
+    return op.run(*(p.detach() for p in params))
 
 
 def foam(graph, raw, dA, cA, sh, sh_deg, o, d, start, near, far, t_thresh=1e-4, w_thresh=1e-4, record_cap=256):
@@ -646,11 +715,9 @@ def foam(graph, raw, dA, cA, sh, sh_deg, o, d, start, near, far, t_thresh=1e-4, 
     transmittance (B,), depth (B,), per-ray stats (B, 3) int: samples, segments with colour, walk steps to
     x(near). With gradients, up to record_cap samples per ray are kept for the backward pass (0: re-trace every
     ray) (ext.py:205-216)."""
-    rays = tuple(t.float().contiguous() for t in (o, d)) + (start.int().contiguous(),) + \
-        tuple(t.float().contiguous() for t in (near, far))
-    cfg = (int(sh_deg), float(t_thresh), float(w_thresh))
-    params = [p.contiguous() for p in (raw, dA, cA, sh)]
-    if not torch.is_grad_enabled() or not any(p.requires_grad for p in params):
-        return foam_extension().foam_forward(graph.points, graph.offsets, graph.adj, *[p.detach() for p in params],
-                                             cfg[0], *rays, *cfg[1:], 0)[:4]
-    return _Foam.apply(*params, graph, rays, cfg, int(record_cap))
+    op = _FoamOp(graph, _rays(o, d, start, near, far), int(sh_deg), float(t_thresh), float(w_thresh),
+                 int(record_cap))
+    params = _dense(raw, dA, cA, sh)
+    if _wants_grad(params):
+        return _OpNode.apply(op, *params)
+    return op.run(*(p.detach() for p in params), record_cap=0)[:4]
