@@ -2,17 +2,20 @@
 
 * ``sphere_exit``, ``ray_bounds`` (render.py:16-25): near = const, mid = exit of the unit ball,
   far = exit of the far_radius ball (at least mid + 1e-3).
-* ``render_rays_foam`` (render.py:127-140): conics of both Gaussians, ``ext.foam``, background composite
-  ``fg + T sigmoid(bg_logit)``.
-* ``render_rays_uniform`` (render.py:109-124): the same with ``ext.march`` and a conic floor of dt / 2.
-* ``sh_basis``, ``morton_order``, ``pack_foam``, ``bake_colors``, ``render_rays_foam_infer``
-  (render.py:143-257): the inference layout and its renderer.
 * ``s_to_t``, ``sample_pdf``, ``composite``, ``proposal_weights``, ``resample``, ``render_rays``
   (render.py:28-106): the NeRF-style proposal sampler over the field kernels (``Graph.walk``,
   ``ext.density``, ``ext.color``): 64 stratified samples in a normalised ray coordinate s (linear in t
   inside the unit ball, linear in disparity beyond), two gradient-free proposal passes with widened
   density Gaussians, then the merged samples walked to their sites and rendered with gradients.
+* ``render_rays_uniform`` (render.py:109-124) and ``render_rays_foam`` (render.py:127-140): conics of
+  both Gaussians, the fused ``ext.march`` / ``ext.foam`` renderers, background composite
+  ``fg + T sigmoid(bg_logit)``.
+* ``sh_basis``, ``morton_order``, ``pack_foam``, ``bake_colors``, ``render_rays_foam_infer``
+  (render.py:143-257): the inference layout (built on the device) and its renderer.
 * ``render_image`` (render.py:260-266).
+
+The sampler arithmetic is written so that every float32 operation matches the reference's, in value and
+order: the sample positions decide which Voronoi cells the walk visits, so they are bit-identical.
 """
 
 from __future__ import annotations
@@ -20,178 +23,209 @@ from __future__ import annotations
 import math
 
 import torch
+import torch.nn.functional as F
 
 from . import ext
 
+_GAP = 1e-3  # minimum distances near -> mid -> far
+
+
+# ------------------------------------------------------------------------------- ray coordinates
 
 def sphere_exit(o, d, radius):
-    b = (o * d).sum(-1)
+    """Distance along unit d from o to where the ray leaves the origin-centred ball of `radius`: the larger
+    root of |o + t d|^2 = radius^2, with the discriminant clamped at 0 for rays that miss the ball."""
+    half_b = (o * d).sum(-1)
     c = (o * o).sum(-1) - radius * radius
-    return -b + (b * b - c).clamp_min(0).sqrt()
+    return torch.sqrt(torch.clamp(half_b * half_b - c, min=0)) - half_b
 
 
 def ray_bounds(o, d, near, far_radius):
-    t_mid = sphere_exit(o, d, 1.0).clamp_min(near + 1e-3)
-    t_far = torch.maximum(sphere_exit(o, d, far_radius), t_mid + 1e-3)
-    return torch.full_like(t_mid, near), t_mid, t_far
+    """(near, mid, far) per ray: the constant near plane, mid where the ray leaves the unit ball (at least
+    1e-3 beyond near), far where it leaves the far_radius ball (at least 1e-3 beyond mid)."""
+    mid = torch.clamp(sphere_exit(o, d, 1.0), min=near + _GAP)
+    far = torch.max(sphere_exit(o, d, far_radius), mid + _GAP)
+    return mid.new_full(mid.shape, near), mid, far
 
 
 def s_to_t(s, t_near, t_mid, t_far):
-    """Ray depth of the normalised coordinate s in [0, 1] (render.py:28-33): s < 1/2 maps linearly onto
-    [near, mid], s >= 1/2 linearly in disparity onto [mid, far]."""
-    t_near, t_mid, t_far = t_near[:, None], t_mid[:, None], t_far[:, None]
-    inside = t_near + (t_mid - t_near) * (2 * s).clamp(max=1)
-    u = (2 * s - 1).clamp(min=0)
-    beyond = 1.0 / (1.0 / t_mid + u * (1.0 / t_far - 1.0 / t_mid))
+    """Ray depth of the normalised coordinate s in [0, 1]: the first half maps linearly in t onto
+    [near, mid], the second half linearly in 1/t onto [mid, far]."""
+    near, mid, far = (b.unsqueeze(1) for b in (t_near, t_mid, t_far))
+    two_s = 2 * s
+    inside = near + (mid - near) * torch.clamp(two_s, max=1)
+    inv_mid = 1.0 / mid
+    beyond = 1.0 / (inv_mid + torch.clamp(two_s - 1, min=0) * (1.0 / far - inv_mid))
     return torch.where(s < 0.5, inside, beyond)
 
 
+def _points(o, d, t):
+    """Sample positions o + t d of every (ray, sample), flattened to (B S, 3)."""
+    return (o.unsqueeze(1) + d.unsqueeze(1) * t.unsqueeze(2)).reshape(-1, 3)
+
+
+# ------------------------------------------------------------------------------- proposal sampler
+
 def sample_pdf(bins, weights, n, det=True):
-    """n samples per row from the piecewise-constant density of `weights` over `bins` (render.py:36-50):
-    inverse-CDF sampling at stratified midpoints (det) or uniform draws."""
+    """n draws per row from the piecewise-constant density that `weights` (plus 1e-5) put on the intervals
+    of `bins`, by inverting its CDF at the n stratified midpoints (det) or at uniform random points."""
     w = weights + 1e-5
-    cdf = torch.cumsum(w / w.sum(-1, keepdim=True), -1)
-    cdf = torch.cat([torch.zeros_like(cdf[:, :1]), cdf], -1)
+    cdf = F.pad(torch.cumsum(w / w.sum(-1, keepdim=True), -1), (1, 0))
+    rows, last = len(bins), cdf.shape[-1] - 1
     if det:
-        u = torch.linspace(0.5 / n, 1 - 0.5 / n, n, device=bins.device).expand(len(bins), n).contiguous()
+        u = torch.linspace(0.5 / n, 1 - 0.5 / n, n, device=bins.device).expand(rows, n).contiguous()
     else:
-        u = torch.rand(len(bins), n, device=bins.device)
-    hi = torch.searchsorted(cdf, u, right=True)
-    lo = (hi - 1).clamp_min(0)
-    hi = hi.clamp_max(cdf.shape[-1] - 1)
-    c0, c1 = cdf.gather(1, lo), cdf.gather(1, hi)
-    b0, b1 = bins.gather(1, lo), bins.gather(1, hi)
-    span = c1 - c0
+        u = torch.rand(rows, n, device=bins.device)
+    right = torch.searchsorted(cdf, u, right=True)
+    lo, hi = torch.clamp(right - 1, min=0), torch.clamp(right, max=last)
+    c_lo, c_hi = cdf.gather(1, lo), cdf.gather(1, hi)
+    span = c_hi - c_lo
     span = torch.where(span < 1e-5, torch.ones_like(span), span)
-    return b0 + (u - c0) / span * (b1 - b0)
+    x_lo = bins.gather(1, lo)
+    return x_lo + (u - c_lo) / span * (bins.gather(1, hi) - x_lo)
 
 
 def composite(sigma, t, t_far):
-    """Front-to-back weights of point samples (render.py:53-57): the last interval runs to t_far;
-    returns (weights (B, S), final transmittance (B))."""
-    delta = torch.cat([t[:, 1:] - t[:, :-1], (t_far[:, None] - t[:, -1:]).clamp_min(0)], 1)
-    alpha = 1.0 - torch.exp(-sigma * delta)
-    trans = torch.cumprod(torch.cat([torch.ones_like(alpha[:, :1]), 1.0 - alpha + 1e-10], 1), 1)
+    """Front-to-back weights of point samples: sample k stands for [t_k, t_k+1) (the last one up to t_far,
+    empty past it), alpha_k = 1 - exp(-sigma_k dt_k), w_k = alpha_k prod_{j<k} (1 - alpha_j + 1e-10).
+    -> (weights (B, S), transmittance after the last sample (B,))."""
+    ends = torch.cat([t[:, 1:], torch.max(t_far.unsqueeze(1), t[:, -1:])], 1)
+    alpha = 1.0 - torch.exp(-sigma * (ends - t))
+    trans = torch.cumprod(F.pad(1.0 - alpha + 1e-10, (1, 0), value=1.0), 1)
     return alpha * trans[:, :-1], trans[:, -1]
 
 
+def _sigma(model, x, site, scale_mult=1.0):
+    return ext.density(model.graph, model.raw, model.d_log_scale, model.d_quat, x, site, scale_mult)
+
+
 def proposal_weights(model, o, d, s, bounds, start, scale_mult):
-    """Compositing weights of samples s under the density widened by scale_mult, without gradients
-    (render.py:60-68)."""
+    """Compositing weights of the samples s under the density widened by scale_mult, without gradients."""
     t = s_to_t(s, *bounds)
     site, _ = model.walk(o, d, t, start)
-    x = (o[:, None] + d[:, None] * t[..., None]).reshape(-1, 3)
     with torch.no_grad():
-        sigma = ext.density(model.graph, model.raw, model.d_log_scale, model.d_quat, x, site.reshape(-1),
-                            scale_mult).view_as(t)
-    w, _ = composite(sigma, t, bounds[2])
-    return w
+        sigma = _sigma(model, _points(o, d, t), site.reshape(-1), scale_mult).view_as(t)
+    return composite(sigma, t, bounds[2])[0]
 
 
 def resample(s, w, n, det):
-    """n new samples drawn from the weights w of the sorted samples s (render.py:71-74)."""
-    mid = 0.5 * (s[:, 1:] + s[:, :-1])
-    bins = torch.cat([torch.zeros_like(s[:, :1]), mid, torch.ones_like(s[:, :1])], 1)
-    return sample_pdf(bins, w, n, det)
+    """n new values of s drawn from the weights w of the sorted samples s, over bins that split [0, 1] at
+    the midpoints between consecutive samples."""
+    mids = 0.5 * (s[:, 1:] + s[:, :-1])
+    return sample_pdf(F.pad(F.pad(mids, (1, 0), value=0.0), (0, 1), value=1.0), w, n, det)
+
+
+def _refine(model, o, d, s, bounds, start, n_fine, proposal_mult, det):
+    """The gradient-free proposal passes: each adds n draws from the widened-density weights of the
+    current samples and keeps the merged set sorted."""
+    for n, mult in zip(n_fine, proposal_mult):
+        drawn = resample(s, proposal_weights(model, o, d, s, bounds, start, mult), n, det)
+        s = torch.sort(torch.cat([s, drawn], 1), 1)[0]
+    return s
 
 
 def render_rays(model, o, d, start, n_coarse=64, n_fine=(64, 64), proposal_mult=(4.0, 2.0), near=0.02,
                 far_radius=4.0, perturb=True, min_weight=1e-4):
     """NeRF-style rendering (render.py:77-106): o, d (B, 3) rays, start (B,) the site containing each
-    origin -> dict with rgb (B, 3), acc, depth and sampler statistics. Colours are evaluated only for the
-    samples with weight > min_weight."""
+    origin -> dict with rgb (B, 3), acc, depth and sampler statistics (walk_steps per sample, active
+    fraction). Colours are evaluated only for the samples with weight > min_weight."""
     B = len(o)
     bounds = ray_bounds(o, d, near, far_radius)
-    s = torch.linspace(0, 1, n_coarse + 1, device=o.device)[:-1].expand(B, n_coarse)
-    s = s + (torch.rand_like(s) if perturb else 0.5) / n_coarse
+    grid = torch.linspace(0, 1, n_coarse + 1, device=o.device)[:-1].expand(B, n_coarse)
+    s = grid + (torch.rand_like(grid) if perturb else 0.5) / n_coarse
     with torch.no_grad():
-        for n, mult in zip(n_fine, proposal_mult):
-            w = proposal_weights(model, o, d, s, bounds, start, mult)
-            s, _ = torch.sort(torch.cat([s, resample(s, w, n, det=not perturb)], 1), 1)
+        s = _refine(model, o, d, s, bounds, start, n_fine, proposal_mult, not perturb)
         t = s_to_t(s, *bounds)
         site, steps = model.walk(o, d, t, start)
     S = t.shape[1]
-    x = (o[:, None] + d[:, None] * t[..., None]).reshape(-1, 3)
-    site = site.reshape(-1)
-    sigma = ext.density(model.graph, model.raw, model.d_log_scale, model.d_quat, x, site).view(B, S)
-    w, t_final = composite(sigma, t, bounds[2])
-    active = (w.detach() > min_weight).reshape(-1).nonzero().squeeze(1)
-    dirs = d[:, None].expand(B, S, 3).reshape(-1, 3)
-    c = ext.color(model.graph, model.c_log_scale, model.c_quat, model.sh(), x[active], dirs[active], site[active],
+    x, site = _points(o, d, t), site.reshape(-1)
+    w, t_last = composite(_sigma(model, x, site).view(B, S), t, bounds[2])
+    lit = torch.nonzero((w.detach() > min_weight).reshape(-1)).squeeze(1)
+    dirs = d.unsqueeze(1).expand(B, S, 3).reshape(-1, 3)
+    c = ext.color(model.graph, model.c_log_scale, model.c_quat, model.sh(), x[lit], dirs[lit], site[lit],
                   model.sh_deg)
-    rgb_s = torch.zeros(B * S, 3, device=o.device, dtype=c.dtype).index_put((active,), c).view(B, S, 3)
-    rgb = (w[..., None] * rgb_s).sum(1) + t_final[:, None] * torch.sigmoid(model.bg_logit)
-    return {'rgb': rgb, 'acc': 1.0 - t_final, 'depth': (w * t).sum(1), 'walk_steps': steps.float().mean() / S,
-            'active': len(active) / (B * S)}
+    sample_rgb = c.new_zeros(B * S, 3).index_put((lit,), c).view(B, S, 3)
+    rgb = _over_background(model, (w.unsqueeze(-1) * sample_rgb).sum(1), t_last)
+    return {'rgb': rgb, 'acc': 1.0 - t_last, 'depth': (w * t).sum(1), 'walk_steps': steps.float().mean() / S,
+            'active': len(lit) / (B * S)}
+
+
+# ------------------------------------------------------------------------------- fused renderers
+
+def _over_background(model, fg, T):
+    """fg + T sigmoid(bg_logit): the learned background behind what the rays leave unabsorbed."""
+    return fg + T.unsqueeze(1) * torch.sigmoid(model.bg_logit)
+
+
+def _conics(model, floor):
+    return (ext.conic(model.d_log_scale, model.d_quat, floor), ext.conic(model.c_log_scale, model.c_quat, floor))
 
 
 def render_rays_uniform(model, o, d, start, dt=1 / 512, n_bg=64, near=0.02, far_radius=4.0, t_thresh=1e-4,
                         w_thresh=1e-4, scale_floor=None, perturb=False):
     """Fixed steps dt inside the unit ball, n_bg steps uniform in disparity beyond it, early termination at
-    T < t_thresh, in one fused kernel; scale_floor (default dt / 2) is added in quadrature to every scale."""
-    near_t, mid_t, far_t = ray_bounds(o, d, near, far_radius)
-    floor = 0.5 * dt if scale_floor is None else scale_floor
-    dA = ext.conic(model.d_log_scale, model.d_quat, floor)
-    cA = ext.conic(model.c_log_scale, model.c_quat, floor)
-    fg, T, depth, stats = ext.march(model.graph, model.raw, dA, cA, model.sh(), model.sh_deg, o, d, start, near_t,
-                                    mid_t, far_t, dt, n_bg, t_thresh, w_thresh)
-    rgb = fg + T[:, None] * torch.sigmoid(model.bg_logit)
-    stats = stats.float()
-    return {'rgb': rgb, 'acc': 1.0 - T, 'depth': depth, 'samples': stats[:, 0].mean(),
-            'active': (stats[:, 1].sum() / stats[:, 0].sum()).item(),
-            'walk_steps': stats[:, 2].sum() / stats[:, 0].sum()}
+    T < t_thresh, in one fused kernel; scale_floor (default dt / 2) is added in quadrature to every scale.
+    Statistics per marched sample: active (coloured) fraction and walk steps."""
+    bounds = ray_bounds(o, d, near, far_radius)
+    dA, cA = _conics(model, 0.5 * dt if scale_floor is None else scale_floor)
+    fg, T, depth, stats = ext.march(model.graph, model.raw, dA, cA, model.sh(), model.sh_deg, o, d, start, *bounds,
+                                    dt, n_bg, t_thresh, w_thresh)
+    samples, coloured, walks = stats.float().unbind(1)
+    return {'rgb': _over_background(model, fg, T), 'acc': 1.0 - T, 'depth': depth, 'samples': samples.mean(),
+            'active': (coloured.sum() / samples.sum()).item(), 'walk_steps': walks.sum() / samples.sum()}
 
 
 def render_rays_foam(model, o, d, start, near=0.02, far_radius=4.0, t_thresh=1e-4, w_thresh=1e-4, scale_floor=0.0,
                      perturb=False):
     """Samples at the interaction points of each ray with the Voronoi faces (plus x(near) and x(far)), segments
-    composited with the trapezoid rule in one fused kernel."""
-    near_t, _, far_t = ray_bounds(o, d, near, far_radius)
-    dA = ext.conic(model.d_log_scale, model.d_quat, scale_floor)
-    cA = ext.conic(model.c_log_scale, model.c_quat, scale_floor)
-    fg, T, depth, stats = ext.foam(model.graph, model.raw, dA, cA, model.sh(), model.sh_deg, o, d, start, near_t,
-                                   far_t, t_thresh, w_thresh)
-    rgb = fg + T[:, None] * torch.sigmoid(model.bg_logit)
-    stats = stats.float()
-    segments = (stats[:, 0] - 1).sum().clamp_min(1)
-    return {'rgb': rgb, 'acc': 1.0 - T, 'depth': depth, 'samples': stats[:, 0].mean(),
-            'active': (stats[:, 1].sum() / segments).item(), 'walk_steps': stats[:, 2].mean()}
+    composited with the trapezoid rule in one fused kernel. Statistics: samples per ray, coloured fraction of
+    the segments, walk steps to x(near) per ray."""
+    t_near, _, t_far = ray_bounds(o, d, near, far_radius)
+    dA, cA = _conics(model, scale_floor)
+    fg, T, depth, stats = ext.foam(model.graph, model.raw, dA, cA, model.sh(), model.sh_deg, o, d, start, t_near,
+                                   t_far, t_thresh, w_thresh)
+    samples, coloured, walks = stats.float().unbind(1)
+    segments = torch.clamp((samples - 1).sum(), min=1)
+    return {'rgb': _over_background(model, fg, T), 'acc': 1.0 - T, 'depth': depth, 'samples': samples.mean(),
+            'active': (coloured.sum() / segments).item(), 'walk_steps': walks.mean()}
+
+
+# ------------------------------------------------------------------------------- inference layout
+
+# Real SH basis up to degree 3 (render.py:143-165; the kernels' constants and signs): band l has the
+# normalisation constants below, the Cartesian polynomials are those of the standard real basis.
+_SH_C = (0.28209479177387814, 0.4886025119029199, 1.0925484305920792, 0.31539156525252005, 0.5462742152960396,
+         0.5900435899266435, 2.890611442640554, 0.4570457994644658, 0.3731763325901154, 1.445305721320277)
 
 
 def sh_basis(d, deg):
-    """Real SH basis (B, 16) of unit directions d (B, 3), the kernels' constants and signs."""
+    """Real SH basis (B, 16) of unit directions d (B, 3); the functions above degree `deg` are zero."""
+    c = _SH_C
     x, y, z = d.unbind(-1)
-    b = torch.zeros(len(d), 16, device=d.device, dtype=d.dtype)
-    b[:, 0] = 0.28209479177387814
+    cols = [torch.full_like(x, c[0])]
     if deg >= 1:
-        b[:, 1], b[:, 2], b[:, 3] = -0.4886025119029199 * y, 0.4886025119029199 * z, -0.4886025119029199 * x
+        cols += [-c[1] * y, c[1] * z, -c[1] * x]
     if deg >= 2:
         xx, yy, zz = x * x, y * y, z * z
-        b[:, 4] = 1.0925484305920792 * x * y
-        b[:, 5] = -1.0925484305920792 * y * z
-        b[:, 6] = 0.31539156525252005 * (2 * zz - xx - yy)
-        b[:, 7] = -1.0925484305920792 * x * z
-        b[:, 8] = 0.5462742152960396 * (xx - yy)
+        cols += [c[2] * x * y, -c[2] * y * z, c[3] * (2 * zz - xx - yy), -c[2] * x * z, c[4] * (xx - yy)]
     if deg >= 3:
-        b[:, 9] = -0.5900435899266435 * y * (3 * xx - yy)
-        b[:, 10] = 2.890611442640554 * x * y * z
-        b[:, 11] = -0.4570457994644658 * y * (4 * zz - xx - yy)
-        b[:, 12] = 0.3731763325901154 * z * (2 * zz - 3 * xx - 3 * yy)
-        b[:, 13] = -0.4570457994644658 * x * (4 * zz - xx - yy)
-        b[:, 14] = 1.445305721320277 * z * (xx - yy)
-        b[:, 15] = -0.5900435899266435 * x * (xx - 3 * yy)
-    return b
+        cols += [-c[5] * y * (3 * xx - yy), c[6] * x * y * z, -c[7] * y * (4 * zz - xx - yy),
+                 c[8] * z * (2 * zz - 3 * xx - 3 * yy), -c[7] * x * (4 * zz - xx - yy), c[9] * z * (xx - yy),
+                 -c[5] * x * (xx - 3 * yy)]
+    cols += [torch.zeros_like(x)] * (16 - len(cols))
+    return torch.stack(cols, -1)
 
 
 def morton_order(points, bits=10):
-    """Permutation sorting the points along a Z-order curve of their bounding box (render.py:168-176); equal
-    codes keep index order."""
+    """Permutation sorting the points along a Z-order curve of their bounding box (render.py:168-176):
+    each coordinate quantised to `bits` bits over the box, bit b of axis a placed at bit 3 b + a of the
+    code; equal codes keep index order."""
     lo, hi = points.amin(0), points.amax(0)
     q = ((points - lo) / (hi - lo).clamp_min(1e-12) * (2 ** bits - 1)).long()
-    code = torch.zeros(len(points), dtype=torch.long, device=points.device)
-    for b in range(bits):
-        for a in range(3):
-            code |= ((q[:, a] >> b) & 1) << (3 * b + a)
+    level = torch.arange(bits, device=points.device)
+    axis = torch.arange(3, device=points.device)
+    digits = (q.unsqueeze(2) >> level) & 1                        # (N, 3, bits)
+    code = (digits << (3 * level + axis.unsqueeze(1))).sum((1, 2))
     return torch.argsort(code, stable=True)
 
 
@@ -257,27 +291,32 @@ def bake_colors(model, pack, center):
 def render_rays_foam_infer(model, pack, o, d, start, near=0.02, far_radius=4.0, t_thresh=1e-4, w_thresh=1e-4,
                            colors='exact', eps_color=0.0, stage=2, cap=None):
     """Inference version of render_rays_foam (render.py:238-257): colors 'exact' (lazy second pass for the
-    segments with weight > w_thresh), 'fused' (blended in the density pass) or 'baked' (bake_colors). Per-ray
-    stats (B, 5): samples, coloured segments, walk steps, density Gaussians evaluated, SH evaluated."""
-    near_t, _, far_t = ray_bounds(o, d, near, far_radius)
-    cap = torch.empty(0, dtype=torch.int32, device=o.device) if cap is None else cap.int().contiguous()
-    if pack['inv'] is not None:
+    segments with weight > w_thresh), 'fused' (blended in the density pass) or 'baked' (bake_colors), the
+    neighbours below eps_color of the normalised colour weight skipped. Per-ray stats (B, 5): samples,
+    coloured segments, walk steps, density Gaussians evaluated, SH evaluated."""
+    mode = {'exact': 0, 'baked': 1, 'fused': 2}[colors]
+    t_near, _, t_far = ray_bounds(o, d, near, far_radius)
+    if cap is None:
+        cap = torch.empty(0, dtype=torch.int32, device=o.device)
+    if pack['inv'] is not None:  # start sites in the renumbered order of the pack
         start = pack['inv'][start.long()]
     color_cut = 2 * math.log(1 / eps_color) if eps_color > 0 else float('inf')
     fg, T, depth, stats = ext.foam_infer_extension().foam_infer(
         pack['points'], pack['offsets'], pack['nbr'], pack['edge'], pack['attr'], pack['sh'], model.sh_deg,
-        o.float().contiguous(), d.float().contiguous(), start.int().contiguous(), near_t.contiguous(),
-        far_t.contiguous(), float(t_thresh), float(w_thresh), color_cut, {'exact': 0, 'baked': 1, 'fused': 2}[colors],
-        int(stage), cap, pack['orig'])
-    rgb = fg + T[:, None] * torch.sigmoid(model.bg_logit)
-    return {'rgb': rgb, 'acc': 1.0 - T, 'depth': depth, 'stats': stats}
+        o.float().contiguous(), d.float().contiguous(), start.int().contiguous(), t_near.contiguous(),
+        t_far.contiguous(), float(t_thresh), float(w_thresh), color_cut, mode, int(stage), cap.int().contiguous(),
+        pack['orig'])
+    return {'rgb': _over_background(model, fg, T), 'acc': 1.0 - T, 'depth': depth, 'stats': stats}
 
 
 @torch.no_grad()
 def render_image(model, scene, i, start, chunk=8192, renderer=render_rays, **kw):
-    """Renders image i of a scene with .image_rays(i) -> (o, d, gt) and .H, .W (render.py:260-266)."""
+    """Image i of a scene with .image_rays(i) -> (o, d, gt) and .H, .W (render.py:260-266), rendered in
+    chunks of rays from the start site `start`. -> (rgb (H, W, 3) in [0, 1], gt)."""
     o, d, gt = scene.image_rays(i)
-    start = torch.full((len(o),), int(start), dtype=torch.int32, device=o.device)
-    out = [renderer(model, o[j:j + chunk], d[j:j + chunk], start[j:j + chunk], perturb=False, **kw)['rgb']
-           for j in range(0, len(o), chunk)]
-    return torch.cat(out).view(scene.H, scene.W, 3).clamp(0, 1), gt
+    first = torch.full((len(o),), int(start), dtype=torch.int32, device=o.device)
+    parts = []
+    for a in range(0, len(o), chunk):
+        b = a + chunk
+        parts.append(renderer(model, o[a:b], d[a:b], first[a:b], perturb=False, **kw)['rgb'])
+    return torch.cat(parts).view(scene.H, scene.W, 3).clamp(0, 1), gt
