@@ -25,6 +25,8 @@ the reference's float64 restatements:
                      intrinsics and camera-to-world matrix built as ColmapScene.__init__ does
                      (colmap.py:104-114) from a SIMPLE_PINHOLE camera (fov 50 deg) and a seeded pose,
                      and bench_infer.tile_order (bench_infer.py:37-41) of the image.
+* model_init.npz   - the initial parameters of the reference's VoronoiGaussField (model.py:23-39) for
+                     200 seeded sites (init_alpha 0.2, spacings including 0), in state_dict order.
 * field_small.npz  - test_grad.py's setup (400 uniform sites, rng(0)): exact nearest sites (cKDTree) of
                      sorted ray samples for the walk, and the float64 density / colour fields with
                      their autograd gradients (test_grad.py:45-125).
@@ -366,10 +368,24 @@ def make_camera_rays():
                         o=o.expand(H * W, 3).numpy(), d=d.numpy(), order=order.numpy())
 
 
+def make_model_init():
+    import model as ref_model
+    g = torch.Generator().manual_seed(0)
+    n = 200
+    pts, colors = torch.rand(n, 3, generator=g), torch.rand(n, 3, generator=g) * 1.4 - 0.2
+    spacing = torch.rand(n, generator=g) * 0.05
+    spacing[3] = 0.0
+    m = ref_model.VoronoiGaussField(pts, torch.zeros(n + 1, dtype=torch.int32), torch.zeros(0, dtype=torch.int32),
+                                    colors, spacing, init_alpha=0.2, sh_deg=2)
+    state = {f'state_{k}': v.numpy() for k, v in m.state_dict().items()}
+    np.savez_compressed(os.path.join(HERE, 'model_init.npz'), points=pts.numpy(), colors=colors.numpy(),
+                        spacing=spacing.numpy(), keys=np.array(list(m.state_dict())), **state)
+
+
 MAKERS = {'sh_basis': make_sh_basis, 'conic': make_conic, 'foam_small': make_foam_small,
           'march_small': make_march_small, 'foam_config1': make_foam_config1, 'field_small': make_field_small,
           'ckpt_small': make_ckpt_small, 'render_host': make_render_host,
-          'camera_rays': make_camera_rays}
+          'camera_rays': make_camera_rays, 'model_init': make_model_init}
 
 if __name__ == '__main__':
     # python make_golden.py [name ...]: only the named fixtures (default all)

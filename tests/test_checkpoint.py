@@ -23,3 +23,22 @@ def test_reference_checkpoint_loads_and_round_trips(tmp_path):
     assert set(ck2) == set(ck) and ck2['sh_deg'] == 2
     for k, v in ck['state'].items():
         assert torch.equal(getattr(again, k).detach(), v), k
+
+
+def test_initial_parameters_match_the_reference_constructor():
+    """VoronoiGaussField's initial state against the reference's constructor (tests/golden/model_init.npz):
+    same parameter names in the same order, bit-identical values."""
+    import numpy as np
+    import torch
+    from conftest import golden
+    from voronoi_gauss_b200.model import VoronoiGaussField
+    z = golden('model_init.npz')
+    n = len(z['points'])
+    m = VoronoiGaussField(torch.tensor(z['points']), torch.zeros(n + 1, dtype=torch.int32),
+                          torch.zeros(0, dtype=torch.int32), torch.tensor(z['colors']), torch.tensor(z['spacing']),
+                          init_alpha=0.2, sh_deg=2)
+    sd = m.state_dict()
+    assert list(sd) == list(z['keys'])
+    for k, v in sd.items():
+        assert np.array_equal(v.numpy(), z[f'state_{k}']), k
+    assert (m.max_sh_deg, m.sh_deg) == (2, 0)
