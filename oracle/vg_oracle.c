@@ -988,14 +988,18 @@ static float half_to_float(uint16_t h) {
     return f;
 }
 
-enum { LAZY = 0, BAKED = 1, FUSED = 2 };
-#define ICACHE 8 /* foam_infer.cu:43 */
+/* Restatement of the inference renderer (foam_infer.cu:121-361) on the packed inference layout: the
+ * same samples, skipping rules (density beyond r2, colour below the r2 lam bound), 8-entry direct-mapped
+ * colour cache and per-ray counts as the reference's kernel, in plain C. */
+enum { EXACT = 0, BAKED = 1, FUSED = 2 }; /* the API's color_mode values */
+#define SLOTS 8                           /* colour cache entries per ray (foam_infer.cu:43) */
+#define ATTR 20                           /* floats per site in attr */
 
 typedef struct {
     const float* points4; /* (N, 4) */
     const int32_t *offsets, *nbr, *orig;
     const float* edge;    /* (E, 4), w = half2 (r2, lam) bits */
-    const float* attr;    /* (N, 20) */
+    const float* attr;    /* (N, 20): density conic (6), min(raw, 30), 0, colour conic (6), 0, 0, baked rgb, 0 */
     const void* sh;
     int sh_half, deg;
     float t_thresh, w_thresh, color_cut;
@@ -1006,234 +1010,243 @@ typedef struct {
     int32_t* stats;
 } ICtx;
 
-static inline int before(const ICtx* N, int k, int j) { return N->orig != NULL ? N->orig[k] < N->orig[j] : k < j; }
+/* tie-break order of sites: their ids before any renumbering */
+static inline int rank_of(const ICtx* N, int k) { return N->orig != NULL ? N->orig[k] : k; }
 
-static inline void cutoffs(const float* e, float* r2, float* lam) {
-    uint32_t w;
-    memcpy(&w, &e[3], 4);
-    *r2 = half_to_float((uint16_t)(w & 0xffff));
-    *lam = half_to_float((uint16_t)(w >> 16));
+/* (r2, lam) of an edge record */
+static inline void record_bounds(const float* rec, float* r2, float* lam) {
+    uint32_t bits;
+    memcpy(&bits, &rec[3], 4);
+    *r2 = half_to_float((uint16_t)(bits & 0xffff));
+    *lam = half_to_float((uint16_t)(bits >> 16));
 }
 
-static inline float maha6(const float* q, float vx, float vy, float vz) {
-    return q[0] * vx * vx + q[3] * vy * vy + q[5] * vz * vz + 2.f * (q[1] * vx * vy + q[2] * vx * vz + q[4] * vy * vz);
+/* v^T A v of a conic stored (xx, xy, xz, yy, yz, zz) */
+static inline float quad6(const float* A, float vx, float vy, float vz) {
+    return A[0] * vx * vx + A[3] * vy * vy + A[5] * vz * vz + 2.f * (A[1] * vx * vy + A[2] * vx * vz + A[4] * vy * vz);
+}
+
+/* online normalised blend: sums kept relative to the smallest m so far (foam_infer.cu:81-88) */
+typedef struct {
+    float m_min, wsum, sum[3];
+} Mix;
+
+static inline void mix_reset(Mix* M) { M->m_min = KINF, M->wsum = M->sum[0] = M->sum[1] = M->sum[2] = 0.f; }
+
+static inline void mix_add(Mix* M, float m, const float rgb[3]) {
+    if (m < M->m_min) {
+        const float shrink = expf(-0.5f * (M->m_min - m));
+        M->wsum *= shrink;
+        for (int ch = 0; ch < 3; ++ch) M->sum[ch] *= shrink;
+        M->m_min = m;
+    }
+    const float a = expf(-0.5f * (m - M->m_min));
+    M->wsum += a;
+    for (int ch = 0; ch < 3; ++ch) M->sum[ch] += a * rgb[ch];
+}
+
+static inline void mix_mean(const Mix* M, float rgb[3]) {
+    const float inv = 1.f / M->wsum;
+    for (int ch = 0; ch < 3; ++ch) rgb[ch] = M->sum[ch] * inv;
+}
+
+/* max(SH_k(d) + 1/2, 0); each channel sums the basis functions in order (foam_infer.cu:121-149) */
+static void clamped_colour(const ICtx* N, int k, const float b[16], float rgb[3]) {
+    float f[48];
+    for (int i = 0; i < 48; ++i)
+        f[i] = N->sh_half ? half_to_float(((const uint16_t*)N->sh)[48 * (int64_t)k + i])
+                          : ((const float*)N->sh)[48 * (int64_t)k + i];
+    rgb[0] = rgb[1] = rgb[2] = 0.5f;
+    for (int j = 0; j < 16; ++j)
+        for (int ch = 0; ch < 3; ++ch) rgb[ch] += b[j] * f[3 * j + ch];
+    for (int ch = 0; ch < 3; ++ch) rgb[ch] = fmaxf(rgb[ch], 0.f);
 }
 
 typedef struct {
-    float m, a, r, g, b;
-} Blend;
+    float rgb[SLOTS][3];
+    int site[SLOTS]; /* -1: empty */
+} SlotCache;
 
-static inline void blend_init(Blend* B) { B->m = KINF, B->a = B->r = B->g = B->b = 0.f; }
-
-/* foam_infer.cu:81-88 */
-static inline void blend_add(Blend* B, float m, float r, float g, float b) {
-    if (m < B->m) {
-        const float s = expf(-0.5f * (B->m - m));
-        B->a *= s, B->r *= s, B->g *= s, B->b *= s, B->m = m;
+/* entry k mod SLOTS; a miss evaluates the SH and counts one evaluation (foam_infer.cu:157-168) */
+static void cache_colour(const ICtx* N, SlotCache* C, int k, const float b[16], float rgb[3], int* n_sh) {
+    const int s = k & (SLOTS - 1);
+    if (C->site[s] != k) {
+        clamped_colour(N, k, b, C->rgb[s]);
+        C->site[s] = k;
+        ++*n_sh;
     }
-    const float w = expf(-0.5f * (m - B->m));
-    B->a += w, B->r += w * r, B->g += w * g, B->b += w * b;
+    for (int ch = 0; ch < 3; ++ch) rgb[ch] = C->rgb[s][ch];
 }
 
-/* foam_infer.cu:121-149 */
-static void site_color(const ICtx* N, int k, const float b[16], float c[3]) {
-    c[0] = c[1] = c[2] = 0.5f;
-    if (N->sh_half) {
-        const uint16_t* s = (const uint16_t*)N->sh + 48 * (int64_t)k;
-        for (int i = 0; i < 48; ++i) c[i % 3] += b[i / 3] * half_to_float(s[i]);
-    } else {
-        const float* s = (const float*)N->sh + 48 * (int64_t)k;
-        for (int i = 0; i < 48; ++i) c[i % 3] += b[i / 3] * s[i];
-    }
-    c[0] = fmaxf(c[0], 0.f), c[1] = fmaxf(c[1], 0.f), c[2] = fmaxf(c[2], 0.f);
+static inline float dist2_to(const float x[3], const float* p) {
+    const float v0 = x[0] - p[0], v1 = x[1] - p[1], v2 = x[2] - p[2];
+    return dot3c(v0, v1, v2, v0, v1, v2);
 }
 
-typedef struct {
-    float c[ICACHE][3];
-    int key[ICACHE];
-} Cache;
-
-/* foam_infer.cu:157-168 */
-static void cached_color(const ICtx* N, Cache* C, int k, const float b[16], float c[3], int* n_sh) {
-    const int s = k & (ICACHE - 1);
-    if (C->key[s] == k) {
-        memcpy(c, C->c[s], sizeof(float) * 3);
-        return;
-    }
-    site_color(N, k, b, c);
-    memcpy(C->c[s], c, sizeof(float) * 3);
-    C->key[s] = k;
-    ++*n_sh;
-}
-
-static int iwalk_to(const ICtx* N, int c, float x0, float x1, float x2, int* steps) {
+/* greedy walk to the site nearest to x, equal distances to the smaller rank (foam_infer.cu:176-194) */
+static int nearest_site(const ICtx* N, int c, const float x[3], int* steps) {
     for (int it = 0; it < WALK_CAP; ++it) {
-        const float* pc = N->points4 + 4 * (int64_t)c;
-        const float v0 = x0 - pc[0], v1 = x1 - pc[1], v2 = x2 - pc[2];
-        float bd = dot3c(v0, v1, v2, v0, v1, v2);
-        int bk = c;
-        const int e0 = N->offsets[c], e1 = N->offsets[c + 1];
-        for (int e = e0 + 1; e < e1; ++e) {
-            const float* ed = N->edge + 4 * (int64_t)e;
+        float best = dist2_to(x, N->points4 + 4 * (int64_t)c);
+        int arg = c;
+        for (int e = N->offsets[c] + 1; e < N->offsets[c + 1]; ++e) {
             const int k = N->nbr[e];
-            const float w0 = x0 - ed[0], w1 = x1 - ed[1], w2 = x2 - ed[2];
-            const float dk = dot3c(w0, w1, w2, w0, w1, w2);
-            if (dk < bd || (dk == bd && before(N, k, bk))) bd = dk, bk = k;
+            const float dk = dist2_to(x, N->edge + 4 * (int64_t)e);
+            if (dk < best || (dk == best && rank_of(N, k) < rank_of(N, arg))) best = dk, arg = k;
         }
-        if (bk == c) break;
-        c = bk;
+        if (arg == c) break;
+        c = arg;
         ++*steps;
     }
     return c;
 }
 
-/* foam_infer.cu:199-257 */
-static void eval_cell(const ICtx* N, int c, float t, const float o[3], const float d[3], const float b[16], Cache* cc,
-                      int want_exit, float* sigma, float* mmin, Blend* B, float* t_exit, int* next, int* n_dens,
-                      int* n_sh) {
-    const int blend = N->mode != LAZY;
+typedef struct {
+    float sigma, m_min, t_exit;
+    int next;
+    Mix mix;
+} CellScan;
+
+/* crossing of the face between site pc and neighbour record p along the ray, when d . (p - pc) > 0 */
+static int face_crossing(const float* p, const float* pc, const float o[3], const float d[3], float* t) {
+    const float n0 = p[0] - pc[0], n1 = p[1] - pc[1], n2 = p[2] - pc[2];
+    const float towards = dot3c(n0, n1, n2, d[0], d[1], d[2]);
+    if (!(towards > 0.f)) return 0;
+    const float h0 = fmaf(0.5f, p[0] + pc[0], -o[0]), h1 = fmaf(0.5f, p[1] + pc[1], -o[1]),
+                h2 = fmaf(0.5f, p[2] + pc[2], -o[2]);
+    *t = dot3c(h0, h1, h2, n0, n1, n2) / towards;
+    return 1;
+}
+
+/* one scan of cell c for the sample at o + t d (foam_infer.cu:199-257) */
+static void scan_cell(const ICtx* N, int c, float t, const float o[3], const float d[3], const float b[16],
+                      SlotCache* cache, int find_exit, CellScan* S, int* n_dens, int* n_sh) {
+    const int mixing = N->mode != EXACT;
     const float* pc = N->points4 + 4 * (int64_t)c;
-    const float x0 = fmaf(t, d[0], o[0]), x1 = fmaf(t, d[1], o[1]), x2 = fmaf(t, d[2], o[2]);
-    const int e0 = N->offsets[c], e1 = N->offsets[c + 1];
-    *sigma = 0.f, *mmin = KINF;
-    blend_init(B);
-    *t_exit = KINF, *next = INT_MAX;
-    for (int e = e0; e < e1; ++e) {
-        const float* ed = N->edge + 4 * (int64_t)e;
+    const float x[3] = {fmaf(t, d[0], o[0]), fmaf(t, d[1], o[1]), fmaf(t, d[2], o[2])};
+    S->sigma = 0.f, S->m_min = KINF, S->t_exit = KINF, S->next = INT_MAX;
+    mix_reset(&S->mix);
+    const int e0 = N->offsets[c];
+    for (int e = e0; e < N->offsets[c + 1]; ++e) {
+        const float* rec = N->edge + 4 * (int64_t)e;
         const int k = N->nbr[e];
-        if (want_exit && e > e0) {
-            const float n0 = ed[0] - pc[0], n1 = ed[1] - pc[1], n2 = ed[2] - pc[2];
-            const float dn = dot3c(n0, n1, n2, d[0], d[1], d[2]);
-            if (dn > 0.f) {
-                const float m0 = fmaf(0.5f, ed[0] + pc[0], -o[0]), m1 = fmaf(0.5f, ed[1] + pc[1], -o[1]),
-                            m2 = fmaf(0.5f, ed[2] + pc[2], -o[2]);
-                const float tt = dot3c(m0, m1, m2, n0, n1, n2) / dn;
-                if (tt < *t_exit || (tt == *t_exit && (*next == INT_MAX || before(N, k, *next)))) *t_exit = tt, *next = k;
-            }
+        float tc;
+        if (find_exit && e != e0 && face_crossing(rec, pc, o, d, &tc) &&
+            (tc < S->t_exit || (tc == S->t_exit && (S->next == INT_MAX || rank_of(N, k) < rank_of(N, S->next)))))
+            S->t_exit = tc, S->next = k;
+        if (N->stage < 1) continue;
+        const float v0 = x[0] - rec[0], v1 = x[1] - rec[1], v2 = x[2] - rec[2];
+        const float r2 = dot3c(v0, v1, v2, v0, v1, v2);
+        float r2_cut, lam;
+        record_bounds(rec, &r2_cut, &lam);
+        const float* row = N->attr + ATTR * (int64_t)k;
+        if (r2 <= r2_cut) {
+            S->sigma += expf(row[6] - 0.5f * quad6(row, v0, v1, v2));
+            ++*n_dens;
         }
-        if (N->stage >= 1) {
-            const float v0 = x0 - ed[0], v1 = x1 - ed[1], v2 = x2 - ed[2];
-            const float r2 = dot3c(v0, v1, v2, v0, v1, v2);
-            float cut_r2, cut_lam;
-            cutoffs(ed, &cut_r2, &cut_lam);
-            const float* a = N->attr + 20 * (int64_t)k;
-            if (r2 <= cut_r2) {
-                *sigma += expf(a[6] - 0.5f * maha6(a, v0, v1, v2));
-                ++*n_dens;
-            }
-            if (N->stage >= 2) {
-                const float lb = r2 * cut_lam;
-                if (blend ? lb <= B->m + N->color_cut : lb < *mmin) {
-                    const float m = maha6(a + 8, v0, v1, v2);
-                    if (blend) {
-                        if (m <= B->m + N->color_cut) {
-                            float c3[3];
-                            if (N->mode == BAKED) {
-                                c3[0] = a[16], c3[1] = a[17], c3[2] = a[18];
-                            } else {
-                                cached_color(N, cc, k, b, c3, n_sh);
-                            }
-                            blend_add(B, m, c3[0], c3[1], c3[2]);
-                        }
-                    } else {
-                        *mmin = fminf(*mmin, m);
-                    }
-                }
-            }
+        if (N->stage < 2) continue;
+        const float floor_m = r2 * lam;
+        if (mixing ? !(floor_m <= S->mix.m_min + N->color_cut) : !(floor_m < S->m_min)) continue;
+        const float m = quad6(row + 8, v0, v1, v2);
+        if (!mixing) {
+            S->m_min = fminf(S->m_min, m);
+            continue;
         }
+        if (!(m <= S->mix.m_min + N->color_cut)) continue;
+        float rgb[3];
+        if (N->mode == BAKED)
+            rgb[0] = row[16], rgb[1] = row[17], rgb[2] = row[18];
+        else
+            cache_colour(N, cache, k, b, rgb, n_sh);
+        mix_add(&S->mix, m, rgb);
     }
 }
 
-/* foam_infer.cu:260-284 */
-static void color_lazy(const ICtx* N, int c, float t, float mmin, const float o[3], const float d[3],
-                       const float b[16], Cache* cc, float C[3], int* n_sh) {
-    const float x0 = fmaf(t, d[0], o[0]), x1 = fmaf(t, d[1], o[1]), x2 = fmaf(t, d[2], o[2]);
-    const int e0 = N->offsets[c], e1 = N->offsets[c + 1];
-    const float cut = mmin + N->color_cut;
-    float A = 0.f, r = 0.f, g = 0.f, bl = 0.f;
-    for (int e = e0; e < e1; ++e) {
-        const float* ed = N->edge + 4 * (int64_t)e;
-        const float v0 = x0 - ed[0], v1 = x1 - ed[1], v2 = x2 - ed[2];
-        float cut_r2, cut_lam;
-        cutoffs(ed, &cut_r2, &cut_lam);
-        if (dot3c(v0, v1, v2, v0, v1, v2) * cut_lam > cut) continue;
+typedef struct {
+    float t, sigma, m_min, rgb[3];
+    int coloured, cell;
+} Point;
+
+/* exact-mode colour of a sample: blend of the neighbours within m_min + color_cut (foam_infer.cu:260-284) */
+static void exact_colour(const ICtx* N, Point* s, const float o[3], const float d[3], const float b[16],
+                         SlotCache* cache, int* n_sh) {
+    const float x[3] = {fmaf(s->t, d[0], o[0]), fmaf(s->t, d[1], o[1]), fmaf(s->t, d[2], o[2])};
+    const float limit = s->m_min + N->color_cut;
+    float wsum = 0.f, sum[3] = {0.f, 0.f, 0.f};
+    for (int e = N->offsets[s->cell]; e < N->offsets[s->cell + 1]; ++e) {
+        const float* rec = N->edge + 4 * (int64_t)e;
+        const float v0 = x[0] - rec[0], v1 = x[1] - rec[1], v2 = x[2] - rec[2];
+        float r2_cut, lam;
+        record_bounds(rec, &r2_cut, &lam);
+        if (dot3c(v0, v1, v2, v0, v1, v2) * lam > limit) continue;
         const int k = N->nbr[e];
-        const float* a = N->attr + 20 * (int64_t)k;
-        const float m = maha6(a + 8, v0, v1, v2);
-        if (m > cut) continue;
-        const float w = expf(-0.5f * (m - mmin));
-        float c3[3];
-        cached_color(N, cc, k, b, c3, n_sh);
-        A += w, r += w * c3[0], g += w * c3[1], bl += w * c3[2];
+        const float m = quad6(N->attr + ATTR * (int64_t)k + 8, v0, v1, v2);
+        if (m > limit) continue;
+        const float a = expf(-0.5f * (m - s->m_min));
+        float rgb[3];
+        cache_colour(N, cache, k, b, rgb, n_sh);
+        wsum += a;
+        for (int ch = 0; ch < 3; ++ch) sum[ch] += a * rgb[ch];
     }
-    const float inv = 1.f / A;
-    C[0] = r * inv, C[1] = g * inv, C[2] = bl * inv;
+    const float inv = 1.f / wsum;
+    for (int ch = 0; ch < 3; ++ch) s->rgb[ch] = sum[ch] * inv;
+    s->coloured = 1;
 }
 
-/* foam_infer.cu:286-361 */
+static void take_point(const ICtx* N, Point* s, const CellScan* S, float t, int cell) {
+    s->t = t, s->sigma = S->sigma, s->m_min = S->m_min, s->cell = cell;
+    s->coloured = N->stage >= 2 && N->mode != EXACT;
+    if (s->coloured)
+        mix_mean(&S->mix, s->rgb);
+    else
+        s->rgb[0] = s->rgb[1] = s->rgb[2] = 0.f;
+}
+
+/* one ray (foam_infer.cu:286-361) */
 static void infer_ray(void* vc, int64_t r) {
     const ICtx* N = (const ICtx*)vc;
-    const int blend = N->stage >= 2 && N->mode != LAZY;
-    Cache cc;
-    for (int i = 0; i < ICACHE; ++i) cc.key[i] = -1, cc.c[i][0] = cc.c[i][1] = cc.c[i][2] = 0.f;
+    SlotCache cache;
+    for (int s = 0; s < SLOTS; ++s) cache.site[s] = -1, cache.rgb[s][0] = cache.rgb[s][1] = cache.rgb[s][2] = 0.f;
     const float o[3] = {N->o[3 * r], N->o[3 * r + 1], N->o[3 * r + 2]};
     const float d[3] = {N->d[3 * r], N->d[3 * r + 1], N->d[3 * r + 2]};
     const float t_near = N->near[r], t_far = N->far[r];
     const int max_samples = N->cap != NULL ? N->cap[r] : INT_MAX;
     float b[16] = {0};
     if (N->stage >= 2 && N->mode != BAKED) sh_basis(d[0], d[1], d[2], N->deg, b);
-    int walk_steps = 0, n_dens = 0, n_sh = 0;
-    int c = iwalk_to(N, N->start[r], fmaf(t_near, d[0], o[0]), fmaf(t_near, d[1], o[1]), fmaf(t_near, d[2], o[2]),
-                     &walk_steps);
-    float sP, mP, t_exit;
-    int next;
-    Blend BP;
-    eval_cell(N, c, t_near, o, d, b, &cc, 1, &sP, &mP, &BP, &t_exit, &next, &n_dens, &n_sh);
-    float tP = t_near, CP[3] = {0.f, 0.f, 0.f};
-    int hasP = 0, cP = c;
-    if (blend) {
-        const float inv = 1.f / BP.a;
-        CP[0] = BP.r * inv, CP[1] = BP.g * inv, CP[2] = BP.b * inv, hasP = 1;
-    }
-    float T = 1.f, acc[3] = {0.f, 0.f, 0.f}, dep = 0.f;
-    int n_samples = 1, n_color = 0;
-    for (int it = 0; it < MAX_CELLS; ++it) {
-        const int last = next == INT_MAX || t_exit >= t_far || n_samples + 1 >= max_samples;
-        const float tQ = last ? t_far : fmaxf(t_exit, tP);
-        const int cQ = last ? c : next;
-        float sQ, mQ;
-        Blend BQ;
-        eval_cell(N, cQ, tQ, o, d, b, &cc, !last, &sQ, &mQ, &BQ, &t_exit, &next, &n_dens, &n_sh);
+    int walk_steps = 0, n_dens = 0, n_sh = 0, n_samples = 1, n_coloured = 0;
+    const float x_near[3] = {fmaf(t_near, d[0], o[0]), fmaf(t_near, d[1], o[1]), fmaf(t_near, d[2], o[2])};
+    const int first = nearest_site(N, N->start[r], x_near, &walk_steps);
+    CellScan S;
+    scan_cell(N, first, t_near, o, d, b, &cache, 1, &S, &n_dens, &n_sh);
+    Point P, Q;
+    take_point(N, &P, &S, t_near, first);
+    float T = 1.f, fg[3] = {0.f, 0.f, 0.f}, depth = 0.f;
+    for (int cell = 0; cell < MAX_CELLS; ++cell) {
+        const int last = S.next == INT_MAX || S.t_exit >= t_far || n_samples + 1 >= max_samples;
+        const float tQ = last ? t_far : fmaxf(S.t_exit, P.t);
+        const int cQ = last ? P.cell : S.next;
+        scan_cell(N, cQ, tQ, o, d, b, &cache, !last, &S, &n_dens, &n_sh);
         ++n_samples;
-        const float delta = tQ - tP;
-        const float alpha = 1.f - expf(-0.5f * (sP + sQ) * delta);
+        take_point(N, &Q, &S, tQ, cQ);
+        const float alpha = 1.f - expf(-0.5f * (P.sigma + Q.sigma) * (Q.t - P.t));
         const float w = T * alpha;
-        float CQ[3] = {0.f, 0.f, 0.f};
-        int hasQ = 0;
-        if (blend) {
-            const float inv = 1.f / BQ.a;
-            CQ[0] = BQ.r * inv, CQ[1] = BQ.g * inv, CQ[2] = BQ.b * inv, hasQ = 1;
-        }
         if (N->stage >= 2 && w > N->w_thresh) {
-            if (!blend) {
-                if (!hasP) color_lazy(N, cP, tP, mP, o, d, b, &cc, CP, &n_sh);
-                color_lazy(N, cQ, tQ, mQ, o, d, b, &cc, CQ, &n_sh);
-                hasQ = 1;
+            if (N->mode == EXACT) {
+                if (!P.coloured) exact_colour(N, &P, o, d, b, &cache, &n_sh);
+                exact_colour(N, &Q, o, d, b, &cache, &n_sh);
             }
-            for (int a = 0; a < 3; ++a) acc[a] += w * 0.5f * (CP[a] + CQ[a]);
-            dep += w * 0.5f * (tP + tQ);
-            ++n_color;
+            for (int a = 0; a < 3; ++a) fg[a] += w * 0.5f * (P.rgb[a] + Q.rgb[a]);
+            depth += w * 0.5f * (P.t + Q.t);
+            ++n_coloured;
         }
         T *= 1.f - alpha;
-        tP = tQ, sP = sQ, mP = mQ, hasP = hasQ, cP = cQ, c = cQ;
-        for (int a = 0; a < 3; ++a) CP[a] = CQ[a];
+        P = Q;
         if (last || T < N->t_thresh) break;
     }
-    for (int a = 0; a < 3; ++a) N->rgb[3 * r + a] = acc[a];
+    for (int a = 0; a < 3; ++a) N->rgb[3 * r + a] = fg[a];
     N->T[r] = T;
-    N->depth[r] = dep;
-    int32_t* s = N->stats + 5 * r;
-    s[0] = n_samples, s[1] = n_color, s[2] = walk_steps, s[3] = n_dens, s[4] = n_sh;
+    N->depth[r] = depth;
+    int32_t* out = N->stats + 5 * r;
+    out[0] = n_samples, out[1] = n_coloured, out[2] = walk_steps, out[3] = n_dens, out[4] = n_sh;
 }
 
 int vgo_foam_infer(const float* points4, const int32_t* offsets, const int32_t* nbr, const float* edge,
@@ -1242,7 +1255,7 @@ int vgo_foam_infer(const float* points4, const int32_t* offsets, const int32_t* 
                    float t_thresh, float w_thresh, float color_cut, int color_mode, int stage, const int32_t* cap,
                    const int32_t* orig, float* rgb, float* T, float* depth, int32_t* stats, int n_threads) {
     (void)n_sites;
-    if (color_mode < LAZY || color_mode > FUSED || stage < 0 || stage > 2) return 1;
+    if (color_mode < EXACT || color_mode > FUSED || stage < 0 || stage > 2) return 1;
     ICtx N;
     memset(&N, 0, sizeof(N));
     N.points4 = points4, N.offsets = offsets, N.nbr = nbr, N.edge = edge, N.attr = attr, N.sh = sh;

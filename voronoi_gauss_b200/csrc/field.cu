@@ -207,7 +207,7 @@ __global__ void __launch_bounds__(kBlock)
     sh_basis(dx, dy, dz, F.sh_deg, b);
     const int e0 = __ldg(g.off + c), e1 = __ldg(g.off + c + 1);
     Blend B;
-    blend_init(B);
+    B.reset();
     for (int e = e0; e < e1; ++e) {
         const float4 E = __ldg(g.edge + e);
         const int k = site_of(E);
@@ -216,9 +216,9 @@ __global__ void __launch_bounds__(kBlock)
         const float v0 = __fsub_rn(x0, E.x), v1 = __fsub_rn(x1, E.y), v2 = __fsub_rn(x2, E.z);
         float col[3];
         site_color(F, k, b, col);
-        blend_add(B, maha(G0, G1, v0, v1, v2), col[0], col[1], col[2]);
+        B.add(maha(G0, G1, v0, v1, v2), col[0], col[1], col[2]);
     }
-    rgb[3 * t] = B.r / B.a, rgb[3 * t + 1] = B.g / B.a, rgb[3 * t + 2] = B.b / B.a;
+    rgb[3 * t] = B.sum[0] / B.wsum, rgb[3 * t + 1] = B.sum[1] / B.wsum, rgb[3 * t + 2] = B.sum[2] / B.wsum;
 }
 
 // vgf.cu:284-335: for each neighbour with normalised weight a_k >= kMinWeight, dL/dsh_k = a_k dL/dC

@@ -292,7 +292,7 @@ __global__ void __launch_bounds__(kBlock, VG_COLOR_MINB)
             x[p][0] = x[p][1] = x[p][2] = 0.f;
 #pragma unroll
             for (int k = 0; k < 16; ++k) b[p][k] = 0.f;
-            blend_init(B[p]);
+            B[p].reset();
             if (li < C.z) {
                 const int sl = __ldg(order + C.y + li);
                 const int64_t r = r0 + sl / K, s = sl % K;
@@ -341,17 +341,17 @@ __global__ void __launch_bounds__(kBlock, VG_COLOR_MINB)
                             if (i < 48) c[i % 3] += b[p][i / 3] * f[u];
                         }
                     }
-                    blend_add(B[p], maha(r2, r3, v0, v1, v2), fmaxf(c[0], 0.f), fmaxf(c[1], 0.f), fmaxf(c[2], 0.f));
+                    B[p].add(maha(r2, r3, v0, v1, v2), fmaxf(c[0], 0.f), fmaxf(c[1], 0.f), fmaxf(c[2], 0.f));
                 }
             }
         }
 #pragma unroll
         for (int p = 0; p < kPer; ++p) {
             if (slot[p] < 0) continue;
-            const float inv_a = 1.f / B[p].a;
+            const float inv_a = 1.f / B[p].wsum;
             float* q = rec + slot[p] * kRecord;
-            q[3] = B[p].r * inv_a;
-            reinterpret_cast<float4*>(q)[1] = make_float4(B[p].g * inv_a, B[p].b * inv_a, B[p].m, inv_a);
+            q[3] = B[p].sum[0] * inv_a;
+            reinterpret_cast<float4*>(q)[1] = make_float4(B[p].sum[1] * inv_a, B[p].sum[2] * inv_a, B[p].m_min, inv_a);
         }
     }
 }

@@ -1,13 +1,23 @@
-// Inference rendering on the reference's packed inference layout (foam_infer.cu:1-25, built by
-// render.py:pack_foam): one thread per ray; the self-first neighbourhood of a cell is one run of
-// float4 edges (p_j, half2(r2_j, lam_j)), per-site records attr (N, 5 x float4) and SH in fp32 or fp16.
+// Inference renderer on the packed inference layout of render.pack_foam (foam_infer.cu:376-435 is the
+// interface it replaces). The layout is self-first: cell c owns the edge run [offsets[c], offsets[c+1]),
+// whose first record is the site itself, each record a float4 (p_j, half2(r2_j, lam_j)) with the site id
+// in a parallel array; per-site rows attr (N, 5 x float4) = density conic + min(raw, 30) | colour conic |
+// baked colour; SH in fp32 or fp16.
 //
-// One pass over a cell's edges gives the exit face, the density (skipping neighbours beyond sqrt(r2))
-// and either the smallest colour Mahalanobis distance (lazy colours, blended in a second pass for the
-// segments with weight > w_thresh), an online colour blend (fused) or a blend of baked per-view site
-// colours (baked). Site colours max(SH_k(d) + 1/2, 0) are kept in an 8-slot per-ray direct-mapped cache
-// in shared memory. STAGE 0 / 1 are the reference's ablations (exit faces only / + density).
-// Per-ray stats (B, 5): samples, coloured segments, walk steps, density terms, SH evaluations.
+// One thread per ray (rays of a pixel tile share a warp). The samples are those of the training renderer:
+// x(near), every exit-face crossing and x(far). Every sample scans its cell's run once for the exit face,
+// the density (neighbours farther than sqrt(r2) skipped) and the colour, which, by mode, is
+//   exact  the smallest colour Mahalanobis distance m_min only (neighbours whose bound r2 lam is not
+//          below the current m_min are skipped); segments with weight > w_thresh then blend their two
+//          end samples in a second scan over the neighbours within m_min + color_cut;
+//   fused  an online blend in the same scan over the neighbours within m + color_cut of the running
+//          minimum;
+//   baked  the same blend of the per-view site colours of bake_colors.
+// Site colours max(SH_k(d) + 1/2, 0) depend only on the ray direction, so each ray keeps a direct-mapped
+// cache of 8 of them in shared memory. Stages 0 and 1 are the reference's ablations: exit faces only, and
+// exit faces + density. Per-ray stats (B, 5): samples, coloured segments, walk steps, density terms
+// evaluated, SH evaluations; these counts follow the reference's skipping and caching rules, so they
+// match its kernel's.
 #include <cuda_fp16.h>
 
 #include "vg_common.cuh"
@@ -15,294 +25,329 @@
 namespace vg {
 namespace {
 
-constexpr int kBlock = 128;
-constexpr int kCache = 8;
-// unroll factor of the per-cell edge loop (loads of later edges issued before earlier arithmetic)
+constexpr int kThreads = 128;
+constexpr int kSlots = 8;  // colour cache entries per ray (a power of two)
+// unroll factor of the per-cell edge scan (loads of later edges issued before earlier arithmetic)
 #ifndef VG_INFER_UNROLL
 #define VG_INFER_UNROLL 2
 #endif
-constexpr int kInferUnroll = VG_INFER_UNROLL;
-constexpr int kLazy = 0, kBaked = 1, kFused = 2;
+constexpr int kScanUnroll = VG_INFER_UNROLL;
+constexpr int kAttrRows = 5;                               // float4 rows per site in attr
+enum ColourMode { kExact = 0, kBakedColour = 1, kFusedColour = 2 };  // the API's color_mode values
 
-struct Net {
-    const float4* __restrict__ points;
-    const int* __restrict__ offsets;
-    const int* __restrict__ nbr;
-    const float4* __restrict__ edge;
-    const float4* __restrict__ attr;
-    const float4* __restrict__ sh;
-    const int* __restrict__ orig;
+// The inference layout as one thread reads it.
+struct Layout {
+    InferNet net;
+    __device__ __forceinline__ int first(int c) const { return __ldg(net.offsets + c); }
+    __device__ __forceinline__ int end(int c) const { return __ldg(net.offsets + c + 1); }
+    __device__ __forceinline__ float4 record(int e) const { return __ldg(net.edge + e); }
+    __device__ __forceinline__ int site(int e) const { return __ldg(net.nbr + e); }
+    __device__ __forceinline__ float4 centre(int c) const { return __ldg(net.points + c); }
+    __device__ __forceinline__ const float4* rows(int k) const { return net.attr + kAttrRows * static_cast<int64_t>(k); }
+    // tie-break order of sites: their ids before any renumbering
+    __device__ __forceinline__ int rank(int k) const { return net.orig != nullptr ? __ldg(net.orig + k) : k; }
 };
 
-__device__ __forceinline__ bool before(const Net& N, int k, int j) {
-    return N.orig != nullptr ? __ldg(N.orig + k) < __ldg(N.orig + j) : k < j;
+// (r2, lam) of an edge record: beyond squared distance r2 the site's density is negligible, lam bounds the
+// eigenvalues of its colour conic from below (so m >= r2 lam).
+__device__ __forceinline__ float2 record_bounds(const float4& rec) {
+    const float packed = rec.w;
+    return __half22float2(*reinterpret_cast<const __half2*>(&packed));
 }
 
-__device__ __forceinline__ float2 cutoffs(const float4& e) {
-    const float w = e.w;
-    return __half22float2(*reinterpret_cast<const __half2*>(&w));
+__device__ __forceinline__ float dist2(float x0, float x1, float x2, const float4& p) {
+    const float v0 = __fsub_rn(x0, p.x), v1 = __fsub_rn(x1, p.y), v2 = __fsub_rn(x2, p.z);
+    return dot3c(v0, v1, v2, v0, v1, v2);
 }
 
+// The 48 SH coefficients of site k as floats, in (basis function, channel) order.
 template <bool HALF>
-__device__ __forceinline__ void site_color(const Net& N, int k, const float (&b)[16], float (&c)[3]) {
-    c[0] = c[1] = c[2] = 0.5f;
+__device__ __forceinline__ void coefficients(const void* sh, int k, float (&f)[48]) {
     if (HALF) {
-        const float4* s = N.sh + 6 * static_cast<int64_t>(k);
+        const float4* row = static_cast<const float4*>(sh) + 6 * static_cast<int64_t>(k);
 #pragma unroll
         for (int q = 0; q < 6; ++q) {
-            const float4 f = __ldg(s + q);
-            const __half2* h = reinterpret_cast<const __half2*>(&f);
+            const float4 v = __ldg(row + q);
+            const __half2* h = reinterpret_cast<const __half2*>(&v);
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
-                const float2 p = __half22float2(h[u]);
-                const int i0 = 8 * q + 2 * u, i1 = i0 + 1;
-                c[i0 % 3] += b[i0 / 3] * p.x;
-                c[i1 % 3] += b[i1 / 3] * p.y;
+                const float2 pair = __half22float2(h[u]);
+                f[8 * q + 2 * u] = pair.x, f[8 * q + 2 * u + 1] = pair.y;
             }
         }
     } else {
-        const float4* s = N.sh + 12 * static_cast<int64_t>(k);
+        const float4* row = static_cast<const float4*>(sh) + 12 * static_cast<int64_t>(k);
 #pragma unroll
         for (int q = 0; q < 12; ++q) {
-            const float4 f = __ldg(s + q);
-            const float v[4] = {f.x, f.y, f.z, f.w};
-#pragma unroll
-            for (int u = 0; u < 4; ++u) c[(4 * q + u) % 3] += b[(4 * q + u) / 3] * v[u];
+            const float4 v = __ldg(row + q);
+            f[4 * q] = v.x, f[4 * q + 1] = v.y, f[4 * q + 2] = v.z, f[4 * q + 3] = v.w;
         }
     }
-    c[0] = fmaxf(c[0], 0.f), c[1] = fmaxf(c[1], 0.f), c[2] = fmaxf(c[2], 0.f);
 }
 
-struct Cache {
-    float4* col;  // slot s of this thread at col[s * kBlock]
-    template <bool HALF>
-    __device__ __forceinline__ void get(const Net& N, int k, const float (&b)[16], float (&c)[3], int& n_sh) {
-        float4& e = col[(k & (kCache - 1)) * kBlock];
-        const float4 v = e;
-        if (__float_as_int(v.w) == k) {
-            c[0] = v.x, c[1] = v.y, c[2] = v.z;
+// max(SH_k(d) + 1/2, 0) with the basis b of the ray direction; each channel sums the basis functions in
+// order.
+template <bool HALF>
+__device__ __forceinline__ void clamped_colour(const void* sh, int k, const float (&b)[16], float (&rgb)[3]) {
+    float f[48];
+    coefficients<HALF>(sh, k, f);
+    rgb[0] = rgb[1] = rgb[2] = 0.5f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+#pragma unroll
+        for (int ch = 0; ch < 3; ++ch) rgb[ch] += b[j] * f[3 * j + ch];
+#pragma unroll
+    for (int ch = 0; ch < 3; ++ch) rgb[ch] = fmaxf(rgb[ch], 0.f);
+}
+
+// Direct-mapped per-ray cache of clamped site colours in shared memory: entry k mod kSlots holds
+// (rgb, k); a miss evaluates the SH, replaces the entry and counts one SH evaluation.
+template <bool HALF>
+struct SlotCache {
+    float4* entry0;  // this thread's first entry; entries kThreads apart
+    __device__ __forceinline__ void clear() {
+#pragma unroll
+        for (int s = 0; s < kSlots; ++s) entry0[s * kThreads] = make_float4(0.f, 0.f, 0.f, __int_as_float(-1));
+    }
+    __device__ __forceinline__ void colour(const Layout& L, int k, const float (&b)[16], float (&rgb)[3],
+                                           int& n_sh) {
+        float4& slot = entry0[(k & (kSlots - 1)) * kThreads];
+        const float4 held = slot;
+        if (__float_as_int(held.w) == k) {
+            rgb[0] = held.x, rgb[1] = held.y, rgb[2] = held.z;
             return;
         }
-        site_color<HALF>(N, k, b, c);
-        e = make_float4(c[0], c[1], c[2], __int_as_float(k));
+        clamped_colour<HALF>(L.net.sh, k, b, rgb);
+        slot = make_float4(rgb[0], rgb[1], rgb[2], __int_as_float(k));
         ++n_sh;
     }
 };
 
-__device__ __forceinline__ int walk(const Net& N, int c, float x0, float x1, float x2, int& steps, int& err) {
+// Greedy walk on the layout to the site nearest to x (steps to the neighbour with the smallest squared
+// distance; equal distances go to the smaller rank).
+__device__ __forceinline__ int nearest_site(const Layout& L, int c, float x0, float x1, float x2, int& steps,
+                                            int& err) {
     for (int it = 0; it < kWalkCap; ++it) {
-        const float4 pc = __ldg(N.points + c);
-        const float u0 = __fsub_rn(x0, pc.x), u1 = __fsub_rn(x1, pc.y), u2 = __fsub_rn(x2, pc.z);
-        float bd = dot3c(u0, u1, u2, u0, u1, u2);
-        int bk = c;
-        const int e0 = __ldg(N.offsets + c), e1 = __ldg(N.offsets + c + 1);
-        for (int e = e0 + 1; e < e1; ++e) {
-            const float4 ed = __ldg(N.edge + e);
-            const int k = __ldg(N.nbr + e);
-            const float v0 = __fsub_rn(x0, ed.x), v1 = __fsub_rn(x1, ed.y), v2 = __fsub_rn(x2, ed.z);
-            const float dk = dot3c(v0, v1, v2, v0, v1, v2);
-            if (dk < bd || (dk == bd && before(N, k, bk))) bd = dk, bk = k;
+        float best = dist2(x0, x1, x2, L.centre(c));
+        int arg = c;
+        const int e1 = L.end(c);
+        for (int e = L.first(c) + 1; e < e1; ++e) {
+            const int k = L.site(e);
+            const float dk = dist2(x0, x1, x2, L.record(e));
+            if (dk < best || (dk == best && L.rank(k) < L.rank(arg))) best = dk, arg = k;
         }
-        if (bk == c) return c;
-        c = bk;
+        if (arg == c) return c;
+        c = arg;
         ++steps;
     }
     err |= kErrWalkCap;
     return c;
 }
 
-struct CellOut {
-    float sigma, mmin, t_exit;
-    int next;
-    Blend B;
+// What one scan of a cell yields for the sample at o + t d.
+struct CellScan {
+    float sigma;   // density
+    float m_min;   // smallest colour Mahalanobis distance among the neighbours not skipped (exact mode)
+    Blend mix;     // blended colour (fused / baked modes)
+    float t_exit;  // exit-face distance along the ray, kInf when none was asked for or none lies ahead
+    int next;      // the cell behind the exit face, INT_MAX when none
 };
 
-template <int STAGE, int COLOR, bool HALF>
-__device__ __forceinline__ void eval_cell(const Net& N, const InferCfg& M, int c, float t, const float (&o)[3],
-                                          const float (&d)[3], const float (&b)[16], Cache& cc, bool want_exit,
-                                          CellOut& out, int& n_dens, int& n_sh) {
-    constexpr bool BLEND = COLOR != kLazy;
-    const float4 pc = __ldg(N.points + c);
+// Crossing of the face between cell site pc and neighbour record p along the ray, when the ray moves
+// towards the neighbour (d . (p - pc) > 0): the t where o + t d reaches the bisector plane.
+__device__ __forceinline__ bool face_crossing(const float4& p, const float4& pc, const float (&o)[3],
+                                              const float (&d)[3], float& t) {
+    const float n0 = __fsub_rn(p.x, pc.x), n1 = __fsub_rn(p.y, pc.y), n2 = __fsub_rn(p.z, pc.z);
+    const float towards = dot3c(n0, n1, n2, d[0], d[1], d[2]);
+    if (!(towards > 0.f)) return false;
+    const float h0 = __fmaf_rn(0.5f, __fadd_rn(p.x, pc.x), -o[0]);
+    const float h1 = __fmaf_rn(0.5f, __fadd_rn(p.y, pc.y), -o[1]);
+    const float h2 = __fmaf_rn(0.5f, __fadd_rn(p.z, pc.z), -o[2]);
+    t = __fdiv_rn(dot3c(h0, h1, h2, n0, n1, n2), towards);
+    return true;
+}
+
+template <int STAGE, int MODE, bool HALF>
+__device__ __forceinline__ void scan_cell(const Layout& L, const InferCfg& cfg, int c, float t, const float (&o)[3],
+                                          const float (&d)[3], const float (&b)[16], SlotCache<HALF>& cache,
+                                          bool find_exit, CellScan& S, int& n_dens, int& n_sh) {
+    constexpr bool kMix = MODE != kExact;
+    const float4 pc = L.centre(c);
     const float x0 = along(o[0], t, d[0]), x1 = along(o[1], t, d[1]), x2 = along(o[2], t, d[2]);
-    const int e0 = __ldg(N.offsets + c), e1 = __ldg(N.offsets + c + 1);
-    out.sigma = 0.f, out.mmin = kInf, out.t_exit = kInf, out.next = INT_MAX;
-    blend_init(out.B);
-#pragma unroll kInferUnroll
+    S.sigma = 0.f, S.m_min = kInf, S.t_exit = kInf, S.next = INT_MAX;
+    S.mix.reset();
+    const int e0 = L.first(c), e1 = L.end(c);
+#pragma unroll kScanUnroll
     for (int e = e0; e < e1; ++e) {
-        const float4 ed = __ldg(N.edge + e);
-        const int k = __ldg(N.nbr + e);
-        if (want_exit && e > e0) {
-            const float n0 = __fsub_rn(ed.x, pc.x), n1 = __fsub_rn(ed.y, pc.y), n2 = __fsub_rn(ed.z, pc.z);
-            const float dn = dot3c(n0, n1, n2, d[0], d[1], d[2]);
-            if (dn > 0.f) {
-                const float m0 = __fmaf_rn(0.5f, __fadd_rn(ed.x, pc.x), -o[0]);
-                const float m1 = __fmaf_rn(0.5f, __fadd_rn(ed.y, pc.y), -o[1]);
-                const float m2 = __fmaf_rn(0.5f, __fadd_rn(ed.z, pc.z), -o[2]);
-                const float tt = __fdiv_rn(dot3c(m0, m1, m2, n0, n1, n2), dn);
-                if (tt < out.t_exit || (tt == out.t_exit && (out.next == INT_MAX || before(N, k, out.next))))
-                    out.t_exit = tt, out.next = k;
-            }
+        const float4 rec = L.record(e);
+        const int k = L.site(e);
+        float tc;
+        if (find_exit && e != e0 && face_crossing(rec, pc, o, d, tc) &&
+            (tc < S.t_exit || (tc == S.t_exit && (S.next == INT_MAX || L.rank(k) < L.rank(S.next)))))
+            S.t_exit = tc, S.next = k;
+        if (STAGE < 1) continue;
+        const float v0 = __fsub_rn(x0, rec.x), v1 = __fsub_rn(x1, rec.y), v2 = __fsub_rn(x2, rec.z);
+        const float r2 = dot3c(v0, v1, v2, v0, v1, v2);
+        const float2 bound = record_bounds(rec);
+        const float4* row = L.rows(k);
+        if (r2 <= bound.x) {
+            const float4 conic_a = __ldg(row), conic_b = __ldg(row + 1);  // conic_b.z = min(raw, 30)
+            S.sigma += __expf(conic_b.z - 0.5f * maha(conic_a, conic_b, v0, v1, v2));
+            ++n_dens;
         }
-        if (STAGE >= 1) {
-            const float v0 = __fsub_rn(x0, ed.x), v1 = __fsub_rn(x1, ed.y), v2 = __fsub_rn(x2, ed.z);
-            const float r2 = dot3c(v0, v1, v2, v0, v1, v2);
-            const float2 cut = cutoffs(ed);
-            const float4* a = N.attr + 5 * static_cast<int64_t>(k);
-            if (r2 <= cut.x) {
-                const float4 q0 = __ldg(a), q1 = __ldg(a + 1);
-                out.sigma += __expf(q1.z - 0.5f * maha(q0, q1, v0, v1, v2));
-                ++n_dens;
-            }
-            if (STAGE >= 2) {
-                const float lb = r2 * cut.y;
-                if (BLEND ? lb <= out.B.m + M.color_cut : lb < out.mmin) {
-                    const float4 q2 = __ldg(a + 2), q3 = __ldg(a + 3);
-                    const float m = maha(q2, q3, v0, v1, v2);
-                    if (BLEND) {
-                        if (m <= out.B.m + M.color_cut) {
-                            float c3[3];
-                            if (COLOR == kBaked) {
-                                const float4 q4 = __ldg(a + 4);
-                                c3[0] = q4.x, c3[1] = q4.y, c3[2] = q4.z;
-                            } else {
-                                cc.get<HALF>(N, k, b, c3, n_sh);
-                            }
-                            blend_add(out.B, m, c3[0], c3[1], c3[2]);
-                        }
-                    } else {
-                        out.mmin = fminf(out.mmin, m);
-                    }
-                }
-            }
+        if (STAGE < 2) continue;
+        const float floor_m = r2 * bound.y;  // no colour distance of this neighbour is below it
+        if (kMix ? !(floor_m <= S.mix.m_min + cfg.color_cut) : !(floor_m < S.m_min)) continue;
+        const float m = maha(__ldg(row + 2), __ldg(row + 3), v0, v1, v2);
+        if (!kMix) {
+            S.m_min = fminf(S.m_min, m);
+            continue;
         }
+        if (!(m <= S.mix.m_min + cfg.color_cut)) continue;
+        float rgb[3];
+        if (MODE == kBakedColour) {
+            const float4 baked = __ldg(row + 4);
+            rgb[0] = baked.x, rgb[1] = baked.y, rgb[2] = baked.z;
+        } else {
+            cache.colour(L, k, b, rgb, n_sh);
+        }
+        S.mix.add(m, rgb[0], rgb[1], rgb[2]);
     }
 }
 
+// One sample along the ray and its colour once known.
+struct Sample {
+    float t, sigma, m_min;
+    float rgb[3];
+    bool coloured;
+    int cell;
+};
+
+// Exact-mode colour of sample s: the blend of the neighbours of its cell within m_min + color_cut.
 template <bool HALF>
-__device__ __forceinline__ void color_lazy(const Net& N, const InferCfg& M, int c, float t, float mmin,
-                                           const float (&o)[3], const float (&d)[3], const float (&b)[16], Cache& cc,
-                                           float (&C)[3], int& n_sh) {
-    const float x0 = along(o[0], t, d[0]), x1 = along(o[1], t, d[1]), x2 = along(o[2], t, d[2]);
-    const int e0 = __ldg(N.offsets + c), e1 = __ldg(N.offsets + c + 1);
-    const float cut = mmin + M.color_cut;
-    float A = 0.f, r = 0.f, g = 0.f, bl = 0.f;
-    for (int e = e0; e < e1; ++e) {
-        const float4 ed = __ldg(N.edge + e);
-        const float v0 = __fsub_rn(x0, ed.x), v1 = __fsub_rn(x1, ed.y), v2 = __fsub_rn(x2, ed.z);
-        if (dot3c(v0, v1, v2, v0, v1, v2) * cutoffs(ed).y > cut) continue;
-        const int k = __ldg(N.nbr + e);
-        const float4* a = N.attr + 5 * static_cast<int64_t>(k);
-        const float4 q2 = __ldg(a + 2), q3 = __ldg(a + 3);
-        const float m = maha(q2, q3, v0, v1, v2);
-        if (m > cut) continue;
-        const float w = __expf(-0.5f * (m - mmin));
-        float c3[3];
-        cc.get<HALF>(N, k, b, c3, n_sh);
-        A += w, r += w * c3[0], g += w * c3[1], bl += w * c3[2];
+__device__ __forceinline__ void exact_colour(const Layout& L, const InferCfg& cfg, Sample& s, const float (&o)[3],
+                                             const float (&d)[3], const float (&b)[16], SlotCache<HALF>& cache,
+                                             int& n_sh) {
+    const float x0 = along(o[0], s.t, d[0]), x1 = along(o[1], s.t, d[1]), x2 = along(o[2], s.t, d[2]);
+    const float limit = s.m_min + cfg.color_cut;
+    float wsum = 0.f, sum[3] = {0.f, 0.f, 0.f};
+    const int e1 = L.end(s.cell);
+    for (int e = L.first(s.cell); e < e1; ++e) {
+        const float4 rec = L.record(e);
+        const float v0 = __fsub_rn(x0, rec.x), v1 = __fsub_rn(x1, rec.y), v2 = __fsub_rn(x2, rec.z);
+        if (dot3c(v0, v1, v2, v0, v1, v2) * record_bounds(rec).y > limit) continue;
+        const int k = L.site(e);
+        const float4* row = L.rows(k);
+        const float m = maha(__ldg(row + 2), __ldg(row + 3), v0, v1, v2);
+        if (m > limit) continue;
+        const float a = __expf(-0.5f * (m - s.m_min));
+        float rgb[3];
+        cache.colour(L, k, b, rgb, n_sh);
+        wsum += a, sum[0] += a * rgb[0], sum[1] += a * rgb[1], sum[2] += a * rgb[2];
     }
-    const float inv = 1.f / A;
-    C[0] = r * inv, C[1] = g * inv, C[2] = bl * inv;
+    const float inv = 1.f / wsum;
+    s.rgb[0] = sum[0] * inv, s.rgb[1] = sum[1] * inv, s.rgb[2] = sum[2] * inv;
+    s.coloured = true;
 }
 
-template <int STAGE, int COLOR, bool HALF>
-__global__ void __launch_bounds__(kBlock)
-    infer_kernel(Net N, InferCfg M, RayView R, Outputs out, int* status) {
-    constexpr bool BLEND = STAGE >= 2 && COLOR != kLazy;
-    __shared__ float4 cache_mem[kCache * kBlock];
-    const int64_t r = static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
+template <int STAGE, int MODE, bool HALF>
+__device__ __forceinline__ void take(Sample& s, const CellScan& S, float t, int cell) {
+    s.t = t, s.sigma = S.sigma, s.m_min = S.m_min, s.cell = cell;
+    s.coloured = STAGE >= 2 && MODE != kExact;
+    if (s.coloured)
+        S.mix.mean(s.rgb);
+    else
+        s.rgb[0] = s.rgb[1] = s.rgb[2] = 0.f;
+}
+
+template <int STAGE, int MODE, bool HALF>
+__global__ void __launch_bounds__(kThreads)
+    infer_kernel(Layout L, InferCfg cfg, RayView R, Outputs out, int* status) {
+    __shared__ float4 cache_mem[kSlots * kThreads];
+    const int64_t r = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
     if (r >= R.n) return;
-    Cache cc{cache_mem + threadIdx.x};
+    SlotCache<HALF> cache{cache_mem + threadIdx.x};
+    cache.clear();
+    float o[3], d[3];
 #pragma unroll
-    for (int i = 0; i < kCache; ++i) cc.col[i * kBlock] = make_float4(0.f, 0.f, 0.f, __int_as_float(-1));
-    const float o[3] = {__ldg(R.o + 3 * r), __ldg(R.o + 3 * r + 1), __ldg(R.o + 3 * r + 2)};
-    const float d[3] = {__ldg(R.d + 3 * r), __ldg(R.d + 3 * r + 1), __ldg(R.d + 3 * r + 2)};
+    for (int a = 0; a < 3; ++a) o[a] = __ldg(R.o + 3 * r + a), d[a] = __ldg(R.d + 3 * r + a);
     const float t_near = __ldg(R.near + r), t_far = __ldg(R.far + r);
-    const int max_samples = M.cap != nullptr ? __ldg(M.cap + r) : INT_MAX;
+    const int max_samples = cfg.cap != nullptr ? __ldg(cfg.cap + r) : INT_MAX;
     float b[16];
-    sh_basis(d[0], d[1], d[2], STAGE >= 2 && COLOR != kBaked ? M.sh_deg : 0, b);
-    int err = 0, walk_steps = 0, n_dens = 0, n_sh = 0;
-    int c = walk(N, __ldg(R.start + r), along(o[0], t_near, d[0]), along(o[1], t_near, d[1]),
-                 along(o[2], t_near, d[2]), walk_steps, err);
-    CellOut P;
-    eval_cell<STAGE, COLOR, HALF>(N, M, c, t_near, o, d, b, cc, true, P, n_dens, n_sh);
-    float tP = t_near, sP = P.sigma, mP = P.mmin, CP[3] = {0.f, 0.f, 0.f};
-    float t_exit = P.t_exit;
-    int next = P.next;
-    bool hasP = false;
-    int cP = c;
-    if (BLEND) {
-        const float inv = 1.f / P.B.a;
-        CP[0] = P.B.r * inv, CP[1] = P.B.g * inv, CP[2] = P.B.b * inv, hasP = true;
-    }
-    float T = 1.f, acc[3] = {0.f, 0.f, 0.f}, dep = 0.f;
-    int n_samples = 1, n_color = 0, it = 0;
-    for (; it < kMaxCells; ++it) {
-        const bool last = next == INT_MAX || t_exit >= t_far || n_samples + 1 >= max_samples;
-        const float tQ = last ? t_far : fmaxf(t_exit, tP);
-        const int cQ = last ? c : next;
-        CellOut Q;
-        eval_cell<STAGE, COLOR, HALF>(N, M, cQ, tQ, o, d, b, cc, !last, Q, n_dens, n_sh);
+    sh_basis(d[0], d[1], d[2], STAGE >= 2 && MODE != kBakedColour ? cfg.sh_deg : 0, b);
+    int err = 0, walk_steps = 0, n_dens = 0, n_sh = 0, n_samples = 1, n_coloured = 0;
+
+    const int first = nearest_site(L, __ldg(R.start + r), along(o[0], t_near, d[0]), along(o[1], t_near, d[1]),
+                                   along(o[2], t_near, d[2]), walk_steps, err);
+    CellScan S;
+    scan_cell<STAGE, MODE, HALF>(L, cfg, first, t_near, o, d, b, cache, true, S, n_dens, n_sh);
+    Sample P;
+    take<STAGE, MODE, HALF>(P, S, t_near, first);
+    float T = 1.f, fg[3] = {0.f, 0.f, 0.f}, depth = 0.f;
+    bool done = false;  // the ray ended (far plane, unbounded cell, sample cap or opacity) within kMaxCells
+    for (int cell = 0; cell < kMaxCells && !done; ++cell) {
+        const bool last = S.next == INT_MAX || S.t_exit >= t_far || n_samples + 1 >= max_samples;
+        const float tQ = last ? t_far : fmaxf(S.t_exit, P.t);
+        const int cQ = last ? P.cell : S.next;
+        scan_cell<STAGE, MODE, HALF>(L, cfg, cQ, tQ, o, d, b, cache, !last, S, n_dens, n_sh);
         ++n_samples;
-        const float delta = tQ - tP;
-        const float alpha = 1.f - __expf(-0.5f * (sP + Q.sigma) * delta);
+        Sample Q;
+        take<STAGE, MODE, HALF>(Q, S, tQ, cQ);
+        const float alpha = 1.f - __expf(-0.5f * (P.sigma + Q.sigma) * (Q.t - P.t));
         const float w = T * alpha;
-        float CQ[3] = {0.f, 0.f, 0.f};
-        bool hasQ = false;
-        if (BLEND) {
-            const float inv = 1.f / Q.B.a;
-            CQ[0] = Q.B.r * inv, CQ[1] = Q.B.g * inv, CQ[2] = Q.B.b * inv, hasQ = true;
-        }
-        if (STAGE >= 2 && w > M.w_thresh) {
-            if (!BLEND) {
-                if (!hasP) color_lazy<HALF>(N, M, cP, tP, mP, o, d, b, cc, CP, n_sh);
-                color_lazy<HALF>(N, M, cQ, tQ, Q.mmin, o, d, b, cc, CQ, n_sh);
-                hasQ = true;
+        if (STAGE >= 2 && w > cfg.w_thresh) {
+            if (MODE == kExact) {
+                if (!P.coloured) exact_colour<HALF>(L, cfg, P, o, d, b, cache, n_sh);
+                exact_colour<HALF>(L, cfg, Q, o, d, b, cache, n_sh);
             }
 #pragma unroll
-            for (int a = 0; a < 3; ++a) acc[a] += w * 0.5f * (CP[a] + CQ[a]);
-            dep += w * 0.5f * (tP + tQ);
-            ++n_color;
+            for (int a = 0; a < 3; ++a) fg[a] += w * 0.5f * (P.rgb[a] + Q.rgb[a]);
+            depth += w * 0.5f * (P.t + Q.t);
+            ++n_coloured;
         }
         T *= 1.f - alpha;
-        tP = tQ, sP = Q.sigma, mP = Q.mmin, hasP = hasQ, cP = cQ, c = cQ;
-        t_exit = Q.t_exit, next = Q.next;
-#pragma unroll
-        for (int a = 0; a < 3; ++a) CP[a] = CQ[a];
-        if (last || T < M.t_thresh) break;
+        P = Q;
+        done = last || T < cfg.t_thresh;
     }
-    if (it == kMaxCells) err |= kErrCellCap;
+    if (!done) err |= kErrCellCap;
 #pragma unroll
-    for (int a = 0; a < 3; ++a) out.rgb[3 * r + a] = acc[a];
+    for (int a = 0; a < 3; ++a) out.rgb[3 * r + a] = fg[a];
     out.T[r] = T;
-    out.depth[r] = dep;
+    out.depth[r] = depth;
     int* s = out.stats + 5 * r;
-    s[0] = n_samples, s[1] = n_color, s[2] = walk_steps, s[3] = n_dens, s[4] = n_sh;
+    s[0] = n_samples, s[1] = n_coloured, s[2] = walk_steps, s[3] = n_dens, s[4] = n_sh;
     if (err) atomicOr(status, err);
 }
 
-template <int STAGE, int COLOR, bool HALF>
-void launch(const Net& N, const InferCfg& M, const RayView& R, const Outputs& out, int* status, cudaStream_t st) {
-    infer_kernel<STAGE, COLOR, HALF>
-        <<<static_cast<int>((R.n + kBlock - 1) / kBlock), kBlock, 0, st>>>(N, M, R, out, status);
+template <int STAGE, int MODE, bool HALF>
+void launch(const Layout& L, const InferCfg& cfg, const RayView& R, const Outputs& out, int* status, cudaStream_t st) {
+    const int blocks = static_cast<int>((R.n + kThreads - 1) / kThreads);
+    infer_kernel<STAGE, MODE, HALF><<<blocks, kThreads, 0, st>>>(L, cfg, R, out, status);
 }
 
 }  // namespace
 
-cudaError_t foam_infer(const InferNet& in, const InferCfg& M, const RayView& R, const Outputs& out, int* status,
+cudaError_t foam_infer(const InferNet& net, const InferCfg& cfg, const RayView& R, const Outputs& out, int* status,
                        cudaStream_t st) {
     if (R.n == 0) return cudaSuccess;
-    const Net N{in.points, in.offsets, in.nbr, in.edge, in.attr, static_cast<const float4*>(in.sh), in.orig};
-    const bool half = in.sh_half != 0;
-    if (M.stage == 0)
-        launch<0, kLazy, false>(N, M, R, out, status, st);
-    else if (M.stage == 1)
-        launch<1, kLazy, false>(N, M, R, out, status, st);
-    else if (M.color_mode == kBaked)
-        launch<2, kBaked, false>(N, M, R, out, status, st);
-    else if (M.color_mode == kLazy)
-        half ? launch<2, kLazy, true>(N, M, R, out, status, st) : launch<2, kLazy, false>(N, M, R, out, status, st);
-    else
-        half ? launch<2, kFused, true>(N, M, R, out, status, st) : launch<2, kFused, false>(N, M, R, out, status, st);
+    const Layout L{net};
+    const bool half = net.sh_half != 0;
+    if (cfg.stage == 0) {
+        launch<0, kExact, false>(L, cfg, R, out, status, st);
+    } else if (cfg.stage == 1) {
+        launch<1, kExact, false>(L, cfg, R, out, status, st);
+    } else if (cfg.color_mode == kBakedColour) {
+        launch<2, kBakedColour, false>(L, cfg, R, out, status, st);
+    } else if (cfg.color_mode == kExact) {
+        if (half)
+            launch<2, kExact, true>(L, cfg, R, out, status, st);
+        else
+            launch<2, kExact, false>(L, cfg, R, out, status, st);
+    } else if (half) {
+        launch<2, kFusedColour, true>(L, cfg, R, out, status, st);
+    } else {
+        launch<2, kFusedColour, false>(L, cfg, R, out, status, st);
+    }
     return cudaGetLastError();
 }
 

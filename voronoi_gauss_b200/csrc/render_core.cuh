@@ -39,7 +39,7 @@ __device__ __forceinline__ void eval_sample(const GraphView& g, const FieldView&
     const float4 Pc = __ldg(g.edge + e0);
     float sigma = 0.f;
     Blend B;
-    blend_init(B);
+    B.reset();
     t_exit = kInf, next = -1;
 #pragma unroll kSampleUnroll
     for (int e = e0; e < e1; ++e) {
@@ -54,14 +54,14 @@ __device__ __forceinline__ void eval_sample(const GraphView& g, const FieldView&
             const float4 r2 = __ldg(r + 2), r3 = __ldg(r + 3);
             float c[3];
             cache.get(F, j, b, c);
-            blend_add(B, maha(r2, r3, v0, v1, v2), c[0], c[1], c[2]);
+            B.add(maha(r2, r3, v0, v1, v2), c[0], c[1], c[2]);
         }
     }
     S.sigma = sigma;
     if (COLOR) {
-        S.mmin = B.m;
-        S.inv_a = 1.f / B.a;
-        S.C0 = B.r * S.inv_a, S.C1 = B.g * S.inv_a, S.C2 = B.b * S.inv_a;
+        S.mmin = B.m_min;
+        S.inv_a = 1.f / B.wsum;
+        S.C0 = B.sum[0] * S.inv_a, S.C1 = B.sum[1] * S.inv_a, S.C2 = B.sum[2] * S.inv_a;
     } else {
         S.mmin = 0.f, S.inv_a = 0.f, S.C0 = S.C1 = S.C2 = 0.f;
     }
@@ -90,7 +90,7 @@ __device__ __forceinline__ void eval_color(const GraphView& g, const FieldView& 
                                            ColorCache<SLOTS>& cache, Sample& S) {
     const int e0 = __ldg(g.off + S.cell), e1 = __ldg(g.off + S.cell + 1);
     Blend B;
-    blend_init(B);
+    B.reset();
     for (int e = e0; e < e1; ++e) {
         const float4 E = __ldg(g.edge + e);
         const int j = site_of(E);
@@ -99,11 +99,11 @@ __device__ __forceinline__ void eval_color(const GraphView& g, const FieldView& 
         const float4 r2 = __ldg(r + 2), r3 = __ldg(r + 3);
         float c[3];
         cache.get(F, j, b, c);
-        blend_add(B, maha(r2, r3, v0, v1, v2), c[0], c[1], c[2]);
+        B.add(maha(r2, r3, v0, v1, v2), c[0], c[1], c[2]);
     }
-    S.mmin = B.m;
-    S.inv_a = 1.f / B.a;
-    S.C0 = B.r * S.inv_a, S.C1 = B.g * S.inv_a, S.C2 = B.b * S.inv_a;
+    S.mmin = B.m_min;
+    S.inv_a = 1.f / B.wsum;
+    S.C0 = B.sum[0] * S.inv_a, S.C1 = B.sum[1] * S.inv_a, S.C2 = B.sum[2] * S.inv_a;
 }
 
 __device__ __forceinline__ void red4(float* p, float a, float b, float c, float d) {

@@ -74,30 +74,31 @@ __device__ __forceinline__ float maha(const float4& a, const float4& b, float v0
     return a.x * v0 * v0 + a.w * v1 * v1 + b.y * v2 * v2 + 2.f * (a.y * v0 * v1 + a.z * v0 * v2 + b.x * v1 * v2);
 }
 
-// Real SH basis with the constants and signs of the reference (foam.cu:118-141).
+// Real SH basis up to degree 3 (foam.cu:118-141): the normalisation constants of each band, with the
+// reference's signs, times the Cartesian polynomials of the standard real basis; functions above `deg`
+// are zero.
+namespace shc {
+constexpr float k0 = 0.28209479177387814f;                                                   // l = 0
+constexpr float k1 = 0.4886025119029199f;                                                    // l = 1
+constexpr float k2xy = 1.0925484305920792f, k2z = 0.31539156525252005f, k2d = 0.5462742152960396f;  // l = 2
+constexpr float k3a = 0.5900435899266435f, k3b = 2.890611442640554f, k3c = 0.4570457994644658f,
+                k3z = 0.3731763325901154f, k3d = 1.445305721320277f;                          // l = 3
+}  // namespace shc
+
 __device__ __forceinline__ void sh_basis(float x, float y, float z, int deg, float (&b)[16]) {
-    b[0] = 0.28209479177387814f;
 #pragma unroll
-    for (int i = 1; i < 16; ++i) b[i] = 0.f;
-    if (deg < 1) return;
-    b[1] = -0.4886025119029199f * y;
-    b[2] = 0.4886025119029199f * z;
-    b[3] = -0.4886025119029199f * x;
+    for (int i = 0; i < 16; ++i) b[i] = 0.f;
+    b[0] = shc::k0;
+    if (deg >= 1) b[1] = -shc::k1 * y, b[2] = shc::k1 * z, b[3] = -shc::k1 * x;
     if (deg < 2) return;
     const float xx = x * x, yy = y * y, zz = z * z;
-    b[4] = 1.0925484305920792f * x * y;
-    b[5] = -1.0925484305920792f * y * z;
-    b[6] = 0.31539156525252005f * (2.f * zz - xx - yy);
-    b[7] = -1.0925484305920792f * x * z;
-    b[8] = 0.5462742152960396f * (xx - yy);
+    b[4] = shc::k2xy * x * y, b[5] = -shc::k2xy * y * z, b[6] = shc::k2z * (2.f * zz - xx - yy);
+    b[7] = -shc::k2xy * x * z, b[8] = shc::k2d * (xx - yy);
     if (deg < 3) return;
-    b[9] = -0.5900435899266435f * y * (3.f * xx - yy);
-    b[10] = 2.890611442640554f * x * y * z;
-    b[11] = -0.4570457994644658f * y * (4.f * zz - xx - yy);
-    b[12] = 0.3731763325901154f * z * (2.f * zz - 3.f * xx - 3.f * yy);
-    b[13] = -0.4570457994644658f * x * (4.f * zz - xx - yy);
-    b[14] = 1.445305721320277f * z * (xx - yy);
-    b[15] = -0.5900435899266435f * x * (xx - 3.f * yy);
+    const float around = 4.f * zz - xx - yy;  // shared by the two m = +-1 functions of band 3
+    b[9] = -shc::k3a * y * (3.f * xx - yy), b[10] = shc::k3b * x * y * z, b[11] = -shc::k3c * y * around;
+    b[12] = shc::k3z * z * (2.f * zz - 3.f * xx - 3.f * yy), b[13] = -shc::k3c * x * around;
+    b[14] = shc::k3d * z * (xx - yy), b[15] = -shc::k3a * x * (xx - 3.f * yy);
 }
 
 // SH_k(d) + 1/2 per channel (unclamped) from the packed coefficients of site k.
@@ -164,32 +165,39 @@ __device__ __forceinline__ void exit_candidate(const float4& E, float pc0, float
     }
 }
 
-// Online normalised blend sum_k a_k c_k / sum_k a_k, a_k = exp(-(m_k - m_min) / 2), keeping the
-// running minimum m (the same quantity as the reference's two passes, foam.cu:224-249).
+// Online normalised blend sum_k a_k c_k / sum_k a_k with a_k = exp(-(m_k - m_min) / 2): the sums are
+// kept relative to the smallest m seen so far and rescaled when a smaller one arrives, so one pass gives
+// the quantity of the reference's two passes (foam.cu:224-249).
 struct Blend {
-    float m, a, r, g, b;
-};
-
-__device__ __forceinline__ void blend_init(Blend& B) { B.m = kInf, B.a = B.r = B.g = B.b = 0.f; }
-
-__device__ __forceinline__ void blend_add(Blend& B, float m, float r, float g, float b) {
-    if (m < B.m) {
-        const float s = __expf(-0.5f * (B.m - m));
-        B.a *= s, B.r *= s, B.g *= s, B.b *= s, B.m = m;
+    float m_min, wsum, sum[3];
+    __device__ __forceinline__ void reset() { m_min = kInf, wsum = sum[0] = sum[1] = sum[2] = 0.f; }
+    __device__ __forceinline__ void add(float m, float r, float g, float b) {
+        if (m < m_min) {
+            const float shrink = __expf(-0.5f * (m_min - m));
+            wsum *= shrink, sum[0] *= shrink, sum[1] *= shrink, sum[2] *= shrink;
+            m_min = m;
+        }
+        const float a = __expf(-0.5f * (m - m_min));
+        wsum += a, sum[0] += a * r, sum[1] += a * g, sum[2] += a * b;
     }
-    const float w = __expf(-0.5f * (m - B.m));
-    B.a += w, B.r += w * r, B.g += w * g, B.b += w * b;
-}
+    // the blended colour sum / wsum
+    __device__ __forceinline__ void mean(float (&c)[3]) const {
+        const float inv = 1.f / wsum;
+        c[0] = sum[0] * inv, c[1] = sum[1] * inv, c[2] = sum[2] * inv;
+    }
+};
 
 // Clamped site colour max(SH_k(d) + 1/2, 0) of site k for the ray direction of basis b.
 __device__ __forceinline__ void site_color(const FieldView& F, int k, const float (&b)[16], float (&c)[3]) {
     sh_color(F, k, b, c);
-    c[0] = fmaxf(c[0], 0.f), c[1] = fmaxf(c[1], 0.f), c[2] = fmaxf(c[2], 0.f);
+#pragma unroll
+    for (int ch = 0; ch < 3; ++ch) c[ch] = fmaxf(c[ch], 0.f);
 }
 
 // Per-thread direct-mapped cache of the clamped site colours in shared memory: a site belongs to the
 // neighbourhoods of several consecutive cells of a ray and its colour depends only on the ray
-// direction. Slot s of thread t lives at base[s * stride + t]. SLOTS = 0: no cache.
+// direction. Entry s of thread t lives at base[s * stride + t] as (rgb, site), site -1 when empty.
+// SLOTS = 0: no cache.
 template <int SLOTS>
 struct ColorCache {
     float4* base;
@@ -199,14 +207,15 @@ struct ColorCache {
         for (int s = 0; s < SLOTS; ++s) base[s * stride] = make_float4(0.f, 0.f, 0.f, __int_as_float(-1));
     }
     __device__ __forceinline__ void get(const FieldView& F, int k, const float (&b)[16], float (&c)[3]) {
-        float4& e = base[(k & (SLOTS - 1)) * stride];
-        const float4 v = e;
-        if (__float_as_int(v.w) == k) {
-            c[0] = v.x, c[1] = v.y, c[2] = v.z;
-            return;
+        float4* entry = base + (k & (SLOTS - 1)) * stride;
+        const float4 held = *entry;
+        const bool hit = __float_as_int(held.w) == k;
+        if (!hit) {
+            site_color(F, k, b, c);
+            *entry = make_float4(c[0], c[1], c[2], __int_as_float(k));
+        } else {
+            c[0] = held.x, c[1] = held.y, c[2] = held.z;
         }
-        site_color(F, k, b, c);
-        e = make_float4(c[0], c[1], c[2], __int_as_float(k));
     }
 };
 
