@@ -240,8 +240,8 @@ def run_b200(args):
                                    T_THRESH, W_THRESH, RECORD_CAP)
         if ev:
             ev[1].record()
-        rgb = fg + T[:, None] * torch.sigmoid(model.bg_logit)
-        loss = ((rgb - target) ** 2).mean()
+        background = torch.sigmoid(model.bg_logit)  # seen through what the rays leave unabsorbed
+        loss = ((fg + T.unsqueeze(1) * background - target) ** 2).mean()
         if ev:
             ext.BACKWARD_EVENTS = (ev[2], ev[3])
         loss.backward()

@@ -30,6 +30,7 @@ def load_model(path, device='cuda', requires_grad=False):
 
 def save_model(model, path, normalization=None, args=None):
     """Writes `model` in the reference's checkpoint format (train.py:168-170)."""
-    torch.save({'state': model.state_dict(), 'points': model.graph.points, 'offsets': model.graph.offsets,
-                'adj': model.graph.adj, 'sh_deg': model.sh_deg, 'normalization': normalization,
-                'args': dict(args or {})}, path)
+    g = model.graph
+    record = dict(state=model.state_dict(), points=g.points, offsets=g.offsets, adj=g.adj, sh_deg=model.sh_deg,
+                  normalization=normalization, args=dict(args or {}))
+    torch.save(record, path)

@@ -672,8 +672,8 @@ def conic_reference(log_scale, quat, floor=0.0):
     R = torch.stack((1 - 2 * (yy + zz), 2 * (xy - wz), 2 * (xz + wy),
                      2 * (xy + wz), 1 - 2 * (xx + zz), 2 * (yz - wx),
                      2 * (xz - wy), 2 * (yz + wx), 1 - 2 * (xx + yy)), -1).view(-1, 3, 3)
-    inv_var = 1.0 / (torch.exp(2 * log_scale.clamp(-20, 20)) + floor * floor)
-    A = (R * inv_var[:, None, :]) @ R.transpose(1, 2)
+    variance = torch.exp(2 * log_scale.clamp(-20, 20)) + floor * floor
+    A = (R * (1.0 / variance)[:, None, :]) @ R.transpose(1, 2)
     return A[:, (0, 0, 0, 1, 1, 2), (0, 1, 2, 1, 2, 2)].contiguous()
 
 
@@ -700,8 +700,9 @@ def color(graph, log_scale, quat, sh, x, dirs, site, sh_deg=3):
 
 
 def march(graph, raw, dA, cA, sh, sh_deg, o, d, start, near, mid, far, dt, n_bg, t_thresh=1e-4, w_thresh=1e-4):
-    """Uniform-step fused rendering -> foreground rgb (B, 3), final transmittance (B,), depth (B,), per-ray
-    stats (B, 3) int: samples marched, samples with colour, walk steps (ext.py:172-182)."""
+    """Fixed-step rendering (ext.py:172-182): midpoints of dt steps from near to mid, then n_bg steps evenly
+    spaced in 1/t out to far. Returns the foreground colour (B, 3), the remaining transmittance (B,), the
+    depth (B,) and int32 counts per ray (B, 3): samples marched, samples coloured, walk steps."""
     op = _MarchOp(graph, _rays(o, d, start, near, mid, far), int(sh_deg),
                   (float(dt), int(n_bg), float(t_thresh), float(w_thresh)))
     params = _dense(raw, dA, cA, sh)
@@ -711,10 +712,11 @@ def march(graph, raw, dA, cA, sh, sh_deg, o, d, start, near, mid, far, dt, n_bg,
 
 
 def foam(graph, raw, dA, cA, sh, sh_deg, o, d, start, near, far, t_thresh=1e-4, w_thresh=1e-4, record_cap=256):
-    """Rendering at the interaction points of the rays with the Voronoi faces -> foreground rgb (B, 3), final
-    transmittance (B,), depth (B,), per-ray stats (B, 3) int: samples, segments with colour, walk steps to
-    x(near). With gradients, up to record_cap samples per ray are kept for the backward pass (0: re-trace every
-    ray) (ext.py:205-216)."""
+    """Renders the rays at their crossings with the Voronoi faces (ext.py:205-216). Returns the foreground
+    colour (B, 3) without background, the transmittance left after the last segment (B,), the depth (B,) and
+    int32 counts per ray (B, 3): samples, coloured segments, walk steps to x(near). When gradients are
+    needed, the first record_cap samples of every ray are recorded for the backward pass; rays with more
+    samples, and all rays when record_cap is 0, are traced again there."""
     op = _FoamOp(graph, _rays(o, d, start, near, far), int(sh_deg), float(t_thresh), float(w_thresh),
                  int(record_cap))
     params = _dense(raw, dA, cA, sh)

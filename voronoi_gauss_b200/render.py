@@ -300,12 +300,15 @@ def render_rays_foam_infer(model, pack, o, d, start, near=0.02, far_radius=4.0, 
         cap = torch.empty(0, dtype=torch.int32, device=o.device)
     if pack['inv'] is not None:  # start sites in the renumbered order of the pack
         start = pack['inv'][start.long()]
-    color_cut = 2 * math.log(1 / eps_color) if eps_color > 0 else float('inf')
-    fg, T, depth, stats = ext.foam_infer_extension().foam_infer(
-        pack['points'], pack['offsets'], pack['nbr'], pack['edge'], pack['attr'], pack['sh'], model.sh_deg,
-        o.float().contiguous(), d.float().contiguous(), start.int().contiguous(), t_near.contiguous(),
-        t_far.contiguous(), float(t_thresh), float(w_thresh), color_cut, mode, int(stage), cap.int().contiguous(),
-        pack['orig'])
+    # a neighbour whose colour weight exp(-(m - m_min) / 2) is below eps_color is skipped:
+    # m - m_min > 2 ln(1 / eps_color)
+    skip_beyond = 2 * math.log(1 / eps_color) if eps_color > 0 else float('inf')
+    layout = [pack[k] for k in ('points', 'offsets', 'nbr', 'edge', 'attr', 'sh')]
+    rays = [o.float().contiguous(), d.float().contiguous(), start.int().contiguous(), t_near.contiguous(),
+            t_far.contiguous()]
+    fg, T, depth, stats = ext.foam_infer_extension().foam_infer(*layout, model.sh_deg, *rays, float(t_thresh),
+                                                                float(w_thresh), skip_beyond, mode, int(stage),
+                                                                cap.int().contiguous(), pack['orig'])
     return {'rgb': _over_background(model, fg, T), 'acc': 1.0 - T, 'depth': depth, 'stats': stats}
 
 
