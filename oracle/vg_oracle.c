@@ -84,265 +84,250 @@ static inline void unlock_site(int k) {
 /* ------------------------------------------------------------------------------ field helpers */
 
 typedef struct {
-    const float* p;
-    const int32_t* off;
-    const int32_t* adj;
+    const float* p;        /* (N, 3) site positions */
+    const int32_t* off;    /* (N + 1) CSR offsets into adj */
+    const int32_t* adj;    /* Delaunay neighbours */
 } Graph;
 
 typedef struct {
-    const float *raw, *dA, *cA, *sh;
+    const float *raw, *dA, *cA, *sh; /* (N), (N, 6), (N, 6), (N, 16, 3) */
     int deg;
 } Field;
 
-/* foam.cu:118-141 */
+/* Real SH basis up to degree 3 with the reference's constants and signs (foam.cu:118-141): per band, a
+ * normalisation constant times the Cartesian polynomial of the standard real basis. */
+static const float SH_K0 = 0.28209479177387814f, SH_K1 = 0.4886025119029199f, SH_K2XY = 1.0925484305920792f,
+                   SH_K2Z = 0.31539156525252005f, SH_K2D = 0.5462742152960396f, SH_K3A = 0.5900435899266435f,
+                   SH_K3B = 2.890611442640554f, SH_K3C = 0.4570457994644658f, SH_K3Z = 0.3731763325901154f,
+                   SH_K3D = 1.445305721320277f;
+
 static void sh_basis(float x, float y, float z, int deg, float b[16]) {
-    b[0] = 0.28209479177387814f;
-    for (int i = 1; i < 16; ++i) b[i] = 0.f;
-    if (deg < 1) return;
-    b[1] = -0.4886025119029199f * y;
-    b[2] = 0.4886025119029199f * z;
-    b[3] = -0.4886025119029199f * x;
+    memset(b, 0, 16 * sizeof(float));
+    b[0] = SH_K0;
+    if (deg >= 1) b[1] = -SH_K1 * y, b[2] = SH_K1 * z, b[3] = -SH_K1 * x;
     if (deg < 2) return;
     const float xx = x * x, yy = y * y, zz = z * z;
-    b[4] = 1.0925484305920792f * x * y;
-    b[5] = -1.0925484305920792f * y * z;
-    b[6] = 0.31539156525252005f * (2.f * zz - xx - yy);
-    b[7] = -1.0925484305920792f * x * z;
-    b[8] = 0.5462742152960396f * (xx - yy);
+    b[4] = SH_K2XY * x * y, b[5] = -SH_K2XY * y * z, b[6] = SH_K2Z * (2.f * zz - xx - yy);
+    b[7] = -SH_K2XY * x * z, b[8] = SH_K2D * (xx - yy);
     if (deg < 3) return;
-    b[9] = -0.5900435899266435f * y * (3.f * xx - yy);
-    b[10] = 2.890611442640554f * x * y * z;
-    b[11] = -0.4570457994644658f * y * (4.f * zz - xx - yy);
-    b[12] = 0.3731763325901154f * z * (2.f * zz - 3.f * xx - 3.f * yy);
-    b[13] = -0.4570457994644658f * x * (4.f * zz - xx - yy);
-    b[14] = 1.445305721320277f * z * (xx - yy);
-    b[15] = -0.5900435899266435f * x * (xx - 3.f * yy);
+    const float ring = 4.f * zz - xx - yy;
+    b[9] = -SH_K3A * y * (3.f * xx - yy), b[10] = SH_K3B * x * y * z, b[11] = -SH_K3C * y * ring;
+    b[12] = SH_K3Z * z * (2.f * zz - 3.f * xx - 3.f * yy), b[13] = -SH_K3C * x * ring;
+    b[14] = SH_K3D * z * (xx - yy), b[15] = -SH_K3A * x * (xx - 3.f * yy);
 }
 
-/* foam.cu:143-153 */
+/* SH_k(d) + 1/2 per channel, unclamped, over the first nb basis functions (foam.cu:143-153) */
 static inline void sh_eval(const float* sh, int k, const float b[16], int nb, float c[3]) {
-    const float* p = sh + 48 * (int64_t)k;
-    c[0] = c[1] = c[2] = 0.5f;
-    for (int j = 0; j < nb; ++j) {
-        c[0] += b[j] * p[3 * j];
-        c[1] += b[j] * p[3 * j + 1];
-        c[2] += b[j] * p[3 * j + 2];
+    const float* coef = sh + 48 * (int64_t)k;
+    for (int ch = 0; ch < 3; ++ch) {
+        float sum = 0.5f;
+        for (int j = 0; j < nb; ++j) sum += b[j] * coef[3 * j + ch];
+        c[ch] = sum;
     }
 }
 
-/* foam.cu:101-105 */
+/* v^T A v for the conic of site k stored (xx, xy, xz, yy, yz, zz) (foam.cu:101-105) */
 static inline float maha(const float* A, int k, const float v[3]) {
     const float* a = A + 6 * (int64_t)k;
-    return a[0] * v[0] * v[0] + a[3] * v[1] * v[1] + a[5] * v[2] * v[2] +
-           2.f * (a[1] * v[0] * v[1] + a[2] * v[0] * v[2] + a[4] * v[1] * v[2]);
+    const float diag = a[0] * v[0] * v[0] + a[3] * v[1] * v[1] + a[5] * v[2] * v[2];
+    const float cross = a[1] * v[0] * v[1] + a[2] * v[0] * v[2] + a[4] * v[1] * v[2];
+    return diag + 2.f * cross;
 }
 
+/* x - p_k */
 static inline void offset_to(const float* p, int k, const float x[3], float v[3]) {
-    const int64_t k3 = 3 * (int64_t)k;
-    v[0] = x[0] - p[k3], v[1] = x[1] - p[k3 + 1], v[2] = x[2] - p[k3 + 2];
+    for (int a = 0; a < 3; ++a) v[a] = x[a] - p[3 * (int64_t)k + a];
 }
 
-static inline int neighbor(const Graph* g, int i, int e0, int e) { return e == 0 ? i : g->adj[e0 + e - 1]; }
+/* member e of the neighbourhood {i} U adj(i): the site itself first, then its neighbours in order */
+static inline int member(const Graph* g, int i, int e) { return e == 0 ? i : g->adj[g->off[i] + e - 1]; }
+static inline int members(const Graph* g, int i) { return g->off[i + 1] - g->off[i] + 1; }
 
-/* Greedy walk to the nearest site of x, ties to the smaller index (foam.cu:163-181). */
-static int walk_to(const Graph* g, int cur, const float x[3], int* steps) {
+static inline float dot3(const float a[3], const float b[3]) { return a[0] * b[0] + a[1] * b[1] + a[2] * b[2]; }
+static inline float dot3_pos(const float g[3], const float c[3]) {
+    return g[0] * fmaxf(c[0], 0.f) + g[1] * fmaxf(c[1], 0.f) + g[2] * fmaxf(c[2], 0.f);
+}
+
+/* Greedy walk to the site nearest to x: each step goes to the member of the neighbourhood with the
+ * smallest (squared distance, index) (foam.cu:163-181). */
+static int nearest_walk(const Graph* g, int cur, const float x[3], int* steps) {
     for (int it = 0; it < WALK_CAP; ++it) {
-        const int e0 = g->off[cur], n = g->off[cur + 1] - e0 + 1;
-        float bd = KINF;
-        int bk = INT_MAX;
-        for (int e = 0; e < n; ++e) {
-            const int k = neighbor(g, cur, e0, e);
+        float best = KINF;
+        int arg = INT_MAX;
+        for (int e = 0; e < members(g, cur); ++e) {
+            const int k = member(g, cur, e);
             float v[3];
             offset_to(g->p, k, x, v);
             const float dk = dot3c(v[0], v[1], v[2], v[0], v[1], v[2]);
-            if (dk < bd || (dk == bd && k < bk)) bd = dk, bk = k;
+            if (dk < best || (dk == best && k < arg)) best = dk, arg = k;
         }
-        if (bk == cur) break;
-        cur = bk;
+        if (arg == cur) break;
+        cur = arg;
         ++*steps;
     }
     return cur;
 }
 
-/* Exit face of cell i along the ray (foam.cu:185-209). */
-static void exit_face(const Graph* g, int i, const float o[3], const float d[3], float* t_exit, int* next) {
-    const int64_t i3 = 3 * (int64_t)i;
-    const float pi[3] = {g->p[i3], g->p[i3 + 1], g->p[i3 + 2]};
-    const int e0 = g->off[i], e1 = g->off[i + 1];
-    float bt = KINF;
-    int bk = INT_MAX;
-    for (int e = e0; e < e1; ++e) {
+/* The face through which the ray leaves cell i: the smallest (crossing t, index) among the neighbours the
+ * ray moves towards, crossing the bisector plane of (p_i, p_j) (foam.cu:185-209). */
+static void leave_cell(const Graph* g, int i, const float o[3], const float d[3], float* t_exit, int* next) {
+    const float* pi = g->p + 3 * (int64_t)i;
+    float best_t = KINF;
+    int best_j = INT_MAX;
+    for (int e = g->off[i]; e < g->off[i + 1]; ++e) {
         const int j = g->adj[e];
-        const int64_t j3 = 3 * (int64_t)j;
-        float n[3], m[3];
-        for (int a = 0; a < 3; ++a) {
-            const float pj = g->p[j3 + a];
-            n[a] = pj - pi[a];
-            m[a] = fmaf(0.5f, pj + pi[a], -o[a]);
-        }
-        const float dn = dot3c(n[0], n[1], n[2], d[0], d[1], d[2]);
-        if (dn > 0.f) {
-            const float t = dot3c(m[0], m[1], m[2], n[0], n[1], n[2]) / dn;
-            if (t < bt || (t == bt && j < bk)) bt = t, bk = j;
-        }
+        const float* pj = g->p + 3 * (int64_t)j;
+        float nrm[3], half[3];
+        for (int a = 0; a < 3; ++a) nrm[a] = pj[a] - pi[a], half[a] = fmaf(0.5f, pj[a] + pi[a], -o[a]);
+        const float towards = dot3c(nrm[0], nrm[1], nrm[2], d[0], d[1], d[2]);
+        if (!(towards > 0.f)) continue;
+        const float t = dot3c(half[0], half[1], half[2], nrm[0], nrm[1], nrm[2]) / towards;
+        if (t < best_t || (t == best_t && j < best_j)) best_t = t, best_j = j;
     }
-    *t_exit = bt, *next = bk;
+    *t_exit = best_t, *next = best_j;
 }
 
-/* foam.cu:211-221 */
-static float density_at(const Graph* g, const Field* F, int i, const float x[3]) {
-    const int e0 = g->off[i], n = g->off[i + 1] - e0 + 1;
-    float s = 0.f;
-    for (int e = 0; e < n; ++e) {
-        const int k = neighbor(g, i, e0, e);
+/* sigma(x) = sum over the neighbourhood of exp(min(raw_k, 30) - v^T dA_k v / 2) (foam.cu:211-221) */
+static float cell_density(const Graph* g, const Field* F, int i, const float x[3]) {
+    float sigma = 0.f;
+    for (int e = 0; e < members(g, i); ++e) {
+        const int k = member(g, i, e);
         float v[3];
         offset_to(g->p, k, x, v);
-        s += expf(fminf(F->raw[k], 30.f) - 0.5f * maha(F->dA, k, v));
+        sigma += expf(fminf(F->raw[k], 30.f) - 0.5f * maha(F->dA, k, v));
     }
-    return s;
+    return sigma;
 }
 
+/* A point of a ray and what is known about it. */
 typedef struct {
     float t, x[3];
     int site;
     float sigma;
-    int has_c;
-    float C[3], mmin, inv_a;
-} Sample;
+    int has_c;          /* colour evaluated */
+    float C[3];         /* blended colour */
+    float mmin, inv_a;  /* smallest colour distance, 1 / sum of colour weights */
+} Stop;
 
-/* Normalised blend of the neighbourhood colours (foam.cu:224-249). */
-static void color_at(const Graph* g, const Field* F, Sample* P, const float b[16]) {
-    const int i = P->site;
-    const int e0 = g->off[i], n = g->off[i + 1] - e0 + 1;
-    const int nb = (F->deg + 1) * (F->deg + 1);
-    float ml = KINF;
+/* Colour of the stop: neighbourhood colours max(SH + 1/2, 0) weighted by exp(-(m_k - m_min) / 2),
+ * normalised (foam.cu:224-249). */
+static void blend_colour(const Graph* g, const Field* F, Stop* P, const float b[16]) {
+    const int i = P->site, n = members(g, i), nb = (F->deg + 1) * (F->deg + 1);
+    float m_low = KINF;
     for (int e = 0; e < n; ++e) {
-        const int k = neighbor(g, i, e0, e);
         float v[3];
-        offset_to(g->p, k, P->x, v);
-        ml = fminf(ml, maha(F->cA, k, v));
+        offset_to(g->p, member(g, i, e), P->x, v);
+        m_low = fminf(m_low, maha(F->cA, member(g, i, e), v));
     }
-    P->mmin = ml;
-    float A = 0.f, cr = 0.f, cg = 0.f, cb = 0.f;
+    P->mmin = m_low;
+    float wsum = 0.f, sum[3] = {0.f, 0.f, 0.f};
     for (int e = 0; e < n; ++e) {
-        const int k = neighbor(g, i, e0, e);
-        float v[3];
+        const int k = member(g, i, e);
+        float v[3], c[3];
         offset_to(g->p, k, P->x, v);
         const float a = expf(-0.5f * (maha(F->cA, k, v) - P->mmin));
-        float c[3];
         sh_eval(F->sh, k, b, nb, c);
-        A += a, cr += a * fmaxf(c[0], 0.f), cg += a * fmaxf(c[1], 0.f), cb += a * fmaxf(c[2], 0.f);
+        wsum += a;
+        for (int ch = 0; ch < 3; ++ch) sum[ch] += a * fmaxf(c[ch], 0.f);
     }
-    P->inv_a = 1.f / A;
-    P->C[0] = cr * P->inv_a, P->C[1] = cg * P->inv_a, P->C[2] = cb * P->inv_a;
+    P->inv_a = 1.f / wsum;
+    for (int ch = 0; ch < 3; ++ch) P->C[ch] = sum[ch] * P->inv_a;
     P->has_c = 1;
 }
 
-static void make_sample(const Graph* g, const Field* F, const float o[3], const float d[3], float t, int site,
-                        Sample* P) {
+static void stop_at(const Graph* g, const Field* F, const float o[3], const float d[3], float t, int site, Stop* P) {
+    memset(P, 0, sizeof(*P));
     P->t = t;
     for (int a = 0; a < 3; ++a) P->x[a] = fmaf(t, d[a], o[a]);
     P->site = site;
-    P->sigma = density_at(g, F, site, P->x);
-    P->has_c = 0;
-    P->C[0] = P->C[1] = P->C[2] = 0.f;
-    P->mmin = 0.f, P->inv_a = 0.f;
+    P->sigma = cell_density(g, F, site, P->x);
 }
 
-/* foam.cu:262-270 */
-static int next_sample(const Graph* g, const Field* F, const float o[3], const float d[3], float far,
-                       const Sample* P, int cur, Sample* Q) {
+/* The stop after P in cell cur: its exit face (t clamped to stay monotone), or x(far) when the cell is
+ * unbounded ahead or the face lies beyond far; returns whether it is the last (foam.cu:262-270). */
+static int advance(const Graph* g, const Field* F, const float o[3], const float d[3], float far, const Stop* P,
+                   int cur, Stop* Q) {
     float t_exit;
-    int nxt;
-    exit_face(g, cur, o, d, &t_exit, &nxt);
-    const int last = nxt == INT_MAX || t_exit >= far;
-    make_sample(g, F, o, d, last ? far : fmaxf(t_exit, P->t), last ? cur : nxt, Q);
+    int next;
+    leave_cell(g, cur, o, d, &t_exit, &next);
+    const int last = next == INT_MAX || t_exit >= far;
+    if (last)
+        stop_at(g, F, o, d, far, cur, Q);
+    else
+        stop_at(g, F, o, d, fmaxf(t_exit, P->t), next, Q);
     return last;
 }
 
-/* foam.cu:276-300 */
-static void store_sample(float* rec, int64_t r, int K, int s, const Sample* P) {
+/* record layout (t, site bits, sigma, C rgb, m_min, 1 / sum of weights or 0) (foam.cu:276-300) */
+static void write_record(float* rec, int64_t r, int K, int s, const Stop* P) {
     if (rec == NULL || s >= K) return;
     float* q = rec + (r * K + s) * RECORD;
+    const int32_t site = P->site;
     q[0] = P->t;
-    int32_t site = P->site;
     memcpy(&q[1], &site, 4);
     q[2] = P->sigma;
-    q[3] = P->C[0], q[4] = P->C[1], q[5] = P->C[2];
+    for (int ch = 0; ch < 3; ++ch) q[3 + ch] = P->C[ch];
     q[6] = P->mmin;
     q[7] = P->has_c ? P->inv_a : 0.f;
 }
 
-static void load_sample(const float* rec, int64_t r, int K, int s, const float o[3], const float d[3],
-                        Sample* P) {
+static void read_record(const float* rec, int64_t r, int K, int s, const float o[3], const float d[3], Stop* P) {
     const float* q = rec + (r * K + s) * RECORD;
     P->t = q[0];
     for (int a = 0; a < 3; ++a) P->x[a] = fmaf(P->t, d[a], o[a]);
     memcpy(&P->site, &q[1], 4);
     P->sigma = q[2];
-    P->C[0] = q[3], P->C[1] = q[4], P->C[2] = q[5];
+    for (int ch = 0; ch < 3; ++ch) P->C[ch] = q[3 + ch];
     P->mmin = q[6];
     P->inv_a = q[7];
     P->has_c = P->inv_a > 0.f;
 }
 
-static inline void scatter_conic(float* gA, int k, float gm, const float v[3]) {
+/* dL/dA of a conic term gm v^T A v in storage order (off-diagonal entries count twice) */
+static inline void add_conic_grad(float* gA, int k, float gm, const float v[3]) {
+    static const int row[6] = {0, 0, 0, 1, 1, 2}, col[6] = {0, 1, 2, 1, 2, 2};
     float* a = gA + 6 * (int64_t)k;
-    a[0] += gm * v[0] * v[0];
-    a[1] += 2.f * gm * v[0] * v[1];
-    a[2] += 2.f * gm * v[0] * v[2];
-    a[3] += gm * v[1] * v[1];
-    a[4] += 2.f * gm * v[1] * v[2];
-    a[5] += gm * v[2] * v[2];
+    for (int e = 0; e < 6; ++e) a[e] += (row[e] == col[e] ? gm : 2.f * gm) * v[row[e]] * v[col[e]];
 }
 
 typedef struct {
     float *g_raw, *g_dA, *g_cA, *g_sh;
 } Grads;
 
-/* Gradients of one sample: gs = dL/dsigma, gC = dL/dC (foam.cu:303-343). */
-static void scatter_sample(const Graph* g, const Field* F, const Sample* P, float gs, const float gC[3],
-                           const float b[16], const Grads* G) {
-    const int i = P->site;
-    const int e0 = g->off[i], n = g->off[i + 1] - e0 + 1;
-    if (gs != 0.f) {
-        for (int e = 0; e < n; ++e) {
-            const int q = neighbor(g, i, e0, e);
-            float v[3];
-            offset_to(g->p, q, P->x, v);
-            const float gc = gs * expf(fminf(F->raw[q], 30.f) - 0.5f * maha(F->dA, q, v));
-            if (fabsf(gc) > 1e-12f) {
-                lock_site(q);
-                G->g_raw[q] += gc;
-                scatter_conic(G->g_dA, q, -0.5f * gc, v);
-                unlock_site(q);
-            }
-        }
+/* Gradients of one stop, gs = dL/dsigma and gC = dL/dC, into the neighbourhood's parameters
+ * (foam.cu:303-343). */
+static void stop_grads(const Graph* g, const Field* F, const Stop* P, float gs, const float gC[3], const float b[16],
+                       const Grads* G) {
+    const int i = P->site, n = members(g, i);
+    for (int e = 0; gs != 0.f && e < n; ++e) {
+        const int k = member(g, i, e);
+        float v[3];
+        offset_to(g->p, k, P->x, v);
+        const float gc = gs * expf(fminf(F->raw[k], 30.f) - 0.5f * maha(F->dA, k, v));
+        if (!(fabsf(gc) > 1e-12f)) continue;
+        lock_site(k);
+        G->g_raw[k] += gc;
+        add_conic_grad(G->g_dA, k, -0.5f * gc, v);
+        unlock_site(k);
     }
     if (!P->has_c || (gC[0] == 0.f && gC[1] == 0.f && gC[2] == 0.f)) return;
     const int nb = (F->deg + 1) * (F->deg + 1);
-    const float gCC = gC[0] * P->C[0] + gC[1] * P->C[1] + gC[2] * P->C[2];
+    const float gCC = dot3(gC, P->C);
     for (int e = 0; e < n; ++e) {
-        const int q = neighbor(g, i, e0, e);
-        float v[3];
-        offset_to(g->p, q, P->x, v);
-        const float a = expf(-0.5f * (maha(F->cA, q, v) - P->mmin)) * P->inv_a;
+        const int k = member(g, i, e);
+        float v[3], c[3], dc[3];
+        offset_to(g->p, k, P->x, v);
+        const float a = expf(-0.5f * (maha(F->cA, k, v) - P->mmin)) * P->inv_a;
         if (a < MIN_WEIGHT) continue;
-        float c[3];
-        sh_eval(F->sh, q, b, nb, c);
-        const float dc0 = c[0] > 0.f ? a * gC[0] : 0.f, dc1 = c[1] > 0.f ? a * gC[1] : 0.f,
-                    dc2 = c[2] > 0.f ? a * gC[2] : 0.f;
-        const float ga = gC[0] * fmaxf(c[0], 0.f) + gC[1] * fmaxf(c[1], 0.f) + gC[2] * fmaxf(c[2], 0.f);
-        const float gm = -0.5f * a * (ga - gCC);
-        lock_site(q);
-        float* gsh = G->g_sh + 48 * (int64_t)q;
-        for (int j = 0; j < nb; ++j) {
-            gsh[3 * j] += b[j] * dc0;
-            gsh[3 * j + 1] += b[j] * dc1;
-            gsh[3 * j + 2] += b[j] * dc2;
-        }
-        if (gm != 0.f) scatter_conic(G->g_cA, q, gm, v);
-        unlock_site(q);
+        sh_eval(F->sh, k, b, nb, c);
+        for (int ch = 0; ch < 3; ++ch) dc[ch] = c[ch] > 0.f ? a * gC[ch] : 0.f;
+        const float gm = -0.5f * a * (dot3_pos(gC, c) - gCC);
+        lock_site(k);
+        float* gsh = G->g_sh + 48 * (int64_t)k;
+        for (int j = 0; j < nb; ++j)
+            for (int ch = 0; ch < 3; ++ch) gsh[3 * j + ch] += b[j] * dc[ch];
+        if (gm != 0.f) add_conic_grad(G->g_cA, k, gm, v);
+        unlock_site(k);
     }
 }
 
@@ -367,109 +352,117 @@ typedef struct {
     int n_bg;
 } Ctx;
 
-static void foam_forward_ray(void* vc, int64_t r) {
-    const Ctx* c = (const Ctx*)vc;
-    const float o[3] = {c->o[3 * r], c->o[3 * r + 1], c->o[3 * r + 2]};
-    const float d[3] = {c->d[3 * r], c->d[3 * r + 1], c->d[3 * r + 2]};
-    const float near = c->near[r], far = c->far[r];
-    float b[16];
-    sh_basis(d[0], d[1], d[2], c->F.deg, b);
-    int walk_steps = 0, n_samples = 1, n_color = 0;
-    float x0[3];
-    for (int a = 0; a < 3; ++a) x0[a] = fmaf(near, d[a], o[a]);
-    int cur = walk_to(&c->g, c->start[r], x0, &walk_steps);
-    Sample P, Q;
-    make_sample(&c->g, &c->F, o, d, near, cur, &P);
-    float T = 1.f, acc[3] = {0.f, 0.f, 0.f}, dep = 0.f;
-    for (int it = 0; it < MAX_CELLS; ++it) {
-        const int last = next_sample(&c->g, &c->F, o, d, far, &P, cur, &Q);
-        ++n_samples;
-        const float delta = Q.t - P.t;
-        const float alpha = 1.f - expf(-0.5f * (P.sigma + Q.sigma) * delta);
-        const float w = T * alpha;
-        if (w > c->w_thresh) {
-            if (!P.has_c) color_at(&c->g, &c->F, &P, b);
-            color_at(&c->g, &c->F, &Q, b);
-            for (int a = 0; a < 3; ++a) acc[a] += w * 0.5f * (P.C[a] + Q.C[a]);
-            dep += w * 0.5f * (P.t + Q.t);
-            ++n_color;
-        }
-        T *= 1.f - alpha;
-        store_sample(c->rec, r, c->K, n_samples - 2, &P);
-        P = Q;
-        cur = Q.site;
-        if (last || T < c->t_thresh) break;
-    }
-    store_sample(c->rec, r, c->K, n_samples - 1, &P);
-    for (int a = 0; a < 3; ++a) c->rgb[3 * r + a] = acc[a];
-    c->T[r] = T;
-    c->depth[r] = dep;
-    c->stats[3 * r] = n_samples, c->stats[3 * r + 1] = n_color, c->stats[3 * r + 2] = walk_steps;
+static void ray_of(const Ctx* c, int64_t r, float o[3], float d[3]) {
+    for (int a = 0; a < 3; ++a) o[a] = c->o[3 * r + a], d[a] = c->d[3 * r + a];
 }
 
-static void foam_backward_ray(void* vc, int64_t r) {
+/* Trapezoid compositing over the stops of one ray, records of the first K stops (foam.cu:345-393). */
+static void foam_forward_ray(void* vc, int64_t r) {
     const Ctx* c = (const Ctx*)vc;
-    const float o[3] = {c->o[3 * r], c->o[3 * r + 1], c->o[3 * r + 2]};
-    const float d[3] = {c->d[3 * r], c->d[3 * r + 1], c->d[3 * r + 2]};
+    float o[3], d[3], b[16], x_near[3];
+    ray_of(c, r, o, d);
     const float near = c->near[r], far = c->far[r];
-    float b[16];
     sh_basis(d[0], d[1], d[2], c->F.deg, b);
-    const float gR[3] = {c->g_rgb[3 * r], c->g_rgb[3 * r + 1], c->g_rgb[3 * r + 2]};
-    const float fg[3] = {c->rgb_in[3 * r], c->rgb_in[3 * r + 1], c->rgb_in[3 * r + 2]};
-    const float gT_final = c->g_T[r] * c->T_in[r];
-    const int K = c->K;
-    const int n_stored = c->rec_in != NULL && c->stats_in[3 * r] <= K ? c->stats_in[3 * r] : 0;
-    Sample P, Q;
-    int cur = 0;
-    if (n_stored > 0) {
-        load_sample(c->rec_in, r, K, 0, o, d, &P);
-    } else {
-        int walk_steps = 0;
-        float x0[3];
-        for (int a = 0; a < 3; ++a) x0[a] = fmaf(near, d[a], o[a]);
-        cur = walk_to(&c->g, c->start[r], x0, &walk_steps);
-        make_sample(&c->g, &c->F, o, d, near, cur, &P);
-    }
-    float T = 1.f, acc[3] = {0.f, 0.f, 0.f};
-    float gs_pending = 0.f, gC_pending[3] = {0.f, 0.f, 0.f};
+    int walk_steps = 0, n_stops = 1, n_coloured = 0;
+    for (int a = 0; a < 3; ++a) x_near[a] = fmaf(near, d[a], o[a]);
+    int cur = nearest_walk(&c->g, c->start[r], x_near, &walk_steps);
+    Stop P, Q;
+    stop_at(&c->g, &c->F, o, d, near, cur, &P);
+    float T = 1.f, fg[3] = {0.f, 0.f, 0.f}, depth = 0.f;
     for (int it = 0; it < MAX_CELLS; ++it) {
-        int last;
-        if (n_stored > 0) {
-            if (it + 1 >= n_stored) break;
-            load_sample(c->rec_in, r, K, it + 1, o, d, &Q);
-            last = it + 2 >= n_stored;
-        } else {
-            last = next_sample(&c->g, &c->F, o, d, far, &P, cur, &Q);
-        }
-        const float delta = Q.t - P.t;
-        const float alpha = 1.f - expf(-0.5f * (P.sigma + Q.sigma) * delta);
+        const int last = advance(&c->g, &c->F, o, d, far, &P, cur, &Q);
+        ++n_stops;
+        const float alpha = 1.f - expf(-0.5f * (P.sigma + Q.sigma) * (Q.t - P.t));
         const float w = T * alpha;
-        const float T_next = T * (1.f - alpha);
-        const int active = w > c->w_thresh;
-        float cc[3] = {0.f, 0.f, 0.f};
-        if (active) {
-            if (!P.has_c) color_at(&c->g, &c->F, &P, b);
-            if (!Q.has_c) color_at(&c->g, &c->F, &Q, b);
-            for (int a = 0; a < 3; ++a) {
-                cc[a] = 0.5f * (P.C[a] + Q.C[a]);
-                acc[a] += w * cc[a];
-            }
+        if (w > c->w_thresh) {
+            if (!P.has_c) blend_colour(&c->g, &c->F, &P, b);
+            blend_colour(&c->g, &c->F, &Q, b);
+            for (int ch = 0; ch < 3; ++ch) fg[ch] += w * 0.5f * (P.C[ch] + Q.C[ch]);
+            depth += w * 0.5f * (P.t + Q.t);
+            ++n_coloured;
         }
-        float g_sbar = 0.f;
-        for (int a = 0; a < 3; ++a) g_sbar += gR[a] * (T_next * cc[a] - (fg[a] - acc[a]));
-        g_sbar = delta * (g_sbar - gT_final);
-        const float gc_half[3] = {active ? 0.5f * w * gR[0] : 0.f, active ? 0.5f * w * gR[1] : 0.f,
-                                  active ? 0.5f * w * gR[2] : 0.f};
-        const float gC_P[3] = {gC_pending[0] + gc_half[0], gC_pending[1] + gc_half[1], gC_pending[2] + gc_half[2]};
-        scatter_sample(&c->g, &c->F, &P, gs_pending + 0.5f * g_sbar, gC_P, b, &c->G);
-        gs_pending = 0.5f * g_sbar;
-        for (int a = 0; a < 3; ++a) gC_pending[a] = gc_half[a];
-        T = T_next;
+        T *= 1.f - alpha;
+        write_record(c->rec, r, c->K, n_stops - 2, &P);
         P = Q;
         cur = Q.site;
         if (last || T < c->t_thresh) break;
     }
-    scatter_sample(&c->g, &c->F, &P, gs_pending, gC_pending, b, &c->G);
+    write_record(c->rec, r, c->K, n_stops - 1, &P);
+    for (int ch = 0; ch < 3; ++ch) c->rgb[3 * r + ch] = fg[ch];
+    c->T[r] = T;
+    c->depth[r] = depth;
+    int32_t* st = c->stats + 3 * r;
+    st[0] = n_stops, st[1] = n_coloured, st[2] = walk_steps;
+}
+
+/* Front-to-back replay of one ray from its records (or by tracing it again when it has more stops than
+ * records): the gradient of the segment opacity is dL/d(sigma bar) = dt (sum_c gR_c (T_{s+1} C_s,c -
+ * (fg_c - acc_c)) - g_T T_final), half of it to each end stop; each end stop's colour gets w gR / 2
+ * (foam.cu:395-469). */
+static void foam_backward_ray(void* vc, int64_t r) {
+    const Ctx* c = (const Ctx*)vc;
+    float o[3], d[3], b[16];
+    ray_of(c, r, o, d);
+    const float near = c->near[r], far = c->far[r];
+    sh_basis(d[0], d[1], d[2], c->F.deg, b);
+    const float* gR = c->g_rgb + 3 * r;
+    const float* fg = c->rgb_in + 3 * r;
+    const float tail = c->g_T[r] * c->T_in[r];
+    const int K = c->K;
+    const int recorded = c->rec_in != NULL && c->stats_in[3 * r] <= K ? c->stats_in[3 * r] : 0;
+    Stop P, Q;
+    int cur = 0;
+    if (recorded > 0) {
+        read_record(c->rec_in, r, K, 0, o, d, &P);
+    } else {
+        int walk_steps = 0;
+        float x_near[3];
+        for (int a = 0; a < 3; ++a) x_near[a] = fmaf(near, d[a], o[a]);
+        cur = nearest_walk(&c->g, c->start[r], x_near, &walk_steps);
+        stop_at(&c->g, &c->F, o, d, near, cur, &P);
+    }
+    float T = 1.f, acc[3] = {0.f, 0.f, 0.f};
+    float carry_sigma = 0.f, carry_colour[3] = {0.f, 0.f, 0.f}; /* P's share from the segment before it */
+    for (int it = 0; it < MAX_CELLS; ++it) {
+        int last;
+        if (recorded > 0) {
+            if (it + 1 >= recorded) break;
+            read_record(c->rec_in, r, K, it + 1, o, d, &Q);
+            last = it + 2 >= recorded;
+        } else {
+            last = advance(&c->g, &c->F, o, d, far, &P, cur, &Q);
+        }
+        const float span = Q.t - P.t;
+        const float alpha = 1.f - expf(-0.5f * (P.sigma + Q.sigma) * span);
+        const float w = T * alpha;
+        const float T_after = T * (1.f - alpha);
+        const int lit = w > c->w_thresh;
+        float mean[3] = {0.f, 0.f, 0.f};
+        if (lit) {
+            if (!P.has_c) blend_colour(&c->g, &c->F, &P, b);
+            if (!Q.has_c) blend_colour(&c->g, &c->F, &Q, b);
+            for (int ch = 0; ch < 3; ++ch) {
+                mean[ch] = 0.5f * (P.C[ch] + Q.C[ch]);
+                acc[ch] += w * mean[ch];
+            }
+        }
+        float g_opacity = 0.f;
+        for (int ch = 0; ch < 3; ++ch) g_opacity += gR[ch] * (T_after * mean[ch] - (fg[ch] - acc[ch]));
+        g_opacity = span * (g_opacity - tail);
+        float share[3], to_P[3];
+        for (int ch = 0; ch < 3; ++ch) {
+            share[ch] = lit ? 0.5f * w * gR[ch] : 0.f;
+            to_P[ch] = carry_colour[ch] + share[ch];
+        }
+        stop_grads(&c->g, &c->F, &P, carry_sigma + 0.5f * g_opacity, to_P, b, &c->G);
+        carry_sigma = 0.5f * g_opacity;
+        for (int ch = 0; ch < 3; ++ch) carry_colour[ch] = share[ch];
+        T = T_after;
+        P = Q;
+        cur = Q.site;
+        if (last || T < c->t_thresh) break;
+    }
+    stop_grads(&c->g, &c->F, &P, carry_sigma, carry_colour, b, &c->G);
 }
 
 static void fill_common(Ctx* c, const float* points, const int32_t* offsets, const int32_t* adj, const float* raw,
@@ -523,110 +516,102 @@ int vgo_foam_backward(const float* points, const int32_t* offsets, const int32_t
 
 /* ------------------------------------------------------------------------------------ march */
 
+/* The fixed-step schedule of one ray: n_in midpoints of dt steps from near to mid, then n_bg steps evenly
+ * spaced in 1/t from mid to far (march.cu:134-153). */
 typedef struct {
     float o[3], d[3];
     float near, mid, far;
     int n_in, n_total;
-} MRay;
+} Schedule;
 
-/* march.cu:134-141 */
-static void load_mray(const Ctx* c, int64_t r, MRay* R) {
-    for (int a = 0; a < 3; ++a) R->o[a] = c->o[3 * r + a], R->d[a] = c->d[3 * r + a];
+static void schedule_of(const Ctx* c, int64_t r, Schedule* R) {
+    ray_of(c, r, R->o, R->d);
     R->near = c->near[r], R->mid = c->mid[r], R->far = c->far[r];
     R->n_in = R->mid > R->near ? (int)ceilf((R->mid - R->near) / c->dt) : 0;
     R->n_total = R->n_in + c->n_bg;
 }
 
-/* march.cu:143-153 */
-static void sample_at(const MRay* R, const Ctx* c, int k, float* t, float* delta) {
+static void schedule_step(const Schedule* R, const Ctx* c, int k, float* t, float* delta) {
     if (k < R->n_in) {
-        const float t0 = fmaf((float)k, c->dt, R->near), t1 = fminf(t0 + c->dt, R->mid);
-        *t = 0.5f * (t0 + t1), *delta = t1 - t0;
-    } else {
-        const float i0 = 1.f / R->mid, i1 = 1.f / R->far;
-        const float u0 = (float)(k - R->n_in) / c->n_bg, u1 = (float)(k - R->n_in + 1) / c->n_bg;
-        *t = 1.f / fmaf(0.5f * (u0 + u1), i1 - i0, i0);
-        *delta = 1.f / fmaf(u1, i1 - i0, i0) - 1.f / fmaf(u0, i1 - i0, i0);
+        const float lo = fmaf((float)k, c->dt, R->near), hi = fminf(lo + c->dt, R->mid);
+        *t = 0.5f * (lo + hi), *delta = hi - lo;
+        return;
     }
+    const float inv_mid = 1.f / R->mid, inv_far = 1.f / R->far, span = inv_far - inv_mid;
+    const float u_lo = (float)(k - R->n_in) / c->n_bg, u_hi = (float)(k - R->n_in + 1) / c->n_bg;
+    *t = 1.f / fmaf(0.5f * (u_lo + u_hi), span, inv_mid);
+    *delta = 1.f / fmaf(u_hi, span, inv_mid) - 1.f / fmaf(u_lo, span, inv_mid);
 }
 
-/* march.cu:195-219 */
-static void color_at_x(const Graph* g, const Field* F, int i, const float x[3], const float b[16], float C[3],
-                       float* mmin, float* inv_a) {
-    Sample P;
-    P.site = i;
-    memcpy(P.x, x, sizeof(P.x));
-    color_at(g, F, &P, b);
-    memcpy(C, P.C, sizeof(P.C));
-    *mmin = P.mmin, *inv_a = P.inv_a;
-}
-
+/* alpha = 1 - exp(-sigma dt) per step, the colour where w > w_thresh (march.cu:221-262) */
 static void march_forward_ray(void* vc, int64_t r) {
     const Ctx* c = (const Ctx*)vc;
-    MRay R;
-    load_mray(c, r, &R);
+    Schedule R;
+    schedule_of(c, r, &R);
     float b[16];
     sh_basis(R.d[0], R.d[1], R.d[2], c->F.deg, b);
-    int cur = c->start[r], n_samples = 0, n_color = 0, walk_steps = 0;
-    float T = 1.f, acc[3] = {0.f, 0.f, 0.f}, dep = 0.f;
+    int cur = c->start[r], n_steps = 0, n_coloured = 0, walk_steps = 0;
+    float T = 1.f, fg[3] = {0.f, 0.f, 0.f}, depth = 0.f;
     for (int k = 0; k < R.n_total; ++k) {
-        float t, delta, x[3];
-        sample_at(&R, c, k, &t, &delta);
-        for (int a = 0; a < 3; ++a) x[a] = fmaf(t, R.d[a], R.o[a]);
-        cur = walk_to(&c->g, cur, x, &walk_steps);
-        const float alpha = 1.f - expf(-density_at(&c->g, &c->F, cur, x) * delta);
+        Stop P;
+        float t, delta;
+        schedule_step(&R, c, k, &t, &delta);
+        memset(&P, 0, sizeof(P));
+        for (int a = 0; a < 3; ++a) P.x[a] = fmaf(t, R.d[a], R.o[a]);
+        P.site = cur = nearest_walk(&c->g, cur, P.x, &walk_steps);
+        const float alpha = 1.f - expf(-cell_density(&c->g, &c->F, cur, P.x) * delta);
         const float w = T * alpha;
-        ++n_samples;
+        ++n_steps;
         if (w > c->w_thresh) {
-            float C[3], mmin, inv_a;
-            color_at_x(&c->g, &c->F, cur, x, b, C, &mmin, &inv_a);
-            for (int a = 0; a < 3; ++a) acc[a] += w * C[a];
-            dep += w * t;
-            ++n_color;
+            blend_colour(&c->g, &c->F, &P, b);
+            for (int ch = 0; ch < 3; ++ch) fg[ch] += w * P.C[ch];
+            depth += w * t;
+            ++n_coloured;
         }
         T *= 1.f - alpha;
         if (T < c->t_thresh) break;
     }
-    for (int a = 0; a < 3; ++a) c->rgb[3 * r + a] = acc[a];
+    for (int ch = 0; ch < 3; ++ch) c->rgb[3 * r + ch] = fg[ch];
     c->T[r] = T;
-    c->depth[r] = dep;
-    c->stats[3 * r] = n_samples, c->stats[3 * r + 1] = n_color, c->stats[3 * r + 2] = walk_steps;
+    c->depth[r] = depth;
+    int32_t* st = c->stats + 3 * r;
+    st[0] = n_steps, st[1] = n_coloured, st[2] = walk_steps;
 }
 
+/* the same march again, each step's gradients scattered as it is passed (march.cu:264-345) */
 static void march_backward_ray(void* vc, int64_t r) {
     const Ctx* c = (const Ctx*)vc;
-    MRay R;
-    load_mray(c, r, &R);
+    Schedule R;
+    schedule_of(c, r, &R);
     float b[16];
     sh_basis(R.d[0], R.d[1], R.d[2], c->F.deg, b);
-    const float gR[3] = {c->g_rgb[3 * r], c->g_rgb[3 * r + 1], c->g_rgb[3 * r + 2]};
-    const float fg[3] = {c->rgb_in[3 * r], c->rgb_in[3 * r + 1], c->rgb_in[3 * r + 2]};
-    const float gT_final = c->g_T[r] * c->T_in[r];
+    const float* gR = c->g_rgb + 3 * r;
+    const float* fg = c->rgb_in + 3 * r;
+    const float tail = c->g_T[r] * c->T_in[r];
     int cur = c->start[r], walk_steps = 0;
     float T = 1.f, acc[3] = {0.f, 0.f, 0.f};
     for (int k = 0; k < R.n_total; ++k) {
-        float t, delta, x[3];
-        sample_at(&R, c, k, &t, &delta);
-        for (int a = 0; a < 3; ++a) x[a] = fmaf(t, R.d[a], R.o[a]);
-        cur = walk_to(&c->g, cur, x, &walk_steps);
-        const float alpha = 1.f - expf(-density_at(&c->g, &c->F, cur, x) * delta);
-        const float w = T * alpha;
-        const float T_next = T * (1.f - alpha);
-        Sample P;
+        Stop P;
+        float t, delta;
+        schedule_step(&R, c, k, &t, &delta);
         memset(&P, 0, sizeof(P));
-        P.site = cur;
-        memcpy(P.x, x, sizeof(P.x));
-        const int active = w > c->w_thresh;
-        if (active) {
-            color_at(&c->g, &c->F, &P, b);
-            for (int a = 0; a < 3; ++a) acc[a] += w * P.C[a];
+        for (int a = 0; a < 3; ++a) P.x[a] = fmaf(t, R.d[a], R.o[a]);
+        P.site = cur = nearest_walk(&c->g, cur, P.x, &walk_steps);
+        const float alpha = 1.f - expf(-cell_density(&c->g, &c->F, cur, P.x) * delta);
+        const float w = T * alpha;
+        const float T_after = T * (1.f - alpha);
+        const int lit = w > c->w_thresh;
+        if (lit) {
+            blend_colour(&c->g, &c->F, &P, b);
+            for (int ch = 0; ch < 3; ++ch) acc[ch] += w * P.C[ch];
         }
-        float gsig = 0.f;
-        for (int a = 0; a < 3; ++a) gsig += gR[a] * (T_next * P.C[a] - (fg[a] - acc[a]));
-        gsig = delta * (gsig - gT_final);
-        const float gC[3] = {active ? w * gR[0] : 0.f, active ? w * gR[1] : 0.f, active ? w * gR[2] : 0.f};
-        scatter_sample(&c->g, &c->F, &P, gsig, gC, b, &c->G);
-        T = T_next;
+        float g_sigma = 0.f, g_colour[3];
+        for (int ch = 0; ch < 3; ++ch) {
+            g_sigma += gR[ch] * (T_after * P.C[ch] - (fg[ch] - acc[ch]));
+            g_colour[ch] = lit ? w * gR[ch] : 0.f;
+        }
+        stop_grads(&c->g, &c->F, &P, delta * (g_sigma - tail), g_colour, b, &c->G);
+        T = T_after;
         if (T < c->t_thresh) break;
     }
 }
@@ -667,76 +652,100 @@ int vgo_march_backward(const float* points, const int32_t* offsets, const int32_
 
 /* ------------------------------------------------------------------------------------ conic */
 
-/* vgf.cu:340-344 */
-static void quat_to_rot(float w, float a, float b, float c, float R[9]) {
-    R[0] = 1.f - 2.f * (b * b + c * c), R[1] = 2.f * (a * b - w * c), R[2] = 2.f * (a * c + w * b);
-    R[3] = 2.f * (a * b + w * c), R[4] = 1.f - 2.f * (a * a + c * c), R[5] = 2.f * (b * c - w * a);
-    R[6] = 2.f * (a * c - w * b), R[7] = 2.f * (b * c + w * a), R[8] = 1.f - 2.f * (a * a + b * b);
+/* Rotation of a unit quaternion (w, x, y, z) from its pairwise products (vgf.cu:340-344). */
+static void rotation(const float u[4], float R[9]) {
+    const float w = u[0], x = u[1], y = u[2], z = u[3];
+    const float xx = x * x, yy = y * y, zz = z * z, xy = x * y, xz = x * z, yz = y * z;
+    const float wx = w * x, wy = w * y, wz = w * z;
+    const float rows[9] = {1.f - 2.f * (yy + zz), 2.f * (xy - wz), 2.f * (xz + wy),
+                           2.f * (xy + wz), 1.f - 2.f * (xx + zz), 2.f * (yz - wx),
+                           2.f * (xz - wy), 2.f * (yz + wx), 1.f - 2.f * (xx + yy)};
+    memcpy(R, rows, sizeof(rows));
+}
+
+/* dL/dq from P = dL/dR of the rotation of q / |q|: P contracted with the partial derivatives of the
+ * entries of rotation() with respect to (w, x, y, z), then the radial part removed and divided by |q|. */
+static void quat_grad(const float u[4], float len, const float P[9], float g[4]) {
+    const float w = u[0], x = u[1], y = u[2], z = u[3];
+    const float J[4][9] = {
+        {0.f, -2.f * z, 2.f * y, 2.f * z, 0.f, -2.f * x, -2.f * y, 2.f * x, 0.f},          /* d/dw */
+        {0.f, 2.f * y, 2.f * z, 2.f * y, -4.f * x, -2.f * w, 2.f * z, 2.f * w, -4.f * x},  /* d/dx */
+        {-4.f * y, 2.f * x, 2.f * w, 2.f * x, 0.f, 2.f * z, -2.f * w, 2.f * z, -4.f * y},  /* d/dy */
+        {-4.f * z, -2.f * w, 2.f * x, 2.f * w, -4.f * z, 2.f * y, 2.f * x, 2.f * y, 0.f}}; /* d/dz */
+    float raw[4], radial = 0.f;
+    for (int c = 0; c < 4; ++c) {
+        raw[c] = 0.f;
+        for (int e = 0; e < 9; ++e) raw[c] += P[e] * J[c][e];
+        radial += raw[c] * u[c];
+    }
+    for (int c = 0; c < 4; ++c) g[c] = (raw[c] - radial * u[c]) / len;
+}
+
+/* unit quaternion of row i and its length (at least 1e-12) */
+static float unit_quat(const float* quat, int64_t i, float u[4]) {
+    const float* q = quat + 4 * i;
+    float sq = 0.f;
+    for (int c = 0; c < 4; ++c) sq += q[c] * q[c];
+    const float len = fmaxf(sqrtf(sq), 1e-12f);
+    for (int c = 0; c < 4; ++c) u[c] = q[c] / len;
+    return len;
 }
 
 typedef struct {
-    float qn[4], qnorm, R[9], iv[3], s2[3];
-} ConicLocal;
+    float u[4], len, R[9], iv[3], s2[3];
+} ConicSite;
 
-/* vgf.cu:350-362 */
-static void conic_local(const float* ls, const float* quat, int64_t i, float floor2, ConicLocal* L) {
-    const float* q = quat + 4 * i;
-    L->qnorm = fmaxf(sqrtf(q[0] * q[0] + q[1] * q[1] + q[2] * q[2] + q[3] * q[3]), 1e-12f);
-    for (int k = 0; k < 4; ++k) L->qn[k] = q[k] / L->qnorm;
-    quat_to_rot(L->qn[0], L->qn[1], L->qn[2], L->qn[3], L->R);
+/* R, s^2 = exp(2 clamp(ls, -20, 20)) and 1 / (s^2 + floor^2) of site i (vgf.cu:350-362) */
+static void conic_site(const float* ls, const float* quat, int64_t i, float floor2, ConicSite* L) {
+    L->len = unit_quat(quat, i, L->u);
+    rotation(L->u, L->R);
     for (int k = 0; k < 3; ++k) {
-        const float s = expf(2.f * fminf(fmaxf(ls[3 * i + k], -20.f), 20.f));
-        L->s2[k] = s;
-        L->iv[k] = 1.f / (s + floor2);
+        L->s2[k] = expf(2.f * fminf(fmaxf(ls[3 * i + k], -20.f), 20.f));
+        L->iv[k] = 1.f / (L->s2[k] + floor2);
     }
 }
 
+static const int SYM_ROW[6] = {0, 0, 0, 1, 1, 2}, SYM_COL[6] = {0, 1, 2, 1, 2, 2};
+
+/* A = R diag(iv) R^T in storage order (xx, xy, xz, yy, yz, zz) (vgf.cu:364-380) */
 void vgo_conic_forward(const float* ls, const float* quat, int64_t n, float floor, float* A) {
-    static const int ab[6][2] = {{0, 0}, {0, 1}, {0, 2}, {1, 1}, {1, 2}, {2, 2}};
-    const float floor2 = floor * floor;
     for (int64_t i = 0; i < n; ++i) {
-        ConicLocal L;
-        conic_local(ls, quat, i, floor2, &L);
-        const float* R = L.R;
+        ConicSite L;
+        conic_site(ls, quat, i, floor * floor, &L);
         for (int e = 0; e < 6; ++e) {
-            const int a = ab[e][0], b = ab[e][1];
-            A[6 * i + e] = R[3 * a] * R[3 * b] * L.iv[0] + R[3 * a + 1] * R[3 * b + 1] * L.iv[1] +
-                           R[3 * a + 2] * R[3 * b + 2] * L.iv[2];
+            const float* ra = L.R + 3 * SYM_ROW[e];
+            const float* rb = L.R + 3 * SYM_COL[e];
+            float sum = 0.f;
+            for (int k = 0; k < 3; ++k) sum += ra[k] * L.iv[k] * rb[k];
+            A[6 * i + e] = sum;
         }
     }
 }
 
-/* vgf.cu:382-421 */
+/* dL/dls and dL/dq from dL/dA (vgf.cu:382-421): with G the symmetric matrix of dL/dA,
+ * dL/d iv_k = (R^T G R)_kk, d iv_k / d ls_k = -2 s_k^2 iv_k^2, dL/dR = 2 G R diag(iv). */
 void vgo_conic_backward(const float* ls, const float* quat, int64_t n, float floor, const float* gA, float* g_ls,
                         float* g_quat) {
-    const float floor2 = floor * floor;
     for (int64_t i = 0; i < n; ++i) {
-        ConicLocal L;
-        conic_local(ls, quat, i, floor2, &L);
-        const float* R = L.R;
-        const float* g = gA + 6 * i;
-        const float G[9] = {g[0], 0.5f * g[1], 0.5f * g[2], 0.5f * g[1], g[3], 0.5f * g[4], 0.5f * g[2], 0.5f * g[4], g[5]};
-        float GR[9];
-        for (int a = 0; a < 3; ++a)
-            for (int k = 0; k < 3; ++k) GR[3 * a + k] = G[3 * a] * R[k] + G[3 * a + 1] * R[3 + k] + G[3 * a + 2] * R[6 + k];
-        for (int k = 0; k < 3; ++k) {
-            const float g_iv = R[k] * GR[k] + R[3 + k] * GR[3 + k] + R[6 + k] * GR[6 + k];
-            g_ls[3 * i + k] = g_iv * (-2.f * L.s2[k] * L.iv[k] * L.iv[k]);
+        ConicSite L;
+        conic_site(ls, quat, i, floor * floor, &L);
+        float G[9];
+        for (int e = 0; e < 6; ++e) {
+            const float v = SYM_ROW[e] == SYM_COL[e] ? gA[6 * i + e] : 0.5f * gA[6 * i + e];
+            G[3 * SYM_ROW[e] + SYM_COL[e]] = G[3 * SYM_COL[e] + SYM_ROW[e]] = v;
         }
-        float dR[9];
-        for (int a = 0; a < 3; ++a)
-            for (int k = 0; k < 3; ++k) dR[3 * a + k] = 2.f * GR[3 * a + k] * L.iv[k];
-        const float w = L.qn[0], x = L.qn[1], y = L.qn[2], z = L.qn[3];
-        float dq[4];
-        dq[0] = 2.f * (-z * dR[1] + y * dR[2] + z * dR[3] - x * dR[5] - y * dR[6] + x * dR[7]);
-        dq[1] = 2.f * (y * dR[1] + z * dR[2] + y * dR[3] - 2.f * x * dR[4] - w * dR[5] + z * dR[6] + w * dR[7] -
-                       2.f * x * dR[8]);
-        dq[2] = 2.f * (-2.f * y * dR[0] + x * dR[1] + w * dR[2] + x * dR[3] + z * dR[5] - w * dR[6] + z * dR[7] -
-                       2.f * y * dR[8]);
-        dq[3] = 2.f * (-2.f * z * dR[0] - w * dR[1] + x * dR[2] + w * dR[3] - 2.f * z * dR[4] + y * dR[5] +
-                       x * dR[6] + y * dR[7]);
-        const float proj = dq[0] * w + dq[1] * x + dq[2] * y + dq[3] * z;
-        for (int k = 0; k < 4; ++k) g_quat[4 * i + k] = (dq[k] - proj * L.qn[k]) / L.qnorm;
+        float P[9];
+        for (int k = 0; k < 3; ++k) {
+            float diag = 0.f;
+            for (int a = 0; a < 3; ++a) {
+                float gr = 0.f; /* (G R)_ak */
+                for (int m = 0; m < 3; ++m) gr += G[3 * a + m] * L.R[3 * m + k];
+                diag += L.R[3 * a + k] * gr;
+                P[3 * a + k] = 2.f * gr * L.iv[k];
+            }
+            g_ls[3 * i + k] = diag * (-2.f * L.s2[k] * L.iv[k] * L.iv[k]);
+        }
+        quat_grad(L.u, L.len, P, g_quat + 4 * i);
     }
 }
 
@@ -778,50 +787,39 @@ int vgo_walk(const float* points, const int32_t* offsets, const int32_t* adj, in
     return 0;
 }
 
+/* One site's Gaussian seen from x, its rotation rebuilt from the quaternion as the reference's field
+ * kernels do (vgf.cu:99-124): v = x - p, y = R^T v, 1 / s_k^2 scaled by 1 / scale_mult^2, and the
+ * Mahalanobis distance m = sum_k y_k^2 / s_k^2. */
 typedef struct {
-    float v[3], y[3], is2[3], qn[4], qnorm, R[9], m;
-} GaussLocal;
+    float v[3], y[3], is2[3], u[4], len, R[9], m;
+} SiteGauss;
 
-/* vgf.cu:99-124: the Gaussian of site i at x, rotation rebuilt from the quaternion. */
-static void gauss_local(const float* points, const float* ls, const float* quat, int i, const float x[3],
-                        float inv_mult2, GaussLocal* L) {
-    const int64_t i3 = 3 * (int64_t)i;
-    for (int a = 0; a < 3; ++a) L->v[a] = x[a] - points[i3 + a];
-    const float* q = quat + 4 * (int64_t)i;
-    L->qnorm = fmaxf(sqrtf(q[0] * q[0] + q[1] * q[1] + q[2] * q[2] + q[3] * q[3]), 1e-12f);
-    for (int k = 0; k < 4; ++k) L->qn[k] = q[k] / L->qnorm;
-    quat_to_rot(L->qn[0], L->qn[1], L->qn[2], L->qn[3], L->R);
+static void site_gauss(const float* points, const float* ls, const float* quat, int i, const float x[3],
+                       float inv_mult2, SiteGauss* L) {
+    offset_to(points, i, x, L->v);
+    L->len = unit_quat(quat, i, L->u);
+    rotation(L->u, L->R);
     L->m = 0.f;
     for (int k = 0; k < 3; ++k) {
         L->y[k] = L->R[k] * L->v[0] + L->R[3 + k] * L->v[1] + L->R[6 + k] * L->v[2];
-        const float s = expf(fminf(fmaxf(ls[i3 + k], -20.f), 20.f));
+        const float s = expf(fminf(fmaxf(ls[3 * (int64_t)i + k], -20.f), 20.f));
         L->is2[k] = inv_mult2 / (s * s);
         L->m += L->y[k] * L->y[k] * L->is2[k];
     }
 }
 
-/* vgf.cu:126-153: dL/dls and dL/dq of one Gaussian from gm = dL/dm (accumulated). */
-static void scatter_gauss_grad(const GaussLocal* L, float gm, int i, float* g_ls, float* g_quat) {
-    const int64_t i3 = 3 * (int64_t)i;
-    float yk[3];
+/* accumulates dL/dls and dL/dq of site i from gm = dL/dm (vgf.cu:126-153): dm/dls_k = -2 y_k^2 / s_k^2,
+ * dL/dR_ab = v_a 2 gm y_b / s_b^2 */
+static void site_gauss_grad(const SiteGauss* L, float gm, int i, float* g_ls, float* g_quat) {
+    float scaled[3], P[9], gq[4];
     for (int k = 0; k < 3; ++k) {
-        yk[k] = 2.f * gm * L->y[k] * L->is2[k];
-        g_ls[i3 + k] += -2.f * gm * L->y[k] * L->y[k] * L->is2[k];
+        scaled[k] = 2.f * gm * L->y[k] * L->is2[k];
+        g_ls[3 * (int64_t)i + k] += -2.f * gm * L->y[k] * L->y[k] * L->is2[k];
     }
-    float GR[9];
     for (int a = 0; a < 3; ++a)
-        for (int b = 0; b < 3; ++b) GR[3 * a + b] = L->v[a] * yk[b];
-    const float w = L->qn[0], x = L->qn[1], y = L->qn[2], z = L->qn[3];
-    float dq[4];
-    dq[0] = 2.f * (-z * GR[1] + y * GR[2] + z * GR[3] - x * GR[5] - y * GR[6] + x * GR[7]);
-    dq[1] = 2.f * (y * GR[1] + z * GR[2] + y * GR[3] - 2.f * x * GR[4] - w * GR[5] + z * GR[6] + w * GR[7] -
-                   2.f * x * GR[8]);
-    dq[2] = 2.f * (-2.f * y * GR[0] + x * GR[1] + w * GR[2] + x * GR[3] + z * GR[5] - w * GR[6] + z * GR[7] -
-                   2.f * y * GR[8]);
-    dq[3] = 2.f * (-2.f * z * GR[0] - w * GR[1] + x * GR[2] + w * GR[3] - 2.f * z * GR[4] + y * GR[5] + x * GR[6] +
-                   y * GR[7]);
-    const float proj = dq[0] * w + dq[1] * x + dq[2] * y + dq[3] * z;
-    for (int k = 0; k < 4; ++k) g_quat[4 * (int64_t)i + k] += (dq[k] - proj * L->qn[k]) / L->qnorm;
+        for (int b = 0; b < 3; ++b) P[3 * a + b] = L->v[a] * scaled[b];
+    quat_grad(L->u, L->len, P, gq);
+    for (int c = 0; c < 4; ++c) g_quat[4 * (int64_t)i + c] += gq[c];
 }
 
 /* neighbourhood {i} U adj(i) in the reference's order (vgf.cu:155-161) */
@@ -841,8 +839,8 @@ int vgo_density_forward(const float* points, const int32_t* offsets, const int32
         float s = 0.f;
         for (int j = 0; j < n; ++j) {
             const int k = nbhd(offsets, adj, i, j);
-            GaussLocal L;
-            gauss_local(points, ls, quat, k, x + 3 * t, inv_mult2, &L);
+            SiteGauss L;
+            site_gauss(points, ls, quat, k, x + 3 * t, inv_mult2, &L);
             s += expf(fminf(raw[k], 30.f) - 0.5f * L.m);
         }
         sigma[t] = s;
@@ -862,12 +860,12 @@ int vgo_density_backward(const float* points, const int32_t* offsets, const int3
         const int n = offsets[i + 1] - offsets[i] + 1;
         for (int j = 0; j < n; ++j) {
             const int k = nbhd(offsets, adj, i, j);
-            GaussLocal L;
-            gauss_local(points, ls, quat, k, x + 3 * t, 1.f, &L);
+            SiteGauss L;
+            site_gauss(points, ls, quat, k, x + 3 * t, 1.f, &L);
             const float c = expf(fminf(raw[k], 30.f) - 0.5f * L.m);
             if (c * fabsf(gs) > 1e-12f) {
                 g_raw[k] += gs * c;
-                scatter_gauss_grad(&L, -0.5f * gs * c, k, g_ls, g_quat);
+                site_gauss_grad(&L, -0.5f * gs * c, k, g_ls, g_quat);
             }
         }
     }
@@ -880,7 +878,8 @@ static void unit_dir(const float* dirs, int64_t t, float d[3]) {
     d[0] *= inv, d[1] *= inv, d[2] *= inv;
 }
 
-/* vgf.cu:248-282 */
+/* C(x, d) = sum_k a_k max(SH_k(d) + 1/2, 0) / sum_k a_k, a_k = exp(-(m_k - m_min) / 2), in one pass
+ * with the sums rescaled whenever a smaller m arrives (vgf.cu:248-282) */
 int vgo_color_forward(const float* points, const int32_t* offsets, const int32_t* adj, int64_t n_sites,
                       const float* ls, const float* quat, const float* sh, int sh_deg, const float* x,
                       const float* dirs, const int32_t* site, int64_t m, float* rgb) {
@@ -891,31 +890,30 @@ int vgo_color_forward(const float* points, const int32_t* offsets, const int32_t
         unit_dir(dirs, t, d);
         sh_basis(d[0], d[1], d[2], sh_deg, b);
         const int i = site[t];
-        const int n = offsets[i + 1] - offsets[i] + 1;
-        float mmin = KINF, A = 0.f, cr = 0.f, cg = 0.f, cb = 0.f;
-        for (int j = 0; j < n; ++j) {
+        float m_low = KINF, wsum = 0.f, sum[3] = {0.f, 0.f, 0.f};
+        for (int j = 0; j < offsets[i + 1] - offsets[i] + 1; ++j) {
             const int k = nbhd(offsets, adj, i, j);
-            GaussLocal L;
-            gauss_local(points, ls, quat, k, x + 3 * t, 1.f, &L);
-            if (L.m < mmin) {
-                const float f = mmin == KINF ? 0.f : expf(-0.5f * (mmin - L.m));
-                A *= f, cr *= f, cg *= f, cb *= f;
-                mmin = L.m;
+            SiteGauss L;
+            site_gauss(points, ls, quat, k, x + 3 * t, 1.f, &L);
+            if (L.m < m_low) {
+                const float shrink = m_low == KINF ? 0.f : expf(-0.5f * (m_low - L.m));
+                wsum *= shrink;
+                for (int ch = 0; ch < 3; ++ch) sum[ch] *= shrink;
+                m_low = L.m;
             }
-            const float a = expf(-0.5f * (L.m - mmin));
+            const float a = expf(-0.5f * (L.m - m_low));
             float c[3];
             sh_eval(sh, k, b, nb, c);
-            A += a;
-            cr += a * fmaxf(c[0], 0.f);
-            cg += a * fmaxf(c[1], 0.f);
-            cb += a * fmaxf(c[2], 0.f);
+            wsum += a;
+            for (int ch = 0; ch < 3; ++ch) sum[ch] += a * fmaxf(c[ch], 0.f);
         }
-        rgb[3 * t] = cr / A, rgb[3 * t + 1] = cg / A, rgb[3 * t + 2] = cb / A;
+        for (int ch = 0; ch < 3; ++ch) rgb[3 * t + ch] = sum[ch] / wsum;
     }
     return 0;
 }
 
-/* vgf.cu:284-335 (gradients accumulated into zero-filled outputs) */
+/* gradients of the blend, accumulated into zero-filled outputs (vgf.cu:284-335): dL/dsh_k = a_k b [c_k > 0]
+ * gR, dL/dm_k = -a_k (gR . max(c_k, 0) - gR . C) / 2 */
 int vgo_color_backward(const float* points, const int32_t* offsets, const int32_t* adj, int64_t n_sites,
                        const float* ls, const float* quat, const float* sh, int sh_deg, const float* x,
                        const float* dirs, const int32_t* site, int64_t m, const float* rgb, const float* grad_rgb,
@@ -923,42 +921,39 @@ int vgo_color_backward(const float* points, const int32_t* offsets, const int32_
     (void)n_sites;
     const int nb = (sh_deg + 1) * (sh_deg + 1);
     for (int64_t t = 0; t < m; ++t) {
-        const float gr = grad_rgb[3 * t], gg = grad_rgb[3 * t + 1], gb = grad_rgb[3 * t + 2];
-        if (gr == 0.f && gg == 0.f && gb == 0.f) continue;
-        const int i = site[t];
-        const int n = offsets[i + 1] - offsets[i] + 1;
-        float mmin = KINF;
+        const float* gR = grad_rgb + 3 * t;
+        if (gR[0] == 0.f && gR[1] == 0.f && gR[2] == 0.f) continue;
+        const int i = site[t], n = offsets[i + 1] - offsets[i] + 1;
+        float m_low = KINF, wsum = 0.f;
         for (int j = 0; j < n; ++j) {
-            GaussLocal L;
-            gauss_local(points, ls, quat, nbhd(offsets, adj, i, j), x + 3 * t, 1.f, &L);
-            mmin = fminf(mmin, L.m);
+            SiteGauss L;
+            site_gauss(points, ls, quat, nbhd(offsets, adj, i, j), x + 3 * t, 1.f, &L);
+            m_low = fminf(m_low, L.m);
         }
-        float A = 0.f;
         for (int j = 0; j < n; ++j) {
-            GaussLocal L;
-            gauss_local(points, ls, quat, nbhd(offsets, adj, i, j), x + 3 * t, 1.f, &L);
-            A += expf(-0.5f * (L.m - mmin));
+            SiteGauss L;
+            site_gauss(points, ls, quat, nbhd(offsets, adj, i, j), x + 3 * t, 1.f, &L);
+            wsum += expf(-0.5f * (L.m - m_low));
         }
-        const float inv_a = 1.f / A;
-        const float gCC = gr * rgb[3 * t] + gg * rgb[3 * t + 1] + gb * rgb[3 * t + 2];
+        const float inv_sum = 1.f / wsum;
+        const float gRC = dot3(gR, rgb + 3 * t);
         float d[3], b[16];
         unit_dir(dirs, t, d);
         sh_basis(d[0], d[1], d[2], sh_deg, b);
         for (int j = 0; j < n; ++j) {
             const int k = nbhd(offsets, adj, i, j);
-            GaussLocal L;
-            gauss_local(points, ls, quat, k, x + 3 * t, 1.f, &L);
-            const float a = expf(-0.5f * (L.m - mmin)) * inv_a;
+            SiteGauss L;
+            site_gauss(points, ls, quat, k, x + 3 * t, 1.f, &L);
+            const float a = expf(-0.5f * (L.m - m_low)) * inv_sum;
             if (a < MIN_WEIGHT) continue;
-            float c[3];
+            float c[3], dc[3];
             sh_eval(sh, k, b, nb, c);
-            const float dc[3] = {c[0] > 0.f ? a * gr : 0.f, c[1] > 0.f ? a * gg : 0.f, c[2] > 0.f ? a * gb : 0.f};
+            for (int ch = 0; ch < 3; ++ch) dc[ch] = c[ch] > 0.f ? a * gR[ch] : 0.f;
             float* gs = g_sh + 48 * (int64_t)k;
             for (int q = 0; q < nb; ++q)
                 for (int ch = 0; ch < 3; ++ch) gs[3 * q + ch] += b[q] * dc[ch];
-            const float ga = gr * fmaxf(c[0], 0.f) + gg * fmaxf(c[1], 0.f) + gb * fmaxf(c[2], 0.f);
-            const float gm = -0.5f * a * (ga - gCC);
-            if (gm != 0.f) scatter_gauss_grad(&L, gm, k, g_ls, g_quat);
+            const float gm = -0.5f * a * (dot3_pos(gR, c) - gRC);
+            if (gm != 0.f) site_gauss_grad(&L, gm, k, g_ls, g_quat);
         }
     }
     return 0;
