@@ -61,6 +61,23 @@ def ragged(seqs, dtype):
     return np.concatenate(seqs).astype(dtype), off
 
 
+def composite64(sigma, delta, colour):
+    """float64 front-to-back compositing of segments with optical depths tau = sigma * delta and colours
+    `colour`: opacity a_k = 1 - exp(-tau_k), transmittance the running product of 1 - a (exactly 0 once a
+    segment is opaque), weight_k = a_k prod_{j<k} (1 - a_j). -> (foreground colour, final transmittance)."""
+    opacity = 1 - torch.exp(-sigma * delta)
+    through = torch.cumprod(torch.nn.functional.pad(1 - opacity, (1, 0), value=1.0), 0)
+    return ((opacity * through[:-1])[:, None] * colour).sum(0), through[-1]
+
+
+def mixture_colour(P, cA, X, mask, basis, sh):
+    """float64 colour at the points X: the neighbourhood's max(SH + 1/2, 0) blended with the normalised
+    weights exp(-m_k / 2) of the colour Mahalanobis distances (masked to each point's neighbourhood)."""
+    logits = (-0.5 * test_march.mahalanobis6(P, cA, X)).masked_fill(~mask, -float('inf'))
+    site_colour = (torch.einsum('j,njc->nc', basis, sh) + 0.5).clamp_min(0)
+    return torch.softmax(logits, 1) @ site_colour
+
+
 def foam_reference(pts, offsets, adj, raw, dA, cA, sh, o, d, near, far, g_rgb, g_T, cells0=None, sh_deg=3):
     """float64 trace + compositing + gradients, as test_foam.py:76-104; only the first (sh_deg + 1)^2 SH
     bands are used, as the kernels do (foam.cu:143-153)."""
@@ -77,21 +94,17 @@ def foam_reference(pts, offsets, adj, raw, dA, cA, sh, o, d, near, far, g_rgb, g
         t, cl = test_foam.trace(pts, offsets, adj, o64[r], d64[r], float(near[r]), float(far[r]), start_cell)
         ts.append(t)
         cells.append(cl)
-        X = torch.tensor(o64[r][None] + t[:, None] * d64[r][None])
+        X = torch.from_numpy(o64[r] + np.outer(t, d64[r]))
         mask = test_grad.neighborhood_mask(offsets, adj, torch.tensor(cl), n)
         sigma = (torch.exp(rraw)[None] * torch.exp(-0.5 * test_march.mahalanobis6(P, rdA, X)) * mask).sum(1)
-        a = torch.softmax((-0.5 * test_march.mahalanobis6(P, rcA, X)).masked_fill(~mask, -float('inf')), 1)
-        D = torch.tensor(d64[r])
-        basis = test_grad.sh_basis(D) * (torch.arange(16) < (sh_deg + 1) ** 2)
-        ck = (torch.einsum('j,njc->nc', basis, rsh) + 0.5).clamp_min(0)
-        C = a @ ck
-        delta = torch.tensor(t[1:] - t[:-1])
-        alpha = 1 - torch.exp(-0.5 * (sigma[1:] + sigma[:-1]) * delta)
-        trans = torch.cumprod(torch.cat([torch.ones(1, dtype=torch.float64), 1 - alpha]), 0)
-        w = alpha * trans[:-1]
-        fg_ref.append((w[:, None] * 0.5 * (C[1:] + C[:-1])).sum(0))
-        T_ref.append(trans[-1])
-    fg_ref, T_ref = torch.stack(fg_ref), torch.stack(T_ref)
+        basis = test_grad.sh_basis(torch.tensor(d64[r])) * (torch.arange(16) < (sh_deg + 1) ** 2)
+        C = mixture_colour(P, rcA, X, mask, basis, rsh)
+        # trapezoid rule between consecutive samples (foam.cu:1-16)
+        fg, T = composite64(0.5 * (sigma[1:] + sigma[:-1]), torch.tensor(t[1:] - t[:-1]), 0.5 * (C[1:] + C[:-1]))
+        fg_ref.append(fg)
+        T_ref.append(T)
+    fg_ref = torch.stack(fg_ref)
+    T_ref = torch.stack(T_ref)
     ((fg_ref * torch.tensor(g_rgb, dtype=torch.float64)).sum() +
      (T_ref * torch.tensor(g_T, dtype=torch.float64)).sum()).backward()
     t_flat, t_off = ragged(ts, np.float64)
@@ -171,19 +184,18 @@ def make_march_small():
     for r in range(B):
         t, delta = test_march.samples(near[r].item(), mid[r].item(), far[r].item(), dt, n_bg)
         O, D = o[r].double(), d[r].double()
-        X = O[None] + torch.tensor(t)[:, None] * D[None]
-        site = torch.tensor(tree.query(X.numpy())[1])
+        X = O + torch.outer(torch.tensor(t), D)
+        _, nearest = tree.query(X.numpy())
+        site = torch.from_numpy(nearest)
         sites_all.append(site.numpy().astype(np.int32))
         mask = test_grad.neighborhood_mask(offsets, adj, site, n)
         sigma = (torch.exp(rraw)[None] * torch.exp(-0.5 * test_march.mahalanobis6(P, rdA, X)) * mask).sum(1)
-        alpha = 1 - torch.exp(-sigma * torch.tensor(delta))
-        trans = torch.cumprod(torch.cat([torch.ones(1, dtype=torch.float64), 1 - alpha]), 0)
-        w = alpha * trans[:-1]
-        a = torch.softmax((-0.5 * test_march.mahalanobis6(P, rcA, X)).masked_fill(~mask, -float('inf')), 1)
-        ck = (torch.einsum('j,njc->nc', test_grad.sh_basis(D), rsh) + 0.5).clamp_min(0)
-        fg_ref.append((w[:, None] * (a @ ck)).sum(0))
-        T_ref.append(trans[-1])
-    fg_ref, T_ref = torch.stack(fg_ref), torch.stack(T_ref)
+        # one segment per fixed step, coloured at its midpoint (march.cu:221-262)
+        fg, T = composite64(sigma, torch.tensor(delta), mixture_colour(P, rcA, X, mask, test_grad.sh_basis(D), rsh))
+        fg_ref.append(fg)
+        T_ref.append(T)
+    fg_ref = torch.stack(fg_ref)
+    T_ref = torch.stack(T_ref)
     ((fg_ref * g_rgb.double()).sum() + (T_ref * g_T.double()).sum()).backward()
     s_flat, s_off = ragged(sites_all, np.int32)
     np.savez_compressed(
