@@ -105,7 +105,7 @@ static_assert(kChunk == 32 || kChunk == 64, "VG_CM_CHUNK must be 32 or 64");
 
 // deferred: the colour fields are filled later; the last field marks the samples that need one (-1)
 // orig: the original id of P's site (loaded when P was evaluated, so the store does not wait for it)
-__device__ __forceinline__ void store_sample(float* __restrict__ rec, int64_t r, int K, int s, const Sample& P,
+__device__ __forceinline__ void put_record(float* __restrict__ rec, int64_t r, int K, int s, const Sample& P,
                                              bool has_c, bool deferred, int orig) {
     if (s >= K) return;
     float4* q = reinterpret_cast<float4*>(rec + (r * K + s) * kRecord);
@@ -114,7 +114,7 @@ __device__ __forceinline__ void store_sample(float* __restrict__ rec, int64_t r,
                     : make_float4(P.C1, P.C2, P.mmin, has_c ? P.inv_a : 0.f);
 }
 
-__device__ __forceinline__ void load_sample(const float* __restrict__ rec, int64_t r, int K, int s,
+__device__ __forceinline__ void get_record(const float* __restrict__ rec, int64_t r, int K, int s,
                                             const float (&o)[3], const float (&d)[3], const int* __restrict__ inv,
                                             Sample& P, bool& has_c) {
     const float4* q = reinterpret_cast<const float4*>(rec + (r * K + s) * kRecord);
@@ -163,7 +163,7 @@ __global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
     float b[16];
     if (!kDefer) sh_basis(d[0], d[1], d[2], F.sh_deg, b);
     int err = 0, walk_steps = 0, n_samples = 1, n_color = 0;
-    int cur = walk_to(g, __ldg(g.inv + __ldg(R.start + r)), along(o[0], near, d[0]), along(o[1], near, d[1]),
+    int cur = walk_nearest(g, __ldg(g.inv + __ldg(R.start + r)), along(o[0], near, d[0]), along(o[1], near, d[1]),
                       along(o[2], near, d[2]), walk_steps, err);
     Sample P;
     float t_exit;
@@ -202,7 +202,7 @@ __global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
             ++n_color;
         }
         T *= 1.f - alpha;
-        if (RECORD) store_sample(out.rec, r, K, n_samples - 2, P, has_p, kDefer, p_orig);
+        if (RECORD) put_record(out.rec, r, K, n_samples - 2, P, has_p, kDefer, p_orig);
         if (kDefer && has_p && n_samples - 2 < K && c.cm_count != nullptr)
             atomicAdd(c.cm_count + (r / c.cm_rays) * c.cm_stride + P.cell, 1);
         P = Q;
@@ -212,7 +212,7 @@ __global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
         if (last || T < c.t_thresh) break;
     }
     if (it == kMaxCells) err |= kErrCellCap;
-    if (RECORD) store_sample(out.rec, r, K, n_samples - 1, P, has_p, kDefer, p_orig);
+    if (RECORD) put_record(out.rec, r, K, n_samples - 1, P, has_p, kDefer, p_orig);
     if (kDefer && has_p && n_samples - 1 < K && c.cm_count != nullptr)
         atomicAdd(c.cm_count + (r / c.cm_rays) * c.cm_stride + P.cell, 1);
     if (!kDefer) out.rgb[3 * r] = acc0, out.rgb[3 * r + 1] = acc1, out.rgb[3 * r + 2] = acc2;
@@ -467,7 +467,7 @@ __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
     sh_basis(d[0], d[1], d[2], F.sh_deg, b);
     const float gR0 = __ldg(gi.g_rgb + 3 * r), gR1 = __ldg(gi.g_rgb + 3 * r + 1), gR2 = __ldg(gi.g_rgb + 3 * r + 2);
     const float fg0 = __ldg(gi.rgb + 3 * r), fg1 = __ldg(gi.rgb + 3 * r + 1), fg2 = __ldg(gi.rgb + 3 * r + 2);
-    const float gT_final = __ldg(gi.g_T + r) * __ldg(gi.T + r);
+    const float tail_grad = __ldg(gi.g_T + r) * __ldg(gi.T + r);
     const int K = gi.record_cap;
     const int s_fwd = __ldg(gi.stats + 3 * r);
     const int n_stored = gi.rec != nullptr && K > 0 && s_fwd <= K ? s_fwd : 0;
@@ -477,17 +477,17 @@ __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
     float t_exit = kInf;
     int next = -1;
     if (n_stored > 0) {
-        load_sample(gi.rec, r, K, 0, o, d, g.inv, P, has_p);
+        get_record(gi.rec, r, K, 0, o, d, g.inv, P, has_p);
     } else {
         int walk_steps = 0;
-        const int cur = walk_to(g, __ldg(g.inv + __ldg(R.start + r)), along(o[0], near, d[0]),
+        const int cur = walk_nearest(g, __ldg(g.inv + __ldg(R.start + r)), along(o[0], near, d[0]),
                                 along(o[1], near, d[1]), along(o[2], near, d[2]), walk_steps, err);
         eval_sample<kBwdSlots, true>(g, F, cur, near, o, d, b, cache, true, P, t_exit, next);
     }
     float4* stage = stage_mem + (kAgg ? 16 * (threadIdx.x & ~31) : 0);
     const int lane = threadIdx.x & 31;
     float T = 1.f, acc0 = 0.f, acc1 = 0.f, acc2 = 0.f;
-    float gs_pending = 0.f, gP0 = 0.f, gP1 = 0.f, gP2 = 0.f;  // gradients of P from the segment before it
+    float carry_sigma = 0.f, gP0 = 0.f, gP1 = 0.f, gP2 = 0.f;  // gradients of P from the segment before it
     DirectItems out_items{io.items, io.offsets, io.fill};
     int n_done = 0;  // index of P
     for (int it = 0; it < kMaxCells; ++it) {
@@ -497,7 +497,7 @@ __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
         int next_q = -1;
         if (n_stored > 0) {
             if (it + 1 >= n_stored) break;
-            load_sample(gi.rec, r, K, it + 1, o, d, g.inv, Q, has_q);
+            get_record(gi.rec, r, K, it + 1, o, d, g.inv, Q, has_q);
             last = it + 2 >= n_stored;
         } else {
             last = next < 0 || t_exit >= far;
@@ -507,7 +507,7 @@ __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
         const float delta = Q.t - P.t;
         const float alpha = 1.f - __expf(-0.5f * (P.sigma + Q.sigma) * delta);
         const float w = T * alpha;
-        const float T_next = T * (1.f - alpha);
+        const float T_after = T * (1.f - alpha);
         const bool active = w > c.w_thresh;
         float c0 = 0.f, c1 = 0.f, c2 = 0.f;
         if (active) {
@@ -517,24 +517,24 @@ __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
             c0 = 0.5f * (P.C0 + Q.C0), c1 = 0.5f * (P.C1 + Q.C1), c2 = 0.5f * (P.C2 + Q.C2);
             acc0 += w * c0, acc1 += w * c1, acc2 += w * c2;
         }
-        float g_sbar = gR0 * (T_next * c0 - (fg0 - acc0)) + gR1 * (T_next * c1 - (fg1 - acc1)) +
-                       gR2 * (T_next * c2 - (fg2 - acc2));
-        g_sbar = delta * (g_sbar - gT_final);
+        float g_opacity = gR0 * (T_after * c0 - (fg0 - acc0)) + gR1 * (T_after * c1 - (fg1 - acc1)) +
+                       gR2 * (T_after * c2 - (fg2 - acc2));
+        g_opacity = delta * (g_opacity - tail_grad);
         const float h0 = active ? 0.5f * w * gR0 : 0.f, h1 = active ? 0.5f * w * gR1 : 0.f,
                     h2 = active ? 0.5f * w * gR2 : 0.f;
         if (MODE == kItems && VG_BWD_DIRECT)
-            out_items.put(P, gs_pending + 0.5f * g_sbar, gP0 + h0, gP1 + h1, gP2 + h2, has_p, d);
+            out_items.put(P, carry_sigma + 0.5f * g_opacity, gP0 + h0, gP1 + h1, gP2 + h2, has_p, d);
         else if (MODE == kItems)
-            emit_item(io.items, (r - io.r0) * K + it, P, gs_pending + 0.5f * g_sbar, gP0 + h0, gP1 + h1, gP2 + h2,
+            emit_item(io.items, (r - io.r0) * K + it, P, carry_sigma + 0.5f * g_opacity, gP0 + h0, gP1 + h1, gP2 + h2,
                       has_p, io.count);
         else if (kAgg)
-            scatter_sample_agg(g, F, P, gs_pending + 0.5f * g_sbar, gP0 + h0, gP1 + h1, gP2 + h2, has_p, b, cache, grad,
+            scatter_sample_agg(g, F, P, carry_sigma + 0.5f * g_opacity, gP0 + h0, gP1 + h1, gP2 + h2, has_p, b, cache, grad,
                                stage, lane);
         else
-            scatter_sample(g, F, P, gs_pending + 0.5f * g_sbar, gP0 + h0, gP1 + h1, gP2 + h2, has_p, b, cache, grad);
-        gs_pending = 0.5f * g_sbar;
+            sample_grads(g, F, P, carry_sigma + 0.5f * g_opacity, gP0 + h0, gP1 + h1, gP2 + h2, has_p, b, cache, grad);
+        carry_sigma = 0.5f * g_opacity;
         gP0 = h0, gP1 = h1, gP2 = h2;
-        T = T_next;
+        T = T_after;
         P = Q;
         has_p = has_q;
         t_exit = t_exit_q, next = next_q;
@@ -542,23 +542,23 @@ __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
         if (last || T < c.t_thresh) break;
     }
     if (MODE == kItems && VG_BWD_DIRECT) {
-        out_items.put(P, gs_pending, gP0, gP1, gP2, has_p, d);
+        out_items.put(P, carry_sigma, gP0, gP1, gP2, has_p, d);
         // every recorded sample was counted into its bucket: fill the places of any the replay did not
         // reach with zero-gradient items (the replay follows the forward, so normally there are none)
         for (int s = n_done + 1; s < n_stored; ++s) {
             Sample Z;
             bool has_z;
-            load_sample(gi.rec, r, K, s, o, d, g.inv, Z, has_z);
+            get_record(gi.rec, r, K, s, o, d, g.inv, Z, has_z);
             out_items.put(Z, 0.f, 0.f, 0.f, 0.f, false, d);
         }
         out_items.flush();
     } else if (MODE == kItems) {
-        emit_item(io.items, (r - io.r0) * K + n_done, P, gs_pending, gP0, gP1, gP2, has_p, io.count);
+        emit_item(io.items, (r - io.r0) * K + n_done, P, carry_sigma, gP0, gP1, gP2, has_p, io.count);
     }
     else if (kAgg)
-        scatter_sample_agg(g, F, P, gs_pending, gP0, gP1, gP2, has_p, b, cache, grad, stage, lane);
+        scatter_sample_agg(g, F, P, carry_sigma, gP0, gP1, gP2, has_p, b, cache, grad, stage, lane);
     else
-        scatter_sample(g, F, P, gs_pending, gP0, gP1, gP2, has_p, b, cache, grad);
+        sample_grads(g, F, P, carry_sigma, gP0, gP1, gP2, has_p, b, cache, grad);
     if (err) atomicOr(status, err);
 }
 
@@ -918,7 +918,7 @@ __global__ void __launch_bounds__(kBlock)
     sh_basis(M.d[0], M.d[1], M.d[2], F.sh_deg, b);
     const float gR0 = __ldg(gi.g_rgb + 3 * r), gR1 = __ldg(gi.g_rgb + 3 * r + 1), gR2 = __ldg(gi.g_rgb + 3 * r + 2);
     const float fg0 = __ldg(gi.rgb + 3 * r), fg1 = __ldg(gi.rgb + 3 * r + 1), fg2 = __ldg(gi.rgb + 3 * r + 2);
-    const float gT_final = __ldg(gi.g_T + r) * __ldg(gi.T + r);
+    const float tail_grad = __ldg(gi.g_T + r) * __ldg(gi.T + r);
     int err = 0, cur = __ldg(g.inv + __ldg(R.start + r)), walk_steps = 0, k = 0;
     float T = 1.f, acc0 = 0.f, acc1 = 0.f, acc2 = 0.f;
     for (; k < M.n_total; ++k) {
@@ -927,20 +927,20 @@ __global__ void __launch_bounds__(kBlock)
         Sample S;
         S.t = t;
         S.x0 = along(M.o[0], t, M.d[0]), S.x1 = along(M.o[1], t, M.d[1]), S.x2 = along(M.o[2], t, M.d[2]);
-        cur = walk_to(g, cur, S.x0, S.x1, S.x2, walk_steps, err);
+        cur = walk_nearest(g, cur, S.x0, S.x1, S.x2, walk_steps, err);
         S.cell = cur;
         const float alpha = 1.f - __expf(-eval_density(g, F, cur, S.x0, S.x1, S.x2) * delta);
         const float w = T * alpha;
-        const float T_next = T * (1.f - alpha);
+        const float T_after = T * (1.f - alpha);
         const bool active = w > c.w_thresh;
         S.C0 = S.C1 = S.C2 = 0.f, S.mmin = 0.f, S.inv_a = 0.f;
         if (active) {
             eval_color(g, F, b, cache, S);
             acc0 += w * S.C0, acc1 += w * S.C1, acc2 += w * S.C2;
         }
-        float gsig = gR0 * (T_next * S.C0 - (fg0 - acc0)) + gR1 * (T_next * S.C1 - (fg1 - acc1)) +
-                     gR2 * (T_next * S.C2 - (fg2 - acc2));
-        gsig = delta * (gsig - gT_final);
+        float gsig = gR0 * (T_after * S.C0 - (fg0 - acc0)) + gR1 * (T_after * S.C1 - (fg1 - acc1)) +
+                     gR2 * (T_after * S.C2 - (fg2 - acc2));
+        gsig = delta * (gsig - tail_grad);
         const float gC0 = active ? w * gR0 : 0.f, gC1 = active ? w * gR1 : 0.f, gC2 = active ? w * gR2 : 0.f;
         if (k < cap) {
             const bool do_c = active && (gC0 != 0.f || gC1 != 0.f || gC2 != 0.f);
@@ -952,9 +952,9 @@ __global__ void __launch_bounds__(kBlock)
             it[3] = make_float4(M.d[0], M.d[1], M.d[2], 0.f);
             atomicAdd(count + cur, 1);
         } else {
-            scatter_sample(g, F, S, gsig, gC0, gC1, gC2, active, b, cache, grad);
+            sample_grads(g, F, S, gsig, gC0, gC1, gC2, active, b, cache, grad);
         }
-        T = T_next;
+        T = T_after;
         if (T < c.t_thresh) {
             ++k;
             break;

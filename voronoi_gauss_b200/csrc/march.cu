@@ -48,7 +48,7 @@ __global__ void __launch_bounds__(kBlock)
         Sample S;
         S.t = t;
         S.x0 = along(M.o[0], t, M.d[0]), S.x1 = along(M.o[1], t, M.d[1]), S.x2 = along(M.o[2], t, M.d[2]);
-        cur = walk_to(g, cur, S.x0, S.x1, S.x2, walk_steps, err);
+        cur = walk_nearest(g, cur, S.x0, S.x1, S.x2, walk_steps, err);
         S.cell = cur;
         const float alpha = 1.f - __expf(-eval_density(g, F, cur, S.x0, S.x1, S.x2) * delta);
         const float w = T * alpha;
@@ -86,7 +86,7 @@ __global__ void __launch_bounds__(kBlock)
     sh_basis(M.d[0], M.d[1], M.d[2], F.sh_deg, b);
     const float gR0 = __ldg(gi.g_rgb + 3 * r), gR1 = __ldg(gi.g_rgb + 3 * r + 1), gR2 = __ldg(gi.g_rgb + 3 * r + 2);
     const float fg0 = __ldg(gi.rgb + 3 * r), fg1 = __ldg(gi.rgb + 3 * r + 1), fg2 = __ldg(gi.rgb + 3 * r + 2);
-    const float gT_final = __ldg(gi.g_T + r) * __ldg(gi.T + r);
+    const float tail_grad = __ldg(gi.g_T + r) * __ldg(gi.T + r);
     int err = 0, cur = __ldg(g.inv + __ldg(R.start + r)), walk_steps = 0;
     float T = 1.f, acc0 = 0.f, acc1 = 0.f, acc2 = 0.f;
     for (int k = 0; k < M.n_total; ++k) {
@@ -95,27 +95,27 @@ __global__ void __launch_bounds__(kBlock)
         Sample S;
         S.t = t;
         S.x0 = along(M.o[0], t, M.d[0]), S.x1 = along(M.o[1], t, M.d[1]), S.x2 = along(M.o[2], t, M.d[2]);
-        cur = walk_to(g, cur, S.x0, S.x1, S.x2, walk_steps, err);
+        cur = walk_nearest(g, cur, S.x0, S.x1, S.x2, walk_steps, err);
         S.cell = cur;
         const float alpha = 1.f - __expf(-eval_density(g, F, cur, S.x0, S.x1, S.x2) * delta);
         const float w = T * alpha;
-        const float T_next = T * (1.f - alpha);
+        const float T_after = T * (1.f - alpha);
         const bool active = w > c.w_thresh;
         S.C0 = S.C1 = S.C2 = 0.f, S.mmin = 0.f, S.inv_a = 0.f;
         if (active) {
             eval_color(g, F, b, cache, S);
             acc0 += w * S.C0, acc1 += w * S.C1, acc2 += w * S.C2;
         }
-        float gsig = gR0 * (T_next * S.C0 - (fg0 - acc0)) + gR1 * (T_next * S.C1 - (fg1 - acc1)) +
-                     gR2 * (T_next * S.C2 - (fg2 - acc2));
-        gsig = delta * (gsig - gT_final);
+        float gsig = gR0 * (T_after * S.C0 - (fg0 - acc0)) + gR1 * (T_after * S.C1 - (fg1 - acc1)) +
+                     gR2 * (T_after * S.C2 - (fg2 - acc2));
+        gsig = delta * (gsig - tail_grad);
         if (kAgg)
             scatter_sample_agg(g, F, S, gsig, active ? w * gR0 : 0.f, active ? w * gR1 : 0.f, active ? w * gR2 : 0.f,
                                active, b, cache, grad, stage, lane);
         else
-            scatter_sample(g, F, S, gsig, active ? w * gR0 : 0.f, active ? w * gR1 : 0.f, active ? w * gR2 : 0.f,
+            sample_grads(g, F, S, gsig, active ? w * gR0 : 0.f, active ? w * gR1 : 0.f, active ? w * gR2 : 0.f,
                            active, b, cache, grad);
-        T = T_next;
+        T = T_after;
         if (T < c.t_thresh) break;
     }
     if (err) atomicOr(status, err);

@@ -46,7 +46,7 @@ __global__ void __launch_bounds__(kBlock)
     const int64_t i = static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
     if (i >= nq) return;
     int steps = 0, err = 0;
-    const int c = walk_to(g, 0, __ldg(q + 3 * i), __ldg(q + 3 * i + 1), __ldg(q + 3 * i + 2), steps, err);
+    const int c = walk_nearest(g, 0, __ldg(q + 3 * i), __ldg(q + 3 * i + 1), __ldg(q + 3 * i + 2), steps, err);
     out[i] = __ldg(g.perm + c);
     if (err) atomicOr(status, err);
 }

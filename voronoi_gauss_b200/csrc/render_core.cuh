@@ -115,7 +115,7 @@ __device__ __forceinline__ void red4(float* p, const float4& v) { atomicAdd(rein
 // Gradients of one sample into the gradient pack: gs = dL/dsigma, gC = dL/dC, has_c whether the
 // sample's colour exists (foam.cu:303-343). Four floats per atomic (16-byte vector reductions).
 template <int SLOTS>
-__device__ __forceinline__ void scatter_sample(const GraphView& g, const FieldView& F, const Sample& P, float gs,
+__device__ __forceinline__ void sample_grads(const GraphView& g, const FieldView& F, const Sample& P, float gs,
                                                float gC0, float gC1, float gC2, bool has_c, const float (&b)[16],
                                                ColorCache<SLOTS>& cache, float* __restrict__ grad) {
     const bool do_c = has_c && (gC0 != 0.f || gC1 != 0.f || gC2 != 0.f);
@@ -167,7 +167,7 @@ __device__ __forceinline__ void scatter_sample(const GraphView& g, const FieldVi
     }
 }
 
-// Warp-aggregated variant of scatter_sample. The 32 rays of a warp come from one pixel tile, so at a
+// Warp-aggregated variant of sample_grads. The 32 rays of a warp come from one pixel tile, so at a
 // given step several of them sample the same cell and scatter into the same neighbour sites. Lanes
 // are grouped by cell (__match_any_sync); a group of g lanes stages its per-neighbour gradients
 // (16 float4) in shared memory and its members sum them column-wise, so a site receives one set of
@@ -186,7 +186,7 @@ __device__ __forceinline__ void scatter_sample_agg(const GraphView& g, const Fie
     if (!any) return;
     const unsigned peers = __match_any_sync(want, P.cell);
     if (__popc(peers) == 1) {
-        scatter_sample(g, F, P, gs, gC0, gC1, gC2, has_c, b, cache, grad);
+        sample_grads(g, F, P, gs, gC0, gC1, gC2, has_c, b, cache, grad);
         return;
     }
     const int gsize = __popc(peers);

@@ -129,7 +129,7 @@ __device__ __forceinline__ bool better(float t, int k, float bt, int bk, const i
 
 // Greedy walk on the packed graph to the nearest site of x, ties to the smaller original index
 // (foam.cu:163-181): each step moves to the neighbour minimising (|x - p|^2, original id).
-__device__ __forceinline__ int walk_to(const GraphView& g, int cur, float x0, float x1, float x2, int& steps,
+__device__ __forceinline__ int walk_nearest(const GraphView& g, int cur, float x0, float x1, float x2, int& steps,
                                        int& err) {
     for (int it = 0; it < kWalkCap; ++it) {
         const int e0 = __ldg(g.off + cur), e1 = __ldg(g.off + cur + 1);
