@@ -912,8 +912,8 @@ __global__ void __launch_bounds__(kBlock)
     if (rl >= nr) return;
     const int64_t r = r0 + rl;
     ColorCache<0> cache{nullptr, 0};
-    MRay M;
-    load_mray(R, c, r, M);
+    Schedule M;
+    schedule_of(R, c, r, M);
     float b[16];
     sh_basis(M.d[0], M.d[1], M.d[2], F.sh_deg, b);
     const float gR0 = __ldg(gi.g_rgb + 3 * r), gR1 = __ldg(gi.g_rgb + 3 * r + 1), gR2 = __ldg(gi.g_rgb + 3 * r + 2);
@@ -923,7 +923,7 @@ __global__ void __launch_bounds__(kBlock)
     float T = 1.f, acc0 = 0.f, acc1 = 0.f, acc2 = 0.f;
     for (; k < M.n_total; ++k) {
         float t, delta;
-        march_sample_at(M, c, k, t, delta);
+        schedule_step(M, c, k, t, delta);
         Sample S;
         S.t = t;
         S.x0 = along(M.o[0], t, M.d[0]), S.x1 = along(M.o[1], t, M.d[1]), S.x2 = along(M.o[2], t, M.d[2]);

@@ -255,13 +255,13 @@ __device__ __forceinline__ void scatter_sample_agg(const GraphView& g, const Fie
 
 // A ray of the fixed-step march: n_in midpoint steps of dt in [near, mid], then n_bg steps uniform in
 // disparity over [mid, far] (march.cu:134-153).
-struct MRay {
+struct Schedule {
     float o[3], d[3];
     float near, mid, far;
     int n_in, n_total;
 };
 
-__device__ __forceinline__ void load_mray(const RayView& R, const MarchCfg& c, int64_t r, MRay& M) {
+__device__ __forceinline__ void schedule_of(const RayView& R, const MarchCfg& c, int64_t r, Schedule& M) {
 #pragma unroll
     for (int a = 0; a < 3; ++a) M.o[a] = __ldg(R.o + 3 * r + a), M.d[a] = __ldg(R.d + 3 * r + a);
     M.near = __ldg(R.near + r), M.mid = __ldg(R.mid + r), M.far = __ldg(R.far + r);
@@ -269,7 +269,7 @@ __device__ __forceinline__ void load_mray(const RayView& R, const MarchCfg& c, i
     M.n_total = M.n_in + c.n_bg;
 }
 
-__device__ __forceinline__ void march_sample_at(const MRay& M, const MarchCfg& c, int k, float& t, float& delta) {
+__device__ __forceinline__ void schedule_step(const Schedule& M, const MarchCfg& c, int k, float& t, float& delta) {
     if (k < M.n_in) {
         const float t0 = __fmaf_rn(static_cast<float>(k), c.dt, M.near), t1 = fminf(__fadd_rn(t0, c.dt), M.mid);
         t = __fmul_rn(0.5f, __fadd_rn(t0, t1)), delta = __fsub_rn(t1, t0);
