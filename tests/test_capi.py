@@ -97,3 +97,25 @@ def test_host_side_argument_errors_of_the_field_packing_and_scene_entry_points(l
     assert rc == 1 and b'reorder' in lib.vg_last_error()
     rc = lib.vg_bake_colors(p, p, 5, 10, 0.0, 0.0, 0.0, p, null)
     assert rc == 1 and b'sh_deg' in lib.vg_last_error()
+
+
+def test_workspace_sizes_are_aligned_and_monotone(lib):
+    """The host-side size queries: every size is a multiple of 256 bytes, grows with the work it covers,
+    and the cell-major march backward (backward = 3) asks for at least the per-sample scatter's size."""
+    ws = lib.vg_foam_workspace_bytes
+    sizes = []
+    for n_sites, n_rays, cap, bwd in [(1000, 4096, 256, 0), (1000, 4096, 256, 1), (1000, 4096, 256, 2),
+                                      (1000, 4096, 0, 3), (3_000_000, 2_073_600, 256, 0),
+                                      (3_000_000, 2_073_600, 256, 1), (8_000_000, 8_294_400, 256, 1)]:
+        b = ws(n_sites, 3, n_rays, cap, bwd)
+        assert b > 0 and b % 256 == 0, (n_sites, n_rays, cap, bwd)
+        sizes.append(b)
+    assert ws(3_000_000, 3, 2_073_600, 256, 1) >= ws(1000, 3, 4096, 256, 1)
+    assert ws(1000, 3, 4096, 0, 3) >= ws(1000, 3, 4096, 0, 1)
+    assert ws(1000, 3, 8192, 0, 3) >= ws(1000, 3, 4096, 0, 3)
+    assert ws(8_000_000, 3, 8_294_400, 256, 1) < 180 * 2 ** 30  # fits a B200 next to the records
+    g = lib.vg_graph_pack_bytes
+    assert g(1000, 15000) % 256 == 0 and g(2000, 30000) > g(1000, 15000)
+    f = lib.vg_field_workspace_bytes
+    assert f(1000, 3, 1, 10 ** 6) >= f(1000, 3, 1, 0) and f(1000, 3, 1, 0) % 256 == 0
+    assert lib.vg_infer_pack_workspace_bytes(10 ** 6) >= 4 * 10 ** 6
