@@ -58,17 +58,30 @@ def parse():
 
 # ------------------------------------------------------------------------------------------ setup
 
-def load_scene(cfg, n_sites, rank):
-    """Graph of the configuration (built once and cached on disk; other ranks wait for the cache)."""
+def load_scene(cfg, n_sites, rank, poll_s=2.0, wait_s=3600.0):
+    """Graph of the configuration, built once by rank 0 and cached on disk; the other ranks wait for the
+    cache. If rank 0 fails to build it, it leaves a marker (named for this launch, so that one left by an
+    earlier launch is never read) and the waiting ranks raise at their next poll instead of waiting."""
     from voronoi_gauss_b200 import scenes
     n = scenes.CONFIGS[cfg]['n'] if n_sites is None else n_sites
     path = os.path.join(scenes.cache_dir(), f'graph_c{cfg}_n{n}_s0.npz')
-    if rank != 0:
-        t0 = time.time()
-        while not os.path.exists(path):
-            if time.time() - t0 > 3600:
-                raise TimeoutError('scene cache was not written by rank 0')
-            time.sleep(2.0)
+    launch = os.environ.get('TORCHELASTIC_RUN_ID') or os.environ.get('MASTER_PORT') or 'single'
+    failed = f'{path}.failed.{launch}'
+    if rank == 0:
+        try:
+            return scenes.build_graph(cfg, n=n)
+        except BaseException as e:
+            with open(failed, 'w') as f:
+                f.write(f'{type(e).__name__}: {e}')
+            raise
+    t0 = time.time()
+    while not os.path.exists(path):
+        if os.path.exists(failed):
+            with open(failed) as f:
+                raise RuntimeError(f'rank 0 could not build the scene ({f.read()})')
+        if time.time() - t0 > wait_s:
+            raise TimeoutError('scene cache was not written by rank 0')
+        time.sleep(poll_s)
     return scenes.build_graph(cfg, n=n)
 
 

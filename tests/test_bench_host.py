@@ -41,3 +41,27 @@ def test_launches_per_step_matches_the_launch_list():
     assert bench.launches_per_step(1920 * 1080, 256) == 2 + 44 + 51 + 2
     # one pass
     assert bench.launches_per_step(4096, 256) == 2 + (3 + 5 + 1) + (2 + 6 + 1) + 2
+
+
+def test_scene_build_failure_reaches_the_waiting_ranks(tmp_path, monkeypatch):
+    """A rank-0 failure while building the scene cache makes the other ranks raise at their next poll
+    instead of waiting for a cache that will never come; a marker from another launch is ignored."""
+    import time
+    import pytest
+    from voronoi_gauss_b200 import scenes
+    monkeypatch.setenv('VG_SCENE_CACHE', str(tmp_path))
+    monkeypatch.setenv('TORCHELASTIC_RUN_ID', 'launch-a')
+
+    def broken(cfg, n=None, **kw):
+        raise MemoryError('no room for the triangulation')
+    monkeypatch.setattr(scenes, 'build_graph', broken)
+    with pytest.raises(MemoryError):
+        bench.load_scene(1, 500, rank=0)
+    t0 = time.time()
+    with pytest.raises(RuntimeError, match='no room for the triangulation'):
+        bench.load_scene(1, 500, rank=1, poll_s=0.05, wait_s=30)
+    assert time.time() - t0 < 5
+    # a later launch does not read launch-a's marker: it waits (and here times out quickly)
+    monkeypatch.setenv('TORCHELASTIC_RUN_ID', 'launch-b')
+    with pytest.raises(TimeoutError):
+        bench.load_scene(1, 500, rank=1, poll_s=0.05, wait_s=0.2)
