@@ -86,6 +86,13 @@ static_assert(VG_BWD_BALANCE >= 0 && VG_BWD_BALANCE <= 31, "VG_BWD_BALANCE must 
 #endif
 // VG_FWD_COUNT       1: the deferred traversal counts the samples that need a colour per (pass, cell) as
 //                    it stores them (no counting pass over the records); 0: cmf_count_kernel per pass
+// VG_BWD_HELPERS     1: for cells with VG_BWD_BALANCE < n < 32 neighbourhood sites, the 32 - n lanes that
+//                    one lane per neighbour leaves idle take over the SH-gradient sums of neighbours
+//                    0..31-n, receiving each sample's colour-gradient factors from the owning lane by
+//                    shuffle (one phase, same sums in the same order); 0: owners do all of it
+#ifndef VG_BWD_HELPERS
+#define VG_BWD_HELPERS 0
+#endif
 #ifndef VG_FWD_COUNT
 #define VG_FWD_COUNT 1
 #endif
@@ -737,6 +744,102 @@ __device__ __forceinline__ int scatter_range(const GraphView& g, const FieldView
     return j;
 }
 
+#if VG_BWD_HELPERS
+// A chunk of a cell with 16 < n < 32 neighbourhood sites: lane l < n owns neighbour l as in
+// scatter_range; lane n + h (h < 32 - n) helps owner h by accumulating its SH-gradient sums. All lanes
+// walk the chunk's samples in step; per sample the owner computes its colour-gradient factors dc
+// (zero when the pair carries no colour gradient) and its helper reads them by shuffle, so the SH sums
+// are the owner's own fused multiply-adds in the same order.
+template <int S4>
+__device__ __forceinline__ void helped_scatter(const GraphView& g, const FieldView& F, const float4* st, int e0, int n,
+                                               int cnt, int lane, float* __restrict__ grad) {
+    const bool owner = lane < n;
+    const bool helped = lane < 32 - n;   // owners whose SH sums go to lane n + lane
+    const int mine = owner ? lane : lane - n;
+    const int src = lane >= n ? lane - n : lane;
+    const float4 E = __ldg(g.edge + e0 + mine);
+    const int j = site_of(E);
+    const float4* fr = F.rec + kFieldVec * static_cast<int64_t>(j);
+    const float4 r0_ = __ldg(fr), r1_ = __ldg(fr + 1), r2_ = __ldg(fr + 2), r3_ = __ldg(fr + 3);
+    float4 coef[S4];
+#pragma unroll
+    for (int q = 0; q < S4; ++q) coef[q] = owner ? __ldg(F.sh + static_cast<int64_t>(S4) * j + q) : make_float4(0, 0, 0, 0);
+    PairAcc<S4> A;
+    A.zero();
+    for (int i = 0; i < cnt; ++i) {
+        const float4* q = st + kItemVec * i;
+        float dc[3] = {0.f, 0.f, 0.f};
+        bool coloured = false;
+        if (owner) {
+            const float4 q0 = q[0];
+            const float v0 = q0.x - E.x, v1 = q0.y - E.y, v2 = q0.z - E.z;
+            const float gs = q0.w;
+            if (gs != 0.f) {
+                const float gc = gs * __expf(r1_.z - 0.5f * maha(r0_, r1_, v0, v1, v2));
+                if (fabsf(gc) > 1e-12f) {
+                    const float gm = -0.5f * gc;
+                    A.ad[0] += gc, A.ad[1] += gm * v0 * v0, A.ad[2] += 2.f * gm * v0 * v1, A.ad[3] += 2.f * gm * v0 * v2;
+                    A.ad[4] += gm * v1 * v1, A.ad[5] += 2.f * gm * v1 * v2, A.ad[6] += gm * v2 * v2;
+                }
+            }
+            const float4 q1 = q[1], q2 = q[2];
+            if (q2.y > 0.f) {
+                const float a = __expf(-0.5f * (maha(r2_, r3_, v0, v1, v2) - q2.x)) * q2.y;
+                if (a >= kMinWeight) {
+                    float b[16];
+                    const float4 b0 = q[3], b1 = q[4], b2 = q[5], b3 = q[6];
+                    b[0] = b0.x, b[1] = b0.y, b[2] = b0.z, b[3] = b0.w, b[4] = b1.x, b[5] = b1.y, b[6] = b1.z;
+                    b[7] = b1.w, b[8] = b2.x, b[9] = b2.y, b[10] = b2.z, b[11] = b2.w, b[12] = b3.x;
+                    b[13] = b3.y, b[14] = b3.z, b[15] = b3.w;
+                    float c[3] = {0.5f, 0.5f, 0.5f}, h[3] = {0.f, 0.f, 0.f};
+#pragma unroll
+                    for (int qq = 0; qq < S4; ++qq) {
+                        const float f[4] = {coef[qq].x, coef[qq].y, coef[qq].z, coef[qq].w};
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int k = 4 * qq + u;
+                            if (k < 48) {
+                                if (VG_BWD_SH_SPLIT && ((k / 3) & 1))
+                                    h[k % 3] += b[k / 3] * f[u];
+                                else
+                                    c[k % 3] += b[k / 3] * f[u];
+                            }
+                        }
+                    }
+                    c[0] += h[0], c[1] += h[1], c[2] += h[2];
+                    dc[0] = c[0] > 0.f ? a * q1.x : 0.f, dc[1] = c[1] > 0.f ? a * q1.y : 0.f;
+                    dc[2] = c[2] > 0.f ? a * q1.z : 0.f;
+                    coloured = true;
+                    if (!helped) {
+#pragma unroll
+                        for (int k = 0; k < 4 * S4; ++k)
+                            if (k < 48) A.ash[k] += b[k / 3] * dc[k % 3];
+                    }
+                    const float ga = q1.x * fmaxf(c[0], 0.f) + q1.y * fmaxf(c[1], 0.f) + q1.z * fmaxf(c[2], 0.f);
+                    const float gm = -0.5f * a * (ga - q1.w);
+                    A.ac[0] += gm * v0 * v0, A.ac[1] += 2.f * gm * v0 * v1, A.ac[2] += 2.f * gm * v0 * v2;
+                    A.ac[3] += gm * v1 * v1, A.ac[4] += 2.f * gm * v1 * v2, A.ac[5] += gm * v2 * v2;
+                }
+            }
+        }
+        // the helpers take their owner's factors (every lane of the warp takes part)
+        const float t0 = __shfl_sync(0xffffffffu, dc[0], src), t1 = __shfl_sync(0xffffffffu, dc[1], src);
+        const float t2 = __shfl_sync(0xffffffffu, dc[2], src);
+        const bool fed = __shfl_sync(0xffffffffu, coloured ? 1 : 0, src) != 0;
+        if (!owner && fed) {
+            const float4 b0 = q[3], b1 = q[4], b2 = q[5], b3 = q[6];
+            const float b[16] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w,
+                                 b2.x, b2.y, b2.z, b2.w, b3.x, b3.y, b3.z, b3.w};
+            const float t[3] = {t0, t1, t2};
+#pragma unroll
+            for (int k = 0; k < 4 * S4; ++k)
+                if (k < 48) A.ash[k] += b[k / 3] * t[k % 3];
+        }
+    }
+    A.flush(grad, j);  // a helper holds only SH sums, a helped owner none: flush skips zero vectors
+}
+#endif
+
 // The (neighbour, sample) pairs of a chunk of a cell with n < 32 neighbour sites (self included) spread
 // over the 32 lanes so that every lane does about n cnt / 32 of them, in at most two phases whose
 // boundaries all lanes cross together:
@@ -831,6 +934,10 @@ __global__ void __launch_bounds__(kBlock, VG_SCATTER_MINB)
             const int e0 = __ldg(g.off + Cur.x), e1 = __ldg(g.off + Cur.x + 1);
             if (e1 - e0 <= VG_BWD_BALANCE) {
                 balanced_scatter<S4>(g, F, st, e0, e1 - e0, Cur.z, lane, grad);
+#if VG_BWD_HELPERS
+            } else if (e1 - e0 < 32) {
+                helped_scatter<S4>(g, F, st, e0, e1 - e0, Cur.z, lane, grad);
+#endif
             } else {
                 for (int e = e0 + lane; e < e1; e += 32) {
                     PairAcc<S4> A;
@@ -884,6 +991,10 @@ __global__ void __launch_bounds__(kBlock, VG_SCATTER_MINB)
         const int e0 = __ldg(g.off + cell), e1 = __ldg(g.off + cell + 1);
         if (e1 - e0 <= VG_BWD_BALANCE) {
             balanced_scatter<S4>(g, F, st, e0, e1 - e0, cnt, lane, grad);
+#if VG_BWD_HELPERS
+        } else if (e1 - e0 < 32) {
+            helped_scatter<S4>(g, F, st, e0, e1 - e0, cnt, lane, grad);
+#endif
         } else {
             for (int e = e0 + lane; e < e1; e += 32) {  // one neighbour site per lane
                 PairAcc<S4> A;
