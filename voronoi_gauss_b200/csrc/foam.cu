@@ -886,6 +886,9 @@ __device__ __forceinline__ void balanced_scatter(const GraphView& g, const Field
 // index array plus the sample's t in the records and its ray (kRecords).
 enum StageMode { kBucketed = 0, kIndexed = 1, kRecords = 2 };
 
+// With kAsync the bucketed stage returns through its copy-ahead loop, so the generic loop below is
+// unreachable in that instantiation (and removed); nvcc's note about it is silenced for this kernel only.
+#pragma nv_diag_suppress 128
 template <int S4, int STAGE>
 __global__ void __launch_bounds__(kBlock, VG_SCATTER_MINB)
     cm_scatter_kernel(GraphView g, FieldView F, RayView R, const float* __restrict__ rec, int K,
@@ -1006,6 +1009,8 @@ __global__ void __launch_bounds__(kBlock, VG_SCATTER_MINB)
         __syncwarp();
     }
 }
+
+#pragma nv_diag_default 128
 
 // ------------------------------------------------------------ cell-major backward of the march path
 //
