@@ -12,9 +12,20 @@
 #define VG_SAMPLE_UNROLL 4
 #endif
 
+// VG_FWD_PREFETCH   1: half way through a cell's neighbours, eval_sample prefetches into L1 the CSR
+//                   offsets of the exit face leading so far (the next cell's first, dependent load);
+//                   0: no prefetch
+#ifndef VG_FWD_PREFETCH
+#define VG_FWD_PREFETCH 0
+#endif
+
 namespace vg {
 
 constexpr int kSampleUnroll = VG_SAMPLE_UNROLL;
+
+#if VG_FWD_PREFETCH
+__device__ __forceinline__ void prefetch_l1(const void* p) { asm volatile("prefetch.global.L1 [%0];" ::"l"(p)); }
+#endif
 
 // One sample of a ray: position, the cell whose neighbourhood evaluates it, density and colour.
 struct Sample {
@@ -41,11 +52,17 @@ __device__ __forceinline__ void eval_sample(const GraphView& g, const FieldView&
     Blend B;
     B.reset();
     t_exit = kInf, next = -1;
+#if VG_FWD_PREFETCH
+    const int e_half = e0 + ((e1 - e0) >> 1);
+#endif
 #pragma unroll kSampleUnroll
     for (int e = e0; e < e1; ++e) {
         const float4 E = e == e0 ? Pc : __ldg(g.edge + e);
         const int j = site_of(E);
         if (want_exit && e > e0) exit_candidate(E, Pc.x, Pc.y, Pc.z, o, d, t_exit, next, g.perm);
+#if VG_FWD_PREFETCH
+        if (want_exit && e == e_half && next >= 0) prefetch_l1(g.off + next);
+#endif
         const float v0 = S.x0 - E.x, v1 = S.x1 - E.y, v2 = S.x2 - E.z;
         const float4* r = F.rec + kFieldVec * static_cast<int64_t>(j);
         const float4 r0 = __ldg(r), r1 = __ldg(r + 1);
