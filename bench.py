@@ -393,6 +393,11 @@ def run_b200(args):
         'clocks': clocks,
     }
     traffic = os.path.join(ROOT, 'profiles', 'traffic.json')
+    if os.environ.get('VG_LIB_PATH'):  # a variant build of the library: name it and its knobs
+        from voronoi_gauss_b200 import _lib
+        knobs = os.path.join(os.path.dirname(_lib.LIB_PATH), 'defines.txt')
+        line['config']['library'] = {'path': _lib.LIB_PATH, 'defines': open(knobs).read().split()
+                                     if os.path.exists(knobs) else []}
     if os.path.exists(traffic) and W * H == 1920 * 1080 and args.config == 3 and args.sites is None:
         with open(traffic) as f:
             tr = json.load(f)

@@ -119,3 +119,14 @@ def test_workspace_sizes_are_aligned_and_monotone(lib):
     f = lib.vg_field_workspace_bytes
     assert f(1000, 3, 1, 10 ** 6) >= f(1000, 3, 1, 0) and f(1000, 3, 1, 0) % 256 == 0
     assert lib.vg_infer_pack_workspace_bytes(10 ** 6) >= 4 * 10 ** 6
+
+
+def test_variant_builds_pass_their_knobs_and_need_their_own_directory():
+    """`build --define` compiles with -D flags into a separate directory; the in-tree library is never
+    overwritten by a variant."""
+    from voronoi_gauss_b200 import build
+    cmd = build.compile_command('x.cu', 'x.o', ('VG_BWD_HELPERS=1', 'VG_FWD_PREFETCH=1'))
+    assert '-DVG_BWD_HELPERS=1' in cmd and '-DVG_FWD_PREFETCH=1' in cmd
+    assert '-gencode' in cmd and 'arch=compute_100a,code=sm_100a' in cmd
+    with pytest.raises(ValueError):
+        build.build(defines=('VG_BWD_HELPERS=1',))

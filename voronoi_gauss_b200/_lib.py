@@ -11,7 +11,8 @@ import ctypes
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, '_lib', 'libvgb200.so')
+# VG_LIB_PATH: load a variant of the library (python -m voronoi_gauss_b200.build --define ... --out DIR)
+LIB_PATH = os.environ.get('VG_LIB_PATH') or os.path.join(HERE, '_lib', 'libvgb200.so')
 
 _lib = None
 

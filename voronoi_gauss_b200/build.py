@@ -1,10 +1,13 @@
 """Builds libvgb200.so (the CUDA kernels + the C ABI of include/vgb200.h) in-tree for sm_100a.
 
     python -m voronoi_gauss_b200.build [--verbose]
+    python -m voronoi_gauss_b200.build --define VG_BWD_HELPERS=1 --out DIR    # a variant library
 
 Every .cu under csrc/ is compiled by nvcc to an object with -gencode arch=compute_100a,code=sm_100a
 (static CUDA runtime, no torch headers) and linked into voronoi_gauss_b200/_lib/libvgb200.so, which
-the package loads with ctypes. Objects are rebuilt only when a source or header is newer.
+the package loads with ctypes. Objects are rebuilt only when a source or header is newer. A variant
+with other values of the kernels' build knobs (the VG_* macros of csrc/) goes to its own directory;
+setting VG_LIB_PATH to its libvgb200.so makes the package load it instead of the in-tree one.
 """
 
 from __future__ import annotations
@@ -34,11 +37,16 @@ def nvcc():
     return path
 
 
-def _compile(src, headers_mtime, verbose):
-    obj = os.path.join(OBJ, os.path.basename(src)[:-3] + '.o')
+def compile_command(src, obj, defines=()):
+    """nvcc command line of one source; `defines` are NAME=VALUE strings passed as -D."""
+    return [nvcc(), *ARCH, *FLAGS, *(f'-D{d}' for d in defines), '-c', src, '-o', obj]
+
+
+def _compile(src, headers_mtime, verbose, obj_dir=OBJ, defines=()):
+    obj = os.path.join(obj_dir, os.path.basename(src)[:-3] + '.o')
     if os.path.exists(obj) and os.path.getmtime(obj) >= max(os.path.getmtime(src), headers_mtime):
         return obj
-    cmd = [nvcc(), *ARCH, *FLAGS, '-c', src, '-o', obj]
+    cmd = compile_command(src, obj, defines)
     if verbose:
         cmd += ['-Xptxas', '-v']
     res = subprocess.run(cmd, capture_output=True, text=True)
@@ -49,24 +57,35 @@ def _compile(src, headers_mtime, verbose):
     return obj
 
 
-def build(verbose=False):
-    os.makedirs(OBJ, exist_ok=True)
+def build(verbose=False, defines=(), out=None):
+    """Builds the library (in-tree by default; with `defines`, a variant into `out`). -> its path."""
+    if defines and out is None:
+        raise ValueError('a variant build (defines) needs its own output directory')
+    out_dir = OUT if out is None else os.path.abspath(out)
+    obj_dir, lib = os.path.join(out_dir, 'obj'), os.path.join(out_dir, 'libvgb200.so')
+    os.makedirs(obj_dir, exist_ok=True)
     sources = sorted(glob.glob(os.path.join(CSRC, '*.cu')))
     headers = glob.glob(os.path.join(CSRC, '*.cuh')) + glob.glob(os.path.join(ROOT, 'include', '*.h'))
     hm = max(os.path.getmtime(h) for h in headers)
     with cf.ThreadPoolExecutor(max_workers=min(8, len(sources))) as ex:
-        objs = list(ex.map(lambda s: _compile(s, hm, verbose), sources))
-    if not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):
-        tmp = LIB + f'.{os.getpid()}.tmp'
+        objs = list(ex.map(lambda s: _compile(s, hm, verbose, obj_dir, tuple(defines)), sources))
+    if not os.path.exists(lib) or os.path.getmtime(lib) < max(os.path.getmtime(o) for o in objs):
+        tmp = lib + f'.{os.getpid()}.tmp'
         res = subprocess.run([nvcc(), *ARCH, '-shared', '-Xcompiler', '-fPIC', '-o', tmp, *objs],
                              capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError(f'link failed:\n{res.stderr}')
-        os.replace(tmp, LIB)
-    return LIB
+        os.replace(tmp, lib)
+    if defines:
+        with open(os.path.join(out_dir, 'defines.txt'), 'w') as f:
+            f.write('\n'.join(defines) + '\n')
+    return lib
 
 
 if __name__ == '__main__':
     ap = argparse.ArgumentParser()
     ap.add_argument('--verbose', action='store_true')
-    print(build(ap.parse_args().verbose))
+    ap.add_argument('--define', action='append', default=[], help='NAME=VALUE of a VG_* build knob (repeatable)')
+    ap.add_argument('--out', default=None, help='output directory of a variant build')
+    a = ap.parse_args()
+    print(build(a.verbose, a.define, a.out))
