@@ -22,13 +22,28 @@ MODULES = {'vgf_foam': 'foam.cu', 'vgf_march': 'march.cu', 'vgf_foam_infer': 'fo
 
 
 def build(names=None, verbose=False):
+    """Builds the named modules (default all). Several modules build at once, one child process each
+    (every module has its own build directory)."""
+    todo = [n for n in MODULES if not names or n in names]
+    if len(todo) > 1:
+        import subprocess
+        procs = [(n, subprocess.Popen([sys.executable, os.path.abspath(__file__), n] + (['-v'] if verbose else []),
+                                      stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)) for n in todo]
+        failed = []
+        for n, p in procs:
+            out, _ = p.communicate()
+            if p.returncode != 0:
+                failed.append(f'{n}: {out[-2000:]}')
+        if failed:
+            raise RuntimeError('reference extension build failed:\n' + '\n'.join(failed))
+        return [os.path.join(OUT, n, n + '.so') for n in todo]
     import torch  # noqa: F401  (the build needs torch's headers)
     from torch.utils.cpp_extension import load
 
     os.environ['TORCH_CUDA_ARCH_LIST'] = '10.0a'
     built = []
     for name, src in MODULES.items():
-        if names and name not in names:
+        if name not in todo:
             continue
         source = os.path.join(REF, 'csrc', src)
         if not os.path.exists(source):
@@ -63,5 +78,5 @@ def load_reference(name):
 
 
 if __name__ == '__main__':
-    for p in build(sys.argv[1:] or None, verbose='-v' in sys.argv):
+    for p in build([a for a in sys.argv[1:] if a != '-v'] or None, verbose='-v' in sys.argv):
         print(p)
