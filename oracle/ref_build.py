@@ -1,6 +1,6 @@
 """TEST INFRASTRUCTURE ONLY — builds the reference's own CUDA extensions, unchanged, into oracle/_ref/.
 
-    python oracle/ref_build.py            (needs the reference checkout: VG_REFERENCE, default /root/reference)
+    python oracle/ref_build.py            (needs the reference checkout, see reference_root())
 
 Each of csrc/foam.cu, csrc/march.cu, csrc/foam_infer.cu and csrc/vgf.cu is compiled from where it lies
 in the reference checkout by torch.utils.cpp_extension (the same tool the reference's ext.py:11-27
@@ -17,8 +17,18 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, '_ref')
-REF = os.environ.get('VG_REFERENCE', '/root/reference')
 MODULES = {'vgf_foam': 'foam.cu', 'vgf_march': 'march.cu', 'vgf_foam_infer': 'foam_infer.cu', 'vgf_ext': 'vgf.cu'}
+
+
+def reference_root():
+    """The reference checkout: the directory named by VG_REFERENCE, else a directory `reference` beside
+    this repository's own directory (where the build machine keeps it); None when neither holds csrc/."""
+    env = os.environ.get('VG_REFERENCE')
+    cands = [env] if env else [os.path.join(os.path.dirname(os.path.dirname(HERE)), 'reference')]
+    for c in cands:
+        if c and os.path.isdir(os.path.join(c, 'csrc')):
+            return os.path.abspath(c)
+    return None
 
 
 def build(names=None, verbose=False):
@@ -41,11 +51,14 @@ def build(names=None, verbose=False):
     from torch.utils.cpp_extension import load
 
     os.environ['TORCH_CUDA_ARCH_LIST'] = '10.0a'
+    ref = reference_root()
+    if ref is None:
+        raise FileNotFoundError('reference checkout not found: set VG_REFERENCE to its directory')
     built = []
     for name, src in MODULES.items():
         if name not in todo:
             continue
-        source = os.path.join(REF, 'csrc', src)
+        source = os.path.join(ref, 'csrc', src)
         if not os.path.exists(source):
             raise FileNotFoundError(source)
         bdir = os.path.join(OUT, name)

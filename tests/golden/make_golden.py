@@ -1,6 +1,7 @@
 """Generates the golden fixtures in this directory from the reference's own CPU code.
 
-Run where the reference checkout is available (VG_REFERENCE, default /root/reference); the GPU box
+Run where the reference checkout is available (VG_REFERENCE, or a `reference` directory beside the
+repository, as oracle/ref_build.reference_root finds it); the GPU box
 and the tests only read the committed .npz files. Every fixture stores its inputs and the outputs of
 the reference's float64 restatements:
 
@@ -39,10 +40,14 @@ from types import SimpleNamespace
 import numpy as np
 import torch
 
-REF = os.environ.get('VG_REFERENCE', '/root/reference')
 HERE = os.path.dirname(os.path.abspath(__file__))
-sys.path.insert(0, REF)
 sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+from oracle.ref_build import reference_root  # noqa: E402
+
+REF = reference_root()
+if REF is None:
+    raise SystemExit('reference checkout not found: set VG_REFERENCE to its directory')
+sys.path.insert(0, REF)
 
 import ext as ref_ext  # noqa: E402
 import render as ref_render  # noqa: E402

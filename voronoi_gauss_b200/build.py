@@ -5,9 +5,10 @@
 
 Every .cu under csrc/ is compiled by nvcc to an object with -gencode arch=compute_100a,code=sm_100a
 (static CUDA runtime, no torch headers) and linked into voronoi_gauss_b200/_lib/libvgb200.so, which
-the package loads with ctypes. Objects are rebuilt only when a source or header is newer. A variant
-with other values of the kernels' build knobs (the VG_* macros of csrc/) goes to its own directory;
-setting VG_LIB_PATH to its libvgb200.so makes the package load it instead of the in-tree one.
+the package loads with ctypes. Objects are rebuilt when a source or header is newer, or when the
+compiler flags or knob defines differ from the ones recorded beside the objects (`flags.txt`). A
+variant with other values of the kernels' build knobs (the VG_* macros of csrc/) goes to its own
+directory; setting VG_LIB_PATH to its libvgb200.so makes the package load it instead of the in-tree one.
 """
 
 from __future__ import annotations
@@ -42,6 +43,24 @@ def compile_command(src, obj, defines=()):
     return [nvcc(), *ARCH, *FLAGS, *(f'-D{d}' for d in defines), '-c', src, '-o', obj]
 
 
+def flag_signature(defines=()):
+    """The compile flags and sorted knob defines an object directory was built with (one per line)."""
+    return '\n'.join([*ARCH, *FLAGS, *sorted(f'-D{d}' for d in defines)]) + '\n'
+
+
+def _sync_flags(obj_dir, defines):
+    """Removes the objects of `obj_dir` when they were compiled with other flags or defines than these,
+    and records the new signature, so that a rebuild with other knobs never reuses stale objects."""
+    stamp = os.path.join(obj_dir, 'flags.txt')
+    want = flag_signature(defines)
+    have = open(stamp).read() if os.path.exists(stamp) else None
+    if have != want:
+        for o in glob.glob(os.path.join(obj_dir, '*.o')):
+            os.remove(o)
+        with open(stamp, 'w') as f:
+            f.write(want)
+
+
 def _compile(src, headers_mtime, verbose, obj_dir=OBJ, defines=()):
     obj = os.path.join(obj_dir, os.path.basename(src)[:-3] + '.o')
     if os.path.exists(obj) and os.path.getmtime(obj) >= max(os.path.getmtime(src), headers_mtime):
@@ -64,6 +83,7 @@ def build(verbose=False, defines=(), out=None):
     out_dir = OUT if out is None else os.path.abspath(out)
     obj_dir, lib = os.path.join(out_dir, 'obj'), os.path.join(out_dir, 'libvgb200.so')
     os.makedirs(obj_dir, exist_ok=True)
+    _sync_flags(obj_dir, defines)
     sources = sorted(glob.glob(os.path.join(CSRC, '*.cu')))
     headers = glob.glob(os.path.join(CSRC, '*.cuh')) + glob.glob(os.path.join(ROOT, 'include', '*.h'))
     hm = max(os.path.getmtime(h) for h in headers)
@@ -76,9 +96,12 @@ def build(verbose=False, defines=(), out=None):
         if res.returncode != 0:
             raise RuntimeError(f'link failed:\n{res.stderr}')
         os.replace(tmp, lib)
+    knobs = os.path.join(out_dir, 'defines.txt')
     if defines:
-        with open(os.path.join(out_dir, 'defines.txt'), 'w') as f:
+        with open(knobs, 'w') as f:
             f.write('\n'.join(defines) + '\n')
+    elif os.path.exists(knobs):
+        os.remove(knobs)
     return lib
 
 

@@ -43,10 +43,8 @@ __global__ void __launch_bounds__(kPrepBlock)
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const int64_t o = __ldg(perm + i);
-    ConicLocal L;
-    conic_local(ls, quat, o, 0.f, L);
     float A[6];
-    conic_of(L, A);
+    gauss_conic(gauss_axes(ls, quat, o, 0.f), A);
     gauss[2 * static_cast<int64_t>(i)] = make_float4(A[0] * scale, A[1] * scale, A[2] * scale, A[3] * scale);
     gauss[2 * static_cast<int64_t>(i) + 1] =
         make_float4(A[4] * scale, A[5] * scale, raw != nullptr ? fminf(__ldg(raw + o), 30.f) : 0.f, 0.f);
@@ -295,12 +293,10 @@ __global__ void __launch_bounds__(kPrepBlock)
     const int64_t o = __ldg(perm + i);
     const float4* G = acc + static_cast<int64_t>(stride) * i;
     const float4 a0 = G[0], a1 = G[1];
-    ConicLocal L;
-    conic_local(ls, quat, o, 0.f, L);
     const float gA[6] = {a0.y, a0.z, a0.w, a1.x, a1.y, a1.z};
     float gl[3];
     float4 gq;
-    conic_grad(L, gA, gl, gq);
+    gauss_conic_grad(gauss_axes(ls, quat, o, 0.f), gA, gl, gq);
 #pragma unroll
     for (int k = 0; k < 3; ++k) g_ls[3 * o + k] = gl[k];
     reinterpret_cast<float4*>(g_quat)[o] = gq;
@@ -331,10 +327,8 @@ __global__ void __launch_bounds__(kPrepBlock)
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const int64_t o = __ldg(perm + i);
-    ConicLocal L;
-    conic_local(ls, quat, o, 0.f, L);
     float A[6];
-    conic_of(L, A);
+    gauss_conic(gauss_axes(ls, quat, o, 0.f), A);
     const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
     const float4 a0 = make_float4(A[0], A[1], A[2], A[3]);
     float4* r = rec + 4 * static_cast<int64_t>(i);
@@ -445,11 +439,9 @@ __global__ void __launch_bounds__(kPrepBlock)
             sd[v] = q;
         }
     }
-    ConicLocal L;
-    conic_local(ls, quat, o, 0.f, L);
     float gl[3];
     float4 gq;
-    conic_grad(L, gA, gl, gq);
+    gauss_conic_grad(gauss_axes(ls, quat, o, 0.f), gA, gl, gq);
 #pragma unroll
     for (int k = 0; k < 3; ++k) g_ls[3 * o + k] = gl[k];
     reinterpret_cast<float4*>(g_quat)[o] = gq;

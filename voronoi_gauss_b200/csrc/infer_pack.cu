@@ -56,12 +56,9 @@ __global__ void __launch_bounds__(kBlock)
     const __half2 h = __floats2half2_rn(r2, lam);
     cut[o] = *reinterpret_cast<const float*>(&h);
     points4[i] = make_float4(__ldg(points + 3 * o), __ldg(points + 3 * o + 1), __ldg(points + 3 * o + 2), 0.f);
-    ConicLocal L;
     float A[6], C[6];
-    conic_local(d_ls, d_quat, o, floor2, L);
-    conic_of(L, A);
-    conic_local(c_ls, c_quat, o, floor2, L);
-    conic_of(L, C);
+    gauss_conic(gauss_axes(d_ls, d_quat, o, floor2), A);
+    gauss_conic(gauss_axes(c_ls, c_quat, o, floor2), C);
     float* a = attr + 20 * static_cast<int64_t>(i);
 #pragma unroll
     for (int k = 0; k < 6; ++k) a[k] = A[k], a[8 + k] = C[k];
