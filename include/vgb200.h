@@ -116,7 +116,9 @@ int vg_grad_unpack(const void* pack, int64_t n_sites, int64_t n_adj, const float
  * held by every device that loads it until exit), so n_sites is limited to 131072 (VG_ERR_WORKSPACE
  * beyond). The first call on a device looks up that array's address (make it before any stream
  * capture). Calls share the array: calls that overlap on the GPU race and must be ordered by the
- * caller (e.g. one stream). Allocates and frees nothing. */
+ * caller (e.g. one stream). Allocates and frees nothing. What the field records leave of the array
+ * serves as the cell-major colour pass's workspace when that fits (small ray batches of small scenes);
+ * otherwise colours are evaluated inline along each ray (same image, slower). */
 int vg_foam_forward_noalloc(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA,
                             const float* cA, const float* sh, int sh_deg, const float* o, const float* d,
                             const int32_t* start, const float* near, const float* far, int64_t n_rays,
@@ -250,6 +252,27 @@ int vg_foam_infer(const float* points, const int32_t* offsets, const int32_t* nb
                   int64_t n_rays, float t_thresh, float w_thresh, float color_cut, int color_mode, int stage,
                   const int32_t* cap, const int32_t* orig, float* rgb, float* T, float* depth, int32_t* stats,
                   void* stream);
+
+/* ------------------------------------------------------------------------------ kernel timing */
+
+/* Measurement aid with no counterpart in the reference (whose benchmarks time whole extension calls).
+ * While enabled, every launch of the kernel classes below is bracketed by a pair of CUDA events
+ * recorded on that launch's own stream, so a benchmark can read one kernel's device time inside a
+ * larger timed region. vg_prof_enable(1) forgets earlier records and starts recording, (0) stops.
+ * vg_prof_read waits for the recorded events of one class and returns their summed time in ms and
+ * the number of launches. Events are created on the current device; use one device per process while
+ * recording. Disabled (the default), the launches carry no events. */
+enum {
+    VG_PROF_TRAVERSAL = 0,   /* interaction-point traversal of vg_foam_forward */
+    VG_PROF_COLOR = 1,       /* cell-major colour pass of vg_foam_forward */
+    VG_PROF_REPLAY = 2,      /* record replay of vg_foam_backward (writes the scatter's items) */
+    VG_PROF_SCATTER = 3,     /* cell-major gradient scatter (foam, march and field backwards) */
+    VG_PROF_INFER = 4,       /* vg_foam_infer */
+    VG_PROF_MARCH_FWD = 5,   /* vg_march_forward */
+    VG_PROF_MARCH_ITEMS = 6  /* re-march of vg_march_backward writing the scatter's items */
+};
+int vg_prof_enable(int on);
+int vg_prof_read(int kernel, double* total_ms, int64_t* launches);
 
 #ifdef __cplusplus
 }

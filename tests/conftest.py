@@ -57,3 +57,49 @@ def small_inputs(z, keys=('raw', 'dA', 'cA', 'sh', 'o', 'd', 'start', 'near', 'f
     for k in keys:
         out[k] = cuda(z[k], torch.int32 if k == 'start' else torch.float32)
     return out
+
+
+TIE_RTOL = 1e-4  # a threshold decision counts as a near-tie when the quantity is this close (relative)
+
+
+def tie_distance(rec, n, t_thresh, w_thresh):
+    """How close one ray's compositing came to a threshold decision, from its records rec (S, 8) (t, site,
+    sigma, ...) of n samples, composited in float64 as the renderer does (foam.cu:370-389): the smallest
+    relative distance, over its segments, of the segment weight w = T alpha to w_thresh (which decides
+    whether the segment is coloured) and of the transmittance after the segment to t_thresh (which ends
+    the ray)."""
+    t = np.asarray(rec[:n, 0], np.float64)
+    sig = np.asarray(rec[:n, 2], np.float64)
+    if n < 2:
+        return np.inf
+    alpha = 1.0 - np.exp(-0.5 * (sig[:-1] + sig[1:]) * (t[1:] - t[:-1]))
+    T_after = np.cumprod(1.0 - alpha)
+    T_before = np.concatenate([[1.0], T_after[:-1]])
+    w = T_before * alpha
+    dist = np.inf
+    if w_thresh > 0:
+        dist = min(dist, float(np.min(np.abs(w - w_thresh))) / w_thresh)
+    if t_thresh > 0:
+        dist = min(dist, float(np.min(np.abs(T_after - t_thresh))) / t_thresh)
+    return dist
+
+
+def audit_stats(stats, ref_stats, ref_rec, t_thresh, w_thresh, rtol=TIE_RTOL):
+    """Rays whose per-ray stats differ between two renderers must be documented near-ties: a segment
+    weight within rtol of w_thresh or a transmittance within rtol of t_thresh (from the second renderer's
+    records, which must hold the whole ray). -> boolean mask of the rays whose stats agree; raises with the
+    unexplained rays otherwise."""
+    stats, ref_stats = np.asarray(stats), np.asarray(ref_stats)
+    same = (stats == ref_stats).all(1)
+    bad = []
+    K = ref_rec.shape[1]
+    for r in np.flatnonzero(~same):
+        n = int(ref_stats[r, 0])
+        if n > K:
+            bad.append((int(r), 'records do not hold the ray'))
+            continue
+        dist = tie_distance(ref_rec[r], n, t_thresh, w_thresh)
+        if not dist <= rtol:
+            bad.append((int(r), f'closest threshold distance {dist:.2e}'))
+    assert not bad, f'stats differ on rays that are not near-ties: {bad[:8]}'
+    return same

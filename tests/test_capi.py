@@ -130,3 +130,14 @@ def test_variant_builds_pass_their_knobs_and_need_their_own_directory():
     assert '-gencode' in cmd and 'arch=compute_100a,code=sm_100a' in cmd
     with pytest.raises(ValueError):
         build.build(defines=('VG_BWD_HELPERS=1',))
+
+
+def test_kernel_timer_without_launches(lib):
+    """vg_prof_enable / vg_prof_read with nothing recorded: zero time and launches, no device call; a bad
+    kernel id is rejected."""
+    from voronoi_gauss_b200 import _lib
+    _lib.prof_enable(True)
+    assert _lib.prof_read('scatter') == (0.0, 0)
+    _lib.prof_enable(False)
+    ms, n = ctypes.c_double(), ctypes.c_int64()
+    assert lib.vg_prof_read(99, ctypes.byref(ms), ctypes.byref(n)) == 1

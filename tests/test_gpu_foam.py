@@ -6,13 +6,14 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import bits, cuda, golden, rel, small_inputs, split
+from conftest import audit_stats, bits, cuda, golden, rel, small_inputs, split
 from oracle import oracle
 
 pytestmark = pytest.mark.gpu
 
 IMG_TOL = 1e-4   # max |rgb / T / depth - oracle|
 GRAD_TOL = 1e-3  # relative error of gradients
+TIE_IMG_TOL = 1e-3  # rays at a documented near-tie of t_thresh / w_thresh (one segment of weight ~1e-4 apart)
 
 
 def _ext():
@@ -133,10 +134,13 @@ def test_foam_config1_full_image_matches_oracle():
     args = (gr['points'], gr['offsets'], gr['adj'], prm['raw'], dA.cpu().numpy(), cA.cpu().numpy(), prm['sh'], 1, o, d,
             start, near, far, 1e-4, 1e-4)
     o_rgb, o_T, o_depth, o_stats, o_rec = oracle.foam_forward(*args, 256, n_threads=nt)
-    same = (stats.cpu().numpy() == o_stats).all(1)
-    assert same.mean() >= 0.999, f'stats differ on {int((~same).sum())} rays'
-    assert np.abs(rgb.detach().cpu().numpy() - o_rgb)[same].max() <= IMG_TOL
-    assert np.abs(T.detach().cpu().numpy() - o_T)[same].max() <= IMG_TOL
+    # the oracle's expf and the GPU's __expf round differently, so a ray whose compositing passes within a
+    # hair of t_thresh or w_thresh may stop or colour one segment apart: every such ray must be a near-tie
+    same = audit_stats(stats.cpu().numpy(), o_stats, o_rec, 1e-4, 1e-4)
+    rgb_d, T_d = np.abs(rgb.detach().cpu().numpy() - o_rgb), np.abs(T.detach().cpu().numpy() - o_T)
+    assert rgb_d[same].max() <= IMG_TOL and T_d[same].max() <= IMG_TOL
+    # a near-tie moves at most one segment of weight ~1e-4 (or a tail of transmittance ~1e-4)
+    assert rgb_d.max() <= TIE_IMG_TOL and T_d.max() <= TIE_IMG_TOL
     og = oracle.foam_backward(*args, o_rgb, o_T, g_rgb.numpy(), g_T.numpy(), o_rec, o_stats, n_threads=nt)
     for name, p, want in zip(('raw', 'dA', 'cA', 'sh'), (raw, dA_, cA_, sh), og):
         assert rel(p.grad.cpu().numpy(), want) <= GRAD_TOL, name

@@ -1,13 +1,17 @@
 """The product against the reference's own CUDA kernels, built unchanged from its sources for sm_100a
 into oracle/_ref (oracle/ref_build.py), on identical inputs: per-ray visited-cell sequences and sample
-parameters bit for bit, stats equal, images within 1e-4 and gradients within 1e-3 relative. Skipped when
-oracle/_ref was not built (the reference checkout is needed to build it)."""
+parameters bit for bit, stats equal (or, where they differ, a documented near-tie of a threshold),
+images within 1e-4 and gradients within 1e-3 relative, on the small fixtures and at the sizes of the
+BASELINE configurations (config 3's scene, config 2's inference scene and view, config 5's march).
+oracle/_ref is built by __graft_entry__.build() where the reference checkout exists and travels with
+the tree; these tests fail (not skip) when it is missing, so that a missing build cannot pass as a
+pass."""
 
 import numpy as np
 import pytest
 import torch
 
-from conftest import bits, cuda, rel, small_inputs
+from conftest import audit_stats, bits, cuda, rel, small_inputs
 
 pytestmark = pytest.mark.gpu
 
@@ -17,8 +21,8 @@ GRAD_TOL = 1e-3
 
 def ref(name):
     from oracle import ref_build
-    if not ref_build.available(name):
-        pytest.skip(f'oracle/_ref/{name} not built')
+    assert ref_build.available(name), f'oracle/_ref/{name} is not built (run __graft_entry__.build() beside the ' \
+                                      'reference checkout)'
     return ref_build.load_reference(name)
 
 
@@ -92,8 +96,9 @@ def test_foam_full_size_scene_against_reference_kernels():
     theirs = rf.foam_forward(*args, K)
     stats, r_stats = compare_records(mine[3], mine[4], theirs[3], theirs[4], K)
     assert (stats[:, 0] <= K).mean() > 0.99
-    same = (stats == r_stats).all(1)
-    assert same.mean() >= 0.999
+    # samples and walk steps agree on every ray (compare_records); a coloured-segment count may differ only
+    # where a segment's weight lies within a hair of w_thresh (the two kernels' sigmas round differently)
+    audit_stats(stats, r_stats, theirs[4].cpu().numpy(), 1e-4, 1e-4)
     for a, b in zip(mine[:3], theirs[:3]):
         assert float((a - b).abs().max()) <= IMG_TOL
     gen = torch.Generator().manual_seed(1)
@@ -162,3 +167,86 @@ def test_conic_against_reference_kernel():
         ga, gb = ext.extension().conic_backward(ls, q, floor, gA), rv.conic_backward(ls, q, floor, gA)
         for u, v in zip(ga, gb):
             assert rel(u.cpu().numpy(), v.cpu().numpy()) <= 1e-5
+
+
+def _mixture_scene():
+    """BASELINE config 2's scene (1M sites from 64 anisotropic Gaussian clusters, SH degree 3) as a model."""
+    from voronoi_gauss_b200 import scenes
+    from voronoi_gauss_b200.model import VoronoiGaussField
+    gr = scenes.build_graph(2)
+    prm = scenes.make_params(2, gr['points'].astype(np.float64))
+    model = VoronoiGaussField.from_params(*(cuda(gr[k]) for k in ('points', 'offsets', 'adj')),
+                                          {k: (v.cuda() if torch.is_tensor(v) else v) for k, v in prm.items()})
+    return gr, model
+
+
+@pytest.mark.parametrize('tag', ['fused_fp16_eps_morton', 'exact_fp32'])
+def test_foam_infer_config2_scene_against_reference_kernel(tag):
+    """foam_infer on BASELINE config 2's 1M-site scene, the 200 x 200 centre crop of an 800 x 800 view of
+    orbit camera 0 (fov 50), in the reference's fast configuration (fused colours, fp16 SH, eps 1e-4,
+    Morton order) and in exact fp32: per-ray stats equal (samples, coloured segments, walk steps, density
+    terms, SH evaluations) and images within 1e-4."""
+    ri = ref('vgf_foam_infer')
+    from voronoi_gauss_b200 import render, scenes, sites
+    gr, model = _mixture_scene()
+    centre, c2w = scenes.orbit_camera(0, 100)
+    o, d = scenes.camera_rays(centre, c2w, 800, 800, 50.0)
+    yy, xx = np.meshgrid(np.arange(300, 500), np.arange(300, 500), indexing='ij')
+    crop = (yy * 800 + xx).ravel()[scenes.tile_order(200, 200)]
+    o, d = o[crop].cuda().contiguous(), d[crop].cuda().contiguous()
+    start = torch.full((len(o),), int(sites.nearest_sites(gr['points'], centre[None])[0]), dtype=torch.int32,
+                       device='cuda')
+    if tag == 'exact_fp32':
+        pack, kw = render.pack_foam(model), dict(colors='exact', eps_color=0.0)
+    else:
+        pack = render.pack_foam(model, sh_half=True, eps_density=1e-4, reorder=True)
+        kw = dict(colors='fused', eps_color=1e-4)
+    mode = {'exact': 0, 'fused': 2}[kw['colors']]
+    cut = 2 * np.log(1 / kw['eps_color']) if kw['eps_color'] > 0 else float('inf')
+    near, _, far = render.ray_bounds(o, d, 0.02, 4.0)
+    s = pack['inv'][start.long()].int() if pack['inv'] is not None else start
+    cap = torch.empty(0, dtype=torch.int32, device='cuda')
+    args = (*(pack[k] for k in ('points', 'offsets', 'nbr', 'edge', 'attr', 'sh')), 3, o, d, s, near, far, 1e-4,
+            1e-4, float(cut), mode, 2, cap, pack['orig'])
+    mine = _ext().foam_infer_extension().foam_infer(*args)
+    theirs = ri.foam_infer(*args)
+    assert torch.equal(mine[3], theirs[3]), 'per-ray stats differ from the reference kernel'
+    for a, b in zip(mine[:3], theirs[:3]):
+        assert float((a - b).abs().max()) <= IMG_TOL
+    assert float(mine[3][:, 0].double().mean()) > 2  # the crop looks into the scene
+
+
+def test_march_config5_scene_against_reference_kernels():
+    """march on BASELINE config 5's workload (config 2's 1M-site scene, dt 2/256 from the unit-ball entry to
+    its exit, n_bg 0, conic floor dt / 2) for a 480 x 270 view of orbit camera 0: per-ray stats equal,
+    images within 1e-4, gradients within 1e-3 relative."""
+    rm = ref('vgf_march')
+    ext = _ext()
+    from voronoi_gauss_b200 import scenes, sites
+    gr, model = _mixture_scene()
+    centre, c2w = scenes.orbit_camera(0, 8)
+    W, H = 480, 270
+    o, d = scenes.camera_rays(centre, c2w, W, H, 50.0, order=scenes.tile_order(H, W))
+    o, d = o.cuda(), d.cuda()
+    start = torch.full((len(o),), int(sites.nearest_sites(gr['points'], centre[None])[0]), dtype=torch.int32,
+                       device='cuda')
+    near, mid, far = scenes.march_bounds(o, d)
+    dt = 2.0 / 256
+    with torch.no_grad():
+        dA = ext.conic(model.d_log_scale, model.d_quat, 0.5 * dt)
+        cA = ext.conic(model.c_log_scale, model.c_quat, 0.5 * dt)
+    g = model.graph
+    args = (g.points, g.offsets, g.adj, model.raw.detach(), dA, cA, model.sh().detach().contiguous(), 3, o, d, start,
+            near, mid, far, dt, 0, 1e-4, 1e-4)
+    mine = ext.march_extension().march_forward(*args)
+    theirs = rm.march_forward(*args)
+    assert torch.equal(mine[3], theirs[3]), 'per-ray stats differ from the reference kernel'
+    assert float(mine[3][:, 0].double().mean()) > 20
+    for a, b in zip(mine[:3], theirs[:3]):
+        assert float((a - b).abs().max()) <= IMG_TOL
+    gen = torch.Generator().manual_seed(2)
+    g_rgb, g_T = torch.randn(len(o), 3, generator=gen).cuda(), torch.randn(len(o), generator=gen).cuda()
+    gm = ext.march_extension().march_backward(*args, mine[0], mine[1], g_rgb, g_T)
+    gr_ = rm.march_backward(*args, theirs[0], theirs[1], g_rgb, g_T)
+    for name, a, b in zip(('raw', 'dA', 'cA', 'sh'), gm, gr_):
+        assert rel(a.cpu().numpy(), b.cpu().numpy()) <= GRAD_TOL, name

@@ -1,8 +1,8 @@
 """vg_foam_forward_noalloc: the forward render for callers that cannot allocate device memory while
 rendering. It must give the same outputs as vg_foam_forward (which takes a caller-allocated workspace)
-on consecutive calls, since every call reuses the same static scratch; and it must refuse scenes larger
-than that scratch instead of overrunning it. Kept in the last test file so that a failure here cannot
-stop the rest of the suite."""
+on consecutive calls, since every call reuses the same static scratch; it must not allocate device
+memory; and it must refuse scenes larger than that scratch instead of overrunning it. Kept in the last
+test file so that a failure here cannot stop the rest of the suite."""
 
 import ctypes
 
@@ -66,6 +66,28 @@ def test_noalloc_forward_matches_workspace_forward_on_consecutive_calls(foam_sma
     b = _call('vg_foam_forward', pk, x2, 1, 0, True)
     _compare(a, b, 0)
     assert not torch.equal(a[0], _call('vg_foam_forward', pk, x, 1, 0, True)[0])  # the field did change
+
+
+def test_noalloc_forward_allocates_no_device_memory(foam_small):
+    """The entry point's promise: with the outputs already allocated, repeated calls leave the device's
+    free memory unchanged (cudaMemGetInfo sees every allocator, the library's own included)."""
+    from voronoi_gauss_b200 import _lib, ext
+    z = foam_small
+    pk = ext.GraphPack(cuda(z['points']), cuda(z['offsets']), cuda(z['adj']))
+    x = small_inputs(z)
+    B, K = x['o'].size(0), 64
+    outs = [torch.empty(B, 3, device='cuda'), torch.empty(B, device='cuda'), torch.empty(B, device='cuda'),
+            torch.empty(B, 3, dtype=torch.int32, device='cuda'), torch.empty(B, K, 8, device='cuda')]
+    args = [pk.ptr, pk.n, pk.m, *(x[k].data_ptr() for k in ('raw', 'dA', 'cA', 'sh')), 3,
+            *(x[k].data_ptr() for k in ('o', 'd', 'start', 'near', 'far')), B, 1e-4, 1e-4, K,
+            *(t.data_ptr() for t in outs), torch.cuda.current_stream().cuda_stream]
+    _lib.call('vg_foam_forward_noalloc', *args)  # first call on this device: looks up the scratch address
+    torch.cuda.synchronize()
+    free_before = torch.cuda.mem_get_info()[0]
+    for _ in range(5):
+        _lib.call('vg_foam_forward_noalloc', *args)
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free_before
 
 
 def test_noalloc_forward_rejects_scenes_beyond_its_scratch():

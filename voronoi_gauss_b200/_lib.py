@@ -61,7 +61,24 @@ SIGNATURES = {
     'vg_nearest_sites': (I32, [P, I64, I64, P, I64, P, P]),
     'vg_foam_infer': (I32, [P, P, P, P, P, P, I32, I32, I64, I64, P, P, P, P, P, I64, F32, F32, F32, I32, I32, P, P, P,
                             P, P, P, P]),
+    'vg_prof_enable': (I32, [I32]),
+    'vg_prof_read': (I32, [I32, P, P]),
 }
+
+# kernel classes of vg_prof_read (VG_PROF_* of include/vgb200.h)
+PROF = {'traversal': 0, 'color': 1, 'replay': 2, 'scatter': 3, 'infer': 4, 'march_fwd': 5, 'march_items': 6}
+
+
+def prof_enable(on):
+    """Starts (forgetting earlier records) or stops recording kernel times (vg_prof_enable)."""
+    check(lib().vg_prof_enable(1 if on else 0), 'vg_prof_enable')
+
+
+def prof_read(kernel):
+    """-> (summed device ms, launches) of one kernel class since prof_enable(True); waits for its events."""
+    ms, n = ctypes.c_double(), ctypes.c_int64()
+    check(lib().vg_prof_read(PROF[kernel], ctypes.byref(ms), ctypes.byref(n)), 'vg_prof_read')
+    return ms.value, n.value
 
 
 def lib():

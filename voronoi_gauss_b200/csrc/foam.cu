@@ -13,6 +13,7 @@
 #include <algorithm>
 #include <cub/device/device_scan.cuh>
 
+#include "prof.cuh"
 #include "render_core.cuh"
 
 // Build-time tuning knobs (defaults chosen by measurement on B200, config-3 scenes at 1080p):
@@ -1164,6 +1165,7 @@ cudaError_t cm_scatter_bucketed(const GraphView& g, const FieldView& F, const fl
     cm_chunks_kernel<<<blocks(n), kBlock, 0, st>>>(offsets, n, chunks, counter);
     const int grid = sm_count() * 3;
     const RayView none{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 0};
+    ProfScope ps(kProfScatter, st);
     switch (F.s4) {
         case 1: cm_scatter_kernel<1, kBucketed><<<grid, kBlock, 0, st>>>(g, F, none, nullptr, 0, items, nullptr, chunks,
                                                                          counter, 0, grad); break;
@@ -1201,14 +1203,18 @@ cudaError_t march_backward_cm(const GraphView& g, const FieldView& F, const RayV
         if (e == cudaSuccess) e = cudaMemsetAsync(fill, 0, 4 * static_cast<size_t>(n), st);
         if (e == cudaSuccess) e = cudaMemsetAsync(counter, 0, 16, st);
         if (e != cudaSuccess) return e;
-        march_items_kernel<<<blocks(nr), kBlock, 0, st>>>(g, F, R, c, gi, grad, items, n_items, count, r0, nr,
-                                                          kMarchCap, status);
+        {
+            ProfScope ps(kProfMarchItems, st);
+            march_items_kernel<<<blocks(nr), kBlock, 0, st>>>(g, F, R, c, gi, grad, items, n_items, count, r0, nr,
+                                                              kMarchCap, status);
+        }
         size_t tb = L.temp_bytes;
         e = cub::DeviceScan::ExclusiveSum(b + L.temp, tb, count, offsets, n + 1, st);
         if (e != cudaSuccess) return e;
         march_bucket_kernel<<<blocks(nr * kMarchCap), kBlock, 0, st>>>(items, n_items, nr, kMarchCap, offsets, fill,
                                                                         order);
         cm_chunks_kernel<<<blocks(n), kBlock, 0, st>>>(offsets, n, chunks, counter);
+        ProfScope ps(kProfScatter, st);
         switch (F.s4) {
             case 1: cm_scatter_kernel<1, kIndexed><<<grid, kBlock, 0, st>>>(g, F, R, nullptr, 0, items, order, chunks,
                                                                             counter, r0, grad); break;
@@ -1252,7 +1258,10 @@ cudaError_t forward_deferred(const GraphView& g, const FieldView& F, const RayVi
         if (e != cudaSuccess) return e;
         cc.cm_count = count_all, cc.cm_rays = L.rays_per_pass, cc.cm_stride = g.n + 1;
     }
-    foam_forward_kernel<true, kDeferred><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, cc, out, status);
+    {
+        ProfScope ps(kProfTraversal, st);
+        foam_forward_kernel<true, kDeferred><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, cc, out, status);
+    }
     foam_forward_kernel<true, kImmediateOverflow><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, cc, out, status);
     int* order = reinterpret_cast<int*>(b + L.order);
     int* fill = reinterpret_cast<int*>(b + L.fill);
@@ -1277,6 +1286,7 @@ cudaError_t forward_deferred(const GraphView& g, const FieldView& F, const RayVi
         cmf_bucket_kernel<<<blocks(32 * nr), kBlock, 0, st>>>(out.rec, out.stats, g.inv, r0, nr, K, offsets, fill,
                                                                order);
         cm_chunks_kernel<<<blocks(n), kBlock, 0, st>>>(offsets, n, chunks, counter);
+        ProfScope ps(kProfColor, st);
         switch (F.s4) {
             case 1: cmf_color_kernel<1><<<grid, kBlock, 0, st>>>(g, F, R, out.rec, K, order, chunks, counter, r0); break;
             case 3: cmf_color_kernel<3><<<grid, kBlock, 0, st>>>(g, F, R, out.rec, K, order, chunks, counter, r0); break;
@@ -1301,12 +1311,14 @@ cudaError_t foam_forward(const GraphView& g, const FieldView& F, const RayView& 
     char* b = static_cast<char*>(cm_ws);
     if (record) {
         if (!room) {
+            ProfScope ps(kProfTraversal, st);
             foam_forward_kernel<true, kImmediate><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, out, status);
             return cudaGetLastError();
         }
         return forward_deferred(g, F, R, c, out, status, cm_layout(g.n, R.n, K, false), b, st);
     }
     if (!room) {
+        ProfScope ps(kProfTraversal, st);
         foam_forward_kernel<false, kImmediate><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, out, status);
         return cudaGetLastError();
     }
@@ -1361,6 +1373,7 @@ cudaError_t foam_backward(const GraphView& g, const FieldView& F, const RayView&
             cmf_count_kernel<<<blocks(32 * nr), kBlock, 0, st>>>(gi.rec, gi.stats, g.inv, r0, nr, K, count, false);
             e = cub::DeviceScan::ExclusiveSum(b + L.temp, tb, count, offsets, n + 1, st);
             if (e != cudaSuccess) return e;
+            ProfScope ps(kProfReplay, st);
             foam_backward_kernel<kItems><<<blocks(nr), kBlock, 0, st>>>(g, F, R, c, gi, grad, io, status);
         } else {
             foam_backward_kernel<kItems><<<blocks(nr), kBlock, 0, st>>>(g, F, R, c, gi, grad, io, status);
@@ -1369,6 +1382,7 @@ cudaError_t foam_backward(const GraphView& g, const FieldView& F, const RayView&
             cm_bucket_kernel<<<blocks(nr), kBlock, 0, st>>>(items, gi.stats, r0, nr, K, offsets, fill, order);
         }
         cm_chunks_kernel<<<blocks(n), kBlock, 0, st>>>(offsets, n, chunks, counter);
+        ProfScope ps(kProfScatter, st);
         switch (F.s4) {
             case 1: cm_scatter_kernel<1, kStage><<<grid, kBlock, 0, st>>>(g, F, R, gi.rec, K, items, order, chunks, counter, r0,
                                                                   grad); break;

@@ -20,6 +20,7 @@
 // match its kernel's.
 #include <cuda_fp16.h>
 
+#include "prof.cuh"
 #include "vg_common.cuh"
 
 namespace vg {
@@ -322,6 +323,7 @@ __global__ void __launch_bounds__(kThreads)
 template <int STAGE, int MODE, bool HALF>
 void launch(const Layout& L, const InferCfg& cfg, const RayView& R, const Outputs& out, int* status, cudaStream_t st) {
     const int blocks = static_cast<int>((R.n + kThreads - 1) / kThreads);
+    ProfScope ps(kProfInfer, st);
     infer_kernel<STAGE, MODE, HALF><<<blocks, kThreads, 0, st>>>(L, cfg, R, out, status);
 }
 

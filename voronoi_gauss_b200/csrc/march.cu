@@ -6,6 +6,7 @@
 // exceeds w_thresh, blends the colour Gaussians (march.cu:221-262). The backward pass re-marches the
 // ray with identical arithmetic (march.cu:264-345); its samples' gradients go to the cell-major scatter
 // of foam.cu (items bucketed by cell) when the workspace allows, else per lane with 16-byte atomics.
+#include "prof.cuh"
 #include "render_core.cuh"
 
 // Colour cache slots and warp-aggregated atomics: see foam.cu.
@@ -128,7 +129,10 @@ inline int blocks(int64_t n) { return static_cast<int>((n + kBlock - 1) / kBlock
 cudaError_t march_forward(const GraphView& g, const FieldView& F, const RayView& R, const MarchCfg& c,
                           const Outputs& out, int* status, cudaStream_t st) {
     if (R.n == 0) return cudaSuccess;
-    march_forward_kernel<<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, out, status);
+    {
+        ProfScope ps(kProfMarchFwd, st);
+        march_forward_kernel<<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, out, status);
+    }
     return cudaGetLastError();
 }
 

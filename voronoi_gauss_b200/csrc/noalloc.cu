@@ -17,6 +17,10 @@
 // with that device current; make that first call before any stream capture. No call allocates or
 // frees device memory.
 //
+// The field records take the front of the array; the space behind them serves as the workspace of the
+// cell-major colour pass when that pass's workspace fits there (small ray batches of small scenes),
+// and otherwise the forward evaluates colours inline along each ray (same image, slower).
+//
 // All calls share the one array and leave their own records in it. Nothing needs clearing: a call
 // writes the records of all its sites before its render kernel reads them. Calls whose work overlaps
 // on the GPU (different streams, or several host threads on one device) race on the array, so the

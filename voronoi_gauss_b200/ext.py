@@ -30,11 +30,6 @@ __all__ = ['Graph', 'foam', 'march', 'conic', 'conic_reference', 'density', 'col
            'foam_extension', 'foam_infer_extension', 'GraphPack', 'graph_pack', 'nearest_sites']
 
 
-# (start, end) CUDA events recorded on the launching stream around the foam backward launch while set
-# (used by bench.py to time the kernel inside a training step)
-BACKWARD_EVENTS = None
-
-
 def _ptr(t):
     return None if t is None or t.numel() == 0 else t.data_ptr()
 
@@ -223,17 +218,12 @@ class FoamExtension:
         g_raw, g_dA, g_cA, g_sh = (torch.empty_like(x) for x in (raw, dA, cA, sh))
         pk = graph_pack(points, offsets, adj)
         ws, nbytes = _workspace(pk.n, sh_deg, 1, dev, B, rec.size(1) if replay else 0)
-        ev = BACKWARD_EVENTS
         with torch.cuda.device(dev):
-            if ev is not None:
-                ev[0].record()
             _lib.call('vg_foam_backward', pk.ptr, pk.n, pk.m, raw.data_ptr(), dA.data_ptr(), cA.data_ptr(),
                       sh.data_ptr(), sh_deg, _ptr(o), _ptr(d), _ptr(start), _ptr(near), _ptr(far), B,
                       float(t_thresh), float(w_thresh), _ptr(rgb), _ptr(T), _ptr(g_rgb), _ptr(g_T),
                       _ptr(rec) if replay else None, rec.size(1) if replay else 0, _ptr(stats), g_raw.data_ptr(),
                       g_dA.data_ptr(), g_cA.data_ptr(), g_sh.data_ptr(), ws.data_ptr(), nbytes, _stream(dev))
-            if ev is not None:
-                ev[1].record()
         return [g_raw, g_dA, g_cA, g_sh]
 
 
