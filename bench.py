@@ -690,6 +690,20 @@ def run_infer(args):
             entry['reference_mrays_s'] = round(B / (ref_ms * 1e-3) / 1e6, 2)
             entry['speedup_vs_reference'] = round(ref_ms / ms, 3)
             entry['max_abs_rgb_vs_reference'] = float((out['rgb'] - ref_out['rgb']).abs().max())
+        if name == 'fused_fp16_eps':
+            # the reference's stage ablation (bench_infer.py:60-67): every ray's traversal fixed to the full
+            # renderer's samples (cap), then exit faces only (stage 0) and exit faces + density (stage 1)
+            cap = out['stats'][:, 0].int().contiguous()
+            abl = {}
+            for stage in (0, 1):
+                skw = dict(kw, stage=stage, cap=cap)
+                o0, d0, s0 = rays[views[0]]
+                abl[f'stage{stage}_ms'] = round(time_reps(lambda: render.render_rays_foam_infer(
+                    model, pack, o0, d0, s0, **skw)), 3)
+                if rf is not None:
+                    abl[f'reference_stage{stage}_ms'] = round(time_reps(lambda: reference_infer(
+                        rf, model, pack, o0, d0, s0, **skw)), 3)
+            entry['ablation_view0'] = abl
         results[name] = entry
         del pack
     head = results['fused_fp16_eps']
@@ -726,7 +740,8 @@ def run_infer(args):
     print(json.dumps(line), flush=True)
 
 
-def reference_infer(rf, model, pack, o, d, start, colors='exact', eps_color=0.0, t_thresh=1e-4, w_thresh=1e-4):
+def reference_infer(rf, model, pack, o, d, start, colors='exact', eps_color=0.0, t_thresh=1e-4, w_thresh=1e-4,
+                    stage=2, cap=None):
     """render.render_rays_foam_infer through the reference's own foam_infer kernel (oracle/_ref)."""
     from voronoi_gauss_b200 import render
     mode = {'exact': 0, 'baked': 1, 'fused': 2}[colors]
@@ -734,10 +749,11 @@ def reference_infer(rf, model, pack, o, d, start, colors='exact', eps_color=0.0,
     if pack['inv'] is not None:
         start = pack['inv'][start.long()].int()
     cut = 2 * math.log(1 / eps_color) if eps_color > 0 else float('inf')
-    cap = torch.empty(0, dtype=torch.int32, device=o.device)
+    if cap is None:
+        cap = torch.empty(0, dtype=torch.int32, device=o.device)
     fg, T, depth, stats = rf.foam_infer(*(pack[k] for k in ('points', 'offsets', 'nbr', 'edge', 'attr', 'sh')),
                                         model.sh_deg, o, d, start, t_near.contiguous(), t_far.contiguous(),
-                                        float(t_thresh), float(w_thresh), cut, mode, 2, cap, pack['orig'])
+                                        float(t_thresh), float(w_thresh), cut, mode, int(stage), cap, pack['orig'])
     return {'rgb': fg + T.unsqueeze(1) * torch.sigmoid(model.bg_logit), 'stats': stats}
 
 
