@@ -1,7 +1,7 @@
 """Builds libvgb200.so (the CUDA kernels + the C ABI of include/vgb200.h) in-tree for sm_100a.
 
     python -m voronoi_gauss_b200.build [--verbose]
-    python -m voronoi_gauss_b200.build --define VG_BWD_HELPERS=1 --out DIR    # a variant library
+    python -m voronoi_gauss_b200.build --define VG_INFER_UNROLL=4 --out DIR   # a variant library
 
 Every .cu under csrc/ is compiled by nvcc to an object with -gencode arch=compute_100a,code=sm_100a
 (static CUDA runtime, no torch headers) and linked into voronoi_gauss_b200/_lib/libvgb200.so, which

@@ -16,100 +16,27 @@
 #include "prof.cuh"
 #include "render_core.cuh"
 
-// Build-time tuning knobs (defaults chosen by measurement on B200, config-3 scenes at 1080p):
-//   VG_FWD_SLOTS / VG_BWD_SLOTS  per-ray colour cache slots in shared memory (0: no cache; a site's
-//                  colour is reused by few consecutive samples of a ray, the cache lost 20-30 %)
-//   VG_LAZY_COLOR  1: colours only for samples next to a segment with weight > w_thresh, in a second
-//                  pass over the cell (~40 % of the samples never need one)
-//   VG_BWD_AGG     1: warp-aggregated gradient atomics through shared memory (2x slower: the staging
-//                  traffic costs more than the atomics it saves)
-//   VG_FWD_MINB / VG_BWD_MINB  minimum resident blocks of 128 threads per SM (register budget)
-#ifndef VG_FWD_SLOTS
-#define VG_FWD_SLOTS 0
-#endif
-#ifndef VG_BWD_SLOTS
-#define VG_BWD_SLOTS 0
-#endif
-#ifndef VG_LAZY_COLOR
-#define VG_LAZY_COLOR 1
-#endif
-#ifndef VG_BWD_AGG
-#define VG_BWD_AGG 0
-#endif
-#ifndef VG_FWD_MINB
+// Tuning constants, chosen by measurement on B200 (config-3 scenes at 1080p); the alternatives tried and
+// rejected are recorded with their times in the design notes of this repository:
+//   kFwdMinBlocks / kBwdMinBlocks / kColorMinBlocks / kScatterMinBlocks  minimum resident blocks of 128
+//                  threads per SM of the traversal, the per-ray backward, the colour pass and the scatter
+//                  (their register budgets)
+//   kChunk         samples of one cell per warp in the cell-major passes (two per lane in the colour
+//                  pass), which sets how often a cell's neighbourhood is reloaded
+//   kReplicaMaxN   largest neighbourhood size (self included) for which cm_scatter_kernel spreads a
+//                  chunk's (neighbour, sample) pairs over all 32 lanes as replicas of each neighbour;
+//                  larger cells get one lane per neighbour
 #define VG_FWD_MINB 6
-#endif
-#ifndef VG_BWD_MINB
 #define VG_BWD_MINB 1
-#endif
-// VG_COLOR_MINB / VG_SCATTER_MINB  the same for cmf_color_kernel and cm_scatter_kernel
-#ifndef VG_COLOR_MINB
 #define VG_COLOR_MINB 1
-#endif
-#ifndef VG_SCATTER_MINB
 #define VG_SCATTER_MINB 3
-#endif
-// VG_CM_CHUNK  samples of one cell per warp in the cell-major passes (32 or 64; 64 = two per lane in
-//              the colour pass), which sets how often a cell's neighbourhood is reloaded
-#ifndef VG_CM_CHUNK
-#define VG_CM_CHUNK 64
-#endif
-// VG_FWD_CELL_MAJOR  1: colours of fully recorded rays evaluated cell-major (see cmf_color_kernel)
-#ifndef VG_FWD_CELL_MAJOR
-#define VG_FWD_CELL_MAJOR 1
-#endif
-// VG_BWD_CELL_MAJOR  1: samples of fully recorded rays scattered cell-major (see cm_scatter_kernel)
-#ifndef VG_BWD_CELL_MAJOR
-#define VG_BWD_CELL_MAJOR 1
-#endif
-// VG_BWD_BALANCE     largest neighbourhood size (self included) for which cm_scatter_kernel spreads a
-//                    chunk's (neighbour, sample) pairs over all 32 lanes (balanced_scatter: replicas up to
-//                    16, two phases above); larger cells get one lane per neighbour; 0: never
-#ifndef VG_BWD_BALANCE
-#define VG_BWD_BALANCE 16
-#endif
-// VG_BWD_SH_SPLIT    1: the scatter evaluates a neighbour's SH colour as two partial sums per channel
-//                    (shorter dependent chains; the colour only gates and weights gradients there)
-#ifndef VG_BWD_SH_SPLIT
-#define VG_BWD_SH_SPLIT 1
-#endif
-static_assert(VG_BWD_BALANCE >= 0 && VG_BWD_BALANCE <= 31, "VG_BWD_BALANCE must be in 0..31");
-// VG_BWD_DIRECT      1: the replay writes 64-byte items (position, gradients, direction) straight into
-//                    their cell's bucket (counted beforehand), so the scatter reads them in order;
-//                    0: 32-byte items in ray order, bucketed through an index array
-#ifndef VG_BWD_DIRECT
-#define VG_BWD_DIRECT 1
-#endif
-// VG_BWD_ASYNC       1 (with VG_BWD_DIRECT): cm_scatter_kernel copies the next chunk's items into shared
-//                    memory asynchronously (cp.async) while it scatters the current one
-#ifndef VG_BWD_ASYNC
-#define VG_BWD_ASYNC 1
-#endif
-// VG_FWD_COUNT       1: the deferred traversal counts the samples that need a colour per (pass, cell) as
-//                    it stores them (no counting pass over the records); 0: cmf_count_kernel per pass
-// VG_BWD_HELPERS     1: for cells with VG_BWD_BALANCE < n < 32 neighbourhood sites, the 32 - n lanes that
-//                    one lane per neighbour leaves idle take over the SH-gradient sums of neighbours
-//                    0..31-n, receiving each sample's colour-gradient factors from the owning lane by
-//                    shuffle (one phase, same sums in the same order); 0: owners do all of it
-#ifndef VG_BWD_HELPERS
-#define VG_BWD_HELPERS 0
-#endif
-#ifndef VG_FWD_COUNT
-#define VG_FWD_COUNT 1
-#endif
 
 namespace vg {
 namespace {
 
 constexpr int kBlock = 128;
-constexpr int kFwdSlots = VG_FWD_SLOTS;
-constexpr int kBwdSlots = VG_BWD_SLOTS;
-constexpr int kFwdSlotMem = kFwdSlots > 0 ? kFwdSlots * kBlock : 1;
-constexpr int kBwdSlotMem = kBwdSlots > 0 ? kBwdSlots * kBlock : 1;
-constexpr bool kLazy = VG_LAZY_COLOR != 0;
-constexpr bool kAgg = VG_BWD_AGG != 0;
-constexpr int kChunk = VG_CM_CHUNK;
-static_assert(kChunk == 32 || kChunk == 64, "VG_CM_CHUNK must be 32 or 64");
+constexpr int kChunk = 64;
+constexpr int kReplicaMaxN = 16;
 
 // deferred: the colour fields are filled later; the last field marks the samples that need one (-1)
 // orig: the original id of P's site (loaded when P was evaluated, so the store does not wait for it)
@@ -150,7 +77,6 @@ enum FwdMode { kImmediate = 0, kImmediateOverflow = 1, kDeferred = 2 };
 template <bool RECORD, int MODE>
 __global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
     foam_forward_kernel(GraphView g, FieldView F, RayView R, FoamCfg c, Outputs out, int* status) {
-    __shared__ float4 cache_mem[kFwdSlotMem];
     const int64_t r = static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
     if (r >= R.n) return;
     const int K = c.record_cap;
@@ -164,8 +90,6 @@ __global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
         }
     }
     constexpr bool kDefer = MODE == kDeferred;
-    ColorCache<kFwdSlots> cache{cache_mem + threadIdx.x, kBlock};
-    cache.init();
     float o[3], d[3], near, far;
     load_ray(R, r, o, d, near, far);
     float b[16];
@@ -176,9 +100,9 @@ __global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
     Sample P;
     float t_exit;
     int next;
-    eval_sample<kFwdSlots, !kLazy && !kDefer>(g, F, cur, near, o, d, b, cache, true, P, t_exit, next);
+    eval_sample<false>(g, F, cur, near, o, d, b, true, P, t_exit, next);
     int p_orig = RECORD ? __ldg(g.perm + P.cell) : 0;
-    bool has_p = !kLazy && !kDefer;
+    bool has_p = false;
     float T = 1.f, acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, dep = 0.f;
     int it = 0;
     for (; it < kMaxCells; ++it) {
@@ -186,9 +110,9 @@ __global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
         Sample Q;
         float t_exit_q;
         int next_q;
-        eval_sample<kFwdSlots, !kLazy && !kDefer>(g, F, last ? P.cell : next, last ? far : fmaxf(t_exit, P.t), o, d, b,
-                                                  cache, !last, Q, t_exit_q, next_q);
-        bool has_q = !kLazy && !kDefer;
+        eval_sample<false>(g, F, last ? P.cell : next, last ? far : fmaxf(t_exit, P.t), o, d, b, !last, Q, t_exit_q,
+                           next_q);
+        bool has_q = false;
         const int q_orig = RECORD ? __ldg(g.perm + Q.cell) : 0;
         ++n_samples;
         const float delta = Q.t - P.t;
@@ -198,10 +122,9 @@ __global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
             if (kDefer) {
                 has_p = has_q = true;  // marked: coloured by the cell-major pass
             } else {
-                if (kLazy) {
-                    if (!has_p) eval_color(g, F, b, cache, P), has_p = true;
-                    eval_color(g, F, b, cache, Q), has_q = true;
-                }
+                // lazy colours: only the samples bordering a segment with weight > w_thresh need one
+                if (!has_p) eval_color(g, F, b, P), has_p = true;
+                eval_color(g, F, b, Q), has_q = true;
                 acc0 += w * 0.5f * (P.C0 + Q.C0);
                 acc1 += w * 0.5f * (P.C1 + Q.C1);
                 acc2 += w * 0.5f * (P.C2 + Q.C2);
@@ -239,11 +162,11 @@ __global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
 // the cell's order with the same arithmetic as eval_color, so the colours are bit-identical to the
 // inline path; cmf_composite_kernel then sums the segments of every ray from its records.
 
-// Samples of a ray chunk counted per cell: those that need a colour (colour_only), or all of them. One
-// warp per ray, lanes over its samples: the records of a ray are read as contiguous 32-byte sectors.
+// Samples of a ray chunk counted per cell (the backward's item buckets). One warp per ray, lanes over its
+// samples: the records of a ray are read as contiguous 32-byte sectors.
 __global__ void __launch_bounds__(kBlock)
     cmf_count_kernel(const float* __restrict__ rec, const int* __restrict__ stats, const int* __restrict__ inv,
-                     int64_t r0, int64_t n, int K, int* __restrict__ count, bool colour_only) {
+                     int64_t r0, int64_t n, int K, int* __restrict__ count) {
     const int64_t rl = (static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (rl >= n) return;
@@ -252,7 +175,7 @@ __global__ void __launch_bounds__(kBlock)
     if (S > K) return;
     for (int s = lane; s < S; s += 32) {
         const float* q = rec + (r * K + s) * kRecord;
-        if (!colour_only || __ldg(q + 7) < 0.f) atomicAdd(count + __ldg(inv + __float_as_int(__ldg(q + 1))), 1);
+        atomicAdd(count + __ldg(inv + __float_as_int(__ldg(q + 1))), 1);
     }
 }
 
@@ -392,10 +315,8 @@ __global__ void __launch_bounds__(kBlock)
     rgb[3 * r] = acc0, rgb[3 * r + 1] = acc1, rgb[3 * r + 2] = acc2;
 }
 
-// Per-sample record of the cell-major backward: the sample's gradient scalars, written by the replay
-// (one slot per recorded sample, indexed ray * K + sample) and consumed by cm_scatter_kernel.
-//   (gs, gC r, gC g, gC b) | (gC . C, m_min, 1 / sum of colour weights or 0, bits(cell) or -1)
-// Direct form (VG_BWD_DIRECT): 64 bytes at the sample's place in its cell's bucket,
+// Per-sample item of the cell-major backward, written by the replay and consumed by cm_scatter_kernel:
+// 64 bytes at the sample's place in its cell's bucket,
 //   (x, gs) | (gC, gC . C) | (m_min, 1 / sum of colour weights or 0, 0, 0) | (d, 0)
 // where every recorded sample gets an item (zero gradients for the samples that have none). The store of
 // an item waits one sample (DirectItems::put writes the previous one) so that the atomic that reserves
@@ -425,40 +346,24 @@ struct DirectItems {
     }
 };
 
-__device__ __forceinline__ void emit_item(float4* __restrict__ items, int64_t slot, const Sample& P, float gs,
-                                          float gC0, float gC1, float gC2, bool has_c, int* __restrict__ count) {
-    const bool do_c = has_c && (gC0 != 0.f || gC1 != 0.f || gC2 != 0.f);
-    float4* it = items + 2 * slot;
-    if (gs == 0.f && !do_c) {
-        it[1] = make_float4(0.f, 0.f, 0.f, __int_as_float(-1));
-        return;
-    }
-    const float gCC = gC0 * P.C0 + gC1 * P.C1 + gC2 * P.C2;
-    it[0] = make_float4(gs, do_c ? gC0 : 0.f, do_c ? gC1 : 0.f, do_c ? gC2 : 0.f);
-    it[1] = make_float4(gCC, P.mmin, do_c ? P.inv_a : 0.f, __int_as_float(P.cell));
-    atomicAdd(count + P.cell, 1);
-}
-
 // What the replay does with each sample's gradients: scatter them to the sites of its neighbourhood
 // (every ray, or only the rays that were not recorded in full), or write them as items of the
 // cell-major backward (only fully recorded rays).
 enum BwdMode { kScatterAll = 0, kScatterRetraced = 1, kItems = 2 };
 
 struct ItemOut {
-    float4* items;         // (rays of the chunk) x K x 2 float4, or the bucketed direct items
+    float4* items;         // the bucketed items
     int* count;            // (N + 1) samples per cell
     int64_t r0;            // first ray of the chunk
     int64_t n;             // rays in the chunk
-    const int* offsets;    // direct items: first bucket position of every cell
-    int* fill;             // direct items: bucket fill cursors
+    const int* offsets;    // first bucket position of every cell
+    int* fill;             // bucket fill cursors
 };
 
 template <int MODE>
 __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
     foam_backward_kernel(GraphView g, FieldView F, RayView R, FoamCfg c, GradIn gi, float* __restrict__ grad,
                          ItemOut io, int* status) {
-    __shared__ float4 cache_mem[kBwdSlotMem];
-    __shared__ float4 stage_mem[kAgg ? 16 * kBlock : 1];
     const int64_t r = (MODE == kItems ? io.r0 : 0) + static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
     if (r >= (MODE == kItems ? io.r0 + io.n : R.n)) return;
     {
@@ -467,8 +372,6 @@ __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
         if (MODE == kItems && !replayable) return;
         if (MODE == kScatterRetraced && replayable) return;
     }
-    ColorCache<kBwdSlots> cache{cache_mem + threadIdx.x, kBlock};
-    cache.init();
     float o[3], d[3], near, far;
     load_ray(R, r, o, d, near, far);
     float b[16];
@@ -490,10 +393,8 @@ __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
         int walk_steps = 0;
         const int cur = walk_nearest(g, __ldg(g.inv + __ldg(R.start + r)), along(o[0], near, d[0]),
                                 along(o[1], near, d[1]), along(o[2], near, d[2]), walk_steps, err);
-        eval_sample<kBwdSlots, true>(g, F, cur, near, o, d, b, cache, true, P, t_exit, next);
+        eval_sample<true>(g, F, cur, near, o, d, b, true, P, t_exit, next);
     }
-    float4* stage = stage_mem + (kAgg ? 16 * (threadIdx.x & ~31) : 0);
-    const int lane = threadIdx.x & 31;
     float T = 1.f, acc0 = 0.f, acc1 = 0.f, acc2 = 0.f;
     float carry_sigma = 0.f, gP0 = 0.f, gP1 = 0.f, gP2 = 0.f;  // gradients of P from the segment before it
     DirectItems out_items{io.items, io.offsets, io.fill};
@@ -509,8 +410,8 @@ __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
             last = it + 2 >= n_stored;
         } else {
             last = next < 0 || t_exit >= far;
-            eval_sample<kBwdSlots, true>(g, F, last ? P.cell : next, last ? far : fmaxf(t_exit, P.t), o, d, b, cache,
-                                      !last, Q, t_exit_q, next_q);
+            eval_sample<true>(g, F, last ? P.cell : next, last ? far : fmaxf(t_exit, P.t), o, d, b, !last, Q, t_exit_q,
+                              next_q);
         }
         const float delta = Q.t - P.t;
         const float alpha = 1.f - __expf(-0.5f * (P.sigma + Q.sigma) * delta);
@@ -520,8 +421,8 @@ __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
         float c0 = 0.f, c1 = 0.f, c2 = 0.f;
         if (active) {
             // colours of records written without them (foam.cu:443-445)
-            if (!has_p) eval_color(g, F, b, cache, P), has_p = true;
-            if (!has_q) eval_color(g, F, b, cache, Q), has_q = true;
+            if (!has_p) eval_color(g, F, b, P), has_p = true;
+            if (!has_q) eval_color(g, F, b, Q), has_q = true;
             c0 = 0.5f * (P.C0 + Q.C0), c1 = 0.5f * (P.C1 + Q.C1), c2 = 0.5f * (P.C2 + Q.C2);
             acc0 += w * c0, acc1 += w * c1, acc2 += w * c2;
         }
@@ -530,16 +431,10 @@ __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
         g_opacity = delta * (g_opacity - tail_grad);
         const float h0 = active ? 0.5f * w * gR0 : 0.f, h1 = active ? 0.5f * w * gR1 : 0.f,
                     h2 = active ? 0.5f * w * gR2 : 0.f;
-        if (MODE == kItems && VG_BWD_DIRECT)
+        if (MODE == kItems)
             out_items.put(P, carry_sigma + 0.5f * g_opacity, gP0 + h0, gP1 + h1, gP2 + h2, has_p, d);
-        else if (MODE == kItems)
-            emit_item(io.items, (r - io.r0) * K + it, P, carry_sigma + 0.5f * g_opacity, gP0 + h0, gP1 + h1, gP2 + h2,
-                      has_p, io.count);
-        else if (kAgg)
-            scatter_sample_agg(g, F, P, carry_sigma + 0.5f * g_opacity, gP0 + h0, gP1 + h1, gP2 + h2, has_p, b, cache, grad,
-                               stage, lane);
         else
-            sample_grads(g, F, P, carry_sigma + 0.5f * g_opacity, gP0 + h0, gP1 + h1, gP2 + h2, has_p, b, cache, grad);
+            sample_grads(g, F, P, carry_sigma + 0.5f * g_opacity, gP0 + h0, gP1 + h1, gP2 + h2, has_p, b, grad);
         carry_sigma = 0.5f * g_opacity;
         gP0 = h0, gP1 = h1, gP2 = h2;
         T = T_after;
@@ -549,7 +444,7 @@ __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
         n_done = it + 1;
         if (last || T < c.t_thresh) break;
     }
-    if (MODE == kItems && VG_BWD_DIRECT) {
+    if (MODE == kItems) {
         out_items.put(P, carry_sigma, gP0, gP1, gP2, has_p, d);
         // every recorded sample was counted into its bucket: fill the places of any the replay did not
         // reach with zero-gradient items (the replay follows the forward, so normally there are none)
@@ -560,13 +455,9 @@ __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
             out_items.put(Z, 0.f, 0.f, 0.f, 0.f, false, d);
         }
         out_items.flush();
-    } else if (MODE == kItems) {
-        emit_item(io.items, (r - io.r0) * K + n_done, P, carry_sigma, gP0, gP1, gP2, has_p, io.count);
+    } else {
+        sample_grads(g, F, P, carry_sigma, gP0, gP1, gP2, has_p, b, grad);
     }
-    else if (kAgg)
-        scatter_sample_agg(g, F, P, carry_sigma, gP0, gP1, gP2, has_p, b, cache, grad, stage, lane);
-    else
-        sample_grads(g, F, P, carry_sigma, gP0, gP1, gP2, has_p, b, cache, grad);
     if (err) atomicOr(status, err);
 }
 
@@ -579,22 +470,6 @@ __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
 // keeps its site's field record and SH coefficients in registers, loops over the samples (staged in
 // shared memory, read as broadcasts), accumulates the site's gradient in registers and issues one set
 // of 16-byte atomics per (chunk, site).
-
-// Counting sort of the items of a ray chunk by cell: order[offsets[cell] + k] = item slot.
-__global__ void __launch_bounds__(kBlock)
-    cm_bucket_kernel(const float4* __restrict__ items, const int* __restrict__ stats, int64_t r0, int64_t n, int K,
-                     const int* __restrict__ offsets, int* __restrict__ fill, int* __restrict__ order) {
-    const int64_t rl = static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
-    if (rl >= n) return;
-    const int S = __ldg(stats + 3 * (r0 + rl));
-    if (S > K) return;
-    for (int s = 0; s < S; ++s) {
-        const int64_t slot = rl * K + s;
-        const int cell = __float_as_int(__ldg(items + 2 * slot + 1).w);
-        if (cell < 0) continue;
-        order[__ldg(offsets + cell) + atomicAdd(fill + cell, 1)] = static_cast<int>(slot);
-    }
-}
 
 // Chunks of at most kChunk samples of one cell: (cell, first position in order, count).
 __global__ void __launch_bounds__(kBlock)
@@ -722,7 +597,7 @@ __device__ __forceinline__ int scatter_range(const GraphView& g, const FieldView
                     for (int u = 0; u < 4; ++u) {
                         const int k = 4 * qq + u;
                         if (k < 48) {
-                            if (VG_BWD_SH_SPLIT && ((k / 3) & 1))
+                            if ((k / 3) & 1)
                                 h[k % 3] += b[k / 3] * f[u];
                             else
                                 c[k % 3] += b[k / 3] * f[u];
@@ -745,157 +620,38 @@ __device__ __forceinline__ int scatter_range(const GraphView& g, const FieldView
     return j;
 }
 
-#if VG_BWD_HELPERS
-// A chunk of a cell with 16 < n < 32 neighbourhood sites: lane l < n owns neighbour l as in
-// scatter_range; lane n + h (h < 32 - n) helps owner h by accumulating its SH-gradient sums. All lanes
-// walk the chunk's samples in step; per sample the owner computes its colour-gradient factors dc
-// (zero when the pair carries no colour gradient) and its helper reads them by shuffle, so the SH sums
-// are the owner's own fused multiply-adds in the same order.
-template <int S4>
-__device__ __forceinline__ void helped_scatter(const GraphView& g, const FieldView& F, const float4* st, int e0, int n,
-                                               int cnt, int lane, float* __restrict__ grad) {
-    const bool owner = lane < n;
-    const bool helped = lane < 32 - n;   // owners whose SH sums go to lane n + lane
-    const int mine = owner ? lane : lane - n;
-    const int src = lane >= n ? lane - n : lane;
-    const float4 E = __ldg(g.edge + e0 + mine);
-    const int j = site_of(E);
-    const float4* fr = F.rec + kFieldVec * static_cast<int64_t>(j);
-    const float4 r0_ = __ldg(fr), r1_ = __ldg(fr + 1), r2_ = __ldg(fr + 2), r3_ = __ldg(fr + 3);
-    float4 coef[S4];
-#pragma unroll
-    for (int q = 0; q < S4; ++q) coef[q] = owner ? __ldg(F.sh + static_cast<int64_t>(S4) * j + q) : make_float4(0, 0, 0, 0);
-    PairAcc<S4> A;
-    A.zero();
-    for (int i = 0; i < cnt; ++i) {
-        const float4* q = st + kItemVec * i;
-        float dc[3] = {0.f, 0.f, 0.f};
-        bool coloured = false;
-        if (owner) {
-            const float4 q0 = q[0];
-            const float v0 = q0.x - E.x, v1 = q0.y - E.y, v2 = q0.z - E.z;
-            const float gs = q0.w;
-            if (gs != 0.f) {
-                const float gc = gs * __expf(r1_.z - 0.5f * maha(r0_, r1_, v0, v1, v2));
-                if (fabsf(gc) > 1e-12f) {
-                    const float gm = -0.5f * gc;
-                    A.ad[0] += gc, A.ad[1] += gm * v0 * v0, A.ad[2] += 2.f * gm * v0 * v1, A.ad[3] += 2.f * gm * v0 * v2;
-                    A.ad[4] += gm * v1 * v1, A.ad[5] += 2.f * gm * v1 * v2, A.ad[6] += gm * v2 * v2;
-                }
-            }
-            const float4 q1 = q[1], q2 = q[2];
-            if (q2.y > 0.f) {
-                const float a = __expf(-0.5f * (maha(r2_, r3_, v0, v1, v2) - q2.x)) * q2.y;
-                if (a >= kMinWeight) {
-                    float b[16];
-                    const float4 b0 = q[3], b1 = q[4], b2 = q[5], b3 = q[6];
-                    b[0] = b0.x, b[1] = b0.y, b[2] = b0.z, b[3] = b0.w, b[4] = b1.x, b[5] = b1.y, b[6] = b1.z;
-                    b[7] = b1.w, b[8] = b2.x, b[9] = b2.y, b[10] = b2.z, b[11] = b2.w, b[12] = b3.x;
-                    b[13] = b3.y, b[14] = b3.z, b[15] = b3.w;
-                    float c[3] = {0.5f, 0.5f, 0.5f}, h[3] = {0.f, 0.f, 0.f};
-#pragma unroll
-                    for (int qq = 0; qq < S4; ++qq) {
-                        const float f[4] = {coef[qq].x, coef[qq].y, coef[qq].z, coef[qq].w};
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            const int k = 4 * qq + u;
-                            if (k < 48) {
-                                if (VG_BWD_SH_SPLIT && ((k / 3) & 1))
-                                    h[k % 3] += b[k / 3] * f[u];
-                                else
-                                    c[k % 3] += b[k / 3] * f[u];
-                            }
-                        }
-                    }
-                    c[0] += h[0], c[1] += h[1], c[2] += h[2];
-                    dc[0] = c[0] > 0.f ? a * q1.x : 0.f, dc[1] = c[1] > 0.f ? a * q1.y : 0.f;
-                    dc[2] = c[2] > 0.f ? a * q1.z : 0.f;
-                    coloured = true;
-                    if (!helped) {
-#pragma unroll
-                        for (int k = 0; k < 4 * S4; ++k)
-                            if (k < 48) A.ash[k] += b[k / 3] * dc[k % 3];
-                    }
-                    const float ga = q1.x * fmaxf(c[0], 0.f) + q1.y * fmaxf(c[1], 0.f) + q1.z * fmaxf(c[2], 0.f);
-                    const float gm = -0.5f * a * (ga - q1.w);
-                    A.ac[0] += gm * v0 * v0, A.ac[1] += 2.f * gm * v0 * v1, A.ac[2] += 2.f * gm * v0 * v2;
-                    A.ac[3] += gm * v1 * v1, A.ac[4] += 2.f * gm * v1 * v2, A.ac[5] += gm * v2 * v2;
-                }
-            }
-        }
-        // the helpers take their owner's factors (every lane of the warp takes part)
-        const float t0 = __shfl_sync(0xffffffffu, dc[0], src), t1 = __shfl_sync(0xffffffffu, dc[1], src);
-        const float t2 = __shfl_sync(0xffffffffu, dc[2], src);
-        const bool fed = __shfl_sync(0xffffffffu, coloured ? 1 : 0, src) != 0;
-        if (!owner && fed) {
-            const float4 b0 = q[3], b1 = q[4], b2 = q[5], b3 = q[6];
-            const float b[16] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w,
-                                 b2.x, b2.y, b2.z, b2.w, b3.x, b3.y, b3.z, b3.w};
-            const float t[3] = {t0, t1, t2};
-#pragma unroll
-            for (int k = 0; k < 4 * S4; ++k)
-                if (k < 48) A.ash[k] += b[k / 3] * t[k % 3];
-        }
-    }
-    A.flush(grad, j);  // a helper holds only SH sums, a helped owner none: flush skips zero vectors
-}
-#endif
 
-// The (neighbour, sample) pairs of a chunk of a cell with n < 32 neighbour sites (self included) spread
-// over the 32 lanes so that every lane does about n cnt / 32 of them, in at most two phases whose
-// boundaries all lanes cross together:
-//   n <= 16  R = 32 / n replicas of every neighbour, replica r taking the r-th of R slices of the samples;
-//   n > 16   phase 1: lane l < n takes neighbour l, and the m = 32 - n spare lanes each take the second
-//            half of the samples of neighbours 0..m-1, whose owners take the first half; the owners of
-//            neighbours m..n-1 take ceil(cnt / 2) samples. Phase 2: the remaining floor(cnt / 2) samples
-//            of those q = n - m neighbours, split among U = 32 / q lanes each.
-// Lanes holding sums of the same neighbour combine them with warp shuffles, then one lane per neighbour
-// adds them to the gradient pack. Same sums as one lane per neighbour, in another order.
+// The (neighbour, sample) pairs of a chunk of a cell with n <= kReplicaMaxN neighbour sites (self
+// included) spread over the 32 lanes: R = 32 / n replicas of every neighbour, replica r taking the r-th
+// of R slices of the samples. Replicas of a neighbour combine their sums with warp shuffles, then one
+// lane per neighbour adds them to the gradient pack. Same sums as one lane per neighbour, in another
+// order.
 template <int S4>
-__device__ __forceinline__ void balanced_scatter(const GraphView& g, const FieldView& F, const float4* st, int e0,
-                                                 int n, int cnt, int lane, float* __restrict__ grad) {
+__device__ __forceinline__ void replicated_scatter(const GraphView& g, const FieldView& F, const float4* st, int e0,
+                                                   int n, int cnt, int lane, float* __restrict__ grad) {
     PairAcc<S4> A;
     A.zero();
-    if (n <= 16) {
-        const int R = 32 / n;
-        const int j = lane % n, r = lane / n;
-        int site = 0;
-        if (r < R) site = scatter_range<S4>(g, F, e0 + j, st, (r * cnt) / R, ((r + 1) * cnt) / R, A);
-        for (int u = 1; u < R; ++u) A.pull(min(lane + u * n, 31), lane < n);
-        if (lane < n) A.flush(grad, site);
-        return;
-    }
-    const int m = 32 - n, h = cnt / 2, T1 = cnt - h;
-    int site;
-    if (lane < n)
-        site = scatter_range<S4>(g, F, e0 + lane, st, 0, lane < m ? h : T1, A);
-    else
-        site = scatter_range<S4>(g, F, e0 + lane - n, st, h, cnt, A);
-    A.pull(min(lane + n, 31), lane < m);
+    const int R = 32 / n;
+    const int j = lane % n, r = lane / n;
+    int site = 0;
+    if (r < R) site = scatter_range<S4>(g, F, e0 + j, st, (r * cnt) / R, ((r + 1) * cnt) / R, A);
+    for (int u = 1; u < R; ++u) A.pull(min(lane + u * n, 31), lane < n);
     if (lane < n) A.flush(grad, site);
-    if (h == 0) return;
-    const int q = n - m, U = 32 / q;
-    const int j = m + lane % q, u = lane / q;
-    A.zero();
-    if (u < U) site = scatter_range<S4>(g, F, e0 + j, st, T1 + (u * h) / U, T1 + ((u + 1) * h) / U, A);
-    for (int w = 1; w < U; ++w) A.pull(min(lane + w * q, 31), lane < q);
-    if (lane < q) A.flush(grad, site);
 }
 
-// Where cm_scatter_kernel finds a chunk's samples: 64-byte items stored contiguously per cell (kBucketed),
-// 64-byte items reached through the cell-sorted index array (kIndexed), or 32-byte items through the
-// index array plus the sample's t in the records and its ray (kRecords).
-enum StageMode { kBucketed = 0, kIndexed = 1, kRecords = 2 };
+// Where cm_scatter_kernel finds a chunk's samples: 64-byte items stored contiguously per cell (kBucketed,
+// the foam backward), or 64-byte items reached through the cell-sorted index array (kIndexed, the march
+// backward).
+enum StageMode { kBucketed = 0, kIndexed = 1 };
 
 // With kAsync the bucketed stage returns through its copy-ahead loop, so the generic loop below is
 // unreachable in that instantiation (and removed); nvcc's note about it is silenced for this kernel only.
 #pragma nv_diag_suppress 128
 template <int S4, int STAGE>
 __global__ void __launch_bounds__(kBlock, VG_SCATTER_MINB)
-    cm_scatter_kernel(GraphView g, FieldView F, RayView R, const float* __restrict__ rec, int K,
-                      const float4* __restrict__ items, const int* __restrict__ order, const int4* __restrict__ chunks,
-                      const int* __restrict__ n_chunks_ptr, int64_t r0, float* __restrict__ grad) {
-    constexpr bool kAsync = STAGE == kBucketed && VG_BWD_ASYNC;
+    cm_scatter_kernel(GraphView g, FieldView F, const float4* __restrict__ items, const int* __restrict__ order,
+                      const int4* __restrict__ chunks, const int* __restrict__ n_chunks_ptr, float* __restrict__ grad) {
+    constexpr bool kAsync = STAGE == kBucketed;
     __shared__ float4 smem[(kBlock / 32) * kChunk * kItemVec];
     __shared__ float4 raw_smem[kAsync ? (kBlock / 32) * kChunk * 4 : 1];
     const int lane = threadIdx.x & 31;
@@ -936,12 +692,8 @@ __global__ void __launch_bounds__(kBlock, VG_SCATTER_MINB)
                 cp_async_commit();
             }
             const int e0 = __ldg(g.off + Cur.x), e1 = __ldg(g.off + Cur.x + 1);
-            if (e1 - e0 <= VG_BWD_BALANCE) {
-                balanced_scatter<S4>(g, F, st, e0, e1 - e0, Cur.z, lane, grad);
-#if VG_BWD_HELPERS
-            } else if (e1 - e0 < 32) {
-                helped_scatter<S4>(g, F, st, e0, e1 - e0, Cur.z, lane, grad);
-#endif
+            if (e1 - e0 <= kReplicaMaxN) {
+                replicated_scatter<S4>(g, F, st, e0, e1 - e0, Cur.z, lane, grad);
             } else {
                 for (int e = e0 + lane; e < e1; e += 32) {
                     PairAcc<S4> A;
@@ -957,7 +709,7 @@ __global__ void __launch_bounds__(kBlock, VG_SCATTER_MINB)
     for (int ch = blockIdx.x * (kBlock / 32) + (threadIdx.x >> 5); ch < n_chunks; ch += warps) {
         const int4 C = __ldg(chunks + ch);
         const int cell = C.x, cnt = C.z;
-        for (int li = lane; li < cnt && STAGE != kRecords; li += 32) {  // stage the chunk's 64-byte items
+        for (int li = lane; li < cnt; li += 32) {  // stage the chunk's 64-byte items
             const int64_t at = STAGE == kIndexed ? __ldg(order + C.y + li) : static_cast<int64_t>(C.y) + li;
             const float4* it = items + 4 * at;
             const float4 i3 = __ldg(it + 3);
@@ -970,35 +722,10 @@ __global__ void __launch_bounds__(kBlock, VG_SCATTER_MINB)
             q[5] = make_float4(b[8], b[9], b[10], b[11]);
             q[6] = make_float4(b[12], b[13], b[14], b[15]);
         }
-        for (int li = lane; li < cnt && STAGE == kRecords; li += 32) {  // stage the chunk's samples
-            const int slot = __ldg(order + C.y + li);
-            const int64_t r = r0 + slot / K;
-            const int sidx = slot % K;
-            const float t = __ldg(rec + (r * K + sidx) * kRecord);
-            float o[3], d[3];
-#pragma unroll
-            for (int a = 0; a < 3; ++a) o[a] = __ldg(R.o + 3 * r + a), d[a] = __ldg(R.d + 3 * r + a);
-            const float4 i0 = __ldg(items + 2 * static_cast<int64_t>(slot));
-            const float4 i1 = __ldg(items + 2 * static_cast<int64_t>(slot) + 1);
-            float b[16];
-            sh_basis(d[0], d[1], d[2], F.sh_deg, b);
-            float4* q = st + kItemVec * li;
-            q[0] = make_float4(along(o[0], t, d[0]), along(o[1], t, d[1]), along(o[2], t, d[2]), i0.x);
-            q[1] = make_float4(i0.y, i0.z, i0.w, i1.x);
-            q[2] = make_float4(i1.y, i1.z, 0.f, 0.f);
-            q[3] = make_float4(b[0], b[1], b[2], b[3]);
-            q[4] = make_float4(b[4], b[5], b[6], b[7]);
-            q[5] = make_float4(b[8], b[9], b[10], b[11]);
-            q[6] = make_float4(b[12], b[13], b[14], b[15]);
-        }
         __syncwarp();
         const int e0 = __ldg(g.off + cell), e1 = __ldg(g.off + cell + 1);
-        if (e1 - e0 <= VG_BWD_BALANCE) {
-            balanced_scatter<S4>(g, F, st, e0, e1 - e0, cnt, lane, grad);
-#if VG_BWD_HELPERS
-        } else if (e1 - e0 < 32) {
-            helped_scatter<S4>(g, F, st, e0, e1 - e0, cnt, lane, grad);
-#endif
+        if (e1 - e0 <= kReplicaMaxN) {
+            replicated_scatter<S4>(g, F, st, e0, e1 - e0, cnt, lane, grad);
         } else {
             for (int e = e0 + lane; e < e1; e += 32) {  // one neighbour site per lane
                 PairAcc<S4> A;
@@ -1028,7 +755,6 @@ __global__ void __launch_bounds__(kBlock)
     const int64_t rl = static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
     if (rl >= nr) return;
     const int64_t r = r0 + rl;
-    ColorCache<0> cache{nullptr, 0};
     Schedule M;
     schedule_of(R, c, r, M);
     float b[16];
@@ -1052,7 +778,7 @@ __global__ void __launch_bounds__(kBlock)
         const bool active = w > c.w_thresh;
         S.C0 = S.C1 = S.C2 = 0.f, S.mmin = 0.f, S.inv_a = 0.f;
         if (active) {
-            eval_color(g, F, b, cache, S);
+            eval_color(g, F, b, S);
             acc0 += w * S.C0, acc1 += w * S.C1, acc2 += w * S.C2;
         }
         float gsig = gR0 * (T_after * S.C0 - (fg0 - acc0)) + gR1 * (T_after * S.C1 - (fg1 - acc1)) +
@@ -1069,7 +795,7 @@ __global__ void __launch_bounds__(kBlock)
             it[3] = make_float4(M.d[0], M.d[1], M.d[2], 0.f);
             atomicAdd(count + cur, 1);
         } else {
-            sample_grads(g, F, S, gsig, gC0, gC1, gC2, active, b, cache, grad);
+            sample_grads(g, F, S, gsig, gC0, gC1, gC2, active, b, grad);
         }
         T = T_after;
         if (T < c.t_thresh) {
@@ -1111,7 +837,7 @@ struct CmLayout {
 // Scratch of the cell-major passes over rays [r0, r0 + rays_per_pass): per-sample items (backward
 // only), the cell-sorted order, per-cell counts / fill cursors / offsets, the chunk list, a counter and
 // the CUB scan storage.
-CmLayout cm_layout(int64_t n_sites, int64_t n_rays, int K, bool with_items, int item_bytes = VG_BWD_DIRECT ? 64 : 32) {
+CmLayout cm_layout(int64_t n_sites, int64_t n_rays, int K, bool with_items, int item_bytes = 64) {
     CmLayout L{};
     if (K <= 0 || n_rays <= 0) return L;
     L.rays_per_pass = std::max<int64_t>(1, std::min<int64_t>(n_rays, kCmItems / K));
@@ -1126,7 +852,7 @@ CmLayout cm_layout(int64_t n_sites, int64_t n_rays, int K, bool with_items, int 
     L.n_items = take(with_items ? 4 * L.rays_per_pass : 0);
     L.order = take(4 * slots);
     const int64_t passes = (n_rays + L.rays_per_pass - 1) / L.rays_per_pass;
-    L.count = take(4 * (n_sites + 1) * (with_items || !VG_FWD_COUNT ? 1 : passes));
+    L.count = take(4 * (n_sites + 1) * (with_items ? 1 : passes));
     L.fill = take(4 * n_sites);
     L.offsets = take(4 * (n_sites + 1));
     L.chunks = take(16 * (slots / 32 + n_sites + 1));
@@ -1164,17 +890,12 @@ cudaError_t cm_scatter_bucketed(const GraphView& g, const FieldView& F, const fl
     if (e != cudaSuccess) return e;
     cm_chunks_kernel<<<blocks(n), kBlock, 0, st>>>(offsets, n, chunks, counter);
     const int grid = sm_count() * 3;
-    const RayView none{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 0};
     ProfScope ps(kProfScatter, st);
     switch (F.s4) {
-        case 1: cm_scatter_kernel<1, kBucketed><<<grid, kBlock, 0, st>>>(g, F, none, nullptr, 0, items, nullptr, chunks,
-                                                                         counter, 0, grad); break;
-        case 3: cm_scatter_kernel<3, kBucketed><<<grid, kBlock, 0, st>>>(g, F, none, nullptr, 0, items, nullptr, chunks,
-                                                                         counter, 0, grad); break;
-        case 7: cm_scatter_kernel<7, kBucketed><<<grid, kBlock, 0, st>>>(g, F, none, nullptr, 0, items, nullptr, chunks,
-                                                                         counter, 0, grad); break;
-        default: cm_scatter_kernel<12, kBucketed><<<grid, kBlock, 0, st>>>(g, F, none, nullptr, 0, items, nullptr,
-                                                                           chunks, counter, 0, grad); break;
+        case 1: cm_scatter_kernel<1, kBucketed><<<grid, kBlock, 0, st>>>(g, F, items, nullptr, chunks, counter, grad); break;
+        case 3: cm_scatter_kernel<3, kBucketed><<<grid, kBlock, 0, st>>>(g, F, items, nullptr, chunks, counter, grad); break;
+        case 7: cm_scatter_kernel<7, kBucketed><<<grid, kBlock, 0, st>>>(g, F, items, nullptr, chunks, counter, grad); break;
+        default: cm_scatter_kernel<12, kBucketed><<<grid, kBlock, 0, st>>>(g, F, items, nullptr, chunks, counter, grad); break;
     }
     return cudaGetLastError();
 }
@@ -1216,14 +937,10 @@ cudaError_t march_backward_cm(const GraphView& g, const FieldView& F, const RayV
         cm_chunks_kernel<<<blocks(n), kBlock, 0, st>>>(offsets, n, chunks, counter);
         ProfScope ps(kProfScatter, st);
         switch (F.s4) {
-            case 1: cm_scatter_kernel<1, kIndexed><<<grid, kBlock, 0, st>>>(g, F, R, nullptr, 0, items, order, chunks,
-                                                                            counter, r0, grad); break;
-            case 3: cm_scatter_kernel<3, kIndexed><<<grid, kBlock, 0, st>>>(g, F, R, nullptr, 0, items, order, chunks,
-                                                                            counter, r0, grad); break;
-            case 7: cm_scatter_kernel<7, kIndexed><<<grid, kBlock, 0, st>>>(g, F, R, nullptr, 0, items, order, chunks,
-                                                                            counter, r0, grad); break;
-            default: cm_scatter_kernel<12, kIndexed><<<grid, kBlock, 0, st>>>(g, F, R, nullptr, 0, items, order,
-                                                                              chunks, counter, r0, grad); break;
+            case 1: cm_scatter_kernel<1, kIndexed><<<grid, kBlock, 0, st>>>(g, F, items, order, chunks, counter, grad); break;
+            case 3: cm_scatter_kernel<3, kIndexed><<<grid, kBlock, 0, st>>>(g, F, items, order, chunks, counter, grad); break;
+            case 7: cm_scatter_kernel<7, kIndexed><<<grid, kBlock, 0, st>>>(g, F, items, order, chunks, counter, grad); break;
+            default: cm_scatter_kernel<12, kIndexed><<<grid, kBlock, 0, st>>>(g, F, items, order, chunks, counter, grad); break;
         }
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
@@ -1236,7 +953,7 @@ cudaError_t march_backward_cm(const GraphView& g, const FieldView& F, const RayV
 constexpr int kScratchK = 256;
 
 size_t foam_forward_workspace(int64_t n_sites, int64_t n_rays, int record_cap) {
-    if (!VG_FWD_CELL_MAJOR || n_rays <= 0) return 0;
+    if (n_rays <= 0) return 0;
     if (record_cap > 0) return cm_layout(n_sites, n_rays, record_cap, false).total;
     const CmLayout L = cm_layout(n_sites, n_rays, kScratchK, false);
     return L.total + al256(static_cast<size_t>(L.rays_per_pass) * kScratchK * kRecord * sizeof(float));
@@ -1252,7 +969,8 @@ cudaError_t forward_deferred(const GraphView& g, const FieldView& F, const RayVi
     const int K = c.record_cap;
     int* count_all = reinterpret_cast<int*>(b + L.count);
     FoamCfg cc = c;
-    if (VG_FWD_COUNT) {
+    {
+        // the traversal counts the samples that need a colour per (pass, cell) as it marks them
         const int64_t passes = (R.n + L.rays_per_pass - 1) / L.rays_per_pass;
         const cudaError_t e = cudaMemsetAsync(count_all, 0, 4 * static_cast<size_t>(g.n + 1) * passes, st);
         if (e != cudaSuccess) return e;
@@ -1272,14 +990,10 @@ cudaError_t forward_deferred(const GraphView& g, const FieldView& F, const RayVi
     const int grid = sm_count() * 8;
     for (int64_t r0 = 0; r0 < R.n; r0 += L.rays_per_pass) {
         const int64_t nr = std::min<int64_t>(L.rays_per_pass, R.n - r0);
-        int* count = VG_FWD_COUNT ? count_all + (r0 / L.rays_per_pass) * static_cast<int64_t>(n + 1) : count_all;
-        cudaError_t e = cudaSuccess;
-        if (!VG_FWD_COUNT) e = cudaMemsetAsync(count, 0, 4 * static_cast<size_t>(n + 1), st);
-        if (e == cudaSuccess) e = cudaMemsetAsync(fill, 0, 4 * static_cast<size_t>(n), st);
+        int* count = count_all + (r0 / L.rays_per_pass) * static_cast<int64_t>(n + 1);
+        cudaError_t e = cudaMemsetAsync(fill, 0, 4 * static_cast<size_t>(n), st);
         if (e == cudaSuccess) e = cudaMemsetAsync(counter, 0, 16, st);
         if (e != cudaSuccess) return e;
-        if (!VG_FWD_COUNT)
-            cmf_count_kernel<<<blocks(32 * nr), kBlock, 0, st>>>(out.rec, out.stats, g.inv, r0, nr, K, count, true);
         size_t tb = L.temp_bytes;
         e = cub::DeviceScan::ExclusiveSum(b + L.temp, tb, count, offsets, n + 1, st);
         if (e != cudaSuccess) return e;
@@ -1307,7 +1021,7 @@ cudaError_t foam_forward(const GraphView& g, const FieldView& F, const RayView& 
     if (R.n == 0) return cudaSuccess;
     const int K = c.record_cap;
     const bool record = K > 0 && out.rec != nullptr;
-    const bool room = VG_FWD_CELL_MAJOR && cm_ws != nullptr && cm_bytes >= foam_forward_workspace(g.n, R.n, K);
+    const bool room = cm_ws != nullptr && cm_bytes >= foam_forward_workspace(g.n, R.n, K);
     char* b = static_cast<char*>(cm_ws);
     if (record) {
         if (!room) {
@@ -1343,7 +1057,7 @@ cudaError_t foam_backward(const GraphView& g, const FieldView& F, const RayView&
     const int K = gi.record_cap;
     const CmLayout L = cm_layout(g.n, R.n, K, true);
     const ItemOut none{nullptr, nullptr, 0, 0, nullptr, nullptr};
-    if (!VG_BWD_CELL_MAJOR || gi.rec == nullptr || K <= 0 || cm_ws == nullptr || cm_bytes < L.total ||
+    if (gi.rec == nullptr || K <= 0 || cm_ws == nullptr || cm_bytes < L.total ||
         L.total == 0) {
         foam_backward_kernel<kScatterAll><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, gi, grad, none, status);
         return cudaGetLastError();
@@ -1360,7 +1074,6 @@ cudaError_t foam_backward(const GraphView& g, const FieldView& F, const RayView&
     int* counter = reinterpret_cast<int*>(b + L.counter);
     const int n = g.n;
     const int grid = sm_count() * 3;
-    constexpr int kStage = VG_BWD_DIRECT ? kBucketed : kRecords;
     for (int64_t r0 = 0; r0 < R.n; r0 += L.rays_per_pass) {
         const int64_t nr = std::min<int64_t>(L.rays_per_pass, R.n - r0);
         cudaError_t e = cudaMemsetAsync(count, 0, 4 * static_cast<size_t>(n + 1), st);
@@ -1369,29 +1082,20 @@ cudaError_t foam_backward(const GraphView& g, const FieldView& F, const RayView&
         if (e != cudaSuccess) return e;
         const ItemOut io{items, count, r0, nr, offsets, fill};
         size_t tb = L.temp_bytes;
-        if (VG_BWD_DIRECT) {
-            cmf_count_kernel<<<blocks(32 * nr), kBlock, 0, st>>>(gi.rec, gi.stats, g.inv, r0, nr, K, count, false);
-            e = cub::DeviceScan::ExclusiveSum(b + L.temp, tb, count, offsets, n + 1, st);
-            if (e != cudaSuccess) return e;
+        cmf_count_kernel<<<blocks(32 * nr), kBlock, 0, st>>>(gi.rec, gi.stats, g.inv, r0, nr, K, count);
+        e = cub::DeviceScan::ExclusiveSum(b + L.temp, tb, count, offsets, n + 1, st);
+        if (e != cudaSuccess) return e;
+        {
             ProfScope ps(kProfReplay, st);
             foam_backward_kernel<kItems><<<blocks(nr), kBlock, 0, st>>>(g, F, R, c, gi, grad, io, status);
-        } else {
-            foam_backward_kernel<kItems><<<blocks(nr), kBlock, 0, st>>>(g, F, R, c, gi, grad, io, status);
-            e = cub::DeviceScan::ExclusiveSum(b + L.temp, tb, count, offsets, n + 1, st);
-            if (e != cudaSuccess) return e;
-            cm_bucket_kernel<<<blocks(nr), kBlock, 0, st>>>(items, gi.stats, r0, nr, K, offsets, fill, order);
         }
         cm_chunks_kernel<<<blocks(n), kBlock, 0, st>>>(offsets, n, chunks, counter);
         ProfScope ps(kProfScatter, st);
         switch (F.s4) {
-            case 1: cm_scatter_kernel<1, kStage><<<grid, kBlock, 0, st>>>(g, F, R, gi.rec, K, items, order, chunks, counter, r0,
-                                                                  grad); break;
-            case 3: cm_scatter_kernel<3, kStage><<<grid, kBlock, 0, st>>>(g, F, R, gi.rec, K, items, order, chunks, counter, r0,
-                                                                  grad); break;
-            case 7: cm_scatter_kernel<7, kStage><<<grid, kBlock, 0, st>>>(g, F, R, gi.rec, K, items, order, chunks, counter, r0,
-                                                                  grad); break;
-            default: cm_scatter_kernel<12, kStage><<<grid, kBlock, 0, st>>>(g, F, R, gi.rec, K, items, order, chunks, counter,
-                                                                    r0, grad); break;
+            case 1: cm_scatter_kernel<1, kBucketed><<<grid, kBlock, 0, st>>>(g, F, items, nullptr, chunks, counter, grad); break;
+            case 3: cm_scatter_kernel<3, kBucketed><<<grid, kBlock, 0, st>>>(g, F, items, nullptr, chunks, counter, grad); break;
+            case 7: cm_scatter_kernel<7, kBucketed><<<grid, kBlock, 0, st>>>(g, F, items, nullptr, chunks, counter, grad); break;
+            default: cm_scatter_kernel<12, kBucketed><<<grid, kBlock, 0, st>>>(g, F, items, nullptr, chunks, counter, grad); break;
         }
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;

@@ -9,34 +9,15 @@
 #include "prof.cuh"
 #include "render_core.cuh"
 
-// Colour cache slots and warp-aggregated atomics: see foam.cu.
-#ifndef VG_MARCH_SLOTS
-#define VG_MARCH_SLOTS 0
-#endif
-#ifndef VG_BWD_AGG
-#define VG_BWD_AGG 0
-#endif
-// VG_MARCH_CELL_MAJOR  1: the backward writes its samples as items scattered cell-major (foam.cu) when
-//                      the caller's workspace holds them; 0: per-lane scatter only
-#ifndef VG_MARCH_CELL_MAJOR
-#define VG_MARCH_CELL_MAJOR 1
-#endif
-
 namespace vg {
 namespace {
 
 constexpr int kBlock = 128;
-constexpr int kSlots = VG_MARCH_SLOTS;
-constexpr int kSlotMem = kSlots > 0 ? kSlots * kBlock : 1;
-constexpr bool kAgg = VG_BWD_AGG != 0;
 
 __global__ void __launch_bounds__(kBlock)
     march_forward_kernel(GraphView g, FieldView F, RayView R, MarchCfg c, Outputs out, int* status) {
-    __shared__ float4 cache_mem[kSlotMem];
     const int64_t r = static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
     if (r >= R.n) return;
-    ColorCache<kSlots> cache{cache_mem + threadIdx.x, kBlock};
-    cache.init();
     Schedule M;
     schedule_of(R, c, r, M);
     float b[16];
@@ -55,7 +36,7 @@ __global__ void __launch_bounds__(kBlock)
         const float w = T * alpha;
         ++n_samples;
         if (w > c.w_thresh) {
-            eval_color(g, F, b, cache, S);
+            eval_color(g, F, b, S);
             acc0 += w * S.C0, acc1 += w * S.C1, acc2 += w * S.C2;
             dep += w * t;
             ++n_color;
@@ -73,14 +54,8 @@ __global__ void __launch_bounds__(kBlock)
 __global__ void __launch_bounds__(kBlock)
     march_backward_kernel(GraphView g, FieldView F, RayView R, MarchCfg c, GradIn gi, float* __restrict__ grad,
                           int* status) {
-    __shared__ float4 cache_mem[kSlotMem];
-    __shared__ float4 stage_mem[kAgg ? 16 * kBlock : 1];
-    float4* stage = stage_mem + (kAgg ? 16 * (threadIdx.x & ~31) : 0);
-    const int lane = threadIdx.x & 31;
     const int64_t r = static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
     if (r >= R.n) return;
-    ColorCache<kSlots> cache{cache_mem + threadIdx.x, kBlock};
-    cache.init();
     Schedule M;
     schedule_of(R, c, r, M);
     float b[16];
@@ -104,18 +79,14 @@ __global__ void __launch_bounds__(kBlock)
         const bool active = w > c.w_thresh;
         S.C0 = S.C1 = S.C2 = 0.f, S.mmin = 0.f, S.inv_a = 0.f;
         if (active) {
-            eval_color(g, F, b, cache, S);
+            eval_color(g, F, b, S);
             acc0 += w * S.C0, acc1 += w * S.C1, acc2 += w * S.C2;
         }
         float gsig = gR0 * (T_after * S.C0 - (fg0 - acc0)) + gR1 * (T_after * S.C1 - (fg1 - acc1)) +
                      gR2 * (T_after * S.C2 - (fg2 - acc2));
         gsig = delta * (gsig - tail_grad);
-        if (kAgg)
-            scatter_sample_agg(g, F, S, gsig, active ? w * gR0 : 0.f, active ? w * gR1 : 0.f, active ? w * gR2 : 0.f,
-                               active, b, cache, grad, stage, lane);
-        else
-            sample_grads(g, F, S, gsig, active ? w * gR0 : 0.f, active ? w * gR1 : 0.f, active ? w * gR2 : 0.f,
-                           active, b, cache, grad);
+        sample_grads(g, F, S, gsig, active ? w * gR0 : 0.f, active ? w * gR1 : 0.f, active ? w * gR2 : 0.f, active,
+                     b, grad);
         T = T_after;
         if (T < c.t_thresh) break;
     }
@@ -139,7 +110,7 @@ cudaError_t march_forward(const GraphView& g, const FieldView& F, const RayView&
 cudaError_t march_backward(const GraphView& g, const FieldView& F, const RayView& R, const MarchCfg& c,
                            const GradIn& gi, float* grad, int* status, void* cm_ws, size_t cm_bytes, cudaStream_t st) {
     if (R.n == 0) return cudaSuccess;
-    if (VG_MARCH_CELL_MAJOR && cm_ws != nullptr && cm_bytes >= march_backward_workspace(g.n, R.n))
+    if (cm_ws != nullptr && cm_bytes >= march_backward_workspace(g.n, R.n))
         return march_backward_cm(g, F, R, c, gi, grad, status, cm_ws, st);
     march_backward_kernel<<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, gi, grad, status);
     return cudaGetLastError();

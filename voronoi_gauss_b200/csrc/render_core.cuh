@@ -6,26 +6,11 @@
 
 #include "vg_common.cuh"
 
-// VG_SAMPLE_UNROLL  unroll factor of the neighbour loops of eval_sample / eval_density
-//                   (loads of later neighbours can then be issued before the arithmetic of earlier ones)
-#ifndef VG_SAMPLE_UNROLL
-#define VG_SAMPLE_UNROLL 4
-#endif
-
-// VG_FWD_PREFETCH   1: half way through a cell's neighbours, eval_sample prefetches into L1 the CSR
-//                   offsets of the exit face leading so far (the next cell's first, dependent load);
-//                   0: no prefetch
-#ifndef VG_FWD_PREFETCH
-#define VG_FWD_PREFETCH 0
-#endif
-
 namespace vg {
 
-constexpr int kSampleUnroll = VG_SAMPLE_UNROLL;
-
-#if VG_FWD_PREFETCH
-__device__ __forceinline__ void prefetch_l1(const void* p) { asm volatile("prefetch.global.L1 [%0];" ::"l"(p)); }
-#endif
+// unroll factor of the neighbour loops of eval_sample / eval_density (loads of later neighbours are
+// issued before the arithmetic of earlier ones; measured best on B200)
+constexpr int kSampleUnroll = 4;
 
 // One sample of a ray: position, the cell whose neighbourhood evaluates it, density and colour.
 struct Sample {
@@ -38,11 +23,10 @@ struct Sample {
 // Density sum_k exp(min(raw_k, 30) - v^T dA_k v / 2) over {cell} U adj(cell) (foam.cu:211-221), with
 // COLOR the colour blend of the neighbourhood (foam.cu:224-249, one online pass) and, when want_exit,
 // the exit face of the cell along the ray (foam.cu:185-209; next = -1 when unbounded ahead).
-template <int SLOTS, bool COLOR>
+template <bool COLOR>
 __device__ __forceinline__ void eval_sample(const GraphView& g, const FieldView& F, int cell, float t,
                                             const float (&o)[3], const float (&d)[3], const float (&b)[16],
-                                            ColorCache<SLOTS>& cache, bool want_exit, Sample& S, float& t_exit,
-                                            int& next) {
+                                            bool want_exit, Sample& S, float& t_exit, int& next) {
     S.t = t;
     S.x0 = along(o[0], t, d[0]), S.x1 = along(o[1], t, d[1]), S.x2 = along(o[2], t, d[2]);
     S.cell = cell;
@@ -52,17 +36,11 @@ __device__ __forceinline__ void eval_sample(const GraphView& g, const FieldView&
     Blend B;
     B.reset();
     t_exit = kInf, next = -1;
-#if VG_FWD_PREFETCH
-    const int e_half = e0 + ((e1 - e0) >> 1);
-#endif
 #pragma unroll kSampleUnroll
     for (int e = e0; e < e1; ++e) {
         const float4 E = e == e0 ? Pc : __ldg(g.edge + e);
         const int j = site_of(E);
         if (want_exit && e > e0) exit_candidate(E, Pc.x, Pc.y, Pc.z, o, d, t_exit, next, g.perm);
-#if VG_FWD_PREFETCH
-        if (want_exit && e == e_half && next >= 0) prefetch_l1(g.off + next);
-#endif
         const float v0 = S.x0 - E.x, v1 = S.x1 - E.y, v2 = S.x2 - E.z;
         const float4* r = F.rec + kFieldVec * static_cast<int64_t>(j);
         const float4 r0 = __ldg(r), r1 = __ldg(r + 1);
@@ -70,7 +48,7 @@ __device__ __forceinline__ void eval_sample(const GraphView& g, const FieldView&
         if (COLOR) {
             const float4 r2 = __ldg(r + 2), r3 = __ldg(r + 3);
             float c[3];
-            cache.get(F, j, b, c);
+            site_color(F, j, b, c);
             B.add(maha(r2, r3, v0, v1, v2), c[0], c[1], c[2]);
         }
     }
@@ -102,9 +80,7 @@ __device__ __forceinline__ float eval_density(const GraphView& g, const FieldVie
 }
 
 // Colour only (march.cu:195-219): fills S.C*, S.mmin, S.inv_a for the sample at S.x in S.cell.
-template <int SLOTS>
-__device__ __forceinline__ void eval_color(const GraphView& g, const FieldView& F, const float (&b)[16],
-                                           ColorCache<SLOTS>& cache, Sample& S) {
+__device__ __forceinline__ void eval_color(const GraphView& g, const FieldView& F, const float (&b)[16], Sample& S) {
     const int e0 = __ldg(g.off + S.cell), e1 = __ldg(g.off + S.cell + 1);
     Blend B;
     B.reset();
@@ -115,7 +91,7 @@ __device__ __forceinline__ void eval_color(const GraphView& g, const FieldView& 
         const float4* r = F.rec + kFieldVec * static_cast<int64_t>(j);
         const float4 r2 = __ldg(r + 2), r3 = __ldg(r + 3);
         float c[3];
-        cache.get(F, j, b, c);
+        site_color(F, j, b, c);
         B.add(maha(r2, r3, v0, v1, v2), c[0], c[1], c[2]);
     }
     S.mmin = B.m_min;
@@ -131,10 +107,9 @@ __device__ __forceinline__ void red4(float* p, const float4& v) { atomicAdd(rein
 
 // Gradients of one sample into the gradient pack: gs = dL/dsigma, gC = dL/dC, has_c whether the
 // sample's colour exists (foam.cu:303-343). Four floats per atomic (16-byte vector reductions).
-template <int SLOTS>
 __device__ __forceinline__ void sample_grads(const GraphView& g, const FieldView& F, const Sample& P, float gs,
-                                               float gC0, float gC1, float gC2, bool has_c, const float (&b)[16],
-                                               ColorCache<SLOTS>& cache, float* __restrict__ grad) {
+                                             float gC0, float gC1, float gC2, bool has_c, const float (&b)[16],
+                                             float* __restrict__ grad) {
     const bool do_c = has_c && (gC0 != 0.f || gC1 != 0.f || gC2 != 0.f);
     if (gs == 0.f && !do_c) return;
     const float gCC = gC0 * P.C0 + gC1 * P.C1 + gC2 * P.C2;
@@ -159,7 +134,7 @@ __device__ __forceinline__ void sample_grads(const GraphView& g, const FieldView
             const float a = __expf(-0.5f * (maha(r2, r3, v0, v1, v2) - P.mmin)) * P.inv_a;
             if (a < kMinWeight) continue;
             float c[3];
-            cache.get(F, j, b, c);  // max(SH + 1/2, 0): positive exactly where the unclamped value is
+            site_color(F, j, b, c);  // max(SH + 1/2, 0): positive exactly where the unclamped value is
             const float dc[3] = {c[0] > 0.f ? a * gC0 : 0.f, c[1] > 0.f ? a * gC1 : 0.f, c[2] > 0.f ? a * gC2 : 0.f};
             if (dc[0] != 0.f || dc[1] != 0.f || dc[2] != 0.f) {
 #pragma unroll
@@ -184,89 +159,7 @@ __device__ __forceinline__ void sample_grads(const GraphView& g, const FieldView
     }
 }
 
-// Warp-aggregated variant of sample_grads. The 32 rays of a warp come from one pixel tile, so at a
-// given step several of them sample the same cell and scatter into the same neighbour sites. Lanes
-// are grouped by cell (__match_any_sync); a group of g lanes stages its per-neighbour gradients
-// (16 float4) in shared memory and its members sum them column-wise, so a site receives one set of
-// 16-byte atomics per group instead of one per lane. stage: this warp's 32 x 16 float4 (shared).
 __device__ __forceinline__ bool nonzero(const float4& v) { return v.x != 0.f || v.y != 0.f || v.z != 0.f || v.w != 0.f; }
-
-template <int SLOTS>
-__device__ __forceinline__ void scatter_sample_agg(const GraphView& g, const FieldView& F, const Sample& P, float gs,
-                                                   float gC0, float gC1, float gC2, bool has_c,
-                                                   const float (&b)[16], ColorCache<SLOTS>& cache,
-                                                   float* __restrict__ grad, float4* stage, int lane) {
-    const bool do_c = has_c && (gC0 != 0.f || gC1 != 0.f || gC2 != 0.f);
-    const bool any = gs != 0.f || do_c;
-    const unsigned active = __activemask();
-    const unsigned want = __ballot_sync(active, any);
-    if (!any) return;
-    const unsigned peers = __match_any_sync(want, P.cell);
-    if (__popc(peers) == 1) {
-        sample_grads(g, F, P, gs, gC0, gC1, gC2, has_c, b, cache, grad);
-        return;
-    }
-    const int gsize = __popc(peers);
-    const int rank = __popc(peers & ((1u << lane) - 1u));
-    const float gCC = gC0 * P.C0 + gC1 * P.C1 + gC2 * P.C2;
-    const int e0 = __ldg(g.off + P.cell), e1 = __ldg(g.off + P.cell + 1);
-    float4* row = stage + 16 * lane;
-    for (int e = e0; e < e1; ++e) {  // identical trip count for the whole group (same cell)
-        const float4 E = __ldg(g.edge + e);
-        const int j = site_of(E);
-        const float v0 = P.x0 - E.x, v1 = P.x1 - E.y, v2 = P.x2 - E.z;
-        const float4* r = F.rec + kFieldVec * static_cast<int64_t>(j);
-        float4 d0 = make_float4(0.f, 0.f, 0.f, 0.f), d1 = d0, c0 = d0, c1 = d0;
-        float dc[3] = {0.f, 0.f, 0.f};
-        if (gs != 0.f) {
-            const float4 r0 = __ldg(r), r1 = __ldg(r + 1);
-            const float gc = gs * __expf(r1.z - 0.5f * maha(r0, r1, v0, v1, v2));
-            if (fabsf(gc) > 1e-12f) {
-                const float gm = -0.5f * gc;
-                d0 = make_float4(gc, gm * v0 * v0, 2.f * gm * v0 * v1, 2.f * gm * v0 * v2);
-                d1 = make_float4(gm * v1 * v1, 2.f * gm * v1 * v2, gm * v2 * v2, 0.f);
-            }
-        }
-        if (do_c) {
-            const float4 r2 = __ldg(r + 2), r3 = __ldg(r + 3);
-            const float a = __expf(-0.5f * (maha(r2, r3, v0, v1, v2) - P.mmin)) * P.inv_a;
-            if (a >= kMinWeight) {
-                float c[3];
-                cache.get(F, j, b, c);
-                dc[0] = c[0] > 0.f ? a * gC0 : 0.f, dc[1] = c[1] > 0.f ? a * gC1 : 0.f;
-                dc[2] = c[2] > 0.f ? a * gC2 : 0.f;
-                const float ga = gC0 * c[0] + gC1 * c[1] + gC2 * c[2];
-                const float gm = -0.5f * a * (ga - gCC);
-                c0 = make_float4(gm * v0 * v0, 2.f * gm * v0 * v1, 2.f * gm * v0 * v2, gm * v1 * v1);
-                c1 = make_float4(2.f * gm * v1 * v2, gm * v2 * v2, 0.f, 0.f);
-            }
-        }
-        row[0] = d0, row[1] = d1, row[2] = c0, row[3] = c1;
-#pragma unroll
-        for (int q = 0; q < 12; ++q) {
-            if (q >= F.s4) break;
-            float f[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int i = 4 * q + u;
-                f[u] = i < 48 ? b[i / 3] * dc[i % 3] : 0.f;
-            }
-            row[4 + q] = make_float4(f[0], f[1], f[2], f[3]);
-        }
-        __syncwarp(peers);
-        float* G = grad + kGradStride * static_cast<int64_t>(j);
-        const int cols = 4 + F.s4;
-        for (int q = rank; q < cols; q += gsize) {
-            float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (unsigned m = peers; m; m &= m - 1u) {
-                const float4 v = stage[16 * (__ffs(m) - 1) + q];
-                s.x += v.x, s.y += v.y, s.z += v.z, s.w += v.w;
-            }
-            if (nonzero(s)) red4(G + 4 * q, s);
-        }
-        __syncwarp(peers);
-    }
-}
 
 // ---------------------------------------------------------------------------------- fixed steps
 

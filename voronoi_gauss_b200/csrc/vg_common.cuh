@@ -194,41 +194,6 @@ __device__ __forceinline__ void site_color(const FieldView& F, int k, const floa
     for (int ch = 0; ch < 3; ++ch) c[ch] = fmaxf(c[ch], 0.f);
 }
 
-// Per-thread direct-mapped cache of the clamped site colours in shared memory: a site belongs to the
-// neighbourhoods of several consecutive cells of a ray and its colour depends only on the ray
-// direction. Entry s of thread t lives at base[s * stride + t] as (rgb, site), site -1 when empty.
-// SLOTS = 0: no cache.
-template <int SLOTS>
-struct ColorCache {
-    float4* base;
-    int stride;
-    __device__ __forceinline__ void init() {
-#pragma unroll
-        for (int s = 0; s < SLOTS; ++s) base[s * stride] = make_float4(0.f, 0.f, 0.f, __int_as_float(-1));
-    }
-    __device__ __forceinline__ void get(const FieldView& F, int k, const float (&b)[16], float (&c)[3]) {
-        float4* entry = base + (k & (SLOTS - 1)) * stride;
-        const float4 held = *entry;
-        const bool hit = __float_as_int(held.w) == k;
-        if (!hit) {
-            site_color(F, k, b, c);
-            *entry = make_float4(c[0], c[1], c[2], __int_as_float(k));
-        } else {
-            c[0] = held.x, c[1] = held.y, c[2] = held.z;
-        }
-    }
-};
-
-template <>
-struct ColorCache<0> {
-    float4* base;
-    int stride;
-    __device__ __forceinline__ void init() {}
-    __device__ __forceinline__ void get(const FieldView& F, int k, const float (&b)[16], float (&c)[3]) {
-        site_color(F, k, b, c);
-    }
-};
-
 // ------------------------------------------------------------------------------ host-side launchers
 
 struct RayView {
