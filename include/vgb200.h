@@ -253,6 +253,24 @@ int vg_foam_infer(const float* points, const int32_t* offsets, const int32_t* nb
                   const int32_t* cap, const int32_t* orig, float* rgb, float* T, float* depth, int32_t* stats,
                   void* stream);
 
+/* Workspace of vg_foam_infer_deferred for n_sites sites and n_rays rays. */
+size_t vg_foam_infer_workspace_bytes(int64_t n_sites, int64_t n_rays);
+
+/* foam_infer (foam_infer.cu:376-435) with deferred, cell-major colours: the same arguments as
+ * vg_foam_infer plus a caller-allocated workspace. At stage 2 the samples, densities and weights are
+ * traced per ray without colours; the samples that border a coloured segment are then sorted by cell and
+ * coloured one cell at a time, and composited per ray in order. rgb, T, depth and stats columns 0-3
+ * (samples, coloured segments, walk steps, density terms) are those of vg_foam_infer, bit for bit;
+ * column 4 counts the SH colours evaluated by the cell-major pass for the ray's samples (vg_foam_infer
+ * counts the misses of its per-ray colour cache, as the reference kernel does). Stages 0 and 1 need no
+ * workspace and run as vg_foam_infer. */
+int vg_foam_infer_deferred(const float* points, const int32_t* offsets, const int32_t* nbr, const float* edge,
+                           const float* attr, const void* sh, int sh_half, int sh_deg, int64_t n_sites,
+                           int64_t n_edges, const float* o, const float* d, const int32_t* start, const float* near,
+                           const float* far, int64_t n_rays, float t_thresh, float w_thresh, float color_cut,
+                           int color_mode, int stage, const int32_t* cap, const int32_t* orig, float* rgb, float* T,
+                           float* depth, int32_t* stats, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------------ kernel timing */
 
 /* Measurement aid with no counterpart in the reference (whose benchmarks time whole extension calls).
@@ -267,9 +285,10 @@ enum {
     VG_PROF_COLOR = 1,       /* cell-major colour pass of vg_foam_forward */
     VG_PROF_REPLAY = 2,      /* record replay of vg_foam_backward (writes the scatter's items) */
     VG_PROF_SCATTER = 3,     /* cell-major gradient scatter (foam, march and field backwards) */
-    VG_PROF_INFER = 4,       /* vg_foam_infer */
+    VG_PROF_INFER = 4,       /* per-ray traversal of vg_foam_infer / vg_foam_infer_deferred */
     VG_PROF_MARCH_FWD = 5,   /* vg_march_forward */
-    VG_PROF_MARCH_ITEMS = 6  /* re-march of vg_march_backward writing the scatter's items */
+    VG_PROF_MARCH_ITEMS = 6, /* re-march of vg_march_backward writing the scatter's items */
+    VG_PROF_INFER_COLOR = 7  /* cell-major colour pass of vg_foam_infer_deferred */
 };
 int vg_prof_enable(int on);
 int vg_prof_read(int kernel, double* total_ms, int64_t* launches);

@@ -147,11 +147,16 @@ def test_foam_infer_against_reference_kernel(foam_small, tag):
         for stage in (0, 1, 2):
             args = (*p, shp, 3, x['o'], x['d'], cuda(start.astype(np.int32)), x['near'], x['far'], 0.0, -1.0, cut,
                     mode, stage, cap, orig)
-            mine = ext.foam_infer_extension().foam_infer(*args)
+            mine = ext.foam_infer_extension().foam_infer(*args, exact_stats=True)
             theirs = ri.foam_infer(*args)
             assert torch.equal(mine[3], theirs[3]), (mode, stage)
             for a, b in zip(mine[:3], theirs[:3]):
                 assert float((a - b).abs().max()) <= IMG_TOL
+            # deferred colours (the default): the same image bit for bit, stats columns 0-3 equal
+            deferred = ext.foam_infer_extension().foam_infer(*args)
+            assert torch.equal(deferred[3][:, :4], theirs[3][:, :4]), (mode, stage)
+            for a, b in zip(deferred[:3], mine[:3]):
+                assert torch.equal(a, b), (mode, stage)
 
 
 def test_conic_against_reference_kernel():
@@ -180,12 +185,15 @@ def _mixture_scene():
     return gr, model
 
 
-@pytest.mark.parametrize('tag', ['fused_fp16_eps_morton', 'exact_fp32'])
+@pytest.mark.parametrize('tag', ['fused_fp16_eps_morton', 'exact_fp32', 'exact_fp32_all_coloured'])
 def test_foam_infer_config2_scene_against_reference_kernel(tag):
     """foam_infer on BASELINE config 2's 1M-site scene, the 200 x 200 centre crop of an 800 x 800 view of
     orbit camera 0 (fov 50), in the reference's fast configuration (fused colours, fp16 SH, eps 1e-4,
-    Morton order) and in exact fp32: per-ray stats equal (samples, coloured segments, walk steps, density
-    terms, SH evaluations) and images within 1e-4."""
+    Morton order), in exact fp32, and in exact fp32 with every segment coloured (w_thresh -1, t_thresh 0:
+    long rays that overflow the deferred pipeline's per-ray slots and are rendered per ray). Per ray
+    (exact_stats): stats equal to the reference kernel's (samples, coloured segments, walk steps, density
+    terms, SH evaluations) and images within 1e-4. Deferred colours (the default): the per-ray image bit
+    for bit and stats columns 0-3 equal."""
     ri = ref('vgf_foam_infer')
     from voronoi_gauss_b200 import render, scenes, sites
     gr, model = _mixture_scene()
@@ -196,7 +204,7 @@ def test_foam_infer_config2_scene_against_reference_kernel(tag):
     o, d = o[crop].cuda().contiguous(), d[crop].cuda().contiguous()
     start = torch.full((len(o),), int(sites.nearest_sites(gr['points'], centre[None])[0]), dtype=torch.int32,
                        device='cuda')
-    if tag == 'exact_fp32':
+    if tag.startswith('exact_fp32'):
         pack, kw = render.pack_foam(model), dict(colors='exact', eps_color=0.0)
     else:
         pack = render.pack_foam(model, sh_half=True, eps_density=1e-4, reorder=True)
@@ -206,14 +214,21 @@ def test_foam_infer_config2_scene_against_reference_kernel(tag):
     near, _, far = render.ray_bounds(o, d, 0.02, 4.0)
     s = pack['inv'][start.long()].int() if pack['inv'] is not None else start
     cap = torch.empty(0, dtype=torch.int32, device='cuda')
-    args = (*(pack[k] for k in ('points', 'offsets', 'nbr', 'edge', 'attr', 'sh')), 3, o, d, s, near, far, 1e-4,
-            1e-4, float(cut), mode, 2, cap, pack['orig'])
-    mine = _ext().foam_infer_extension().foam_infer(*args)
+    t_thresh, w_thresh = (0.0, -1.0) if tag.endswith('all_coloured') else (1e-4, 1e-4)
+    args = (*(pack[k] for k in ('points', 'offsets', 'nbr', 'edge', 'attr', 'sh')), 3, o, d, s, near, far, t_thresh,
+            w_thresh, float(cut), mode, 2, cap, pack['orig'])
+    mine = _ext().foam_infer_extension().foam_infer(*args, exact_stats=True)
     theirs = ri.foam_infer(*args)
     assert torch.equal(mine[3], theirs[3]), 'per-ray stats differ from the reference kernel'
     for a, b in zip(mine[:3], theirs[:3]):
         assert float((a - b).abs().max()) <= IMG_TOL
     assert float(mine[3][:, 0].double().mean()) > 2  # the crop looks into the scene
+    deferred = _ext().foam_infer_extension().foam_infer(*args)
+    assert torch.equal(deferred[3][:, :4], theirs[3][:, :4])
+    for a, b in zip(deferred[:3], mine[:3]):
+        assert torch.equal(a, b), 'deferred colours changed the image'
+    if tag.endswith('all_coloured'):
+        assert int((mine[3][:, 0] > 97).sum()) > 100  # rays beyond the deferred pipeline's slots
 
 
 def test_march_config5_scene_against_reference_kernels():

@@ -61,12 +61,16 @@ SIGNATURES = {
     'vg_nearest_sites': (I32, [P, I64, I64, P, I64, P, P]),
     'vg_foam_infer': (I32, [P, P, P, P, P, P, I32, I32, I64, I64, P, P, P, P, P, I64, F32, F32, F32, I32, I32, P, P, P,
                             P, P, P, P]),
+    'vg_foam_infer_workspace_bytes': (SZ, [I64, I64]),
+    'vg_foam_infer_deferred': (I32, [P, P, P, P, P, P, I32, I32, I64, I64, P, P, P, P, P, I64, F32, F32, F32, I32, I32,
+                                     P, P, P, P, P, P, P, SZ, P]),
     'vg_prof_enable': (I32, [I32]),
     'vg_prof_read': (I32, [I32, P, P]),
 }
 
 # kernel classes of vg_prof_read (VG_PROF_* of include/vgb200.h)
-PROF = {'traversal': 0, 'color': 1, 'replay': 2, 'scatter': 3, 'infer': 4, 'march_fwd': 5, 'march_items': 6}
+PROF = {'traversal': 0, 'color': 1, 'replay': 2, 'scatter': 3, 'infer': 4, 'march_fwd': 5, 'march_items': 6,
+        'infer_color': 7}
 
 
 def prof_enable(on):

@@ -540,12 +540,12 @@ int vg_nearest_sites(const void* pack, int64_t n_sites, int64_t n_adj, const flo
     return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_nearest_sites");
 }
 
-int vg_foam_infer(const float* points, const int32_t* offsets, const int32_t* nbr, const float* edge,
-                  const float* attr, const void* sh, int sh_half, int sh_deg, int64_t n_sites, int64_t n_edges,
-                  const float* o, const float* d, const int32_t* start, const float* near, const float* far,
-                  int64_t n_rays, float t_thresh, float w_thresh, float color_cut, int color_mode, int stage,
-                  const int32_t* cap, const int32_t* orig, float* rgb, float* T, float* depth, int32_t* stats,
-                  void* stream) {
+namespace {
+
+int infer_args(const float* points, const int32_t* offsets, const int32_t* nbr, const float* edge, const float* attr,
+               const void* sh, int sh_deg, int64_t n_sites, int64_t n_edges, const float* o, const float* d,
+               const int32_t* start, const float* near, const float* far, int64_t n_rays, int color_mode, int stage,
+               float* rgb, float* T, float* depth, int32_t* stats) {
     REQUIRE(points && offsets && nbr && edge && attr, "pack arrays must be non-null");
     REQUIRE(n_sites > 0 && n_sites < INT32_MAX && n_edges >= n_sites && n_edges < INT32_MAX, "bad pack sizes");
     REQUIRE(color_mode >= 0 && color_mode <= 2, "color_mode must be 0 (lazy), 1 (baked) or 2 (fused)");
@@ -557,6 +557,20 @@ int vg_foam_infer(const float* points, const int32_t* offsets, const int32_t* nb
     int rc = check_rays(n_rays, o, d, start, near, far);
     if (rc) return rc;
     REQUIRE(n_rays == 0 || (rgb && T && depth && stats), "outputs must be non-null");
+    return VG_OK;
+}
+
+}  // namespace
+
+int vg_foam_infer(const float* points, const int32_t* offsets, const int32_t* nbr, const float* edge,
+                  const float* attr, const void* sh, int sh_half, int sh_deg, int64_t n_sites, int64_t n_edges,
+                  const float* o, const float* d, const int32_t* start, const float* near, const float* far,
+                  int64_t n_rays, float t_thresh, float w_thresh, float color_cut, int color_mode, int stage,
+                  const int32_t* cap, const int32_t* orig, float* rgb, float* T, float* depth, int32_t* stats,
+                  void* stream) {
+    int rc = infer_args(points, offsets, nbr, edge, attr, sh, sh_deg, n_sites, n_edges, o, d, start, near, far, n_rays,
+                        color_mode, stage, rgb, T, depth, stats);
+    if (rc) return rc;
     if (n_rays == 0) return VG_OK;
     int* status = status_ptr();
     if (status == nullptr) return fail(VG_ERR_CUDA, "status word unavailable");
@@ -567,6 +581,37 @@ int vg_foam_infer(const float* points, const int32_t* offsets, const int32_t* nb
     const vg::Outputs out{rgb, T, depth, stats, nullptr};
     const cudaError_t e = vg::foam_infer(N, c, R, out, status, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_foam_infer");
+}
+
+size_t vg_foam_infer_workspace_bytes(int64_t n_sites, int64_t n_rays) {
+    if (n_sites <= 0 || n_sites >= INT32_MAX || n_rays < 0) return 0;
+    return vg::foam_infer_workspace(n_sites, n_rays);
+}
+
+int vg_foam_infer_deferred(const float* points, const int32_t* offsets, const int32_t* nbr, const float* edge,
+                           const float* attr, const void* sh, int sh_half, int sh_deg, int64_t n_sites,
+                           int64_t n_edges, const float* o, const float* d, const int32_t* start, const float* near,
+                           const float* far, int64_t n_rays, float t_thresh, float w_thresh, float color_cut,
+                           int color_mode, int stage, const int32_t* cap, const int32_t* orig, float* rgb, float* T,
+                           float* depth, int32_t* stats, void* workspace, size_t workspace_bytes, void* stream) {
+    int rc = infer_args(points, offsets, nbr, edge, attr, sh, sh_deg, n_sites, n_edges, o, d, start, near, far, n_rays,
+                        color_mode, stage, rgb, T, depth, stats);
+    if (rc) return rc;
+    if (n_rays == 0) return VG_OK;
+    REQUIRE(aligned(workspace, 256), "workspace must be 256-byte aligned");
+    const size_t need = stage == 2 ? vg::foam_infer_workspace(n_sites, n_rays) : 0;
+    if (need > 0 && (workspace == nullptr || workspace_bytes < need))
+        return fail(VG_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);
+    int* status = status_ptr();
+    if (status == nullptr) return fail(VG_ERR_CUDA, "status word unavailable");
+    const vg::InferNet N{reinterpret_cast<const float4*>(points), offsets, nbr, reinterpret_cast<const float4*>(edge),
+                         reinterpret_cast<const float4*>(attr), sh, orig, sh_half};
+    const vg::InferCfg c{t_thresh, w_thresh, color_cut, sh_deg, color_mode, stage, cap};
+    const vg::RayView R{o, d, start, near, nullptr, far, n_rays};
+    const vg::Outputs out{rgb, T, depth, stats, nullptr};
+    const cudaError_t e = vg::foam_infer_deferred(N, n_sites, c, R, out, status, workspace, workspace_bytes,
+                                                  static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_foam_infer_deferred");
 }
 
 }  // extern "C"

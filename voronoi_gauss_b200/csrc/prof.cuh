@@ -14,10 +14,11 @@ enum ProfKernel {
     kProfColor = 1,       // cmf_color_kernel: cell-major colours
     kProfReplay = 2,      // foam_backward_kernel<items>: record replay writing the scatter's items
     kProfScatter = 3,     // cm_scatter_kernel: cell-major gradient scatter
-    kProfInfer = 4,       // infer_kernel: inference renderer
+    kProfInfer = 4,       // infer_kernel / trace_kernel: inference traversal (per ray)
     kProfMarchFwd = 5,    // march_forward_kernel
     kProfMarchItems = 6,  // march_items_kernel: march backward re-march writing items
-    kProfKernels = 7
+    kProfInferColour = 7, // colour_kernel of the deferred inference pipeline
+    kProfKernels = 8
 };
 
 int prof_begin(int kernel, cudaStream_t st);  // slot of the event pair, or -1 when not recording

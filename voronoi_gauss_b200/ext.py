@@ -413,11 +413,16 @@ class FieldExtension:
 
 
 class FoamInferExtension:
-    """foam_infer with the reference's signature (foam_infer.cu:376-435)."""
+    """foam_infer with the reference's signature (foam_infer.cu:376-435).
+
+    At stage 2 the colours are deferred to a cell-major pass (vg_foam_infer_deferred): the same rgb, T,
+    depth and stats columns 0-3 bit for bit, with stats column 4 counting the SH colours that pass
+    evaluated. exact_stats=True renders per ray instead (vg_foam_infer), whose column 4 counts the misses
+    of a per-ray colour cache like the reference kernel's."""
 
     @staticmethod
     def foam_infer(points, offsets, nbr, edge, attr, sh, sh_deg, o, d, start, near, far, t_thresh, w_thresh,
-                   color_cut, color_mode, stage, cap, orig):
+                   color_cut, color_mode, stage, cap, orig, exact_stats=False):
         for x, name, dt in ((points, 'points', torch.float32), (offsets, 'offsets', torch.int32),
                             (nbr, 'nbr', torch.int32), (edge, 'edge', torch.float32), (attr, 'attr', torch.float32),
                             (cap, 'cap', torch.int32), (orig, 'orig', torch.int32)):
@@ -452,13 +457,19 @@ class FoamInferExtension:
         stats = torch.empty(B, 5, dtype=torch.int32, device=dev)
         if B == 0:
             return [rgb, T, depth, stats]
+        args = [points.data_ptr(), offsets.data_ptr(), nbr.data_ptr(), edge.data_ptr(), attr.data_ptr(),
+                None if baked else _ptr(sh), int(half), _sh_deg(sh_deg), n, nbr.numel(), o.data_ptr(), d.data_ptr(),
+                start.data_ptr(), near.data_ptr(), far.data_ptr(), B, float(t_thresh), float(w_thresh),
+                float(color_cut), color_mode, stage, _ptr(cap) if cap.numel() == B else None,
+                _ptr(orig) if orig.numel() == n else None, rgb.data_ptr(), T.data_ptr(), depth.data_ptr(),
+                stats.data_ptr()]
         with torch.cuda.device(dev):
-            _lib.call('vg_foam_infer', points.data_ptr(), offsets.data_ptr(), nbr.data_ptr(), edge.data_ptr(),
-                      attr.data_ptr(), None if baked else _ptr(sh), int(half), _sh_deg(sh_deg), n, nbr.numel(),
-                      o.data_ptr(), d.data_ptr(), start.data_ptr(), near.data_ptr(), far.data_ptr(), B,
-                      float(t_thresh), float(w_thresh), float(color_cut), color_mode, stage,
-                      _ptr(cap) if cap.numel() == B else None, _ptr(orig) if orig.numel() == n else None,
-                      rgb.data_ptr(), T.data_ptr(), depth.data_ptr(), stats.data_ptr(), _stream(dev))
+            if stage == 2 and not exact_stats:
+                nbytes = _lib.lib().vg_foam_infer_workspace_bytes(n, B)
+                ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
+                _lib.call('vg_foam_infer_deferred', *args, ws.data_ptr(), nbytes, _stream(dev))
+            else:
+                _lib.call('vg_foam_infer', *args, _stream(dev))
         return [rgb, T, depth, stats]
 
 

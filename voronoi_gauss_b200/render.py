@@ -289,11 +289,13 @@ def bake_colors(model, pack, center):
 
 @torch.no_grad()
 def render_rays_foam_infer(model, pack, o, d, start, near=0.02, far_radius=4.0, t_thresh=1e-4, w_thresh=1e-4,
-                           colors='exact', eps_color=0.0, stage=2, cap=None):
+                           colors='exact', eps_color=0.0, stage=2, cap=None, exact_stats=False):
     """Inference version of render_rays_foam (render.py:238-257): colors 'exact' (lazy second pass for the
     segments with weight > w_thresh), 'fused' (blended in the density pass) or 'baked' (bake_colors), the
     neighbours below eps_color of the normalised colour weight skipped. Per-ray stats (B, 5): samples,
-    coloured segments, walk steps, density Gaussians evaluated, SH evaluated."""
+    coloured segments, walk steps, density Gaussians evaluated, SH evaluated (colours are deferred to a
+    cell-major pass, whose SH count is reported; exact_stats=True renders per ray with the reference's
+    per-ray colour cache and its SH count, same image)."""
     mode = {'exact': 0, 'baked': 1, 'fused': 2}[colors]
     t_near, _, t_far = ray_bounds(o, d, near, far_radius)
     if cap is None:
@@ -308,7 +310,8 @@ def render_rays_foam_infer(model, pack, o, d, start, near=0.02, far_radius=4.0, 
             t_far.contiguous()]
     fg, T, depth, stats = ext.foam_infer_extension().foam_infer(*layout, model.sh_deg, *rays, float(t_thresh),
                                                                 float(w_thresh), skip_beyond, mode, int(stage),
-                                                                cap.int().contiguous(), pack['orig'])
+                                                                cap.int().contiguous(), pack['orig'],
+                                                                exact_stats=exact_stats)
     return {'rgb': _over_background(model, fg, T), 'acc': 1.0 - T, 'depth': depth, 'stats': stats}
 
 
