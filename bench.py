@@ -109,6 +109,27 @@ def load_scene(cfg, n_sites, rank, poll_s=2.0, wait_s=3600.0):
     return scenes.build_graph(cfg, n=n)
 
 
+POOL_VIEWS = 8  # orbit views of the training workload's pool (dist.pool_tile_pixels)
+
+
+def pool_rays(cfg, gr, W, H, rank):
+    """The training workload's rays for `rank`: of each of POOL_VIEWS orbit views (radius 3), the 16x16
+    tiles t = rank + v mod POOL_VIEWS, i.e. one W x H frame's worth of rays drawn evenly from the pool, the
+    same share at every world size. -> o, d (B, 3), start (B) int32 (each view's nearest site to its
+    camera), on the host."""
+    from voronoi_gauss_b200 import dist as vdist
+    from voronoi_gauss_b200 import scenes, sites
+    o_l, d_l, s_l = [], [], []
+    for v, pix in enumerate(vdist.pool_tile_pixels(H, W, rank, POOL_VIEWS)):
+        centre, c2w = scenes.orbit_camera(v, POOL_VIEWS)
+        o_v, d_v = scenes.camera_rays(centre, c2w, W, H, scenes.CONFIGS[cfg]['fov'])
+        pix = torch.from_numpy(pix)
+        o_l.append(o_v[pix]), d_l.append(d_v[pix])
+        s_l.append(torch.full((len(pix),), int(sites.nearest_sites(gr['points'], centre[None])[0]),
+                              dtype=torch.int32))
+    return torch.cat(o_l).contiguous(), torch.cat(d_l).contiguous(), torch.cat(s_l).contiguous()
+
+
 def camera(cfg, view, W, H, n_views=8):
     """Orbit camera `view` of n_views; rays in 4x8 pixel-tile order on the host."""
     from voronoi_gauss_b200 import scenes
@@ -335,25 +356,13 @@ def run_training(args):
         o_v, d_v = scenes.camera_rays(centre, c2w, W, H, cfgd['fov'])
         pix = torch.from_numpy(vdist.tile_pixels(H, W, world, rank))
         o_h, d_h = o_v[pix].contiguous(), d_v[pix].contiguous()
-        start_site = int(sites.nearest_sites(gr['points'], centre[None])[0])
-        start_h = torch.full((len(o_h),), start_site, dtype=torch.int32)
-    elif world == 1:
-        centre, o_h, d_h = camera(args.config, 0, W, H)
-        start_site = int(sites.nearest_sites(gr['points'], centre[None])[0])
-        start_h = torch.full((len(o_h),), start_site, dtype=torch.int32)
+        start_h = torch.full((len(o_h),), int(sites.nearest_sites(gr['points'], centre[None])[0]),
+                             dtype=torch.int32)
     else:
-        # N views, 16x16 tiles of each dealt round-robin over the ranks (dist.view_tile_pixels): every rank
-        # renders one view's worth of rays from the same mix of views
-        o_l, d_l, s_l = [], [], []
-        for v, pix in enumerate(vdist.view_tile_pixels(H, W, world, rank)):
-            centre, c2w = scenes.orbit_camera(v, 8)
-            o_v, d_v = scenes.camera_rays(centre, c2w, W, H, cfgd['fov'])
-            pix = torch.from_numpy(pix)
-            o_l.append(o_v[pix]), d_l.append(d_v[pix])
-            s_l.append(torch.full((len(pix),), int(sites.nearest_sites(gr['points'], centre[None])[0]),
-                                  dtype=torch.int32))
-        o_h, d_h, start_h = torch.cat(o_l).contiguous(), torch.cat(d_l).contiguous(), torch.cat(s_l)
-        start_site = int(start_h[0])
+        # one frame's worth of rays per GPU from a fixed pool of views: the same share at every world size
+        if world > POOL_VIEWS:
+            raise SystemExit(f'--gpus {world}: the weak-scaling workload deals a pool of {POOL_VIEWS} views')
+        o_h, d_h, start_h = pool_rays(args.config, gr, W, H, rank)
     B = len(o_h)
     gen = torch.Generator().manual_seed(0)
     target_h = torch.rand(B, 3, generator=gen)
@@ -491,10 +500,12 @@ def run_training(args):
         'data': 'synthetic',
         'config': {'workload': f'config{args.config}: {len(gr["points"])} sites ({cfgd["kind"]}), SH deg '
                                f'{model.sh_deg}, {W}x{H} rays per GPU, training step (fwd+bwd+Adam), record_cap '
-                               f'{RECORD_CAP}, t/w_thresh {T_THRESH:g}',
+                               f'{RECORD_CAP}, t/w_thresh {T_THRESH:g}' + ('' if args.strong else
+                               f'; each GPU renders the 16x16 tiles t = rank + v mod {POOL_VIEWS} of orbit views '
+                               f'v = 0..{POOL_VIEWS - 1} (one {W}x{H} frame of rays, the same share at every N)'),
                    'rays_per_gpu': B, 'sites': len(gr['points']),
-                   'parallelism': f'dp{world} (16x16 tiles of {world} views dealt over the GPUs, NCCL all-reduce of '
-                                  'site gradients)' if world > 1 else 'single GPU',
+                   'parallelism': f'dp{world} (each GPU its own share of the view pool, NCCL all-reduce of site '
+                                  'gradients)' if world > 1 else 'single GPU',
                    'l2': 'inputs larger than L2 (scene records + adjacency ~1 GB read every step)'},
         'fps': round(1000.0 / ms, 3), 'samples_per_ray': round(samples_per_ray, 2),
         'roofline': roofline(ktimes, nbytes, args.steps, peak, peak_kind, training_unit_counts(units),
@@ -516,7 +527,7 @@ def run_training(args):
         line['config']['library'] = {'path': _lib.LIB_PATH, 'defines': open(knobs).read().split()
                                      if os.path.exists(knobs) else []}
     if rank == 0 and world == 1 and not args.no_baselines:
-        line['cpu_baseline'] = cpu_baseline(gr, prm, o_h, d_h, start_site, args)
+        line['cpu_baseline'] = cpu_baseline(gr, prm, o_h, d_h, start_h, args)
         line['ref_cuda'] = ref_cuda_training(model, o, d, start, args)
     if world > 1:
         dist.destroy_process_group()
@@ -566,7 +577,7 @@ def ref_cuda_training(model, o, d, start, args):
                 'fwd_bwd_mrays_s': round(B / ((f_ms + b_ms) * 1e-3) / 1e6, 3)}
 
 
-def cpu_baseline(gr, prm, o_h, d_h, start_site, args, seconds=10.0, max_chunks=64):
+def cpu_baseline(gr, prm, o_h, d_h, start_h, args, seconds=10.0, max_chunks=64):
     """The CPU restatement of the path (oracle/, all host threads) on a bounded sample of the workload:
     chunks of rays drawn without replacement from the view (seeded), each timed through the forward with
     records and the backward, until `seconds` of CPU work have been spent (or `max_chunks` chunks); host
@@ -585,7 +596,7 @@ def cpu_baseline(gr, prm, o_h, d_h, start_site, args, seconds=10.0, max_chunks=6
         sel = torch.sort(order[k * chunk:(k + 1) * chunk])[0]
         o, d = o_h[sel].contiguous(), d_h[sel].contiguous()
         near, _, far = render.ray_bounds(o, d, 0.02, 4.0)
-        start = np.full(chunk, start_site, np.int32)
+        start = start_h[sel].numpy()
         a = (gr['points'], gr['offsets'], gr['adj'], prm['raw'], dA, cA, prm['sh'], prm['sh_deg'], o, d, start, near,
              far, T_THRESH, W_THRESH)
         t0 = time.time()
@@ -876,8 +887,7 @@ def run_reference(args):
     H = args.height or cfgd['H']
     gr = load_scene(args.config, args.sites, 0)
     prm = scenes.make_params(args.config, gr['points'].astype(np.float64))
-    centre, o_h, d_h = camera(args.config, 0, W, H)
-    start_site = int(sites.nearest_sites(gr['points'], centre[None])[0])
+    o_h, d_h, start_h = pool_rays(args.config, gr, W, H, 0)
     # the site-parallel part of a step (conics of both Gaussians and their backward) runs once per full
     # view: timed once here and charged to each sample by its share of the view's rays
     t0 = time.time()
@@ -896,7 +906,7 @@ def run_reference(args):
         sel = torch.from_numpy(np.sort(rng.choice(B, n_rays, replace=False)))
         o, d = o_h[sel].contiguous(), d_h[sel].contiguous()
         near, _, far = render.ray_bounds(o, d, 0.02, 4.0)
-        start = np.full(n_rays, start_site, np.int32)
+        start = start_h[sel].numpy()
         a = (gr['points'], gr['offsets'], gr['adj'], prm['raw'], dA, cA, prm['sh'], prm['sh_deg'], o, d, start, near,
              far, T_THRESH, W_THRESH)
         t0 = time.time()

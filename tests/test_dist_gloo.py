@@ -104,17 +104,22 @@ def test_tile_pixels_partition_image():
         assert max(sizes) - min(sizes) <= 2 * 16 * 16  # at most two tiles apart (ragged edge tiles)
 
 
-def test_view_tile_pixels_cover_every_view_once():
+def test_pool_tile_pixels_cover_every_view_once():
     from voronoi_gauss_b200 import dist as vdist
     H, W = 70, 90
-    for world in (1, 2, 4, 8):
-        per_rank = [vdist.view_tile_pixels(H, W, world, r) for r in range(world)]
-        for v in range(world):
-            allp = np.concatenate([per_rank[r][v] for r in range(world)])
-            assert len(allp) == H * W and len(np.unique(allp)) == H * W
-        sizes = [sum(len(p) for p in views) for views in per_rank]
-        # every rank renders about one view's worth of rays
-        assert max(sizes) - min(sizes) <= 2 * world * 16 * 16 and abs(sum(sizes) - world * H * W) == 0
+    views = 8
+    per_rank = [vdist.pool_tile_pixels(H, W, r, views) for r in range(views)]
+    for v in range(views):
+        allp = np.concatenate([per_rank[r][v] for r in range(views)])
+        assert len(allp) == H * W and len(np.unique(allp)) == H * W
+    sizes = [sum(len(p) for p in vs) for vs in per_rank]
+    # every rank renders about one view's worth of rays, from all the views
+    assert max(sizes) - min(sizes) <= 2 * views * 16 * 16 and sum(sizes) == views * H * W
+    assert all(len(p) > 0 for p in per_rank[0])
+    # a rank's share does not depend on the world size
+    assert all(np.array_equal(a, b) for a, b in zip(per_rank[1], vdist.pool_tile_pixels(H, W, 1, views)))
+    with pytest.raises(ValueError):
+        vdist.pool_tile_pixels(H, W, views, views)
 
 
 def _scene_worker(rank, world, port, q):

@@ -1,7 +1,8 @@
 """Data-parallel rendering and training across the GPUs of one node (one process per GPU).
 
 Rays are independent, so rendering shards with no data-path communication: an image is cut into 16x16
-pixel tiles dealt round-robin to the ranks (``tile_pixels``), or every rank renders its own view. The
+pixel tiles dealt round-robin to the ranks (``tile_pixels``), or every rank renders its own share of the
+tiles of a pool of views (``pool_tile_pixels``). The
 scene (sites, adjacency, parameters) is replicated on every GPU (``broadcast_scene`` at load time), and
 ``gather_image`` assembles a tile-sharded frame for output. The one exchange step is in training:
 the per-site gradients of all ranks are summed before the (replicated) optimizer step, by asynchronous
@@ -38,12 +39,15 @@ def tile_pixels(H, W, world, rank, tile=TILE):
     return np.concatenate(out) if out else np.zeros(0, np.int64)
 
 
-def view_tile_pixels(H, W, world, rank, tile=TILE):
-    """Weak-scaling deal of `world` views over `world` ranks: the 16x16 tiles of view v go to the ranks
-    as by ``tile_pixels`` shifted by v (rank r takes the tiles t of view v with t = r - v mod world), so
-    every rank renders one view's worth of rays from the same mix of views. Returns one pixel-index
-    array per view."""
-    return [tile_pixels(H, W, world, (rank - v) % world, tile) for v in range(world)]
+def pool_tile_pixels(H, W, rank, views=8, tile=TILE):
+    """Weak-scaling deal over a fixed pool of `views` camera views: rank r renders, of every view v, the
+    16x16 tiles t with t = r + v mod views (``tile_pixels`` with `views` parts), i.e. one view's worth of
+    rays drawn evenly from all the views. A rank's share does not depend on how many ranks run (up to
+    `views`), so adding ranks adds work without changing any rank's mix. Returns one pixel-index array
+    per view."""
+    if not 0 <= rank < views:
+        raise ValueError(f'rank {rank} outside the pool of {views} views')
+    return [tile_pixels(H, W, views, (rank + v) % views, tile) for v in range(views)]
 
 
 def allreduce_grads(params, group=None):
