@@ -253,8 +253,8 @@ int vg_foam_infer(const float* points, const int32_t* offsets, const int32_t* nb
                   const int32_t* cap, const int32_t* orig, float* rgb, float* T, float* depth, int32_t* stats,
                   void* stream);
 
-/* Workspace of vg_foam_infer_deferred for n_sites sites and n_rays rays. */
-size_t vg_foam_infer_workspace_bytes(int64_t n_sites, int64_t n_rays);
+/* Workspace of vg_foam_infer_deferred for n_sites sites, n_edges records of the layout and n_rays rays. */
+size_t vg_foam_infer_workspace_bytes(int64_t n_sites, int64_t n_edges, int64_t n_rays);
 
 /* foam_infer (foam_infer.cu:376-435) with deferred, cell-major colours: the same arguments as
  * vg_foam_infer plus a caller-allocated workspace. At stage 2 the samples, densities and weights are

@@ -583,9 +583,9 @@ int vg_foam_infer(const float* points, const int32_t* offsets, const int32_t* nb
     return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_foam_infer");
 }
 
-size_t vg_foam_infer_workspace_bytes(int64_t n_sites, int64_t n_rays) {
-    if (n_sites <= 0 || n_sites >= INT32_MAX || n_rays < 0) return 0;
-    return vg::foam_infer_workspace(n_sites, n_rays);
+size_t vg_foam_infer_workspace_bytes(int64_t n_sites, int64_t n_edges, int64_t n_rays) {
+    if (n_sites <= 0 || n_sites >= INT32_MAX || n_edges < n_sites || n_edges >= INT32_MAX || n_rays < 0) return 0;
+    return vg::foam_infer_workspace(n_sites, n_edges, n_rays);
 }
 
 int vg_foam_infer_deferred(const float* points, const int32_t* offsets, const int32_t* nbr, const float* edge,
@@ -599,7 +599,7 @@ int vg_foam_infer_deferred(const float* points, const int32_t* offsets, const in
     if (rc) return rc;
     if (n_rays == 0) return VG_OK;
     REQUIRE(aligned(workspace, 256), "workspace must be 256-byte aligned");
-    const size_t need = stage == 2 ? vg::foam_infer_workspace(n_sites, n_rays) : 0;
+    const size_t need = stage == 2 ? vg::foam_infer_workspace(n_sites, n_edges, n_rays) : 0;
     if (need > 0 && (workspace == nullptr || workspace_bytes < need))
         return fail(VG_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);
     int* status = status_ptr();
@@ -609,7 +609,7 @@ int vg_foam_infer_deferred(const float* points, const int32_t* offsets, const in
     const vg::InferCfg c{t_thresh, w_thresh, color_cut, sh_deg, color_mode, stage, cap};
     const vg::RayView R{o, d, start, near, nullptr, far, n_rays};
     const vg::Outputs out{rgb, T, depth, stats, nullptr};
-    const cudaError_t e = vg::foam_infer_deferred(N, n_sites, c, R, out, status, workspace, workspace_bytes,
+    const cudaError_t e = vg::foam_infer_deferred(N, n_sites, n_edges, c, R, out, status, workspace, workspace_bytes,
                                                   static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_foam_infer_deferred");
 }

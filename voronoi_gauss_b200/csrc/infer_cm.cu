@@ -36,6 +36,54 @@ namespace {
 constexpr int kKept = 96;                          // kept samples per ray
 constexpr int64_t kPassSlots = int64_t(1) << 26;   // kept-sample slots per pass of rays
 constexpr int kChunkSamples = 64;                  // samples of one cell per warp in the colour pass
+#ifndef VG_TRACE_MINB
+#define VG_TRACE_MINB 8
+#endif
+constexpr int kTraceMinBlocks = VG_TRACE_MINB;     // resident blocks of the trace per SM (its register budget)
+
+// The trace's per-edge records, built once per call from the layout: edge e of cell c's run as three
+// float4 = (p_j, half2(r2_j, lam_j)) | density conic (xx, xy, xz, yy) of site j | (yz, zz, min(raw_j, 30),
+// bits(j)), i.e. the edge record followed by the rows attr[j, 0:8] with the site id in the unused slot.
+// A cell's neighbourhood is then one contiguous run of 48-byte records, and the density terms need no
+// gather through the site ids.
+__global__ void __launch_bounds__(kThreads)
+    trace_records_kernel(Layout L, int64_t n_edges, float4* __restrict__ recs) {
+    const int64_t e = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+    if (e >= n_edges) return;
+    const int k = L.site(static_cast<int>(e));
+    const float4* row = L.rows(k);
+    const float4 b = __ldg(row + 1);
+    recs[3 * e] = L.record(static_cast<int>(e));
+    recs[3 * e + 1] = __ldg(row);
+    recs[3 * e + 2] = make_float4(b.x, b.y, b.z, __int_as_float(k));
+}
+
+// The exit face and density of the sample at o + t d in cell c from the trace records: the arithmetic,
+// neighbour order and skips of scan_cell<1> (infer_core.cuh), so both give the same samples and weights.
+__device__ __forceinline__ void trace_scan(const Layout& L, const float4* __restrict__ recs, int c, float t,
+                                           const float (&o)[3], const float (&d)[3], bool find_exit, CellScan& S,
+                                           int& n_dens) {
+    const int e0 = L.first(c), e1 = L.end(c);
+    const float4 pc = __ldg(recs + 3 * static_cast<int64_t>(e0));  // the self-first run starts with the site
+    const float x0 = along(o[0], t, d[0]), x1 = along(o[1], t, d[1]), x2 = along(o[2], t, d[2]);
+    S.sigma = 0.f, S.t_exit = kInf, S.next = INT_MAX;
+#pragma unroll kScanUnroll
+    for (int e = e0; e < e1; ++e) {
+        const float4* q = recs + 3 * static_cast<int64_t>(e);
+        const float4 rec = __ldg(q), ca = __ldg(q + 1), cb = __ldg(q + 2);
+        const int k = __float_as_int(cb.w);
+        float tc;
+        if (find_exit && e != e0 && face_crossing(rec, pc, o, d, tc) &&
+            (tc < S.t_exit || (tc == S.t_exit && (S.next == INT_MAX || L.rank(k) < L.rank(S.next)))))
+            S.t_exit = tc, S.next = k;
+        const float v0 = __fsub_rn(x0, rec.x), v1 = __fsub_rn(x1, rec.y), v2 = __fsub_rn(x2, rec.z);
+        const float r2 = dot3c(v0, v1, v2, v0, v1, v2);
+        if (r2 <= record_bounds(rec).x) {
+            S.sigma += __expf(cb.z - 0.5f * maha(ca, cb, v0, v1, v2));
+            ++n_dens;
+        }
+    }
+}
 
 struct Kept {
     float4* slot;   // (rays of the pass, kKept): x, weight of the coloured segment ending here (0: none);
@@ -50,20 +98,17 @@ struct Kept {
     int* counter;   // number of chunks
 };
 
-__global__ void __launch_bounds__(kThreads)
-    trace_kernel(Layout L, InferCfg cfg, RayView R, Outputs out, Kept K, int64_t nr, int* status) {
+__global__ void __launch_bounds__(kThreads, kTraceMinBlocks)
+    trace_kernel(Layout L, const float4* __restrict__ recs, InferCfg cfg, RayView R, Outputs out, Kept K, int64_t nr,
+                 int* status) {
     const int64_t r = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
     if (r >= nr) return;
-    SlotCache<false> no_cache{nullptr};  // no colours in this pass
     float o[3], d[3];
 #pragma unroll
     for (int a = 0; a < 3; ++a) o[a] = __ldg(R.o + 3 * r + a), d[a] = __ldg(R.d + 3 * r + a);
     const float t_near = __ldg(R.near + r), t_far = __ldg(R.far + r);
     const int max_samples = cfg.cap != nullptr ? __ldg(cfg.cap + r) : INT_MAX;
-    float b[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) b[j] = 0.f;
-    int err = 0, walk_steps = 0, n_dens = 0, n_sh = 0, n_samples = 1, n_coloured = 0, kept = 0;
+    int err = 0, walk_steps = 0, n_dens = 0, n_samples = 1, n_coloured = 0, kept = 0;
     float4* slot = K.slot + r * kKept;
     int* slot_cell = K.cell + r * kKept;
     auto keep = [&](float t, int cell, float w_before) {
@@ -78,7 +123,7 @@ __global__ void __launch_bounds__(kThreads)
     const int first = nearest_site(L, __ldg(R.start + r), along(o[0], t_near, d[0]), along(o[1], t_near, d[1]),
                                    along(o[2], t_near, d[2]), walk_steps, err);
     CellScan S;
-    scan_cell<1, kExact, false>(L, cfg, first, t_near, o, d, b, no_cache, true, S, n_dens, n_sh);
+    trace_scan(L, recs, first, t_near, o, d, true, S, n_dens);
     float tP = t_near, sigmaP = S.sigma;
     int cP = first;
     bool keptP = false;
@@ -88,7 +133,7 @@ __global__ void __launch_bounds__(kThreads)
         const bool last = S.next == INT_MAX || S.t_exit >= t_far || n_samples + 1 >= max_samples;
         const float tQ = last ? t_far : fmaxf(S.t_exit, tP);
         const int cQ = last ? cP : S.next;
-        scan_cell<1, kExact, false>(L, cfg, cQ, tQ, o, d, b, no_cache, !last, S, n_dens, n_sh);
+        trace_scan(L, recs, cQ, tQ, o, d, !last, S, n_dens);
         ++n_samples;
         const float alpha = 1.f - __expf(-0.5f * (sigmaP + S.sigma) * (tQ - tP));
         const float w = T * alpha;
@@ -149,16 +194,16 @@ __global__ void __launch_bounds__(kThreads) chunks_kernel(const int* __restrict_
 }
 
 // What the colour pass stages per neighbour: its edge record, colour conic (two rows) and either its SH
-// coefficient rows or its baked colour.
-template <int MODE, bool HALF>
-constexpr int staged_rows() { return 3 + (MODE == kBakedColour ? 1 : coef_rows<HALF>()); }
+// coefficients (as 12 fp32 rows, fp16 ones converted once while staging) or its baked colour.
+template <int MODE>
+constexpr int staged_rows() { return 3 + (MODE == kBakedColour ? 1 : 12); }
 
 template <int MODE, bool HALF>
 __global__ void __launch_bounds__(kThreads)
     colour_kernel(Layout L, InferCfg cfg, RayView R, Kept K, const int* __restrict__ n_chunks_ptr,
                   int* __restrict__ stats) {
     constexpr int kPer = kChunkSamples / 32;  // samples per lane
-    constexpr int kNv = staged_rows<MODE, HALF>();
+    constexpr int kNv = staged_rows<MODE>();
     constexpr int kCoef = coef_rows<HALF>();
     __shared__ float4 smem[(kThreads / 32) * 32 * kNv];
     float4* nbr = smem + (threadIdx.x >> 5) * 32 * kNv;
@@ -207,10 +252,13 @@ __global__ void __launch_bounds__(kThreads)
                         if (MODE == kBakedColour) {
                             dst[3] = __ldg(row + 4);
                         } else {
-                            const float4* c = static_cast<const float4*>(L.net.sh) +
-                                              kCoef * static_cast<int64_t>(L.site(eb + lane));
+                            float4 rows[kCoef];
+                            load_coefficient_rows<HALF>(L.net.sh, L.site(eb + lane), rows);
+                            float f[48];
+                            unpack_coefficients<HALF>(rows, f);
 #pragma unroll
-                            for (int q = 0; q < kCoef; ++q) dst[3 + q] = __ldg(c + q);
+                            for (int q = 0; q < 12; ++q)
+                                dst[3 + q] = make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
                         }
                     }
                     __syncwarp();
@@ -252,10 +300,11 @@ __global__ void __launch_bounds__(kThreads)
                         const float4 baked = src[3];
                         rgb[0] = baked.x, rgb[1] = baked.y, rgb[2] = baked.z;
                     } else {
-                        float4 rows[kCoef];
 #pragma unroll
-                        for (int q = 0; q < kCoef; ++q) rows[q] = src[3 + q];
-                        unpack_coefficients<HALF>(rows, f);
+                        for (int q = 0; q < 12; ++q) {
+                            const float4 c4 = src[3 + q];
+                            f[4 * q] = c4.x, f[4 * q + 1] = c4.y, f[4 * q + 2] = c4.z, f[4 * q + 3] = c4.w;
+                        }
                     }
 #pragma unroll
                     for (int p = 0; p < kPer; ++p) {
@@ -307,11 +356,11 @@ __global__ void __launch_bounds__(kThreads) composite_kernel(Kept K, int64_t nr,
 inline size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct KeptLayout {
-    size_t slot, cell, n_kept, count, fill, offsets, order, chunks, counter, temp, temp_bytes, total;
+    size_t recs, slot, cell, n_kept, count, fill, offsets, order, chunks, counter, temp, temp_bytes, total;
     int64_t rays_per_pass;
 };
 
-KeptLayout kept_layout(int64_t n_sites, int64_t n_rays) {
+KeptLayout kept_layout(int64_t n_sites, int64_t n_edges, int64_t n_rays) {
     KeptLayout L{};
     if (n_rays <= 0) return L;
     L.rays_per_pass = std::max<int64_t>(1, std::min<int64_t>(n_rays, kPassSlots / kKept));
@@ -322,6 +371,7 @@ KeptLayout kept_layout(int64_t n_sites, int64_t n_rays) {
         at += al256(bytes);
         return h;
     };
+    L.recs = take(48 * static_cast<size_t>(n_edges));
     L.slot = take(16 * static_cast<size_t>(slots));
     L.cell = take(4 * static_cast<size_t>(slots));
     L.n_kept = take(4 * static_cast<size_t>(L.rays_per_pass));
@@ -358,13 +408,16 @@ inline int blocks(int64_t n) { return static_cast<int>((n + kThreads - 1) / kThr
 }  // namespace
 }  // namespace infer
 
-size_t foam_infer_workspace(int64_t n_sites, int64_t n_rays) { return infer::kept_layout(n_sites, n_rays).total; }
+size_t foam_infer_workspace(int64_t n_sites, int64_t n_edges, int64_t n_rays) {
+    return infer::kept_layout(n_sites, n_edges, n_rays).total;
+}
 
-cudaError_t foam_infer_deferred(const InferNet& net, int64_t n_sites, const InferCfg& cfg, const RayView& R,
-                                const Outputs& out, int* status, void* ws, size_t ws_bytes, cudaStream_t st) {
+cudaError_t foam_infer_deferred(const InferNet& net, int64_t n_sites, int64_t n_edges, const InferCfg& cfg,
+                                const RayView& R, const Outputs& out, int* status, void* ws, size_t ws_bytes,
+                                cudaStream_t st) {
     using namespace infer;
     if (R.n == 0) return cudaSuccess;
-    const KeptLayout KL = kept_layout(n_sites, R.n);
+    const KeptLayout KL = kept_layout(n_sites, n_edges, R.n);
     if (cfg.stage < 2 || ws == nullptr || ws_bytes < KL.total) return foam_infer(net, cfg, R, out, status, st);
     const Layout L{net};
     char* base = static_cast<char*>(ws);
@@ -375,6 +428,8 @@ cudaError_t foam_infer_deferred(const InferNet& net, int64_t n_sites, const Infe
            reinterpret_cast<int*>(base + KL.counter)};
     const int n = static_cast<int>(n_sites);
     const bool half = net.sh_half != 0;
+    float4* recs = reinterpret_cast<float4*>(base + KL.recs);
+    trace_records_kernel<<<blocks(n_edges), kThreads, 0, st>>>(L, n_edges, recs);
     for (int64_t r0 = 0; r0 < R.n; r0 += KL.rays_per_pass) {
         const int64_t nr = std::min<int64_t>(KL.rays_per_pass, R.n - r0);
         const RayView Rp{R.o + 3 * r0, R.d + 3 * r0, R.start + r0, R.near + r0, nullptr, R.far + r0, nr};
@@ -387,7 +442,7 @@ cudaError_t foam_infer_deferred(const InferNet& net, int64_t n_sites, const Infe
         if (e != cudaSuccess) return e;
         {
             ProfScope ps(kProfInfer, st);
-            trace_kernel<<<blocks(nr), kThreads, 0, st>>>(L, cp, Rp, op, K, nr, status);
+            trace_kernel<<<blocks(nr), kThreads, 0, st>>>(L, recs, cp, Rp, op, K, nr, status);
         }
         size_t tb = KL.temp_bytes;
         e = cub::DeviceScan::ExclusiveSum(base + KL.temp, tb, K.count, K.offsets, n + 1, st);

@@ -465,7 +465,7 @@ class FoamInferExtension:
                 stats.data_ptr()]
         with torch.cuda.device(dev):
             if stage == 2 and not exact_stats:
-                nbytes = _lib.lib().vg_foam_infer_workspace_bytes(n, B)
+                nbytes = _lib.lib().vg_foam_infer_workspace_bytes(n, nbr.numel(), B)
                 ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
                 _lib.call('vg_foam_infer_deferred', *args, ws.data_ptr(), nbytes, _stream(dev))
             else:
