@@ -253,11 +253,19 @@ int vg_foam_infer(const float* points, const int32_t* offsets, const int32_t* nb
                   const int32_t* cap, const int32_t* orig, float* rgb, float* T, float* depth, int32_t* stats,
                   void* stream);
 
-/* Workspace of vg_foam_infer_deferred for n_sites sites, n_edges records of the layout and n_rays rays. */
-size_t vg_foam_infer_workspace_bytes(int64_t n_sites, int64_t n_edges, int64_t n_rays);
+/* Workspace of vg_foam_infer_deferred for n_sites sites and n_rays rays. */
+size_t vg_foam_infer_workspace_bytes(int64_t n_sites, int64_t n_rays);
+
+/* Trace records of an inference layout for vg_foam_infer_deferred: records (n_edges, 12) float32, built
+ * once per layout and kept by the caller (they change only when nbr, edge or attr change): edge e as
+ * (edge[e] | attr[nbr[e], 0:4] | attr[nbr[e], 4:7], bits(nbr[e])), so the traversal reads each cell's
+ * neighbourhood with its density conics as one contiguous run. No reference counterpart (an auxiliary
+ * layout of foam_infer.cu's inputs). */
+int vg_infer_trace_records(const int32_t* nbr, const float* edge, const float* attr, int64_t n_sites, int64_t n_edges,
+                           float* records, void* stream);
 
 /* foam_infer (foam_infer.cu:376-435) with deferred, cell-major colours: the same arguments as
- * vg_foam_infer plus a caller-allocated workspace. At stage 2 the samples, densities and weights are
+ * vg_foam_infer plus the layout's trace records (vg_infer_trace_records) and a caller-allocated workspace. At stage 2 the samples, densities and weights are
  * traced per ray without colours; the samples that border a coloured segment are then sorted by cell and
  * coloured one cell at a time, and composited per ray in order. rgb, T, depth and stats columns 0-3
  * (samples, coloured segments, walk steps, density terms) are those of vg_foam_infer, bit for bit;
@@ -268,8 +276,9 @@ int vg_foam_infer_deferred(const float* points, const int32_t* offsets, const in
                            const float* attr, const void* sh, int sh_half, int sh_deg, int64_t n_sites,
                            int64_t n_edges, const float* o, const float* d, const int32_t* start, const float* near,
                            const float* far, int64_t n_rays, float t_thresh, float w_thresh, float color_cut,
-                           int color_mode, int stage, const int32_t* cap, const int32_t* orig, float* rgb, float* T,
-                           float* depth, int32_t* stats, void* workspace, size_t workspace_bytes, void* stream);
+                           int color_mode, int stage, const int32_t* cap, const int32_t* orig,
+                           const float* trace_records, float* rgb, float* T, float* depth, int32_t* stats,
+                           void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------------ kernel timing */
 

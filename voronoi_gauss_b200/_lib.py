@@ -61,9 +61,10 @@ SIGNATURES = {
     'vg_nearest_sites': (I32, [P, I64, I64, P, I64, P, P]),
     'vg_foam_infer': (I32, [P, P, P, P, P, P, I32, I32, I64, I64, P, P, P, P, P, I64, F32, F32, F32, I32, I32, P, P, P,
                             P, P, P, P]),
-    'vg_foam_infer_workspace_bytes': (SZ, [I64, I64, I64]),
+    'vg_foam_infer_workspace_bytes': (SZ, [I64, I64]),
+    'vg_infer_trace_records': (I32, [P, P, P, I64, I64, P, P]),
     'vg_foam_infer_deferred': (I32, [P, P, P, P, P, P, I32, I32, I64, I64, P, P, P, P, P, I64, F32, F32, F32, I32, I32,
-                                     P, P, P, P, P, P, P, SZ, P]),
+                                     P, P, P, P, P, P, P, P, SZ, P]),
     'vg_prof_enable': (I32, [I32]),
     'vg_prof_read': (I32, [I32, P, P]),
 }

@@ -583,23 +583,37 @@ int vg_foam_infer(const float* points, const int32_t* offsets, const int32_t* nb
     return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_foam_infer");
 }
 
-size_t vg_foam_infer_workspace_bytes(int64_t n_sites, int64_t n_edges, int64_t n_rays) {
-    if (n_sites <= 0 || n_sites >= INT32_MAX || n_edges < n_sites || n_edges >= INT32_MAX || n_rays < 0) return 0;
-    return vg::foam_infer_workspace(n_sites, n_edges, n_rays);
+size_t vg_foam_infer_workspace_bytes(int64_t n_sites, int64_t n_rays) {
+    if (n_sites <= 0 || n_sites >= INT32_MAX || n_rays < 0) return 0;
+    return vg::foam_infer_workspace(n_sites, n_rays);
+}
+
+int vg_infer_trace_records(const int32_t* nbr, const float* edge, const float* attr, int64_t n_sites, int64_t n_edges,
+                           float* records, void* stream) {
+    REQUIRE(nbr && edge && attr && records, "nbr, edge, attr and records must be non-null");
+    REQUIRE(n_sites > 0 && n_sites < INT32_MAX && n_edges >= n_sites && n_edges < INT32_MAX, "bad pack sizes");
+    REQUIRE(aligned(edge, 16) && aligned(attr, 16) && aligned(records, 16), "edge, attr and records must be 16-byte aligned");
+    const vg::InferNet N{nullptr, nullptr, nbr, reinterpret_cast<const float4*>(edge),
+                         reinterpret_cast<const float4*>(attr), nullptr, nullptr, 0};
+    const cudaError_t e = vg::infer_trace_records(N, n_edges, records, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_infer_trace_records");
 }
 
 int vg_foam_infer_deferred(const float* points, const int32_t* offsets, const int32_t* nbr, const float* edge,
                            const float* attr, const void* sh, int sh_half, int sh_deg, int64_t n_sites,
                            int64_t n_edges, const float* o, const float* d, const int32_t* start, const float* near,
                            const float* far, int64_t n_rays, float t_thresh, float w_thresh, float color_cut,
-                           int color_mode, int stage, const int32_t* cap, const int32_t* orig, float* rgb, float* T,
-                           float* depth, int32_t* stats, void* workspace, size_t workspace_bytes, void* stream) {
+                           int color_mode, int stage, const int32_t* cap, const int32_t* orig,
+                           const float* trace_records, float* rgb, float* T, float* depth, int32_t* stats,
+                           void* workspace, size_t workspace_bytes, void* stream) {
     int rc = infer_args(points, offsets, nbr, edge, attr, sh, sh_deg, n_sites, n_edges, o, d, start, near, far, n_rays,
                         color_mode, stage, rgb, T, depth, stats);
     if (rc) return rc;
     if (n_rays == 0) return VG_OK;
     REQUIRE(aligned(workspace, 256), "workspace must be 256-byte aligned");
-    const size_t need = stage == 2 ? vg::foam_infer_workspace(n_sites, n_edges, n_rays) : 0;
+    REQUIRE(stage < 2 || (trace_records != nullptr && aligned(trace_records, 16)),
+            "trace_records (from vg_infer_trace_records) must be non-null and 16-byte aligned");
+    const size_t need = stage == 2 ? vg::foam_infer_workspace(n_sites, n_rays) : 0;
     if (need > 0 && (workspace == nullptr || workspace_bytes < need))
         return fail(VG_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);
     int* status = status_ptr();
@@ -609,8 +623,8 @@ int vg_foam_infer_deferred(const float* points, const int32_t* offsets, const in
     const vg::InferCfg c{t_thresh, w_thresh, color_cut, sh_deg, color_mode, stage, cap};
     const vg::RayView R{o, d, start, near, nullptr, far, n_rays};
     const vg::Outputs out{rgb, T, depth, stats, nullptr};
-    const cudaError_t e = vg::foam_infer_deferred(N, n_sites, n_edges, c, R, out, status, workspace, workspace_bytes,
-                                                  static_cast<cudaStream_t>(stream));
+    const cudaError_t e = vg::foam_infer_deferred(N, trace_records, n_sites, c, R, out, status, workspace,
+                                                  workspace_bytes, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_foam_infer_deferred");
 }
 

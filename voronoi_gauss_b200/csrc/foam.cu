@@ -26,10 +26,22 @@
 //   kReplicaMaxN   largest neighbourhood size (self included) for which cm_scatter_kernel spreads a
 //                  chunk's (neighbour, sample) pairs over all 32 lanes as replicas of each neighbour;
 //                  larger cells get one lane per neighbour
+//   kScatterUnroll samples of a chunk whose dependent chains one scatter lane interleaves
+#ifndef VG_FWD_MINB
 #define VG_FWD_MINB 6
+#endif
+#ifndef VG_BWD_MINB
 #define VG_BWD_MINB 1
+#endif
+#ifndef VG_COLOR_MINB
 #define VG_COLOR_MINB 1
+#endif
+#ifndef VG_SCATTER_MINB
 #define VG_SCATTER_MINB 3
+#endif
+#ifndef VG_SCATTER_UNROLL
+#define VG_SCATTER_UNROLL 1
+#endif
 
 namespace vg {
 namespace {
@@ -37,6 +49,7 @@ namespace {
 constexpr int kBlock = 128;
 constexpr int kChunk = 64;
 constexpr int kReplicaMaxN = 16;
+constexpr int kScatterUnroll = VG_SCATTER_UNROLL;
 
 // deferred: the colour fields are filled later; the last field marks the samples that need one (-1)
 // orig: the original id of P's site (loaded when P was evaluated, so the store does not wait for it)
@@ -565,6 +578,7 @@ __device__ __forceinline__ int scatter_range(const GraphView& g, const FieldView
     float4 coef[S4];
 #pragma unroll
     for (int q = 0; q < S4; ++q) coef[q] = __ldg(F.sh + static_cast<int64_t>(S4) * j + q);
+#pragma unroll kScatterUnroll
     for (int i = s0; i < s1; ++i) {
         const float4* q = st + kItemVec * i;
         const float4 q0 = q[0];
@@ -837,7 +851,8 @@ struct CmLayout {
 // Scratch of the cell-major passes over rays [r0, r0 + rays_per_pass): per-sample items (backward
 // only), the cell-sorted order, per-cell counts / fill cursors / offsets, the chunk list, a counter and
 // the CUB scan storage.
-CmLayout cm_layout(int64_t n_sites, int64_t n_rays, int K, bool with_items, int item_bytes = 64) {
+CmLayout cm_layout(int64_t n_sites, int64_t n_rays, int K, bool with_items, bool with_order = true,
+                   int item_bytes = 64) {
     CmLayout L{};
     if (K <= 0 || n_rays <= 0) return L;
     L.rays_per_pass = std::max<int64_t>(1, std::min<int64_t>(n_rays, kCmItems / K));
@@ -850,7 +865,7 @@ CmLayout cm_layout(int64_t n_sites, int64_t n_rays, int K, bool with_items, int 
     };
     L.items = take(with_items ? static_cast<size_t>(item_bytes) * slots : 0);
     L.n_items = take(with_items ? 4 * L.rays_per_pass : 0);
-    L.order = take(4 * slots);
+    L.order = take(with_order ? 4 * slots : 0);
     const int64_t passes = (n_rays + L.rays_per_pass - 1) / L.rays_per_pass;
     L.count = take(4 * (n_sites + 1) * (with_items ? 1 : passes));
     L.fill = take(4 * n_sites);
@@ -880,7 +895,7 @@ int sm_count() {
 }  // namespace
 
 size_t foam_backward_workspace(int64_t n_sites, int64_t n_rays, int record_cap) {
-    return cm_layout(n_sites, n_rays, record_cap, true).total;
+    return cm_layout(n_sites, n_rays, record_cap, true, false).total;
 }
 
 cudaError_t cm_scatter_bucketed(const GraphView& g, const FieldView& F, const float4* items, const int* offsets,
@@ -901,12 +916,12 @@ cudaError_t cm_scatter_bucketed(const GraphView& g, const FieldView& F, const fl
 }
 
 size_t march_backward_workspace(int64_t n_sites, int64_t n_rays) {
-    return cm_layout(n_sites, n_rays, kMarchCap, true, 64).total;
+    return cm_layout(n_sites, n_rays, kMarchCap, true, true, 64).total;
 }
 
 cudaError_t march_backward_cm(const GraphView& g, const FieldView& F, const RayView& R, const MarchCfg& c,
                               const GradIn& gi, float* grad, int* status, void* cm_ws, cudaStream_t st) {
-    const CmLayout L = cm_layout(g.n, R.n, kMarchCap, true, 64);
+    const CmLayout L = cm_layout(g.n, R.n, kMarchCap, true, true, 64);
     char* b = static_cast<char*>(cm_ws);
     float4* items = reinterpret_cast<float4*>(b + L.items);
     int* n_items = reinterpret_cast<int*>(b + L.n_items);
@@ -1055,7 +1070,7 @@ cudaError_t foam_backward(const GraphView& g, const FieldView& F, const RayView&
                           const GradIn& gi, float* grad, int* status, void* cm_ws, size_t cm_bytes, cudaStream_t st) {
     if (R.n == 0) return cudaSuccess;
     const int K = gi.record_cap;
-    const CmLayout L = cm_layout(g.n, R.n, K, true);
+    const CmLayout L = cm_layout(g.n, R.n, K, true, false);
     const ItemOut none{nullptr, nullptr, 0, 0, nullptr, nullptr};
     if (gi.rec == nullptr || K <= 0 || cm_ws == nullptr || cm_bytes < L.total ||
         L.total == 0) {
@@ -1066,7 +1081,6 @@ cudaError_t foam_backward(const GraphView& g, const FieldView& F, const RayView&
     foam_backward_kernel<kScatterRetraced><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, gi, grad, none, status);
     char* b = static_cast<char*>(cm_ws);
     float4* items = reinterpret_cast<float4*>(b + L.items);
-    int* order = reinterpret_cast<int*>(b + L.order);
     int* count = reinterpret_cast<int*>(b + L.count);
     int* fill = reinterpret_cast<int*>(b + L.fill);
     int* offsets = reinterpret_cast<int*>(b + L.offsets);

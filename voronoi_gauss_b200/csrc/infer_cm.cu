@@ -41,7 +41,8 @@ constexpr int kChunkSamples = 64;                  // samples of one cell per wa
 #endif
 constexpr int kTraceMinBlocks = VG_TRACE_MINB;     // resident blocks of the trace per SM (its register budget)
 
-// The trace's per-edge records, built once per call from the layout: edge e of cell c's run as three
+// The trace's per-edge records, built from the layout (once per layout: the caller keeps them): edge e of
+// cell c's run as three
 // float4 = (p_j, half2(r2_j, lam_j)) | density conic (xx, xy, xz, yy) of site j | (yz, zz, min(raw_j, 30),
 // bits(j)), i.e. the edge record followed by the rows attr[j, 0:8] with the site id in the unused slot.
 // A cell's neighbourhood is then one contiguous run of 48-byte records, and the density terms need no
@@ -356,11 +357,11 @@ __global__ void __launch_bounds__(kThreads) composite_kernel(Kept K, int64_t nr,
 inline size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct KeptLayout {
-    size_t recs, slot, cell, n_kept, count, fill, offsets, order, chunks, counter, temp, temp_bytes, total;
+    size_t slot, cell, n_kept, count, fill, offsets, order, chunks, counter, temp, temp_bytes, total;
     int64_t rays_per_pass;
 };
 
-KeptLayout kept_layout(int64_t n_sites, int64_t n_edges, int64_t n_rays) {
+KeptLayout kept_layout(int64_t n_sites, int64_t n_rays) {
     KeptLayout L{};
     if (n_rays <= 0) return L;
     L.rays_per_pass = std::max<int64_t>(1, std::min<int64_t>(n_rays, kPassSlots / kKept));
@@ -371,7 +372,6 @@ KeptLayout kept_layout(int64_t n_sites, int64_t n_edges, int64_t n_rays) {
         at += al256(bytes);
         return h;
     };
-    L.recs = take(48 * static_cast<size_t>(n_edges));
     L.slot = take(16 * static_cast<size_t>(slots));
     L.cell = take(4 * static_cast<size_t>(slots));
     L.n_kept = take(4 * static_cast<size_t>(L.rays_per_pass));
@@ -408,17 +408,23 @@ inline int blocks(int64_t n) { return static_cast<int>((n + kThreads - 1) / kThr
 }  // namespace
 }  // namespace infer
 
-size_t foam_infer_workspace(int64_t n_sites, int64_t n_edges, int64_t n_rays) {
-    return infer::kept_layout(n_sites, n_edges, n_rays).total;
+size_t foam_infer_workspace(int64_t n_sites, int64_t n_rays) { return infer::kept_layout(n_sites, n_rays).total; }
+
+cudaError_t infer_trace_records(const InferNet& net, int64_t n_edges, float* recs, cudaStream_t st) {
+    using namespace infer;
+    if (n_edges == 0) return cudaSuccess;
+    trace_records_kernel<<<blocks(n_edges), kThreads, 0, st>>>(Layout{net}, n_edges, reinterpret_cast<float4*>(recs));
+    return cudaGetLastError();
 }
 
-cudaError_t foam_infer_deferred(const InferNet& net, int64_t n_sites, int64_t n_edges, const InferCfg& cfg,
+cudaError_t foam_infer_deferred(const InferNet& net, const float* trace_recs, int64_t n_sites, const InferCfg& cfg,
                                 const RayView& R, const Outputs& out, int* status, void* ws, size_t ws_bytes,
                                 cudaStream_t st) {
     using namespace infer;
     if (R.n == 0) return cudaSuccess;
-    const KeptLayout KL = kept_layout(n_sites, n_edges, R.n);
-    if (cfg.stage < 2 || ws == nullptr || ws_bytes < KL.total) return foam_infer(net, cfg, R, out, status, st);
+    const KeptLayout KL = kept_layout(n_sites, R.n);
+    if (cfg.stage < 2 || trace_recs == nullptr || ws == nullptr || ws_bytes < KL.total)
+        return foam_infer(net, cfg, R, out, status, st);
     const Layout L{net};
     char* base = static_cast<char*>(ws);
     Kept K{reinterpret_cast<float4*>(base + KL.slot), reinterpret_cast<int*>(base + KL.cell),
@@ -428,8 +434,7 @@ cudaError_t foam_infer_deferred(const InferNet& net, int64_t n_sites, int64_t n_
            reinterpret_cast<int*>(base + KL.counter)};
     const int n = static_cast<int>(n_sites);
     const bool half = net.sh_half != 0;
-    float4* recs = reinterpret_cast<float4*>(base + KL.recs);
-    trace_records_kernel<<<blocks(n_edges), kThreads, 0, st>>>(L, n_edges, recs);
+    const float4* recs = reinterpret_cast<const float4*>(trace_recs);
     for (int64_t r0 = 0; r0 < R.n; r0 += KL.rays_per_pass) {
         const int64_t nr = std::min<int64_t>(KL.rays_per_pass, R.n - r0);
         const RayView Rp{R.o + 3 * r0, R.d + 3 * r0, R.start + r0, R.near + r0, nullptr, R.far + r0, nr};

@@ -346,11 +346,12 @@ struct InferCfg {
 };
 cudaError_t foam_infer(const InferNet& N, const InferCfg& c, const RayView& R, const Outputs& out, int* status,
                        cudaStream_t st);
-// Stage-2 rendering with deferred, cell-major colours (infer_cm.cu); workspace of
-// foam_infer_workspace(N, E, B) bytes. Outputs rgb / T / depth and stats columns 0-3 as foam_infer; column
-// 4 counts the SH evaluations of the cell-major pass.
-size_t foam_infer_workspace(int64_t n_sites, int64_t n_edges, int64_t n_rays);
-cudaError_t foam_infer_deferred(const InferNet& N, int64_t n_sites, int64_t n_edges, const InferCfg& c,
+// Stage-2 rendering with deferred, cell-major colours (infer_cm.cu) from the layout and its trace records
+// (infer_trace_records: 12 floats per edge); workspace of foam_infer_workspace(N, B) bytes. Outputs rgb /
+// T / depth and stats columns 0-3 as foam_infer; column 4 counts the SH evaluations of the cell-major pass.
+size_t foam_infer_workspace(int64_t n_sites, int64_t n_rays);
+cudaError_t infer_trace_records(const InferNet& N, int64_t n_edges, float* recs, cudaStream_t st);
+cudaError_t foam_infer_deferred(const InferNet& N, const float* trace_recs, int64_t n_sites, const InferCfg& c,
                                 const RayView& R, const Outputs& out, int* status, void* ws, size_t ws_bytes,
                                 cudaStream_t st);
 

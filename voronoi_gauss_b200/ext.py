@@ -412,17 +412,40 @@ class FieldExtension:
         return [g_ls, g_quat]
 
 
+_TRACE_CACHE = {}  # trace records of recent inference layouts (see trace_records)
+_TRACE_CACHE_SIZE = 4
+
+
+def trace_records(nbr, edge, attr, n_sites):
+    """Trace records (E, 12) of an inference layout for the deferred renderer (vg_infer_trace_records).
+    They depend only on nbr, edge and attr, so they are built once per layout and reused: the cache key
+    holds the three tensors' storage and their in-place version counters, so a layout modified in place
+    gets new records."""
+    key = tuple((t.data_ptr(), t._version, t.numel()) for t in (nbr, edge, attr)) + (n_sites,)
+    rec = _TRACE_CACHE.get(key)
+    if rec is None:
+        rec = torch.empty(nbr.numel(), 12, device=edge.device)
+        with torch.cuda.device(edge.device):
+            _lib.call('vg_infer_trace_records', nbr.data_ptr(), edge.data_ptr(), attr.data_ptr(), n_sites, nbr.numel(),
+                      rec.data_ptr(), _stream(edge.device))
+        while len(_TRACE_CACHE) >= _TRACE_CACHE_SIZE:
+            _TRACE_CACHE.pop(next(iter(_TRACE_CACHE)))
+        _TRACE_CACHE[key] = rec
+    return rec
+
+
 class FoamInferExtension:
     """foam_infer with the reference's signature (foam_infer.cu:376-435).
 
     At stage 2 the colours are deferred to a cell-major pass (vg_foam_infer_deferred): the same rgb, T,
     depth and stats columns 0-3 bit for bit, with stats column 4 counting the SH colours that pass
     evaluated. exact_stats=True renders per ray instead (vg_foam_infer), whose column 4 counts the misses
-    of a per-ray colour cache like the reference kernel's."""
+    of a per-ray colour cache like the reference kernel's. trace: the layout's trace records
+    (trace_records), built and cached here when not given."""
 
     @staticmethod
     def foam_infer(points, offsets, nbr, edge, attr, sh, sh_deg, o, d, start, near, far, t_thresh, w_thresh,
-                   color_cut, color_mode, stage, cap, orig, exact_stats=False):
+                   color_cut, color_mode, stage, cap, orig, exact_stats=False, trace=None):
         for x, name, dt in ((points, 'points', torch.float32), (offsets, 'offsets', torch.int32),
                             (nbr, 'nbr', torch.int32), (edge, 'edge', torch.float32), (attr, 'attr', torch.float32),
                             (cap, 'cap', torch.int32), (orig, 'orig', torch.int32)):
@@ -457,19 +480,23 @@ class FoamInferExtension:
         stats = torch.empty(B, 5, dtype=torch.int32, device=dev)
         if B == 0:
             return [rgb, T, depth, stats]
-        args = [points.data_ptr(), offsets.data_ptr(), nbr.data_ptr(), edge.data_ptr(), attr.data_ptr(),
+        head = [points.data_ptr(), offsets.data_ptr(), nbr.data_ptr(), edge.data_ptr(), attr.data_ptr(),
                 None if baked else _ptr(sh), int(half), _sh_deg(sh_deg), n, nbr.numel(), o.data_ptr(), d.data_ptr(),
                 start.data_ptr(), near.data_ptr(), far.data_ptr(), B, float(t_thresh), float(w_thresh),
                 float(color_cut), color_mode, stage, _ptr(cap) if cap.numel() == B else None,
-                _ptr(orig) if orig.numel() == n else None, rgb.data_ptr(), T.data_ptr(), depth.data_ptr(),
-                stats.data_ptr()]
+                _ptr(orig) if orig.numel() == n else None]
+        outs = [rgb.data_ptr(), T.data_ptr(), depth.data_ptr(), stats.data_ptr()]
         with torch.cuda.device(dev):
             if stage == 2 and not exact_stats:
-                nbytes = _lib.lib().vg_foam_infer_workspace_bytes(n, nbr.numel(), B)
+                if trace is None:
+                    trace = trace_records(nbr, edge, attr, n)
+                elif trace.shape != (nbr.numel(), 12) or trace.dtype != torch.float32 or not trace.is_contiguous():
+                    raise RuntimeError('trace must be the (E, 12) float32 trace records of the layout')
+                nbytes = _lib.lib().vg_foam_infer_workspace_bytes(n, B)
                 ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
-                _lib.call('vg_foam_infer_deferred', *args, ws.data_ptr(), nbytes, _stream(dev))
+                _lib.call('vg_foam_infer_deferred', *head, trace.data_ptr(), *outs, ws.data_ptr(), nbytes, _stream(dev))
             else:
-                _lib.call('vg_foam_infer', *args, _stream(dev))
+                _lib.call('vg_foam_infer', *head, *outs, _stream(dev))
         return [rgb, T, depth, stats]
 
 

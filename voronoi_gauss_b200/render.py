@@ -269,8 +269,9 @@ def pack_foam(model, scale_floor=0.0, eps_density=0.0, sh_half=False, reorder=Fa
         perm = orig.long()
         inv = torch.empty_like(perm)
         inv[perm] = torch.arange(n, device=dev)
+    trace = ext.trace_records(nbr, edge, attr, n)  # the deferred renderer's per-edge records
     return {'points': points, 'offsets': offsets, 'nbr': nbr, 'edge': edge, 'attr': attr, 'sh': sh, 'sh32': sh32,
-            'perm': perm, 'inv': inv, 'orig': orig, 'baked_center': None}
+            'perm': perm, 'inv': inv, 'orig': orig, 'baked_center': None, 'trace': trace}
 
 
 @torch.no_grad()
@@ -311,7 +312,7 @@ def render_rays_foam_infer(model, pack, o, d, start, near=0.02, far_radius=4.0, 
     fg, T, depth, stats = ext.foam_infer_extension().foam_infer(*layout, model.sh_deg, *rays, float(t_thresh),
                                                                 float(w_thresh), skip_beyond, mode, int(stage),
                                                                 cap.int().contiguous(), pack['orig'],
-                                                                exact_stats=exact_stats)
+                                                                exact_stats=exact_stats, trace=pack.get('trace'))
     return {'rgb': _over_background(model, fg, T), 'acc': 1.0 - T, 'depth': depth, 'stats': stats}
 
 
