@@ -418,19 +418,27 @@ _TRACE_CACHE_SIZE = 4
 
 def trace_records(nbr, edge, attr, n_sites):
     """Trace records (E, 12) of an inference layout for the deferred renderer (vg_infer_trace_records).
-    They depend only on nbr, edge and attr, so they are built once per layout and reused: the cache key
-    holds the three tensors' storage and their in-place version counters, so a layout modified in place
-    gets new records."""
-    key = tuple((t.data_ptr(), t._version, t.numel()) for t in (nbr, edge, attr)) + (n_sites,)
-    rec = _TRACE_CACHE.get(key)
-    if rec is None:
-        rec = torch.empty(nbr.numel(), 12, device=edge.device)
-        with torch.cuda.device(edge.device):
-            _lib.call('vg_infer_trace_records', nbr.data_ptr(), edge.data_ptr(), attr.data_ptr(), n_sites, nbr.numel(),
-                      rec.data_ptr(), _stream(edge.device))
-        while len(_TRACE_CACHE) >= _TRACE_CACHE_SIZE:
-            _TRACE_CACHE.pop(next(iter(_TRACE_CACHE)))
-        _TRACE_CACHE[key] = rec
+    They depend only on nbr, edge and attr (columns 0-7), so they are built once per layout and reused.
+    An entry is valid while the very tensor objects it was built from are alive and unmodified: it holds
+    weak references to them and their in-place version counters (a new layout that reuses freed memory
+    is a different object, so it never matches a stale entry)."""
+    import weakref
+    entry = _TRACE_CACHE.get(id(edge))
+    if entry is not None:
+        refs, versions, rec = entry
+        live = tuple(r() for r in refs)
+        if (live[0] is nbr and live[1] is edge and live[2] is attr and
+                versions == (nbr._version, edge._version, attr._version) and rec.size(0) == nbr.numel()):
+            return rec
+        del _TRACE_CACHE[id(edge)]
+    rec = torch.empty(nbr.numel(), 12, device=edge.device)
+    with torch.cuda.device(edge.device):
+        _lib.call('vg_infer_trace_records', nbr.data_ptr(), edge.data_ptr(), attr.data_ptr(), n_sites, nbr.numel(),
+                  rec.data_ptr(), _stream(edge.device))
+    while len(_TRACE_CACHE) >= _TRACE_CACHE_SIZE:
+        _TRACE_CACHE.pop(next(iter(_TRACE_CACHE)))
+    _TRACE_CACHE[id(edge)] = (tuple(weakref.ref(t) for t in (nbr, edge, attr)),
+                              (nbr._version, edge._version, attr._version), rec)
     return rec
 
 
