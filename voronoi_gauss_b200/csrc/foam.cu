@@ -658,38 +658,7 @@ __device__ __forceinline__ void replicated_scatter(const GraphView& g, const Fie
 // backward).
 enum StageMode { kBucketed = 0, kIndexed = 1 };
 
-// Expands a chunk's 64-byte items (copied into raw) into the staging layout: x, gs | gC, gC.C | m_min,
-// 1/sum a | SH basis of the direction (16).
-__device__ __forceinline__ void expand_items(const FieldView& F, const float4* raw, float4* st, int cnt, int lane) {
-    for (int li = lane; li < cnt; li += 32) {
-        const float4 i3 = raw[4 * li + 3];
-        float b[16];
-        sh_basis(i3.x, i3.y, i3.z, F.sh_deg, b);
-        float4* q = st + kItemVec * li;
-        q[0] = raw[4 * li], q[1] = raw[4 * li + 1], q[2] = raw[4 * li + 2];
-        q[3] = make_float4(b[0], b[1], b[2], b[3]);
-        q[4] = make_float4(b[4], b[5], b[6], b[7]);
-        q[5] = make_float4(b[8], b[9], b[10], b[11]);
-        q[6] = make_float4(b[12], b[13], b[14], b[15]);
-    }
-}
-
-// A staged chunk of the queued scatter: its cell's edge run [e0, e0 + n), its sample count and the staging
-// buffer that holds its samples (n = 0: none).
-struct StagedChunk {
-    int e0, n, cnt, buf;
-};
-
-// Shared memory of cm_scatter_kernel per warp: two staging buffers and the copy-ahead buffer (bucketed
-// stage), or one staging buffer (indexed stage).
-constexpr size_t kScatterWarpSmem = sizeof(float4) * (2 * kChunk * kItemVec + kChunk * 4);
-constexpr size_t kScatterWarpSmemIndexed = sizeof(float4) * kChunk * kItemVec;
-
-#ifndef VG_SCATTER_QUEUE
-#define VG_SCATTER_QUEUE 1
-#endif
-
-// With the bucketed stage the kernel returns through its copy-ahead loop, so the generic loop below is
+// With kAsync the bucketed stage returns through its copy-ahead loop, so the generic loop below is
 // unreachable in that instantiation (and removed); nvcc's note about it is silenced for this kernel only.
 #pragma nv_diag_suppress 128
 template <int S4, int STAGE>
@@ -697,98 +666,66 @@ __global__ void __launch_bounds__(kBlock, VG_SCATTER_MINB)
     cm_scatter_kernel(GraphView g, FieldView F, const float4* __restrict__ items, const int* __restrict__ order,
                       const int4* __restrict__ chunks, const int* __restrict__ n_chunks_ptr, float* __restrict__ grad) {
     constexpr bool kAsync = STAGE == kBucketed;
-    extern __shared__ float4 dyn_smem[];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __shared__ float4 smem[(kBlock / 32) * kChunk * kItemVec];
+    __shared__ float4 raw_smem[kAsync ? (kBlock / 32) * kChunk * 4 : 1];
+    const int lane = threadIdx.x & 31;
+    float4* st = smem + (threadIdx.x >> 5) * kChunk * kItemVec;
     const int n_chunks = *n_chunks_ptr;
     const int warps = gridDim.x * (kBlock / 32);
     if (kAsync) {
-        // Work queue of the warp: the (chunk, neighbour site) tasks of its chunks in order. A round gives
-        // the 32 lanes the next 32 tasks, which may span the end of one chunk and the start of the next,
-        // so cells with 17-31 neighbours no longer leave 32 - n lanes idle. Cells of at most kReplicaMaxN
-        // neighbours take a whole round each (replicas). Items of the next chunk are copied (cp.async)
-        // while the current rounds run; two staging buffers hold the chunks a round can span.
-        float4* base_smem = dyn_smem + warp * (kScatterWarpSmem / sizeof(float4));
-        auto stb = [&](int buf) { return base_smem + buf * (kChunk * kItemVec); };  // staging buffer 0 or 1
-        float4* raw = base_smem + 2 * kChunk * kItemVec;
-        int ch = blockIdx.x * (kBlock / 32) + warp;
-        int4 P = make_int4(0, 0, 0, 0);  // the chunk whose items are being copied into raw
-        int p_e0 = 0, p_n = 0;
-        bool p_valid = false;
-        auto prefetch = [&]() {
-            p_valid = ch < n_chunks;
-            if (p_valid) {
-                P = __ldg(chunks + ch);
-                p_e0 = __ldg(g.off + P.x), p_n = __ldg(g.off + P.x + 1) - p_e0;
-                for (int k = lane; k < 4 * P.z; k += 32) cp_async16(raw + k, items + 4 * static_cast<int64_t>(P.y) + k);
-                cp_async_commit();
-            }
-            ch += warps;
-        };
-        auto stage = [&](int buf) {
+        // items of chunk i+1 are copied while chunk i is scattered: wait for the copy, expand the items
+        // (SH basis of the direction) into the staging area, start the next copy, then scatter
+        float4* raw = raw_smem + (threadIdx.x >> 5) * kChunk * 4;
+        int ch = blockIdx.x * (kBlock / 32) + (threadIdx.x >> 5);
+        int4 C = make_int4(0, 0, 0, 0);
+        if (ch < n_chunks) {
+            C = __ldg(chunks + ch);
+            for (int k = lane; k < 4 * C.z; k += 32) cp_async16(raw + k, items + 4 * static_cast<int64_t>(C.y) + k);
+            cp_async_commit();
+        }
+        for (; ch < n_chunks; ch += warps) {
             cp_async_wait_all();
             __syncwarp();
-            expand_items(F, raw, stb(buf), P.z, lane);
-            __syncwarp();
-            const StagedChunk s{p_e0, p_n, P.z, buf};
-            prefetch();
-            return s;
-        };
-        prefetch();
-        StagedChunk X{0, 0, 0, 0}, Y{0, 0, 0, 1};
-        int base = 0;  // next task of X
-        while (true) {
-            if (X.n == 0) {
-                if (!p_valid) break;
-                X = stage(X.buf);
-                base = 0;
+            for (int li = lane; li < C.z; li += 32) {
+                const float4 i3 = raw[4 * li + 3];
+                float b[16];
+                sh_basis(i3.x, i3.y, i3.z, F.sh_deg, b);
+                float4* q = st + kItemVec * li;
+                q[0] = raw[4 * li], q[1] = raw[4 * li + 1], q[2] = raw[4 * li + 2];
+                q[3] = make_float4(b[0], b[1], b[2], b[3]);
+                q[4] = make_float4(b[4], b[5], b[6], b[7]);
+                q[5] = make_float4(b[8], b[9], b[10], b[11]);
+                q[6] = make_float4(b[12], b[13], b[14], b[15]);
             }
-            if (X.n <= kReplicaMaxN || !VG_SCATTER_QUEUE) {
-                if (X.n <= kReplicaMaxN) {
-                    replicated_scatter<S4>(g, F, stb(X.buf), X.e0, X.n, X.cnt, lane, grad);
-                } else {
-                    for (int e = X.e0 + lane; e < X.e0 + X.n; e += 32) {
-                        PairAcc<S4> A;
-                        A.zero();
-                        const int j = scatter_range<S4>(g, F, e, stb(X.buf), 0, X.cnt, A);
-                        A.flush(grad, j);
-                    }
+            __syncwarp();
+            const int4 Cur = C;
+            if (ch + warps < n_chunks) {
+                C = __ldg(chunks + ch + warps);
+                for (int k = lane; k < 4 * C.z; k += 32)
+                    cp_async16(raw + k, items + 4 * static_cast<int64_t>(C.y) + k);
+                cp_async_commit();
+            }
+            const int e0 = __ldg(g.off + Cur.x), e1 = __ldg(g.off + Cur.x + 1);
+            if (e1 - e0 <= kReplicaMaxN) {
+                replicated_scatter<S4>(g, F, st, e0, e1 - e0, Cur.z, lane, grad);
+            } else {
+                for (int e = e0 + lane; e < e1; e += 32) {
+                    PairAcc<S4> A;
+                    A.zero();
+                    const int j = scatter_range<S4>(g, F, e, st, 0, Cur.z, A);
+                    A.flush(grad, j);
                 }
-                __syncwarp();
-                X.n = 0;
-                continue;
-            }
-            // the round would leave lanes idle: bring in the next chunk when it is another large one
-            if (X.n - base < 32 && Y.n == 0 && p_valid && p_n > kReplicaMaxN) Y = stage(Y.buf);
-            const int t = base + lane;
-            int e = -1, cnt = 0, buf = 0;
-            if (t < X.n)
-                e = X.e0 + t, cnt = X.cnt, buf = X.buf;
-            else if (t - X.n < Y.n)
-                e = Y.e0 + (t - X.n), cnt = Y.cnt, buf = Y.buf;
-            if (e >= 0) {
-                PairAcc<S4> A;
-                A.zero();
-                const int j = scatter_range<S4>(g, F, e, stb(buf), 0, cnt, A);
-                A.flush(grad, j);
             }
             __syncwarp();
-            base += 32;
-            while (X.n > 0 && base >= X.n) {  // chunks whose tasks are all done leave the queue
-                base -= X.n;
-                const int freed = X.buf;
-                X = Y;
-                Y = StagedChunk{0, 0, 0, freed};
-            }
-            if (X.n == 0) base = 0;
         }
         return;
     }
-    float4* st = dyn_smem + warp * (kScatterWarpSmemIndexed / sizeof(float4));
-    for (int ch = blockIdx.x * (kBlock / 32) + warp; ch < n_chunks; ch += warps) {
+    for (int ch = blockIdx.x * (kBlock / 32) + (threadIdx.x >> 5); ch < n_chunks; ch += warps) {
         const int4 C = __ldg(chunks + ch);
         const int cell = C.x, cnt = C.z;
-        for (int li = lane; li < cnt; li += 32) {  // stage the chunk's 64-byte items, reached through order
-            const float4* it = items + 4 * static_cast<int64_t>(__ldg(order + C.y + li));
+        for (int li = lane; li < cnt; li += 32) {  // stage the chunk's 64-byte items
+            const int64_t at = STAGE == kIndexed ? __ldg(order + C.y + li) : static_cast<int64_t>(C.y) + li;
+            const float4* it = items + 4 * at;
             const float4 i3 = __ldg(it + 3);
             float b[16];
             sh_basis(i3.x, i3.y, i3.z, F.sh_deg, b);
@@ -814,6 +751,7 @@ __global__ void __launch_bounds__(kBlock, VG_SCATTER_MINB)
         __syncwarp();
     }
 }
+
 #pragma nv_diag_default 128
 
 // ------------------------------------------------------------ cell-major backward of the march path
@@ -954,32 +892,6 @@ int sm_count() {
     return n;
 }
 
-// Launches cm_scatter_kernel for the SH row count s4 with its dynamic shared memory (above the 48 KB
-// default for the bucketed stage: two staging buffers and the copy-ahead buffer per warp).
-template <int S4, int STAGE>
-cudaError_t scatter_launch(int grid, const GraphView& g, const FieldView& F, const float4* items, const int* order,
-                           const int4* chunks, const int* counter, float* grad, cudaStream_t st) {
-    const int smem = static_cast<int>((kBlock / 32) * (STAGE == kBucketed ? kScatterWarpSmem : kScatterWarpSmemIndexed));
-    cudaError_t e = cudaFuncSetAttribute(cm_scatter_kernel<S4, STAGE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(cm_scatter_kernel<S4, STAGE>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                 cudaSharedmemCarveoutMaxShared);
-    if (e != cudaSuccess) return e;
-    cm_scatter_kernel<S4, STAGE><<<grid, kBlock, smem, st>>>(g, F, items, order, chunks, counter, grad);
-    return cudaGetLastError();
-}
-
-template <int STAGE>
-cudaError_t scatter(int grid, const GraphView& g, const FieldView& F, const float4* items, const int* order,
-                    const int4* chunks, const int* counter, float* grad, cudaStream_t st) {
-    switch (F.s4) {
-        case 1: return scatter_launch<1, STAGE>(grid, g, F, items, order, chunks, counter, grad, st);
-        case 3: return scatter_launch<3, STAGE>(grid, g, F, items, order, chunks, counter, grad, st);
-        case 7: return scatter_launch<7, STAGE>(grid, g, F, items, order, chunks, counter, grad, st);
-        default: return scatter_launch<12, STAGE>(grid, g, F, items, order, chunks, counter, grad, st);
-    }
-}
-
 }  // namespace
 
 size_t foam_backward_workspace(int64_t n_sites, int64_t n_rays, int record_cap) {
@@ -994,7 +906,13 @@ cudaError_t cm_scatter_bucketed(const GraphView& g, const FieldView& F, const fl
     cm_chunks_kernel<<<blocks(n), kBlock, 0, st>>>(offsets, n, chunks, counter);
     const int grid = sm_count() * 3;
     ProfScope ps(kProfScatter, st);
-    return scatter<kBucketed>(grid, g, F, items, nullptr, chunks, counter, grad, st);
+    switch (F.s4) {
+        case 1: cm_scatter_kernel<1, kBucketed><<<grid, kBlock, 0, st>>>(g, F, items, nullptr, chunks, counter, grad); break;
+        case 3: cm_scatter_kernel<3, kBucketed><<<grid, kBlock, 0, st>>>(g, F, items, nullptr, chunks, counter, grad); break;
+        case 7: cm_scatter_kernel<7, kBucketed><<<grid, kBlock, 0, st>>>(g, F, items, nullptr, chunks, counter, grad); break;
+        default: cm_scatter_kernel<12, kBucketed><<<grid, kBlock, 0, st>>>(g, F, items, nullptr, chunks, counter, grad); break;
+    }
+    return cudaGetLastError();
 }
 
 size_t march_backward_workspace(int64_t n_sites, int64_t n_rays) {
@@ -1033,7 +951,13 @@ cudaError_t march_backward_cm(const GraphView& g, const FieldView& F, const RayV
                                                                         order);
         cm_chunks_kernel<<<blocks(n), kBlock, 0, st>>>(offsets, n, chunks, counter);
         ProfScope ps(kProfScatter, st);
-        e = scatter<kIndexed>(grid, g, F, items, order, chunks, counter, grad, st);
+        switch (F.s4) {
+            case 1: cm_scatter_kernel<1, kIndexed><<<grid, kBlock, 0, st>>>(g, F, items, order, chunks, counter, grad); break;
+            case 3: cm_scatter_kernel<3, kIndexed><<<grid, kBlock, 0, st>>>(g, F, items, order, chunks, counter, grad); break;
+            case 7: cm_scatter_kernel<7, kIndexed><<<grid, kBlock, 0, st>>>(g, F, items, order, chunks, counter, grad); break;
+            default: cm_scatter_kernel<12, kIndexed><<<grid, kBlock, 0, st>>>(g, F, items, order, chunks, counter, grad); break;
+        }
+        e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
@@ -1181,7 +1105,13 @@ cudaError_t foam_backward(const GraphView& g, const FieldView& F, const RayView&
         }
         cm_chunks_kernel<<<blocks(n), kBlock, 0, st>>>(offsets, n, chunks, counter);
         ProfScope ps(kProfScatter, st);
-        e = scatter<kBucketed>(grid, g, F, items, nullptr, chunks, counter, grad, st);
+        switch (F.s4) {
+            case 1: cm_scatter_kernel<1, kBucketed><<<grid, kBlock, 0, st>>>(g, F, items, nullptr, chunks, counter, grad); break;
+            case 3: cm_scatter_kernel<3, kBucketed><<<grid, kBlock, 0, st>>>(g, F, items, nullptr, chunks, counter, grad); break;
+            case 7: cm_scatter_kernel<7, kBucketed><<<grid, kBlock, 0, st>>>(g, F, items, nullptr, chunks, counter, grad); break;
+            default: cm_scatter_kernel<12, kBucketed><<<grid, kBlock, 0, st>>>(g, F, items, nullptr, chunks, counter, grad); break;
+        }
+        e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
