@@ -39,9 +39,6 @@ constexpr int kChunkSamples = 64;                  // samples of one cell per wa
 #ifndef VG_TRACE_MINB
 #define VG_TRACE_MINB 8
 #endif
-#ifndef VG_TRACE_QUEUE
-#define VG_TRACE_QUEUE 1
-#endif
 constexpr int kTraceMinBlocks = VG_TRACE_MINB;     // resident blocks of the trace per SM (its register budget)
 
 // The trace's per-edge records, built from the layout (once per layout: the caller keeps them): edge e of
@@ -160,98 +157,6 @@ __global__ void __launch_bounds__(kThreads, kTraceMinBlocks)
     s[0] = n_samples, s[1] = n_coloured, s[2] = walk_steps, s[3] = n_dens, s[4] = 0;
     K.n_kept[r] = kept;
     if (err) atomicOr(status, err);
-}
-
-// The trace of trace_kernel with the rays of a warp taken from a queue: each warp owns a contiguous run of
-// rays (consecutive 4x8 pixel tiles), and a lane whose ray has ended takes the next ray of the run, so a
-// warp no longer waits for its longest ray with the other lanes idle, while the rays it holds stay
-// neighbours in the image. Every lane does one cell scan per round (the first one of a new ray after its
-// walk to x(near)), with the arithmetic and outputs of trace_kernel.
-__global__ void __launch_bounds__(kThreads, kTraceMinBlocks)
-    trace_queue_kernel(Layout L, const float4* __restrict__ recs, InferCfg cfg, RayView R, Outputs out, Kept K,
-                       int64_t nr, int rays_per_warp, int* status) {
-    const int lane = threadIdx.x & 31;
-    const int64_t q0 = ((static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5) * rays_per_warp;
-    const int64_t q1 = min(nr, q0 + rays_per_warp);
-    if (q0 >= nr) return;  // whole warps
-    int64_t next = q0;     // first ray of the run not yet taken (the same in every lane)
-    int64_t r = -1;
-    bool active = false, fresh = false, keptP = false;
-    float o[3] = {0.f, 0.f, 0.f}, d[3] = {0.f, 0.f, 0.f};
-    float t_near = 0.f, t_far = 0.f, tP = 0.f, sigmaP = 0.f, T = 1.f, depth = 0.f;
-    int max_samples = 0, cP = 0, err = 0, walk_steps = 0, n_dens = 0, n_samples = 1, n_coloured = 0, kept = 0;
-    int cells = 0;
-    CellScan S;
-    S.sigma = 0.f, S.t_exit = kInf, S.next = INT_MAX;
-    auto keep = [&](float t, int cell, float w_before) {
-        if (kept < kKept) {
-            K.slot[r * kKept + kept] =
-                make_float4(along(o[0], t, d[0]), along(o[1], t, d[1]), along(o[2], t, d[2]), w_before);
-            K.cell[r * kKept + kept] = cell;
-            atomicAdd(K.count + cell, 1);
-        }
-        ++kept;
-    };
-    while (true) {
-        const unsigned idle = __ballot_sync(0xffffffffu, !active);
-        if (idle != 0u && next < q1) {  // idle lanes take the next rays of the run, in lane order
-            const int64_t mine = next + __popc(idle & ((1u << lane) - 1u));
-            if (!active && mine < q1) {
-                r = mine, active = true, fresh = true;
-#pragma unroll
-                for (int a = 0; a < 3; ++a) o[a] = __ldg(R.o + 3 * r + a), d[a] = __ldg(R.d + 3 * r + a);
-                t_near = __ldg(R.near + r), t_far = __ldg(R.far + r);
-                max_samples = cfg.cap != nullptr ? __ldg(cfg.cap + r) : INT_MAX;
-                err = walk_steps = n_dens = n_coloured = kept = cells = 0;
-                n_samples = 1, T = 1.f, depth = 0.f, keptP = false;
-            }
-            next += __popc(idle);
-        }
-        if (!__any_sync(0xffffffffu, active)) break;
-        if (!active) continue;
-        int c;
-        float t;
-        bool last = false;
-        if (fresh) {
-            c = nearest_site(L, __ldg(R.start + r), along(o[0], t_near, d[0]), along(o[1], t_near, d[1]),
-                             along(o[2], t_near, d[2]), walk_steps, err);
-            t = t_near;
-        } else {
-            last = S.next == INT_MAX || S.t_exit >= t_far || n_samples + 1 >= max_samples;
-            t = last ? t_far : fmaxf(S.t_exit, tP);
-            c = last ? cP : S.next;
-        }
-        trace_scan(L, recs, c, t, o, d, fresh || !last, S, n_dens);
-        bool done = false;
-        if (fresh) {
-            tP = t, sigmaP = S.sigma, cP = c, fresh = false;
-        } else {
-            ++n_samples;
-            const float alpha = 1.f - __expf(-0.5f * (sigmaP + S.sigma) * (t - tP));
-            const float w = T * alpha;
-            bool keptQ = false;
-            if (w > cfg.w_thresh) {
-                if (!keptP) keep(tP, cP, 0.f);
-                keep(t, c, w);
-                keptQ = true;
-                depth += w * 0.5f * (tP + t);
-                ++n_coloured;
-            }
-            T *= 1.f - alpha;
-            tP = t, sigmaP = S.sigma, cP = c, keptP = keptQ;
-            done = last || T < cfg.t_thresh;
-            if (!done && ++cells == kMaxCells) err |= kErrCellCap, done = true;
-        }
-        if (done) {
-            out.T[r] = T;
-            out.depth[r] = depth;
-            int* st = out.stats + 5 * r;
-            st[0] = n_samples, st[1] = n_coloured, st[2] = walk_steps, st[3] = n_dens, st[4] = 0;
-            K.n_kept[r] = kept;
-            if (err) atomicOr(status, err);
-            active = false;
-        }
-    }
 }
 
 // The kept slots of the pass's rays counting-sorted by cell; one warp per ray.
@@ -542,17 +447,7 @@ cudaError_t foam_infer_deferred(const InferNet& net, const float* trace_recs, in
         if (e != cudaSuccess) return e;
         {
             ProfScope ps(kProfInfer, st);
-            if (VG_TRACE_QUEUE) {
-                // rays per warp: a multiple of 32, at most 8 tiles, with at least 32 warps per SM
-                const int64_t warps_wanted = static_cast<int64_t>(sm_count()) * 32;
-                const int per_warp = static_cast<int>(std::max<int64_t>(
-                    32, std::min<int64_t>(256, (nr / std::max<int64_t>(warps_wanted, 1)) / 32 * 32)));
-                const int64_t warps = (nr + per_warp - 1) / per_warp;
-                trace_queue_kernel<<<blocks(32 * warps), kThreads, 0, st>>>(L, recs, cp, Rp, op, K, nr, per_warp,
-                                                                           status);
-            } else {
-                trace_kernel<<<blocks(nr), kThreads, 0, st>>>(L, recs, cp, Rp, op, K, nr, status);
-            }
+            trace_kernel<<<blocks(nr), kThreads, 0, st>>>(L, recs, cp, Rp, op, K, nr, status);
         }
         size_t tb = KL.temp_bytes;
         e = cub::DeviceScan::ExclusiveSum(base + KL.temp, tb, K.count, K.offsets, n + 1, st);
