@@ -71,6 +71,8 @@ def parse():
     ap.add_argument('--no-baselines', action='store_true', help='skip the CPU and reference-CUDA baselines')
     ap.add_argument('--strong', action='store_true',
                     help='strong scaling: one frame (default 3840x2160) whose 16x16 tiles are dealt over the GPUs')
+    ap.add_argument('--field', action='store_true',
+                    help='the NeRF-sampler field kernels (walk, density, colour) on the config-2 scene')
     return ap.parse_args()
 
 
@@ -872,6 +874,74 @@ def run_march(args):
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------------------- field arm
+
+FIELD_SAMPLES = 192  # samples per ray of the field workload (64 coarse + 2 x 64 proposal, render.py:77-106)
+
+
+def run_field(args):
+    """The NeRF-sampler field kernels (vgf.cu:438-533) on the config-2 scene: a 512x512 view of orbit camera 0,
+    FIELD_SAMPLES sorted samples per ray (the midpoints of equal steps in the sampler's normalised
+    coordinate, render.s_to_t), their nearest sites by walk, then density and colour forward and
+    backward over every sample, each timed by itself (REF_REPS calls) beside the reference's kernels."""
+    from oracle import ref_build
+    from voronoi_gauss_b200 import ext, render, scenes, sites
+    from voronoi_gauss_b200.model import VoronoiGaussField
+    torch.cuda.set_device(0)
+    dev = torch.device('cuda', 0)
+    W = args.width or 512
+    H = args.height or 512
+    gr = load_scene(2, args.sites, 0)
+    prm = scenes.make_params(2, gr['points'].astype(np.float64))
+    model = VoronoiGaussField.from_params(*(torch.from_numpy(gr[k]).to(dev) for k in ('points', 'offsets', 'adj')),
+                                          {k: (v.to(dev) if torch.is_tensor(v) else v) for k, v in prm.items()})
+    centre, o_h, d_h = camera(2, 0, W, H)
+    o, d = o_h.to(dev), d_h.to(dev)
+    B = W * H
+    start = torch.full((B,), int(sites.nearest_sites(gr['points'], centre[None])[0]), dtype=torch.int32, device=dev)
+    bounds = render.ray_bounds(o, d, 0.02, 4.0)
+    s = ((torch.arange(FIELD_SAMPLES, device=dev, dtype=torch.float32) + 0.5) / FIELD_SAMPLES).expand(B, -1)
+    z = render.s_to_t(s.contiguous(), *bounds).contiguous()
+    g = model.graph
+    fx = ext.extension()
+    site, _ = fx.walk(g.points, g.offsets, g.adj, o, d, z, start)
+    x = (o[:, None, :] + z[..., None] * d[:, None, :]).reshape(-1, 3).contiguous()
+    dirs = d[:, None, :].expand(B, FIELD_SAMPLES, 3).reshape(-1, 3).contiguous()
+    site = site.reshape(-1).contiguous()
+    M = x.size(0)
+    gen = torch.Generator().manual_seed(0)
+    g_sigma = torch.randn(M, generator=gen).to(dev)
+    g_rgb = torch.randn(M, 3, generator=gen).to(dev)
+    raw, dls, dq = model.raw.detach(), model.d_log_scale.detach(), model.d_quat.detach()
+    cls, cq, sh = model.c_log_scale.detach(), model.c_quat.detach(), model.sh().detach().contiguous()
+    rgb = fx.color_forward(g.points, g.offsets, g.adj, cls, cq, sh, model.sh_deg, x, dirs, site)
+
+    def calls(m):
+        return {
+            'walk': lambda: m.walk(g.points, g.offsets, g.adj, o, d, z, start),
+            'density_forward': lambda: m.density_forward(g.points, g.offsets, g.adj, raw, dls, dq, x, site, 1.0),
+            'density_backward': lambda: m.density_backward(g.points, g.offsets, g.adj, raw, dls, dq, x, site, g_sigma),
+            'color_forward': lambda: m.color_forward(g.points, g.offsets, g.adj, cls, cq, sh, model.sh_deg, x, dirs,
+                                                     site),
+            'color_backward': lambda: m.color_backward(g.points, g.offsets, g.adj, cls, cq, sh, model.sh_deg, x, dirs,
+                                                       site, rgb, g_rgb),
+        }
+    mine = {k: round(time_reps(f), 3) for k, f in calls(fx).items()}
+    total = sum(mine.values())
+    line = {'metric': f'NeRF-sampler field kernels Msamples/s (walk + density fwd/bwd + colour fwd/bwd), {B} rays x '
+                      f'{FIELD_SAMPLES} samples, {len(gr["points"])} sites', 'value': round(M / (total * 1e-3) / 1e6, 2),
+            'unit': 'Msamples/s', 'n_gpus': 1, 'steps': REF_REPS, 'warmup': 1, 'ms_per_step': round(total, 3),
+            'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
+            'config': {'workload': f'config2 scene (mixture), {W}x{H} view of orbit camera 0, {FIELD_SAMPLES} sorted '
+                                   'samples per ray (render.s_to_t midpoints), cell-major backwards'},
+            'ms': mine}
+    if not args.no_baselines and ref_build.available('vgf_ext'):
+        ref = {k: round(time_reps(f), 3) for k, f in calls(ref_build.load_reference('vgf_ext')).items()}
+        line['reference_ms'] = ref
+        line['speedup_vs_reference'] = {k: round(ref[k] / mine[k], 2) for k in mine}
+    print(json.dumps(line), flush=True)
+
+
 # ---------------------------------------------------------------------------------- reference arm
 
 def run_reference(args):
@@ -936,6 +1006,8 @@ if __name__ == '__main__':
     a = parse()
     if a.impl == 'reference':
         run_reference(a)
+    elif a.field:
+        run_field(a)
     elif a.config == 2:
         run_infer(a)
     elif a.config == 5:
