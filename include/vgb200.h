@@ -93,6 +93,27 @@ int vg_foam_backward(const void* pack, int64_t n_sites, int64_t n_adj, const flo
                      float* g_dA, float* g_cA, float* g_sh, void* workspace, size_t workspace_bytes,
                      void* stream);
 
+/* Training variants of vg_foam_forward / vg_foam_backward with no reference counterpart: the forward
+ * also writes, into `counts` (vg_foam_counts_bytes, int32, caller-owned until the backward), how many of
+ * its recorded samples fall into each cell per pass of the cell-major backward, which the backward then
+ * reads instead of counting the records again. Same arguments and results otherwise; the forward needs
+ * the full vg_foam_workspace_bytes(..., backward = 0) workspace and record_cap > 0, and the backward
+ * must get the records, stats and counts of that forward with the same rays and record_cap. */
+size_t vg_foam_counts_bytes(int64_t n_sites, int64_t n_rays, int record_cap);
+int vg_foam_forward_counted(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA,
+                            const float* cA, const float* sh, int sh_deg, const float* o, const float* d,
+                            const int32_t* start, const float* near, const float* far, int64_t n_rays,
+                            float t_thresh, float w_thresh, int record_cap, float* rgb, float* T, float* depth,
+                            int32_t* stats, float* rec, int32_t* counts, void* workspace, size_t workspace_bytes,
+                            void* stream);
+int vg_foam_backward_counted(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA,
+                             const float* cA, const float* sh, int sh_deg, const float* o, const float* d,
+                             const int32_t* start, const float* near, const float* far, int64_t n_rays,
+                             float t_thresh, float w_thresh, const float* rgb, const float* T, const float* g_rgb,
+                             const float* g_T, const float* rec, int record_cap, const int32_t* stats,
+                             const int32_t* counts, float* g_raw, float* g_dA, float* g_cA, float* g_sh,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
 /* The two halves of vg_foam_backward, for data-parallel training: the gradients of this device's
  * rays are summed into grad_pack (N, 64) float32 (zero-filled first when zero_first != 0; layout
  * g_raw, g_dA[6], 0, g_cA[6], 0, 0, g_sh[48] in packed site order), which can be all-reduced across

@@ -16,6 +16,7 @@ class FakeRender:
 
     def __init__(self):
         self.calls = []
+        self.kwargs = []
 
     def _fwd(self, name, args, B, with_rec, cap):
         self.calls.append((name, args, cap))
@@ -29,7 +30,8 @@ class FakeRender:
             out.append(torch.full((B if cap else 0, cap, 8), 7.0))
         return out
 
-    def foam_forward(self, *args):
+    def foam_forward(self, *args, counts=None):
+        self.kwargs.append(('foam_forward', counts))
         return self._fwd('foam_forward', args, len(args[8]), True, args[-1])
 
     def march_forward(self, *args):
@@ -40,7 +42,8 @@ class FakeRender:
         raw, dA, cA, sh = args[3:7]
         return [torch.full_like(raw, 1.0), torch.full_like(dA, 2.0), torch.full_like(cA, 3.0), torch.full_like(sh, 4.0)]
 
-    def foam_backward(self, *args):
+    def foam_backward(self, *args, counts=None):
+        self.kwargs.append(('foam_backward', counts))
         return self._bwd('foam_backward', args)
 
     def march_backward(self, *args):
@@ -117,6 +120,10 @@ def test_foam_saves_records_and_routes_gradients(fakes):
     assert torch.equal(args[8], o) and torch.equal(args[9], d)  # the same rays reach the backward
     assert bool((raw.grad == 1).all()) and bool((dA.grad == 2).all()) and bool((cA.grad == 3).all())
     assert bool((sh.grad == 4).all())
+    # the recording forward keeps the per-cell sample counts of its records and hands them to its backward
+    (f_name, f_counts), (b_name, b_counts) = render.kwargs[-2], render.kwargs[-1]
+    assert (f_name, b_name) == ('foam_forward', 'foam_backward')
+    assert f_counts is not None and f_counts.dtype == torch.int32 and b_counts is f_counts
 
 
 def test_foam_missing_output_gradient_is_zero(fakes):

@@ -175,3 +175,34 @@ def test_conic_matches_oracle_and_reference():
         inside = (np.abs(z['ls']) < 20).all(1)
         assert rel(ls.grad.cpu().numpy()[inside], z[f'g_ls_{floor}'][inside]) <= 1e-4
         assert rel(q.grad.cpu().numpy(), z[f'g_quat_{floor}']) <= 1e-4
+
+
+@pytest.mark.parametrize('record_cap', [256, 24])
+def test_counted_backward_matches_counting_backward(record_cap):
+    """The forward's kept per-cell sample counts (foam_forward(..., counts=)) replace the backward's
+    counting pass: they sum to the recorded samples of the rays that fit their records (rays with more
+    samples are re-traced and left out), and the gradients equal those of the backward that counts the
+    records itself (up to the order of float atomics)."""
+    ext = _ext()
+    gr, prm, o, d, start, near, far = _config1()
+    g = ext.Graph(cuda(gr['points']), cuda(gr['offsets']), cuda(gr['adj']))
+    dA = ext.conic(cuda(prm['d_log_scale']), cuda(prm['d_quat']))
+    cA = ext.conic(cuda(prm['c_log_scale']), cuda(prm['c_quat']))
+    raw, sh = cuda(prm['raw']), cuda(prm['sh'])
+    rays = [cuda(x) for x in (o, d, start, near, far)]
+    args = (g.points, g.offsets, g.adj, raw, dA, cA, sh, 1, *rays, 1e-4, 1e-4)
+    B = len(o)
+    counts = torch.empty(ext.sample_counts_size(len(gr['points']), B, record_cap), dtype=torch.int32, device='cuda')
+    fx = ext.foam_extension()
+    rgb, T, _, stats, rec = fx.foam_forward(*args, record_cap, counts=counts)
+    S = stats[:, 0].long()
+    fits = S <= record_cap
+    assert int(counts.long().sum()) == int(S[fits].sum())
+    if record_cap == 24:
+        assert int((~fits).sum()) > 0  # some rays overflow their records
+    gen = torch.Generator().manual_seed(5)
+    g_rgb, g_T = torch.randn(B, 3, generator=gen).cuda(), torch.randn(B, generator=gen).cuda()
+    kept = fx.foam_backward(*args, rgb, T, g_rgb, g_T, rec, stats, counts=counts)
+    counted = fx.foam_backward(*args, rgb, T, g_rgb, g_T, rec, stats)
+    for name, a, b in zip(('raw', 'dA', 'cA', 'sh'), kept, counted):
+        assert rel(a.cpu().numpy(), b.cpu().numpy()) <= 1e-5, name

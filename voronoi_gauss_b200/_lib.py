@@ -38,6 +38,11 @@ SIGNATURES = {
                                       P, P]),
     'vg_foam_backward': (I32, [P, I64, I64, P, P, P, P, I32, P, P, P, P, P, I64, F32, F32, P, P, P, P, P, I32, P, P, P,
                                P, P, P, SZ, P]),
+    'vg_foam_counts_bytes': (SZ, [I64, I64, I32]),
+    'vg_foam_forward_counted': (I32, [P, I64, I64, P, P, P, P, I32, P, P, P, P, P, I64, F32, F32, I32, P, P, P, P, P,
+                                      P, P, SZ, P]),
+    'vg_foam_backward_counted': (I32, [P, I64, I64, P, P, P, P, I32, P, P, P, P, P, I64, F32, F32, P, P, P, P, P, I32,
+                                       P, P, P, P, P, P, P, SZ, P]),
     'vg_foam_backward_packed': (I32, [P, I64, I64, P, P, P, P, I32, P, P, P, P, P, I64, F32, F32, P, P, P, P, P, I32,
                                       P, P, I32, P, SZ, P]),
     'vg_grad_unpack': (I32, [P, I64, I64, P, I32, P, P, P, P, P]),

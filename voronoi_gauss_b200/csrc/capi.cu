@@ -159,11 +159,12 @@ size_t vg_foam_workspace_bytes(int64_t n_sites, int sh_deg, int64_t n_rays, int 
     return field_ws(n_sites, sh_deg) + (backward == 1 ? grad_ws(n_sites) : 0) + cm;
 }
 
-int vg_foam_forward(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA,
-                    const float* cA, const float* sh, int sh_deg, const float* o, const float* d,
-                    const int32_t* start, const float* near, const float* far, int64_t n_rays, float t_thresh,
-                    float w_thresh, int record_cap, float* rgb, float* T, float* depth, int32_t* stats, float* rec,
-                    void* workspace, size_t workspace_bytes, void* stream) {
+static int foam_forward_impl(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA,
+                             const float* cA, const float* sh, int sh_deg, const float* o, const float* d,
+                             const int32_t* start, const float* near, const float* far, int64_t n_rays,
+                             float t_thresh, float w_thresh, int record_cap, float* rgb, float* T, float* depth,
+                             int32_t* stats, float* rec, int32_t* counts, void* workspace, size_t workspace_bytes,
+                             void* stream) {
     int rc = check_scene(pack, n_sites, n_adj, raw, dA, cA, sh, sh_deg);
     if (rc) return rc;
     if ((rc = check_rays(n_rays, o, d, start, near, far))) return rc;
@@ -172,9 +173,12 @@ int vg_foam_forward(const void* pack, int64_t n_sites, int64_t n_adj, const floa
     REQUIRE(record_cap == 0 || n_rays == 0 || rec != nullptr, "rec is null with record_cap > 0");
     if ((rc = check_alignment(dA, cA, sh, record_cap > 0 ? rec : nullptr))) return rc;
     REQUIRE(aligned(workspace, 256), "workspace must be 256-byte aligned");
-    const size_t need = field_ws(n_sites, sh_deg);
+    // with counts, the cell-major forward must run (it keeps them): the full workspace is required
+    const size_t need = counts != nullptr ? vg_foam_workspace_bytes(n_sites, sh_deg, n_rays, record_cap, 0)
+                                          : field_ws(n_sites, sh_deg);
     if (workspace_bytes < need || workspace == nullptr)
         return fail(VG_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);
+    REQUIRE(counts == nullptr || record_cap > 0, "sample counts need records (record_cap > 0)");
     if (n_rays == 0) return VG_OK;
     int* status = status_ptr();
     if (status == nullptr) return fail(VG_ERR_CUDA, "status word unavailable");
@@ -184,12 +188,41 @@ int vg_foam_forward(const void* pack, int64_t n_sites, int64_t n_adj, const floa
     if (e != cudaSuccess) return cuda_fail(e, "field pack");
     const vg::FieldView F = vg::field_view(workspace, n_sites, sh_deg);
     const vg::RayView R{o, d, start, near, nullptr, far, n_rays};
-    const vg::FoamCfg c{t_thresh, w_thresh, record_cap};
+    vg::FoamCfg c{t_thresh, w_thresh, record_cap};
+    c.all_count = counts;
     const vg::Outputs out{rgb, T, depth, stats, record_cap > 0 ? rec : nullptr};
     // scratch beyond the field records enables the cell-major colour pass (inline colours otherwise)
     const size_t fw = field_ws(n_sites, sh_deg);
     e = vg::foam_forward(g, F, R, c, out, status, static_cast<char*>(workspace) + fw, workspace_bytes - fw, st);
     return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_foam_forward");
+}
+
+int vg_foam_forward(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA,
+                    const float* cA, const float* sh, int sh_deg, const float* o, const float* d,
+                    const int32_t* start, const float* near, const float* far, int64_t n_rays, float t_thresh,
+                    float w_thresh, int record_cap, float* rgb, float* T, float* depth, int32_t* stats, float* rec,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+    return foam_forward_impl(pack, n_sites, n_adj, raw, dA, cA, sh, sh_deg, o, d, start, near, far, n_rays, t_thresh,
+                             w_thresh, record_cap, rgb, T, depth, stats, rec, nullptr, workspace, workspace_bytes,
+                             stream);
+}
+
+size_t vg_foam_counts_bytes(int64_t n_sites, int64_t n_rays, int record_cap) {
+    if (n_sites <= 0 || n_rays <= 0 || record_cap <= 0) return 0;
+    return 4 * static_cast<size_t>(vg::foam_count_entries(n_sites, n_rays, record_cap));
+}
+
+int vg_foam_forward_counted(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA,
+                            const float* cA, const float* sh, int sh_deg, const float* o, const float* d,
+                            const int32_t* start, const float* near, const float* far, int64_t n_rays,
+                            float t_thresh, float w_thresh, int record_cap, float* rgb, float* T, float* depth,
+                            int32_t* stats, float* rec, int32_t* counts, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+    REQUIRE(n_rays == 0 || counts != nullptr, "counts is null");
+    REQUIRE(aligned(counts, 4), "counts must be 4-byte aligned");
+    return foam_forward_impl(pack, n_sites, n_adj, raw, dA, cA, sh, sh_deg, o, d, start, near, far, n_rays, t_thresh,
+                             w_thresh, record_cap, rgb, T, depth, stats, rec, n_rays ? counts : nullptr, workspace,
+                             workspace_bytes, stream);
 }
 
 static int foam_backward_impl(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA,
@@ -198,7 +231,7 @@ static int foam_backward_impl(const void* pack, int64_t n_sites, int64_t n_adj, 
                               float t_thresh, float w_thresh, const float* rgb, const float* T, const float* g_rgb,
                               const float* g_T, const float* rec, int record_cap, const int32_t* stats, float* grad,
                               bool zero_first, void* workspace, size_t workspace_bytes, size_t need, size_t cm_off,
-                              cudaStream_t st) {
+                              cudaStream_t st, const int32_t* counts = nullptr) {
     int rc = check_scene(pack, n_sites, n_adj, raw, dA, cA, sh, sh_deg);
     if (rc) return rc;
     if ((rc = check_rays(n_rays, o, d, start, near, far))) return rc;
@@ -221,19 +254,21 @@ static int foam_backward_impl(const void* pack, int64_t n_sites, int64_t n_adj, 
     if (e != cudaSuccess) return cuda_fail(e, "field pack");
     const vg::FieldView F = vg::field_view(workspace, n_sites, sh_deg);
     const vg::RayView R{o, d, start, near, nullptr, far, n_rays};
-    const vg::FoamCfg c{t_thresh, w_thresh, record_cap};
+    vg::FoamCfg c{t_thresh, w_thresh, record_cap};
+    c.all_count = record_cap > 0 ? const_cast<int32_t*>(counts) : nullptr;  // read only in the backward
     const vg::GradIn gi{rgb, T, g_rgb, g_T, record_cap > 0 ? rec : nullptr, stats, record_cap};
     void* cm = static_cast<char*>(workspace) + cm_off;
     e = vg::foam_backward(g, F, R, c, gi, grad, status, cm, workspace_bytes - cm_off, st);
     return e == cudaSuccess ? VG_OK : cuda_fail(e, "vg_foam_backward");
 }
 
-int vg_foam_backward(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA,
-                     const float* cA, const float* sh, int sh_deg, const float* o, const float* d,
-                     const int32_t* start, const float* near, const float* far, int64_t n_rays, float t_thresh,
-                     float w_thresh, const float* rgb, const float* T, const float* g_rgb, const float* g_T,
-                     const float* rec, int record_cap, const int32_t* stats, float* g_raw, float* g_dA, float* g_cA,
-                     float* g_sh, void* workspace, size_t workspace_bytes, void* stream) {
+static int foam_backward_unpacked(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA,
+                                  const float* cA, const float* sh, int sh_deg, const float* o, const float* d,
+                                  const int32_t* start, const float* near, const float* far, int64_t n_rays,
+                                  float t_thresh, float w_thresh, const float* rgb, const float* T, const float* g_rgb,
+                                  const float* g_T, const float* rec, int record_cap, const int32_t* stats,
+                                  const int32_t* counts, float* g_raw, float* g_dA, float* g_cA, float* g_sh,
+                                  void* workspace, size_t workspace_bytes, void* stream) {
     REQUIRE(g_raw && g_dA && g_cA && g_sh, "gradient outputs must be non-null");
     REQUIRE(aligned(g_dA, 8) && aligned(g_cA, 8) && aligned(g_sh, 16), "gradient outputs misaligned");
     if (sh_deg < 0 || sh_deg > 3) return fail(VG_ERR_INVALID_ARG, "sh_deg must be in 0..3");
@@ -242,11 +277,35 @@ int vg_foam_backward(const void* pack, int64_t n_sites, int64_t n_adj, const flo
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     int rc = foam_backward_impl(pack, n_sites, n_adj, raw, dA, cA, sh, sh_deg, o, d, start, near, far, n_rays,
                                 t_thresh, w_thresh, rgb, T, g_rgb, g_T, rec, record_cap, stats, grad, true, workspace,
-                                workspace_bytes, need, field_ws(n_sites, sh_deg) + grad_ws(n_sites), st);
+                                workspace_bytes, need, field_ws(n_sites, sh_deg) + grad_ws(n_sites), st, counts);
     if (rc) return rc;
     const cudaError_t e =
         vg::grad_unpack(vg::graph_view(pack, n_sites, n_adj), grad, sh_deg, g_raw, g_dA, g_cA, g_sh, st);
     return e == cudaSuccess ? VG_OK : cuda_fail(e, "gradient unpack");
+}
+
+int vg_foam_backward(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA,
+                     const float* cA, const float* sh, int sh_deg, const float* o, const float* d,
+                     const int32_t* start, const float* near, const float* far, int64_t n_rays, float t_thresh,
+                     float w_thresh, const float* rgb, const float* T, const float* g_rgb, const float* g_T,
+                     const float* rec, int record_cap, const int32_t* stats, float* g_raw, float* g_dA, float* g_cA,
+                     float* g_sh, void* workspace, size_t workspace_bytes, void* stream) {
+    return foam_backward_unpacked(pack, n_sites, n_adj, raw, dA, cA, sh, sh_deg, o, d, start, near, far, n_rays,
+                                  t_thresh, w_thresh, rgb, T, g_rgb, g_T, rec, record_cap, stats, nullptr, g_raw, g_dA,
+                                  g_cA, g_sh, workspace, workspace_bytes, stream);
+}
+
+int vg_foam_backward_counted(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA,
+                             const float* cA, const float* sh, int sh_deg, const float* o, const float* d,
+                             const int32_t* start, const float* near, const float* far, int64_t n_rays,
+                             float t_thresh, float w_thresh, const float* rgb, const float* T, const float* g_rgb,
+                             const float* g_T, const float* rec, int record_cap, const int32_t* stats,
+                             const int32_t* counts, float* g_raw, float* g_dA, float* g_cA, float* g_sh,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+    REQUIRE(n_rays == 0 || record_cap == 0 || counts != nullptr, "counts is null");
+    return foam_backward_unpacked(pack, n_sites, n_adj, raw, dA, cA, sh, sh_deg, o, d, start, near, far, n_rays,
+                                  t_thresh, w_thresh, rgb, T, g_rgb, g_T, rec, record_cap, stats, counts, g_raw, g_dA,
+                                  g_cA, g_sh, workspace, workspace_bytes, stream);
 }
 
 int vg_foam_backward_packed(const void* pack, int64_t n_sites, int64_t n_adj, const float* raw, const float* dA,

@@ -94,12 +94,15 @@ __global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
     if (r >= R.n) return;
     const int K = c.record_cap;
     if (MODE == kImmediateOverflow && __ldg(out.stats + 3 * r) <= K) return;
-    if (MODE == kImmediateOverflow && c.cm_count != nullptr) {
-        // the deferred traversal counted this ray's marked records; it leaves the colour pass
-        int* cnt = c.cm_count + (r / c.cm_rays) * c.cm_stride;
+    if (MODE == kImmediateOverflow && (c.cm_count != nullptr || c.all_count != nullptr)) {
+        // the deferred traversal counted this ray's records; it leaves the cell-major passes
+        int* cnt = c.cm_count != nullptr ? c.cm_count + (r / c.cm_rays) * c.cm_stride : nullptr;
+        int* all = c.all_count != nullptr ? c.all_count + (r / c.cm_rays) * c.cm_stride : nullptr;
         for (int s = 0; s < K; ++s) {
             const float* q = out.rec + (r * K + s) * kRecord;
-            if (q[7] < 0.f) atomicAdd(cnt + __ldg(g.inv + __float_as_int(q[1])), -1);
+            const int cell = __ldg(g.inv + __float_as_int(q[1]));
+            if (cnt != nullptr && q[7] < 0.f) atomicAdd(cnt + cell, -1);
+            if (all != nullptr) atomicAdd(all + cell, -1);
         }
     }
     constexpr bool kDefer = MODE == kDeferred;
@@ -149,6 +152,8 @@ __global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
         if (RECORD) put_record(out.rec, r, K, n_samples - 2, P, has_p, kDefer, p_orig);
         if (kDefer && has_p && n_samples - 2 < K && c.cm_count != nullptr)
             atomicAdd(c.cm_count + (r / c.cm_rays) * c.cm_stride + P.cell, 1);
+        if (kDefer && n_samples - 2 < K && c.all_count != nullptr)
+            atomicAdd(c.all_count + (r / c.cm_rays) * c.cm_stride + P.cell, 1);
         P = Q;
         p_orig = q_orig;
         has_p = has_q;
@@ -159,6 +164,8 @@ __global__ void __launch_bounds__(kBlock, VG_FWD_MINB)
     if (RECORD) put_record(out.rec, r, K, n_samples - 1, P, has_p, kDefer, p_orig);
     if (kDefer && has_p && n_samples - 1 < K && c.cm_count != nullptr)
         atomicAdd(c.cm_count + (r / c.cm_rays) * c.cm_stride + P.cell, 1);
+    if (kDefer && n_samples - 1 < K && c.all_count != nullptr)
+        atomicAdd(c.all_count + (r / c.cm_rays) * c.cm_stride + P.cell, 1);
     if (!kDefer) out.rgb[3 * r] = acc0, out.rgb[3 * r + 1] = acc1, out.rgb[3 * r + 2] = acc2;
     out.T[r] = T;
     out.depth[r] = dep;
@@ -894,6 +901,12 @@ int sm_count() {
 
 }  // namespace
 
+int64_t foam_count_entries(int64_t n_sites, int64_t n_rays, int record_cap) {
+    const CmLayout L = cm_layout(n_sites, n_rays, record_cap, false);
+    if (L.rays_per_pass <= 0) return 0;
+    return (n_rays + L.rays_per_pass - 1) / L.rays_per_pass * (n_sites + 1);
+}
+
 size_t foam_backward_workspace(int64_t n_sites, int64_t n_rays, int record_cap) {
     return cm_layout(n_sites, n_rays, record_cap, true, false).total;
 }
@@ -987,7 +1000,9 @@ cudaError_t forward_deferred(const GraphView& g, const FieldView& F, const RayVi
     {
         // the traversal counts the samples that need a colour per (pass, cell) as it marks them
         const int64_t passes = (R.n + L.rays_per_pass - 1) / L.rays_per_pass;
-        const cudaError_t e = cudaMemsetAsync(count_all, 0, 4 * static_cast<size_t>(g.n + 1) * passes, st);
+        cudaError_t e = cudaMemsetAsync(count_all, 0, 4 * static_cast<size_t>(g.n + 1) * passes, st);
+        if (e == cudaSuccess && cc.all_count != nullptr)
+            e = cudaMemsetAsync(cc.all_count, 0, 4 * static_cast<size_t>(g.n + 1) * passes, st);
         if (e != cudaSuccess) return e;
         cc.cm_count = count_all, cc.cm_rays = L.rays_per_pass, cc.cm_stride = g.n + 1;
     }
@@ -1090,14 +1105,18 @@ cudaError_t foam_backward(const GraphView& g, const FieldView& F, const RayView&
     const int grid = sm_count() * 3;
     for (int64_t r0 = 0; r0 < R.n; r0 += L.rays_per_pass) {
         const int64_t nr = std::min<int64_t>(L.rays_per_pass, R.n - r0);
-        cudaError_t e = cudaMemsetAsync(count, 0, 4 * static_cast<size_t>(n + 1), st);
-        if (e == cudaSuccess) e = cudaMemsetAsync(fill, 0, 4 * static_cast<size_t>(n), st);
+        // samples per cell of this pass: kept by the forward (c.all_count), else counted from the records
+        int* pass_count = c.all_count != nullptr ? c.all_count + (r0 / L.rays_per_pass) * static_cast<int64_t>(n + 1)
+                                                 : count;
+        cudaError_t e = cudaMemsetAsync(fill, 0, 4 * static_cast<size_t>(n), st);
         if (e == cudaSuccess) e = cudaMemsetAsync(counter, 0, 16, st);
+        if (e == cudaSuccess && c.all_count == nullptr) e = cudaMemsetAsync(count, 0, 4 * static_cast<size_t>(n + 1), st);
         if (e != cudaSuccess) return e;
-        const ItemOut io{items, count, r0, nr, offsets, fill};
+        const ItemOut io{items, pass_count, r0, nr, offsets, fill};
         size_t tb = L.temp_bytes;
-        cmf_count_kernel<<<blocks(32 * nr), kBlock, 0, st>>>(gi.rec, gi.stats, g.inv, r0, nr, K, count);
-        e = cub::DeviceScan::ExclusiveSum(b + L.temp, tb, count, offsets, n + 1, st);
+        if (c.all_count == nullptr)
+            cmf_count_kernel<<<blocks(32 * nr), kBlock, 0, st>>>(gi.rec, gi.stats, g.inv, r0, nr, K, count);
+        e = cub::DeviceScan::ExclusiveSum(b + L.temp, tb, pass_count, offsets, n + 1, st);
         if (e != cudaSuccess) return e;
         {
             ProfScope ps(kProfReplay, st);

@@ -214,6 +214,10 @@ struct FoamCfg {
     int* cm_count = nullptr;
     int64_t cm_rays = 1;
     int cm_stride = 0;
+    // per-pass counts of every recorded sample of the fully recorded rays, all_count[pass * (N + 1) + cell]
+    // (the backward's item buckets): filled by the deferred forward, read by the backward instead of
+    // counting the records again (null: not kept)
+    int* all_count = nullptr;
 };
 
 struct MarchCfg {
@@ -262,6 +266,8 @@ cudaError_t foam_forward(const GraphView& g, const FieldView& F, const RayView& 
                          const Outputs& out, int* status, void* cm_ws, size_t cm_bytes, cudaStream_t st);
 // Scratch of the cell-major backward (rays fully recorded in records of capacity record_cap).
 size_t foam_backward_workspace(int64_t n_sites, int64_t n_rays, int record_cap);
+// int32 entries of FoamCfg::all_count for a call of n_rays rays with records of capacity record_cap
+int64_t foam_count_entries(int64_t n_sites, int64_t n_rays, int record_cap);
 cudaError_t foam_backward(const GraphView& g, const FieldView& F, const RayView& R, const FoamCfg& c,
                           const GradIn& gi, float* grad, int* status, void* cm_ws, size_t cm_bytes, cudaStream_t st);
 

@@ -167,6 +167,11 @@ def _workspace(n, sh_deg, backward, dev, n_rays=0, record_cap=0):
     return torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev), nbytes
 
 
+def sample_counts_size(n_sites, n_rays, record_cap):
+    """int32 entries of the per-cell sample counts that foam_forward(..., counts=) keeps for the backward."""
+    return _lib.lib().vg_foam_counts_bytes(int(n_sites), int(n_rays), int(record_cap)) // 4
+
+
 def _sh_deg(sh_deg):
     if not 0 <= int(sh_deg) <= 3:
         raise RuntimeError('sh_deg must be in 0..3')
@@ -178,7 +183,9 @@ class FoamExtension:
 
     @staticmethod
     def foam_forward(points, offsets, adj, raw, dA, cA, sh, sh_deg, o, d, start, near, far, t_thresh, w_thresh,
-                     record_cap):
+                     record_cap, counts=None):
+        """counts (optional, int32 of sample_counts_size entries): also keep the per-cell sample counts of the
+        records for foam_backward(..., counts=) (vg_foam_forward_counted)."""
         _scene_checks(points, offsets, adj, raw, dA, cA, sh)
         B = _ray_checks(o=o, d=d, start=start, near=near, far=far)
         sh_deg, K = _sh_deg(sh_deg), int(record_cap)
@@ -194,16 +201,24 @@ class FoamExtension:
             return [rgb, T, depth, stats, rec]
         pk = graph_pack(points, offsets, adj)
         ws, nbytes = _workspace(pk.n, sh_deg, 0, dev, B, K)
+        args = [pk.ptr, pk.n, pk.m, raw.data_ptr(), dA.data_ptr(), cA.data_ptr(), sh.data_ptr(), sh_deg, o.data_ptr(),
+                d.data_ptr(), start.data_ptr(), near.data_ptr(), far.data_ptr(), B, float(t_thresh), float(w_thresh),
+                K, rgb.data_ptr(), T.data_ptr(), depth.data_ptr(), stats.data_ptr(), _ptr(rec)]
         with torch.cuda.device(dev):
-            _lib.call('vg_foam_forward', pk.ptr, pk.n, pk.m, raw.data_ptr(), dA.data_ptr(), cA.data_ptr(),
-                      sh.data_ptr(), sh_deg, o.data_ptr(), d.data_ptr(), start.data_ptr(), near.data_ptr(),
-                      far.data_ptr(), B, float(t_thresh), float(w_thresh), K, rgb.data_ptr(), T.data_ptr(),
-                      depth.data_ptr(), stats.data_ptr(), _ptr(rec), ws.data_ptr(), nbytes, _stream(dev))
+            if counts is not None and K > 0:
+                if counts.dtype != torch.int32 or not counts.is_contiguous() or \
+                        counts.numel() < sample_counts_size(pk.n, B, K):
+                    raise RuntimeError('counts must be a contiguous int32 tensor of sample_counts_size entries')
+                _lib.call('vg_foam_forward_counted', *args, counts.data_ptr(), ws.data_ptr(), nbytes, _stream(dev))
+            else:
+                _lib.call('vg_foam_forward', *args, ws.data_ptr(), nbytes, _stream(dev))
         return [rgb, T, depth, stats, rec]
 
     @staticmethod
     def foam_backward(points, offsets, adj, raw, dA, cA, sh, sh_deg, o, d, start, near, far, t_thresh, w_thresh,
-                      rgb, T, g_rgb, g_T, rec, stats):
+                      rgb, T, g_rgb, g_T, rec, stats, counts=None):
+        """counts: the per-cell sample counts kept by foam_forward(..., counts=) for these records
+        (vg_foam_backward_counted), so the records are not counted again."""
         _scene_checks(points, offsets, adj, raw, dA, cA, sh)
         B = _ray_checks(o=o, d=d, start=start, near=near, far=far)
         for x, name, dt in ((rgb, 'rgb', torch.float32), (T, 'T', torch.float32), (g_rgb, 'g_rgb', torch.float32),
@@ -218,12 +233,17 @@ class FoamExtension:
         g_raw, g_dA, g_cA, g_sh = (torch.empty_like(x) for x in (raw, dA, cA, sh))
         pk = graph_pack(points, offsets, adj)
         ws, nbytes = _workspace(pk.n, sh_deg, 1, dev, B, rec.size(1) if replay else 0)
+        head = [pk.ptr, pk.n, pk.m, raw.data_ptr(), dA.data_ptr(), cA.data_ptr(), sh.data_ptr(), sh_deg, _ptr(o),
+                _ptr(d), _ptr(start), _ptr(near), _ptr(far), B, float(t_thresh), float(w_thresh), _ptr(rgb), _ptr(T),
+                _ptr(g_rgb), _ptr(g_T), _ptr(rec) if replay else None, rec.size(1) if replay else 0, _ptr(stats)]
+        tail = [g_raw.data_ptr(), g_dA.data_ptr(), g_cA.data_ptr(), g_sh.data_ptr(), ws.data_ptr(), nbytes, _stream(dev)]
         with torch.cuda.device(dev):
-            _lib.call('vg_foam_backward', pk.ptr, pk.n, pk.m, raw.data_ptr(), dA.data_ptr(), cA.data_ptr(),
-                      sh.data_ptr(), sh_deg, _ptr(o), _ptr(d), _ptr(start), _ptr(near), _ptr(far), B,
-                      float(t_thresh), float(w_thresh), _ptr(rgb), _ptr(T), _ptr(g_rgb), _ptr(g_T),
-                      _ptr(rec) if replay else None, rec.size(1) if replay else 0, _ptr(stats), g_raw.data_ptr(),
-                      g_dA.data_ptr(), g_cA.data_ptr(), g_sh.data_ptr(), ws.data_ptr(), nbytes, _stream(dev))
+            if counts is not None and replay:
+                if counts.numel() < sample_counts_size(pk.n, B, rec.size(1)):
+                    raise RuntimeError('counts does not match the records')
+                _lib.call('vg_foam_backward_counted', *head, counts.data_ptr(), *tail)
+            else:
+                _lib.call('vg_foam_backward', *head, *tail)
         return [g_raw, g_dA, g_cA, g_sh]
 
 
@@ -657,18 +677,26 @@ class _FoamOp(_RenderOp):
 
     def run(self, raw, dA, cA, sh, record_cap=None):
         cap = self.record_cap if record_cap is None else record_cap
-        return foam_extension().foam_forward(*self.scene(), raw, dA, cA, sh, self.sh_deg, *self.rays, *self.settings,
-                                             cap)
+        B = self.rays[0].size(0)
+        # a recording (training) forward also keeps the per-cell sample counts of its records, which its
+        # backward reads instead of counting the records again
+        counts = None
+        if cap > 0 and B > 0:
+            counts = torch.empty(sample_counts_size(self.graph.points.size(0), B, cap), dtype=torch.int32,
+                                 device=raw.device)
+        out = foam_extension().foam_forward(*self.scene(), raw, dA, cA, sh, self.sh_deg, *self.rays, *self.settings,
+                                            cap, counts=counts)
+        return [*out, counts if counts is not None else out[3].new_empty(0)]
 
     def needs(self, outputs):
-        rgb, T, _, stats, rec = outputs
-        return (rgb, T, rec, stats, *self.rays)
+        rgb, T, _, stats, rec, counts = outputs
+        return (rgb, T, rec, stats, counts, *self.rays)
 
     def grads(self, inputs, kept, grads):
-        rgb, T, rec, stats, *rays = kept
+        rgb, T, rec, stats, counts, *rays = kept
         return foam_extension().foam_backward(*self.scene(), *inputs, self.sh_deg, *rays, *self.settings, rgb, T,
                                               _grad_or_zeros(grads[0], rgb), _grad_or_zeros(grads[1], T), rec,
-                                              stats)
+                                              stats, counts=counts if counts.numel() else None)
 
 
 class _MarchOp(_RenderOp):
