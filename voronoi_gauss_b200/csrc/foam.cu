@@ -62,17 +62,30 @@ __device__ __forceinline__ void put_record(float* __restrict__ rec, int64_t r, i
                     : make_float4(P.C1, P.C2, P.mmin, has_c ? P.inv_a : 0.f);
 }
 
-__device__ __forceinline__ void get_record(const float* __restrict__ rec, int64_t r, int K, int s,
-                                            const float (&o)[3], const float (&d)[3], const int* __restrict__ inv,
-                                            Sample& P, bool& has_c) {
-    const float4* q = reinterpret_cast<const float4*>(rec + (r * K + s) * kRecord);
-    const float4 a = __ldg(q), b = __ldg(q + 1);
+// The two float4 of record s of ray r.
+__device__ __forceinline__ void load_record(const float* __restrict__ rec, int64_t r, int K, int s, float4 (&q)[2]) {
+    const float4* p = reinterpret_cast<const float4*>(rec + (r * K + s) * kRecord);
+    q[0] = __ldg(p), q[1] = __ldg(p + 1);
+}
+
+// A sample from its record's two float4.
+__device__ __forceinline__ void decode_record(const float4 (&q)[2], const float (&o)[3], const float (&d)[3],
+                                              const int* __restrict__ inv, Sample& P, bool& has_c) {
+    const float4 a = q[0], b = q[1];
     P.t = a.x;
     P.x0 = along(o[0], P.t, d[0]), P.x1 = along(o[1], P.t, d[1]), P.x2 = along(o[2], P.t, d[2]);
     P.cell = __ldg(inv + __float_as_int(a.y));
     P.sigma = a.z;
     P.C0 = a.w, P.C1 = b.x, P.C2 = b.y, P.mmin = b.z, P.inv_a = b.w;
     has_c = P.inv_a > 0.f;
+}
+
+__device__ __forceinline__ void get_record(const float* __restrict__ rec, int64_t r, int K, int s,
+                                           const float (&o)[3], const float (&d)[3], const int* __restrict__ inv,
+                                           Sample& P, bool& has_c) {
+    float4 q[2];
+    load_record(rec, r, K, s, q);
+    decode_record(q, o, d, inv, P, has_c);
 }
 
 __device__ __forceinline__ void load_ray(const RayView& R, int64_t r, float (&o)[3], float (&d)[3], float& near,
@@ -335,41 +348,15 @@ __global__ void __launch_bounds__(kBlock)
     rgb[3 * r] = acc0, rgb[3 * r + 1] = acc1, rgb[3 * r + 2] = acc2;
 }
 
-// Per-sample item of the cell-major backward, written by the replay and consumed by cm_scatter_kernel:
-// 64 bytes at the sample's place in its cell's bucket,
+// Per-sample item of the cell-major backward, written by the replay (replay_items_kernel) and consumed by
+// cm_scatter_kernel: 64 bytes at the sample's place in its cell's bucket,
 //   (x, gs) | (gC, gC . C) | (m_min, 1 / sum of colour weights or 0, 0, 0) | (d, 0)
-// where every recorded sample gets an item (zero gradients for the samples that have none). The store of
-// an item waits one sample (DirectItems::put writes the previous one) so that the atomic that reserves
-// its place completes while the replay computes the next sample.
-struct DirectItems {
-    float4* items;
-    const int* offsets;
-    int* fill;
-    float4 a, b, c, d;
-    int64_t pos = -1;
-    __device__ __forceinline__ void flush() {
-        if (pos < 0) return;
-        float4* it = items + 4 * pos;
-        it[0] = a, it[1] = b, it[2] = c, it[3] = d;
-    }
-    __device__ __forceinline__ void put(const Sample& P, float gs, float gC0, float gC1, float gC2, bool has_c,
-                                        const float (&dir)[3]) {
-        const bool do_c = has_c && (gC0 != 0.f || gC1 != 0.f || gC2 != 0.f);
-        const int64_t next_pos = __ldg(offsets + P.cell) + atomicAdd(fill + P.cell, 1);
-        flush();
-        const float gCC = do_c ? gC0 * P.C0 + gC1 * P.C1 + gC2 * P.C2 : 0.f;
-        a = make_float4(P.x0, P.x1, P.x2, gs);
-        b = make_float4(do_c ? gC0 : 0.f, do_c ? gC1 : 0.f, do_c ? gC2 : 0.f, gCC);
-        c = make_float4(P.mmin, do_c ? P.inv_a : 0.f, 0.f, 0.f);
-        d = make_float4(dir[0], dir[1], dir[2], 0.f);
-        pos = next_pos;
-    }
-};
+// where every recorded sample gets an item (zero gradients for the samples that have none).
 
-// What the replay does with each sample's gradients: scatter them to the sites of its neighbourhood
-// (every ray, or only the rays that were not recorded in full), or write them as items of the
-// cell-major backward (only fully recorded rays).
-enum BwdMode { kScatterAll = 0, kScatterRetraced = 1, kItems = 2 };
+// What the per-ray backward does: scatter each sample's gradients to the sites of its neighbourhood, for
+// every ray or only for the rays that were not recorded in full (the fully recorded ones go through
+// replay_items_kernel and the cell-major scatter).
+enum BwdMode { kScatterAll = 0, kScatterRetraced = 1 };
 
 struct ItemOut {
     float4* items;         // the bucketed items
@@ -383,13 +370,12 @@ struct ItemOut {
 template <int MODE>
 __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
     foam_backward_kernel(GraphView g, FieldView F, RayView R, FoamCfg c, GradIn gi, float* __restrict__ grad,
-                         ItemOut io, int* status) {
-    const int64_t r = (MODE == kItems ? io.r0 : 0) + static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
-    if (r >= (MODE == kItems ? io.r0 + io.n : R.n)) return;
+                         int* status) {
+    const int64_t r = static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
+    if (r >= R.n) return;
     {
         const int K_ = gi.record_cap;
         const bool replayable = gi.rec != nullptr && K_ > 0 && __ldg(gi.stats + 3 * r) <= K_;
-        if (MODE == kItems && !replayable) return;
         if (MODE == kScatterRetraced && replayable) return;
     }
     float o[3], d[3], near, far;
@@ -417,8 +403,6 @@ __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
     }
     float T = 1.f, acc0 = 0.f, acc1 = 0.f, acc2 = 0.f;
     float carry_sigma = 0.f, gP0 = 0.f, gP1 = 0.f, gP2 = 0.f;  // gradients of P from the segment before it
-    DirectItems out_items{io.items, io.offsets, io.fill};
-    int n_done = 0;  // index of P
     for (int it = 0; it < kMaxCells; ++it) {
         Sample Q;
         bool last, has_q = true;
@@ -451,34 +435,130 @@ __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
         g_opacity = delta * (g_opacity - tail_grad);
         const float h0 = active ? 0.5f * w * gR0 : 0.f, h1 = active ? 0.5f * w * gR1 : 0.f,
                     h2 = active ? 0.5f * w * gR2 : 0.f;
-        if (MODE == kItems)
-            out_items.put(P, carry_sigma + 0.5f * g_opacity, gP0 + h0, gP1 + h1, gP2 + h2, has_p, d);
-        else
-            sample_grads(g, F, P, carry_sigma + 0.5f * g_opacity, gP0 + h0, gP1 + h1, gP2 + h2, has_p, b, grad);
+        sample_grads(g, F, P, carry_sigma + 0.5f * g_opacity, gP0 + h0, gP1 + h1, gP2 + h2, has_p, b, grad);
         carry_sigma = 0.5f * g_opacity;
         gP0 = h0, gP1 = h1, gP2 = h2;
         T = T_after;
         P = Q;
         has_p = has_q;
         t_exit = t_exit_q, next = next_q;
-        n_done = it + 1;
         if (last || T < c.t_thresh) break;
     }
-    if (MODE == kItems) {
-        out_items.put(P, carry_sigma, gP0, gP1, gP2, has_p, d);
-        // every recorded sample was counted into its bucket: fill the places of any the replay did not
-        // reach with zero-gradient items (the replay follows the forward, so normally there are none)
-        for (int s = n_done + 1; s < n_stored; ++s) {
-            Sample Z;
-            bool has_z;
-            get_record(gi.rec, r, K, s, o, d, g.inv, Z, has_z);
-            out_items.put(Z, 0.f, 0.f, 0.f, 0.f, false, d);
-        }
-        out_items.flush();
-    } else {
-        sample_grads(g, F, P, carry_sigma, gP0, gP1, gP2, has_p, b, grad);
-    }
+    sample_grads(g, F, P, carry_sigma, gP0, gP1, gP2, has_p, b, grad);
     if (err) atomicOr(status, err);
+}
+
+// The replay of a fully recorded ray into 64-byte items of its samples' cell buckets (foam_backward_kernel's
+// arithmetic, items instead of atomics). A record is loaded one segment before it is decoded, and a
+// sample's place in its bucket (the fill cursor's ticket) is taken when its record is decoded, one
+// segment before its item is written, so both round trips overlap a segment's arithmetic. The loop is
+// unrolled in pairs with the two samples (and their record buffers) trading the roles P and Q, so no
+// value still in flight is copied between registers.
+struct Ticketed {
+    Sample S;
+    bool has_c;
+    int base, tick;  // first position of the sample's cell bucket, the sample's ticket in it
+    float4 raw[2];   // the next record this slot decodes
+};
+
+__device__ __forceinline__ void replay_decode(const GradIn& gi, const ItemOut& io, const GraphView& g, int64_t r,
+                                              int K, int s, const float (&o)[3], const float (&d)[3], Ticketed& X) {
+    get_record(gi.rec, r, K, s, o, d, g.inv, X.S, X.has_c);
+    X.base = __ldg(io.offsets + X.S.cell);
+    X.tick = atomicAdd(io.fill + X.S.cell, 1);
+}
+
+// decodes the record already loaded into X.raw
+__device__ __forceinline__ void replay_decode_loaded(const ItemOut& io, const GraphView& g, const float (&o)[3],
+                                                     const float (&d)[3], Ticketed& X) {
+    decode_record(X.raw, o, d, g.inv, X.S, X.has_c);
+    X.base = __ldg(io.offsets + X.S.cell);
+    X.tick = atomicAdd(io.fill + X.S.cell, 1);
+}
+
+__device__ __forceinline__ void replay_put(float4* __restrict__ items, const Ticketed& X, float gs, float gC0,
+                                           float gC1, float gC2, bool has_c, const float (&dir)[3]) {
+    const Sample& P = X.S;
+    const bool do_c = has_c && (gC0 != 0.f || gC1 != 0.f || gC2 != 0.f);
+    const float gCC = do_c ? gC0 * P.C0 + gC1 * P.C1 + gC2 * P.C2 : 0.f;
+    float4* it = items + 4 * static_cast<int64_t>(X.base + X.tick);
+    it[0] = make_float4(P.x0, P.x1, P.x2, gs);
+    it[1] = make_float4(do_c ? gC0 : 0.f, do_c ? gC1 : 0.f, do_c ? gC2 : 0.f, gCC);
+    it[2] = make_float4(P.mmin, do_c ? P.inv_a : 0.f, 0.f, 0.f);
+    it[3] = make_float4(dir[0], dir[1], dir[2], 0.f);
+}
+
+__global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
+    replay_items_kernel(GraphView g, FieldView F, RayView R, FoamCfg c, GradIn gi, ItemOut io) {
+    const int64_t r = io.r0 + static_cast<int64_t>(blockIdx.x) * kBlock + threadIdx.x;
+    if (r >= io.r0 + io.n) return;
+    const int K = gi.record_cap;
+    const int n_stored = __ldg(gi.stats + 3 * r);
+    if (gi.rec == nullptr || K <= 0 || n_stored > K || n_stored <= 0) return;
+    float o[3], d[3], near, far;
+    load_ray(R, r, o, d, near, far);
+    float b[16];
+    sh_basis(d[0], d[1], d[2], F.sh_deg, b);
+    const float gR0 = __ldg(gi.g_rgb + 3 * r), gR1 = __ldg(gi.g_rgb + 3 * r + 1), gR2 = __ldg(gi.g_rgb + 3 * r + 2);
+    const float fg0 = __ldg(gi.rgb + 3 * r), fg1 = __ldg(gi.rgb + 3 * r + 1), fg2 = __ldg(gi.rgb + 3 * r + 2);
+    const float tail_grad = __ldg(gi.g_T + r) * __ldg(gi.T + r);
+    float T = 1.f, acc0 = 0.f, acc1 = 0.f, acc2 = 0.f;
+    float carry_sigma = 0.f, gP0 = 0.f, gP1 = 0.f, gP2 = 0.f;  // gradients of P from the segment before it
+    // segment k between P (record k) and Q (record k + 1, decoded here); writes P's item; false when the
+    // replay ends after it
+    auto segment = [&](Ticketed& P, Ticketed& Q, int k) -> bool {
+        replay_decode_loaded(io, g, o, d, Q);                                  // record k + 1
+        if (k + 2 < n_stored) load_record(gi.rec, r, K, k + 2, P.raw);          // P's slot decodes it next
+        const bool last = k + 2 >= n_stored;
+        const float delta = Q.S.t - P.S.t;
+        const float alpha = 1.f - __expf(-0.5f * (P.S.sigma + Q.S.sigma) * delta);
+        const float w = T * alpha;
+        const float T_after = T * (1.f - alpha);
+        const bool active = w > c.w_thresh;
+        float c0 = 0.f, c1 = 0.f, c2 = 0.f;
+        if (active) {
+            // colours of records written without them (foam.cu:443-445)
+            if (!P.has_c) eval_color(g, F, b, P.S), P.has_c = true;
+            if (!Q.has_c) eval_color(g, F, b, Q.S), Q.has_c = true;
+            c0 = 0.5f * (P.S.C0 + Q.S.C0), c1 = 0.5f * (P.S.C1 + Q.S.C1), c2 = 0.5f * (P.S.C2 + Q.S.C2);
+            acc0 += w * c0, acc1 += w * c1, acc2 += w * c2;
+        }
+        float g_opacity = gR0 * (T_after * c0 - (fg0 - acc0)) + gR1 * (T_after * c1 - (fg1 - acc1)) +
+                          gR2 * (T_after * c2 - (fg2 - acc2));
+        g_opacity = delta * (g_opacity - tail_grad);
+        const float h0 = active ? 0.5f * w * gR0 : 0.f, h1 = active ? 0.5f * w * gR1 : 0.f,
+                    h2 = active ? 0.5f * w * gR2 : 0.f;
+        replay_put(io.items, P, carry_sigma + 0.5f * g_opacity, gP0 + h0, gP1 + h1, gP2 + h2, P.has_c, d);
+        carry_sigma = 0.5f * g_opacity;
+        gP0 = h0, gP1 = h1, gP2 = h2;
+        T = T_after;
+        return !(last || T < c.t_thresh);
+    };
+    Ticketed X0, X1;
+    replay_decode(gi, io, g, r, K, 0, o, d, X0);
+    if (n_stored > 1) load_record(gi.rec, r, K, 1, X1.raw);
+    int k = 0;          // segments done; the current P is record k
+    bool p_is_1 = false;  // whether the current P is X1
+    for (;;) {
+        if (k + 1 >= n_stored || k >= kMaxCells) break;
+        const bool go = segment(X0, X1, k);
+        ++k, p_is_1 = true;
+        if (!go || k + 1 >= n_stored || k >= kMaxCells) break;
+        const bool go2 = segment(X1, X0, k);
+        ++k, p_is_1 = false;
+        if (!go2) break;
+    }
+    if (p_is_1)
+        replay_put(io.items, X1, carry_sigma, gP0, gP1, gP2, X1.has_c, d);
+    else
+        replay_put(io.items, X0, carry_sigma, gP0, gP1, gP2, X0.has_c, d);
+    // every recorded sample was counted into its bucket: fill the places of any the replay did not reach
+    // with zero-gradient items (the replay follows the forward, so normally there are none)
+    for (int s2 = k + 1; s2 < n_stored; ++s2) {
+        Ticketed Z;
+        replay_decode(gi, io, g, r, K, s2, o, d, Z);
+        replay_put(io.items, Z, 0.f, 0.f, 0.f, 0.f, false, d);
+    }
 }
 
 // ----------------------------------------------------------------------------- cell-major scatter
@@ -1086,14 +1166,13 @@ cudaError_t foam_backward(const GraphView& g, const FieldView& F, const RayView&
     if (R.n == 0) return cudaSuccess;
     const int K = gi.record_cap;
     const CmLayout L = cm_layout(g.n, R.n, K, true, false);
-    const ItemOut none{nullptr, nullptr, 0, 0, nullptr, nullptr};
     if (gi.rec == nullptr || K <= 0 || cm_ws == nullptr || cm_bytes < L.total ||
         L.total == 0) {
-        foam_backward_kernel<kScatterAll><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, gi, grad, none, status);
+        foam_backward_kernel<kScatterAll><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, gi, grad, status);
         return cudaGetLastError();
     }
     // rays with more samples than records: re-traced and scattered per ray
-    foam_backward_kernel<kScatterRetraced><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, gi, grad, none, status);
+    foam_backward_kernel<kScatterRetraced><<<blocks(R.n), kBlock, 0, st>>>(g, F, R, c, gi, grad, status);
     char* b = static_cast<char*>(cm_ws);
     float4* items = reinterpret_cast<float4*>(b + L.items);
     int* count = reinterpret_cast<int*>(b + L.count);
@@ -1120,7 +1199,7 @@ cudaError_t foam_backward(const GraphView& g, const FieldView& F, const RayView&
         if (e != cudaSuccess) return e;
         {
             ProfScope ps(kProfReplay, st);
-            foam_backward_kernel<kItems><<<blocks(nr), kBlock, 0, st>>>(g, F, R, c, gi, grad, io, status);
+            replay_items_kernel<<<blocks(nr), kBlock, 0, st>>>(g, F, R, c, gi, io);
         }
         cm_chunks_kernel<<<blocks(n), kBlock, 0, st>>>(offsets, n, chunks, counter);
         ProfScope ps(kProfScatter, st);
