@@ -141,28 +141,42 @@ __global__ void __launch_bounds__(kBlock)
     }
 }
 
+// Zeroes the components of a float4 row v of SH coefficients at or beyond nc.
+__device__ __forceinline__ float4 sh_row_masked(float4 x, int v, int nc) {
+    if (4 * v + 0 >= nc) x.x = 0.f;
+    if (4 * v + 1 >= nc) x.y = 0.f;
+    if (4 * v + 2 >= nc) x.z = 0.f;
+    if (4 * v + 3 >= nc) x.w = 0.f;
+    return x;
+}
+
+// Site records and SH rows in internal (Morton) order. The conic part is one thread per site; the SH rows
+// (s4 float4 per site, 48 floats per site in the parameter) are copied by the whole warp over its 32 sites
+// row after row, so every load and store instruction moves contiguous 16-byte pieces.
 __global__ void __launch_bounds__(kBlock)
     field_kernel(const int* __restrict__ perm, int n, const float* __restrict__ raw, const float* __restrict__ dA,
                  const float* __restrict__ cA, const float* __restrict__ sh, int nc, int s4, float4* __restrict__ rec,
                  float4* __restrict__ shp) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const int64_t o = perm[i];
-    const float2* a = reinterpret_cast<const float2*>(dA + 6 * o);
-    const float2* c = reinterpret_cast<const float2*>(cA + 6 * o);
-    const float2 a0 = a[0], a1 = a[1], a2 = a[2], c0 = c[0], c1 = c[1], c2 = c[2];
-    float4* r = rec + 4 * static_cast<int64_t>(i);
-    r[0] = make_float4(a0.x, a0.y, a1.x, a1.y);
-    r[1] = make_float4(a2.x, a2.y, fminf(raw[o], 30.f), 0.f);
-    r[2] = make_float4(c0.x, c0.y, c1.x, c1.y);
-    r[3] = make_float4(c2.x, c2.y, 0.f, 0.f);
-    const float* s = sh + 48 * o;
-    float4* q = shp + static_cast<int64_t>(s4) * i;
-    for (int v = 0; v < s4; ++v) {
-        float f[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) f[u] = 4 * v + u < nc ? s[4 * v + u] : 0.f;
-        q[v] = make_float4(f[0], f[1], f[2], f[3]);
+    const int lane = threadIdx.x & 31, i0 = i - lane;
+    if (i0 >= n) return;  // whole warp
+    const int64_t o = i < n ? perm[i] : 0;
+    if (i < n) {
+        const float2* a = reinterpret_cast<const float2*>(dA + 6 * o);
+        const float2* c = reinterpret_cast<const float2*>(cA + 6 * o);
+        const float2 a0 = a[0], a1 = a[1], a2 = a[2], c0 = c[0], c1 = c[1], c2 = c[2];
+        float4* r = rec + 4 * static_cast<int64_t>(i);
+        r[0] = make_float4(a0.x, a0.y, a1.x, a1.y);
+        r[1] = make_float4(a2.x, a2.y, fminf(raw[o], 30.f), 0.f);
+        r[2] = make_float4(c0.x, c0.y, c1.x, c1.y);
+        r[3] = make_float4(c2.x, c2.y, 0.f, 0.f);
+    }
+    const float4* sh4 = reinterpret_cast<const float4*>(sh);
+    const int sites = min(32, n - i0), total = sites * s4;
+    for (int f = lane; f < 32 * s4; f += 32) {  // warp-uniform trip count
+        const int site = f / s4, v = f - site * s4;
+        const int64_t os = __shfl_sync(0xffffffffu, o, site & 31);
+        if (f < total) shp[static_cast<int64_t>(s4) * i0 + f] = sh_row_masked(__ldg(sh4 + 12 * os + v), v, nc);
     }
 }
 
@@ -171,24 +185,27 @@ __global__ void __launch_bounds__(kBlock)
                   float* __restrict__ g_raw, float* __restrict__ g_dA, float* __restrict__ g_cA,
                   float* __restrict__ g_sh) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const int64_t o = perm[i];
-    const float4* G = grad + (kGradStride / 4) * static_cast<int64_t>(i);
-    const float4 d0 = G[0], d1 = G[1], c0 = G[2], c1 = G[3];
-    g_raw[o] = d0.x;
-    float2* a = reinterpret_cast<float2*>(g_dA + 6 * o);
-    a[0] = make_float2(d0.y, d0.z), a[1] = make_float2(d0.w, d1.x), a[2] = make_float2(d1.y, d1.z);
-    float2* c = reinterpret_cast<float2*>(g_cA + 6 * o);
-    c[0] = make_float2(c0.x, c0.y), c[1] = make_float2(c0.z, c0.w), c[2] = make_float2(c1.x, c1.y);
-    float4* s = reinterpret_cast<float4*>(g_sh + 48 * o);
-#pragma unroll
-    for (int v = 0; v < 12; ++v) {
-        float4 x = G[4 + v];
-        if (4 * v + 0 >= nc) x.x = 0.f;
-        if (4 * v + 1 >= nc) x.y = 0.f;
-        if (4 * v + 2 >= nc) x.z = 0.f;
-        if (4 * v + 3 >= nc) x.w = 0.f;
-        s[v] = x;
+    const int lane = threadIdx.x & 31, i0 = i - lane;
+    if (i0 >= n) return;  // whole warp
+    const int64_t o = i < n ? perm[i] : 0;
+    if (i < n) {
+        const float4* G = grad + (kGradStride / 4) * static_cast<int64_t>(i);
+        const float4 d0 = G[0], d1 = G[1], c0 = G[2], c1 = G[3];
+        g_raw[o] = d0.x;
+        float2* a = reinterpret_cast<float2*>(g_dA + 6 * o);
+        a[0] = make_float2(d0.y, d0.z), a[1] = make_float2(d0.w, d1.x), a[2] = make_float2(d1.y, d1.z);
+        float2* c = reinterpret_cast<float2*>(g_cA + 6 * o);
+        c[0] = make_float2(c0.x, c0.y), c[1] = make_float2(c0.z, c0.w), c[2] = make_float2(c1.x, c1.y);
+    }
+    // the 12 SH-gradient rows of the warp's 32 sites, row after row by the whole warp (contiguous 16-byte
+    // pieces per instruction on both sides)
+    float4* s4 = reinterpret_cast<float4*>(g_sh);
+    const int sites = min(32, n - i0), total = sites * 12;
+    for (int f = lane; f < 32 * 12; f += 32) {  // warp-uniform trip count
+        const int site = f / 12, v = f - site * 12;
+        const int64_t os = __shfl_sync(0xffffffffu, o, site & 31);
+        if (f < total)
+            s4[12 * os + v] = sh_row_masked(grad[(kGradStride / 4) * static_cast<int64_t>(i0 + site) + 4 + v], v, nc);
     }
 }
 
