@@ -47,7 +47,9 @@ const char* vg_last_error(void);
 
 /* Bits of the status word accumulated by the render launches since the last vg_status_reset():
  * 1 = a greedy walk hit its 4096-step cap, 2 = a ray hit the 8192-cell cap, 4 = a start or sample site
- * outside [0, N) was skipped. Synchronises the device. */
+ * outside [0, N) was skipped, 8 = the per-cell counts given to vg_foam_backward_counted do not belong to
+ * its records (samples that found no place in their cell's bucket, or a whole pass whose buckets do not
+ * fit the item buffer, were left out of the gradients). Synchronises the device. */
 int vg_status(int* bits);
 int vg_status_reset(void);
 

@@ -206,3 +206,41 @@ def test_counted_backward_matches_counting_backward(record_cap):
     counted = fx.foam_backward(*args, rgb, T, g_rgb, g_T, rec, stats)
     for name, a, b in zip(('raw', 'dA', 'cA', 'sh'), kept, counted):
         assert rel(a.cpu().numpy(), b.cpu().numpy()) <= 1e-5, name
+
+
+
+def test_counted_backward_with_foreign_counts_sets_status():
+    """Per-cell counts that do not belong to the records given to the counted backward never make it write
+    outside its buffers: all-zero counts leave every recorded sample without a place in its cell's bucket
+    (its item is dropped), and counts whose buckets overflow the item buffer drop the whole pass; both set
+    status bit 8 and the call returns with finite gradients. The forward's own counts set no such bit."""
+    import ctypes
+
+    from voronoi_gauss_b200 import _lib
+    ext = _ext()
+    gr, prm, o, d, start, near, far = _config1()
+    g = ext.Graph(cuda(gr['points']), cuda(gr['offsets']), cuda(gr['adj']))
+    dA = ext.conic(cuda(prm['d_log_scale']), cuda(prm['d_quat']))
+    cA = ext.conic(cuda(prm['c_log_scale']), cuda(prm['c_quat']))
+    raw, sh = cuda(prm['raw']), cuda(prm['sh'])
+    rays = [cuda(x) for x in (o, d, start, near, far)]
+    args = (g.points, g.offsets, g.adj, raw, dA, cA, sh, 1, *rays, 1e-4, 1e-4)
+    B, K = len(o), 256
+    counts = torch.empty(ext.sample_counts_size(len(gr['points']), B, K), dtype=torch.int32, device='cuda')
+    fx = ext.foam_extension()
+    rgb, T, _, stats, rec = fx.foam_forward(*args, K, counts=counts)
+    gen = torch.Generator().manual_seed(7)
+    g_rgb, g_T = torch.randn(B, 3, generator=gen).cuda(), torch.randn(B, generator=gen).cuda()
+
+    def status_after(cnt):
+        _lib.call('vg_status_reset')
+        grads = fx.foam_backward(*args, rgb, T, g_rgb, g_T, rec, stats, counts=cnt)
+        torch.cuda.synchronize()
+        assert all(bool(torch.isfinite(x).all()) for x in grads)
+        bits_ = ctypes.c_int(-1)
+        _lib.call('vg_status', ctypes.addressof(bits_))
+        return bits_.value
+
+    assert status_after(torch.zeros_like(counts)) & 8
+    assert status_after(torch.full_like(counts, 1 << 24)) & 8
+    assert not status_after(counts) & 8

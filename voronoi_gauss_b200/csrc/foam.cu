@@ -365,6 +365,9 @@ struct ItemOut {
     int64_t n;             // rays in the chunk
     const int* offsets;    // first bucket position of every cell
     int* fill;             // bucket fill cursors
+    int64_t cap;           // item slots of the buffer
+    const int* bad;        // set by bucket_check_kernel when the buckets do not fit the buffer
+    int* status;
 };
 
 template <int MODE>
@@ -457,14 +460,14 @@ __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
 struct Ticketed {
     Sample S;
     bool has_c;
-    int base, tick;  // first position of the sample's cell bucket, the sample's ticket in it
+    int base, tick, limit;  // first position of the sample's cell bucket, its ticket in it, the bucket's end
     float4 raw[2];   // the next record this slot decodes
 };
 
 __device__ __forceinline__ void replay_decode(const GradIn& gi, const ItemOut& io, const GraphView& g, int64_t r,
                                               int K, int s, const float (&o)[3], const float (&d)[3], Ticketed& X) {
     get_record(gi.rec, r, K, s, o, d, g.inv, X.S, X.has_c);
-    X.base = __ldg(io.offsets + X.S.cell);
+    X.base = __ldg(io.offsets + X.S.cell), X.limit = __ldg(io.offsets + X.S.cell + 1);
     X.tick = atomicAdd(io.fill + X.S.cell, 1);
 }
 
@@ -472,16 +475,23 @@ __device__ __forceinline__ void replay_decode(const GradIn& gi, const ItemOut& i
 __device__ __forceinline__ void replay_decode_loaded(const ItemOut& io, const GraphView& g, const float (&o)[3],
                                                      const float (&d)[3], Ticketed& X) {
     decode_record(X.raw, o, d, g.inv, X.S, X.has_c);
-    X.base = __ldg(io.offsets + X.S.cell);
+    X.base = __ldg(io.offsets + X.S.cell), X.limit = __ldg(io.offsets + X.S.cell + 1);
     X.tick = atomicAdd(io.fill + X.S.cell, 1);
 }
 
-__device__ __forceinline__ void replay_put(float4* __restrict__ items, const Ticketed& X, float gs, float gC0,
-                                           float gC1, float gC2, bool has_c, const float (&dir)[3]) {
+// Writes X's item at its place; a ticket beyond its cell's bucket (counts that do not belong to these
+// records) drops the item and sets kErrBuckets instead of writing outside the bucket.
+__device__ __forceinline__ void replay_put(const ItemOut& io, const Ticketed& X, float gs, float gC0, float gC1,
+                                           float gC2, bool has_c, const float (&dir)[3]) {
+    const int pos = X.base + X.tick;
+    if (pos >= X.limit || pos < 0 || pos >= io.cap) {
+        atomicOr(io.status, kErrBuckets);
+        return;
+    }
     const Sample& P = X.S;
     const bool do_c = has_c && (gC0 != 0.f || gC1 != 0.f || gC2 != 0.f);
     const float gCC = do_c ? gC0 * P.C0 + gC1 * P.C1 + gC2 * P.C2 : 0.f;
-    float4* it = items + 4 * static_cast<int64_t>(X.base + X.tick);
+    float4* it = io.items + 4 * static_cast<int64_t>(pos);
     it[0] = make_float4(P.x0, P.x1, P.x2, gs);
     it[1] = make_float4(do_c ? gC0 : 0.f, do_c ? gC1 : 0.f, do_c ? gC2 : 0.f, gCC);
     it[2] = make_float4(P.mmin, do_c ? P.inv_a : 0.f, 0.f, 0.f);
@@ -494,7 +504,7 @@ __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
     if (r >= io.r0 + io.n) return;
     const int K = gi.record_cap;
     const int n_stored = __ldg(gi.stats + 3 * r);
-    if (gi.rec == nullptr || K <= 0 || n_stored > K || n_stored <= 0) return;
+    if (gi.rec == nullptr || K <= 0 || n_stored > K || n_stored <= 0 || *io.bad) return;
     float o[3], d[3], near, far;
     load_ray(R, r, o, d, near, far);
     float b[16];
@@ -528,7 +538,7 @@ __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
         g_opacity = delta * (g_opacity - tail_grad);
         const float h0 = active ? 0.5f * w * gR0 : 0.f, h1 = active ? 0.5f * w * gR1 : 0.f,
                     h2 = active ? 0.5f * w * gR2 : 0.f;
-        replay_put(io.items, P, carry_sigma + 0.5f * g_opacity, gP0 + h0, gP1 + h1, gP2 + h2, P.has_c, d);
+        replay_put(io, P, carry_sigma + 0.5f * g_opacity, gP0 + h0, gP1 + h1, gP2 + h2, P.has_c, d);
         carry_sigma = 0.5f * g_opacity;
         gP0 = h0, gP1 = h1, gP2 = h2;
         T = T_after;
@@ -549,15 +559,15 @@ __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
         if (!go2) break;
     }
     if (p_is_1)
-        replay_put(io.items, X1, carry_sigma, gP0, gP1, gP2, X1.has_c, d);
+        replay_put(io, X1, carry_sigma, gP0, gP1, gP2, X1.has_c, d);
     else
-        replay_put(io.items, X0, carry_sigma, gP0, gP1, gP2, X0.has_c, d);
+        replay_put(io, X0, carry_sigma, gP0, gP1, gP2, X0.has_c, d);
     // every recorded sample was counted into its bucket: fill the places of any the replay did not reach
     // with zero-gradient items (the replay follows the forward, so normally there are none)
     for (int s2 = k + 1; s2 < n_stored; ++s2) {
         Ticketed Z;
         replay_decode(gi, io, g, r, K, s2, o, d, Z);
-        replay_put(io.items, Z, 0.f, 0.f, 0.f, 0.f, false, d);
+        replay_put(io, Z, 0.f, 0.f, 0.f, 0.f, false, d);
     }
 }
 
@@ -571,9 +581,24 @@ __global__ void __launch_bounds__(kBlock, VG_BWD_MINB)
 // shared memory, read as broadcasts), accumulates the site's gradient in registers and issues one set
 // of 16-byte atomics per (chunk, site).
 
-// Chunks of at most kChunk samples of one cell: (cell, first position in order, count).
+// Buckets given by per-cell counts that may come from the caller (vg_foam_backward_counted): their
+// offsets must be non-decreasing and end within the item buffer, else the pass is dropped (*bad = 1,
+// kErrBuckets) before anything is written or chunked.
 __global__ void __launch_bounds__(kBlock)
-    cm_chunks_kernel(const int* __restrict__ offsets, int n_cells, int4* __restrict__ chunks, int* n_chunks) {
+    bucket_check_kernel(const int* __restrict__ offsets, int n_cells, int64_t cap, int* bad, int* status) {
+    const int i = blockIdx.x * kBlock + threadIdx.x;
+    if (i > n_cells) return;
+    const int a = __ldg(offsets + i);
+    const bool ok = i == n_cells ? a >= 0 && a <= cap : a >= 0 && __ldg(offsets + i + 1) >= a;
+    if (!ok) *bad = 1, atomicOr(status, kErrBuckets);
+}
+
+// Chunks of at most kChunk samples of one cell: (cell, first position in order, count). Nothing when
+// bucket_check_kernel rejected the buckets (bad may be null).
+__global__ void __launch_bounds__(kBlock)
+    cm_chunks_kernel(const int* __restrict__ offsets, int n_cells, int4* __restrict__ chunks, int* n_chunks,
+                     const int* bad) {
+    if (bad != nullptr && *bad) return;
     const int i = blockIdx.x * kBlock + threadIdx.x;
     const int lane = threadIdx.x & 31;
     int cnt = 0, a = 0;
@@ -996,7 +1021,7 @@ cudaError_t cm_scatter_bucketed(const GraphView& g, const FieldView& F, const fl
     const int n = g.n;
     cudaError_t e = cudaMemsetAsync(counter, 0, 16, st);
     if (e != cudaSuccess) return e;
-    cm_chunks_kernel<<<blocks(n), kBlock, 0, st>>>(offsets, n, chunks, counter);
+    cm_chunks_kernel<<<blocks(n), kBlock, 0, st>>>(offsets, n, chunks, counter, nullptr);
     const int grid = sm_count() * 3;
     ProfScope ps(kProfScatter, st);
     switch (F.s4) {
@@ -1042,7 +1067,7 @@ cudaError_t march_backward_cm(const GraphView& g, const FieldView& F, const RayV
         if (e != cudaSuccess) return e;
         march_bucket_kernel<<<blocks(nr * kMarchCap), kBlock, 0, st>>>(items, n_items, nr, kMarchCap, offsets, fill,
                                                                         order);
-        cm_chunks_kernel<<<blocks(n), kBlock, 0, st>>>(offsets, n, chunks, counter);
+        cm_chunks_kernel<<<blocks(n), kBlock, 0, st>>>(offsets, n, chunks, counter, nullptr);
         ProfScope ps(kProfScatter, st);
         switch (F.s4) {
             case 1: cm_scatter_kernel<1, kIndexed><<<grid, kBlock, 0, st>>>(g, F, items, order, chunks, counter, grad); break;
@@ -1109,7 +1134,7 @@ cudaError_t forward_deferred(const GraphView& g, const FieldView& F, const RayVi
         if (e != cudaSuccess) return e;
         cmf_bucket_kernel<<<blocks(32 * nr), kBlock, 0, st>>>(out.rec, out.stats, g.inv, r0, nr, K, offsets, fill,
                                                                order);
-        cm_chunks_kernel<<<blocks(n), kBlock, 0, st>>>(offsets, n, chunks, counter);
+        cm_chunks_kernel<<<blocks(n), kBlock, 0, st>>>(offsets, n, chunks, counter, nullptr);
         ProfScope ps(kProfColor, st);
         switch (F.s4) {
             case 1: cmf_color_kernel<1><<<grid, kBlock, 0, st>>>(g, F, R, out.rec, K, order, chunks, counter, r0); break;
@@ -1191,17 +1216,19 @@ cudaError_t foam_backward(const GraphView& g, const FieldView& F, const RayView&
         if (e == cudaSuccess) e = cudaMemsetAsync(counter, 0, 16, st);
         if (e == cudaSuccess && c.all_count == nullptr) e = cudaMemsetAsync(count, 0, 4 * static_cast<size_t>(n + 1), st);
         if (e != cudaSuccess) return e;
-        const ItemOut io{items, pass_count, r0, nr, offsets, fill};
+        int* bad = counter + 1;  // zeroed with the chunk counter
+        const ItemOut io{items, pass_count, r0, nr, offsets, fill, L.rays_per_pass * K, bad, status};
         size_t tb = L.temp_bytes;
         if (c.all_count == nullptr)
             cmf_count_kernel<<<blocks(32 * nr), kBlock, 0, st>>>(gi.rec, gi.stats, g.inv, r0, nr, K, count);
         e = cub::DeviceScan::ExclusiveSum(b + L.temp, tb, pass_count, offsets, n + 1, st);
         if (e != cudaSuccess) return e;
+        bucket_check_kernel<<<blocks(n + 1), kBlock, 0, st>>>(offsets, n, io.cap, bad, status);
         {
             ProfScope ps(kProfReplay, st);
             replay_items_kernel<<<blocks(nr), kBlock, 0, st>>>(g, F, R, c, gi, io);
         }
-        cm_chunks_kernel<<<blocks(n), kBlock, 0, st>>>(offsets, n, chunks, counter);
+        cm_chunks_kernel<<<blocks(n), kBlock, 0, st>>>(offsets, n, chunks, counter, bad);
         ProfScope ps(kProfScatter, st);
         switch (F.s4) {
             case 1: cm_scatter_kernel<1, kBucketed><<<grid, kBlock, 0, st>>>(g, F, items, nullptr, chunks, counter, grad); break;

@@ -42,6 +42,9 @@ constexpr int kFieldVec = 4;             // float4 per site in the field pack
 constexpr int kErrWalkCap = 1;   // a greedy walk hit kWalkCap
 constexpr int kErrCellCap = 2;   // a ray hit kMaxCells
 constexpr int kErrBadSite = 4;   // a start or sample site outside [0, N): that ray or sample is skipped
+constexpr int kErrBuckets = 8;   // per-cell sample counts that do not fit the records: the cell-major items
+                                 // that fall outside their cell's bucket (or all of a pass's, when the
+                                 // counts' buckets overflow the item buffer) are dropped
 
 inline __host__ __device__ int sh_coeffs(int deg) { return (deg + 1) * (deg + 1); }
 inline __host__ __device__ int sh_vec4(int deg) { return (3 * sh_coeffs(deg) + 3) / 4; }
